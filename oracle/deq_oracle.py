@@ -1,0 +1,635 @@
+"""CPU oracle for the AIDEEN DEQ training hot path.  TEST INFRASTRUCTURE ONLY.
+
+This module is the parity checker.  Only `tests/`, `__graft_entry__.smoke()`
+and the CPU-baseline leg of `bench.py` may import it; the product path
+(`aideen_b200`) never calls it.
+
+It restates, in float64 numpy, the reference's live GPU semantics:
+
+* input projection          `deq_slot_attn_unified_clean.wgsl:762-804`
+* iter-0 slot attention      `deq_slot_attn_unified_clean.wgsl:281-495`
+* Picard solve + stop rule   `deq_slot_attn_unified_clean.wgsl:900-943, 960-1806`
+* FPM read (Model A inject)  `deq_slot_attn_unified_clean.wgsl:855-883, 1006-1200`
+* FPM write (memory scan)    `deq_slot_attn_unified_clean.wgsl:1965-2140, 2290-2300`
+* slot pooling               `aideen-block/src/shaders/deq_forward_pool.wgsl:32-65`
+* LM-head CE + RMSNorm bwd   `aideen-backbone/src/shaders/lm_train.wgsl:79-130, 327-395`
+* clean adjoint init/step    `staged_adjoint_picard_clean.wgsl:143-248`
+* Anderson store/mix         `staged_adjoint_picard_clean.wgsl:1011-1135`
+* source-grad reduce         `staged_adjoint_picard_clean.wgsl:250-327`
+* Adam                       `aideen-training-lab/src/optimizer.rs:105-183`
+* clipped SGD apply          `aideen-backbone/src/shaders/fused_deq_update.wgsl:809-823`
+* spectral renorm            `aideen-block/src/shaders/spectral_renorm.wgsl:83-196`
+
+Weight gradients are derived analytically (implicit-function theorem through
+the map the clean adjoint linearises); the reference's own stage-4 shaders
+read a stale scratch layout and are not used as a source.  The gradients are
+pinned by central finite differences in `tests/test_oracle_cpu.py`.
+
+PARITY PIN STATUS: partially pinned.  The reference is Rust + WGSL and cannot
+run here (no cargo, no wgpu adapter); its tests hold no golden vectors for
+this path.  What pins the oracle: the reference's spectral-norm known answers
+(`spectral_norm.rs:102-149`), the reference's numeric-adjoint test case
+(`aideen-backbone/tests/picard_pipeline_test.rs:1859-1935`, cosine > 0.80),
+and finite-difference checks of every gradient.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+
+RANK = 32
+HOMEO_MIN_ITERS = 4           # FPM_HOMEO_MIN_ITERS
+HOMEO_ALPHA_ERR_SCALE = 0.15  # FPM_HOMEO_ALPHA_ERR_SCALE
+HOMEO_PLATEAU_TOL = 0.10      # FPM_HOMEO_PLATEAU_TOL
+FPM_ALPHA_H = 0.2
+FPM_GATE_BIAS = -1.5
+FPM_RESIDUAL_SCALE = 0.1
+
+
+def es(spec, *ops):
+    return np.einsum(spec, *ops, optimize=True)
+
+
+class Offsets:
+    """AllWeights offsets, restated independently of the package
+    (`deq_slot_attn_unified_clean.wgsl:189-237`, `gpu_deq.rs:260-422`)."""
+
+    def __init__(self, d: int, h: int):
+        r = RANK
+        self.d, self.h = d, h
+        dd = d * d
+        self.wq = 0
+        self.q_bias = h * dd
+        self.wk = h * dd + h * d
+        self.k_bias = self.wk + h * dd
+        self.wv = self.wk + h * dd + h * d
+        self.wo = self.wv + h * dd
+        self.win = self.wo + h * dd
+        self.wx = self.win + h * dd
+        self.wout = self.wx + dd
+        self.alog = self.wout + dd
+        self.nscale = self.alog + h * d
+        self.hist = self.nscale + d
+        o = self.hist + dd                 # after hist_mat
+        self.hist_scale = o; o += h * d
+        self.hist_bias = o; o += h * d
+        self.hist_gate = o; o += h
+        self.slot_anchor = o; o += h * d
+        self.w_k_write = o; o += h * d * r
+        self.w_v_write = o; o += h * r * d
+        self.b_delta = o; o += h * d
+        self.flags = o; o += 21
+        self.signal_zero = self.flags + 9
+        self.signal_scale = self.flags + 16
+        self.hist_gate_query = o; o += h * d
+        self.w_write_gate = o; o += h * d
+        self.b_write_mem = o; o += h
+        self.hhist_gamma = o; o += h
+        self.w_retain_up = o; o += h * d * r
+        self.w_retain_down = o; o += h * r * d
+        self.b_retain = o; o += h * d
+        self.w_q_mem = o; o += h * d * r
+        self.w_k_mem = o; o += h * d * r
+        self.b_read_mem = o; o += h
+        o += 3 * h * d * r + h + h * d + h   # associative block (kept off)
+        self.total = o
+
+
+class View:
+    """Named float64 views of an AllWeights vector."""
+
+    def __init__(self, w: np.ndarray, d: int, h: int):
+        L = Offsets(d, h)
+        self.L = L
+        w = np.asarray(w, dtype=np.float64)
+        dd, r = d * d, RANK
+        self.hd = min(d, 32)
+        self.Wq = w[L.wq:L.wq + h * dd].reshape(h, d, d)       # [s][j][o]
+        self.qb = w[L.q_bias:L.q_bias + h * d].reshape(h, d)
+        self.Wk = w[L.wk:L.wk + h * dd].reshape(h, d, d)
+        self.kb = w[L.k_bias:L.k_bias + h * d].reshape(h, d)
+        self.Wv = w[L.wv:L.wv + h * dd].reshape(h, d, d)
+        self.Wo = w[L.wo:L.wo + h * dd].reshape(h, d, d)       # [s][k][o]
+        self.Win = w[L.win:L.win + h * dd].reshape(h, d, d)
+        self.Wx = w[L.wx:L.wx + dd].reshape(d, d)
+        self.Wout = w[L.wout:L.wout + dd].reshape(d, d)
+        self.Alog = w[L.alog:L.alog + h * d].reshape(h, d)
+        self.NS = w[L.nscale:L.nscale + d]
+        self.anchor = w[L.slot_anchor:L.slot_anchor + h * d].reshape(h, d)
+        self.hscale = w[L.hist_scale:L.hist_scale + h * d].reshape(h, d)
+        self.hbias = w[L.hist_bias:L.hist_bias + h * d].reshape(h, d)
+        self.Wkw = w[L.w_k_write:L.w_k_write + h * d * r].reshape(h, d, r)
+        self.Wvw = w[L.w_v_write:L.w_v_write + h * r * d].reshape(h, r, d)
+        self.bdelta = w[L.b_delta:L.b_delta + h * d].reshape(h, d)
+        self.signal_zero = w[L.signal_zero] > 0.5
+        self.sig_scale = float(w[L.signal_scale])
+        self.wgate = w[L.w_write_gate:L.w_write_gate + h * d].reshape(h, d)
+        self.bwrite = w[L.b_write_mem:L.b_write_mem + h]
+        self.Wup = w[L.w_retain_up:L.w_retain_up + h * d * r].reshape(h, d, r)
+        self.Wdown = w[L.w_retain_down:L.w_retain_down + h * r * d].reshape(h, r, d)
+        self.bret = w[L.b_retain:L.b_retain + h * d].reshape(h, d)
+        self.Wqm = w[L.w_q_mem:L.w_q_mem + h * d * r].reshape(h, d, r)
+        self.Wkm = w[L.w_k_mem:L.w_k_mem + h * d * r].reshape(h, d, r)
+        self.bread = w[L.b_read_mem:L.b_read_mem + h]
+
+
+@dataclass
+class Cfg:
+    d: int
+    h: int
+    max_iters: int = 12
+    eps: float = 1e-4
+    damping: float = 0.85          # forward blend (generic path) and adjoint beta
+    slot_coord: bool = True        # residual_alpha in (-1.5, -0.9]: attention branch on
+    fpm: bool = False              # Model-A memory read/inject/write
+    fpm_alpha_m: float = 0.01
+    fpm_tau: float = 0.5
+    fpm_read_gate_min: float = 0.0
+    adj_iters: int = 12
+    anderson_m: int = 0
+
+
+def rms(x, axis=-1, eps=1e-6):
+    return np.sqrt(np.mean(x * x, axis=axis) + eps)
+
+
+# ---------------------------------------------------------------------------
+# forward
+# ---------------------------------------------------------------------------
+
+def project_signal(S, V: View):
+    """signal[n,s,o] = sigma * sum_j Win[s][j][o] S[n,j]  (`:762-804`)."""
+    S = np.asarray(S, np.float64)
+    sig = es('nj,sjo->nso', S, V.Win) * V.sig_scale
+    if V.signal_zero:
+        sig = np.zeros_like(sig)
+    return sig
+
+
+def slot_attention(signal, V: View):
+    """Iter-0 slot attention per token (`compute_slot_coord`, `:281-495`).
+
+    signal: [N,h,d].  Returns A = attn*scale [N,h,d] and a cache dict.
+    """
+    N, h, d = signal.shape
+    hd = V.hd
+    src = signal + V.anchor[None]
+    R = rms(src)                                         # slot_coord_prev, [N,h]
+    K = es('nkj,kjc->nkc', src, V.Wk[:, :, :hd]) + V.kb[None, :, :hd]
+    Vv = es('nkj,kjc->nkc', src, V.Wv[:, :, :hd])
+    Q = es('nsj,sjc->nsc', src, V.Wq[:, :, :hd]) + V.qb[None, :, :hd]
+    logits = es('nsc,nkc->nsk', Q, K) * (2.0 / math.sqrt(max(1, hd)))
+    if h > 1:
+        idx = np.arange(h)
+        logits[:, idx, idx] = -1e30
+    mx = logits.max(axis=-1, keepdims=True)
+    e = np.exp(logits - mx)
+    ssum = np.maximum(e.sum(-1, keepdims=True), 1e-12)
+    alpha = e / ssum                                      # [N,s,k]
+    mix = es('nsk,nkc->nsc', alpha, Vv) - Vv.mean(axis=1, keepdims=True)
+    r = np.sqrt(np.mean(mix * mix, -1) + 1e-6)            # [N,s]
+    nmix = mix / r[..., None]
+    a = es('nsc,sco->nso', nmix, V.Wo[:, :hd, :])
+    rho = rms(a)
+    scale = np.maximum(R, 1e-3) / np.maximum(rho, 1e-6)
+    A = a * scale[..., None]
+    cache = dict(src=src, R=R, K=K, V=Vv, Q=Q, alpha=alpha, mix=mix, r=r, n=nmix,
+                 a=a, rho=rho, scale=scale)
+    return A, cache
+
+
+def _converged(err, prev, it, eps):
+    band = max(eps, HOMEO_ALPHA_ERR_SCALE * FPM_ALPHA_H)
+    plateau = np.abs(err - prev) / np.maximum(prev, eps)
+    strict = err < eps
+    homeo = (it + 1 >= HOMEO_MIN_ITERS) & (err <= band) & (plateau <= HOMEO_PLATEAU_TOL)
+    return strict | homeo
+
+
+def fpm_keys(m_prev, V: View):
+    """k_mem[b,ms,r] = sum_j Wkm[ms][j][r] (m + scale*tanh(m) + bias)  (`:855-883`)."""
+    keyed = m_prev + V.hscale[None] * np.tanh(m_prev) + V.hbias[None]
+    return es('bmj,mjr->bmr', keyed, V.Wkm)
+
+
+def fpm_read(h_cur, sig_t, keys, m_prev, V: View, cfg: Cfg):
+    """Memory context from the first structured state (`:1031-1200`).
+
+    h_cur: [B,h,d] (state after iteration 0), sig_t: [B,h,d].
+    """
+    B, h, d = h_cur.shape
+    hq = h_cur / np.sqrt(np.maximum((h_cur * h_cur).sum(-1, keepdims=True), 1e-6))
+    q = es('bsj,sjr->bsr', hq, V.Wqm)
+    score = es('bsr,bmr->bsm', q, keys) + V.bread[None, None, :]
+    score = score / math.sqrt(RANK) / max(cfg.fpm_tau, 1e-3)
+    mx = score.max(-1, keepdims=True)
+    e = np.exp(score - mx)
+    w = e / np.maximum(e.sum(-1, keepdims=True), 1e-12)
+    peak = w.max(-1)
+    uni = 1.0 / max(1, h)
+    conf = np.clip((peak - uni) / max(1e-6, 1.0 - uni), 0.0, 1.0)
+    gate = np.maximum(np.sqrt(conf), cfg.fpm_read_gate_min)
+    mem_raw = es('bsm,bmd->bsd', w, m_prev)
+    mu = np.tanh(mem_raw)
+    mu_norm = np.sqrt(np.maximum((mu * mu).sum(-1), 1e-6))
+    sig_norm = np.sqrt(np.maximum((sig_t * sig_t).sum(-1), 1e-6))
+    alpha_m = max(cfg.fpm_alpha_m, 0.001)
+    coef = sig_norm * alpha_m / np.maximum(mu_norm, 1e-6) * gate
+    return mu * coef[..., None]
+
+
+def fpm_write(h_star, sig_t, m_prev, V: View, Wx_diag):
+    """Post-solve memory update (`:1965-2140`); returns m_inner [B,h,d]."""
+    B, h, d = h_star.shape
+    c = 0.5 * (h_star + sig_t)
+    h_rms = np.sqrt(np.maximum((h_star * h_star).sum(-1) / d, 1e-6))
+    hu = h_star / h_rms[..., None]
+    gate_in = (c * V.wgate[None]).sum(-1) / math.sqrt(d) + V.bwrite[None] + FPM_GATE_BIAS
+    z = np.clip(1.0 / (1.0 + np.exp(-gate_in)), 0.0, 1.0)
+    bott = es('bsj,sjr->bsr', c, V.Wkw)
+    prop = np.tanh(V.bdelta[None] + es('bsr,sro->bso', bott, V.Wvw))
+    prev_norm = np.sqrt(np.maximum((m_prev * m_prev).sum(-1), 1e-6))
+    diff = prop - m_prev
+    diff_norm = np.sqrt(np.maximum((diff * diff).sum(-1), 1e-6))
+    novelty = diff_norm / (diff_norm + prev_norm + 1e-6)
+    up = es('bsj,sjr->bsr', c, V.Wup)
+    retain_raw = 1.0 / (1.0 + np.exp(-(V.bret[None] + es('bsr,sro->bso', up, V.Wdown))))
+    retain = 1.0 - novelty[..., None] * (1.0 - retain_raw)
+    write = z[..., None] * (FPM_RESIDUAL_SCALE * prop)
+    wx = 0.5 * np.tanh(Wx_diag)[None, None, :]
+    x = np.sqrt(np.maximum(z, 1e-6))[..., None] * hu + wx * hu + write
+    a = 1.0 / (1.0 + np.exp(V.Alog))[None]
+    base = a * m_prev + (1.0 - a) * x
+    return retain * m_prev + (1.0 - retain) * base
+
+
+@dataclass
+class ForwardOut:
+    signal: np.ndarray        # [B,T,h,d]
+    A: np.ndarray             # [B,T,h,d] attention injection (attn*scale)
+    hstar: np.ndarray         # [B,T,h,d]
+    iters: np.ndarray         # [B,T,h] int
+    pooled: np.ndarray        # [B,T,d]
+    hist_ctx: np.ndarray      # [B,T,h,d] (FPM memory per token; zeros without FPM)
+    mstate: np.ndarray        # [B,h,d]
+    fpm_ctx: np.ndarray       # [B,T,h,d]
+    attn_cache: dict = field(default_factory=dict)   # flattened [B*T, ...]
+
+
+def forward(S_in, W, cfg: Cfg, mstate=None) -> ForwardOut:
+    """Forward DEQ solve over a [B,T,d] chunk (token carry on, `:900`)."""
+    d, h = cfg.d, cfg.h
+    V = View(W, d, h)
+    S = np.asarray(S_in, np.float64)
+    B, T, _ = S.shape
+    signal = project_signal(S.reshape(B * T, d), V).reshape(B, T, h, d)
+    if cfg.slot_coord:
+        A, cache = slot_attention(signal.reshape(B * T, h, d), V)
+        A = A.reshape(B, T, h, d)
+    else:
+        A, cache = np.zeros_like(signal), {}
+    NS = V.NS[None, None, :]
+    anchor = V.anchor[None]
+    blend = FPM_ALPHA_H if cfg.fpm else cfg.damping
+    Wx_diag = np.diag(V.Wx)
+    m = np.zeros((B, h, d)) if mstate is None else np.asarray(mstate, np.float64).copy()
+    hstar = np.zeros((B, T, h, d))
+    iters = np.zeros((B, T, h), np.int64)
+    hist = np.zeros((B, T, h, d))
+    ctx_all = np.zeros((B, T, h, d))
+    hcur = None
+    for t in range(T):
+        sig = signal[:, t]
+        if t == 0:
+            hcur = sig / np.maximum(rms(sig), 1e-6)[..., None]
+        ctx = np.zeros((B, h, d))
+        keys = fpm_keys(m, V) if cfg.fpm else None
+        active = np.ones((B, h), bool)
+        prev = np.ones((B, h))
+        it_count = np.zeros((B, h), np.int64)
+        for it in range(cfg.max_iters):
+            if not active.any():
+                break
+            if cfg.fpm and it == 1:
+                ctx_new = fpm_read(hcur, sig, keys, m, V, cfg)
+                ctx = np.where(active[..., None], ctx_new, ctx)
+            dep = sig + hcur + anchor + (A[:, t] if it == 0 else 0.0)
+            pre = dep + (ctx if (cfg.fpm and it >= 1) else 0.0)
+            r = rms(dep)
+            f = NS * pre / r[..., None]
+            hn = blend * f + (1.0 - blend) * hcur
+            dh = hn - hcur
+            err = np.sqrt(np.mean(dh * dh, -1) + 1e-12) / np.maximum(r, 1e-6)
+            conv = _converged(err, prev, it, cfg.eps)
+            hcur = np.where(active[..., None], hn, hcur)
+            prev = np.where(active, err, prev)
+            it_count = it_count + active
+            active = active & ~conv
+        hstar[:, t] = hcur
+        iters[:, t] = it_count
+        ctx_all[:, t] = ctx
+        if cfg.fpm:
+            m = fpm_write(hcur, sig, m, V, Wx_diag)
+            hist[:, t] = m
+    pooled = hstar.mean(axis=2)
+    return ForwardOut(signal=signal, A=A, hstar=hstar, iters=iters, pooled=pooled,
+                      hist_ctx=hist, mstate=m, fpm_ctx=ctx_all, attn_cache=cache)
+
+
+# ---------------------------------------------------------------------------
+# LM head (producer of the adjoint RHS)
+# ---------------------------------------------------------------------------
+
+def lm_head(pooled, targets, w_lm, b_lm, g_lm):
+    """Dense full-vocab CE through RMSNorm (`lm_train.wgsl:79-130, 327-395`).
+
+    pooled: [N,d], targets: [N] (negative = ignored).  Returns loss (mean over
+    active tokens), dL/dpooled [N,d], and grads of (w_lm, b_lm, g_lm).
+    """
+    P = np.asarray(pooled, np.float64)
+    W = np.asarray(w_lm, np.float64)
+    g_lm = np.asarray(g_lm, np.float64)
+    N, d = P.shape
+    r = np.sqrt(np.mean(P * P, -1) + 1e-5)
+    xhat = P / r[:, None]
+    y = xhat * g_lm[None]
+    logits = y @ W.T + np.asarray(b_lm, np.float64)[None]
+    mx = logits.max(-1, keepdims=True)
+    e = np.exp(logits - mx)
+    Z = e.sum(-1, keepdims=True)
+    p = e / Z
+    tg = np.asarray(targets).astype(np.int64)
+    act = tg >= 0
+    n_act = max(1, int(act.sum()))
+    rows = np.nonzero(act)[0]
+    loss = float(-(logits[rows, tg[rows]] - mx[rows, 0] - np.log(Z[rows, 0])).sum()) / n_act
+    dlog = p.copy()
+    dlog[rows, tg[rows]] -= 1.0
+    dlog[~act] = 0.0
+    dlog /= n_act
+    dy = dlog @ W
+    gW = dlog.T @ y
+    gb = dlog.sum(0)
+    gg = (dy * xhat).sum(0)
+    dyg = dy * g_lm[None]
+    dot = (dyg * P).sum(-1)
+    dP = dyg / r[:, None] - P * (dot / (d * r ** 3))[:, None]
+    return loss, dP, gW, gb, gg
+
+
+# ---------------------------------------------------------------------------
+# adjoint
+# ---------------------------------------------------------------------------
+
+def adjoint(hstar, branch, rhs_tok, NS, cfg: Cfg, rhs_slot=None):
+    """Clean Picard adjoint (`staged_adjoint_picard_clean.wgsl:143-248`) with
+    optional Anderson mixing (`:1011-1135`).
+
+    hstar, branch: [N,h,d] (branch = signal + attn*scale + anchor),
+    rhs_tok: [N,d] (pooled dL/dH, scaled 1/h per slot) or None,
+    rhs_slot: optional [N,h,d] added to the per-slot RHS.
+    Returns v [N,h,d], g_pre = beta*J_norm^T v [N,h,d], pre, rms(pre).
+    """
+    N, h, d = hstar.shape
+    beta = cfg.damping
+    pre = np.asarray(branch, np.float64) + np.asarray(hstar, np.float64)
+    r = np.sqrt(np.mean(pre * pre, -1) + 1e-6)
+    inv = 1.0 / np.maximum(r, 1e-6)
+    den = np.maximum(d * r ** 3, 1e-6)
+    rhs = np.zeros((N, h, d))
+    if rhs_tok is not None:
+        rhs = rhs + (np.asarray(rhs_tok, np.float64) / max(1, h))[:, None, :]
+    if rhs_slot is not None:
+        rhs = rhs + np.asarray(rhs_slot, np.float64)
+    NSb = np.asarray(NS, np.float64)[None, None, :]
+
+    def norm_grad(v):
+        up = beta * v
+        coeff = (up * NSb * pre).sum(-1)
+        return NSb * inv[..., None] * up - pre * (coeff / den)[..., None]
+
+    v = rhs.copy()
+    m = cfg.anderson_m
+    hist = [np.zeros_like(v) for _ in range(m)] if m > 0 else []
+    for k in range(cfg.adj_iters):
+        v = rhs + (norm_grad(v) + (1.0 - beta) * v)
+        if m > 0:
+            hist[k % m] = v.copy()
+            n_res = min(k, m - 1)
+            if k >= 2 and n_res >= 2:
+                v = _anderson_mix(hist, k, m, n_res)
+    return v, norm_grad(v), pre, r
+
+
+def _anderson_mix(hist, k, m, n_res):
+    N = hist[0].shape[0]
+    deltas = [hist[(k + m - i) % m] - hist[(k + m - i - 1) % m] for i in range(n_res)]
+    G = np.zeros((N, 3, 3))
+    for i in range(n_res):
+        for j in range(i, n_res):
+            dot = (deltas[i] * deltas[j]).sum(axis=(1, 2))
+            G[:, i, j] = dot
+            G[:, j, i] = dot
+    beta = np.zeros((N, 3))
+    if n_res == 2:
+        g00, g01, g10, g11 = G[:, 0, 0], G[:, 0, 1], G[:, 1, 0], G[:, 1, 1]
+        reg = np.maximum(1e-8, 1e-4 * (np.abs(g00) + np.abs(g11)))
+        g00 = g00 + reg
+        g11 = g11 + reg
+        det = g00 * g11 - g01 * g10
+        sdet = np.where(det < 0, np.minimum(det, -1e-10), np.maximum(det, 1e-10))
+        beta[:, 0] = (g11 - g01) / sdet
+        beta[:, 1] = (g00 - g10) / sdet
+    else:
+        g = G.copy()
+        reg = np.maximum(1e-8, 1e-4 * (np.abs(g[:, 0, 0]) + np.abs(g[:, 1, 1]) + np.abs(g[:, 2, 2])))
+        for i in range(3):
+            g[:, i, i] += reg
+        g00, g01, g02 = g[:, 0, 0], g[:, 0, 1], g[:, 0, 2]
+        g10, g11, g12 = g[:, 1, 0], g[:, 1, 1], g[:, 1, 2]
+        g20, g21, g22 = g[:, 2, 0], g[:, 2, 1], g[:, 2, 2]
+        det = (g00 * (g11 * g22 - g12 * g21) - g01 * (g10 * g22 - g12 * g20)
+               + g02 * (g10 * g21 - g11 * g20))
+        sdet = np.where(det < 0, np.minimum(det, -1e-8), np.maximum(det, 1e-8))
+        beta[:, 0] = ((g11 * g22 - g12 * g21) - g01 * (g22 - g12) + g02 * (g21 - g11)) / sdet
+        beta[:, 1] = (g00 * (g22 - g12) - (g10 * g22 - g12 * g20) + g02 * (g10 - g20)) / sdet
+        beta[:, 2] = (g00 * (g11 - g21) - g01 * (g10 - g20) + (g10 * g21 - g11 * g20)) / sdet
+    beta = np.clip(beta[:, :n_res], -2.0, 3.0)
+    s = beta.sum(1)
+    small = np.abs(s) < 1e-6
+    beta = np.where(small[:, None], 0.0, beta / np.where(small, 1.0, s)[:, None])
+    beta[small, 0] = 1.0
+    out = np.zeros_like(hist[0])
+    for i in range(n_res):
+        out += beta[:, i][:, None, None] * hist[(k + m - i) % m]
+    return out
+
+
+def source_grad(g_pre):
+    """dL/dsignal pooled over slots (`picard_source_grad_reduce_main`, `:250-327`)."""
+    return g_pre.sum(axis=1)
+
+
+# ---------------------------------------------------------------------------
+# weight gradients (analytic)
+# ---------------------------------------------------------------------------
+
+def weight_grads(S_flat, signal, A, cache, v, g_pre, pre, r_pre, W, cfg: Cfg):
+    """dL/dtheta for every DEQ-core parameter, in the AllWeights layout.
+
+    S_flat [N,d]; signal, A, v, g_pre, pre [N,h,d]; r_pre [N,h]; cache from
+    `slot_attention` on the same N tokens.  Returns (G, dS_in).
+    """
+    d, h = cfg.d, cfg.h
+    V = View(W, d, h)
+    L = V.L
+    hd = V.hd
+    G = np.zeros(L.total)
+    beta = cfg.damping
+    gNS = (beta * v * pre / np.maximum(r_pre, 1e-6)[..., None]).sum(axis=(0, 1))
+    G[L.nscale:L.nscale + d] = gNS
+    dsig = g_pre.copy()                 # dL/dsignal
+    if cfg.slot_coord:
+        c = cache
+        gA = g_pre
+        a, rho, R, scale = c['a'], c['rho'], c['R'], c['scale']
+        rhoc = np.maximum(rho, 1e-6)
+        dscale = (gA * a).sum(-1)
+        da = gA * scale[..., None]
+        drho = np.where(rho > 1e-6, -dscale * scale / rhoc, 0.0)
+        da += (drho / (d * rho))[..., None] * a
+        dR = np.where(R > 1e-3, dscale / rhoc, 0.0)
+        src = c['src']
+        dsrc = (dR / (d * R))[..., None] * src
+        n = c['n']
+        dn = es('sco,nso->nsc', V.Wo[:, :hd, :], da)
+        gWo = es('nsc,nso->sco', n, da)
+        rr = c['r']
+        dmix = (dn - n * ((n * dn).sum(-1) / hd)[..., None]) / rr[..., None]
+        alpha, K, Vv, Q = c['alpha'], c['K'], c['V'], c['Q']
+        dalpha = es('nsc,nkc->nsk', dmix, Vv)
+        dV = es('nsk,nsc->nkc', alpha, dmix) - dmix.sum(1, keepdims=True) / h
+        dlog = alpha * (dalpha - (alpha * dalpha).sum(-1, keepdims=True))
+        gain = 2.0 / math.sqrt(max(1, hd))
+        dQ = es('nsk,nkc->nsc', dlog, K) * gain
+        dK = es('nsk,nsc->nkc', dlog, Q) * gain
+        gWq = es('nsj,nsc->sjc', src, dQ)
+        gWk = es('nsj,nsc->sjc', src, dK)
+        gWv = es('nsj,nsc->sjc', src, dV)
+        dsrc += (es('sjc,nsc->nsj', V.Wq[:, :, :hd], dQ)
+                 + es('sjc,nsc->nsj', V.Wk[:, :, :hd], dK)
+                 + es('sjc,nsc->nsj', V.Wv[:, :, :hd], dV))
+        G[L.wq:L.wq + h * d * d].reshape(h, d, d)[:, :, :hd] = gWq
+        G[L.wk:L.wk + h * d * d].reshape(h, d, d)[:, :, :hd] = gWk
+        G[L.wv:L.wv + h * d * d].reshape(h, d, d)[:, :, :hd] = gWv
+        G[L.wo:L.wo + h * d * d].reshape(h, d, d)[:, :hd, :] = gWo
+        G[L.q_bias:L.q_bias + h * d].reshape(h, d)[:, :hd] = dQ.sum(0)
+        G[L.k_bias:L.k_bias + h * d].reshape(h, d)[:, :hd] = dK.sum(0)
+        dsig += dsrc
+        G[L.slot_anchor:L.slot_anchor + h * d] = dsig.sum(0).ravel()
+    if not V.signal_zero:
+        G[L.win:L.win + h * d * d] = (es('nj,nso->sjo', S_flat, dsig) * V.sig_scale).ravel()
+        dS = es('sjo,nso->nj', V.Win, dsig) * V.sig_scale
+    else:
+        dS = np.zeros_like(S_flat)
+    return G, dS
+
+
+# ---------------------------------------------------------------------------
+# optimizers and spectral renorm
+# ---------------------------------------------------------------------------
+
+def adam(w, g, m, v, t, lr=1e-3, b1=0.9, b2=0.999, eps=1e-8, grad_scale=1.0):
+    """`Adam::step_matrix_scaled_inplace` (`optimizer.rs:105-183`)."""
+    w = np.asarray(w, np.float64).copy()
+    g = np.asarray(g, np.float64) * grad_scale
+    m = b1 * np.asarray(m, np.float64) + (1 - b1) * g
+    v = b2 * np.asarray(v, np.float64) + (1 - b2) * g * g
+    tt = max(1, t)
+    bc1 = 1 - b1 ** tt
+    bc2 = 1 - b2 ** tt
+    w -= lr * (m / bc1) / (np.sqrt(v / bc2) + eps)
+    return w, m, v
+
+
+def clipped_sgd(w, g, lr, wd, main_len, grad_scale=1.0):
+    """`apply_grad_update_main` (`fused_deq_update.wgsl:809-823`) with the
+    lr*grad_scale product of the stage kernels (`:402-410`)."""
+    w = np.asarray(w, np.float64).copy()
+    step = lr * np.asarray(g, np.float64) * grad_scale
+    mult = np.ones_like(w)
+    mult[:main_len] = 1.0 - lr * wd
+    return w * mult - np.clip(step, -0.5, 0.5)
+
+
+def spectral_renorm(W, d, h, n_iters=12, attn=0.10, win=0.30, fpm=0.70, wv=0.50, wo=0.50):
+    """`spectral_renorm_main` for every matrix index (`spectral_renorm.wgsl:83-196`).
+
+    Row-major view A[r][c] = flat[r*d + c]; v = A^T u / |.|, u = A v,
+    sigma = sqrt(|u|^2 + 1e-12).  Returns the new weights and the sigmas.
+    """
+    W = np.asarray(W, np.float64).copy()
+    L = Offsets(d, h)
+    mats = []
+    for base, thr in ((L.wq, attn), (L.wk, attn), (L.wv, wv), (L.wo, wo), (L.win, win)):
+        for s in range(h):
+            mats.append((base + s * d * d, thr))
+    mats.append((L.wx, fpm))
+    mats.append((L.wout, fpm))
+    sigmas = []
+    for off, thr in mats:
+        A = W[off:off + d * d].reshape(d, d)
+        u = np.full(d, 1.0 / math.sqrt(d))
+        sigma = 1.0
+        for _ in range(n_iters):
+            vv = A.T @ u
+            vv = vv / math.sqrt((vv * vv).sum() + 1e-12)
+            uu = A @ vv
+            sigma = math.sqrt((uu * uu).sum() + 1e-12)
+            u = uu / sigma
+        sigmas.append(sigma)
+        if sigma > thr:
+            W[off:off + d * d] = (A * (thr / sigma)).ravel()
+    return W, np.array(sigmas)
+
+
+# ---------------------------------------------------------------------------
+# one full training step
+# ---------------------------------------------------------------------------
+
+def branch_of(fwd: ForwardOut, W, cfg: Cfg):
+    V = View(W, cfg.d, cfg.h)
+    if cfg.slot_coord:
+        return fwd.signal + fwd.A + V.anchor[None, None]
+    return fwd.signal.copy()
+
+
+def train_step(S_in, targets, W, lm, cfg: Cfg, adam_state=None, step=1, lr=1e-3,
+               mstate=None):
+    """Forward -> LM-head CE -> adjoint -> weight grads -> Adam (DEQ core and LM head).
+
+    Returns a dict with every intermediate the GPU path is compared on.
+    """
+    B, T, d = S_in.shape
+    h = cfg.h
+    N = B * T
+    fwd = forward(S_in, W, cfg, mstate)
+    w_lm, b_lm, g_lm = lm
+    loss, dP, gW_lm, gb_lm, gg_lm = lm_head(fwd.pooled.reshape(N, d), np.asarray(targets).reshape(N),
+                                             w_lm, b_lm, g_lm)
+    br = branch_of(fwd, W, cfg).reshape(N, h, d)
+    V = View(W, d, h)
+    v, g_pre, pre, r_pre = adjoint(fwd.hstar.reshape(N, h, d), br, dP, V.NS, cfg)
+    G, dS = weight_grads(np.asarray(S_in, np.float64).reshape(N, d),
+                         fwd.signal.reshape(N, h, d), fwd.A.reshape(N, h, d), fwd.attn_cache,
+                         v, g_pre, pre, r_pre, W, cfg)
+    if adam_state is None:
+        adam_state = (np.zeros_like(G), np.zeros_like(G))
+    Wn, m1, m2 = adam(W, G, adam_state[0], adam_state[1], step, lr=lr)
+    lm_flat = np.concatenate([np.ravel(w_lm), np.ravel(b_lm), np.ravel(g_lm)]).astype(np.float64)
+    lm_g = np.concatenate([gW_lm.ravel(), gb_lm, gg_lm])
+    lm_new, _, _ = adam(lm_flat, lm_g, np.zeros_like(lm_g), np.zeros_like(lm_g), step, lr=lr)
+    return dict(fwd=fwd, loss=loss, dP=dP, v=v, g_pre=g_pre, grads=G, dS=dS, W_new=Wn,
+                adam=(m1, m2), lm_grads=lm_g, lm_new=lm_new)
