@@ -1,0 +1,365 @@
+// Backward of the AIDEEN slot block on sm_100a.
+//
+//   adjoint          fused clean Picard adjoint: all `iters` iterations of
+//                    v' = rhs + beta*J_norm^T v + (1-beta) v run on-chip, one
+//                    warp per (token, slot) entry and one CTA per token so the
+//                    optional Anderson mixing can form its per-token Gram
+//                    (staged_adjoint_picard_clean.wgsl:143-248, 1011-1135).
+//                    HBM traffic: pre + rhs in, v + g_pre out, once.
+//   source_grad      sum_s beta*J_norm^T v (picard_source_grad_reduce_main, :250-327)
+//   attn_bwd_scale   d(attn*scale)/d(attn, R) per entry
+//   attn_bwd_softmax per-token softmax / mean-subtracted mix backward
+//   dsig_init        dL/dsignal = g_pre + dL/dR * dR/dsrc
+//   colsum           column sums (bias / anchor / NormScale gradients)
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace aideen {
+
+template <int F, int MA>
+__global__ void __launch_bounds__(512) adjoint_kernel(AdjointArgs a) {
+  extern __shared__ float sm[];
+  float *gram = sm;                 // [2][6][16]
+  float *nsacc = sm + 2 * 6 * 16;   // [h][d] when nsg requested
+  const int n = blockIdx.x, s = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int d = a.d, h = a.h;
+  const float beta = a.beta;
+  const size_t e = ((size_t)n * h + s) * d;
+  float4 pre[F], rhs[F], ns[F], v[F];
+  float ss = 0.f;
+  const float ih = 1.f / (float)h;
+#pragma unroll
+  for (int f = 0; f < F; ++f) {
+    const int j = (f * 32 + lane) * 4;
+    pre[f] = ld4(a.pre_a + e + j);
+    if (a.pre_b) pre[f] = pre[f] + ld4(a.pre_b + e + j);
+    ns[f] = ld4(a.NS + j);
+    float4 r = f4(0.f);
+    if (a.rhs_tok) r = ih * ld4(a.rhs_tok + (size_t)n * d + j);
+    if (a.rhs_slot) r = r + ld4(a.rhs_slot + e + j);
+    rhs[f] = r;
+    v[f] = r;
+    ss += dot4(pre[f], pre[f]);
+  }
+  ss = warp_sum(ss);
+  const float rms = sqrtf(ss / (float)d + 1e-6f);
+  const float inv = 1.f / fmaxf(rms, 1e-6f);
+  const float den = fmaxf((float)d * rms * rms * rms, 1e-6f);
+  float4 hist[MA > 0 ? MA : 1][F];
+  for (int k = 0; k < a.iters; ++k) {
+    float c = 0.f;
+#pragma unroll
+    for (int f = 0; f < F; ++f) c += dot4((beta * v[f]) * ns[f], pre[f]);
+    const float cs = warp_sum(c) / den;
+#pragma unroll
+    for (int f = 0; f < F; ++f) {
+      const float4 up = beta * v[f];
+      const float4 ng = (inv * ns[f]) * up - cs * pre[f];
+      v[f] = rhs[f] + (ng + (1.f - beta) * v[f]);
+    }
+    if constexpr (MA > 0) {
+      // ring buffer as a shift register: hist[i] = iterate stored i steps ago
+#pragma unroll
+      for (int i = MA - 1; i > 0; --i)
+#pragma unroll
+        for (int f = 0; f < F; ++f) hist[i][f] = hist[i - 1][f];
+#pragma unroll
+      for (int f = 0; f < F; ++f) hist[0][f] = v[f];
+      const int n_res = k < MA - 1 ? k : MA - 1;
+      if (k >= 2 && n_res >= 2) {
+        // Gram of pseudo-residuals D_i = hist[i] - hist[i+1] over all h*d of the token
+        float g6[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int f = 0; f < F; ++f) {
+          const float4 d0 = hist[0][f] - hist[1][f];
+          const float4 d1 = hist[1][f] - hist[MA > 2 ? 2 : 1][f];
+          g6[0] += dot4(d0, d0);
+          g6[1] += dot4(d0, d1);
+          g6[3] += dot4(d1, d1);
+          if (MA > 3 && n_res == 3) {
+            const float4 d2 = hist[MA > 3 ? 2 : 1][f] - hist[MA > 3 ? 3 : 1][f];
+            g6[2] += dot4(d0, d2);
+            g6[4] += dot4(d1, d2);
+            g6[5] += dot4(d2, d2);
+          }
+        }
+        float *buf = gram + (k & 1) * 96;
+#pragma unroll
+        for (int q = 0; q < 6; ++q) {
+          const float x = warp_sum(g6[q]);
+          if (lane == 0) buf[q * 16 + s] = x;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < 6; ++q) {
+          float t = 0.f;
+          for (int w = 0; w < h; ++w) t += buf[q * 16 + w];
+          g6[q] = t;
+        }
+        float b0, b1, b2 = 0.f;
+        if (n_res == 2) {
+          float g00 = g6[0], g01 = g6[1], g10 = g6[1], g11 = g6[3];
+          const float reg = fmaxf(1e-8f, 1e-4f * (fabsf(g00) + fabsf(g11)));
+          g00 += reg;
+          g11 += reg;
+          const float det = g00 * g11 - g01 * g10;
+          const float sdet = det < 0.f ? fminf(det, -1e-10f) : fmaxf(det, 1e-10f);
+          b0 = (g11 - g01) / sdet;
+          b1 = (g00 - g10) / sdet;
+        } else {
+          float g00 = g6[0], g01 = g6[1], g02 = g6[2];
+          float g10 = g6[1], g11 = g6[3], g12 = g6[4];
+          float g20 = g6[2], g21 = g6[4], g22 = g6[5];
+          const float reg = fmaxf(1e-8f, 1e-4f * (fabsf(g00) + fabsf(g11) + fabsf(g22)));
+          g00 += reg;
+          g11 += reg;
+          g22 += reg;
+          const float det = g00 * (g11 * g22 - g12 * g21) - g01 * (g10 * g22 - g12 * g20) +
+                            g02 * (g10 * g21 - g11 * g20);
+          const float sdet = det < 0.f ? fminf(det, -1e-8f) : fmaxf(det, 1e-8f);
+          b0 = ((g11 * g22 - g12 * g21) - g01 * (g22 - g12) + g02 * (g21 - g11)) / sdet;
+          b1 = (g00 * (g22 - g12) - (g10 * g22 - g12 * g20) + g02 * (g10 - g20)) / sdet;
+          b2 = (g00 * (g11 - g21) - g01 * (g10 - g20) + (g10 * g21 - g11 * g20)) / sdet;
+        }
+        b0 = fminf(fmaxf(b0, -2.f), 3.f);
+        b1 = fminf(fmaxf(b1, -2.f), 3.f);
+        if (n_res == 3) b2 = fminf(fmaxf(b2, -2.f), 3.f);
+        const float ssum = b0 + b1 + (n_res == 3 ? b2 : 0.f);
+        if (fabsf(ssum) < 1e-6f) {
+          b0 = 1.f; b1 = 0.f; b2 = 0.f;
+        } else {
+          b0 /= ssum; b1 /= ssum; b2 = n_res == 3 ? b2 / ssum : 0.f;
+        }
+#pragma unroll
+        for (int f = 0; f < F; ++f) {
+          float4 mixed = b0 * hist[0][f] + b1 * hist[1][f];
+          if (MA > 3 && n_res == 3) mixed = mixed + b2 * hist[MA > 3 ? 2 : 1][f];
+          v[f] = mixed;
+        }
+      }
+    }
+  }
+  float c = 0.f;
+#pragma unroll
+  for (int f = 0; f < F; ++f) c += dot4((beta * v[f]) * ns[f], pre[f]);
+  const float cs = warp_sum(c) / den;
+  const size_t vbase = ((size_t)s * a.N + n) * d;
+#pragma unroll
+  for (int f = 0; f < F; ++f) {
+    const int j = (f * 32 + lane) * 4;
+    const float4 up = beta * v[f];
+    st4(a.v + vbase + j, v[f]);
+    st4(a.gpre + e + j, (inv * ns[f]) * up - cs * pre[f]);
+    if (a.nsg) st4(nsacc + (size_t)s * d + j, (inv * up) * pre[f]);
+  }
+  if (a.nsg) {
+    __syncthreads();
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+      float t = 0.f;
+      for (int q = 0; q < h; ++q) t += nsacc[(size_t)q * d + j];
+      a.nsg[(size_t)n * d + j] = t;
+    }
+  }
+}
+
+template <int F, int MA>
+static cudaError_t adjoint_launch(const AdjointArgs &a, size_t smem, cudaStream_t st) {
+  auto k = adjoint_kernel<F, MA>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  k<<<a.N, 32 * a.h, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int F>
+static cudaError_t adjoint_dispatch_m(const AdjointArgs &a, cudaStream_t st) {
+  const size_t smem = (2 * 6 * 16 + (a.nsg ? (size_t)a.h * a.d : 0)) * sizeof(float);
+  const int ma = a.anderson_m <= 2 ? 0 : a.anderson_m;  // m <= 2 never mixes (n_res < 2)
+  switch (ma) {
+    case 0: return adjoint_launch<F, 0>(a, smem, st);
+    case 3: return adjoint_launch<F, 3>(a, smem, st);
+    case 4: return adjoint_launch<F, 4>(a, smem, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_adjoint(const AdjointArgs &a, cudaStream_t st) {
+  if (a.N <= 0) return cudaSuccess;
+  switch (a.d) {
+    case 128: return adjoint_dispatch_m<1>(a, st);
+    case 256: return adjoint_dispatch_m<2>(a, st);
+    case 512: return adjoint_dispatch_m<4>(a, st);
+    case 1024: return adjoint_dispatch_m<8>(a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+__global__ void source_grad_kernel(const float *__restrict__ gpre, float *__restrict__ out, int h,
+                                   int d) {
+  const int n = blockIdx.x;
+  for (int j = threadIdx.x * 4; j < d; j += blockDim.x * 4) {
+    float4 acc = f4(0.f);
+    for (int s = 0; s < h; ++s) acc = acc + ld4(gpre + ((size_t)n * h + s) * d + j);
+    st4(out + (size_t)n * d + j, acc);
+  }
+}
+
+cudaError_t launch_source_grad(const float *gpre, float *out, int N, int h, int d, cudaStream_t st) {
+  if (N <= 0) return cudaSuccess;
+  source_grad_kernel<<<N, d / 4, 0, st>>>(gpre, out, h, d);
+  return cudaGetLastError();
+}
+
+// One warp per (token, slot): backward of A = attn * max(R,1e-3)/max(rho,1e-6).
+__global__ void attn_bwd_scale_kernel(AttnBwdArgs a, int rows) {
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= rows) return;
+  const int d = a.d;
+  const float *gA = a.gpre + (size_t)w * d;
+  const float *am = a.amat + (size_t)w * d;
+  float ds = 0.f;
+  for (int j = lane * 4; j < d; j += 128) ds += dot4(ld4(gA + j), ld4(am + j));
+  ds = warp_sum(ds);
+  const float sc = a.scale[w], rho = a.rho[w], R = a.Rsrc[w];
+  const float rhoc = fmaxf(rho, 1e-6f);
+  const float drho = rho > 1e-6f ? -ds * sc / rhoc : 0.f;
+  const float ca = drho / ((float)d * rho);
+  for (int j = lane * 4; j < d; j += 128)
+    st4(a.da + (size_t)w * d + j, sc * ld4(gA + j) + ca * ld4(am + j));
+  if (lane == 0) {
+    const float dR = R > 1e-3f ? ds / rhoc : 0.f;
+    a.dRc[w] = dR / ((float)d * R);
+  }
+}
+
+cudaError_t launch_attn_bwd_scale(const AttnBwdArgs &a, int rows, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  attn_bwd_scale_kernel<<<(rows + 7) / 8, 256, 0, st>>>(a, rows);
+  return cudaGetLastError();
+}
+
+// One block per token, warp per slot.  From dn (grad of the normalised mix)
+// to dQ, dK, dV of the 32-wide head.
+__global__ void attn_bwd_softmax_kernel(AttnBwdArgs a) {
+  __shared__ float Ks[16][33], Qs[16][33], Vs[16][33], dmix[16][33], al[16][17], dlg[16][17];
+  const int n = blockIdx.x, s = threadIdx.x >> 5, c = threadIdx.x & 31;
+  const int h = a.h, d = a.d;
+  const size_t row = ((size_t)n * h + s) * kHeadDim + c;
+  Ks[s][c] = a.Kh[row] + a.W[a.off_kb + (size_t)s * d + c];
+  Qs[s][c] = a.Qh[row] + a.W[a.off_qb + (size_t)s * d + c];
+  Vs[s][c] = a.Vh[row];
+  if (c < h) al[s][c] = a.alpha[((size_t)n * h + s) * h + c];
+  const float nn = a.nmix[row], dnn = a.dn[row], r = a.rmix[(size_t)n * h + s];
+  const float ndn = warp_sum(nn * dnn);
+  dmix[s][c] = (dnn - nn * ndn / (float)kHeadDim) / r;
+  __syncthreads();
+  // query slot s: dalpha, softmax backward, dQ
+  float dal[16];
+  float adot = 0.f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k)
+    if (k < h) {
+      dal[k] = warp_sum(dmix[s][c] * Vs[k][c]);
+      adot += al[s][k] * dal[k];
+    }
+  const float gain = 2.0f * rsqrtf((float)kHeadDim);
+  float dq = 0.f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k)
+    if (k < h) {
+      const float dl = al[s][k] * (dal[k] - adot);
+      dq += dl * Ks[k][c];
+      if (c == 0) dlg[s][k] = dl;
+    }
+  a.dQ[row] = gain * dq;
+  __syncthreads();
+  // key/value slot s
+  float dk = 0.f, dv = 0.f;
+  const float ih = 1.f / (float)h;
+  for (int q = 0; q < h; ++q) {
+    dk += dlg[q][s] * Qs[q][c];
+    dv += (al[q][s] - ih) * dmix[q][c];
+  }
+  a.dK[row] = gain * dk;
+  a.dV[row] = dv;
+}
+
+cudaError_t launch_attn_bwd_softmax(const AttnBwdArgs &a, int N, cudaStream_t st) {
+  if (N <= 0) return cudaSuccess;
+  attn_bwd_softmax_kernel<<<N, 32 * a.h, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+__global__ void dsig_init_kernel(AttnBwdArgs a, float *__restrict__ dsig, int rows, int slot_coord) {
+  const size_t total4 = (size_t)rows * a.d / 4;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total4;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t idx = i * 4;
+    const size_t w = idx / a.d;
+    const int j = (int)(idx % a.d);
+    float4 g = ld4(a.gpre + idx);
+    if (slot_coord) {
+      const int s = (int)(w % a.h);
+      const float4 src = ld4(a.signal + idx) + ld4(a.W + a.off_anchor + (size_t)s * a.d + j);
+      g = g + a.dRc[w] * src;
+    }
+    st4(dsig + idx, g);
+  }
+}
+
+static int grid_for(size_t n4) {
+  size_t blocks = (n4 + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  return blocks < 1 ? 1 : (int)blocks;
+}
+
+cudaError_t launch_dsig_init(const AttnBwdArgs &a, float *dsig, int rows, int slot_coord,
+                             cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  dsig_init_kernel<<<grid_for((size_t)rows * a.d / 4), 256, 0, st>>>(a, dsig, rows, slot_coord);
+  return cudaGetLastError();
+}
+
+__global__ void add_kernel(float *__restrict__ dst, const float *__restrict__ x,
+                           const float *__restrict__ y, size_t n4) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+       i += (size_t)gridDim.x * blockDim.x)
+    st4(dst + 4 * i, ld4(x + 4 * i) + ld4(y + 4 * i));
+}
+
+cudaError_t launch_add(float *dst, const float *a, const float *b, size_t n, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  add_kernel<<<grid_for(n / 4), 256, 0, st>>>(dst, a, b, n / 4);
+  return cudaGetLastError();
+}
+
+__global__ void colsum_kernel(const float *__restrict__ X, int rows, int ncols, long ld,
+                              float *__restrict__ out, int seg, long ostride, int accumulate) {
+  __shared__ float red[32][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + tx;
+  float acc = 0.f;
+  if (c < ncols)
+    for (int r = ty; r < rows; r += 32) acc += X[(size_t)r * ld + c];
+  red[ty][tx] = acc;
+  __syncthreads();
+  if (ty == 0 && c < ncols) {
+    float t = 0.f;
+    for (int q = 0; q < 32; ++q) t += red[q][tx];
+    const long o = (long)(c / seg) * ostride + (c % seg);
+    out[o] = accumulate ? out[o] + t : t;
+  }
+}
+
+cudaError_t launch_colsum(const float *X, int rows, int ncols, long ld, float *out, int seg,
+                          long ostride, bool accumulate, cudaStream_t st) {
+  if (ncols <= 0) return cudaSuccess;
+  colsum_kernel<<<(ncols + 31) / 32, 1024, 0, st>>>(X, rows, ncols, ld, out, seg, ostride,
+                                                     accumulate ? 1 : 0);
+  return cudaGetLastError();
+}
+
+}  // namespace aideen

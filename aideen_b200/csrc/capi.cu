@@ -1,0 +1,767 @@
+// C ABI of libaideen_b200: context lifetime, buffer ownership and the
+// orchestration of one training step.  Mirrors the reference's
+// GpuDeqBackend (aideen-backbone/src/gpu_deq.rs:80-218) call sequence:
+// forward (:3855) -> LM head (lm_train.wgsl) -> clean adjoint (:4736) ->
+// fused weight gradients + update (:4980) -> spectral renorm (:5568).
+#include <cublas_v2.h>
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <thread>
+
+#include "../../include/aideen_b200.h"
+#include "kernels.cuh"
+
+using namespace aideen;
+
+namespace {
+
+struct DevBufs {
+  float *W = nullptr, *G = nullptr, *M1 = nullptr, *M2 = nullptr;
+  float *S_in = nullptr;
+  int32_t *tokens = nullptr, *targets = nullptr;
+  float *signal = nullptr, *A = nullptr, *amat = nullptr;
+  float *Qh = nullptr, *Kh = nullptr, *Vh = nullptr, *alpha = nullptr, *nmix = nullptr,
+        *rmix = nullptr, *scale = nullptr, *rho = nullptr, *Rsrc = nullptr;
+  float *hstar = nullptr, *pre = nullptr, *pooled = nullptr, *hist = nullptr, *fpmctx = nullptr,
+        *mstate = nullptr;
+  int32_t *iters = nullptr;
+  float *v = nullptr, *gpre = nullptr, *dl_dh = nullptr, *rhs_slot = nullptr, *nsg = nullptr;
+  float *da = nullptr, *dn = nullptr, *dQ = nullptr, *dK = nullptr, *dV = nullptr,
+        *dsig = nullptr, *dRc = nullptr, *dS = nullptr;
+  float *lmp = nullptr, *Glm = nullptr, *Mlm1 = nullptr, *Mlm2 = nullptr;  // [V*d | V | d]
+  float *y = nullptr, *lrms = nullptr, *logits = nullptr, *dy = nullptr, *ggp = nullptr,
+        *loss_rows = nullptr, *scal = nullptr;  // scal: [n_active, loss]
+  float *emb = nullptr;
+  unsigned long long *stats = nullptr;
+  float *sigmas = nullptr;
+};
+
+}  // namespace
+
+struct aideen_ctx {
+  aideen_cfg cfg{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  cublasHandle_t cublas = nullptr;
+  ncclComm_t comm = nullptr;
+  int nranks = 1, rank = 0;
+  std::string err;
+  unsigned long long launches = 0;
+  size_t W_len = 0, lm_len = 0, max_tokens = 0;
+  float signal_scale = 1.f;
+  bool signal_zero = false;
+  aideen_run last_run{};
+  uint32_t N = 0;         // tokens of the last forward (B*T)
+  uint32_t adj_N = 0;     // tokens of the last adjoint
+  float adj_beta = 0.85f;
+  bool lm_ready = false, emb_ready = false;
+  DevBufs b;
+  Layout L{128, 1};
+};
+
+namespace {
+
+int set_err(aideen_ctx *c, int code, const std::string &msg) {
+  if (c) c->err = msg;
+  return code;
+}
+
+#define CU(expr)                                                                       \
+  do {                                                                                 \
+    cudaError_t _e = (expr);                                                           \
+    if (_e != cudaSuccess)                                                             \
+      return set_err(ctx, AIDEEN_E_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
+  } while (0)
+// A launch of one of this library's kernels.
+#define KL(expr)                                                                       \
+  do {                                                                                 \
+    ctx->launches++;                                                                   \
+    cudaError_t _e = (expr);                                                           \
+    if (_e != cudaSuccess)                                                             \
+      return set_err(ctx, AIDEEN_E_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
+  } while (0)
+#define CB(expr)                                                                       \
+  do {                                                                                 \
+    cublasStatus_t _s = (expr);                                                        \
+    if (_s != CUBLAS_STATUS_SUCCESS)                                                   \
+      return set_err(ctx, AIDEEN_E_CUDA, std::string(#expr) + ": cublas status " + std::to_string((int)_s)); \
+  } while (0)
+#define CHK(expr)                  \
+  do {                             \
+    int _r = (expr);               \
+    if (_r != AIDEEN_OK) return _r; \
+  } while (0)
+
+template <typename T>
+cudaError_t dalloc(T **p, size_t n) {
+  if (n == 0) n = 1;
+  return cudaMalloc((void **)p, n * sizeof(T));
+}
+
+int copy_in(aideen_ctx *ctx, void *dst, const void *src, size_t bytes, int where) {
+  if (bytes == 0) return AIDEEN_OK;
+  if (!src) return set_err(ctx, AIDEEN_E_INVALID, "null input pointer");
+  CU(cudaMemcpyAsync(dst, src, bytes,
+                     where == AIDEEN_DEVICE ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                     ctx->stream));
+  return AIDEEN_OK;
+}
+
+GemmArgs gemm(int M, int N, int K, int batch, const float *A, long lda, long sA, bool tA,
+              const float *B, long ldb, long sB, bool tB, float *C, long ldc, long sC,
+              float alpha = 1.f, float beta = 0.f, const float *abias = nullptr, long sbias = 0) {
+  GemmArgs g;
+  g.M = M; g.N = N; g.K = K; g.batch = batch;
+  g.A = A; g.lda = lda; g.strideA = sA; g.transA = tA;
+  g.B = B; g.ldb = ldb; g.strideB = sB; g.transB = tB;
+  g.C = C; g.ldc = ldc; g.strideC = sC;
+  g.alpha = alpha; g.beta = beta; g.abias = abias; g.strideAbias = sbias;
+  return g;
+}
+
+int check_run(aideen_ctx *ctx, const aideen_run *r) {
+  if (!r) return set_err(ctx, AIDEEN_E_INVALID, "null run");
+  if (r->batch == 0 || r->seq_len == 0 || r->batch > ctx->cfg.max_batch ||
+      r->seq_len > ctx->cfg.max_seq_len)
+    return set_err(ctx, AIDEEN_E_INVALID, "batch/seq_len outside the context caps");
+  if (r->max_iters == 0) return set_err(ctx, AIDEEN_E_INVALID, "max_iters must be >= 1");
+  return AIDEEN_OK;
+}
+
+// Everything after S_in is resident: projection, slot attention, Picard, pool.
+int run_forward(aideen_ctx *ctx, const aideen_run *r, aideen_stats *stats) {
+  const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
+  const int N = r->batch * r->seq_len;
+  const Layout &L = ctx->L;
+  DevBufs &b = ctx->b;
+  cudaStream_t st = ctx->stream;
+  const float *W = b.W;
+  if (ctx->signal_zero) {
+    CU(cudaMemsetAsync(b.signal, 0, (size_t)N * h * d * sizeof(float), st));
+  } else {
+    // signal[n][s][:] = sigma * S_in[n] . W_in[s]   (deq_slot_attn_unified_clean.wgsl:762-804)
+    KL(gemm_f32(gemm(N, d, d, h, b.S_in, d, 0, false, W + L.win, d, (long)d * d, false, b.signal,
+                     (long)h * d, d, ctx->signal_scale), st));
+  }
+  if (r->slot_coord) {
+    // 32-wide K/V/Q heads of src = signal + anchor (:281-355)
+    KL(gemm_f32(gemm(N, kHeadDim, d, h, b.signal, (long)h * d, d, false, W + L.wk, d, (long)d * d,
+                     false, b.Kh, (long)h * kHeadDim, kHeadDim, 1.f, 0.f, W + L.slot_anchor, d), st));
+    KL(gemm_f32(gemm(N, kHeadDim, d, h, b.signal, (long)h * d, d, false, W + L.wv, d, (long)d * d,
+                     false, b.Vh, (long)h * kHeadDim, kHeadDim, 1.f, 0.f, W + L.slot_anchor, d), st));
+    KL(gemm_f32(gemm(N, kHeadDim, d, h, b.signal, (long)h * d, d, false, W + L.wq, d, (long)d * d,
+                     false, b.Qh, (long)h * kHeadDim, kHeadDim, 1.f, 0.f, W + L.slot_anchor, d), st));
+    AttnArgs a{};
+    a.h = h; a.d = d; a.W = W; a.off_qb = L.q_bias; a.off_kb = L.k_bias; a.off_anchor = L.slot_anchor;
+    a.Qh = b.Qh; a.Kh = b.Kh; a.Vh = b.Vh; a.alpha = b.alpha; a.nmix = b.nmix; a.rmix = b.rmix;
+    a.signal = b.signal; a.amat = b.amat; a.A = b.A; a.scale = b.scale; a.rho = b.rho; a.Rsrc = b.Rsrc;
+    KL(launch_attn_softmax(a, N, st));
+    // attn[o] = sum_k W_o[s][k*d + o] n[k]  (:452-470)
+    KL(gemm_f32(gemm(N, d, kHeadDim, h, b.nmix, (long)h * kHeadDim, kHeadDim, false, W + L.wo, d,
+                     (long)d * d, false, b.amat, (long)h * d, d), st));
+    KL(launch_attn_scale(a, N * h, st));
+  }
+  if (!r->fpm) CU(cudaMemsetAsync(b.hist, 0, (size_t)N * h * d * sizeof(float), st));
+  PicardArgs p{};
+  p.B = r->batch; p.T = r->seq_len; p.h = h; p.d = d; p.max_iters = r->max_iters;
+  p.slot_coord = r->slot_coord ? 1 : 0;
+  p.eps = r->epsilon; p.blend = r->fpm ? 0.2f : r->damping;
+  p.alpha_m = r->fpm_alpha_m; p.tau = r->fpm_tau; p.gate_min = r->fpm_read_gate_min;
+  p.W = W;
+  p.off_ns = L.nscale; p.off_anchor = L.slot_anchor; p.off_hscale = L.hist_scale;
+  p.off_hbias = L.hist_bias; p.off_wkm = L.w_k_mem; p.off_wqm = L.w_q_mem; p.off_bread = L.b_read_mem;
+  p.off_wgate = L.w_write_gate; p.off_bwrite = L.b_write_mem; p.off_wkw = L.w_k_write;
+  p.off_wvw = L.w_v_write; p.off_bdelta = L.b_delta; p.off_wup = L.w_retain_up;
+  p.off_wdown = L.w_retain_down; p.off_bret = L.b_retain; p.off_alog = L.alog; p.off_wx = L.wx;
+  p.signal = b.signal; p.A = b.A;
+  p.hstar = b.hstar; p.pre = b.pre; p.hist = b.hist; p.fpmctx = b.fpmctx; p.mstate = b.mstate;
+  p.iters = b.iters;
+  KL(launch_picard(p, r->fpm != 0, st));
+  KL(launch_pool_rmsnorm(b.hstar, ctx->lm_ready ? b.lmp + (size_t)ctx->cfg.vocab * d + ctx->cfg.vocab : nullptr,
+                         b.pooled, ctx->lm_ready ? b.y : nullptr, b.lrms, N, h, d, st));
+  ctx->last_run = *r;
+  ctx->N = N;
+  if (stats) {
+    CU(cudaMemsetAsync(b.stats, 0, 4 * sizeof(unsigned long long), st));
+    KL(launch_solve_stats(b.iters, b.hstar, N * h, d, r->max_iters, b.stats, st));
+    unsigned long long hs[4];
+    CU(cudaMemcpyAsync(hs, b.stats, sizeof(hs), cudaMemcpyDeviceToHost, st));
+    CU(cudaStreamSynchronize(st));
+    stats->total_iters = hs[0];
+    stats->max_iters_seen = (uint32_t)hs[1];
+    stats->unconverged = (uint32_t)hs[2];
+    stats->nonfinite = (uint32_t)hs[3];
+    stats->solves = (uint32_t)(N * h);
+  }
+  return AIDEEN_OK;
+}
+
+int run_lm_head(aideen_ctx *ctx, int N, float *loss_out) {
+  if (!ctx->lm_ready) return set_err(ctx, AIDEEN_E_INVALID, "LM head not uploaded");
+  const int d = ctx->cfg.d_model, V = ctx->cfg.vocab;
+  DevBufs &b = ctx->b;
+  cudaStream_t st = ctx->stream;
+  const float *Wlm = b.lmp, *glm = b.lmp + (size_t)V * d + V;
+  const float one = 1.f, zero = 0.f;
+  KL(launch_count_active(b.targets, N, b.scal, st));
+  // logits^T (V x N, col-major) = W_lm (d x V col-major)^T . y (d x N col-major); then + b_lm
+  CB(cublasSgemm(ctx->cublas, CUBLAS_OP_T, CUBLAS_OP_N, V, N, d, &one, Wlm, d, b.y, d, &zero,
+                 b.logits, V));
+  KL(launch_softmax_ce(b.logits, b.lmp + (size_t)V * d, b.targets, b.scal, N, V, b.loss_rows, st));
+  KL(launch_sum(b.loss_rows, N, b.scal + 1, st));
+  // dy (d x N col-major) = W_lm (d x V) . dlog (V x N)
+  CB(cublasSgemm(ctx->cublas, CUBLAS_OP_N, CUBLAS_OP_N, d, N, V, &one, Wlm, d, b.logits, V, &zero,
+                 b.dy, d));
+  // dW_lm^T (d x V col-major) = y (d x N) . dlog^T (N x V)
+  CB(cublasSgemm(ctx->cublas, CUBLAS_OP_N, CUBLAS_OP_T, d, V, N, &one, b.y, d, b.logits, V, &zero,
+                 b.Glm, d));
+  KL(launch_colsum(b.logits, N, V, V, b.Glm + (size_t)V * d, V, 0, false, st));
+  KL(launch_rmsnorm_bwd(b.dy, b.pooled, b.lrms, glm, b.dl_dh, b.ggp, N, d, st));
+  KL(launch_colsum(b.ggp, N, d, d, b.Glm + (size_t)V * d + V, d, 0, false, st));
+  if (loss_out) {
+    CU(cudaMemcpyAsync(loss_out, b.scal + 1, sizeof(float), cudaMemcpyDeviceToHost, st));
+    CU(cudaStreamSynchronize(st));
+  }
+  return AIDEEN_OK;
+}
+
+int run_adjoint(aideen_ctx *ctx, int N, const float *pre_a, const float *pre_b,
+                const float *rhs_tok, const float *rhs_slot, uint32_t iters, float beta,
+                uint32_t anderson_m) {
+  if (anderson_m > 4) return set_err(ctx, AIDEEN_E_UNSUPPORTED, "anderson_m > 4");
+  AdjointArgs a{};
+  a.N = N; a.h = ctx->cfg.h_slots; a.d = ctx->cfg.d_model; a.iters = iters;
+  a.anderson_m = anderson_m; a.beta = beta;
+  a.pre_a = pre_a; a.pre_b = pre_b; a.rhs_tok = rhs_tok; a.rhs_slot = rhs_slot;
+  a.NS = ctx->b.W + ctx->L.nscale; a.v = ctx->b.v; a.gpre = ctx->b.gpre; a.nsg = ctx->b.nsg;
+  KL(launch_adjoint(a, ctx->stream));
+  ctx->adj_N = N;
+  ctx->adj_beta = beta;
+  return AIDEEN_OK;
+}
+
+int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
+  const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
+  const int N = ctx->N;
+  if (N == 0 || ctx->adj_N != ctx->N)
+    return set_err(ctx, AIDEEN_E_INVALID, "weight grads need a forward and an adjoint over the same tokens");
+  const Layout &L = ctx->L;
+  DevBufs &b = ctx->b;
+  cudaStream_t st = ctx->stream;
+  const float *W = b.W;
+  float *G = b.G;
+  const bool sc = ctx->last_run.slot_coord != 0;
+  const int H32 = h * kHeadDim;
+  CU(cudaMemsetAsync(G, 0, ctx->W_len * sizeof(float), st));
+  KL(launch_colsum(b.nsg, N, d, d, G + L.nscale, d, 0, false, st));
+  AttnBwdArgs a{};
+  a.h = h; a.d = d; a.W = W; a.off_qb = L.q_bias; a.off_kb = L.k_bias; a.off_anchor = L.slot_anchor;
+  a.gpre = b.gpre; a.amat = b.amat; a.scale = b.scale; a.rho = b.rho; a.Rsrc = b.Rsrc;
+  a.signal = b.signal; a.da = b.da; a.dRc = b.dRc; a.dn = b.dn; a.nmix = b.nmix; a.rmix = b.rmix;
+  a.alpha = b.alpha; a.Qh = b.Qh; a.Kh = b.Kh; a.Vh = b.Vh; a.dQ = b.dQ; a.dK = b.dK; a.dV = b.dV;
+  if (sc) {
+    KL(launch_attn_bwd_scale(a, N * h, st));
+    // dn[n][s][c] = sum_o da[n][s][o] W_o[s][c*d + o]
+    KL(gemm_f32(gemm(N, kHeadDim, d, h, b.da, (long)h * d, d, false, W + L.wo, d, (long)d * d, true,
+                     b.dn, H32, kHeadDim), st));
+    // gW_o[s][c][o] = sum_n n[n][s][c] da[n][s][o]
+    KL(gemm_f32(gemm(kHeadDim, d, N, h, b.nmix, H32, kHeadDim, true, b.da, (long)h * d, d, false,
+                     G + L.wo, d, (long)d * d), st));
+    KL(launch_attn_bwd_softmax(a, N, st));
+    // gW_{q,k,v}[s][j][c] = sum_n src[n][s][j] d{Q,K,V}[n][s][c]
+    const float *dqkv[3] = {b.dQ, b.dK, b.dV};
+    const size_t woff[3] = {L.wq, L.wk, L.wv};
+    for (int i = 0; i < 3; ++i)
+      KL(gemm_f32(gemm(d, kHeadDim, N, h, b.signal, (long)h * d, d, true, dqkv[i], H32, kHeadDim,
+                       false, G + woff[i], d, (long)d * d, 1.f, 0.f, W + L.slot_anchor, d), st));
+    KL(launch_dsig_init(a, b.dsig, N * h, 1, st));
+    // dsrc[n][s][j] += sum_c d{Q,K,V}[n][s][c] W[s][j*d + c]
+    for (int i = 0; i < 3; ++i)
+      KL(gemm_f32(gemm(N, d, kHeadDim, h, dqkv[i], H32, kHeadDim, false, W + woff[i], d, (long)d * d,
+                       true, b.dsig, (long)h * d, d, 1.f, 1.f), st));
+    KL(launch_colsum(b.dQ, N, H32, H32, G + L.q_bias, kHeadDim, d, false, st));
+    KL(launch_colsum(b.dK, N, H32, H32, G + L.k_bias, kHeadDim, d, false, st));
+    KL(launch_colsum(b.dsig, N, h * d, (long)h * d, G + L.slot_anchor, h * d, 0, false, st));
+  } else {
+    KL(launch_dsig_init(a, b.dsig, N * h, 0, st));
+  }
+  if (!ctx->signal_zero) {
+    // gW_in[s][j][o] = sigma * sum_n S_in[n][j] dsig[n][s][o]
+    KL(gemm_f32(gemm(d, d, N, h, b.S_in, d, 0, true, b.dsig, (long)h * d, d, false, G + L.win, d,
+                     (long)d * d, ctx->signal_scale), st));
+    if (want_ds) {
+      for (int s = 0; s < h; ++s)
+        KL(gemm_f32(gemm(N, d, d, 1, b.dsig + (size_t)s * d, (long)h * d, 0, false,
+                         W + L.win + (size_t)s * d * d, d, 0, true, b.dS, d, 0, ctx->signal_scale,
+                         s == 0 ? 0.f : 1.f), st));
+    }
+  } else if (want_ds) {
+    CU(cudaMemsetAsync(b.dS, 0, (size_t)N * d * sizeof(float), st));
+  }
+  return AIDEEN_OK;
+}
+
+int run_allreduce(aideen_ctx *ctx, int timeout_ms) {
+  if (!ctx->comm || ctx->nranks <= 1) return AIDEEN_OK;
+  ncclResult_t r = ncclGroupStart();
+  if (r == ncclSuccess)
+    r = ncclAllReduce(ctx->b.G, ctx->b.G, ctx->W_len, ncclFloat, ncclSum, ctx->comm, ctx->stream);
+  if (r == ncclSuccess && ctx->lm_ready)
+    r = ncclAllReduce(ctx->b.Glm, ctx->b.Glm, ctx->lm_len, ncclFloat, ncclSum, ctx->comm, ctx->stream);
+  ncclResult_t r2 = ncclGroupEnd();
+  if (r != ncclSuccess || r2 != ncclSuccess)
+    return set_err(ctx, AIDEEN_E_NCCL, std::string("ncclAllReduce: ") +
+                                           ncclGetErrorString(r != ncclSuccess ? r : r2));
+  if (timeout_ms <= 0) return AIDEEN_OK;  // stream-ordered, no host wait
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    cudaError_t q = cudaStreamQuery(ctx->stream);
+    if (q == cudaSuccess) return AIDEEN_OK;
+    if (q != cudaErrorNotReady) CU(q);
+    ncclResult_t ae = ncclSuccess;
+    ncclCommGetAsyncError(ctx->comm, &ae);
+    if (ae != ncclSuccess && ae != ncclInProgress) {
+      ncclCommAbort(ctx->comm);
+      ctx->comm = nullptr;
+      return set_err(ctx, AIDEEN_E_NCCL, std::string("async NCCL error: ") + ncclGetErrorString(ae));
+    }
+    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) {
+      ncclCommAbort(ctx->comm);
+      ctx->comm = nullptr;
+      return set_err(ctx, AIDEEN_E_TIMEOUT, "gradient allreduce did not finish in time; communicator aborted");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+int run_update(aideen_ctx *ctx, const aideen_update *u) {
+  if (!u) return set_err(ctx, AIDEEN_E_INVALID, "null update");
+  if (u->allreduce) CHK(run_allreduce(ctx, 0));
+  DevBufs &b = ctx->b;
+  cudaStream_t st = ctx->stream;
+  if (u->rule == AIDEEN_RULE_ADAM) {
+    const double t = u->step < 1 ? 1.0 : (double)u->step;
+    const float bc1 = (float)(1.0 - std::pow((double)u->beta1, t));
+    const float bc2 = (float)(1.0 - std::pow((double)u->beta2, t));
+    KL(launch_adam(b.W, b.G, b.M1, b.M2, ctx->W_len, u->lr, u->beta1, u->beta2, u->eps, bc1, bc2,
+                   u->grad_scale, st));
+    if (u->update_lm_head && ctx->lm_ready)
+      KL(launch_adam(b.lmp, b.Glm, b.Mlm1, b.Mlm2, ctx->lm_len, u->lr, u->beta1, u->beta2, u->eps,
+                     bc1, bc2, u->grad_scale, st));
+  } else if (u->rule == AIDEEN_RULE_CLIPPED_SGD) {
+    KL(launch_clipped_sgd(b.W, b.G, ctx->W_len, ctx->L.hist, u->lr, u->weight_decay, u->grad_scale, st));
+    if (u->update_lm_head && ctx->lm_ready)
+      KL(launch_clipped_sgd(b.lmp, b.Glm, ctx->lm_len, ctx->lm_len, u->lr, u->weight_decay,
+                            u->grad_scale, st));
+  } else {
+    return set_err(ctx, AIDEEN_E_INVALID, "unknown update rule");
+  }
+  return AIDEEN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t aideen_all_weights_len(uint32_t d, uint32_t h) { return Layout(d, h).total; }
+
+const char *aideen_last_error(const aideen_ctx *ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+uint64_t aideen_launch_count(const aideen_ctx *ctx) { return ctx ? ctx->launches : 0; }
+
+aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
+  auto fail = [&](int code) -> aideen_ctx * {
+    if (status) *status = code;
+    return nullptr;
+  };
+  if (!cfg) return fail(AIDEEN_E_INVALID);
+  const uint32_t d = cfg->d_model, h = cfg->h_slots;
+  if (!(d == 128 || d == 256 || d == 512 || d == 1024) || h < 1 || h > 16 || cfg->max_batch == 0 ||
+      cfg->max_seq_len == 0)
+    return fail(AIDEEN_E_INVALID);
+  if (cudaSetDevice(device) != cudaSuccess) return fail(AIDEEN_E_CUDA);
+  aideen_ctx *ctx = new aideen_ctx();
+  ctx->cfg = *cfg;
+  ctx->device = device;
+  ctx->L = Layout(d, h);
+  ctx->W_len = ctx->L.total;
+  const size_t N = (size_t)cfg->max_batch * cfg->max_seq_len;
+  ctx->max_tokens = N;
+  const size_t V = cfg->vocab;
+  ctx->lm_len = V ? V * d + V + d : 0;
+  DevBufs &b = ctx->b;
+  const size_t Nhd = N * h * d, NH32 = N * h * kHeadDim;
+  cudaError_t e = cudaSuccess;
+  auto A = [&](auto **p, size_t n) { if (e == cudaSuccess) e = dalloc(p, n); };
+  A(&b.W, ctx->W_len); A(&b.G, ctx->W_len); A(&b.M1, ctx->W_len); A(&b.M2, ctx->W_len);
+  A(&b.S_in, N * d); A(&b.tokens, N); A(&b.targets, N);
+  A(&b.signal, Nhd); A(&b.A, Nhd); A(&b.amat, Nhd);
+  A(&b.Qh, NH32); A(&b.Kh, NH32); A(&b.Vh, NH32); A(&b.nmix, NH32); A(&b.dn, NH32);
+  A(&b.dQ, NH32); A(&b.dK, NH32); A(&b.dV, NH32);
+  A(&b.alpha, N * h * h); A(&b.rmix, N * h); A(&b.scale, N * h); A(&b.rho, N * h);
+  A(&b.Rsrc, N * h); A(&b.dRc, N * h); A(&b.iters, N * h);
+  A(&b.hstar, Nhd); A(&b.pre, Nhd); A(&b.hist, Nhd); A(&b.fpmctx, Nhd);
+  A(&b.v, Nhd); A(&b.gpre, Nhd); A(&b.dsig, Nhd); A(&b.da, Nhd);
+  A(&b.mstate, (size_t)cfg->max_batch * h * d);
+  A(&b.pooled, N * d); A(&b.dl_dh, N * d); A(&b.nsg, N * d); A(&b.dS, N * d);
+  A(&b.y, N * d); A(&b.dy, N * d); A(&b.ggp, N * d); A(&b.lrms, N); A(&b.loss_rows, N);
+  A(&b.scal, 4); A(&b.stats, 4); A(&b.sigmas, 5 * h + 2);
+  if (V) {
+    A(&b.lmp, ctx->lm_len); A(&b.Glm, ctx->lm_len); A(&b.Mlm1, ctx->lm_len); A(&b.Mlm2, ctx->lm_len);
+    A(&b.logits, N * V); A(&b.emb, V * d);
+  }
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+  ctx->own_stream = true;
+  if (e != cudaSuccess) {
+    aideen_destroy(ctx);
+    return fail(AIDEEN_E_CUDA);
+  }
+  if (cublasCreate(&ctx->cublas) != CUBLAS_STATUS_SUCCESS) {
+    aideen_destroy(ctx);
+    return fail(AIDEEN_E_CUDA);
+  }
+  cublasSetStream(ctx->cublas, ctx->stream);
+  // fp32-accurate tensor-core emulation (BF16x9) for the plain LM-head GEMMs
+  cublasSetMathMode(ctx->cublas, CUBLAS_FP32_EMULATED_BF16X9_MATH);
+  cudaMemsetAsync(b.mstate, 0, (size_t)cfg->max_batch * h * d * sizeof(float), ctx->stream);
+  cudaMemsetAsync(b.M1, 0, ctx->W_len * sizeof(float), ctx->stream);
+  cudaMemsetAsync(b.M2, 0, ctx->W_len * sizeof(float), ctx->stream);
+  cudaMemsetAsync(b.hist, 0, Nhd * sizeof(float), ctx->stream);
+  cudaMemsetAsync(b.fpmctx, 0, Nhd * sizeof(float), ctx->stream);
+  if (V) {
+    cudaMemsetAsync(b.Mlm1, 0, ctx->lm_len * sizeof(float), ctx->stream);
+    cudaMemsetAsync(b.Mlm2, 0, ctx->lm_len * sizeof(float), ctx->stream);
+  }
+  if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) {
+    aideen_destroy(ctx);
+    return fail(AIDEEN_E_CUDA);
+  }
+  if (status) *status = AIDEEN_OK;
+  return ctx;
+}
+
+void aideen_destroy(aideen_ctx *ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->comm) ncclCommDestroy(ctx->comm);
+  if (ctx->cublas) cublasDestroy(ctx->cublas);
+  DevBufs &b = ctx->b;
+  void *ptrs[] = {b.W, b.G, b.M1, b.M2, b.S_in, b.tokens, b.targets, b.signal, b.A, b.amat, b.Qh,
+                  b.Kh, b.Vh, b.alpha, b.nmix, b.rmix, b.scale, b.rho, b.Rsrc, b.hstar, b.pre,
+                  b.pooled, b.hist, b.fpmctx, b.mstate, b.iters, b.v, b.gpre, b.dl_dh, b.rhs_slot,
+                  b.nsg, b.da, b.dn, b.dQ, b.dK, b.dV, b.dsig, b.dRc, b.dS, b.lmp, b.Glm, b.Mlm1,
+                  b.Mlm2, b.y, b.lrms, b.logits, b.dy, b.ggp, b.loss_rows, b.scal, b.emb, b.stats,
+                  b.sigmas};
+  for (void *p : ptrs)
+    if (p) cudaFree(p);
+  if (ctx->stream && ctx->own_stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+int aideen_set_stream(aideen_ctx *ctx, void *s) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  CU(cudaStreamSynchronize(ctx->stream));
+  if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
+  ctx->stream = (cudaStream_t)s;
+  ctx->own_stream = false;
+  cublasSetStream(ctx->cublas, ctx->stream);
+  return AIDEEN_OK;
+}
+
+int aideen_sync(aideen_ctx *ctx) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  CU(cudaStreamSynchronize(ctx->stream));
+  return AIDEEN_OK;
+}
+
+int aideen_upload_weights(aideen_ctx *ctx, const float *w, size_t n, int where) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  if (n != ctx->W_len) return set_err(ctx, AIDEEN_E_INVALID, "AllWeights length mismatch");
+  CHK(copy_in(ctx, ctx->b.W, w, n * sizeof(float), where));
+  float fl[2];
+  CU(cudaMemcpyAsync(&fl[0], ctx->b.W + ctx->L.signal_scale, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+  CU(cudaMemcpyAsync(&fl[1], ctx->b.W + ctx->L.signal_zero, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+  CU(cudaStreamSynchronize(ctx->stream));
+  ctx->signal_scale = fl[0];
+  ctx->signal_zero = fl[1] > 0.5f;
+  return AIDEEN_OK;
+}
+
+int aideen_download_weights(aideen_ctx *ctx, float *out, size_t n) {
+  if (!ctx || !out || n > ctx->W_len) return set_err(ctx, AIDEEN_E_INVALID, "bad download");
+  CU(cudaMemcpyAsync(out, ctx->b.W, n * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+  CU(cudaStreamSynchronize(ctx->stream));
+  return AIDEEN_OK;
+}
+
+int aideen_download_grads(aideen_ctx *ctx, float *out, size_t n) {
+  if (!ctx || !out || n > ctx->W_len) return set_err(ctx, AIDEEN_E_INVALID, "bad download");
+  CU(cudaMemcpyAsync(out, ctx->b.G, n * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+  CU(cudaStreamSynchronize(ctx->stream));
+  return AIDEEN_OK;
+}
+
+int aideen_upload_lm_head(aideen_ctx *ctx, const float *w_lm, const float *b_lm, const float *g_lm) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  const size_t V = ctx->cfg.vocab, d = ctx->cfg.d_model;
+  if (!V) return set_err(ctx, AIDEEN_E_INVALID, "context created with vocab = 0");
+  CHK(copy_in(ctx, ctx->b.lmp, w_lm, V * d * sizeof(float), AIDEEN_HOST));
+  CHK(copy_in(ctx, ctx->b.lmp + V * d, b_lm, V * sizeof(float), AIDEEN_HOST));
+  CHK(copy_in(ctx, ctx->b.lmp + V * d + V, g_lm, d * sizeof(float), AIDEEN_HOST));
+  CU(cudaStreamSynchronize(ctx->stream));
+  ctx->lm_ready = true;
+  return AIDEEN_OK;
+}
+
+int aideen_download_lm_head(aideen_ctx *ctx, float *w_lm, float *b_lm, float *g_lm) {
+  if (!ctx || !ctx->lm_ready) return set_err(ctx, AIDEEN_E_INVALID, "no LM head");
+  const size_t V = ctx->cfg.vocab, d = ctx->cfg.d_model;
+  if (w_lm) CU(cudaMemcpyAsync(w_lm, ctx->b.lmp, V * d * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (b_lm) CU(cudaMemcpyAsync(b_lm, ctx->b.lmp + V * d, V * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (g_lm) CU(cudaMemcpyAsync(g_lm, ctx->b.lmp + V * d + V, d * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  CU(cudaStreamSynchronize(ctx->stream));
+  return AIDEEN_OK;
+}
+
+int aideen_upload_embedding(aideen_ctx *ctx, const float *emb) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  if (!ctx->cfg.vocab) return set_err(ctx, AIDEEN_E_INVALID, "context created with vocab = 0");
+  CHK(copy_in(ctx, ctx->b.emb, emb, (size_t)ctx->cfg.vocab * ctx->cfg.d_model * 4, AIDEEN_HOST));
+  CU(cudaStreamSynchronize(ctx->stream));
+  ctx->emb_ready = true;
+  return AIDEEN_OK;
+}
+
+int aideen_reset_state(aideen_ctx *ctx) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  CU(cudaMemsetAsync(ctx->b.mstate, 0,
+                     (size_t)ctx->cfg.max_batch * ctx->cfg.h_slots * ctx->cfg.d_model * 4, ctx->stream));
+  return AIDEEN_OK;
+}
+
+int aideen_reset_optimizer(aideen_ctx *ctx) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  CU(cudaMemsetAsync(ctx->b.M1, 0, ctx->W_len * 4, ctx->stream));
+  CU(cudaMemsetAsync(ctx->b.M2, 0, ctx->W_len * 4, ctx->stream));
+  if (ctx->lm_len) {
+    CU(cudaMemsetAsync(ctx->b.Mlm1, 0, ctx->lm_len * 4, ctx->stream));
+    CU(cudaMemsetAsync(ctx->b.Mlm2, 0, ctx->lm_len * 4, ctx->stream));
+  }
+  return AIDEEN_OK;
+}
+
+int aideen_forward(aideen_ctx *ctx, const aideen_run *run, const float *s_in, int where,
+                   aideen_stats *stats) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  CHK(check_run(ctx, run));
+  const size_t N = (size_t)run->batch * run->seq_len;
+  CHK(copy_in(ctx, ctx->b.S_in, s_in, N * ctx->cfg.d_model * 4, where));
+  return run_forward(ctx, run, stats);
+}
+
+int aideen_forward_tokens(aideen_ctx *ctx, const aideen_run *run, const int32_t *tokens, int where,
+                          aideen_stats *stats) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  CHK(check_run(ctx, run));
+  if (!ctx->emb_ready) return set_err(ctx, AIDEEN_E_INVALID, "embedding not uploaded");
+  const int N = run->batch * run->seq_len;
+  CHK(copy_in(ctx, ctx->b.tokens, tokens, (size_t)N * 4, where));
+  KL(launch_embed(ctx->b.tokens, ctx->b.emb, ctx->b.S_in, N, ctx->cfg.d_model, ctx->cfg.vocab, ctx->stream));
+  return run_forward(ctx, run, stats);
+}
+
+int aideen_lm_head_loss(aideen_ctx *ctx, uint32_t batch, uint32_t seq_len, const int32_t *targets,
+                        int where, float *loss_out) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  const uint32_t N = batch * seq_len;
+  if (N == 0 || N != ctx->N) return set_err(ctx, AIDEEN_E_INVALID, "LM head must follow a forward of the same shape");
+  CHK(copy_in(ctx, ctx->b.targets, targets, (size_t)N * 4, where));
+  return run_lm_head(ctx, N, loss_out);
+}
+
+int aideen_adjoint(aideen_ctx *ctx, const aideen_adjoint_args *a, const float *dl_dh,
+                   const float *rhs_slot, int where) {
+  if (!ctx || !a) return AIDEEN_E_INVALID;
+  const uint32_t N = a->batch * a->seq_len;
+  if (N == 0 || N != ctx->N) return set_err(ctx, AIDEEN_E_INVALID, "adjoint must follow a forward of the same shape");
+  const size_t d = ctx->cfg.d_model, h = ctx->cfg.h_slots;
+  if (dl_dh) CHK(copy_in(ctx, ctx->b.dl_dh, dl_dh, (size_t)N * d * 4, where));
+  const float *rs = nullptr;
+  if (rhs_slot) {
+    if (!ctx->b.rhs_slot) CU(dalloc(&ctx->b.rhs_slot, ctx->max_tokens * h * d));
+    CHK(copy_in(ctx, ctx->b.rhs_slot, rhs_slot, (size_t)N * h * d * 4, where));
+    rs = ctx->b.rhs_slot;
+  }
+  return run_adjoint(ctx, N, ctx->b.pre, nullptr, ctx->b.dl_dh, rs, a->iters, a->damping, a->anderson_m);
+}
+
+int aideen_adjoint_on(aideen_ctx *ctx, const aideen_adjoint_args *a, const float *hstar,
+                      const float *branch, const float *dl_dh, const float *rhs_slot, int where) {
+  if (!ctx || !a || !hstar || !branch) return AIDEEN_E_INVALID;
+  const uint32_t N = a->batch * a->seq_len;
+  if (N == 0 || N > ctx->max_tokens) return set_err(ctx, AIDEEN_E_INVALID, "tokens beyond the context caps");
+  const size_t d = ctx->cfg.d_model, h = ctx->cfg.h_slots, bytes = (size_t)N * h * d * 4;
+  const float *pa = hstar, *pb = branch;
+  if (where != AIDEEN_DEVICE) {
+    CHK(copy_in(ctx, ctx->b.hstar, hstar, bytes, where));
+    CHK(copy_in(ctx, ctx->b.signal, branch, bytes, where));
+    pa = ctx->b.hstar;
+    pb = ctx->b.signal;
+  }
+  const float *rt = nullptr, *rs = nullptr;
+  if (dl_dh) {
+    if (where != AIDEEN_DEVICE) { CHK(copy_in(ctx, ctx->b.dl_dh, dl_dh, (size_t)N * d * 4, where)); rt = ctx->b.dl_dh; }
+    else rt = dl_dh;
+  }
+  if (rhs_slot) {
+    if (where != AIDEEN_DEVICE) {
+      if (!ctx->b.rhs_slot) CU(dalloc(&ctx->b.rhs_slot, ctx->max_tokens * h * d));
+      CHK(copy_in(ctx, ctx->b.rhs_slot, rhs_slot, bytes, where));
+      rs = ctx->b.rhs_slot;
+    } else {
+      rs = rhs_slot;
+    }
+  }
+  ctx->N = 0;  // the forward state no longer matches this adjoint
+  return run_adjoint(ctx, N, pa, pb, rt, rs, a->iters, a->damping, a->anderson_m);
+}
+
+int aideen_source_grad(aideen_ctx *ctx, float *out, int where) {
+  if (!ctx || !out) return AIDEEN_E_INVALID;
+  const int N = ctx->adj_N, h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
+  if (N == 0) return set_err(ctx, AIDEEN_E_INVALID, "no adjoint has run");
+  float *dst = where == AIDEEN_DEVICE ? out : ctx->b.dS;  // dS doubles as host staging
+  KL(launch_source_grad(ctx->b.gpre, dst, N, h, d, ctx->stream));
+  if (where != AIDEEN_DEVICE) {
+    CU(cudaMemcpyAsync(out, dst, (size_t)N * d * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    CU(cudaStreamSynchronize(ctx->stream));
+  }
+  return AIDEEN_OK;
+}
+
+int aideen_weight_grads(aideen_ctx *ctx) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  return run_weight_grads(ctx, true);
+}
+
+int aideen_apply_update(aideen_ctx *ctx, const aideen_update *u) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  return run_update(ctx, u);
+}
+
+int aideen_renormalize_spectral(aideen_ctx *ctx, uint32_t n_iters, float attn, float win, float fpm,
+                                float wv, float wo, float *sig) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  KL(launch_spectral(ctx->b.W, ctx->cfg.d_model, ctx->cfg.h_slots, ctx->L, n_iters, attn, win, fpm,
+                     wv, wo, ctx->b.sigmas, ctx->stream));
+  if (sig) {
+    CU(cudaMemcpyAsync(sig, ctx->b.sigmas, (5 * ctx->cfg.h_slots + 2) * 4, cudaMemcpyDeviceToHost,
+                       ctx->stream));
+    CU(cudaStreamSynchronize(ctx->stream));
+  }
+  return AIDEEN_OK;
+}
+
+int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t *tokens,
+                      const int32_t *targets, int where, float *loss_out, aideen_stats *stats) {
+  if (!ctx || !a) return AIDEEN_E_INVALID;
+  CHK(check_run(ctx, &a->run));
+  if (!ctx->emb_ready || !ctx->lm_ready)
+    return set_err(ctx, AIDEEN_E_INVALID, "train step needs the embedding and the LM head");
+  const int N = a->run.batch * a->run.seq_len;
+  CHK(copy_in(ctx, ctx->b.tokens, tokens, (size_t)N * 4, where));
+  CHK(copy_in(ctx, ctx->b.targets, targets, (size_t)N * 4, where));
+  KL(launch_embed(ctx->b.tokens, ctx->b.emb, ctx->b.S_in, N, ctx->cfg.d_model, ctx->cfg.vocab, ctx->stream));
+  CHK(run_forward(ctx, &a->run, stats));
+  CHK(run_lm_head(ctx, N, nullptr));
+  CHK(run_adjoint(ctx, N, ctx->b.pre, nullptr, ctx->b.dl_dh, nullptr, a->adj_iters, a->run.damping,
+                  a->anderson_m));
+  CHK(run_weight_grads(ctx, false));
+  CHK(run_update(ctx, &a->update));
+  if (a->renorm)
+    KL(launch_spectral(ctx->b.W, ctx->cfg.d_model, ctx->cfg.h_slots, ctx->L, 12, 0.10f, 0.30f, 0.70f,
+                       0.50f, 0.50f, ctx->b.sigmas, ctx->stream));
+  if (loss_out) {
+    CU(cudaMemcpyAsync(loss_out, ctx->b.scal + 1, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+    CU(cudaStreamSynchronize(ctx->stream));
+  }
+  return AIDEEN_OK;
+}
+
+static void *buf_ptr(aideen_ctx *ctx, int which, size_t *count) {
+  const size_t N = ctx->N ? ctx->N : ctx->adj_N, h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
+  const size_t Na = ctx->adj_N ? ctx->adj_N : N;
+  DevBufs &b = ctx->b;
+  switch (which) {
+    case AIDEEN_BUF_HSTAR: *count = N * h * d; return b.hstar;
+    case AIDEEN_BUF_POOLED: *count = N * d; return b.pooled;
+    case AIDEEN_BUF_SIGNAL: *count = N * h * d; return b.signal;
+    case AIDEEN_BUF_ATTN: *count = N * h * d; return b.A;
+    case AIDEEN_BUF_ITERS: *count = N * h; return b.iters;
+    case AIDEEN_BUF_ADJ_V: *count = Na * h * d; return b.v;
+    case AIDEEN_BUF_GPRE: *count = Na * h * d; return b.gpre;
+    case AIDEEN_BUF_DL_DH: *count = N * d; return b.dl_dh;
+    case AIDEEN_BUF_HIST_CTX: *count = N * h * d; return b.hist;
+    case AIDEEN_BUF_MSTATE: *count = (size_t)ctx->cfg.max_batch * h * d; return b.mstate;
+    case AIDEEN_BUF_FPM_CTX: *count = N * h * d; return b.fpmctx;
+    case AIDEEN_BUF_ALPHA: *count = N * h * h; return b.alpha;
+    case AIDEEN_BUF_S_IN: *count = N * d; return b.S_in;
+    case AIDEEN_BUF_DS_IN: *count = N * d; return b.dS;
+    case AIDEEN_BUF_LM_GRADS: *count = ctx->lm_len; return b.Glm;
+    case AIDEEN_BUF_PRE: *count = N * h * d; return b.pre;
+    default: *count = 0; return nullptr;
+  }
+}
+
+int aideen_read(aideen_ctx *ctx, int which, void *dst, size_t n) {
+  if (!ctx || !dst) return AIDEEN_E_INVALID;
+  size_t count = 0;
+  void *p = buf_ptr(ctx, which, &count);
+  if (!p) return set_err(ctx, AIDEEN_E_INVALID, "unknown or absent buffer");
+  if (n > count) return set_err(ctx, AIDEEN_E_INVALID, "read beyond the buffer's valid extent");
+  CU(cudaMemcpyAsync(dst, p, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  CU(cudaStreamSynchronize(ctx->stream));
+  return AIDEEN_OK;
+}
+
+void *aideen_device_ptr(aideen_ctx *ctx, int which) {
+  if (!ctx) return nullptr;
+  size_t count = 0;
+  return buf_ptr(ctx, which, &count);
+}
+
+int aideen_comm_unique_id(char out[AIDEEN_UNIQUE_ID_BYTES]) {
+  static_assert(sizeof(ncclUniqueId) == AIDEEN_UNIQUE_ID_BYTES, "ncclUniqueId size");
+  ncclUniqueId id;
+  if (ncclGetUniqueId(&id) != ncclSuccess) return AIDEEN_E_NCCL;
+  std::memcpy(out, &id, sizeof(id));
+  return AIDEEN_OK;
+}
+
+int aideen_comm_init(aideen_ctx *ctx, const char id_bytes[AIDEEN_UNIQUE_ID_BYTES], int nranks, int rank) {
+  if (!ctx || nranks < 1 || rank < 0 || rank >= nranks) return AIDEEN_E_INVALID;
+  if (nranks == 1) return AIDEEN_OK;
+  ncclUniqueId id;
+  std::memcpy(&id, id_bytes, sizeof(id));
+  CU(cudaSetDevice(ctx->device));
+  ncclResult_t r = ncclCommInitRank(&ctx->comm, nranks, id, rank);
+  if (r != ncclSuccess) return set_err(ctx, AIDEEN_E_NCCL, std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
+  ctx->nranks = nranks;
+  ctx->rank = rank;
+  return AIDEEN_OK;
+}
+
+int aideen_allreduce_grads(aideen_ctx *ctx, int timeout_ms) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  return run_allreduce(ctx, timeout_ms);
+}
+
+}  // extern "C"

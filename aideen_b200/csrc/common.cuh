@@ -1,0 +1,94 @@
+// Shared device helpers: warp/block reductions and small vector ops.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace aideen {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sums of K (<= 8) values per thread; every thread receives the
+// totals.  `red` is shared scratch of 2 * 8 * 32 floats.  Consecutive calls
+// alternate halves of `red`, so one __syncthreads per call suffices: a thread
+// reaches call i+2 (same half as call i) only after passing call i+1's
+// barrier, which every thread reaches only after reading call i's result.
+struct BlockReducer {
+  float *red;
+  int parity;
+  __device__ __forceinline__ explicit BlockReducer(float *r) : red(r), parity(0) {}
+  template <int K>
+  __device__ __forceinline__ void sum(float (&v)[K]) {
+    static_assert(K <= 8, "at most 8 values per reduction");
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nw = (blockDim.x + 31) >> 5;
+    float *buf = red + parity * 8 * 32;
+    parity ^= 1;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      float x = warp_sum(v[k]);
+      if (lane == 0) buf[k * 32 + warp] = x;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      float s = 0.f;
+      for (int w = 0; w < nw; ++w) s += buf[k * 32 + w];
+      v[k] = s;
+    }
+  }
+};
+
+// Reduce 32 per-lane partial vectors p[0..31] across a warp so that lane r
+// ends up holding the sum over lanes of p[r] (31 shuffles in total).  At each
+// step a lane keeps one half of its window and ships the other half to its
+// partner (lane ^ off), which keeps the mirror half.
+__device__ __forceinline__ float warp_transpose_reduce32(float (&p)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const float send = upper ? p[i] : p[i + off];
+      const float keep = upper ? p[i + off] : p[i];
+      p[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return p[0];
+}
+
+__device__ __forceinline__ float4 f4(float a) { return make_float4(a, a, a, a); }
+__device__ __forceinline__ float4 operator+(float4 a, float4 b) {
+  return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+__device__ __forceinline__ float4 operator-(float4 a, float4 b) {
+  return make_float4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w);
+}
+__device__ __forceinline__ float4 operator*(float4 a, float4 b) {
+  return make_float4(a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w);
+}
+__device__ __forceinline__ float4 operator*(float s, float4 a) {
+  return make_float4(s * a.x, s * a.y, s * a.z, s * a.w);
+}
+__device__ __forceinline__ float dot4(float4 a, float4 b) {
+  return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+}
+__device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ void st4(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
+__device__ __forceinline__ float4 tanh4(float4 a) {
+  return make_float4(tanhf(a.x), tanhf(a.y), tanhf(a.z), tanhf(a.w));
+}
+__device__ __forceinline__ bool finite4(float4 a) {
+  return isfinite(a.x) && isfinite(a.y) && isfinite(a.z) && isfinite(a.w);
+}
+
+}  // namespace aideen

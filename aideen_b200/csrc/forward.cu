@@ -1,0 +1,417 @@
+// Forward DEQ solve of the AIDEEN slot block on sm_100a.
+//
+//   embed_gather       tokens -> S_in          (embedding_train.wgsl:35, gather only)
+//   attn_softmax       iter-0 slot attention softmax / mix / RMS-normalise
+//                      (deq_slot_attn_unified_clean.wgsl:395-450)
+//   attn_scale         attention RMS scale + injection A = attn*scale (:452-495)
+//   picard             persistent token-serial Picard solve, one CTA per
+//                      (sequence, slot); with FPM memory the h CTAs of one
+//                      sequence form a thread-block cluster and exchange the
+//                      per-slot memory and its read keys through distributed
+//                      shared memory (:700-2300)
+//   pool_rmsnorm       H_pooled = mean over slots (deq_forward_pool.wgsl:32-65)
+//                      + the LM-head RMSNorm input (lm_train.wgsl:100-125)
+//   solve_stats        iteration / non-finite counters
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace aideen {
+
+__global__ void embed_gather_kernel(const int32_t *__restrict__ tok, const float *__restrict__ emb,
+                                    float *__restrict__ S, int N, int d, int vocab) {
+  const int n = blockIdx.x;
+  if (n >= N) return;
+  int t = tok[n];
+  t = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
+  for (int j = threadIdx.x * 4; j < d; j += blockDim.x * 4)
+    st4(S + (size_t)n * d + j, ld4(emb + (size_t)t * d + j));
+}
+
+// One block per token, one warp per slot, lane = head dimension (32).
+__global__ void attn_softmax_kernel(AttnArgs a) {
+  __shared__ float Ks[16][33], Vs[16][33];
+  const int n = blockIdx.x;
+  const int s = threadIdx.x >> 5, c = threadIdx.x & 31;
+  const int h = a.h, d = a.d;
+  const size_t row = ((size_t)n * h + s) * kHeadDim + c;
+  Ks[s][c] = a.Kh[row] + a.W[a.off_kb + (size_t)s * d + c];
+  Vs[s][c] = a.Vh[row];
+  const float q = a.Qh[row] + a.W[a.off_qb + (size_t)s * d + c];
+  __syncthreads();
+  const float gain = 2.0f * rsqrtf((float)kHeadDim);
+  float logit[16];
+  float mx = -1e30f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    if (k < h) {
+      float l = warp_sum(q * Ks[k][c]) * gain;
+      if (h > 1 && k == s) l = -1e30f;
+      logit[k] = l;
+      mx = fmaxf(mx, l);
+    }
+  }
+  float se = 0.f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k)
+    if (k < h) { logit[k] = expf(logit[k] - mx); se += logit[k]; }
+  se = fmaxf(se, 1e-12f);
+  float mix = 0.f, vmean = 0.f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k)
+    if (k < h) {
+      logit[k] = logit[k] / se;
+      mix += logit[k] * Vs[k][c];
+      vmean += Vs[k][c];
+    }
+  mix -= vmean / (float)h;
+  const float r = sqrtf(warp_sum(mix * mix) / (float)kHeadDim + 1e-6f);
+  a.nmix[row] = mix / r;
+  if (c == 0) {
+    a.rmix[(size_t)n * h + s] = r;
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      if (k < h) a.alpha[((size_t)n * h + s) * h + k] = logit[k];
+  }
+}
+
+// One warp per (token, slot): A = attn * max(R,1e-3)/max(rho,1e-6).
+__global__ void attn_scale_kernel(AttnArgs a, int rows) {
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= rows) return;
+  const int d = a.d, s = w % a.h;
+  const float *sig = a.signal + (size_t)w * d;
+  const float *am = a.amat + (size_t)w * d;
+  const float *anc = a.W + a.off_anchor + (size_t)s * d;
+  float ss = 0.f, aa = 0.f;
+  for (int j = lane * 4; j < d; j += 128) {
+    const float4 src = ld4(sig + j) + ld4(anc + j);
+    const float4 x = ld4(am + j);
+    ss += dot4(src, src);
+    aa += dot4(x, x);
+  }
+  ss = warp_sum(ss);
+  aa = warp_sum(aa);
+  const float R = sqrtf(ss / d + 1e-6f), rho = sqrtf(aa / d + 1e-6f);
+  const float sc = fmaxf(R, 1e-3f) / fmaxf(rho, 1e-6f);
+  for (int j = lane * 4; j < d; j += 128) st4(a.A + (size_t)w * d + j, sc * ld4(am + j));
+  if (lane == 0) { a.scale[w] = sc; a.rho[w] = rho; a.Rsrc[w] = R; }
+}
+
+// y[r] = sum_j M[j*32 + r] x[j] for r < 32; each thread owns 4 consecutive j.
+// Result lands in out[0..32) (shared).  Two block barriers.
+__device__ __forceinline__ void mv_d_to_32(const float *__restrict__ M, float4 x, float *out,
+                                           float *part) {
+  float p[32];
+  const float *row = M + (size_t)(threadIdx.x * 4) * kRank;
+#pragma unroll
+  for (int r4 = 0; r4 < 8; ++r4) {
+    const float4 w0 = ld4(row + 0 * kRank + 4 * r4), w1 = ld4(row + 1 * kRank + 4 * r4);
+    const float4 w2 = ld4(row + 2 * kRank + 4 * r4), w3 = ld4(row + 3 * kRank + 4 * r4);
+    p[4 * r4 + 0] = x.x * w0.x + x.y * w1.x + x.z * w2.x + x.w * w3.x;
+    p[4 * r4 + 1] = x.x * w0.y + x.y * w1.y + x.z * w2.y + x.w * w3.y;
+    p[4 * r4 + 2] = x.x * w0.z + x.y * w1.z + x.z * w2.z + x.w * w3.z;
+    p[4 * r4 + 3] = x.x * w0.w + x.y * w1.w + x.z * w2.w + x.w * w3.w;
+  }
+  const float v = warp_transpose_reduce32(p);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  part[warp * 32 + lane] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float s = 0.f;
+    for (int w = 0; w < nw; ++w) s += part[w * 32 + threadIdx.x];
+    out[threadIdx.x] = s;
+  }
+  __syncthreads();
+}
+
+// out[o] = sum_r M[r*d + o] in[r] for the thread's 4 outputs.
+__device__ __forceinline__ float4 mv_32_to_d(const float *__restrict__ M, const float *in, int d) {
+  float4 acc = f4(0.f);
+  const float *col = M + threadIdx.x * 4;
+#pragma unroll 8
+  for (int r = 0; r < kRank; ++r) acc = acc + in[r] * ld4(col + (size_t)r * d);
+  return acc;
+}
+
+__device__ __forceinline__ float4 sigmoid4(float4 x) {
+  return make_float4(1.f / (1.f + expf(-x.x)), 1.f / (1.f + expf(-x.y)), 1.f / (1.f + expf(-x.z)),
+                     1.f / (1.f + expf(-x.w)));
+}
+
+// Persistent token-serial solve.  blockDim = d/4 (one float4 per thread),
+// grid = B*h, block = b*h + s.  FPM=true requires a cluster of h CTAs.
+template <bool FPM>
+__global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
+  extern __shared__ float sm[];
+  float *red = sm;               // 512
+  float *vec = red + 512;        // 64   (q / bottleneck | retain-up)
+  float *part = vec + 64;        // 256  (8 warps x 32)
+  float *wsm = part + 256;       // 32   (read weights, gate)
+  float *keybuf = wsm + 32;      // 2 x 32
+  float *mbuf = keybuf + 64;     // 2 x d
+  const int d = a.d, h = a.h, T = a.T;
+  const int b = blockIdx.x / h, s = blockIdx.x % h;
+  const int j0 = threadIdx.x * 4;
+  const float inv_d = 1.f / (float)d;
+  const float *W = a.W;
+  const float4 NS = ld4(W + a.off_ns + j0);
+  const float4 anc = ld4(W + a.off_anchor + (size_t)s * d + j0);
+  BlockReducer R(red);
+  float4 hcur = f4(0.f), m = f4(0.f), hs4 = f4(0.f), hb4 = f4(0.f), wx4 = f4(0.f), ad4 = f4(0.f);
+  int cur = 0;
+  if constexpr (FPM) {
+    m = ld4(a.mstate + ((size_t)b * h + s) * d + j0);
+    st4(mbuf + j0, m);
+    hs4 = ld4(W + a.off_hscale + (size_t)s * d + j0);
+    hb4 = ld4(W + a.off_hbias + (size_t)s * d + j0);
+    wx4 = make_float4(0.5f * tanhf(W[a.off_wx + (size_t)(j0 + 0) * d + j0 + 0]),
+                      0.5f * tanhf(W[a.off_wx + (size_t)(j0 + 1) * d + j0 + 1]),
+                      0.5f * tanhf(W[a.off_wx + (size_t)(j0 + 2) * d + j0 + 2]),
+                      0.5f * tanhf(W[a.off_wx + (size_t)(j0 + 3) * d + j0 + 3]));
+    const float4 al = ld4(W + a.off_alog + (size_t)s * d + j0);
+    ad4 = make_float4(1.f / (1.f + expf(al.x)), 1.f / (1.f + expf(al.y)), 1.f / (1.f + expf(al.z)),
+                      1.f / (1.f + expf(al.w)));
+  }
+  const float band = fmaxf(a.eps, 0.15f * 0.2f);
+  for (int t = 0; t < T; ++t) {
+    const size_t n = (size_t)b * T + t;
+    const size_t e = (n * h + s) * d + j0;
+    const float4 sig = ld4(a.signal + e);
+    const float4 A4 = a.slot_coord ? ld4(a.A + e) : f4(0.f);
+    if (t == 0) {
+      float v[1] = {dot4(sig, sig)};
+      R.sum(v);
+      const float den = fmaxf(sqrtf(v[0] * inv_d + 1e-6f), 1e-6f);
+      hcur = make_float4(sig.x / den, sig.y / den, sig.z / den, sig.w / den);
+    }
+    float4 ctx = f4(0.f);
+    if constexpr (FPM) {
+      // read key of this slot's carried memory (:855-883)
+      const float4 keyed = m + hs4 * tanh4(m) + hb4;
+      mv_d_to_32(W + a.off_wkm + (size_t)s * d * kRank, keyed, keybuf + cur * 32, part);
+      cg::this_cluster().sync();
+    }
+    float prev = 1.f;
+    int it = 0;
+    bool conv = false;
+    while (it < a.max_iters && !conv) {
+      if constexpr (FPM) {
+        if (it == 1) {
+          // Model-A memory read from the first structured state (:1031-1200)
+          float v2[2] = {dot4(hcur, hcur), dot4(sig, sig)};
+          R.sum(v2);
+          const float hq = sqrtf(fmaxf(v2[0], 1e-6f));
+          const float sig_norm = sqrtf(fmaxf(v2[1], 1e-6f));
+          mv_d_to_32(W + a.off_wqm + (size_t)s * d * kRank,
+                     make_float4(hcur.x / hq, hcur.y / hq, hcur.z / hq, hcur.w / hq), vec, part);
+          cg::cluster_group cl = cg::this_cluster();
+          if (threadIdx.x < 32) {
+            const int lane = threadIdx.x;
+            float sc = -1e30f;
+            if (lane < h) {
+              const float *rk = cl.map_shared_rank(keybuf + cur * 32, lane);
+              float acc = 0.f;
+#pragma unroll 8
+              for (int r = 0; r < kRank; ++r) acc += vec[r] * rk[r];
+              sc = (acc + W[a.off_bread + lane]) * rsqrtf((float)kRank) / fmaxf(a.tau, 1e-3f);
+            }
+            const float mx = warp_max(sc);
+            const float ex = lane < h ? expf(sc - mx) : 0.f;
+            const float se = fmaxf(warp_sum(ex), 1e-12f);
+            const float w = ex / se;
+            const float peak = warp_max(lane < h ? w : 0.f);
+            if (lane < h) wsm[lane] = w;
+            if (lane == 0) {
+              const float uni = 1.f / (float)(h > 1 ? h : 1);
+              const float conf = fminf(fmaxf((peak - uni) / fmaxf(1e-6f, 1.f - uni), 0.f), 1.f);
+              wsm[16] = fmaxf(sqrtf(conf), a.gate_min);
+            }
+          }
+          __syncthreads();
+          float4 mr = f4(0.f);
+          for (int ms = 0; ms < h; ++ms) {
+            const float *rm = cl.map_shared_rank(mbuf + cur * d, ms);
+            mr = mr + wsm[ms] * ld4(rm + j0);
+          }
+          const float4 mu = tanh4(mr);
+          float v1[1] = {dot4(mu, mu)};
+          R.sum(v1);
+          const float mu_norm = sqrtf(fmaxf(v1[0], 1e-6f));
+          const float coef = sig_norm * fmaxf(a.alpha_m, 0.001f) / fmaxf(mu_norm, 1e-6f) * wsm[16];
+          ctx = coef * mu;
+        }
+      }
+      float4 dep = sig + hcur + anc;
+      if (it == 0) dep = dep + A4;
+      float4 pre = dep;
+      if (FPM && it >= 1) pre = pre + ctx;
+      float v1[1] = {dot4(dep, dep)};
+      R.sum(v1);
+      const float rr = sqrtf(v1[0] * inv_d + 1e-6f);
+      const float4 f = make_float4(NS.x * (pre.x / rr), NS.y * (pre.y / rr), NS.z * (pre.z / rr),
+                                   NS.w * (pre.w / rr));
+      const float4 hn = a.blend * f + (1.f - a.blend) * hcur;
+      const float4 dh = hn - hcur;
+      float v2[1] = {dot4(dh, dh)};
+      R.sum(v2);
+      const float err = sqrtf(v2[0] * inv_d + 1e-12f) / fmaxf(rr, 1e-6f);
+      hcur = hn;
+      const bool strict = err < a.eps;
+      const float plateau = fabsf(err - prev) / fmaxf(prev, a.eps);
+      const bool homeo = (it + 1 >= 4) && (err <= band) && (plateau <= 0.10f);
+      conv = strict || homeo;
+      prev = err;
+      ++it;
+    }
+    st4(a.hstar + e, hcur);
+    float4 pre_adj = sig + hcur;
+    if (a.slot_coord) pre_adj = pre_adj + A4 + anc;
+    st4(a.pre + e, pre_adj);
+    if (threadIdx.x == 0) a.iters[n * h + s] = it;
+    if constexpr (FPM) {
+      st4(a.fpmctx + e, ctx);
+      // post-solve memory write (:1965-2140)
+      const float4 c = 0.5f * (hcur + sig);
+      float v2[2] = {dot4(hcur, hcur), dot4(ld4(W + a.off_wgate + (size_t)s * d + j0), c)};
+      R.sum(v2);
+      const float h_rms = sqrtf(fmaxf(v2[0] * inv_d, 1e-6f));
+      const float4 hu = make_float4(hcur.x / h_rms, hcur.y / h_rms, hcur.z / h_rms, hcur.w / h_rms);
+      const float raw_z = 1.f / (1.f + expf(-(v2[1] * rsqrtf((float)d) + W[a.off_bwrite + s] - 1.5f)));
+      const float z = fminf(fmaxf(raw_z, 0.f), 1.f);
+      mv_d_to_32(W + a.off_wkw + (size_t)s * d * kRank, c, vec, part);
+      mv_d_to_32(W + a.off_wup + (size_t)s * d * kRank, c, vec + 32, part);
+      const float4 prop = tanh4(ld4(W + a.off_bdelta + (size_t)s * d + j0) +
+                                mv_32_to_d(W + a.off_wvw + (size_t)s * kRank * d, vec, d));
+      const float4 df = prop - m;
+      float v3[2] = {dot4(m, m), dot4(df, df)};
+      R.sum(v3);
+      const float prev_norm = sqrtf(fmaxf(v3[0], 1e-6f));
+      const float diff_norm = sqrtf(fmaxf(v3[1], 1e-6f));
+      const float novelty = diff_norm / (diff_norm + prev_norm + 1e-6f);
+      const float4 rr4 = sigmoid4(ld4(W + a.off_bret + (size_t)s * d + j0) +
+                                  mv_32_to_d(W + a.off_wdown + (size_t)s * kRank * d, vec + 32, d));
+      const float4 retain = f4(1.f) - novelty * (f4(1.f) - rr4);
+      const float4 write = (z * 0.1f) * prop;
+      const float4 x = sqrtf(fmaxf(z, 1e-6f)) * hu + wx4 * hu + write;
+      const float4 base = ad4 * m + (f4(1.f) - ad4) * x;
+      const float4 mn = retain * m + (f4(1.f) - retain) * base;
+      st4(a.hist + e, mn);
+      st4(mbuf + (cur ^ 1) * d + j0, mn);
+      m = mn;
+      cur ^= 1;
+    }
+  }
+  if constexpr (FPM) {
+    st4(a.mstate + ((size_t)b * h + s) * d + j0, m);
+    cg::this_cluster().sync();  // keep shared memory alive for remote readers
+  }
+}
+
+__global__ void pool_rmsnorm_kernel(const float *__restrict__ hstar, const float *__restrict__ g,
+                                    float *__restrict__ pooled, float *__restrict__ y,
+                                    float *__restrict__ lrms, int h, int d) {
+  __shared__ float red[512];
+  const int n = blockIdx.x, j0 = threadIdx.x * 4;
+  float4 p = f4(0.f);
+  for (int s = 0; s < h; ++s) p = p + ld4(hstar + ((size_t)n * h + s) * d + j0);
+  p = (1.f / (float)h) * p;
+  st4(pooled + (size_t)n * d + j0, p);
+  if (!y) return;
+  BlockReducer R(red);
+  float v[1] = {dot4(p, p)};
+  R.sum(v);
+  const float r = sqrtf(v[0] / d + 1e-5f);
+  const float4 gg = ld4(g + j0);
+  st4(y + (size_t)n * d + j0,
+      make_float4(p.x / r * gg.x, p.y / r * gg.y, p.z / r * gg.z, p.w / r * gg.w));
+  if (threadIdx.x == 0) lrms[n] = r;
+}
+
+__global__ void solve_stats_kernel(const int32_t *__restrict__ iters, const float *__restrict__ hstar,
+                                   int rows, int d, int max_iters,
+                                   unsigned long long *__restrict__ st) {
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= rows) return;
+  bool bad = false;
+  for (int j = lane * 4; j < d; j += 128) bad |= !finite4(ld4(hstar + (size_t)w * d + j));
+  bad = __any_sync(0xffffffffu, bad);
+  if (lane == 0) {
+    const int it = iters[w];
+    atomicAdd(&st[0], (unsigned long long)it);
+    atomicMax(&st[1], (unsigned long long)it);
+    if (it >= max_iters) atomicAdd(&st[2], 1ull);
+    if (bad) atomicAdd(&st[3], 1ull);
+  }
+}
+
+// ---------------------------------------------------------------------------
+cudaError_t launch_embed(const int32_t *tok, const float *emb, float *S, int N, int d, int vocab,
+                         cudaStream_t st) {
+  if (N <= 0) return cudaSuccess;
+  embed_gather_kernel<<<N, 128, 0, st>>>(tok, emb, S, N, d, vocab);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attn_softmax(const AttnArgs &a, int N, cudaStream_t st) {
+  if (N <= 0) return cudaSuccess;
+  attn_softmax_kernel<<<N, 32 * a.h, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attn_scale(const AttnArgs &a, int rows, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  attn_scale_kernel<<<(rows + 7) / 8, 256, 0, st>>>(a, rows);
+  return cudaGetLastError();
+}
+
+static size_t picard_smem_bytes(int d) { return (size_t)(512 + 64 + 256 + 32 + 64 + 2 * d) * sizeof(float); }
+
+cudaError_t launch_picard(const PicardArgs &a, bool fpm, cudaStream_t st) {
+  if (a.B <= 0 || a.T <= 0) return cudaSuccess;
+  const int threads = a.d / 4;
+  const size_t smem = picard_smem_bytes(a.d);
+  if (!fpm) {
+    picard_kernel<false><<<a.B * a.h, threads, smem, st>>>(a);
+    return cudaGetLastError();
+  }
+  cudaError_t e = cudaFuncSetAttribute(picard_kernel<true>,
+                                       cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.B * a.h);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = a.h;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, picard_kernel<true>, a);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pool_rmsnorm(const float *hstar, const float *g, float *pooled, float *y,
+                                float *lrms, int N, int h, int d, cudaStream_t st) {
+  if (N <= 0) return cudaSuccess;
+  pool_rmsnorm_kernel<<<N, d / 4, 0, st>>>(hstar, g, pooled, y, lrms, h, d);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_solve_stats(const int32_t *iters, const float *hstar, int rows, int d,
+                               int max_iters, unsigned long long *st4p, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  solve_stats_kernel<<<(rows + 7) / 8, 256, 0, st>>>(iters, hstar, rows, d, max_iters, st4p);
+  return cudaGetLastError();
+}
+
+}  // namespace aideen

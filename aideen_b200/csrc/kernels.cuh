@@ -1,0 +1,108 @@
+// Kernel argument blocks and launchers shared between the .cu files.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "layout.h"
+
+namespace aideen {
+
+// Strided batched fp32 GEMM on CUDA cores:
+//   C[b] = alpha * opA(A[b]) * opB(B[b]) + beta * C[b]   (row-major)
+// opA(m,k) = transA ? A[k*lda+m] : A[m*lda+k], plus abias[stored column]
+// when abias != nullptr (the stored column is m when transA, else k).
+// opB(k,n) = transB ? B[n*ldb+k] : B[k*ldb+n].
+struct GemmArgs {
+  int M, N, K, batch;
+  const float *A; long lda, strideA; bool transA;
+  const float *B; long ldb, strideB; bool transB;
+  float *C; long ldc, strideC;
+  float alpha, beta;
+  const float *abias; long strideAbias;
+};
+cudaError_t gemm_f32(const GemmArgs &g, cudaStream_t s);
+
+struct AttnArgs {
+  int h, d;
+  const float *W;
+  size_t off_qb, off_kb, off_anchor;
+  const float *Qh, *Kh, *Vh;      // [N][h][32] projections without bias
+  float *alpha, *nmix, *rmix;     // [N][h][h], [N][h][32], [N][h]
+  const float *signal, *amat;     // [N][h][d]
+  float *A, *scale, *rho, *Rsrc;  // [N][h][d], [N][h] x3
+};
+
+struct PicardArgs {
+  int B, T, h, d, max_iters, slot_coord;
+  float eps, blend, alpha_m, tau, gate_min;
+  const float *W;
+  size_t off_ns, off_anchor, off_hscale, off_hbias, off_wkm, off_wqm, off_bread, off_wgate,
+      off_bwrite, off_wkw, off_wvw, off_bdelta, off_wup, off_wdown, off_bret, off_alog, off_wx;
+  const float *signal, *A;
+  float *hstar, *pre, *hist, *fpmctx, *mstate;
+  int32_t *iters;
+};
+
+struct AdjointArgs {
+  int N, h, d, iters, anderson_m;
+  float beta;
+  const float *pre_a, *pre_b;  // pre = pre_a (+ pre_b)
+  const float *rhs_tok;        // [N][d] or null (scaled 1/h per slot)
+  const float *rhs_slot;       // [N][h][d] or null
+  const float *NS;
+  float *v;                    // [h][N][d]
+  float *gpre;                 // [N][h][d]
+  float *nsg;                  // [N][d] per-token NormScale-gradient partials or null
+};
+
+struct AttnBwdArgs {
+  int h, d;
+  const float *W;
+  size_t off_qb, off_kb, off_anchor;
+  const float *gpre, *amat, *scale, *rho, *Rsrc, *signal;
+  float *da, *dRc;
+  const float *dn, *nmix, *rmix, *alpha, *Qh, *Kh, *Vh;
+  float *dQ, *dK, *dV;
+};
+
+cudaError_t launch_embed(const int32_t *tok, const float *emb, float *S, int N, int d, int vocab,
+                         cudaStream_t st);
+cudaError_t launch_attn_softmax(const AttnArgs &a, int N, cudaStream_t st);
+cudaError_t launch_attn_scale(const AttnArgs &a, int rows, cudaStream_t st);
+cudaError_t launch_picard(const PicardArgs &a, bool fpm, cudaStream_t st);
+cudaError_t launch_pool_rmsnorm(const float *hstar, const float *g, float *pooled, float *y,
+                                float *lrms, int N, int h, int d, cudaStream_t st);
+cudaError_t launch_solve_stats(const int32_t *iters, const float *hstar, int rows, int d,
+                               int max_iters, unsigned long long *st4p, cudaStream_t st);
+
+cudaError_t launch_adjoint(const AdjointArgs &a, cudaStream_t st);
+cudaError_t launch_source_grad(const float *gpre, float *out, int N, int h, int d, cudaStream_t st);
+cudaError_t launch_attn_bwd_scale(const AttnBwdArgs &a, int rows, cudaStream_t st);
+cudaError_t launch_attn_bwd_softmax(const AttnBwdArgs &a, int N, cudaStream_t st);
+cudaError_t launch_dsig_init(const AttnBwdArgs &a, float *dsig, int rows, int slot_coord,
+                             cudaStream_t st);
+// out[map(c)] (+)= sum_r X[r*ld + c], c < ncols; map(c) = (c/seg)*ostride + c%seg.
+cudaError_t launch_colsum(const float *X, int rows, int ncols, long ld, float *out, int seg,
+                          long ostride, bool accumulate, cudaStream_t st);
+cudaError_t launch_add(float *dst, const float *a, const float *b, size_t n, cudaStream_t st);
+
+// optimizer / renorm
+cudaError_t launch_adam(float *w, const float *g, float *m1, float *m2, size_t n, float lr,
+                        float b1, float b2, float eps, float bc1, float bc2, float gs,
+                        cudaStream_t st);
+cudaError_t launch_clipped_sgd(float *w, const float *g, size_t n, size_t main_len, float lr,
+                               float wd, float gs, cudaStream_t st);
+cudaError_t launch_spectral(float *W, int d, int h, const Layout &L, int n_iters, float attn,
+                            float win, float fpm, float wv, float wo, float *sigmas,
+                            cudaStream_t st);
+
+// LM head helpers
+cudaError_t launch_count_active(const int32_t *tg, int N, float *out, cudaStream_t st);
+cudaError_t launch_softmax_ce(float *logits, const float *bias, const int32_t *tg,
+                              const float *n_active, int N, int V, float *loss_rows, cudaStream_t st);
+cudaError_t launch_rmsnorm_bwd(const float *dy, const float *P, const float *lrms,
+                               const float *g, float *dl_dh, float *ggp, int N, int d,
+                               cudaStream_t st);
+cudaError_t launch_sum(const float *x, int n, float *out, cudaStream_t st);
+
+}  // namespace aideen

@@ -1,0 +1,262 @@
+// Fused optimizer sweeps, spectral renormalisation and LM-head helpers.
+//
+//   adam        bias-corrected Adam, one float4 pass over w, g, m, v
+//               (aideen-training-lab/src/optimizer.rs:105-183)
+//   clipped_sgd w <- w*(1 - lr*wd [main weights]) - clamp(lr*g*scale, +-0.5)
+//               (fused_deq_update.wgsl:402-410, 809-823)
+//   spectral    power iteration + rescale, one CTA per matrix
+//               (aideen-block/src/shaders/spectral_renorm.wgsl:83-196)
+//   softmax_ce / rmsnorm_bwd: dense LM-head loss and dL/dH_pooled
+//               (lm_train.wgsl:79-130, 327-395)
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace aideen {
+
+__global__ void adam_kernel(float *__restrict__ w, const float *__restrict__ g, float *__restrict__ m1,
+                            float *__restrict__ m2, size_t n, float lr, float b1, float b2,
+                            float eps, float bc1, float bc2, float gs) {
+  const size_t n4 = n / 4;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 gg = gs * ld4(g + 4 * i);
+    const float4 m = b1 * ld4(m1 + 4 * i) + (1.f - b1) * gg;
+    const float4 v = b2 * ld4(m2 + 4 * i) + (1.f - b2) * (gg * gg);
+    st4(m1 + 4 * i, m);
+    st4(m2 + 4 * i, v);
+    float4 ww = ld4(w + 4 * i);
+    ww.x -= lr * (m.x / bc1) / (sqrtf(v.x / bc2) + eps);
+    ww.y -= lr * (m.y / bc1) / (sqrtf(v.y / bc2) + eps);
+    ww.z -= lr * (m.z / bc1) / (sqrtf(v.z / bc2) + eps);
+    ww.w -= lr * (m.w / bc1) / (sqrtf(v.w / bc2) + eps);
+    st4(w + 4 * i, ww);
+  }
+  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {  // tail
+    const size_t i = n4 * 4 + threadIdx.x;
+    const float gg = gs * g[i];
+    const float m = b1 * m1[i] + (1.f - b1) * gg;
+    const float v = b2 * m2[i] + (1.f - b2) * gg * gg;
+    m1[i] = m;
+    m2[i] = v;
+    w[i] -= lr * (m / bc1) / (sqrtf(v / bc2) + eps);
+  }
+}
+
+__global__ void clipped_sgd_kernel(float *__restrict__ w, const float *__restrict__ g, size_t n,
+                                   size_t main_len, float lr, float wd, float gs) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float mult = i < main_len ? 1.f - lr * wd : 1.f;
+    const float step = fminf(fmaxf(lr * g[i] * gs, -0.5f), 0.5f);
+    w[i] = w[i] * mult - step;
+  }
+}
+
+static int sweep_blocks(size_t n4) {
+  size_t b = (n4 + 255) / 256;
+  if (b > 148 * 8) b = 148 * 8;
+  return b < 1 ? 1 : (int)b;
+}
+
+cudaError_t launch_adam(float *w, const float *g, float *m1, float *m2, size_t n, float lr, float b1,
+                        float b2, float eps, float bc1, float bc2, float gs, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  adam_kernel<<<sweep_blocks(n / 4), 256, 0, st>>>(w, g, m1, m2, n, lr, b1, b2, eps, bc1, bc2, gs);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_clipped_sgd(float *w, const float *g, size_t n, size_t main_len, float lr,
+                               float wd, float gs, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  clipped_sgd_kernel<<<sweep_blocks(n), 256, 0, st>>>(w, g, n, main_len, lr, wd, gs);
+  return cudaGetLastError();
+}
+
+// One CTA (1024 threads) per matrix.  Row-major view A[r][c] = M[r*d + c]:
+// v = A^T u / |A^T u|, u = A v, sigma = |u|, u /= sigma; rescale if sigma > thr.
+struct SpecArgs {
+  float *W;
+  int d, h, n_iters;
+  size_t wq, wk, wv, wo, win, wx, wout;
+  float attn, winth, fpm, wvth, woth;
+  float *sigmas;
+};
+
+__global__ void __launch_bounds__(1024) spectral_kernel(SpecArgs a) {
+  extern __shared__ float sm[];
+  float *u = sm, *v = sm + a.d, *red = sm + 2 * a.d;  // red: 64
+  const int mi = blockIdx.x, h = a.h, d = a.d;
+  size_t off;
+  float thr;
+  if (mi < h) { off = a.wq + (size_t)mi * d * d; thr = a.attn; }
+  else if (mi < 2 * h) { off = a.wk + (size_t)(mi - h) * d * d; thr = a.attn; }
+  else if (mi < 3 * h) { off = a.wv + (size_t)(mi - 2 * h) * d * d; thr = a.wvth; }
+  else if (mi < 4 * h) { off = a.wo + (size_t)(mi - 3 * h) * d * d; thr = a.woth; }
+  else if (mi < 5 * h) { off = a.win + (size_t)(mi - 4 * h) * d * d; thr = a.winth; }
+  else if (mi == 5 * h) { off = a.wx; thr = a.fpm; }
+  else { off = a.wout; thr = a.fpm; }
+  float *M = a.W + off;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  const float u0 = 1.f / sqrtf((float)d);
+  for (int i = tid; i < d; i += blockDim.x) u[i] = u0;
+  __syncthreads();
+  float sigma = 1.f;
+  for (int it = 0; it < a.n_iters; ++it) {
+    float part = 0.f;
+    for (int c = tid; c < d; c += blockDim.x) {  // v[c] = sum_r A[r][c] u[r]
+      float acc = 0.f;
+      for (int r = 0; r < d; ++r) acc += M[(size_t)r * d + c] * u[r];
+      v[c] = acc;
+      part += acc * acc;
+    }
+    part = warp_sum(part);
+    if (lane == 0) red[warp] = part;
+    __syncthreads();
+    float vn = 0.f;
+    for (int w = 0; w < nw; ++w) vn += red[w];
+    vn = sqrtf(vn + 1e-12f);
+    for (int c = tid; c < d; c += blockDim.x) v[c] /= vn;
+    __syncthreads();
+    float upart = 0.f;
+    for (int r = warp; r < d; r += nw) {  // u[r] = sum_c A[r][c] v[c], warp per row
+      float acc = 0.f;
+      for (int c = lane; c < d; c += 32) acc += M[(size_t)r * d + c] * v[c];
+      acc = warp_sum(acc);
+      if (lane == 0) { u[r] = acc; upart += acc * acc; }
+    }
+    if (lane == 0) red[32 + warp] = upart;
+    __syncthreads();
+    float un = 0.f;
+    for (int w = 0; w < nw; ++w) un += red[32 + w];
+    sigma = sqrtf(un + 1e-12f);
+    for (int r = tid; r < d; r += blockDim.x) u[r] /= sigma;
+    __syncthreads();
+  }
+  if (tid == 0 && a.sigmas) a.sigmas[mi] = sigma;
+  if (sigma > thr) {
+    const float sc = thr / sigma;
+    for (size_t i = tid; i < (size_t)d * d; i += blockDim.x) M[i] *= sc;
+  }
+}
+
+cudaError_t launch_spectral(float *W, int d, int h, const Layout &L, int n_iters, float attn,
+                            float win, float fpm, float wv, float wo, float *sigmas,
+                            cudaStream_t st) {
+  SpecArgs a{W, d, h, n_iters, L.wq, L.wk, L.wv, L.wo, L.win, L.wx, L.wout,
+             attn, win, fpm, wv, wo, sigmas};
+  const size_t smem = (2 * (size_t)d + 64) * sizeof(float);
+  spectral_kernel<<<5 * h + 2, 1024, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- LM head
+__global__ void count_active_kernel(const int32_t *__restrict__ tg, int N, float *out) {
+  __shared__ int cnt;
+  if (threadIdx.x == 0) cnt = 0;
+  __syncthreads();
+  int c = 0;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) c += tg[i] >= 0;
+  atomicAdd(&cnt, c);
+  __syncthreads();
+  if (threadIdx.x == 0) *out = (float)(cnt > 0 ? cnt : 1);
+}
+
+cudaError_t launch_count_active(const int32_t *tg, int N, float *out, cudaStream_t st) {
+  count_active_kernel<<<1, 1024, 0, st>>>(tg, N, out);
+  return cudaGetLastError();
+}
+
+// One block per row: logits += b_lm, online max/sum, then dlogits = (softmax - onehot)/n_active in place.
+__global__ void softmax_ce_kernel(float *__restrict__ logits, const float *__restrict__ bias,
+                                  const int32_t *__restrict__ tg,
+                                  const float *__restrict__ n_active, int V,
+                                  float *__restrict__ loss_rows) {
+  __shared__ float rm[32], rs[32];
+  const int n = blockIdx.x;
+  float *row = logits + (size_t)n * V;
+  const int t = tg[n];
+  float m = -INFINITY, s = 0.f;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float x = row[i] + bias[i];
+    row[i] = x;
+    if (x > m) { s = s * expf(m - x) + 1.f; m = x; }
+    else s += expf(x - m);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    const float mm = fmaxf(m, m2);
+    s = (m == -INFINITY ? 0.f : s * expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * expf(m2 - mm));
+    m = mm;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) { rm[warp] = m; rs[warp] = s; }
+  __syncthreads();
+  float M = -INFINITY;
+  for (int w = 0; w < nw; ++w) M = fmaxf(M, rm[w]);
+  float S = 0.f;
+  for (int w = 0; w < nw; ++w) S += (rm[w] == -INFINITY) ? 0.f : rs[w] * expf(rm[w] - M);
+  const float inv_na = 1.f / *n_active;
+  if (t < 0 || t >= V) {
+    for (int i = threadIdx.x; i < V; i += blockDim.x) row[i] = 0.f;
+    if (threadIdx.x == 0) loss_rows[n] = 0.f;
+    return;
+  }
+  const float lt = row[t];
+  __syncthreads();  // every thread has read row[t] before it is overwritten
+  if (threadIdx.x == 0) loss_rows[n] = -(lt - M - logf(S)) * inv_na;
+  const float invS = 1.f / S;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    float p = expf(row[i] - M) * invS;
+    if (i == t) p -= 1.f;
+    row[i] = p * inv_na;
+  }
+}
+
+cudaError_t launch_softmax_ce(float *logits, const float *bias, const int32_t *tg,
+                              const float *n_active, int N, int V, float *loss_rows, cudaStream_t st) {
+  if (N <= 0) return cudaSuccess;
+  softmax_ce_kernel<<<N, 1024, 0, st>>>(logits, bias, tg, n_active, V, loss_rows);
+  return cudaGetLastError();
+}
+
+// dl_dh = g/r * dy - P * (sum dy*g*P) / (d r^3); ggp = dy * P / r (per-token gain-gradient part)
+__global__ void rmsnorm_bwd_kernel(const float *__restrict__ dy, const float *__restrict__ P,
+                                   const float *__restrict__ lrms, const float *__restrict__ g,
+                                   float *__restrict__ dl_dh, float *__restrict__ ggp, int d) {
+  __shared__ float red[512];
+  const int n = blockIdx.x, j0 = threadIdx.x * 4;
+  const float4 dd = ld4(dy + (size_t)n * d + j0), p = ld4(P + (size_t)n * d + j0), gg = ld4(g + j0);
+  const float r = lrms[n];
+  const float4 dyg = dd * gg;
+  BlockReducer R(red);
+  float v[1] = {dot4(dyg, p)};
+  R.sum(v);
+  const float coef = v[0] / ((float)d * r * r * r);
+  const float ir = 1.f / r;
+  st4(dl_dh + (size_t)n * d + j0, ir * dyg - coef * p);
+  st4(ggp + (size_t)n * d + j0, ir * (dd * p));
+}
+
+cudaError_t launch_rmsnorm_bwd(const float *dy, const float *P, const float *lrms, const float *g,
+                               float *dl_dh, float *ggp, int N, int d, cudaStream_t st) {
+  if (N <= 0) return cudaSuccess;
+  rmsnorm_bwd_kernel<<<N, d / 4, 0, st>>>(dy, P, lrms, g, dl_dh, ggp, d);
+  return cudaGetLastError();
+}
+
+__global__ void sum_kernel(const float *__restrict__ x, int n, float *out) {
+  __shared__ float red[512];
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
+  BlockReducer R(red);
+  float v[1] = {s};
+  R.sum(v);
+  if (threadIdx.x == 0) *out = v[0];
+}
+
+cudaError_t launch_sum(const float *x, int n, float *out, cudaStream_t st) {
+  sum_kernel<<<1, 1024, 0, st>>>(x, n, out);
+  return cudaGetLastError();
+}
+
+}  // namespace aideen

@@ -1,0 +1,225 @@
+/*
+ * aideen_b200 — C ABI of the B200-native AIDEEN DEQ training hot path.
+ *
+ * Drop-in boundary for the reference's `GpuDeqBackend`
+ * (aideen-backbone/src/gpu_deq.rs:80-218) wrapping `RustDeqBridge`
+ * (aideen-block/src/deq_bridge.rs:55-101).  Plain pointers and sizes only; no
+ * torch and no CUDA types in the signatures (streams are passed as void*).
+ *
+ * Ownership: the context owns every device buffer, sized at create time from
+ * the caps in `aideen_cfg` (the reference sizes its wgpu buffers from
+ * `forward_seq_cap/forward_batch_cap`, gpu_deq.rs:82-83).  Caller memory is
+ * only read or written during the call.  Pointers flagged AIDEEN_DEVICE are
+ * device pointers on the context's device, ordered on the context's stream.
+ *
+ * Errors: every call returns an `aideen_status`; `aideen_last_error` gives the
+ * message.  No call aborts the process.  A context is single-thread affine.
+ *
+ * Layouts (identical to the reference so its trainer needs no change):
+ *   AllWeights   deq_bridge.rs:103-137 (+ HistParams gpu_deq.rs:260-422)
+ *   S_in         [B*T][d]               token-major
+ *   H* / HistCtx [B*T][h][d]            deq_slot_attn_unified_clean.wgsl:712
+ *   MState       [B][h][d]
+ *   dl_dh        [B*T][d]
+ *   adjoint v    [h][B*T][d] slot-major staged_adjoint_picard_clean.wgsl:57-67
+ */
+#ifndef AIDEEN_B200_H
+#define AIDEEN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum aideen_status {
+  AIDEEN_OK = 0,
+  AIDEEN_E_INVALID = 1,   /* bad argument / size beyond caps */
+  AIDEEN_E_CUDA = 2,      /* CUDA runtime or cuBLAS failure */
+  AIDEEN_E_NCCL = 3,      /* collective failure */
+  AIDEEN_E_TIMEOUT = 4,   /* bounded wait ran out */
+  AIDEEN_E_NONFINITE = 5, /* non-finite value detected in a checked buffer */
+  AIDEEN_E_UNSUPPORTED = 6
+} aideen_status;
+
+enum { AIDEEN_HOST = 0, AIDEEN_DEVICE = 1 };
+
+/* Construction caps + static architecture (ArchitectureConfig,
+ * aideen-core/src/state.rs:7-58).  d_model in {128, 256, 512, 1024};
+ * h_slots in [1, 16]. */
+typedef struct aideen_cfg {
+  uint32_t d_model;
+  uint32_t h_slots;
+  uint32_t max_batch;    /* forward_batch_cap */
+  uint32_t max_seq_len;  /* forward_seq_cap */
+  uint32_t vocab;        /* LM head / embedding rows; 0 = no LM head */
+  uint32_t flags;        /* reserved, 0 */
+} aideen_cfg;
+
+/* One forward dispatch (RunUniforms, deq_slot_attn_unified_clean.wgsl:1-21;
+ * DeqComputeShape, deq_bridge.rs:4-25). */
+typedef struct aideen_run {
+  uint32_t batch;
+  uint32_t seq_len;
+  uint32_t max_iters;
+  float epsilon;
+  float damping;          /* Picard blend of the generic path; adjoint beta */
+  uint32_t slot_coord;    /* 1 = iter-0 slot attention on (residual_alpha = -1) */
+  uint32_t fpm;           /* 1 = FPM memory read/inject/write (Model A) */
+  float fpm_alpha_m;
+  float fpm_tau;
+  float fpm_read_gate_min;
+} aideen_run;
+
+/* Forward convergence statistics (DebugLog[13..17] equivalents). */
+typedef struct aideen_stats {
+  uint64_t total_iters;   /* summed over (b, t, slot) */
+  uint32_t max_iters_seen;
+  uint32_t unconverged;   /* solves that ran to max_iters */
+  uint32_t nonfinite;     /* (token, slot) rows of h* holding a non-finite value */
+  uint32_t solves;        /* B*T*h */
+} aideen_stats;
+
+/* Adjoint call (run_staged_adjoint_picard_no_readback, gpu_deq.rs:4080). */
+typedef struct aideen_adjoint_args {
+  uint32_t batch;
+  uint32_t seq_len;
+  uint32_t iters;         /* fixed count, no early exit (gpu_deq.rs:4879) */
+  float damping;
+  uint32_t anderson_m;    /* 0 = off, else ring depth (<= 4) */
+} aideen_adjoint_args;
+
+/* Fused update (apply_fused_deq_update gpu_deq.rs:4980; apply_gradient_update :5509). */
+enum { AIDEEN_RULE_ADAM = 0, AIDEEN_RULE_CLIPPED_SGD = 1 };
+typedef struct aideen_update {
+  uint32_t rule;
+  float lr;
+  float beta1, beta2, eps;   /* Adam (optimizer.rs:105-183) */
+  float weight_decay;        /* clipped SGD main-weight decay */
+  float grad_scale;          /* multiplies the gradient before the rule */
+  uint32_t step;             /* Adam step t (>= 1) */
+  uint32_t allreduce;        /* 1 = sum gradients over the communicator first */
+  uint32_t update_lm_head;   /* 1 = also apply the rule to the LM head */
+} aideen_update;
+
+typedef struct aideen_ctx aideen_ctx;
+
+/* ---- lifecycle (GpuDeqBackend::new_blocking, gpu_deq.rs:3122) ---------- */
+aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status);
+void aideen_destroy(aideen_ctx *ctx);
+const char *aideen_last_error(const aideen_ctx *ctx);
+int aideen_set_stream(aideen_ctx *ctx, void *cuda_stream);
+int aideen_sync(aideen_ctx *ctx);
+/* Number of this library's own kernel launches issued since create. */
+uint64_t aideen_launch_count(const aideen_ctx *ctx);
+
+/* Length of AllWeights for (d, h) (deq_bridge.rs:103-137). */
+size_t aideen_all_weights_len(uint32_t d_model, uint32_t h_slots);
+
+/* ---- weights (upload_weights gpu_deq.rs:3529; read_weights :5595) -------- */
+int aideen_upload_weights(aideen_ctx *ctx, const float *all_weights, size_t n, int where);
+int aideen_download_weights(aideen_ctx *ctx, float *out, size_t n);
+int aideen_download_grads(aideen_ctx *ctx, float *out, size_t n);
+/* LM head W_lm [vocab][d], b_lm [vocab], g_lm [d] (lm_train.wgsl bindings 2, 3, 10). */
+int aideen_upload_lm_head(aideen_ctx *ctx, const float *w_lm, const float *b_lm,
+                          const float *g_lm);
+int aideen_download_lm_head(aideen_ctx *ctx, float *w_lm, float *b_lm, float *g_lm);
+int aideen_upload_embedding(aideen_ctx *ctx, const float *emb /*[vocab][d]*/);
+/* Zero the carried FPM memory MState (reset_state gpu_deq.rs:3127). */
+int aideen_reset_state(aideen_ctx *ctx);
+/* Zero the Adam moments of the DEQ core and LM head. */
+int aideen_reset_optimizer(aideen_ctx *ctx);
+
+/* ---- forward (run_forward_deq_no_readback gpu_deq.rs:3855;
+ *      run_forward_from_seq_buf :3918) ------------------------------------ */
+int aideen_forward(aideen_ctx *ctx, const aideen_run *run, const float *s_in, int where,
+                   aideen_stats *stats /*nullable*/);
+/* Token ids -> S_in by embedding gather, then the forward
+ * (GpuEmbeddingTrainer::gather_only_to_sbuf, trainer.rs:2823). */
+int aideen_forward_tokens(aideen_ctx *ctx, const aideen_run *run, const int32_t *tokens,
+                          int where, aideen_stats *stats);
+
+/* ---- LM head: dense CE + RMSNorm backward -> dl_dh (lm_train.wgsl:79-395).
+ * Also leaves the LM-head gradients for aideen_apply_update. */
+int aideen_lm_head_loss(aideen_ctx *ctx, uint32_t batch, uint32_t seq_len,
+                        const int32_t *targets, int where, float *loss_out /*host*/);
+
+/* ---- adjoint (run_staged_adjoint_picard_no_readback gpu_deq.rs:4080) ----
+ * dl_dh: [B*T][d] pooled upstream gradient; NULL = the LM head's last dl_dh.
+ * rhs_slot: optional [B*T][h][d] per-slot RHS added to dl_dh/h.
+ * Linearises around the state of the last aideen_forward. */
+int aideen_adjoint(aideen_ctx *ctx, const aideen_adjoint_args *args, const float *dl_dh,
+                   const float *rhs_slot, int where);
+/* Adjoint on caller-provided fixed point (isolated adjoint benchmark): pre =
+ * branch + hstar, both [B*T][h][d] (branch = signal + attn*scale + anchor). */
+int aideen_adjoint_on(aideen_ctx *ctx, const aideen_adjoint_args *args, const float *hstar,
+                      const float *branch, const float *dl_dh, const float *rhs_slot,
+                      int where);
+/* reduce_clean_adjoint_to_source_grad_no_readback (gpu_deq.rs:4922):
+ * out[B*T][d] = sum_s beta*J_norm^T v. */
+int aideen_source_grad(aideen_ctx *ctx, float *out, int where);
+
+/* ---- gradients + update (apply_fused_deq_update gpu_deq.rs:4980) -------- */
+int aideen_weight_grads(aideen_ctx *ctx);
+int aideen_apply_update(aideen_ctx *ctx, const aideen_update *upd);
+
+/* ---- spectral renorm (renormalize_spectral gpu_deq.rs:5568) -------------- */
+int aideen_renormalize_spectral(aideen_ctx *ctx, uint32_t n_iters, float attn_threshold,
+                                float win_threshold, float fpm_threshold,
+                                float wv_threshold, float wo_threshold,
+                                float *sigmas_out /*nullable, 5h+2 host floats*/);
+
+/* ---- whole training step (Trainer::apply_training_update_from_gpu_buffers,
+ *      trainer.rs:2640): gather -> forward -> LM head -> adjoint -> grads ->
+ *      [allreduce] -> update -> [renorm]. ----------------------------------- */
+typedef struct aideen_step_args {
+  aideen_run run;
+  uint32_t adj_iters;
+  uint32_t anderson_m;
+  aideen_update update;
+  uint32_t renorm;           /* 1 = spectral renorm after the update (reference thresholds) */
+} aideen_step_args;
+int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *args, const int32_t *tokens,
+                      const int32_t *targets, int where, float *loss_out /*host, nullable*/,
+                      aideen_stats *stats /*nullable*/);
+
+/* ---- readbacks (read_hnext_seq gpu_deq.rs:5842, read_hpooled_seq :5886,
+ *      read_adj_v_out :5821, ...) ----------------------------------------- */
+enum aideen_buf {
+  AIDEEN_BUF_HSTAR = 0,     /* [N][h][d] */
+  AIDEEN_BUF_POOLED = 1,    /* [N][d] */
+  AIDEEN_BUF_SIGNAL = 2,    /* [N][h][d] */
+  AIDEEN_BUF_ATTN = 3,      /* [N][h][d] attention injection attn*scale */
+  AIDEEN_BUF_ITERS = 4,     /* [N][h] int32 */
+  AIDEEN_BUF_ADJ_V = 5,     /* [h][N][d] */
+  AIDEEN_BUF_GPRE = 6,      /* [N][h][d] beta*J_norm^T v */
+  AIDEEN_BUF_DL_DH = 7,     /* [N][d] */
+  AIDEEN_BUF_HIST_CTX = 8,  /* [N][h][d] */
+  AIDEEN_BUF_MSTATE = 9,    /* [B][h][d] */
+  AIDEEN_BUF_FPM_CTX = 10,  /* [N][h][d] */
+  AIDEEN_BUF_ALPHA = 11,    /* [N][h][h] */
+  AIDEEN_BUF_S_IN = 12,     /* [N][d] */
+  AIDEEN_BUF_DS_IN = 13,    /* [N][d] exact dL/dS_in */
+  AIDEEN_BUF_LM_GRADS = 14, /* [vocab*d + vocab + d] */
+  AIDEEN_BUF_PRE = 15       /* [N][h][d] pre = branch + h* of the adjoint */
+};
+/* Copies the first n_elems elements (4 bytes each) of a buffer to host dst. */
+int aideen_read(aideen_ctx *ctx, int which, void *dst, size_t n_elems);
+/* Device pointer of a buffer (zero-copy consumers); NULL if absent. */
+void *aideen_device_ptr(aideen_ctx *ctx, int which);
+
+/* ---- multi-GPU (one process per GPU; NCCL over NVLink) ----------------- */
+#define AIDEEN_UNIQUE_ID_BYTES 128
+int aideen_comm_unique_id(char out[AIDEEN_UNIQUE_ID_BYTES]);
+int aideen_comm_init(aideen_ctx *ctx, const char id[AIDEEN_UNIQUE_ID_BYTES], int nranks,
+                     int rank);
+/* Sum-allreduce of the gradient buffers (DEQ core and LM head) over the
+ * communicator; waits at most timeout_ms, then aborts the communicator and
+ * returns AIDEEN_E_TIMEOUT. */
+int aideen_allreduce_grads(aideen_ctx *ctx, int timeout_ms);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AIDEEN_B200_H */
