@@ -40,6 +40,7 @@ struct DevBufs {
   float *emb = nullptr;
   unsigned long long *stats = nullptr;
   float *sigmas = nullptr;
+  float *stage = nullptr;  // packed AllWeights staging for upload/download
 };
 
 }  // namespace
@@ -55,6 +56,7 @@ struct aideen_ctx {
   std::string err;
   unsigned long long launches = 0;
   size_t W_len = 0, lm_len = 0, max_tokens = 0;
+  size_t lm_b = 0, lm_g = 0;   // offsets of b_lm and g_lm in the padded LM block
   float signal_scale = 1.f;
   bool signal_zero = false;
   aideen_run last_run{};
@@ -63,7 +65,8 @@ struct aideen_ctx {
   float adj_beta = 0.85f;
   bool lm_ready = false, emb_ready = false;
   DevBufs b;
-  Layout L{128, 1};
+  Layout P{128, 1, 64};   // device (padded) layout
+  Layout Lx{128, 1};      // packed reference layout at the boundary
 };
 
 namespace {
@@ -139,7 +142,7 @@ int check_run(aideen_ctx *ctx, const aideen_run *r) {
 int run_forward(aideen_ctx *ctx, const aideen_run *r, aideen_stats *stats) {
   const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
   const int N = r->batch * r->seq_len;
-  const Layout &L = ctx->L;
+  const Layout &L = ctx->P;
   DevBufs &b = ctx->b;
   cudaStream_t st = ctx->stream;
   const float *W = b.W;
@@ -184,7 +187,7 @@ int run_forward(aideen_ctx *ctx, const aideen_run *r, aideen_stats *stats) {
   p.hstar = b.hstar; p.pre = b.pre; p.hist = b.hist; p.fpmctx = b.fpmctx; p.mstate = b.mstate;
   p.iters = b.iters;
   KL(launch_picard(p, r->fpm != 0, st));
-  KL(launch_pool_rmsnorm(b.hstar, ctx->lm_ready ? b.lmp + (size_t)ctx->cfg.vocab * d + ctx->cfg.vocab : nullptr,
+  KL(launch_pool_rmsnorm(b.hstar, ctx->lm_ready ? b.lmp + ctx->lm_g : nullptr,
                          b.pooled, ctx->lm_ready ? b.y : nullptr, b.lrms, N, h, d, st));
   ctx->last_run = *r;
   ctx->N = N;
@@ -208,13 +211,13 @@ int run_lm_head(aideen_ctx *ctx, int N, float *loss_out) {
   const int d = ctx->cfg.d_model, V = ctx->cfg.vocab;
   DevBufs &b = ctx->b;
   cudaStream_t st = ctx->stream;
-  const float *Wlm = b.lmp, *glm = b.lmp + (size_t)V * d + V;
+  const float *Wlm = b.lmp, *glm = b.lmp + ctx->lm_g;
   const float one = 1.f, zero = 0.f;
   KL(launch_count_active(b.targets, N, b.scal, st));
   // logits^T (V x N, col-major) = W_lm (d x V col-major)^T . y (d x N col-major); then + b_lm
   CB(cublasSgemm(ctx->cublas, CUBLAS_OP_T, CUBLAS_OP_N, V, N, d, &one, Wlm, d, b.y, d, &zero,
                  b.logits, V));
-  KL(launch_softmax_ce(b.logits, b.lmp + (size_t)V * d, b.targets, b.scal, N, V, b.loss_rows, st));
+  KL(launch_softmax_ce(b.logits, b.lmp + ctx->lm_b, b.targets, b.scal, N, V, b.loss_rows, st));
   KL(launch_sum(b.loss_rows, N, b.scal + 1, st));
   // dy (d x N col-major) = W_lm (d x V) . dlog (V x N)
   CB(cublasSgemm(ctx->cublas, CUBLAS_OP_N, CUBLAS_OP_N, d, N, V, &one, Wlm, d, b.logits, V, &zero,
@@ -222,9 +225,9 @@ int run_lm_head(aideen_ctx *ctx, int N, float *loss_out) {
   // dW_lm^T (d x V col-major) = y (d x N) . dlog^T (N x V)
   CB(cublasSgemm(ctx->cublas, CUBLAS_OP_N, CUBLAS_OP_T, d, V, N, &one, b.y, d, b.logits, V, &zero,
                  b.Glm, d));
-  KL(launch_colsum(b.logits, N, V, V, b.Glm + (size_t)V * d, V, 0, false, st));
+  KL(launch_colsum(b.logits, N, V, V, b.Glm + ctx->lm_b, V, 0, false, st));
   KL(launch_rmsnorm_bwd(b.dy, b.pooled, b.lrms, glm, b.dl_dh, b.ggp, N, d, st));
-  KL(launch_colsum(b.ggp, N, d, d, b.Glm + (size_t)V * d + V, d, 0, false, st));
+  KL(launch_colsum(b.ggp, N, d, d, b.Glm + ctx->lm_g, d, 0, false, st));
   if (loss_out) {
     CU(cudaMemcpyAsync(loss_out, b.scal + 1, sizeof(float), cudaMemcpyDeviceToHost, st));
     CU(cudaStreamSynchronize(st));
@@ -240,7 +243,7 @@ int run_adjoint(aideen_ctx *ctx, int N, const float *pre_a, const float *pre_b,
   a.N = N; a.h = ctx->cfg.h_slots; a.d = ctx->cfg.d_model; a.iters = iters;
   a.anderson_m = anderson_m; a.beta = beta;
   a.pre_a = pre_a; a.pre_b = pre_b; a.rhs_tok = rhs_tok; a.rhs_slot = rhs_slot;
-  a.NS = ctx->b.W + ctx->L.nscale; a.v = ctx->b.v; a.gpre = ctx->b.gpre; a.nsg = ctx->b.nsg;
+  a.NS = ctx->b.W + ctx->P.nscale; a.v = ctx->b.v; a.gpre = ctx->b.gpre; a.nsg = ctx->b.nsg;
   KL(launch_adjoint(a, ctx->stream));
   ctx->adj_N = N;
   ctx->adj_beta = beta;
@@ -252,7 +255,7 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   const int N = ctx->N;
   if (N == 0 || ctx->adj_N != ctx->N)
     return set_err(ctx, AIDEEN_E_INVALID, "weight grads need a forward and an adjoint over the same tokens");
-  const Layout &L = ctx->L;
+  const Layout &L = ctx->P;
   DevBufs &b = ctx->b;
   cudaStream_t st = ctx->stream;
   const float *W = b.W;
@@ -356,7 +359,7 @@ int run_update(aideen_ctx *ctx, const aideen_update *u) {
       KL(launch_adam(b.lmp, b.Glm, b.Mlm1, b.Mlm2, ctx->lm_len, u->lr, u->beta1, u->beta2, u->eps,
                      bc1, bc2, u->grad_scale, st));
   } else if (u->rule == AIDEEN_RULE_CLIPPED_SGD) {
-    KL(launch_clipped_sgd(b.W, b.G, ctx->W_len, ctx->L.hist, u->lr, u->weight_decay, u->grad_scale, st));
+    KL(launch_clipped_sgd(b.W, b.G, ctx->W_len, ctx->P.hist, u->lr, u->weight_decay, u->grad_scale, st));
     if (u->update_lm_head && ctx->lm_ready)
       KL(launch_clipped_sgd(b.lmp, b.Glm, ctx->lm_len, ctx->lm_len, u->lr, u->weight_decay,
                             u->grad_scale, st));
@@ -370,7 +373,7 @@ int run_update(aideen_ctx *ctx, const aideen_update *u) {
 
 extern "C" {
 
-size_t aideen_all_weights_len(uint32_t d, uint32_t h) { return Layout(d, h).total; }
+size_t aideen_all_weights_len(uint32_t d, uint32_t h) { return Layout(d, h, 1).total; }
 
 const char *aideen_last_error(const aideen_ctx *ctx) { return ctx ? ctx->err.c_str() : "null context"; }
 
@@ -390,12 +393,15 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   aideen_ctx *ctx = new aideen_ctx();
   ctx->cfg = *cfg;
   ctx->device = device;
-  ctx->L = Layout(d, h);
-  ctx->W_len = ctx->L.total;
+  ctx->P = Layout(d, h, 64);
+  ctx->Lx = Layout(d, h, 1);
+  ctx->W_len = ctx->P.total;
   const size_t N = (size_t)cfg->max_batch * cfg->max_seq_len;
   ctx->max_tokens = N;
   const size_t V = cfg->vocab;
-  ctx->lm_len = V ? V * d + V + d : 0;
+  ctx->lm_b = V * d;
+  ctx->lm_g = V * d + (V + 63) / 64 * 64;
+  ctx->lm_len = V ? ctx->lm_g + d : 0;
   DevBufs &b = ctx->b;
   const size_t Nhd = N * h * d, NH32 = N * h * kHeadDim;
   cudaError_t e = cudaSuccess;
@@ -412,7 +418,7 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   A(&b.mstate, (size_t)cfg->max_batch * h * d);
   A(&b.pooled, N * d); A(&b.dl_dh, N * d); A(&b.nsg, N * d); A(&b.dS, N * d);
   A(&b.y, N * d); A(&b.dy, N * d); A(&b.ggp, N * d); A(&b.lrms, N); A(&b.loss_rows, N);
-  A(&b.scal, 4); A(&b.stats, 4); A(&b.sigmas, 5 * h + 2);
+  A(&b.scal, 4); A(&b.stage, ctx->Lx.total); A(&b.stats, 4); A(&b.sigmas, 5 * h + 2);
   if (V) {
     A(&b.lmp, ctx->lm_len); A(&b.Glm, ctx->lm_len); A(&b.Mlm1, ctx->lm_len); A(&b.Mlm2, ctx->lm_len);
     A(&b.logits, N * V); A(&b.emb, V * d);
@@ -431,6 +437,8 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   // fp32-accurate tensor-core emulation (BF16x9) for the plain LM-head GEMMs
   cublasSetMathMode(ctx->cublas, CUBLAS_FP32_EMULATED_BF16X9_MATH);
   cudaMemsetAsync(b.mstate, 0, (size_t)cfg->max_batch * h * d * sizeof(float), ctx->stream);
+  cudaMemsetAsync(b.W, 0, ctx->W_len * sizeof(float), ctx->stream);
+  cudaMemsetAsync(b.G, 0, ctx->W_len * sizeof(float), ctx->stream);
   cudaMemsetAsync(b.M1, 0, ctx->W_len * sizeof(float), ctx->stream);
   cudaMemsetAsync(b.M2, 0, ctx->W_len * sizeof(float), ctx->stream);
   cudaMemsetAsync(b.hist, 0, Nhd * sizeof(float), ctx->stream);
@@ -459,7 +467,7 @@ void aideen_destroy(aideen_ctx *ctx) {
                   b.pooled, b.hist, b.fpmctx, b.mstate, b.iters, b.v, b.gpre, b.dl_dh, b.rhs_slot,
                   b.nsg, b.da, b.dn, b.dQ, b.dK, b.dV, b.dsig, b.dRc, b.dS, b.lmp, b.Glm, b.Mlm1,
                   b.Mlm2, b.y, b.lrms, b.logits, b.dy, b.ggp, b.loss_rows, b.scal, b.emb, b.stats,
-                  b.sigmas};
+                  b.sigmas, b.stage};
   for (void *p : ptrs)
     if (p) cudaFree(p);
   if (ctx->stream && ctx->own_stream) cudaStreamDestroy(ctx->stream);
@@ -482,31 +490,52 @@ int aideen_sync(aideen_ctx *ctx) {
   return AIDEEN_OK;
 }
 
+// Packed reference layout <-> padded device layout, one copy per tensor.
+static int repack(aideen_ctx *ctx, float *dst, const float *src, bool to_device, cudaMemcpyKind kind) {
+  for (int k = 0; k < kSegments; ++k) {
+    const size_t len = ctx->P.seg_len[k];
+    const size_t dof = to_device ? ctx->P.seg_off[k] : ctx->Lx.seg_off[k];
+    const size_t sof = to_device ? ctx->Lx.seg_off[k] : ctx->P.seg_off[k];
+    CU(cudaMemcpyAsync(dst + dof, src + sof, len * sizeof(float), kind, ctx->stream));
+  }
+  return AIDEEN_OK;
+}
+
 int aideen_upload_weights(aideen_ctx *ctx, const float *w, size_t n, int where) {
   if (!ctx) return AIDEEN_E_INVALID;
-  if (n != ctx->W_len) return set_err(ctx, AIDEEN_E_INVALID, "AllWeights length mismatch");
-  CHK(copy_in(ctx, ctx->b.W, w, n * sizeof(float), where));
+  if (n != ctx->Lx.total) return set_err(ctx, AIDEEN_E_INVALID, "AllWeights length mismatch");
+  if (!w) return set_err(ctx, AIDEEN_E_INVALID, "null weights");
+  if (where == AIDEEN_DEVICE) {
+    CHK(repack(ctx, ctx->b.W, w, true, cudaMemcpyDeviceToDevice));
+  } else {
+    CU(cudaMemcpyAsync(ctx->b.stage, w, n * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+    CHK(repack(ctx, ctx->b.W, ctx->b.stage, true, cudaMemcpyDeviceToDevice));
+  }
   float fl[2];
-  CU(cudaMemcpyAsync(&fl[0], ctx->b.W + ctx->L.signal_scale, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-  CU(cudaMemcpyAsync(&fl[1], ctx->b.W + ctx->L.signal_zero, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+  CU(cudaMemcpyAsync(&fl[0], ctx->b.W + ctx->P.signal_scale, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+  CU(cudaMemcpyAsync(&fl[1], ctx->b.W + ctx->P.signal_zero, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
   CU(cudaStreamSynchronize(ctx->stream));
   ctx->signal_scale = fl[0];
   ctx->signal_zero = fl[1] > 0.5f;
   return AIDEEN_OK;
 }
 
-int aideen_download_weights(aideen_ctx *ctx, float *out, size_t n) {
-  if (!ctx || !out || n > ctx->W_len) return set_err(ctx, AIDEEN_E_INVALID, "bad download");
-  CU(cudaMemcpyAsync(out, ctx->b.W, n * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+static int download_packed(aideen_ctx *ctx, const float *src, float *out, size_t n) {
+  if (!out || n > ctx->Lx.total) return set_err(ctx, AIDEEN_E_INVALID, "bad download size");
+  CHK(repack(ctx, ctx->b.stage, src, false, cudaMemcpyDeviceToDevice));
+  CU(cudaMemcpyAsync(out, ctx->b.stage, n * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
   CU(cudaStreamSynchronize(ctx->stream));
   return AIDEEN_OK;
 }
 
+int aideen_download_weights(aideen_ctx *ctx, float *out, size_t n) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  return download_packed(ctx, ctx->b.W, out, n);
+}
+
 int aideen_download_grads(aideen_ctx *ctx, float *out, size_t n) {
-  if (!ctx || !out || n > ctx->W_len) return set_err(ctx, AIDEEN_E_INVALID, "bad download");
-  CU(cudaMemcpyAsync(out, ctx->b.G, n * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-  CU(cudaStreamSynchronize(ctx->stream));
-  return AIDEEN_OK;
+  if (!ctx) return AIDEEN_E_INVALID;
+  return download_packed(ctx, ctx->b.G, out, n);
 }
 
 int aideen_upload_lm_head(aideen_ctx *ctx, const float *w_lm, const float *b_lm, const float *g_lm) {
@@ -514,8 +543,8 @@ int aideen_upload_lm_head(aideen_ctx *ctx, const float *w_lm, const float *b_lm,
   const size_t V = ctx->cfg.vocab, d = ctx->cfg.d_model;
   if (!V) return set_err(ctx, AIDEEN_E_INVALID, "context created with vocab = 0");
   CHK(copy_in(ctx, ctx->b.lmp, w_lm, V * d * sizeof(float), AIDEEN_HOST));
-  CHK(copy_in(ctx, ctx->b.lmp + V * d, b_lm, V * sizeof(float), AIDEEN_HOST));
-  CHK(copy_in(ctx, ctx->b.lmp + V * d + V, g_lm, d * sizeof(float), AIDEEN_HOST));
+  CHK(copy_in(ctx, ctx->b.lmp + ctx->lm_b, b_lm, V * sizeof(float), AIDEEN_HOST));
+  CHK(copy_in(ctx, ctx->b.lmp + ctx->lm_g, g_lm, d * sizeof(float), AIDEEN_HOST));
   CU(cudaStreamSynchronize(ctx->stream));
   ctx->lm_ready = true;
   return AIDEEN_OK;
@@ -525,8 +554,8 @@ int aideen_download_lm_head(aideen_ctx *ctx, float *w_lm, float *b_lm, float *g_
   if (!ctx || !ctx->lm_ready) return set_err(ctx, AIDEEN_E_INVALID, "no LM head");
   const size_t V = ctx->cfg.vocab, d = ctx->cfg.d_model;
   if (w_lm) CU(cudaMemcpyAsync(w_lm, ctx->b.lmp, V * d * 4, cudaMemcpyDeviceToHost, ctx->stream));
-  if (b_lm) CU(cudaMemcpyAsync(b_lm, ctx->b.lmp + V * d, V * 4, cudaMemcpyDeviceToHost, ctx->stream));
-  if (g_lm) CU(cudaMemcpyAsync(g_lm, ctx->b.lmp + V * d + V, d * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (b_lm) CU(cudaMemcpyAsync(b_lm, ctx->b.lmp + ctx->lm_b, V * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (g_lm) CU(cudaMemcpyAsync(g_lm, ctx->b.lmp + ctx->lm_g, d * 4, cudaMemcpyDeviceToHost, ctx->stream));
   CU(cudaStreamSynchronize(ctx->stream));
   return AIDEEN_OK;
 }
@@ -660,7 +689,7 @@ int aideen_apply_update(aideen_ctx *ctx, const aideen_update *u) {
 int aideen_renormalize_spectral(aideen_ctx *ctx, uint32_t n_iters, float attn, float win, float fpm,
                                 float wv, float wo, float *sig) {
   if (!ctx) return AIDEEN_E_INVALID;
-  KL(launch_spectral(ctx->b.W, ctx->cfg.d_model, ctx->cfg.h_slots, ctx->L, n_iters, attn, win, fpm,
+  KL(launch_spectral(ctx->b.W, ctx->cfg.d_model, ctx->cfg.h_slots, ctx->P, n_iters, attn, win, fpm,
                      wv, wo, ctx->b.sigmas, ctx->stream));
   if (sig) {
     CU(cudaMemcpyAsync(sig, ctx->b.sigmas, (5 * ctx->cfg.h_slots + 2) * 4, cudaMemcpyDeviceToHost,
@@ -687,7 +716,7 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
   CHK(run_weight_grads(ctx, false));
   CHK(run_update(ctx, &a->update));
   if (a->renorm)
-    KL(launch_spectral(ctx->b.W, ctx->cfg.d_model, ctx->cfg.h_slots, ctx->L, 12, 0.10f, 0.30f, 0.70f,
+    KL(launch_spectral(ctx->b.W, ctx->cfg.d_model, ctx->cfg.h_slots, ctx->P, 12, 0.10f, 0.30f, 0.70f,
                        0.50f, 0.50f, ctx->b.sigmas, ctx->stream));
   if (loss_out) {
     CU(cudaMemcpyAsync(loss_out, ctx->b.scal + 1, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
@@ -715,7 +744,7 @@ static void *buf_ptr(aideen_ctx *ctx, int which, size_t *count) {
     case AIDEEN_BUF_ALPHA: *count = N * h * h; return b.alpha;
     case AIDEEN_BUF_S_IN: *count = N * d; return b.S_in;
     case AIDEEN_BUF_DS_IN: *count = N * d; return b.dS;
-    case AIDEEN_BUF_LM_GRADS: *count = ctx->lm_len; return b.Glm;
+    case AIDEEN_BUF_LM_GRADS: *count = ctx->lm_len ? ctx->lm_b + ctx->cfg.vocab + d : 0; return b.Glm;
     case AIDEEN_BUF_PRE: *count = N * h * d; return b.pre;
     default: *count = 0; return nullptr;
   }
@@ -727,6 +756,17 @@ int aideen_read(aideen_ctx *ctx, int which, void *dst, size_t n) {
   void *p = buf_ptr(ctx, which, &count);
   if (!p) return set_err(ctx, AIDEEN_E_INVALID, "unknown or absent buffer");
   if (n > count) return set_err(ctx, AIDEEN_E_INVALID, "read beyond the buffer's valid extent");
+  if (which == AIDEEN_BUF_LM_GRADS) {  // packed [gW | gb | gg] from the padded block
+    const size_t segs[3][2] = {{0, ctx->lm_b}, {ctx->lm_b, ctx->cfg.vocab}, {ctx->lm_g, ctx->cfg.d_model}};
+    size_t o = 0;
+    for (auto &sg : segs) {
+      const size_t m = sg[1] < n - o ? sg[1] : n - o;
+      if (m) CU(cudaMemcpyAsync((float *)dst + o, ctx->b.Glm + sg[0], m * 4, cudaMemcpyDeviceToHost, ctx->stream));
+      o += m;
+    }
+    CU(cudaStreamSynchronize(ctx->stream));
+    return AIDEEN_OK;
+  }
   CU(cudaMemcpyAsync(dst, p, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
   CU(cudaStreamSynchronize(ctx->stream));
   return AIDEEN_OK;
