@@ -314,12 +314,15 @@ class GpuDeqBackend:
 
     def train_step(self, tokens, targets, batch, seq_len, cfg: RunConfig, adj_iters=12,
                    anderson_m=0, lr=1e-3, step=1, rule=RULE_ADAM, renorm=False, allreduce=False,
-                   grad_scale=1.0, where=HOST, want_loss=True):
+                   grad_scale=1.0, where=HOST, want_loss=True, raw_ptr=False):
+        """One full step.  With raw_ptr=True, `tokens`/`targets` are integer
+        addresses (device memory when where=DEVICE, pinned host memory when
+        where=HOST) instead of arrays."""
         a = StepArgs(cfg.run(batch, seq_len), adj_iters, anderson_m,
                      Update(rule, lr, 0.9, 0.999, 1e-8, 0.0, grad_scale, step, int(allreduce), 1),
                      int(renorm))
         loss = C.c_float(0.0)
-        if where == HOST:
+        if not raw_ptr:
             t, g = _i32(tokens), _i32(targets)
             tp, gp = _ptr(t), _ptr(g)
         else:
