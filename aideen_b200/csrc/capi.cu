@@ -436,6 +436,7 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   cublasSetStream(ctx->cublas, ctx->stream);
   // fp32-accurate tensor-core emulation (BF16x9) for the plain LM-head GEMMs
   cublasSetMathMode(ctx->cublas, CUBLAS_FP32_EMULATED_BF16X9_MATH);
+  cublasSetEmulationStrategy(ctx->cublas, CUBLAS_EMULATION_STRATEGY_EAGER);
   cudaMemsetAsync(b.mstate, 0, (size_t)cfg->max_batch * h * d * sizeof(float), ctx->stream);
   cudaMemsetAsync(b.W, 0, ctx->W_len * sizeof(float), ctx->stream);
   cudaMemsetAsync(b.G, 0, ctx->W_len * sizeof(float), ctx->stream);
