@@ -39,20 +39,24 @@ def needs_build() -> bool:
     return any(os.path.getmtime(f) > t for f in deps)
 
 
-def build(verbose: bool = False, force: bool = False) -> str:
-    if not force and not needs_build():
+def build(verbose: bool = False, force: bool = False, out: str | None = None,
+          defines: tuple = ()) -> str:
+    """Compile every csrc/*.cu into one shared library (default: in-tree LIB)."""
+    if out is None and not force and not needs_build():
         return LIB
+    target = out or LIB
     nccl = nccl_dir()
     nvcc = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
     cmd = [nvcc, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
-           "-I", os.path.join(nccl, "include"), "-o", LIB + ".tmp", *sources(),
+           "-I", os.path.join(nccl, "include"), *[f"-D{x}" for x in defines],
+           "-o", target + ".tmp", *sources(),
            "-lcublas", "-L", os.path.join(nccl, "lib"), "-l:libnccl.so.2",
            "-Xlinker", "-rpath," + os.path.join(nccl, "lib")]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)
-    os.replace(LIB + ".tmp", LIB)
-    return LIB
+    os.replace(target + ".tmp", target)
+    return target
 
 
 if __name__ == "__main__":

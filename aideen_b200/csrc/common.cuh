@@ -47,6 +47,35 @@ struct BlockReducer {
   }
 };
 
+// Same protocol for doubles; `red` holds 2 * 8 * 32 doubles.
+struct BlockReducerD {
+  double *red;
+  int parity;
+  __device__ __forceinline__ explicit BlockReducerD(double *r) : red(r), parity(0) {}
+  template <int K>
+  __device__ __forceinline__ void sum(double (&v)[K]) {
+    static_assert(K <= 8, "at most 8 values per reduction");
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nw = (blockDim.x + 31) >> 5;
+    double *buf = red + parity * 8 * 32;
+    parity ^= 1;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      double x = v[k];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+      if (lane == 0) buf[k * 32 + warp] = x;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      double s = 0.0;
+      for (int w = 0; w < nw; ++w) s += buf[k * 32 + w];
+      v[k] = s;
+    }
+  }
+};
+
 // Reduce 32 per-lane partial vectors p[0..31] across a warp so that lane r
 // ends up holding the sum over lanes of p[r] (31 shuffles in total).  At each
 // step a lane keeps one half of its window and ships the other half to its

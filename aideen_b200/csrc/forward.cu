@@ -21,6 +21,20 @@ namespace cg = cooperative_groups;
 
 namespace aideen {
 
+#ifdef AIDEEN_PICARD_PROF
+// Phase timer of the Picard kernel (profiling builds only): cycles per CTA in
+// [0] token sync, [1] Picard iterations, [2] FPM read, [3] h* stores, [4] FPM write.
+__device__ unsigned long long g_picard_prof[1024 * 8];
+#define PT(i)                                               \
+  {                                                         \
+    const long long _n = clock64();                         \
+    _pacc[i] += _n - _pt;                                   \
+    _pt = _n;                                               \
+  }
+#else
+#define PT(i)
+#endif
+
 __global__ void embed_gather_kernel(const int32_t *__restrict__ tok, const float *__restrict__ emb,
                                     float *__restrict__ S, int N, int d, int vocab) {
   const int n = blockIdx.x;
@@ -102,29 +116,45 @@ __global__ void attn_scale_kernel(AttnArgs a, int rows) {
   if (lane == 0) { a.scale[w] = sc; a.rho[w] = rho; a.Rsrc[w] = R; }
 }
 
-// y[r] = sum_j M[j*32 + r] x[j] for r < 32; each thread owns 4 consecutive j.
-// Result lands in out[0..32) (shared).  Two block barriers.
-__device__ __forceinline__ void mv_d_to_32(const float *__restrict__ M, float4 x, float *out,
-                                           float *part) {
-  float p[32];
-  const float *row = M + (size_t)(threadIdx.x * 4) * kRank;
-#pragma unroll
-  for (int r4 = 0; r4 < 8; ++r4) {
-    const float4 w0 = ld4(row + 0 * kRank + 4 * r4), w1 = ld4(row + 1 * kRank + 4 * r4);
-    const float4 w2 = ld4(row + 2 * kRank + 4 * r4), w3 = ld4(row + 3 * kRank + 4 * r4);
-    p[4 * r4 + 0] = x.x * w0.x + x.y * w1.x + x.z * w2.x + x.w * w3.x;
-    p[4 * r4 + 1] = x.x * w0.y + x.y * w1.y + x.z * w2.y + x.w * w3.y;
-    p[4 * r4 + 2] = x.x * w0.z + x.y * w1.z + x.z * w2.z + x.w * w3.z;
-    p[4 * r4 + 3] = x.x * w0.w + x.y * w1.w + x.z * w2.w + x.w * w3.w;
-  }
-  const float v = warp_transpose_reduce32(p);
+// y_q[r] = sum_j Mq[j*32 + r] x[j], r < 32, for Q (1 or 2) matrices sharing x.
+// Each thread stages its float4 of x in xs; then lane l of warp w reads rows
+// j = w*128 + 4*i + (l>>3), columns 4*(l&7)..+3, so one warp load covers four
+// whole 128-byte rows (coalesced, conflict-free in shared memory).  Results
+// land in out[q*32 + r].  Three block barriers.
+template <int Q>
+__device__ __forceinline__ void mv_d_to_32(const float *M0, const float *M1, float4 x, float *xs,
+                                           float *out, float *part) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  part[warp * 32 + lane] = v;
+  st4(xs + threadIdx.x * 4, x);
   __syncthreads();
-  if (threadIdx.x < 32) {
-    float s = 0.f;
-    for (int w = 0; w < nw; ++w) s += part[w * 32 + threadIdx.x];
-    out[threadIdx.x] = s;
+  const int g = lane >> 3, rq = (lane & 7) * 4;
+  float4 acc[Q];
+#pragma unroll
+  for (int q = 0; q < Q; ++q) acc[q] = f4(0.f);
+  const int j0 = warp * 128 + g;
+#pragma unroll 8
+  for (int i = 0; i < 32; ++i) {
+    const int j = j0 + 4 * i;
+    const float xj = xs[j];
+    acc[0] = acc[0] + xj * ld4(M0 + (size_t)j * kRank + rq);
+    if (Q > 1) acc[Q - 1] = acc[Q - 1] + xj * ld4(M1 + (size_t)j * kRank + rq);
+  }
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+#pragma unroll
+    for (int o = 8; o <= 16; o <<= 1) {
+      acc[q].x += __shfl_xor_sync(0xffffffffu, acc[q].x, o);
+      acc[q].y += __shfl_xor_sync(0xffffffffu, acc[q].y, o);
+      acc[q].z += __shfl_xor_sync(0xffffffffu, acc[q].z, o);
+      acc[q].w += __shfl_xor_sync(0xffffffffu, acc[q].w, o);
+    }
+    if (g == 0) st4(part + warp * 64 + q * 32 + rq, acc[q]);
+  }
+  __syncthreads();
+  if (threadIdx.x < 32 * Q) {
+    float t = 0.f;
+    for (int w = 0; w < nw; ++w) t += part[w * 64 + threadIdx.x];
+    out[threadIdx.x] = t;
   }
   __syncthreads();
 }
@@ -138,6 +168,20 @@ __device__ __forceinline__ float4 mv_32_to_d(const float *__restrict__ M, const 
   return acc;
 }
 
+// Two 32->d products in one pass: ya = Ma . ina, yb = Mb . inb (thread's 4 outputs).
+__device__ __forceinline__ void mv2_32_to_d(const float *Ma, const float *ina, const float *Mb,
+                                            const float *inb, int d, float4 &ya, float4 &yb) {
+  float4 a = f4(0.f), b = f4(0.f);
+  const size_t c = threadIdx.x * 4;
+#pragma unroll
+  for (int r = 0; r < kRank; ++r) {
+    a = a + ina[r] * ld4(Ma + (size_t)r * d + c);
+    b = b + inb[r] * ld4(Mb + (size_t)r * d + c);
+  }
+  ya = a;
+  yb = b;
+}
+
 __device__ __forceinline__ float4 sigmoid4(float4 x) {
   return make_float4(1.f / (1.f + expf(-x.x)), 1.f / (1.f + expf(-x.y)), 1.f / (1.f + expf(-x.z)),
                      1.f / (1.f + expf(-x.w)));
@@ -147,13 +191,16 @@ __device__ __forceinline__ float4 sigmoid4(float4 x) {
 // grid = B*h, block = b*h + s.  FPM=true requires a cluster of h CTAs.
 template <bool FPM>
 __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
-  extern __shared__ float sm[];
+  extern __shared__ float4 sm4[];
+  float *sm = reinterpret_cast<float *>(sm4);
   float *red = sm;               // 512
   float *vec = red + 512;        // 64   (q / bottleneck | retain-up)
-  float *part = vec + 64;        // 256  (8 warps x 32)
-  float *wsm = part + 256;       // 32   (read weights, gate)
-  float *keybuf = wsm + 32;      // 2 x 32
+  float *part = vec + 64;        // 512  (8 warps x 64)
+  float *wsm = part + 512;       // 64   ([0,16) read weights, [16] gate, [17,33) b_read_mem)
+  float *keybuf = wsm + 64;      // 2 x 32
   float *mbuf = keybuf + 64;     // 2 x d
+  float *xs = mbuf + 2 * a.d;    // d    (matvec input staging)
+  float *wres = xs + a.d;        // n_resident x (d x 32) staged FPM matrices
   const int d = a.d, h = a.h, T = a.T;
   const int b = blockIdx.x / h, s = blockIdx.x % h;
   const int j0 = threadIdx.x * 4;
@@ -164,9 +211,25 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
   BlockReducer R(red);
   float4 hcur = f4(0.f), m = f4(0.f), hs4 = f4(0.f), hb4 = f4(0.f), wx4 = f4(0.f), ad4 = f4(0.f);
   int cur = 0;
+  // Per-slot rank-32 FPM matrices, staged in shared memory as far as they fit:
+  // 0 W_k_mem, 1 W_q_mem, 2 W_k_write, 3 W_retain_up ([d][32]); 4 W_v_write,
+  // 5 W_retain_down ([32][d]).  The rest stay in global memory (L2-resident).
+  const float *mat[6];
   if constexpr (FPM) {
+    const size_t ms = (size_t)s * d * kRank;
+    const float *src[6] = {W + a.off_wkm + ms, W + a.off_wqm + ms, W + a.off_wkw + ms,
+                           W + a.off_wup + ms, W + a.off_wvw + ms, W + a.off_wdown + ms};
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      float *dst = wres + (size_t)i * d * kRank;
+      const bool res = i < a.n_resident;
+      if (res)
+        for (int q = threadIdx.x * 4; q < d * kRank; q += blockDim.x * 4) st4(dst + q, ld4(src[i] + q));
+      mat[i] = res ? dst : src[i];
+    }
     m = ld4(a.mstate + ((size_t)b * h + s) * d + j0);
     st4(mbuf + j0, m);
+    if (threadIdx.x < h) wsm[17 + threadIdx.x] = W[a.off_bread + threadIdx.x];  // b_read_mem
     hs4 = ld4(W + a.off_hscale + (size_t)s * d + j0);
     hb4 = ld4(W + a.off_hbias + (size_t)s * d + j0);
     wx4 = make_float4(0.5f * tanhf(W[a.off_wx + (size_t)(j0 + 0) * d + j0 + 0]),
@@ -176,8 +239,15 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
     const float4 al = ld4(W + a.off_alog + (size_t)s * d + j0);
     ad4 = make_float4(1.f / (1.f + expf(al.x)), 1.f / (1.f + expf(al.y)), 1.f / (1.f + expf(al.z)),
                       1.f / (1.f + expf(al.w)));
+    __syncthreads();
+    // read key of the carried memory for the first token (:855-883)
+    mv_d_to_32<1>(mat[0], nullptr, m + hs4 * tanh4(m) + hb4, xs, keybuf, part);
   }
   const float band = fmaxf(a.eps, 0.15f * 0.2f);
+#ifdef AIDEEN_PICARD_PROF
+  long long _pt = clock64();
+  long long _pacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#endif
   for (int t = 0; t < T; ++t) {
     const size_t n = (size_t)b * T + t;
     const size_t e = (n * h + s) * d + j0;
@@ -191,11 +261,9 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
     }
     float4 ctx = f4(0.f);
     if constexpr (FPM) {
-      // read key of this slot's carried memory (:855-883)
-      const float4 keyed = m + hs4 * tanh4(m) + hb4;
-      mv_d_to_32(W + a.off_wkm + (size_t)s * d * kRank, keyed, keybuf + cur * 32, part);
-      cg::this_cluster().sync();
+      cg::this_cluster().sync();  // every slot's key + memory for this token is visible
     }
+    PT(0);
     float prev = 1.f;
     int it = 0;
     bool conv = false;
@@ -207,19 +275,35 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
           R.sum(v2);
           const float hq = sqrtf(fmaxf(v2[0], 1e-6f));
           const float sig_norm = sqrtf(fmaxf(v2[1], 1e-6f));
-          mv_d_to_32(W + a.off_wqm + (size_t)s * d * kRank,
-                     make_float4(hcur.x / hq, hcur.y / hq, hcur.z / hq, hcur.w / hq), vec, part);
+          mv_d_to_32<1>(mat[1], nullptr,
+                        make_float4(hcur.x / hq, hcur.y / hq, hcur.z / hq, hcur.w / hq), xs, vec, part);
+          PT(6);
           cg::cluster_group cl = cg::this_cluster();
           if (threadIdx.x < 32) {
             const int lane = threadIdx.x;
-            float sc = -1e30f;
-            if (lane < h) {
-              const float *rk = cl.map_shared_rank(keybuf + cur * 32, lane);
-              float acc = 0.f;
-#pragma unroll 8
-              for (int r = 0; r < kRank; ++r) acc += vec[r] * rk[r];
-              sc = (acc + W[a.off_bread + lane]) * rsqrtf((float)kRank) / fmaxf(a.tau, 1e-3f);
+            float kr[16];
+#pragma unroll
+            for (int ms = 0; ms < 16; ++ms)
+              kr[ms] = ms < h ? cl.map_shared_rank(keybuf + cur * 32, ms)[lane] : 0.f;
+#ifdef AIDEEN_PICARD_PROF
+            {
+              float chk = 0.f;
+#pragma unroll
+              for (int ms = 0; ms < 16; ++ms) chk += kr[ms];
+              if (chk == 12345.678f) wsm[40] = chk;
+              PT(5);
             }
+#endif
+            const float qv = vec[lane];
+            float sc = -1e30f;
+#pragma unroll
+            for (int ms = 0; ms < 16; ++ms) {
+              if (ms < h) {
+                const float dot = warp_sum(qv * kr[ms]);
+                if (lane == ms) sc = dot;
+              }
+            }
+            if (lane < h) sc = (sc + wsm[17 + lane]) * rsqrtf((float)kRank) / fmaxf(a.tau, 1e-3f);
             const float mx = warp_max(sc);
             const float ex = lane < h ? expf(sc - mx) : 0.f;
             const float se = fmaxf(warp_sum(ex), 1e-12f);
@@ -233,10 +317,16 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
             }
           }
           __syncthreads();
+          PT(7);
           float4 mr = f4(0.f);
-          for (int ms = 0; ms < h; ++ms) {
-            const float *rm = cl.map_shared_rank(mbuf + cur * d, ms);
-            mr = mr + wsm[ms] * ld4(rm + j0);
+          for (int base = 0; base < h; base += 8) {   // 8 remote loads in flight at a time
+            float4 mm[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              if (base + q < h) mm[q] = ld4(cl.map_shared_rank(mbuf + cur * d, base + q) + j0);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              if (base + q < h) mr = mr + wsm[base + q] * mm[q];
           }
           const float4 mu = tanh4(mr);
           float v1[1] = {dot4(mu, mu)};
@@ -244,6 +334,7 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
           const float mu_norm = sqrtf(fmaxf(v1[0], 1e-6f));
           const float coef = sig_norm * fmaxf(a.alpha_m, 0.001f) / fmaxf(mu_norm, 1e-6f) * wsm[16];
           ctx = coef * mu;
+          PT(2);
         }
       }
       float4 dep = sig + hcur + anc;
@@ -267,34 +358,37 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
       conv = strict || homeo;
       prev = err;
       ++it;
+      PT(1);
     }
     st4(a.hstar + e, hcur);
     float4 pre_adj = sig + hcur;
     if (a.slot_coord) pre_adj = pre_adj + A4 + anc;
     st4(a.pre + e, pre_adj);
     if (threadIdx.x == 0) a.iters[n * h + s] = it;
+    PT(3);
     if constexpr (FPM) {
       st4(a.fpmctx + e, ctx);
       // post-solve memory write (:1965-2140)
       const float4 c = 0.5f * (hcur + sig);
-      float v2[2] = {dot4(hcur, hcur), dot4(ld4(W + a.off_wgate + (size_t)s * d + j0), c)};
-      R.sum(v2);
-      const float h_rms = sqrtf(fmaxf(v2[0] * inv_d, 1e-6f));
-      const float4 hu = make_float4(hcur.x / h_rms, hcur.y / h_rms, hcur.z / h_rms, hcur.w / h_rms);
-      const float raw_z = 1.f / (1.f + expf(-(v2[1] * rsqrtf((float)d) + W[a.off_bwrite + s] - 1.5f)));
-      const float z = fminf(fmaxf(raw_z, 0.f), 1.f);
-      mv_d_to_32(W + a.off_wkw + (size_t)s * d * kRank, c, vec, part);
-      mv_d_to_32(W + a.off_wup + (size_t)s * d * kRank, c, vec + 32, part);
-      const float4 prop = tanh4(ld4(W + a.off_bdelta + (size_t)s * d + j0) +
-                                mv_32_to_d(W + a.off_wvw + (size_t)s * kRank * d, vec, d));
+      PT(4);
+      mv_d_to_32<2>(mat[2], mat[3], c, xs, vec, part);   // bottleneck | retain-up
+      PT(5);
+      float4 pv, dv;
+      mv2_32_to_d(mat[4], vec, mat[5], vec + 32, d, pv, dv);
+      PT(6);
+      const float4 prop = tanh4(ld4(W + a.off_bdelta + (size_t)s * d + j0) + pv);
       const float4 df = prop - m;
-      float v3[2] = {dot4(m, m), dot4(df, df)};
+      float v3[4] = {dot4(m, m), dot4(df, df), dot4(hcur, hcur),
+                     dot4(ld4(W + a.off_wgate + (size_t)s * d + j0), c)};
       R.sum(v3);
+      const float h_rms = sqrtf(fmaxf(v3[2] * inv_d, 1e-6f));
+      const float4 hu = make_float4(hcur.x / h_rms, hcur.y / h_rms, hcur.z / h_rms, hcur.w / h_rms);
+      const float raw_z = 1.f / (1.f + expf(-(v3[3] * rsqrtf((float)d) + W[a.off_bwrite + s] - 1.5f)));
+      const float z = fminf(fmaxf(raw_z, 0.f), 1.f);
       const float prev_norm = sqrtf(fmaxf(v3[0], 1e-6f));
       const float diff_norm = sqrtf(fmaxf(v3[1], 1e-6f));
       const float novelty = diff_norm / (diff_norm + prev_norm + 1e-6f);
-      const float4 rr4 = sigmoid4(ld4(W + a.off_bret + (size_t)s * d + j0) +
-                                  mv_32_to_d(W + a.off_wdown + (size_t)s * kRank * d, vec + 32, d));
+      const float4 rr4 = sigmoid4(ld4(W + a.off_bret + (size_t)s * d + j0) + dv);
       const float4 retain = f4(1.f) - novelty * (f4(1.f) - rr4);
       const float4 write = (z * 0.1f) * prop;
       const float4 x = sqrtf(fmaxf(z, 1e-6f)) * hu + wx4 * hu + write;
@@ -303,9 +397,18 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
       st4(a.hist + e, mn);
       st4(mbuf + (cur ^ 1) * d + j0, mn);
       m = mn;
+      PT(4);
+      // read key of the new memory, used by every slot at the next token
+      mv_d_to_32<1>(mat[0], nullptr, m + hs4 * tanh4(m) + hb4, xs, keybuf + (cur ^ 1) * 32, part);
+      PT(7);
       cur ^= 1;
+      PT(4);
     }
   }
+#ifdef AIDEEN_PICARD_PROF
+  if (threadIdx.x == 0)
+    for (int i = 0; i < 8; ++i) g_picard_prof[blockIdx.x * 8 + i] += _pacc[i];
+#endif
   if constexpr (FPM) {
     st4(a.mstate + ((size_t)b * h + s) * d + j0, m);
     cg::this_cluster().sync();  // keep shared memory alive for remote readers
@@ -370,18 +473,32 @@ cudaError_t launch_attn_scale(const AttnArgs &a, int rows, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-static size_t picard_smem_bytes(int d) { return (size_t)(512 + 64 + 256 + 32 + 64 + 2 * d) * sizeof(float); }
+static size_t picard_smem_base(int d) {
+  return (size_t)(512 + 64 + 512 + 64 + 64 + 3 * d) * sizeof(float);
+}
 
 cudaError_t launch_picard(const PicardArgs &a, bool fpm, cudaStream_t st) {
   if (a.B <= 0 || a.T <= 0) return cudaSuccess;
   const int threads = a.d / 4;
-  const size_t smem = picard_smem_bytes(a.d);
+  size_t smem = picard_smem_base(a.d);
   if (!fpm) {
     picard_kernel<false><<<a.B * a.h, threads, smem, st>>>(a);
     return cudaGetLastError();
   }
   cudaError_t e = cudaFuncSetAttribute(picard_kernel<true>,
                                        cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) return e;
+  int dev = 0, optin = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  const size_t mat_bytes = (size_t)a.d * kRank * sizeof(float);
+  PicardArgs p = a;
+  p.n_resident = 0;
+  while (p.n_resident < 6 && smem + mat_bytes <= (size_t)optin) {
+    smem += mat_bytes;
+    ++p.n_resident;
+  }
+  e = cudaFuncSetAttribute(picard_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.B * a.h);
@@ -395,7 +512,7 @@ cudaError_t launch_picard(const PicardArgs &a, bool fpm, cudaStream_t st) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, picard_kernel<true>, a);
+  e = cudaLaunchKernelEx(&cfg, picard_kernel<true>, p);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
@@ -415,3 +532,14 @@ cudaError_t launch_solve_stats(const int32_t *iters, const float *hstar, int row
 }
 
 }  // namespace aideen
+
+#ifdef AIDEEN_PICARD_PROF
+extern "C" int aideen_debug_picard_prof(unsigned long long *out, int n, int reset) {
+  if (out && cudaMemcpyFromSymbol(out, aideen::g_picard_prof, n * sizeof(unsigned long long)) != cudaSuccess) return 2;
+  if (reset) {
+    static unsigned long long zeros[1024 * 8];
+    cudaMemcpyToSymbol(aideen::g_picard_prof, zeros, sizeof(zeros));
+  }
+  return 0;
+}
+#endif
