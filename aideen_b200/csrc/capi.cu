@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <dlfcn.h>
+
 #include <chrono>
 #include <cmath>
 #include <cstdio>
@@ -435,8 +437,13 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   }
   cublasSetStream(ctx->cublas, ctx->stream);
   // fp32-accurate tensor-core emulation (BF16x9) for the plain LM-head GEMMs
+  // fp32-accurate BF16x9 tensor-core emulation for the plain LM-head GEMMs when
+  // the loaded cuBLAS offers it (an older cuBLAS already loaded by the host
+  // process keeps its fp32 SIMT kernels; results are fp32-accurate either way).
   cublasSetMathMode(ctx->cublas, CUBLAS_FP32_EMULATED_BF16X9_MATH);
-  cublasSetEmulationStrategy(ctx->cublas, CUBLAS_EMULATION_STRATEGY_EAGER);
+  using SetStrategy = cublasStatus_t (*)(cublasHandle_t, int);
+  if (auto fn = (SetStrategy)dlsym(RTLD_DEFAULT, "cublasSetEmulationStrategy"))
+    fn(ctx->cublas, 2 /* CUBLAS_EMULATION_STRATEGY_EAGER */);
   cudaMemsetAsync(b.mstate, 0, (size_t)cfg->max_batch * h * d * sizeof(float), ctx->stream);
   cudaMemsetAsync(b.W, 0, ctx->W_len * sizeof(float), ctx->stream);
   cudaMemsetAsync(b.G, 0, ctx->W_len * sizeof(float), ctx->stream);

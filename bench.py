@@ -147,9 +147,11 @@ def main():
     if args.impl == "reference":
         return run_reference(args, rank, world)
 
+    # load the library (and the CUDA toolkit's cuBLAS it links) before torch
+    from aideen_b200.backend import DEVICE, HOST, GpuDeqBackend, RunConfig, load_library
+    load_library()
     import torch
     import torch.distributed as dist
-    from aideen_b200.backend import DEVICE, HOST, GpuDeqBackend, RunConfig
     from aideen_b200.weights import init_all_weights, init_embedding, init_lm_head
 
     torch.cuda.set_device(local)
