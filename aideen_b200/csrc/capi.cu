@@ -12,6 +12,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <thread>
@@ -66,6 +67,7 @@ struct aideen_ctx {
   uint32_t adj_N = 0;     // tokens of the last adjoint
   float adj_beta = 0.85f;
   bool lm_ready = false, emb_ready = false;
+  bool use_tc = true;     // tcgen05 GEMMs where the operand shapes allow
   DevBufs b;
   Layout P{128, 1, 64};   // device (padded) layout
   Layout Lx{128, 1};      // packed reference layout at the boundary
@@ -131,6 +133,12 @@ GemmArgs gemm(int M, int N, int K, int batch, const float *A, long lda, long sA,
   return g;
 }
 
+// GEMM dispatch: tcgen05 (3xTF32) when supported for these operands, else CUDA cores.
+cudaError_t gemm_any(aideen_ctx *ctx, const GemmArgs &g) {
+  if (ctx->use_tc && tc_gemm_supported(g)) return tc_gemm(g, ctx->stream);
+  return gemm_f32(g, ctx->stream);
+}
+
 int check_run(aideen_ctx *ctx, const aideen_run *r) {
   if (!r) return set_err(ctx, AIDEEN_E_INVALID, "null run");
   if (r->batch == 0 || r->seq_len == 0 || r->batch > ctx->cfg.max_batch ||
@@ -152,25 +160,25 @@ int run_forward(aideen_ctx *ctx, const aideen_run *r, aideen_stats *stats) {
     CU(cudaMemsetAsync(b.signal, 0, (size_t)N * h * d * sizeof(float), st));
   } else {
     // signal[n][s][:] = sigma * S_in[n] . W_in[s]   (deq_slot_attn_unified_clean.wgsl:762-804)
-    KL(gemm_f32(gemm(N, d, d, h, b.S_in, d, 0, false, W + L.win, d, (long)d * d, false, b.signal,
-                     (long)h * d, d, ctx->signal_scale), st));
+    KL(gemm_any(ctx, gemm(N, d, d, h, b.S_in, d, 0, false, W + L.win, d, (long)d * d, false, b.signal,
+                     (long)h * d, d, ctx->signal_scale)));
   }
   if (r->slot_coord) {
     // 32-wide K/V/Q heads of src = signal + anchor (:281-355)
-    KL(gemm_f32(gemm(N, kHeadDim, d, h, b.signal, (long)h * d, d, false, W + L.wk, d, (long)d * d,
-                     false, b.Kh, (long)h * kHeadDim, kHeadDim, 1.f, 0.f, W + L.slot_anchor, d), st));
-    KL(gemm_f32(gemm(N, kHeadDim, d, h, b.signal, (long)h * d, d, false, W + L.wv, d, (long)d * d,
-                     false, b.Vh, (long)h * kHeadDim, kHeadDim, 1.f, 0.f, W + L.slot_anchor, d), st));
-    KL(gemm_f32(gemm(N, kHeadDim, d, h, b.signal, (long)h * d, d, false, W + L.wq, d, (long)d * d,
-                     false, b.Qh, (long)h * kHeadDim, kHeadDim, 1.f, 0.f, W + L.slot_anchor, d), st));
+    KL(gemm_any(ctx, gemm(N, kHeadDim, d, h, b.signal, (long)h * d, d, false, W + L.wk, d, (long)d * d,
+                     false, b.Kh, (long)h * kHeadDim, kHeadDim, 1.f, 0.f, W + L.slot_anchor, d)));
+    KL(gemm_any(ctx, gemm(N, kHeadDim, d, h, b.signal, (long)h * d, d, false, W + L.wv, d, (long)d * d,
+                     false, b.Vh, (long)h * kHeadDim, kHeadDim, 1.f, 0.f, W + L.slot_anchor, d)));
+    KL(gemm_any(ctx, gemm(N, kHeadDim, d, h, b.signal, (long)h * d, d, false, W + L.wq, d, (long)d * d,
+                     false, b.Qh, (long)h * kHeadDim, kHeadDim, 1.f, 0.f, W + L.slot_anchor, d)));
     AttnArgs a{};
     a.h = h; a.d = d; a.W = W; a.off_qb = L.q_bias; a.off_kb = L.k_bias; a.off_anchor = L.slot_anchor;
     a.Qh = b.Qh; a.Kh = b.Kh; a.Vh = b.Vh; a.alpha = b.alpha; a.nmix = b.nmix; a.rmix = b.rmix;
     a.signal = b.signal; a.amat = b.amat; a.A = b.A; a.scale = b.scale; a.rho = b.rho; a.Rsrc = b.Rsrc;
     KL(launch_attn_softmax(a, N, st));
     // attn[o] = sum_k W_o[s][k*d + o] n[k]  (:452-470)
-    KL(gemm_f32(gemm(N, d, kHeadDim, h, b.nmix, (long)h * kHeadDim, kHeadDim, false, W + L.wo, d,
-                     (long)d * d, false, b.amat, (long)h * d, d), st));
+    KL(gemm_any(ctx, gemm(N, d, kHeadDim, h, b.nmix, (long)h * kHeadDim, kHeadDim, false, W + L.wo, d,
+                     (long)d * d, false, b.amat, (long)h * d, d)));
     KL(launch_attn_scale(a, N * h, st));
   }
   if (!r->fpm) CU(cudaMemsetAsync(b.hist, 0, (size_t)N * h * d * sizeof(float), st));
@@ -274,23 +282,23 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   if (sc) {
     KL(launch_attn_bwd_scale(a, N * h, st));
     // dn[n][s][c] = sum_o da[n][s][o] W_o[s][c*d + o]
-    KL(gemm_f32(gemm(N, kHeadDim, d, h, b.da, (long)h * d, d, false, W + L.wo, d, (long)d * d, true,
-                     b.dn, H32, kHeadDim), st));
+    KL(gemm_any(ctx, gemm(N, kHeadDim, d, h, b.da, (long)h * d, d, false, W + L.wo, d, (long)d * d, true,
+                     b.dn, H32, kHeadDim)));
     // gW_o[s][c][o] = sum_n n[n][s][c] da[n][s][o]
-    KL(gemm_f32(gemm(kHeadDim, d, N, h, b.nmix, H32, kHeadDim, true, b.da, (long)h * d, d, false,
-                     G + L.wo, d, (long)d * d), st));
+    KL(gemm_any(ctx, gemm(kHeadDim, d, N, h, b.nmix, H32, kHeadDim, true, b.da, (long)h * d, d, false,
+                     G + L.wo, d, (long)d * d)));
     KL(launch_attn_bwd_softmax(a, N, st));
     // gW_{q,k,v}[s][j][c] = sum_n src[n][s][j] d{Q,K,V}[n][s][c]
     const float *dqkv[3] = {b.dQ, b.dK, b.dV};
     const size_t woff[3] = {L.wq, L.wk, L.wv};
     for (int i = 0; i < 3; ++i)
-      KL(gemm_f32(gemm(d, kHeadDim, N, h, b.signal, (long)h * d, d, true, dqkv[i], H32, kHeadDim,
-                       false, G + woff[i], d, (long)d * d, 1.f, 0.f, W + L.slot_anchor, d), st));
+      KL(gemm_any(ctx, gemm(d, kHeadDim, N, h, b.signal, (long)h * d, d, true, dqkv[i], H32, kHeadDim,
+                       false, G + woff[i], d, (long)d * d, 1.f, 0.f, W + L.slot_anchor, d)));
     KL(launch_dsig_init(a, b.dsig, N * h, 1, st));
     // dsrc[n][s][j] += sum_c d{Q,K,V}[n][s][c] W[s][j*d + c]
     for (int i = 0; i < 3; ++i)
-      KL(gemm_f32(gemm(N, d, kHeadDim, h, dqkv[i], H32, kHeadDim, false, W + woff[i], d, (long)d * d,
-                       true, b.dsig, (long)h * d, d, 1.f, 1.f), st));
+      KL(gemm_any(ctx, gemm(N, d, kHeadDim, h, dqkv[i], H32, kHeadDim, false, W + woff[i], d, (long)d * d,
+                       true, b.dsig, (long)h * d, d, 1.f, 1.f)));
     KL(launch_colsum(b.dQ, N, H32, H32, G + L.q_bias, kHeadDim, d, false, st));
     KL(launch_colsum(b.dK, N, H32, H32, G + L.k_bias, kHeadDim, d, false, st));
     KL(launch_colsum(b.dsig, N, h * d, (long)h * d, G + L.slot_anchor, h * d, 0, false, st));
@@ -299,13 +307,13 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   }
   if (!ctx->signal_zero) {
     // gW_in[s][j][o] = sigma * sum_n S_in[n][j] dsig[n][s][o]
-    KL(gemm_f32(gemm(d, d, N, h, b.S_in, d, 0, true, b.dsig, (long)h * d, d, false, G + L.win, d,
-                     (long)d * d, ctx->signal_scale), st));
+    KL(gemm_any(ctx, gemm(d, d, N, h, b.S_in, d, 0, true, b.dsig, (long)h * d, d, false, G + L.win, d,
+                     (long)d * d, ctx->signal_scale)));
     if (want_ds) {
       for (int s = 0; s < h; ++s)
-        KL(gemm_f32(gemm(N, d, d, 1, b.dsig + (size_t)s * d, (long)h * d, 0, false,
+        KL(gemm_any(ctx, gemm(N, d, d, 1, b.dsig + (size_t)s * d, (long)h * d, 0, false,
                          W + L.win + (size_t)s * d * d, d, 0, true, b.dS, d, 0, ctx->signal_scale,
-                         s == 0 ? 0.f : 1.f), st));
+                         s == 0 ? 0.f : 1.f)));
     }
   } else if (want_ds) {
     CU(cudaMemsetAsync(b.dS, 0, (size_t)N * d * sizeof(float), st));
@@ -395,6 +403,7 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   aideen_ctx *ctx = new aideen_ctx();
   ctx->cfg = *cfg;
   ctx->device = device;
+  if (const char *gm = getenv("AIDEEN_GEMM")) ctx->use_tc = strcmp(gm, "simt") != 0;
   ctx->P = Layout(d, h, 64);
   ctx->Lx = Layout(d, h, 1);
   ctx->W_len = ctx->P.total;
@@ -784,6 +793,75 @@ void *aideen_device_ptr(aideen_ctx *ctx, int which) {
   if (!ctx) return nullptr;
   size_t count = 0;
   return buf_ptr(ctx, which, &count);
+}
+
+namespace {
+__global__ void fill_kernel(float *x, size_t n, uint32_t seed) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    uint32_t v = (uint32_t)i * 2654435761u ^ seed;
+    v ^= v >> 13; v *= 0x5bd1e995u; v ^= v >> 15;
+    x[i] = (float)(v & 0xFFFFFF) / 8388608.0f - 1.0f;
+  }
+}
+__global__ void relerr_kernel(const float *a, const float *b, size_t n, double *out) {
+  double num = 0, den = 0;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const double d = (double)a[i] - b[i];
+    num += d * d;
+    den += (double)b[i] * b[i];
+  }
+  atomicAdd(&out[0], num);
+  atomicAdd(&out[1], den);
+}
+}  // namespace
+
+int aideen_gemm_selftest(aideen_ctx *ctx, int M, int N, int K, int batch, int trans_a, int trans_b,
+                         float *rel_err, float *ms_tc, float *ms_simt) {
+  if (!ctx || M <= 0 || N <= 0 || K <= 0 || batch <= 0) return AIDEEN_E_INVALID;
+  const size_t na = (size_t)M * K * batch, nb = (size_t)K * N * batch, nc = (size_t)M * N * batch;
+  float *A = nullptr, *B = nullptr, *C1 = nullptr, *C2 = nullptr;
+  double *acc = nullptr;
+  CU(cudaMalloc(&A, na * 4)); CU(cudaMalloc(&B, nb * 4)); CU(cudaMalloc(&C1, nc * 4));
+  CU(cudaMalloc(&C2, nc * 4)); CU(cudaMalloc(&acc, 16));
+  cudaStream_t st = ctx->stream;
+  fill_kernel<<<256, 256, 0, st>>>(A, na, 1u);
+  fill_kernel<<<256, 256, 0, st>>>(B, nb, 2u);
+  CU(cudaMemsetAsync(acc, 0, 16, st));
+  const long lda = trans_a ? M : K, ldb = trans_b ? K : N;
+  GemmArgs g = gemm(M, N, K, batch, A, lda, (long)M * K, trans_a != 0, B, ldb, (long)K * N, trans_b != 0,
+                    C1, N, (long)M * N);
+  int rc = AIDEEN_OK;
+  if (!tc_gemm_supported(g)) {
+    rc = set_err(ctx, AIDEEN_E_UNSUPPORTED, "shape not supported by the tensor-core GEMM");
+  } else {
+    cudaEvent_t e0, e1, e2;
+    cudaEventCreate(&e0); cudaEventCreate(&e1); cudaEventCreate(&e2);
+    tc_gemm(g, st);  // warm-up
+    cudaEventRecord(e0, st);
+    cudaError_t ce = tc_gemm(g, st);
+    cudaEventRecord(e1, st);
+    GemmArgs g2 = g;
+    g2.C = C2;
+    cudaError_t ce2 = gemm_f32(g2, st);
+    cudaEventRecord(e2, st);
+    relerr_kernel<<<256, 256, 0, st>>>(C1, C2, nc, acc);
+    double h[2] = {0, 0};
+    cudaMemcpyAsync(h, acc, 16, cudaMemcpyDeviceToHost, st);
+    cudaError_t se = cudaStreamSynchronize(st);
+    float t1 = 0, t2 = 0;
+    cudaEventElapsedTime(&t1, e0, e1);
+    cudaEventElapsedTime(&t2, e1, e2);
+    cudaEventDestroy(e0); cudaEventDestroy(e1); cudaEventDestroy(e2);
+    if (ce != cudaSuccess || ce2 != cudaSuccess || se != cudaSuccess)
+      rc = set_err(ctx, AIDEEN_E_CUDA, "GEMM self-test launch failed");
+    else if (tc_gemm_error(true))
+      rc = set_err(ctx, AIDEEN_E_TIMEOUT, "tensor-core GEMM pipeline wait timed out");
+    if (rel_err) *rel_err = (float)std::sqrt(h[0] / (h[1] > 0 ? h[1] : 1.0));
+    if (ms_tc) *ms_tc = t1;
+    if (ms_simt) *ms_simt = t2;
+  }
+  cudaFree(A); cudaFree(B); cudaFree(C1); cudaFree(C2); cudaFree(acc);
+  return rc;
 }
 
 int aideen_comm_unique_id(char out[AIDEEN_UNIQUE_ID_BYTES]) {

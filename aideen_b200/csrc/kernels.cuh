@@ -21,6 +21,10 @@ struct GemmArgs {
   const float *abias; long strideAbias;
 };
 cudaError_t gemm_f32(const GemmArgs &g, cudaStream_t s);
+// Same contract on tcgen05 tensor cores (3xTF32, fp32-accurate); no abias.
+bool tc_gemm_supported(const GemmArgs &g);
+cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t s);
+unsigned int tc_gemm_error(bool reset);
 
 struct AttnArgs {
   int h, d;

@@ -1,0 +1,374 @@
+// fp32-accurate GEMM on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// C[b] = alpha * opA(A[b]) * opB(B[b]) + beta * C[b], row-major, the same
+// contract as gemm_f32 (kernels.cuh).  One CTA computes a 128 x BN tile:
+//
+//   * TMA (cp.async.bulk.tensor, no multicast) brings fp32 tiles of A and B
+//     into 128-byte-swizzled shared memory, BK = 32 along K per stage;
+//   * all threads split each staged value x into x_hi = x with the low 13
+//     mantissa bits cleared (exactly representable in tf32) and
+//     x_lo = x - x_hi, in the same swizzled layout;
+//   * one thread issues, per K=8 step, three tcgen05.mma kind::tf32
+//     (hi*hi + hi*lo + lo*hi) accumulating in TMEM (fp32), then
+//     tcgen05.commit releases the stage to the TMA producer;
+//   * the epilogue reads the accumulator with tcgen05.ld (warp w owns TMEM
+//     lanes 32w..32w+31 = tile rows) and applies alpha/beta.
+//
+// The 3-term split keeps the product error at ~2^-21 relative, i.e. fp32
+// level, which the DEQ forward needs (its stop rule compares residuals near
+// 1e-4).  Operands may be K-major or MN-major, so transposed views
+// (weight gradients A^T B) need no copies.  Every mbarrier wait is bounded;
+// on timeout the kernel records an error code and skips the remaining work.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+
+#include "kernels.cuh"
+
+namespace aideen {
+namespace {
+
+constexpr int BM = 128, BK = 32, STAGES = 3, TC_THREADS = 128;
+constexpr uint32_t kMaxSpin = 1u << 26;
+
+__device__ unsigned int g_tc_error;  // first error code seen by any tcgemm CTA
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Bounded wait for the phase with the given parity; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t i = 0; i < kMaxSpin; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x,
+                                            int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (sm100 version field = 1).
+__device__ __forceinline__ uint64_t sdesc(const void *base, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  const uint64_t addr = smem_u32(base);
+  return ((addr & 0x3FFFFull) >> 4) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_c, uint64_t da, uint64_t db, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_c),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void split_tf32(float4 *raw, float4 *lo, int n4) {
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+    float4 v = raw[i];
+    float4 hv;
+    hv.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+    hv.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+    hv.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+    hv.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+    raw[i] = hv;
+    lo[i] = make_float4(v.x - hv.x, v.y - hv.y, v.z - hv.z, v.w - hv.w);
+  }
+}
+
+struct TcParams {
+  int M, N, K;
+  bool a_kmajor, b_kmajor;  // K contiguous in memory (else M/N contiguous)
+  float *C;
+  long ldc, strideC;
+  float alpha, beta;
+  int a_batched, b_batched;  // operand map has a batch dimension
+};
+
+template <int BN>
+__global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constant__ CUtensorMap mapA,
+                                                            const __grid_constant__ CUtensorMap mapB,
+                                                            TcParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 1024-byte aligned stage buffers
+  unsigned char *sm = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4;
+  constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+  uint64_t *full = reinterpret_cast<uint64_t *>(sm + STAGES * STAGE_BYTES);
+  uint64_t *empty = full + STAGES;
+  uint64_t *done = empty + STAGES;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, bz = blockIdx.z;
+  const int kblocks = (p.K + BK - 1) / BK;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    const uint32_t ncols = BN < 32 ? 32 : BN;
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(ncols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  auto stage_ptr = [&](int s, int which) -> unsigned char * {
+    // which: 0 A hi, 1 A lo, 2 B hi, 3 B lo
+    unsigned char *base = sm + s * STAGE_BYTES;
+    return which == 0 ? base : which == 1 ? base + A_BYTES : which == 2 ? base + 2 * A_BYTES
+                                                                        : base + 2 * A_BYTES + B_BYTES;
+  };
+  auto issue_loads = [&](int kb) {
+    const int s = kb % STAGES;
+    const int k0 = kb * BK;
+    mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
+    const int za = p.a_batched ? bz : 0;
+    if (p.a_kmajor) {
+      tma_load_3d(stage_ptr(s, 0), &mapA, &full[s], k0, m0, za);
+    } else {
+      for (int c = 0; c < BM / 32; ++c)
+        tma_load_3d(stage_ptr(s, 0) + c * (BK * 128), &mapA, &full[s], m0 + 32 * c, k0, za);
+    }
+    if (p.b_kmajor) {
+      tma_load_3d(stage_ptr(s, 2), &mapB, &full[s], k0, n0, p.b_batched ? bz : 0);
+    } else {
+      for (int c = 0; c < BN / 32; ++c)
+        tma_load_3d(stage_ptr(s, 2) + c * (BK * 128), &mapB, &full[s], n0 + 32 * c, k0, p.b_batched ? bz : 0);
+    }
+  };
+
+  // instruction descriptor: fp32 accumulate, tf32 A/B, majors, N, M = 128
+  const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((p.a_kmajor ? 0u : 1u) << 15) |
+                         ((p.b_kmajor ? 0u : 1u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+                         ((uint32_t)(BM >> 4) << 24);
+  bool ok = true;
+  int issued = 0, consumed = 0;  // meaningful in thread 0 (producer)
+  if (tid == 0)
+    for (int kb = 0; kb < STAGES - 1 && kb < kblocks; ++kb) { issue_loads(kb); issued = kb + 1; }
+  for (int kb = 0; kb < kblocks && ok; ++kb) {
+    const int s = kb % STAGES;
+    const uint32_t ph = (kb / STAGES) & 1;
+    // keep the producer STAGES-1 blocks ahead: reuse the stage freed by block kb-1
+    if (tid == 0 && kb + STAGES - 1 < kblocks) {
+      const int nk = kb + STAGES - 1;
+      const int ns = nk % STAGES;
+      if (nk >= STAGES) ok = mbar_wait(&empty[ns], ((nk / STAGES) - 1) & 1);
+      if (ok) { issue_loads(nk); issued = nk + 1; }
+    }
+    if (!mbar_wait(&full[s], ph)) ok = false;
+    ok = __syncthreads_and(ok);
+    if (!ok) break;
+    consumed = kb + 1;
+    split_tf32(reinterpret_cast<float4 *>(stage_ptr(s, 0)), reinterpret_cast<float4 *>(stage_ptr(s, 1)),
+               A_BYTES / 16);
+    split_tf32(reinterpret_cast<float4 *>(stage_ptr(s, 2)), reinterpret_cast<float4 *>(stage_ptr(s, 3)),
+               B_BYTES / 16);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (tid == 0) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+      for (int k8 = 0; k8 < BK / 8; ++k8) {
+        // K-major: +32 B along the swizzled row; MN-major: +1024 B (8 K rows)
+        const uint32_t koffA = p.a_kmajor ? k8 * 32 : k8 * 1024;
+        const uint32_t koffB = p.b_kmajor ? k8 * 32 : k8 * 1024;
+        const uint32_t lboA = p.a_kmajor ? 16 : BK * 128, lboB = p.b_kmajor ? 16 : BK * 128;
+        const uint64_t ahi = sdesc(stage_ptr(s, 0) + koffA, lboA, 1024);
+        const uint64_t alo = sdesc(stage_ptr(s, 1) + koffA, lboA, 1024);
+        const uint64_t bhi = sdesc(stage_ptr(s, 2) + koffB, lboB, 1024);
+        const uint64_t blo = sdesc(stage_ptr(s, 3) + koffB, lboB, 1024);
+        const uint32_t acc0 = (kb > 0 || k8 > 0) ? 1u : 0u;
+        umma_tf32(tmem, ahi, bhi, idesc, acc0);
+        umma_tf32(tmem, ahi, blo, idesc, 1u);
+        umma_tf32(tmem, alo, bhi, idesc, 1u);
+      }
+      umma_commit(&empty[s]);
+    }
+  }
+  if (tid == 0) {
+    if (ok && kblocks > 0) umma_commit(done);
+  }
+  if (ok && kblocks > 0) ok = mbar_wait(done, 0);
+  ok = __syncthreads_and(ok);
+  if (!ok && tid == 0) {
+    // drain: let every TMA copy already issued land before the CTA exits (bounded)
+    for (int kb = consumed; kb < issued; ++kb) mbar_wait(&full[kb % STAGES], (kb / STAGES) & 1);
+  }
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (ok) {
+    const int row = m0 + warp * 32 + lane;
+    float *crow = p.C + (long)bz * p.strideC + (long)row * p.ldc;
+#pragma unroll
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      uint32_t r[32];
+      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+          "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+          "%28, %29, %30, %31}, [%32];"
+          : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+            "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+            "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+            "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+            "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          : "r"(taddr));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      if (row < p.M) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int col = n0 + c0 + j;
+          if (col < p.N) {
+            float v = p.alpha * __uint_as_float(r[j]);
+            if (p.beta != 0.f) v += p.beta * crow[col];
+            crow[col] = v;
+          }
+        }
+      }
+    }
+  } else if (tid == 0) {
+    atomicCAS(&g_tc_error, 0u, 1u);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t ncols = BN < 32 ? 32 : BN;
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
+  }
+}
+
+// ---------------------------------------------------------------- host side
+using EncodeFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                              const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                              CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                              CUtensorMapFloatOOBfill);
+
+EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  }
+  return fn;
+}
+
+// 3-D fp32 map: dim0 contiguous (extent e0), dim1 stride s1 elements, dim2 stride s2.
+bool make_map(CUtensorMap *m, const float *base, uint64_t e0, uint64_t e1, uint64_t e2, uint64_t s1,
+              uint64_t s2, uint32_t box0, uint32_t box1) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {e0, e1, e2 ? e2 : 1};
+  const cuuint64_t strides[2] = {s1 * 4, (s2 ? s2 : s1 * e1) * 4};
+  const cuuint32_t box[3] = {box0, box1, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN>
+size_t tc_smem() {
+  return 1024 + STAGES * (size_t)(2 * BM * BK * 4 + 2 * BN * BK * 4) + 8 * (2 * STAGES + 1) + 16;
+}
+
+}  // namespace
+
+bool tc_gemm_supported(const GemmArgs &g) {
+  if (g.abias) return false;
+  if (g.K <= 0) return false;
+  if (g.N % 32 != 0) return false;
+  if ((reinterpret_cast<uintptr_t>(g.A) | reinterpret_cast<uintptr_t>(g.B)) & 15) return false;
+  if ((g.lda | g.ldb | g.strideA | g.strideB) & 3) return false;
+  return encode_fn() != nullptr;
+}
+
+cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st) {
+  // A: K-major when not transposed (row m contiguous along k).
+  const bool a_k = !g.transA, b_k = g.transB;
+  CUtensorMap ma, mb;
+  const bool a_batched = g.strideA != 0 && g.batch > 1;
+  bool ok;
+  if (a_k)  // dims: k (contiguous), m, batch
+    ok = make_map(&ma, g.A, g.K, g.M, a_batched ? g.batch : 1, g.lda, g.strideA, BK, BM);
+  else      // dims: m (contiguous), k, batch
+    ok = make_map(&ma, g.A, g.M, g.K, a_batched ? g.batch : 1, g.lda, g.strideA, 32, BK);
+  if (!ok) return cudaErrorInvalidValue;
+  const int BN = g.N % 128 == 0 ? 128 : 32;
+  const bool b_batched = g.strideB != 0 && g.batch > 1;
+  if (b_k)  // B stored [n][k]
+    ok = make_map(&mb, g.B, g.K, g.N, b_batched ? g.batch : 1, g.ldb, g.strideB, BK, BN);
+  else      // B stored [k][n]
+    ok = make_map(&mb, g.B, g.N, g.K, b_batched ? g.batch : 1, g.ldb, g.strideB, 32, BK);
+  if (!ok) return cudaErrorInvalidValue;
+  TcParams p{g.M, g.N, g.K, a_k, b_k, g.C, g.ldc, g.strideC, g.alpha, g.beta, a_batched ? 1 : 0,
+             b_batched ? 1 : 0};
+  dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.batch);
+  if (BN == 128) {
+    const size_t smem = tc_smem<128>();
+    cudaFuncSetAttribute(tcgemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    tcgemm_kernel<128><<<grid, TC_THREADS, smem, st>>>(ma, mb, p);
+  } else {
+    const size_t smem = tc_smem<32>();
+    cudaFuncSetAttribute(tcgemm_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    tcgemm_kernel<32><<<grid, TC_THREADS, smem, st>>>(ma, mb, p);
+  }
+  return cudaGetLastError();
+}
+
+unsigned int tc_gemm_error(bool reset) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(v));
+  if (reset) {
+    const unsigned int z = 0;
+    cudaMemcpyToSymbol(g_tc_error, &z, sizeof(z));
+  }
+  return v;
+}
+
+}  // namespace aideen

@@ -209,6 +209,14 @@ int aideen_read(aideen_ctx *ctx, int which, void *dst, size_t n_elems);
 /* Device pointer of a buffer (zero-copy consumers); NULL if absent. */
 void *aideen_device_ptr(aideen_ctx *ctx, int which);
 
+/* ---- diagnostics (no counterpart in the reference) --------------------------
+ * Runs the tcgen05 3xTF32 GEMM and the CUDA-core fp32 GEMM on the same seeded
+ * device operands (C = op(A) op(B), row-major, `batch` independent problems)
+ * and reports the relative L2 difference and both kernel times.  Allocates
+ * its own temporaries. */
+int aideen_gemm_selftest(aideen_ctx *ctx, int M, int N, int K, int batch, int trans_a, int trans_b,
+                         float *rel_err, float *ms_tc, float *ms_simt);
+
 /* ---- multi-GPU (one process per GPU; NCCL over NVLink) ----------------- */
 #define AIDEEN_UNIQUE_ID_BYTES 128
 int aideen_comm_unique_id(char out[AIDEEN_UNIQUE_ID_BYTES]);

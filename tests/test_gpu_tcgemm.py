@@ -1,0 +1,29 @@
+"""tcgen05 3xTF32 GEMM vs the CUDA-core fp32 GEMM on every operand pattern the
+hot path uses (projections: A row-major; weight gradients: A transposed;
+backprop through weights: B transposed)."""
+import pytest
+
+from aideen_b200.backend import GpuDeqBackend
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [
+    # M, N, K, batch, transA, transB
+    (2048, 512, 512, 8, False, False),   # signal = S_in . W_in[s]
+    (2048, 512, 32, 8, False, False),    # attn = n . W_o[s][:32]
+    (512, 512, 2048, 8, True, False),    # gW_in = S_in^T . dsig
+    (32, 512, 2048, 8, True, False),     # gW_o = n^T . da
+    (2048, 512, 32, 8, False, True),     # dsrc += dQ . W[:, :32]^T
+    (2048, 32, 512, 8, False, True),     # dn = da . W_o[s][:32]^T
+    (300, 96, 100, 2, False, False),     # ragged M / K
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s[:4])) + f"_t{int(s[4])}{int(s[5])}")
+def test_tensor_core_gemm_matches_fp32(shape):
+    M, N, K, B, ta, tb = shape
+    be = GpuDeqBackend(128, 2, 1, 1)
+    err, t_tc, t_simt = be.gemm_selftest(M, N, K, B, ta, tb)
+    print(f"{shape}: rel {err:.2e}  tc {t_tc:.3f} ms  simt {t_simt:.3f} ms")
+    assert err < 2e-6
+    be.close()
