@@ -856,6 +856,13 @@ int aideen_gemm_selftest(aideen_ctx *ctx, int M, int N, int K, int batch, int tr
       rc = set_err(ctx, AIDEEN_E_CUDA, "GEMM self-test launch failed");
     else if (tc_gemm_error(true))
       rc = set_err(ctx, AIDEEN_E_TIMEOUT, "tensor-core GEMM pipeline wait timed out");
+    if (getenv("AIDEEN_SELFTEST_DUMP")) {
+      float a[8], b2[8];
+      cudaMemcpy(a, C1, 32, cudaMemcpyDeviceToHost);
+      cudaMemcpy(b2, C2, 32, cudaMemcpyDeviceToHost);
+      for (int i = 0; i < 8; ++i) fprintf(stderr, "selftest C[%d] tc=%g fp32=%g\n", i, a[i], b2[i]);
+      fprintf(stderr, "tc err flag %u\n", tc_gemm_error(false));
+    }
     if (rel_err) *rel_err = (float)std::sqrt(h[0] / (h[1] > 0 ? h[1] : 1.0));
     if (ms_tc) *ms_tc = t1;
     if (ms_simt) *ms_simt = t2;

@@ -22,6 +22,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <cstring>
 
 #include "kernels.cuh"
@@ -74,11 +75,14 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
-// Shared-memory matrix descriptor, 128-byte swizzle (sm100 version field = 1).
-__device__ __forceinline__ uint64_t sdesc(const void *base, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+// Shared-memory matrix descriptor (sm100 version field = 1).  layout 2 =
+// 128-byte swizzle (K-major operands), layout 1 = 128-byte swizzle on 32-byte
+// atoms, the only layout the tf32 MMA accepts for MN-major operands.
+__device__ __forceinline__ uint64_t sdesc(const void *base, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                          uint32_t layout) {
   const uint64_t addr = smem_u32(base);
   return ((addr & 0x3FFFFull) >> 4) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16) |
-         ((uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
+         ((uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
 }
 
 __device__ __forceinline__ void umma_tf32(uint32_t tmem_c, uint64_t da, uint64_t db, uint32_t idesc,
@@ -216,11 +220,15 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
         // K-major: +32 B along the swizzled row; MN-major: +1024 B (8 K rows)
         const uint32_t koffA = p.a_kmajor ? k8 * 32 : k8 * 1024;
         const uint32_t koffB = p.b_kmajor ? k8 * 32 : k8 * 1024;
-        const uint32_t lboA = p.a_kmajor ? 16 : BK * 128, lboB = p.b_kmajor ? 16 : BK * 128;
-        const uint64_t ahi = sdesc(stage_ptr(s, 0) + koffA, lboA, 1024);
-        const uint64_t alo = sdesc(stage_ptr(s, 1) + koffA, lboA, 1024);
-        const uint64_t bhi = sdesc(stage_ptr(s, 2) + koffB, lboB, 1024);
-        const uint64_t blo = sdesc(stage_ptr(s, 3) + koffB, lboB, 1024);
+        // K-major: LBO unused (16), 8-row atoms (SBO 1024).  MN-major: 32-wide MN
+        // blocks BK*128 bytes apart (LBO), 4-row K atoms (SBO 512).
+        const uint32_t lboA = p.a_kmajor ? 16u : BK * 128u, sboA = p.a_kmajor ? 1024u : 512u;
+        const uint32_t lboB = p.b_kmajor ? 16u : BK * 128u, sboB = p.b_kmajor ? 1024u : 512u;
+        const uint32_t layA = p.a_kmajor ? 2u : 1u, layB = p.b_kmajor ? 2u : 1u;
+        const uint64_t ahi = sdesc(stage_ptr(s, 0) + koffA, lboA, sboA, layA);
+        const uint64_t alo = sdesc(stage_ptr(s, 1) + koffA, lboA, sboA, layA);
+        const uint64_t bhi = sdesc(stage_ptr(s, 2) + koffB, lboB, sboB, layB);
+        const uint64_t blo = sdesc(stage_ptr(s, 3) + koffB, lboB, sboB, layB);
         const uint32_t acc0 = (kb > 0 || k8 > 0) ? 1u : 0u;
         umma_tf32(tmem, ahi, bhi, idesc, acc0);
         umma_tf32(tmem, ahi, blo, idesc, 1u);
@@ -300,7 +308,7 @@ EncodeFn encode_fn() {
 
 // 3-D fp32 map: dim0 contiguous (extent e0), dim1 stride s1 elements, dim2 stride s2.
 bool make_map(CUtensorMap *m, const float *base, uint64_t e0, uint64_t e1, uint64_t e2, uint64_t s1,
-              uint64_t s2, uint32_t box0, uint32_t box1) {
+              uint64_t s2, uint32_t box0, uint32_t box1, bool kmajor) {
   EncodeFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[3] = {e0, e1, e2 ? e2 : 1};
@@ -308,7 +316,8 @@ bool make_map(CUtensorMap *m, const float *base, uint64_t e0, uint64_t e1, uint6
   const cuuint32_t box[3] = {box0, box1, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE,
+            kmajor ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -335,16 +344,16 @@ cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st) {
   const bool a_batched = g.strideA != 0 && g.batch > 1;
   bool ok;
   if (a_k)  // dims: k (contiguous), m, batch
-    ok = make_map(&ma, g.A, g.K, g.M, a_batched ? g.batch : 1, g.lda, g.strideA, BK, BM);
+    ok = make_map(&ma, g.A, g.K, g.M, a_batched ? g.batch : 1, g.lda, g.strideA, BK, BM, true);
   else      // dims: m (contiguous), k, batch
-    ok = make_map(&ma, g.A, g.M, g.K, a_batched ? g.batch : 1, g.lda, g.strideA, 32, BK);
+    ok = make_map(&ma, g.A, g.M, g.K, a_batched ? g.batch : 1, g.lda, g.strideA, 32, BK, false);
   if (!ok) return cudaErrorInvalidValue;
   const int BN = g.N % 128 == 0 ? 128 : 32;
   const bool b_batched = g.strideB != 0 && g.batch > 1;
   if (b_k)  // B stored [n][k]
-    ok = make_map(&mb, g.B, g.K, g.N, b_batched ? g.batch : 1, g.ldb, g.strideB, BK, BN);
+    ok = make_map(&mb, g.B, g.K, g.N, b_batched ? g.batch : 1, g.ldb, g.strideB, BK, BN, true);
   else      // B stored [k][n]
-    ok = make_map(&mb, g.B, g.N, g.K, b_batched ? g.batch : 1, g.ldb, g.strideB, 32, BK);
+    ok = make_map(&mb, g.B, g.N, g.K, b_batched ? g.batch : 1, g.ldb, g.strideB, 32, BK, false);
   if (!ok) return cudaErrorInvalidValue;
   TcParams p{g.M, g.N, g.K, a_k, b_k, g.C, g.ldc, g.strideC, g.alpha, g.beta, a_batched ? 1 : 0,
              b_batched ? 1 : 0};
