@@ -2,7 +2,7 @@
 
     python -m aideen_b200.build
 
-Links the CUDA runtime, cuBLAS (LM-head GEMMs only) and NCCL (the wheel that
+Links the CUDA runtime and NCCL (the wheel that
 ships with the interpreter's torch, found under site-packages/nvidia/nccl).
 """
 from __future__ import annotations
@@ -50,7 +50,7 @@ def build(verbose: bool = False, force: bool = False, out: str | None = None,
     cmd = [nvcc, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
            "-I", os.path.join(nccl, "include"), *[f"-D{x}" for x in defines],
            "-o", target + ".tmp", *sources(),
-           "-lcublas", "-L", os.path.join(nccl, "lib"), "-l:libnccl.so.2",
+           "-L", os.path.join(nccl, "lib"), "-l:libnccl.so.2",
            "-Xlinker", "-rpath," + os.path.join(nccl, "lib")]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")

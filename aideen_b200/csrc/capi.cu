@@ -3,11 +3,8 @@
 // GpuDeqBackend (aideen-backbone/src/gpu_deq.rs:80-218) call sequence:
 // forward (:3855) -> LM head (lm_train.wgsl) -> clean adjoint (:4736) ->
 // fused weight gradients + update (:4980) -> spectral renorm (:5568).
-#include <cublas_v2.h>
 #include <cuda_runtime.h>
 #include <nccl.h>
-
-#include <dlfcn.h>
 
 #include <chrono>
 #include <cmath>
@@ -53,13 +50,13 @@ struct aideen_ctx {
   int device = 0;
   cudaStream_t stream = nullptr;
   bool own_stream = false;
-  cublasHandle_t cublas = nullptr;
   ncclComm_t comm = nullptr;
   int nranks = 1, rank = 0;
   std::string err;
   unsigned long long launches = 0;
   size_t W_len = 0, lm_len = 0, max_tokens = 0;
-  size_t lm_b = 0, lm_g = 0;   // offsets of b_lm and g_lm in the padded LM block
+  size_t lm_b = 0, lm_g = 0;
+  long Vp = 0;                 // logits row stride (vocab rounded up to 4 floats)   // offsets of b_lm and g_lm in the padded LM block
   float signal_scale = 1.f;
   bool signal_zero = false;
   aideen_run last_run{};
@@ -93,12 +90,6 @@ int set_err(aideen_ctx *c, int code, const std::string &msg) {
     cudaError_t _e = (expr);                                                           \
     if (_e != cudaSuccess)                                                             \
       return set_err(ctx, AIDEEN_E_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
-  } while (0)
-#define CB(expr)                                                                       \
-  do {                                                                                 \
-    cublasStatus_t _s = (expr);                                                        \
-    if (_s != CUBLAS_STATUS_SUCCESS)                                                   \
-      return set_err(ctx, AIDEEN_E_CUDA, std::string(#expr) + ": cublas status " + std::to_string((int)_s)); \
   } while (0)
 #define CHK(expr)                  \
   do {                             \
@@ -222,20 +213,17 @@ int run_lm_head(aideen_ctx *ctx, int N, float *loss_out) {
   DevBufs &b = ctx->b;
   cudaStream_t st = ctx->stream;
   const float *Wlm = b.lmp, *glm = b.lmp + ctx->lm_g;
-  const float one = 1.f, zero = 0.f;
+  const long Vp = ctx->Vp;
   KL(launch_count_active(b.targets, N, b.scal, st));
-  // logits^T (V x N, col-major) = W_lm (d x V col-major)^T . y (d x N col-major); then + b_lm
-  CB(cublasSgemm(ctx->cublas, CUBLAS_OP_T, CUBLAS_OP_N, V, N, d, &one, Wlm, d, b.y, d, &zero,
-                 b.logits, V));
-  KL(launch_softmax_ce(b.logits, b.lmp + ctx->lm_b, b.targets, b.scal, N, V, b.loss_rows, st));
+  // logits[n][v] = y[n] . W_lm[v]   (K-major A and B)
+  KL(gemm_any(ctx, gemm(N, V, d, 1, b.y, d, 0, false, Wlm, d, 0, true, b.logits, Vp, 0)));
+  KL(launch_softmax_ce(b.logits, b.lmp + ctx->lm_b, b.targets, b.scal, N, V, Vp, b.loss_rows, st));
   KL(launch_sum(b.loss_rows, N, b.scal + 1, st));
-  // dy (d x N col-major) = W_lm (d x V) . dlog (V x N)
-  CB(cublasSgemm(ctx->cublas, CUBLAS_OP_N, CUBLAS_OP_N, d, N, V, &one, Wlm, d, b.logits, V, &zero,
-                 b.dy, d));
-  // dW_lm^T (d x V col-major) = y (d x N) . dlog^T (N x V)
-  CB(cublasSgemm(ctx->cublas, CUBLAS_OP_N, CUBLAS_OP_T, d, V, N, &one, b.y, d, b.logits, V, &zero,
-                 b.Glm, d));
-  KL(launch_colsum(b.logits, N, V, V, b.Glm + ctx->lm_b, V, 0, false, st));
+  // dy = dlogits . W_lm
+  KL(gemm_any(ctx, gemm(N, d, V, 1, b.logits, Vp, 0, false, Wlm, d, 0, false, b.dy, d, 0)));
+  // dW_lm = dlogits^T . y
+  KL(gemm_any(ctx, gemm(V, d, N, 1, b.logits, Vp, 0, true, b.y, d, 0, false, b.Glm, d, 0)));
+  KL(launch_colsum(b.logits, N, V, Vp, b.Glm + ctx->lm_b, V, 0, false, st));
   KL(launch_rmsnorm_bwd(b.dy, b.pooled, b.lrms, glm, b.dl_dh, b.ggp, N, d, st));
   KL(launch_colsum(b.ggp, N, d, d, b.Glm + ctx->lm_g, d, 0, false, st));
   if (loss_out) {
@@ -410,6 +398,7 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   const size_t N = (size_t)cfg->max_batch * cfg->max_seq_len;
   ctx->max_tokens = N;
   const size_t V = cfg->vocab;
+  ctx->Vp = (long)((V + 3) / 4 * 4);
   ctx->lm_b = V * d;
   ctx->lm_g = V * d + (V + 63) / 64 * 64;
   ctx->lm_len = V ? ctx->lm_g + d : 0;
@@ -432,7 +421,7 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   A(&b.scal, 4); A(&b.stage, ctx->Lx.total); A(&b.stats, 4); A(&b.sigmas, 5 * h + 2);
   if (V) {
     A(&b.lmp, ctx->lm_len); A(&b.Glm, ctx->lm_len); A(&b.Mlm1, ctx->lm_len); A(&b.Mlm2, ctx->lm_len);
-    A(&b.logits, N * V); A(&b.emb, V * d);
+    A(&b.logits, N * (size_t)ctx->Vp); A(&b.emb, V * d);
   }
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
   ctx->own_stream = true;
@@ -440,19 +429,6 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
     aideen_destroy(ctx);
     return fail(AIDEEN_E_CUDA);
   }
-  if (cublasCreate(&ctx->cublas) != CUBLAS_STATUS_SUCCESS) {
-    aideen_destroy(ctx);
-    return fail(AIDEEN_E_CUDA);
-  }
-  cublasSetStream(ctx->cublas, ctx->stream);
-  // fp32-accurate tensor-core emulation (BF16x9) for the plain LM-head GEMMs
-  // fp32-accurate BF16x9 tensor-core emulation for the plain LM-head GEMMs when
-  // the loaded cuBLAS offers it (an older cuBLAS already loaded by the host
-  // process keeps its fp32 SIMT kernels; results are fp32-accurate either way).
-  cublasSetMathMode(ctx->cublas, CUBLAS_FP32_EMULATED_BF16X9_MATH);
-  using SetStrategy = cublasStatus_t (*)(cublasHandle_t, int);
-  if (auto fn = (SetStrategy)dlsym(RTLD_DEFAULT, "cublasSetEmulationStrategy"))
-    fn(ctx->cublas, 2 /* CUBLAS_EMULATION_STRATEGY_EAGER */);
   cudaMemsetAsync(b.mstate, 0, (size_t)cfg->max_batch * h * d * sizeof(float), ctx->stream);
   cudaMemsetAsync(b.W, 0, ctx->W_len * sizeof(float), ctx->stream);
   cudaMemsetAsync(b.G, 0, ctx->W_len * sizeof(float), ctx->stream);
@@ -477,7 +453,6 @@ void aideen_destroy(aideen_ctx *ctx) {
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   if (ctx->comm) ncclCommDestroy(ctx->comm);
-  if (ctx->cublas) cublasDestroy(ctx->cublas);
   DevBufs &b = ctx->b;
   void *ptrs[] = {b.W, b.G, b.M1, b.M2, b.S_in, b.tokens, b.targets, b.signal, b.A, b.amat, b.Qh,
                   b.Kh, b.Vh, b.alpha, b.nmix, b.rmix, b.scale, b.rho, b.Rsrc, b.hstar, b.pre,
@@ -497,7 +472,6 @@ int aideen_set_stream(aideen_ctx *ctx, void *s) {
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   ctx->stream = (cudaStream_t)s;
   ctx->own_stream = false;
-  cublasSetStream(ctx->cublas, ctx->stream);
   return AIDEEN_OK;
 }
 

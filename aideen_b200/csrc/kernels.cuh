@@ -104,7 +104,7 @@ cudaError_t launch_spectral(float *W, int d, int h, const Layout &L, int n_iters
 // LM head helpers
 cudaError_t launch_count_active(const int32_t *tg, int N, float *out, cudaStream_t st);
 cudaError_t launch_softmax_ce(float *logits, const float *bias, const int32_t *tg,
-                              const float *n_active, int N, int V, float *loss_rows, cudaStream_t st);
+                              const float *n_active, int N, int V, long ld, float *loss_rows, cudaStream_t st);
 cudaError_t launch_rmsnorm_bwd(const float *dy, const float *P, const float *lrms,
                                const float *g, float *dl_dh, float *ggp, int N, int d,
                                cudaStream_t st);

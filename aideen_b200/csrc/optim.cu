@@ -169,11 +169,11 @@ cudaError_t launch_count_active(const int32_t *tg, int N, float *out, cudaStream
 // One block per row: logits += b_lm, online max/sum, then dlogits = (softmax - onehot)/n_active in place.
 __global__ void softmax_ce_kernel(float *__restrict__ logits, const float *__restrict__ bias,
                                   const int32_t *__restrict__ tg,
-                                  const float *__restrict__ n_active, int V,
+                                  const float *__restrict__ n_active, int V, long ld,
                                   float *__restrict__ loss_rows) {
   __shared__ float rm[32], rs[32];
   const int n = blockIdx.x;
-  float *row = logits + (size_t)n * V;
+  float *row = logits + (size_t)n * ld;
   const int t = tg[n];
   float m = -INFINITY, s = 0.f;
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
@@ -213,9 +213,10 @@ __global__ void softmax_ce_kernel(float *__restrict__ logits, const float *__res
 }
 
 cudaError_t launch_softmax_ce(float *logits, const float *bias, const int32_t *tg,
-                              const float *n_active, int N, int V, float *loss_rows, cudaStream_t st) {
+                              const float *n_active, int N, int V, long ld, float *loss_rows,
+                              cudaStream_t st) {
   if (N <= 0) return cudaSuccess;
-  softmax_ce_kernel<<<N, 1024, 0, st>>>(logits, bias, tg, n_active, V, loss_rows);
+  softmax_ce_kernel<<<N, 1024, 0, st>>>(logits, bias, tg, n_active, V, ld, loss_rows);
   return cudaGetLastError();
 }
 

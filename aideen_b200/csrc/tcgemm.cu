@@ -30,7 +30,7 @@
 namespace aideen {
 namespace {
 
-constexpr int BM = 128, BK = 32, STAGES = 3, TC_THREADS = 128;
+constexpr int BM = 128, BK = 32, STAGES = 3, TC_THREADS = 192;
 constexpr uint32_t kMaxSpin = 1u << 26;
 
 __device__ unsigned int g_tc_error;  // first error code seen by any tcgemm CTA
@@ -100,17 +100,20 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
                : "memory");
 }
 
-__device__ __forceinline__ void split_tf32(float4 *raw, float4 *lo, int n4) {
-  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
-    float4 v = raw[i];
-    float4 hv;
-    hv.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-    hv.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-    hv.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-    hv.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
-    raw[i] = hv;
-    lo[i] = make_float4(v.x - hv.x, v.y - hv.y, v.z - hv.z, v.w - hv.w);
-  }
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// x -> (x_hi, x_lo) in place / alongside: x_hi keeps the 10 tf32 mantissa bits.
+__device__ __forceinline__ void split1(float4 *raw, float4 *lo) {
+  const float4 v = *raw;
+  float4 hv;
+  hv.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+  hv.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+  hv.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+  hv.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+  *raw = hv;
+  *lo = make_float4(v.x - hv.x, v.y - hv.y, v.z - hv.z, v.w - hv.w);
 }
 
 struct TcParams {
@@ -122,20 +125,26 @@ struct TcParams {
   int a_batched, b_batched;  // operand map has a batch dimension
 };
 
+// Warp roles (192 threads): warp 0 lane 0 = TMA producer, warp 1 = TMEM
+// owner + MMA issuer (lane 0), warps 2..5 = hi/lo splitters and epilogue
+// (warp w reads TMEM lanes 32*(w%4)..+31, so the four cover all 128 rows).
+// Per stage s: full[s] (TMA landed) -> conv[s] (split done, 4 warp arrivals)
+// -> empty[s] (MMAs done, tcgen05.commit) -> producer refills.
 template <int BN>
 __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constant__ CUtensorMap mapA,
                                                             const __grid_constant__ CUtensorMap mapB,
                                                             TcParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  // 1024-byte aligned stage buffers
   unsigned char *sm = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4;
   constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   uint64_t *full = reinterpret_cast<uint64_t *>(sm + STAGES * STAGE_BYTES);
-  uint64_t *empty = full + STAGES;
+  uint64_t *conv = full + STAGES;
+  uint64_t *empty = conv + STAGES;
   uint64_t *done = empty + STAGES;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+  uint32_t *err = tmem_slot + 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, bz = blockIdx.z;
   const int kblocks = (p.K + BK - 1) / BK;
@@ -143,16 +152,17 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 4);
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, 1);
+    *err = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 0) {
-    const uint32_t ncols = BN < 32 ? 32 : BN;
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(ncols));
+                 "r"((uint32_t)BN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -161,131 +171,143 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
   const uint32_t tmem = *tmem_slot;
 
   auto stage_ptr = [&](int s, int which) -> unsigned char * {
-    // which: 0 A hi, 1 A lo, 2 B hi, 3 B lo
-    unsigned char *base = sm + s * STAGE_BYTES;
+    unsigned char *base = sm + s * STAGE_BYTES;  // 0 A hi, 1 A lo, 2 B hi, 3 B lo
     return which == 0 ? base : which == 1 ? base + A_BYTES : which == 2 ? base + 2 * A_BYTES
                                                                         : base + 2 * A_BYTES + B_BYTES;
   };
-  auto issue_loads = [&](int kb) {
-    const int s = kb % STAGES;
-    const int k0 = kb * BK;
-    mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
-    const int za = p.a_batched ? bz : 0;
-    if (p.a_kmajor) {
-      tma_load_3d(stage_ptr(s, 0), &mapA, &full[s], k0, m0, za);
-    } else {
-      for (int c = 0; c < BM / 32; ++c)
-        tma_load_3d(stage_ptr(s, 0) + c * (BK * 128), &mapA, &full[s], m0 + 32 * c, k0, za);
-    }
-    if (p.b_kmajor) {
-      tma_load_3d(stage_ptr(s, 2), &mapB, &full[s], k0, n0, p.b_batched ? bz : 0);
-    } else {
-      for (int c = 0; c < BN / 32; ++c)
-        tma_load_3d(stage_ptr(s, 2) + c * (BK * 128), &mapB, &full[s], n0 + 32 * c, k0, p.b_batched ? bz : 0);
-    }
-  };
 
-  // instruction descriptor: fp32 accumulate, tf32 A/B, majors, N, M = 128
-  const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((p.a_kmajor ? 0u : 1u) << 15) |
-                         ((p.b_kmajor ? 0u : 1u) << 16) | ((uint32_t)(BN >> 3) << 17) |
-                         ((uint32_t)(BM >> 4) << 24);
-  bool ok = true;
-  int issued = 0, consumed = 0;  // meaningful in thread 0 (producer)
-  if (tid == 0)
-    for (int kb = 0; kb < STAGES - 1 && kb < kblocks; ++kb) { issue_loads(kb); issued = kb + 1; }
-  for (int kb = 0; kb < kblocks && ok; ++kb) {
-    const int s = kb % STAGES;
-    const uint32_t ph = (kb / STAGES) & 1;
-    // keep the producer STAGES-1 blocks ahead: reuse the stage freed by block kb-1
-    if (tid == 0 && kb + STAGES - 1 < kblocks) {
-      const int nk = kb + STAGES - 1;
-      const int ns = nk % STAGES;
-      if (nk >= STAGES) ok = mbar_wait(&empty[ns], ((nk / STAGES) - 1) & 1);
-      if (ok) { issue_loads(nk); issued = nk + 1; }
-    }
-    if (!mbar_wait(&full[s], ph)) ok = false;
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    consumed = kb + 1;
-    split_tf32(reinterpret_cast<float4 *>(stage_ptr(s, 0)), reinterpret_cast<float4 *>(stage_ptr(s, 1)),
-               A_BYTES / 16);
-    split_tf32(reinterpret_cast<float4 *>(stage_ptr(s, 2)), reinterpret_cast<float4 *>(stage_ptr(s, 3)),
-               B_BYTES / 16);
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();
-    if (tid == 0) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 0) {
+    if (lane == 0) {  // ---------------- TMA producer
+      int issued = 0;
+      bool ok = true;
+      for (int kb = 0; kb < kblocks && ok; ++kb) {
+        const int s = kb % STAGES;
+        if (kb >= STAGES && !mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { ok = false; break; }
+        if (*(volatile uint32_t *)err) { ok = false; break; }
+        const int k0 = kb * BK;
+        mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
+        const int za = p.a_batched ? bz : 0, zb = p.b_batched ? bz : 0;
+        if (p.a_kmajor) {
+          tma_load_3d(stage_ptr(s, 0), &mapA, &full[s], k0, m0, za);
+        } else {
 #pragma unroll
-      for (int k8 = 0; k8 < BK / 8; ++k8) {
-        // K-major: +32 B along the swizzled row; MN-major: +1024 B (8 K rows)
-        const uint32_t koffA = p.a_kmajor ? k8 * 32 : k8 * 1024;
-        const uint32_t koffB = p.b_kmajor ? k8 * 32 : k8 * 1024;
-        // K-major: LBO unused (16), 8-row atoms (SBO 1024).  MN-major: 32-wide MN
-        // blocks BK*128 bytes apart (LBO), 4-row K atoms (SBO 512).
-        const uint32_t lboA = p.a_kmajor ? 16u : BK * 128u, sboA = p.a_kmajor ? 1024u : 512u;
-        const uint32_t lboB = p.b_kmajor ? 16u : BK * 128u, sboB = p.b_kmajor ? 1024u : 512u;
-        const uint32_t layA = p.a_kmajor ? 2u : 1u, layB = p.b_kmajor ? 2u : 1u;
-        const uint64_t ahi = sdesc(stage_ptr(s, 0) + koffA, lboA, sboA, layA);
-        const uint64_t alo = sdesc(stage_ptr(s, 1) + koffA, lboA, sboA, layA);
-        const uint64_t bhi = sdesc(stage_ptr(s, 2) + koffB, lboB, sboB, layB);
-        const uint64_t blo = sdesc(stage_ptr(s, 3) + koffB, lboB, sboB, layB);
-        const uint32_t acc0 = (kb > 0 || k8 > 0) ? 1u : 0u;
-        umma_tf32(tmem, ahi, bhi, idesc, acc0);
-        umma_tf32(tmem, ahi, blo, idesc, 1u);
-        umma_tf32(tmem, alo, bhi, idesc, 1u);
+          for (int c = 0; c < BM / 32; ++c)
+            tma_load_3d(stage_ptr(s, 0) + c * (BK * 128), &mapA, &full[s], m0 + 32 * c, k0, za);
+        }
+        if (p.b_kmajor) {
+          tma_load_3d(stage_ptr(s, 2), &mapB, &full[s], k0, n0, zb);
+        } else {
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c)
+            tma_load_3d(stage_ptr(s, 2) + c * (BK * 128), &mapB, &full[s], n0 + 32 * c, k0, zb);
+        }
+        issued = kb + 1;
       }
-      umma_commit(&empty[s]);
+      if (!ok) atomicExch(err, 1u);
+      // every issued copy must land before the CTA can exit (bounded)
+      for (int kb = issued - STAGES < 0 ? 0 : issued - STAGES; kb < issued; ++kb)
+        mbar_wait(&full[kb % STAGES], (kb / STAGES) & 1);
     }
-  }
-  if (tid == 0) {
-    if (ok && kblocks > 0) umma_commit(done);
-  }
-  if (ok && kblocks > 0) ok = mbar_wait(done, 0);
-  ok = __syncthreads_and(ok);
-  if (!ok && tid == 0) {
-    // drain: let every TMA copy already issued land before the CTA exits (bounded)
-    for (int kb = consumed; kb < issued; ++kb) mbar_wait(&full[kb % STAGES], (kb / STAGES) & 1);
-  }
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  if (ok) {
-    const int row = m0 + warp * 32 + lane;
-    float *crow = p.C + (long)bz * p.strideC + (long)row * p.ldc;
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---------------- MMA issuer
+      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((p.a_kmajor ? 0u : 1u) << 15) |
+                             ((p.b_kmajor ? 0u : 1u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+                             ((uint32_t)(BM >> 4) << 24);
+      // K-major: LBO unused (16), 8-row atoms (SBO 1024).  MN-major: 32-wide MN
+      // blocks BK*128 bytes apart (LBO), 4-row K atoms (SBO 512).
+      const uint32_t lboA = p.a_kmajor ? 16u : BK * 128u, sboA = p.a_kmajor ? 1024u : 512u;
+      const uint32_t lboB = p.b_kmajor ? 16u : BK * 128u, sboB = p.b_kmajor ? 1024u : 512u;
+      const uint32_t layA = p.a_kmajor ? 2u : 1u, layB = p.b_kmajor ? 2u : 1u;
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        const int s = kb % STAGES;
+        if (!mbar_wait(&conv[s], (kb / STAGES) & 1) || *(volatile uint32_t *)err) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      uint32_t r[32];
-      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-          "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
-          "%28, %29, %30, %31}, [%32];"
-          : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-            "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-            "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-            "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-            "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-          : "r"(taddr));
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      if (row < p.M) {
+        for (int k8 = 0; k8 < BK / 8; ++k8) {
+          // K-major: +32 B along the swizzled row; MN-major: +1024 B (8 K rows)
+          const uint32_t koffA = p.a_kmajor ? k8 * 32 : k8 * 1024;
+          const uint32_t koffB = p.b_kmajor ? k8 * 32 : k8 * 1024;
+          const uint64_t ahi = sdesc(stage_ptr(s, 0) + koffA, lboA, sboA, layA);
+          const uint64_t alo = sdesc(stage_ptr(s, 1) + koffA, lboA, sboA, layA);
+          const uint64_t bhi = sdesc(stage_ptr(s, 2) + koffB, lboB, sboB, layB);
+          const uint64_t blo = sdesc(stage_ptr(s, 3) + koffB, lboB, sboB, layB);
+          umma_tf32(tmem, ahi, bhi, idesc, (kb > 0 || k8 > 0) ? 1u : 0u);
+          umma_tf32(tmem, ahi, blo, idesc, 1u);
+          umma_tf32(tmem, alo, bhi, idesc, 1u);
+        }
+        umma_commit(&empty[s]);
+      }
+      if (!ok) atomicExch(err, 1u);
+      umma_commit(done);  // arrives once every MMA issued so far has completed
+    }
+  } else {  // ---------------- splitters (128 threads) + epilogue
+    const int ct = tid - 64;
+    for (int kb = 0; kb < kblocks; ++kb) {
+      const int s = kb % STAGES;
+      if (!mbar_wait(&full[s], (kb / STAGES) & 1)) { atomicExch(err, 1u); break; }
+      if (*(volatile uint32_t *)err) break;
+      float4 *ra = reinterpret_cast<float4 *>(stage_ptr(s, 0));
+      float4 *la = reinterpret_cast<float4 *>(stage_ptr(s, 1));
+      float4 *rb = reinterpret_cast<float4 *>(stage_ptr(s, 2));
+      float4 *lb = reinterpret_cast<float4 *>(stage_ptr(s, 3));
+#pragma unroll 4
+      for (int i = ct; i < A_BYTES / 16; i += 128) split1(ra + i, la + i);
+#pragma unroll 4
+      for (int i = ct; i < B_BYTES / 16; i += 128) split1(rb + i, lb + i);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&conv[s]);
+    }
+    const bool ok = mbar_wait(done, 0) && !*(volatile uint32_t *)err;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ok) {
+      const int q = warp & 3;  // TMEM lane quadrant this warp may access
+      const int row = m0 + q * 32 + lane;
+      float *crow = p.C + (long)bz * p.strideC + (long)row * p.ldc;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+            "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+            "%28, %29, %30, %31}, [%32];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+              "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+              "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+              "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+              "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (row < p.M) {
+          if (p.beta == 0.f && n0 + c0 + 32 <= p.N && ((p.ldc | (long)(n0 + c0)) & 3) == 0 &&
+              ((reinterpret_cast<uintptr_t>(crow) & 15) == 0)) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int col = n0 + c0 + j;
-          if (col < p.N) {
-            float v = p.alpha * __uint_as_float(r[j]);
-            if (p.beta != 0.f) v += p.beta * crow[col];
-            crow[col] = v;
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4 *>(crow + n0 + c0 + j) =
+                  make_float4(p.alpha * __uint_as_float(r[j]), p.alpha * __uint_as_float(r[j + 1]),
+                              p.alpha * __uint_as_float(r[j + 2]), p.alpha * __uint_as_float(r[j + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int col = n0 + c0 + j;
+              if (col < p.N) {
+                float v = p.alpha * __uint_as_float(r[j]);
+                if (p.beta != 0.f) v += p.beta * crow[col];
+                crow[col] = v;
+              }
+            }
           }
         }
       }
     }
-  } else if (tid == 0) {
-    atomicCAS(&g_tc_error, 0u, 1u);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 0) {
-    const uint32_t ncols = BN < 32 ? 32 : BN;
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
-  }
+  if (tid == 0 && *(volatile uint32_t *)err) atomicCAS(&g_tc_error, 0u, 1u);
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN));
 }
 
 // ---------------------------------------------------------------- host side
@@ -323,7 +345,7 @@ bool make_map(CUtensorMap *m, const float *base, uint64_t e0, uint64_t e1, uint6
 
 template <int BN>
 size_t tc_smem() {
-  return 1024 + STAGES * (size_t)(2 * BM * BK * 4 + 2 * BN * BK * 4) + 8 * (2 * STAGES + 1) + 16;
+  return 1024 + STAGES * (size_t)(2 * BM * BK * 4 + 2 * BN * BK * 4) + 8 * (3 * STAGES + 1) + 16;
 }
 
 }  // namespace
@@ -331,7 +353,6 @@ size_t tc_smem() {
 bool tc_gemm_supported(const GemmArgs &g) {
   if (g.abias) return false;
   if (g.K <= 0) return false;
-  if (g.N % 32 != 0) return false;
   if ((reinterpret_cast<uintptr_t>(g.A) | reinterpret_cast<uintptr_t>(g.B)) & 15) return false;
   if ((g.lda | g.ldb | g.strideA | g.strideB) & 3) return false;
   return encode_fn() != nullptr;
@@ -348,7 +369,7 @@ cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st) {
   else      // dims: m (contiguous), k, batch
     ok = make_map(&ma, g.A, g.M, g.K, a_batched ? g.batch : 1, g.lda, g.strideA, 32, BK, false);
   if (!ok) return cudaErrorInvalidValue;
-  const int BN = g.N % 128 == 0 ? 128 : 32;
+  const int BN = g.N >= 128 ? 128 : 32;
   const bool b_batched = g.strideB != 0 && g.batch > 1;
   if (b_k)  // B stored [n][k]
     ok = make_map(&mb, g.B, g.K, g.N, b_batched ? g.batch : 1, g.ldb, g.strideB, BK, BN, true);

@@ -36,7 +36,7 @@ extern "C" {
 typedef enum aideen_status {
   AIDEEN_OK = 0,
   AIDEEN_E_INVALID = 1,   /* bad argument / size beyond caps */
-  AIDEEN_E_CUDA = 2,      /* CUDA runtime or cuBLAS failure */
+  AIDEEN_E_CUDA = 2,      /* CUDA runtime failure */
   AIDEEN_E_NCCL = 3,      /* collective failure */
   AIDEEN_E_TIMEOUT = 4,   /* bounded wait ran out */
   AIDEEN_E_NONFINITE = 5, /* non-finite value detected in a checked buffer */
