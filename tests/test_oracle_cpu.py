@@ -139,7 +139,6 @@ def test_lm_head_gradient_finite_differences():
         Pm[i, j] -= e
         fd = (O.lm_head(Pp, tg, w, b, g)[0] - O.lm_head(Pm, tg, w, b, g)[0]) / (2 * e)
         assert abs(dP[i, j] - fd) < 1e-7 + 1e-6 * abs(fd)
-    assert abs(dP[2]).max() == 0 or True  # ignored row only through nothing else
     gp = g.copy(); gp[2] += e
     gm = g.copy(); gm[2] -= e
     fd = (O.lm_head(P, tg, w, b, gp)[0] - O.lm_head(P, tg, w, b, gm)[0]) / (2 * e)
