@@ -97,6 +97,8 @@ _SIGS = {
                                     C.POINTER(C.c_float), C.POINTER(Stats)]),
     "aideen_read": (C.c_int, [_P, C.c_int, _P, C.c_size_t]),
     "aideen_device_ptr": (_P, [_P, C.c_int]),
+    "aideen_adjoint_noalloc": (C.c_int, [_P, _P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32,
+                                         C.c_uint32, C.c_float, C.c_uint32, _P, _P, _P, _P]),
     "aideen_gemm_selftest": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                        C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(C.c_float)]),
     "aideen_comm_unique_id": (C.c_int, [_P]),

@@ -209,6 +209,28 @@ int aideen_read(aideen_ctx *ctx, int which, void *dst, size_t n_elems);
 /* Device pointer of a buffer (zero-copy consumers); NULL if absent. */
 void *aideen_device_ptr(aideen_ctx *ctx, int which);
 
+/* ---- allocation-free adjoint (no counterpart in the reference) -------------
+ * For callers that cannot allocate device memory (inside someone else's stream
+ * capture, under allocators that forbid cudaMalloc after start-up, or in
+ * embedders that own every buffer): the same fused clean adjoint as
+ * aideen_adjoint_on, with no context and no allocation.  All pointers are
+ * device pointers on the current device, 16-byte aligned; layouts as
+ * aideen_adjoint_on (hstar, branch, rhs_slot [N][h][d]; dl_dh [N][d] or NULL;
+ * norm_scale [d]; v_out [h][N][d]; gpre_out [N][h][d]).  ns_grad_out (nullable,
+ * [d]) receives sum over tokens and slots of beta*v*pre/rms(pre), the NormScale
+ * gradient.  Its per-token partials live in a fixed device array of 2^22 floats
+ * (16 MiB) that every GPU loading the library holds until exit, so
+ * n_tokens * d_model must be <= 4194304 when ns_grad_out is given
+ * (AIDEEN_E_INVALID otherwise).  The first call on a device looks up that
+ * array's address; make that first call before any stream capture.  All calls
+ * share the array: calls that overlap on the GPU (different streams or
+ * devices' contexts sharing a device) race.  Nothing in it needs zeroing. */
+int aideen_adjoint_noalloc(const float *hstar, const float *branch, const float *dl_dh,
+                           const float *rhs_slot, const float *norm_scale, uint32_t n_tokens,
+                           uint32_t h_slots, uint32_t d_model, uint32_t iters, float damping,
+                           uint32_t anderson_m, float *v_out, float *gpre_out, float *ns_grad_out,
+                           void *stream);
+
 /* ---- diagnostics (no counterpart in the reference) --------------------------
  * Runs the tcgen05 3xTF32 GEMM and the CUDA-core fp32 GEMM on the same seeded
  * device operands (C = op(A) op(B), row-major, `batch` independent problems)
