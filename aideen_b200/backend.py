@@ -74,6 +74,8 @@ _SIGS = {
     "aideen_set_stream": (C.c_int, [_P, _P]),
     "aideen_sync": (C.c_int, [_P]),
     "aideen_launch_count": (C.c_uint64, [_P]),
+    "aideen_profile": (C.c_int, [_P, C.c_int]),
+    "aideen_profile_read": (C.c_int, [_P, _P, _P, C.c_int]),
     "aideen_all_weights_len": (C.c_size_t, [C.c_uint32, C.c_uint32]),
     "aideen_upload_weights": (C.c_int, [_P, _P, C.c_size_t, C.c_int]),
     "aideen_download_weights": (C.c_int, [_P, _P, C.c_size_t]),
@@ -199,6 +201,18 @@ class GpuDeqBackend:
     @property
     def launch_count(self) -> int:
         return int(self.lib.aideen_launch_count(self.ctx))
+
+    PROF_CLASSES = ("picard", "adjoint", "gemm", "lm_softmax", "optimizer", "other")
+
+    def profile(self, enable: bool = True):
+        """Bracket every kernel launch with CUDA events (per-class device time)."""
+        self._check(self.lib.aideen_profile(self.ctx, int(enable)), "profile")
+
+    def profile_read(self, reset: bool = True) -> dict:
+        ms = np.zeros(6, np.float32)
+        n = np.zeros(6, np.uint64)
+        self._check(self.lib.aideen_profile_read(self.ctx, _ptr(ms), _ptr(n), int(reset)), "profile_read")
+        return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(self.PROF_CLASSES)}
 
     def device_ptr(self, name: str) -> int:
         return int(self.lib.aideen_device_ptr(self.ctx, BUF[name]) or 0)

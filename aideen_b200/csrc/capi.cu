@@ -11,8 +11,11 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <string.h>
 #include <string>
 #include <thread>
+#include <utility>
+#include <vector>
 
 #include "../../include/aideen_b200.h"
 #include "kernels.cuh"
@@ -66,6 +69,11 @@ struct aideen_ctx {
   bool lm_ready = false, emb_ready = false;
   bool use_tc = true;     // tcgen05 GEMMs where the operand shapes allow
   DevBufs b;
+  // opt-in per-kernel-class timing (aideen_profile): events around each launch
+  bool prof = false;
+  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> pev;
+  double prof_ms[AIDEEN_PROF_CLASSES] = {};
+  unsigned long long prof_n[AIDEEN_PROF_CLASSES] = {};
   Layout P{128, 1, 64};   // device (padded) layout
   Layout Lx{128, 1};      // packed reference layout at the boundary
 };
@@ -83,11 +91,30 @@ int set_err(aideen_ctx *c, int code, const std::string &msg) {
     if (_e != cudaSuccess)                                                             \
       return set_err(ctx, AIDEEN_E_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
   } while (0)
-// A launch of one of this library's kernels.
+int prof_class(const char *expr) {
+  if (strstr(expr, "launch_picard")) return AIDEEN_PROF_PICARD;
+  if (strstr(expr, "launch_adjoint")) return AIDEEN_PROF_ADJOINT;
+  if (strstr(expr, "gemm_any")) return AIDEEN_PROF_GEMM;
+  if (strstr(expr, "launch_softmax_ce")) return AIDEEN_PROF_LM_SOFTMAX;
+  if (strstr(expr, "launch_adam") || strstr(expr, "launch_clipped_sgd")) return AIDEEN_PROF_OPTIMIZER;
+  return AIDEEN_PROF_OTHER;
+}
+
+// A launch of one of this library's kernels (timed per class when profiling).
 #define KL(expr)                                                                       \
   do {                                                                                 \
     ctx->launches++;                                                                   \
+    cudaEvent_t _e0 = nullptr, _e1 = nullptr;                                          \
+    if (ctx->prof) {                                                                   \
+      cudaEventCreate(&_e0);                                                           \
+      cudaEventCreate(&_e1);                                                           \
+      cudaEventRecord(_e0, ctx->stream);                                               \
+    }                                                                                  \
     cudaError_t _e = (expr);                                                           \
+    if (ctx->prof) {                                                                   \
+      cudaEventRecord(_e1, ctx->stream);                                               \
+      ctx->pev.push_back({prof_class(#expr), {_e0, _e1}});                            \
+    }                                                                                  \
     if (_e != cudaSuccess)                                                             \
       return set_err(ctx, AIDEEN_E_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
   } while (0)
@@ -472,6 +499,32 @@ int aideen_set_stream(aideen_ctx *ctx, void *s) {
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   ctx->stream = (cudaStream_t)s;
   ctx->own_stream = false;
+  return AIDEEN_OK;
+}
+
+int aideen_profile(aideen_ctx *ctx, int enable) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  ctx->prof = enable != 0;
+  return AIDEEN_OK;
+}
+
+int aideen_profile_read(aideen_ctx *ctx, float *ms, uint64_t *launches, int reset) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  CU(cudaStreamSynchronize(ctx->stream));
+  for (auto &pe : ctx->pev) {
+    float t = 0.f;
+    cudaEventElapsedTime(&t, pe.second.first, pe.second.second);
+    ctx->prof_ms[pe.first] += t;
+    ctx->prof_n[pe.first] += 1;
+    cudaEventDestroy(pe.second.first);
+    cudaEventDestroy(pe.second.second);
+  }
+  ctx->pev.clear();
+  for (int i = 0; i < AIDEEN_PROF_CLASSES; ++i) {
+    if (ms) ms[i] = (float)ctx->prof_ms[i];
+    if (launches) launches[i] = ctx->prof_n[i];
+    if (reset) { ctx->prof_ms[i] = 0; ctx->prof_n[i] = 0; }
+  }
   return AIDEEN_OK;
 }
 

@@ -113,6 +113,48 @@ def cpu_baseline(sample_tokens: int = 16):
                       f"(numpy float64 oracle, BLAS threads = host cores), {dt:.1f} s"}
 
 
+def adjoint_micro(torch, hbm, src, device):
+    """isolated clean adjoint on a given fixed point, B*T = 16384
+    tokens x 8 slots x d 512, h* and upstream dL/dh ~ N(0,1) per slot, 20 iterations,
+    through the C ABI with device pointers (inputs resident in HBM, each 268 MB > L2)."""
+    from aideen_b200.backend import GpuDeqBackend
+    from aideen_b200.weights import init_all_weights
+    n_tok, iters = 16384, 20
+    be = GpuDeqBackend(D, H, max_batch=1, max_seq_len=n_tok, device=device)
+    be.upload_weights(init_all_weights(D, H, seed=0, attn_sigma=0.8, win_sigma=0.8))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    shape = (n_tok, H, D)
+    hs = torch.randn(shape, device="cuda", generator=g)
+    br = torch.randn(shape, device="cuda", generator=g)
+    rs = torch.randn(shape, device="cuda", generator=g)
+    import ctypes as C
+    from aideen_b200.backend import AdjArgs, DEVICE
+    a = AdjArgs(1, n_tok, iters, 0.85, 0)
+
+    def run():
+        rc = be.lib.aideen_adjoint_on(be.ctx, C.byref(a), C.c_void_p(hs.data_ptr()), C.c_void_p(br.data_ptr()),
+                                      None, C.c_void_p(rs.data_ptr()), DEVICE)
+        assert rc == 0, be.lib.aideen_last_error(be.ctx)
+
+    for _ in range(3):
+        run()
+    be.sync()
+    be.profile(True)
+    be.profile_read(reset=True)
+    reps = 10
+    for _ in range(reps):
+        run()
+    kp = be.profile_read(reset=True)["adjoint"]
+    be.close()
+    ms = kp[0] / max(kp[1], 1)
+    E = n_tok * H
+    nbytes = 4 * (5 * E * D + n_tok * D)  # h*, branch, rhs in; v, g_pre out; NormScale partials out
+    ach = nbytes / (ms / 1e3) / 1e9
+    return {"kernel": "adjoint_kernel<F=4, m=0>", "workload": "16384 tokens x 8 slots x 512, 20 iterations",
+            "bound": "hbm", "achieved": ach, "peak": hbm, "peak_source": src, "unit": "GB/s",
+            "frac": ach / hbm, "ms_per_launch": ms, "algorithmic_bytes_per_launch": nbytes}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -140,6 +182,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-micro", action="store_true", help="skip the isolated-adjoint microbenchmark")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -226,28 +269,35 @@ def main():
     value = tokens / (ms / 1e3)
     e2e = tokens / (ms_e2e / 1e3)
 
-    # dominant-kernel roofline: the fused adjoint (bandwidth-bound), timed alone
+    # per-kernel-class device time of the same step (profiled, outside the timed region)
+    be.profile(True)
+    be.profile_read(reset=True)
+    prof_steps = 3
+    for _ in range(prof_steps):
+        step(DEVICE)
+    kprof = {k: (v[0] / prof_steps, v[1] / prof_steps) for k, v in be.profile_read(reset=True).items()}
+    be.profile(False)
+    hbm, src = peaks()
     N = B_PER_GPU * T
     E = N * H
-    adj_bytes = 4 * (3 * E * D + 2 * N * D)   # pre in; v, g_pre out; dl_dh in; NS partials out
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            be.run_staged_adjoint_picard_no_readback(0.85, ADJ_ITERS, anderson_m=ANDERSON_M)
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = 20
-        s.record(stream)
-        for _ in range(reps):
-            be.run_staged_adjoint_picard_no_readback(0.85, ADJ_ITERS, anderson_m=ANDERSON_M)
-        e.record(stream)
-    torch.cuda.synchronize()
-    adj_ms = s.elapsed_time(e) / reps
-    hbm, src = peaks()
-    achieved = adj_bytes / (adj_ms / 1e3) / 1e9
-    traffic = None
-    prof = os.path.join(ROOT, "profiles", "adjoint_traffic.json")
-    if os.path.exists(prof):
-        with open(prof) as f:
-            traffic = json.load(f).get("bytes_per_launch")
+    dominant = max(kprof, key=lambda k: kprof[k][0])
+    # algorithmic bytes of the Picard solve per launch: signal + attention injection in,
+    # h*, pre, FPM memory and FPM context out (the rank-32 FPM weights are read once).
+    picard_bytes = 4 * 6 * E * D + 4 * 6 * H * D * 32
+    adj_bytes = 4 * (3 * E * D + 2 * N * D)  # pre in; v, g_pre out; dl_dh in; NormScale partials out
+    bytes_of = {"picard": picard_bytes, "adjoint": adj_bytes}
+    roof = None
+    if dominant in bytes_of:
+        kms = kprof[dominant][0] / max(kprof[dominant][1], 1)
+        ach = bytes_of[dominant] / (kms / 1e3) / 1e9
+        roof = {"kernel": {"picard": "picard_kernel<FPM> (token-serial Picard solve + FPM scan)",
+                           "adjoint": "adjoint_kernel (fused clean adjoint)"}[dominant],
+                "bound": "hbm", "achieved": ach, "peak": hbm, "peak_source": src, "unit": "GB/s",
+                "frac": ach / hbm, "traffic": None, "ms_per_launch": kms,
+                "algorithmic_bytes_per_launch": bytes_of[dominant],
+                "note": "latency-bound serial chain (token x iteration); HBM is not the limit"
+                        if dominant == "picard" else ""}
+    c4 = adjoint_micro(torch, hbm, src, local) if world == 1 and not args.no_micro else None
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -262,11 +312,9 @@ def main():
                 "e2e": {"value": e2e, "unit": "tokens/s",
                         "h2d_bytes_per_step": int(tok.nbytes + tg.nbytes), "d2h_bytes_per_step": 4},
                 "gpu_launches": int(launches),
-                "roofline": {"kernel": "adjoint_kernel (fused clean Picard adjoint, all iterations on-chip)",
-                             "bound": "hbm", "achieved": achieved, "peak": hbm,
-                             "peak_source": src, "unit": "GB/s", "frac": achieved / hbm,
-                             "traffic": traffic, "ms_per_launch": adj_ms,
-                             "algorithmic_bytes_per_launch": adj_bytes},
+                "roofline": roof,
+                "kernel_ms_per_step": {k: round(v[0], 4) for k, v in kprof.items()},
+                "roofline_adjoint_c4": c4,
                 "clocks": clk.summary()}
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(16)

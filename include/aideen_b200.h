@@ -114,6 +114,18 @@ int aideen_sync(aideen_ctx *ctx);
 /* Number of this library's own kernel launches issued since create. */
 uint64_t aideen_launch_count(const aideen_ctx *ctx);
 
+/* Per-kernel-class device time (no counterpart in the reference; the
+ * reference's AIDEEN_*_PROFILE timers, gpu_deq.rs:212-217, are host wall
+ * clocks).  When enabled, every launch is bracketed by CUDA events on the
+ * context's stream; aideen_profile_read synchronises and returns cumulative
+ * milliseconds and launch counts per class. */
+enum { AIDEEN_PROF_PICARD = 0, AIDEEN_PROF_ADJOINT = 1, AIDEEN_PROF_GEMM = 2,
+       AIDEEN_PROF_LM_SOFTMAX = 3, AIDEEN_PROF_OPTIMIZER = 4, AIDEEN_PROF_OTHER = 5,
+       AIDEEN_PROF_CLASSES = 6 };
+int aideen_profile(aideen_ctx *ctx, int enable);
+int aideen_profile_read(aideen_ctx *ctx, float *ms /*[6]*/, uint64_t *launches /*[6], nullable*/,
+                        int reset);
+
 /* Length of AllWeights for (d, h) (deq_bridge.rs:103-137). */
 size_t aideen_all_weights_len(uint32_t d_model, uint32_t h_slots);
 
