@@ -45,17 +45,29 @@ __global__ void __launch_bounds__(512) adjoint_kernel(AdjointArgs a) {
   const float rms = sqrtf(ss / (float)d + 1e-6f);
   const float inv = 1.f / fmaxf(rms, 1e-6f);
   const float den = fmaxf((float)d * rms * rms * rms, 1e-6f);
+  // The step is diagonal + rank one: v' = rhs + a*v - ((w . v) / den) * pre with
+  // a = beta*NS/rms + (1 - beta) and w = beta*NS*pre, so each iteration costs
+  // three FMAs per element plus one warp reduction.
+  float4 av[F], wv[F];
+#pragma unroll
+  for (int f = 0; f < F; ++f) {
+    av[f] = (beta * inv) * ns[f] + f4(1.f - beta);
+    wv[f] = beta * (ns[f] * pre[f]);
+  }
   float4 hist[MA > 0 ? MA : 1][F];
   for (int k = 0; k < a.iters; ++k) {
     float c = 0.f;
 #pragma unroll
-    for (int f = 0; f < F; ++f) c += dot4((beta * v[f]) * ns[f], pre[f]);
-    const float cs = warp_sum(c) / den;
+    for (int f = 0; f < F; ++f) c += dot4(wv[f], v[f]);
+    const float ncs = -warp_sum(c) / den;
 #pragma unroll
     for (int f = 0; f < F; ++f) {
-      const float4 up = beta * v[f];
-      const float4 ng = (inv * ns[f]) * up - cs * pre[f];
-      v[f] = rhs[f] + (ng + (1.f - beta) * v[f]);
+      float4 x;
+      x.x = fmaf(ncs, pre[f].x, fmaf(av[f].x, v[f].x, rhs[f].x));
+      x.y = fmaf(ncs, pre[f].y, fmaf(av[f].y, v[f].y, rhs[f].y));
+      x.z = fmaf(ncs, pre[f].z, fmaf(av[f].z, v[f].z, rhs[f].z));
+      x.w = fmaf(ncs, pre[f].w, fmaf(av[f].w, v[f].w, rhs[f].w));
+      v[f] = x;
     }
     if constexpr (MA > 0) {
       // ring buffer as a shift register: hist[i] = iterate stored i steps ago
@@ -141,16 +153,16 @@ __global__ void __launch_bounds__(512) adjoint_kernel(AdjointArgs a) {
   }
   float c = 0.f;
 #pragma unroll
-  for (int f = 0; f < F; ++f) c += dot4((beta * v[f]) * ns[f], pre[f]);
+  for (int f = 0; f < F; ++f) c += dot4(wv[f], v[f]);
   const float cs = warp_sum(c) / den;
   const size_t vbase = ((size_t)s * a.N + n) * d;
 #pragma unroll
   for (int f = 0; f < F; ++f) {
     const int j = (f * 32 + lane) * 4;
-    const float4 up = beta * v[f];
     st4(a.v + vbase + j, v[f]);
-    st4(a.gpre + e + j, (inv * ns[f]) * up - cs * pre[f]);
-    if (a.nsg) st4(nsacc + (size_t)s * d + j, (inv * up) * pre[f]);
+    // g_pre = beta*J_norm^T v = (a - (1 - beta)) * v - (w . v / den) * pre
+    st4(a.gpre + e + j, (av[f] - f4(1.f - beta)) * v[f] - cs * pre[f]);
+    if (a.nsg) st4(nsacc + (size_t)s * d + j, (beta * inv) * (v[f] * pre[f]));
   }
   if (a.nsg) {
     __syncthreads();
