@@ -16,183 +16,270 @@
 
 namespace aideen {
 
-template <int F, int MA>
-__global__ void __launch_bounds__(512) adjoint_kernel(AdjointArgs a) {
-  extern __shared__ float sm[];
-  float *gram = sm;                 // [2][6][16]
-  float *nsacc = sm + 2 * 6 * 16;   // [h][d] when nsg requested
-  const int n = blockIdx.x, s = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+  const uint32_t addr = smem_addr(bar);
+  for (uint32_t i = 0; i < (1u << 26); ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Persistent fused clean adjoint.  Each CTA walks tokens n = blockIdx.x,
+// blockIdx.x + gridDim.x, ...; while a token's h warps (one per slot) run all
+// `iters` iterations in registers, thread 0 has the next token's inputs
+// (pre parts, per-slot RHS, pooled RHS row) streaming into the other half of a
+// double-buffered shared-memory stage with cp.async.bulk, so HBM traffic
+// overlaps the on-chip iterations.  Waits are bounded.
+template <int F, int MA, int MAXT, int MINB>
+__global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
+  extern __shared__ __align__(128) unsigned char smraw[];
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smraw);  // [2]
+  float *gram = reinterpret_cast<float *>(smraw + 128);  // [2][6][16]
+  const int s = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int d = a.d, h = a.h;
+  const size_t hd = (size_t)h * d;
+  const int has_b = a.pre_b != nullptr, has_rs = a.rhs_slot != nullptr, has_tok = a.rhs_tok != nullptr;
+  const size_t stage_f = hd * (1 + has_b + has_rs) + (has_tok ? d : 0);
+  float *stage0 = gram + 192;
+  float *nsacc = stage0 + 2 * stage_f;  // [h][d] when nsg requested
   const float beta = a.beta;
-  const size_t e = ((size_t)n * h + s) * d;
-  float4 pre[F], rhs[F], ns[F], v[F];
-  float ss = 0.f;
-  const float ih = 1.f / (float)h;
-#pragma unroll
-  for (int f = 0; f < F; ++f) {
-    const int j = (f * 32 + lane) * 4;
-    pre[f] = ld4(a.pre_a + e + j);
-    if (a.pre_b) pre[f] = pre[f] + ld4(a.pre_b + e + j);
-    ns[f] = ld4(a.NS + j);
-    float4 r = f4(0.f);
-    if (a.rhs_tok) r = ih * ld4(a.rhs_tok + (size_t)n * d + j);
-    if (a.rhs_slot) r = r + ld4(a.rhs_slot + e + j);
-    rhs[f] = r;
-    v[f] = r;
-    ss += dot4(pre[f], pre[f]);
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&bar[0])));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&bar[1])));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  ss = warp_sum(ss);
-  const float rms = sqrtf(ss / (float)d + 1e-6f);
-  const float inv = 1.f / fmaxf(rms, 1e-6f);
-  const float den = fmaxf((float)d * rms * rms * rms, 1e-6f);
-  // The step is diagonal + rank one: v' = rhs + a*v - ((w . v) / den) * pre with
-  // a = beta*NS/rms + (1 - beta) and w = beta*NS*pre, so each iteration costs
-  // three FMAs per element plus one warp reduction.
-  float4 av[F], wv[F];
-#pragma unroll
-  for (int f = 0; f < F; ++f) {
-    av[f] = (beta * inv) * ns[f] + f4(1.f - beta);
-    wv[f] = beta * (ns[f] * pre[f]);
-  }
-  float4 hist[MA > 0 ? MA : 1][F];
-  for (int k = 0; k < a.iters; ++k) {
-    float c = 0.f;
-#pragma unroll
-    for (int f = 0; f < F; ++f) c += dot4(wv[f], v[f]);
-    const float ncs = -warp_sum(c) / den;
-#pragma unroll
-    for (int f = 0; f < F; ++f) {
-      float4 x;
-      x.x = fmaf(ncs, pre[f].x, fmaf(av[f].x, v[f].x, rhs[f].x));
-      x.y = fmaf(ncs, pre[f].y, fmaf(av[f].y, v[f].y, rhs[f].y));
-      x.z = fmaf(ncs, pre[f].z, fmaf(av[f].z, v[f].z, rhs[f].z));
-      x.w = fmaf(ncs, pre[f].w, fmaf(av[f].w, v[f].w, rhs[f].w));
-      v[f] = x;
+  __syncthreads();
+  auto issue = [&](int n, int b) {
+    float *st = stage0 + b * stage_f;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(&bar[b])),
+                 "r"((uint32_t)(stage_f * 4))
+                 : "memory");
+    size_t o = 0;
+    bulk_g2s(st, a.pre_a + (size_t)n * hd, (uint32_t)(hd * 4), &bar[b]);
+    o += hd;
+    if (has_b) { bulk_g2s(st + o, a.pre_b + (size_t)n * hd, (uint32_t)(hd * 4), &bar[b]); o += hd; }
+    if (has_rs) { bulk_g2s(st + o, a.rhs_slot + (size_t)n * hd, (uint32_t)(hd * 4), &bar[b]); o += hd; }
+    if (has_tok) bulk_g2s(st + o, a.rhs_tok + (size_t)n * d, (uint32_t)(d * 4), &bar[b]);
+  };
+  if (threadIdx.x == 0 && (int)blockIdx.x < a.N) issue(blockIdx.x, 0);
+  int it = 0;
+  bool pending = (int)blockIdx.x < a.N;
+  for (int n = blockIdx.x; n < a.N; n += gridDim.x, ++it) {
+    const int b = it & 1;
+    const int nn = n + (int)gridDim.x;
+    if (threadIdx.x == 0 && nn < a.N) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(nn, b ^ 1);
     }
-    if constexpr (MA > 0) {
-      // ring buffer as a shift register: hist[i] = iterate stored i steps ago
-#pragma unroll
-      for (int i = MA - 1; i > 0; --i)
-#pragma unroll
-        for (int f = 0; f < F; ++f) hist[i][f] = hist[i - 1][f];
-#pragma unroll
-      for (int f = 0; f < F; ++f) hist[0][f] = v[f];
-      const int n_res = k < MA - 1 ? k : MA - 1;
-      if (k >= 2 && n_res >= 2) {
-        // Gram of pseudo-residuals D_i = hist[i] - hist[i+1] over all h*d of the token
-        float g6[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int f = 0; f < F; ++f) {
-          const float4 d0 = hist[0][f] - hist[1][f];
-          const float4 d1 = hist[1][f] - hist[MA > 2 ? 2 : 1][f];
-          g6[0] += dot4(d0, d0);
-          g6[1] += dot4(d0, d1);
-          g6[3] += dot4(d1, d1);
-          if (MA > 3 && n_res == 3) {
-            const float4 d2 = hist[MA > 3 ? 2 : 1][f] - hist[MA > 3 ? 3 : 1][f];
-            g6[2] += dot4(d0, d2);
-            g6[4] += dot4(d1, d2);
-            g6[5] += dot4(d2, d2);
+    const bool ok = mbar_wait_bounded(&bar[b], (it >> 1) & 1);
+    if (!__syncthreads_and(ok)) break;
+    pending = nn < a.N;
+    const float *sa = stage0 + b * stage_f;
+    const float *sb = sa + hd;
+    const float *srs = sa + hd * (1 + has_b);
+    const float *st_tok = sa + hd * (1 + has_b + has_rs);
+    const size_t e = ((size_t)n * h + s) * d;
+    float4 pre[F], rhs[F], ns[F], v[F];
+    float ss = 0.f;
+    const float ih = 1.f / (float)h;
+  #pragma unroll
+    for (int f = 0; f < F; ++f) {
+      const int j = (f * 32 + lane) * 4;
+      pre[f] = ld4(sa + (size_t)s * d + j);
+      if (a.pre_b) pre[f] = pre[f] + ld4(sb + (size_t)s * d + j);
+      ns[f] = ld4(a.NS + j);
+      float4 r = f4(0.f);
+      if (a.rhs_tok) r = ih * ld4(st_tok + j);
+      if (a.rhs_slot) r = r + ld4(srs + (size_t)s * d + j);
+      rhs[f] = r;
+      v[f] = r;
+      ss += dot4(pre[f], pre[f]);
+    }
+    ss = warp_sum(ss);
+    __syncthreads();  // this token's stage is consumed; it may be refilled
+    const float rms = sqrtf(ss / (float)d + 1e-6f);
+    const float inv = 1.f / fmaxf(rms, 1e-6f);
+    const float den = fmaxf((float)d * rms * rms * rms, 1e-6f);
+    // The step is diagonal + rank one: v' = rhs + a*v - ((w . v) / den) * pre with
+    // a = beta*NS/rms + (1 - beta) and w = beta*NS*pre, so each iteration costs
+    // three FMAs per element plus one warp reduction.
+    float4 av[F], wv[F];
+  #pragma unroll
+    for (int f = 0; f < F; ++f) {
+      av[f] = (beta * inv) * ns[f] + f4(1.f - beta);
+      wv[f] = beta * (ns[f] * pre[f]);
+    }
+    float4 hist[MA > 0 ? MA : 1][F];
+    for (int k = 0; k < a.iters; ++k) {
+      float c = 0.f;
+  #pragma unroll
+      for (int f = 0; f < F; ++f) c += dot4(wv[f], v[f]);
+      const float ncs = -warp_sum(c) / den;
+  #pragma unroll
+      for (int f = 0; f < F; ++f) {
+        float4 x;
+        x.x = fmaf(ncs, pre[f].x, fmaf(av[f].x, v[f].x, rhs[f].x));
+        x.y = fmaf(ncs, pre[f].y, fmaf(av[f].y, v[f].y, rhs[f].y));
+        x.z = fmaf(ncs, pre[f].z, fmaf(av[f].z, v[f].z, rhs[f].z));
+        x.w = fmaf(ncs, pre[f].w, fmaf(av[f].w, v[f].w, rhs[f].w));
+        v[f] = x;
+      }
+      if constexpr (MA > 0) {
+        // ring buffer as a shift register: hist[i] = iterate stored i steps ago
+  #pragma unroll
+        for (int i = MA - 1; i > 0; --i)
+  #pragma unroll
+          for (int f = 0; f < F; ++f) hist[i][f] = hist[i - 1][f];
+  #pragma unroll
+        for (int f = 0; f < F; ++f) hist[0][f] = v[f];
+        const int n_res = k < MA - 1 ? k : MA - 1;
+        if (k >= 2 && n_res >= 2) {
+          // Gram of pseudo-residuals D_i = hist[i] - hist[i+1] over all h*d of the token
+          float g6[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  #pragma unroll
+          for (int f = 0; f < F; ++f) {
+            const float4 d0 = hist[0][f] - hist[1][f];
+            const float4 d1 = hist[1][f] - hist[MA > 2 ? 2 : 1][f];
+            g6[0] += dot4(d0, d0);
+            g6[1] += dot4(d0, d1);
+            g6[3] += dot4(d1, d1);
+            if (MA > 3 && n_res == 3) {
+              const float4 d2 = hist[MA > 3 ? 2 : 1][f] - hist[MA > 3 ? 3 : 1][f];
+              g6[2] += dot4(d0, d2);
+              g6[4] += dot4(d1, d2);
+              g6[5] += dot4(d2, d2);
+            }
           }
-        }
-        float *buf = gram + (k & 1) * 96;
-#pragma unroll
-        for (int q = 0; q < 6; ++q) {
-          const float x = warp_sum(g6[q]);
-          if (lane == 0) buf[q * 16 + s] = x;
-        }
-        __syncthreads();
-#pragma unroll
-        for (int q = 0; q < 6; ++q) {
-          float t = 0.f;
-          for (int w = 0; w < h; ++w) t += buf[q * 16 + w];
-          g6[q] = t;
-        }
-        float b0, b1, b2 = 0.f;
-        if (n_res == 2) {
-          float g00 = g6[0], g01 = g6[1], g10 = g6[1], g11 = g6[3];
-          const float reg = fmaxf(1e-8f, 1e-4f * (fabsf(g00) + fabsf(g11)));
-          g00 += reg;
-          g11 += reg;
-          const float det = g00 * g11 - g01 * g10;
-          const float sdet = det < 0.f ? fminf(det, -1e-10f) : fmaxf(det, 1e-10f);
-          b0 = (g11 - g01) / sdet;
-          b1 = (g00 - g10) / sdet;
-        } else {
-          float g00 = g6[0], g01 = g6[1], g02 = g6[2];
-          float g10 = g6[1], g11 = g6[3], g12 = g6[4];
-          float g20 = g6[2], g21 = g6[4], g22 = g6[5];
-          const float reg = fmaxf(1e-8f, 1e-4f * (fabsf(g00) + fabsf(g11) + fabsf(g22)));
-          g00 += reg;
-          g11 += reg;
-          g22 += reg;
-          const float det = g00 * (g11 * g22 - g12 * g21) - g01 * (g10 * g22 - g12 * g20) +
-                            g02 * (g10 * g21 - g11 * g20);
-          const float sdet = det < 0.f ? fminf(det, -1e-8f) : fmaxf(det, 1e-8f);
-          b0 = ((g11 * g22 - g12 * g21) - g01 * (g22 - g12) + g02 * (g21 - g11)) / sdet;
-          b1 = (g00 * (g22 - g12) - (g10 * g22 - g12 * g20) + g02 * (g10 - g20)) / sdet;
-          b2 = (g00 * (g11 - g21) - g01 * (g10 - g20) + (g10 * g21 - g11 * g20)) / sdet;
-        }
-        b0 = fminf(fmaxf(b0, -2.f), 3.f);
-        b1 = fminf(fmaxf(b1, -2.f), 3.f);
-        if (n_res == 3) b2 = fminf(fmaxf(b2, -2.f), 3.f);
-        const float ssum = b0 + b1 + (n_res == 3 ? b2 : 0.f);
-        if (fabsf(ssum) < 1e-6f) {
-          b0 = 1.f; b1 = 0.f; b2 = 0.f;
-        } else {
-          b0 /= ssum; b1 /= ssum; b2 = n_res == 3 ? b2 / ssum : 0.f;
-        }
-#pragma unroll
-        for (int f = 0; f < F; ++f) {
-          float4 mixed = b0 * hist[0][f] + b1 * hist[1][f];
-          if (MA > 3 && n_res == 3) mixed = mixed + b2 * hist[MA > 3 ? 2 : 1][f];
-          v[f] = mixed;
+          float *buf = gram + (k & 1) * 96;
+  #pragma unroll
+          for (int q = 0; q < 6; ++q) {
+            const float x = warp_sum(g6[q]);
+            if (lane == 0) buf[q * 16 + s] = x;
+          }
+          __syncthreads();
+  #pragma unroll
+          for (int q = 0; q < 6; ++q) {
+            float t = 0.f;
+            for (int w = 0; w < h; ++w) t += buf[q * 16 + w];
+            g6[q] = t;
+          }
+          float b0, b1, b2 = 0.f;
+          if (n_res == 2) {
+            float g00 = g6[0], g01 = g6[1], g10 = g6[1], g11 = g6[3];
+            const float reg = fmaxf(1e-8f, 1e-4f * (fabsf(g00) + fabsf(g11)));
+            g00 += reg;
+            g11 += reg;
+            const float det = g00 * g11 - g01 * g10;
+            const float sdet = det < 0.f ? fminf(det, -1e-10f) : fmaxf(det, 1e-10f);
+            b0 = (g11 - g01) / sdet;
+            b1 = (g00 - g10) / sdet;
+          } else {
+            float g00 = g6[0], g01 = g6[1], g02 = g6[2];
+            float g10 = g6[1], g11 = g6[3], g12 = g6[4];
+            float g20 = g6[2], g21 = g6[4], g22 = g6[5];
+            const float reg = fmaxf(1e-8f, 1e-4f * (fabsf(g00) + fabsf(g11) + fabsf(g22)));
+            g00 += reg;
+            g11 += reg;
+            g22 += reg;
+            const float det = g00 * (g11 * g22 - g12 * g21) - g01 * (g10 * g22 - g12 * g20) +
+                              g02 * (g10 * g21 - g11 * g20);
+            const float sdet = det < 0.f ? fminf(det, -1e-8f) : fmaxf(det, 1e-8f);
+            b0 = ((g11 * g22 - g12 * g21) - g01 * (g22 - g12) + g02 * (g21 - g11)) / sdet;
+            b1 = (g00 * (g22 - g12) - (g10 * g22 - g12 * g20) + g02 * (g10 - g20)) / sdet;
+            b2 = (g00 * (g11 - g21) - g01 * (g10 - g20) + (g10 * g21 - g11 * g20)) / sdet;
+          }
+          b0 = fminf(fmaxf(b0, -2.f), 3.f);
+          b1 = fminf(fmaxf(b1, -2.f), 3.f);
+          if (n_res == 3) b2 = fminf(fmaxf(b2, -2.f), 3.f);
+          const float ssum = b0 + b1 + (n_res == 3 ? b2 : 0.f);
+          if (fabsf(ssum) < 1e-6f) {
+            b0 = 1.f; b1 = 0.f; b2 = 0.f;
+          } else {
+            b0 /= ssum; b1 /= ssum; b2 = n_res == 3 ? b2 / ssum : 0.f;
+          }
+  #pragma unroll
+          for (int f = 0; f < F; ++f) {
+            float4 mixed = b0 * hist[0][f] + b1 * hist[1][f];
+            if (MA > 3 && n_res == 3) mixed = mixed + b2 * hist[MA > 3 ? 2 : 1][f];
+            v[f] = mixed;
+          }
         }
       }
     }
-  }
-  float c = 0.f;
-#pragma unroll
-  for (int f = 0; f < F; ++f) c += dot4(wv[f], v[f]);
-  const float cs = warp_sum(c) / den;
-  const size_t vbase = ((size_t)s * a.N + n) * d;
-#pragma unroll
-  for (int f = 0; f < F; ++f) {
-    const int j = (f * 32 + lane) * 4;
-    st4(a.v + vbase + j, v[f]);
-    // g_pre = beta*J_norm^T v = (a - (1 - beta)) * v - (w . v / den) * pre
-    st4(a.gpre + e + j, (av[f] - f4(1.f - beta)) * v[f] - cs * pre[f]);
-    if (a.nsg) st4(nsacc + (size_t)s * d + j, (beta * inv) * (v[f] * pre[f]));
-  }
-  if (a.nsg) {
-    __syncthreads();
-    for (int j = threadIdx.x; j < d; j += blockDim.x) {
-      float t = 0.f;
-      for (int q = 0; q < h; ++q) t += nsacc[(size_t)q * d + j];
-      a.nsg[(size_t)n * d + j] = t;
+    float c = 0.f;
+  #pragma unroll
+    for (int f = 0; f < F; ++f) c += dot4(wv[f], v[f]);
+    const float cs = warp_sum(c) / den;
+    const size_t vbase = ((size_t)s * a.N + n) * d;
+  #pragma unroll
+    for (int f = 0; f < F; ++f) {
+      const int j = (f * 32 + lane) * 4;
+      st4(a.v + vbase + j, v[f]);
+      // g_pre = beta*J_norm^T v = (a - (1 - beta)) * v - (w . v / den) * pre
+      st4(a.gpre + e + j, (av[f] - f4(1.f - beta)) * v[f] - cs * pre[f]);
+      if (a.nsg) st4(nsacc + (size_t)s * d + j, (beta * inv) * (v[f] * pre[f]));
+    }
+    if (a.nsg) {
+      __syncthreads();
+      for (int j = threadIdx.x; j < d; j += blockDim.x) {
+        float t = 0.f;
+        for (int q = 0; q < h; ++q) t += nsacc[(size_t)q * d + j];
+        a.nsg[(size_t)n * d + j] = t;
+      }
     }
   }
+  // a copy issued for a token this CTA did not reach (timeout path) must land first
+  if (threadIdx.x == 0 && pending && it < 1 << 30) mbar_wait_bounded(&bar[(it + 1) & 1], ((it + 1) >> 1) & 1);
 }
 
-template <int F, int MA>
-static cudaError_t adjoint_launch(const AdjointArgs &a, size_t smem, cudaStream_t st) {
-  auto k = adjoint_kernel<F, MA>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-  }
-  k<<<a.N, 32 * a.h, smem, st>>>(a);
+template <int F, int MA, int MAXT, int MINB>
+static cudaError_t adjoint_launch(const AdjointArgs &a, cudaStream_t st) {
+  const size_t hd = (size_t)a.h * a.d;
+  const size_t stage_f = hd * (1 + (a.pre_b != nullptr) + (a.rhs_slot != nullptr)) +
+                         (a.rhs_tok ? (size_t)a.d : 0);
+  const size_t smem = 128 + 192 * 4 + 2 * stage_f * 4 + (a.nsg ? hd * 4 : 0);
+  auto k = adjoint_kernel<F, MA, MAXT, MINB>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  int per_sm = 0, dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, 32 * a.h, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  const int grid = a.N < sms * per_sm ? a.N : sms * per_sm;
+  k<<<grid, 32 * a.h, smem, st>>>(a);
   return cudaGetLastError();
 }
 
 template <int F>
 static cudaError_t adjoint_dispatch_m(const AdjointArgs &a, cudaStream_t st) {
-  const size_t smem = (2 * 6 * 16 + (a.nsg ? (size_t)a.h * a.d : 0)) * sizeof(float);
   const int ma = a.anderson_m <= 2 ? 0 : a.anderson_m;  // m <= 2 never mixes (n_res < 2)
+  const bool small = a.h <= 8;
   switch (ma) {
-    case 0: return adjoint_launch<F, 0>(a, smem, st);
-    case 3: return adjoint_launch<F, 3>(a, smem, st);
-    case 4: return adjoint_launch<F, 4>(a, smem, st);
+    case 0: return small ? adjoint_launch<F, 0, 256, 2>(a, st) : adjoint_launch<F, 0, 512, 1>(a, st);
+    case 3: return small ? adjoint_launch<F, 3, 256, 1>(a, st) : adjoint_launch<F, 3, 512, 1>(a, st);
+    case 4: return small ? adjoint_launch<F, 4, 256, 1>(a, st) : adjoint_launch<F, 4, 512, 1>(a, st);
     default: return cudaErrorInvalidValue;
   }
 }
