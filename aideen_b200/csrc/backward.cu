@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
   const int has_b = a.pre_b != nullptr, has_rs = a.rhs_slot != nullptr, has_tok = a.rhs_tok != nullptr;
   const size_t stage_f = hd * (1 + has_b + has_rs) + (has_tok ? d : 0);
   float *stage0 = gram + 192;
-  float *nsacc = stage0 + 2 * stage_f;  // [h][d] when nsg requested
+  // NormScale partials [h][d] reuse the current token's stage, consumed by then.
   const float beta = a.beta;
   if (threadIdx.x == 0) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&bar[0])));
@@ -95,6 +95,7 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
     if (!__syncthreads_and(ok)) break;
     pending = nn < a.N;
     const float *sa = stage0 + b * stage_f;
+    float *nsacc = stage0 + b * stage_f;
     const float *sb = sa + hd;
     const float *srs = sa + hd * (1 + has_b);
     const float *st_tok = sa + hd * (1 + has_b + has_rs);
@@ -120,6 +121,7 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
     const float rms = sqrtf(ss / (float)d + 1e-6f);
     const float inv = 1.f / fmaxf(rms, 1e-6f);
     const float den = fmaxf((float)d * rms * rms * rms, 1e-6f);
+    const float inv_den = 1.f / den;
     // The step is diagonal + rank one: v' = rhs + a*v - ((w . v) / den) * pre with
     // a = beta*NS/rms + (1 - beta) and w = beta*NS*pre, so each iteration costs
     // three FMAs per element plus one warp reduction.
@@ -131,10 +133,15 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
     }
     float4 hist[MA > 0 ? MA : 1][F];
     for (int k = 0; k < a.iters; ++k) {
-      float c = 0.f;
-  #pragma unroll
-      for (int f = 0; f < F; ++f) c += dot4(wv[f], v[f]);
-      const float ncs = -warp_sum(c) / den;
+      float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;  // independent partial sums (ILP)
+#pragma unroll
+      for (int f = 0; f < F; ++f) {
+        c0 = fmaf(wv[f].x, v[f].x, c0);
+        c1 = fmaf(wv[f].y, v[f].y, c1);
+        c2 = fmaf(wv[f].z, v[f].z, c2);
+        c3 = fmaf(wv[f].w, v[f].w, c3);
+      }
+      const float ncs = -warp_sum((c0 + c1) + (c2 + c3)) * inv_den;
   #pragma unroll
       for (int f = 0; f < F; ++f) {
         float4 x;
@@ -246,6 +253,7 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
         for (int q = 0; q < h; ++q) t += nsacc[(size_t)q * d + j];
         a.nsg[(size_t)n * d + j] = t;
       }
+      __syncthreads();  // nsacc (this stage) is read before thread 0 refills it
     }
   }
   // a copy issued for a token this CTA did not reach (timeout path) must land first
@@ -257,7 +265,7 @@ static cudaError_t adjoint_launch(const AdjointArgs &a, cudaStream_t st) {
   const size_t hd = (size_t)a.h * a.d;
   const size_t stage_f = hd * (1 + (a.pre_b != nullptr) + (a.rhs_slot != nullptr)) +
                          (a.rhs_tok ? (size_t)a.d : 0);
-  const size_t smem = 128 + 192 * 4 + 2 * stage_f * 4 + (a.nsg ? hd * 4 : 0);
+  const size_t smem = 128 + 192 * 4 + 2 * stage_f * 4;
   auto k = adjoint_kernel<F, MA, MAXT, MINB>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
