@@ -44,6 +44,7 @@ struct DevBufs {
   unsigned long long *stats = nullptr;
   float *sigmas = nullptr;
   float *stage = nullptr;  // packed AllWeights staging for upload/download
+  float *ws = nullptr;     // split-K partial sums of the tensor-core GEMM
 };
 
 }  // namespace
@@ -59,7 +60,8 @@ struct aideen_ctx {
   unsigned long long launches = 0;
   size_t W_len = 0, lm_len = 0, max_tokens = 0;
   size_t lm_b = 0, lm_g = 0;
-  long Vp = 0;                 // logits row stride (vocab rounded up to 4 floats)   // offsets of b_lm and g_lm in the padded LM block
+  long Vp = 0;
+  size_t ws_floats = 0;                 // logits row stride (vocab rounded up to 4 floats)   // offsets of b_lm and g_lm in the padded LM block
   float signal_scale = 1.f;
   bool signal_zero = false;
   aideen_run last_run{};
@@ -153,7 +155,7 @@ GemmArgs gemm(int M, int N, int K, int batch, const float *A, long lda, long sA,
 
 // GEMM dispatch: tcgen05 (3xTF32) when supported for these operands, else CUDA cores.
 cudaError_t gemm_any(aideen_ctx *ctx, const GemmArgs &g) {
-  if (ctx->use_tc && tc_gemm_supported(g)) return tc_gemm(g, ctx->stream);
+  if (ctx->use_tc && tc_gemm_supported(g)) return tc_gemm(g, ctx->stream, ctx->b.ws, ctx->ws_floats);
   return gemm_f32(g, ctx->stream);
 }
 
@@ -445,7 +447,9 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   A(&b.mstate, (size_t)cfg->max_batch * h * d);
   A(&b.pooled, N * d); A(&b.dl_dh, N * d); A(&b.nsg, N * d); A(&b.dS, N * d);
   A(&b.y, N * d); A(&b.dy, N * d); A(&b.ggp, N * d); A(&b.lrms, N); A(&b.loss_rows, N);
-  A(&b.scal, 4); A(&b.stage, ctx->Lx.total); A(&b.stats, 4); A(&b.sigmas, 5 * h + 2);
+  A(&b.scal, 4); A(&b.stage, ctx->Lx.total);
+  ctx->ws_floats = 16 * N * d;  // up to 16 splits of an [N][d] output
+  A(&b.ws, ctx->ws_floats); A(&b.stats, 4); A(&b.sigmas, 5 * h + 2);
   if (V) {
     A(&b.lmp, ctx->lm_len); A(&b.Glm, ctx->lm_len); A(&b.Mlm1, ctx->lm_len); A(&b.Mlm2, ctx->lm_len);
     A(&b.logits, N * (size_t)ctx->Vp); A(&b.emb, V * d);
@@ -486,7 +490,7 @@ void aideen_destroy(aideen_ctx *ctx) {
                   b.pooled, b.hist, b.fpmctx, b.mstate, b.iters, b.v, b.gpre, b.dl_dh, b.rhs_slot,
                   b.nsg, b.da, b.dn, b.dQ, b.dK, b.dV, b.dsig, b.dRc, b.dS, b.lmp, b.Glm, b.Mlm1,
                   b.Mlm2, b.y, b.lrms, b.logits, b.dy, b.ggp, b.loss_rows, b.scal, b.emb, b.stats,
-                  b.sigmas, b.stage};
+                  b.sigmas, b.stage, b.ws};
   for (void *p : ptrs)
     if (p) cudaFree(p);
   if (ctx->stream && ctx->own_stream) cudaStreamDestroy(ctx->stream);
@@ -863,9 +867,12 @@ int aideen_gemm_selftest(aideen_ctx *ctx, int M, int N, int K, int batch, int tr
   } else {
     cudaEvent_t e0, e1, e2;
     cudaEventCreate(&e0); cudaEventCreate(&e1); cudaEventCreate(&e2);
-    tc_gemm(g, st);  // warm-up
+    float *wsp = nullptr;
+    const size_t wsn = 16 * (size_t)M * N;
+    cudaMalloc(&wsp, wsn * 4);
+    tc_gemm(g, st, wsp, wsn);  // warm-up
     cudaEventRecord(e0, st);
-    cudaError_t ce = tc_gemm(g, st);
+    cudaError_t ce = tc_gemm(g, st, wsp, wsn);
     cudaEventRecord(e1, st);
     GemmArgs g2 = g;
     g2.C = C2;
@@ -879,6 +886,7 @@ int aideen_gemm_selftest(aideen_ctx *ctx, int M, int N, int K, int batch, int tr
     cudaEventElapsedTime(&t1, e0, e1);
     cudaEventElapsedTime(&t2, e1, e2);
     cudaEventDestroy(e0); cudaEventDestroy(e1); cudaEventDestroy(e2);
+    cudaFree(wsp);
     if (ce != cudaSuccess || ce2 != cudaSuccess || se != cudaSuccess)
       rc = set_err(ctx, AIDEEN_E_CUDA, "GEMM self-test launch failed");
     else if (tc_gemm_error(true))

@@ -23,7 +23,8 @@ struct GemmArgs {
 cudaError_t gemm_f32(const GemmArgs &g, cudaStream_t s);
 // Same contract on tcgen05 tensor cores (3xTF32, fp32-accurate); no abias.
 bool tc_gemm_supported(const GemmArgs &g);
-cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t s);
+// ws: optional workspace for split-K partial sums (ws_floats capacity).
+cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t s, float *ws = nullptr, size_t ws_floats = 0);
 unsigned int tc_gemm_error(bool reset);
 
 struct AttnArgs {

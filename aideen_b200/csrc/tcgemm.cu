@@ -123,6 +123,7 @@ struct TcParams {
   long ldc, strideC;
   float alpha, beta;
   int a_batched, b_batched;  // operand map has a batch dimension
+  int ksplit, kchunk;        // split-K: blockIdx.z = split index, kchunk K-blocks each
 };
 
 // Warp roles (192 threads): warp 0 lane 0 = TMA producer, warp 1 = TMEM
@@ -147,7 +148,11 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
   uint32_t *err = tmem_slot + 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, bz = blockIdx.z;
-  const int kblocks = (p.K + BK - 1) / BK;
+  // with split-K, z selects the K range (operands unbatched) and the output slice
+  const int zab = p.ksplit > 1 ? 0 : bz;
+  const int kb0 = p.ksplit > 1 ? bz * p.kchunk : 0;
+  const int ktot = (p.K + BK - 1) / BK;
+  const int kblocks = p.ksplit > 1 ? min(p.kchunk, ktot - kb0) : ktot;
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -184,9 +189,9 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
         const int s = kb % STAGES;
         if (kb >= STAGES && !mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { ok = false; break; }
         if (*(volatile uint32_t *)err) { ok = false; break; }
-        const int k0 = kb * BK;
+        const int k0 = (kb0 + kb) * BK;
         mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
-        const int za = p.a_batched ? bz : 0, zb = p.b_batched ? bz : 0;
+        const int za = p.a_batched ? zab : 0, zb = p.b_batched ? zab : 0;
         if (p.a_kmajor) {
           tma_load_3d(stage_ptr(s, 0), &mapA, &full[s], k0, m0, za);
         } else {
@@ -358,7 +363,23 @@ bool tc_gemm_supported(const GemmArgs &g) {
   return encode_fn() != nullptr;
 }
 
-cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st) {
+namespace {
+// C = alpha * sum_s ws[s] + beta * C, summed in split order (deterministic).
+__global__ void splitk_reduce_kernel(const float *__restrict__ ws, int splits, int M, int N, float *C,
+                                     long ldc, float alpha, float beta) {
+  const size_t total = (size_t)M * N;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < splits; ++s) acc += ws[(size_t)s * total + i];
+    const size_t m = i / N, n = i % N;
+    float *c = C + m * ldc + n;
+    *c = beta != 0.f ? alpha * acc + beta * *c : alpha * acc;
+  }
+}
+}  // namespace
+
+cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st, float *ws, size_t ws_floats) {
   // A: K-major when not transposed (row m contiguous along k).
   const bool a_k = !g.transA, b_k = g.transB;
   CUtensorMap ma, mb;
@@ -377,8 +398,29 @@ cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st) {
     ok = make_map(&mb, g.B, g.N, g.K, b_batched ? g.batch : 1, g.ldb, g.strideB, 32, BK, false);
   if (!ok) return cudaErrorInvalidValue;
   TcParams p{g.M, g.N, g.K, a_k, b_k, g.C, g.ldc, g.strideC, g.alpha, g.beta, a_batched ? 1 : 0,
-             b_batched ? 1 : 0};
-  dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.batch);
+             b_batched ? 1 : 0, 1, 0};
+  const int tiles_n = (g.N + BN - 1) / BN, tiles_m = (g.M + BM - 1) / BM;
+  const int tiles = tiles_n * tiles_m * g.batch;
+  const int kblocks = (g.K + BK - 1) / BK;
+  int zdim = g.batch;
+  // Split K when the output has too few tiles to fill the GPU and K is long.
+  if (ws && g.batch == 1 && tiles < 148 && kblocks >= 64) {
+    int splits = (2 * 148 + tiles - 1) / tiles;
+    if (splits > 16) splits = 16;
+    const int chunk = (kblocks + splits - 1) / splits;
+    splits = (kblocks + chunk - 1) / chunk;
+    if ((size_t)splits * g.M * g.N <= ws_floats && splits > 1) {
+      p.ksplit = splits;
+      p.kchunk = chunk;
+      p.C = ws;
+      p.ldc = g.N;
+      p.strideC = (long)g.M * g.N;
+      p.alpha = 1.f;
+      p.beta = 0.f;
+      zdim = splits;
+    }
+  }
+  dim3 grid(tiles_n, tiles_m, zdim);
   if (BN == 128) {
     const size_t smem = tc_smem<128>();
     cudaFuncSetAttribute(tcgemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -388,6 +430,9 @@ cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st) {
     cudaFuncSetAttribute(tcgemm_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     tcgemm_kernel<32><<<grid, TC_THREADS, smem, st>>>(ma, mb, p);
   }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || p.ksplit <= 1) return e;
+  splitk_reduce_kernel<<<148 * 4, 256, 0, st>>>(ws, p.ksplit, g.M, g.N, g.C, g.ldc, g.alpha, g.beta);
   return cudaGetLastError();
 }
 
