@@ -20,7 +20,8 @@ from .layout import Layout
 HOST, DEVICE = 0, 1
 
 BUF = dict(hstar=0, pooled=1, signal=2, attn=3, iters=4, adj_v=5, gpre=6, dl_dh=7, hist_ctx=8,
-           mstate=9, fpm_ctx=10, alpha=11, s_in=12, ds_in=13, lm_grads=14, pre=15)
+           mstate=9, fpm_ctx=10, alpha=11, s_in=12, ds_in=13, lm_grads=14, pre=15, fpm_dm=16,
+           fpm_carry=17)
 
 RULE_ADAM, RULE_CLIPPED_SGD = 0, 1
 
@@ -202,15 +203,15 @@ class GpuDeqBackend:
     def launch_count(self) -> int:
         return int(self.lib.aideen_launch_count(self.ctx))
 
-    PROF_CLASSES = ("picard", "adjoint", "gemm", "lm_softmax", "optimizer", "other")
+    PROF_CLASSES = ("picard", "adjoint", "gemm", "lm_softmax", "optimizer", "other", "fpm_bwd")
 
     def profile(self, enable: bool = True):
         """Bracket every kernel launch with CUDA events (per-class device time)."""
         self._check(self.lib.aideen_profile(self.ctx, int(enable)), "profile")
 
     def profile_read(self, reset: bool = True) -> dict:
-        ms = np.zeros(6, np.float32)
-        n = np.zeros(6, np.uint64)
+        ms = np.zeros(len(self.PROF_CLASSES), np.float32)
+        n = np.zeros(len(self.PROF_CLASSES), np.uint64)
         self._check(self.lib.aideen_profile_read(self.ctx, _ptr(ms), _ptr(n), int(reset)), "profile_read")
         return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(self.PROF_CLASSES)}
 

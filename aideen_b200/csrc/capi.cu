@@ -45,6 +45,14 @@ struct DevBufs {
   float *sigmas = nullptr;
   float *stage = nullptr;  // packed AllWeights staging for upload/download
   float *ws = nullptr;     // split-K partial sums of the tensor-core GEMM
+  // FPM backward (allocated on first use): [N][h][d] unless noted
+  float *fc = nullptr, *frp = nullptr, *fdl = nullptr, *falpha = nullptr, *fcpre = nullptr,
+        *fcbd = nullptr, *fcalog = nullptr, *fcgz = nullptr, *fcwx = nullptr, *fminner = nullptr,
+        *fdm = nullptr, *fgpre = nullptr;
+  float *fup = nullptr, *fkw = nullptr, *fdup = nullptr;  // [N][h][32]
+  float *frz = nullptr, *fgraw = nullptr;                 // [N][h]
+  float *fcarry = nullptr;                                // [max_batch][h][d] TBPTT carry
+  float *fpart = nullptr;                                 // [4][max_batch][h][d]
 };
 
 }  // namespace
@@ -74,6 +82,7 @@ struct aideen_ctx {
   // opt-in per-kernel-class timing (aideen_profile): events around each launch
   bool prof = false;
   std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> pev;
+  int prof_phase = -1;    // >= 0: every launch is charged to this class
   double prof_ms[AIDEEN_PROF_CLASSES] = {};
   unsigned long long prof_n[AIDEEN_PROF_CLASSES] = {};
   Layout P{128, 1, 64};   // device (padded) layout
@@ -93,7 +102,8 @@ int set_err(aideen_ctx *c, int code, const std::string &msg) {
     if (_e != cudaSuccess)                                                             \
       return set_err(ctx, AIDEEN_E_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
   } while (0)
-int prof_class(const char *expr) {
+int prof_class(const char *expr, int phase) {
+  if (phase >= 0) return phase;
   if (strstr(expr, "launch_picard")) return AIDEEN_PROF_PICARD;
   if (strstr(expr, "launch_adjoint")) return AIDEEN_PROF_ADJOINT;
   if (strstr(expr, "gemm_any")) return AIDEEN_PROF_GEMM;
@@ -115,7 +125,7 @@ int prof_class(const char *expr) {
     cudaError_t _e = (expr);                                                           \
     if (ctx->prof) {                                                                   \
       cudaEventRecord(_e1, ctx->stream);                                               \
-      ctx->pev.push_back({prof_class(#expr), {_e0, _e1}});                            \
+      ctx->pev.push_back({prof_class(#expr, ctx->prof_phase), {_e0, _e1}});                            \
     }                                                                                  \
     if (_e != cudaSuccess)                                                             \
       return set_err(ctx, AIDEEN_E_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
@@ -277,6 +287,8 @@ int run_adjoint(aideen_ctx *ctx, int N, const float *pre_a, const float *pre_b,
   return AIDEEN_OK;
 }
 
+int run_fpm_backward(aideen_ctx *ctx);
+
 int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
   const int N = ctx->N;
@@ -335,6 +347,73 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   } else if (want_ds) {
     CU(cudaMemsetAsync(b.dS, 0, (size_t)N * d * sizeof(float), st));
   }
+  if (ctx->last_run.fpm) CHK(run_fpm_backward(ctx));
+  return AIDEEN_OK;
+}
+
+// FPM memory backward over the last forward's chunk (fpm_bwd.cu); adds the
+// FPM parameters' gradients to G and advances the TBPTT carry.
+int run_fpm_backward(aideen_ctx *ctx) {
+  const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
+  const int B = ctx->last_run.batch, T = ctx->last_run.seq_len, N = B * T;
+  const Layout &L = ctx->P;
+  DevBufs &b = ctx->b;
+  cudaStream_t st = ctx->stream;
+  const size_t Nhd = ctx->max_tokens * h * d, NH32 = ctx->max_tokens * h * kRank;
+  if (!b.fc) {
+    cudaError_t e = cudaSuccess;
+    auto A = [&](float **p, size_t n) { if (e == cudaSuccess) e = dalloc(p, n); };
+    A(&b.fc, Nhd); A(&b.frp, Nhd); A(&b.fdl, Nhd); A(&b.falpha, Nhd); A(&b.fcpre, Nhd);
+    A(&b.fcbd, Nhd); A(&b.fcalog, Nhd); A(&b.fcgz, Nhd); A(&b.fcwx, Nhd); A(&b.fminner, Nhd);
+    A(&b.fdm, Nhd); A(&b.fgpre, Nhd); A(&b.fup, NH32); A(&b.fkw, NH32); A(&b.fdup, NH32);
+    A(&b.frz, ctx->max_tokens * h); A(&b.fgraw, ctx->max_tokens * h);
+    A(&b.fpart, 4 * (size_t)ctx->cfg.max_batch * h * d);
+    CU(e);
+  }
+  const float *W = b.W;
+  float *G = b.G;
+  const int R = kRank, HR = h * kRank;
+  const long hd = (long)h * d;
+  FpmBwdArgs a{};
+  a.B = B; a.T = T; a.h = h; a.d = d; a.W = W;
+  a.off_bdelta = L.b_delta; a.off_bret = L.b_retain; a.off_wgate = L.w_write_gate;
+  a.off_bwrite = L.b_write_mem; a.off_alog = L.alog; a.off_wx = L.wx;
+  a.hstar = b.hstar; a.hist = b.hist; a.c = b.fc; a.rpre = b.frp; a.dpre = b.fdl; a.v = b.v;
+  a.alpha = b.falpha; a.cpre = b.fcpre; a.cbd = b.fcbd; a.calog = b.fcalog; a.cgz = b.fcgz;
+  a.cwx = b.fcwx; a.minner = b.fminner; a.rz = b.frz; a.graw = b.fgraw; a.dm = b.fdm;
+  a.gpre = b.fgpre; a.carry = b.fcarry; a.part = b.fpart;
+  ctx->prof_phase = AIDEEN_PROF_FPM_BWD;
+  struct PhaseReset { aideen_ctx *c; ~PhaseReset() { c->prof_phase = -1; } } phase_reset{ctx};
+  KL(launch_fpm_c(b.hstar, b.signal, b.fc, (size_t)N * h * d, st));
+  // up[n][s][r] = sum_j c W_retain_up[s][j][r];  kw = same with W_k_write
+  KL(gemm_any(ctx, gemm(N, R, d, h, b.fc, hd, d, false, W + L.w_retain_up, R, (long)d * R, false,
+                   b.fup, HR, R)));
+  KL(gemm_any(ctx, gemm(N, R, d, h, b.fc, hd, d, false, W + L.w_k_write, R, (long)d * R, false,
+                   b.fkw, HR, R)));
+  // retain / proposal pre-activations (bias added in the coefficient kernel)
+  KL(gemm_any(ctx, gemm(N, d, R, h, b.fup, HR, R, false, W + L.w_retain_down, d, (long)R * d, false,
+                   b.frp, hd, d)));
+  KL(gemm_any(ctx, gemm(N, d, R, h, b.fkw, HR, R, false, W + L.w_v_write, d, (long)R * d, false,
+                   b.fdl, hd, d)));
+  KL(launch_fpm_coef(a, st));
+  KL(launch_fpm_scan(a, st));
+  KL(launch_fpm_gate(a, st));
+  KL(launch_fpm_finalize(a, G, st));
+  // W_retain_down[s][r][k] = sum_n up[n][s][r] g_pre[n][s][k]
+  KL(gemm_any(ctx, gemm(R, d, N, h, b.fup, HR, R, true, b.fgpre, hd, d, false, G + L.w_retain_down, d,
+                   (long)R * d)));
+  // dup[n][s][r] = sum_k g_pre[n][s][k] W_retain_down[s][r][k]
+  KL(gemm_any(ctx, gemm(N, R, d, h, b.fgpre, hd, d, false, W + L.w_retain_down, d, (long)R * d, true,
+                   b.fdup, HR, R)));
+  // W_retain_up[s][j][r] = sum_n c[n][s][j] dup[n][s][r]
+  KL(gemm_any(ctx, gemm(d, R, N, h, b.fc, hd, d, true, b.fdup, HR, R, false, G + L.w_retain_up, R,
+                   (long)d * R)));
+  // W_write_gate[s][k] = d^-1/2 sum_n graw[n][s] c[n][s][k];  b_write_mem[s] = sum_n graw[n][s]
+  KL(gemm_any(ctx, gemm(1, d, N, h, b.fgraw, h, 1, true, b.fc, hd, d, false, G + L.w_write_gate, d, d,
+                   1.f / std::sqrt((float)d))));
+  KL(launch_colsum(b.fgraw, N, h, h, G + L.b_write_mem, h, 0, false, st));
+  // W_out[r][c] = sum_{n,s} dm[n][s][r] m_inner[n][s][c]
+  KL(gemm_any(ctx, gemm(d, d, N * h, 1, b.fdm, d, 0, true, b.fminner, d, 0, false, G + L.wout, d, 0)));
   return AIDEEN_OK;
 }
 
@@ -444,7 +523,7 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   A(&b.Rsrc, N * h); A(&b.dRc, N * h); A(&b.iters, N * h);
   A(&b.hstar, Nhd); A(&b.pre, Nhd); A(&b.hist, Nhd); A(&b.fpmctx, Nhd);
   A(&b.v, Nhd); A(&b.gpre, Nhd); A(&b.dsig, Nhd); A(&b.da, Nhd);
-  A(&b.mstate, (size_t)cfg->max_batch * h * d);
+  A(&b.mstate, (size_t)cfg->max_batch * h * d); A(&b.fcarry, (size_t)cfg->max_batch * h * d);
   A(&b.pooled, N * d); A(&b.dl_dh, N * d); A(&b.nsg, N * d); A(&b.dS, N * d);
   A(&b.y, N * d); A(&b.dy, N * d); A(&b.ggp, N * d); A(&b.lrms, N); A(&b.loss_rows, N);
   A(&b.scal, 4); A(&b.stage, ctx->Lx.total);
@@ -461,6 +540,7 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
     return fail(AIDEEN_E_CUDA);
   }
   cudaMemsetAsync(b.mstate, 0, (size_t)cfg->max_batch * h * d * sizeof(float), ctx->stream);
+  cudaMemsetAsync(b.fcarry, 0, (size_t)cfg->max_batch * h * d * sizeof(float), ctx->stream);
   cudaMemsetAsync(b.W, 0, ctx->W_len * sizeof(float), ctx->stream);
   cudaMemsetAsync(b.G, 0, ctx->W_len * sizeof(float), ctx->stream);
   cudaMemsetAsync(b.M1, 0, ctx->W_len * sizeof(float), ctx->stream);
@@ -490,7 +570,9 @@ void aideen_destroy(aideen_ctx *ctx) {
                   b.pooled, b.hist, b.fpmctx, b.mstate, b.iters, b.v, b.gpre, b.dl_dh, b.rhs_slot,
                   b.nsg, b.da, b.dn, b.dQ, b.dK, b.dV, b.dsig, b.dRc, b.dS, b.lmp, b.Glm, b.Mlm1,
                   b.Mlm2, b.y, b.lrms, b.logits, b.dy, b.ggp, b.loss_rows, b.scal, b.emb, b.stats,
-                  b.sigmas, b.stage, b.ws};
+                  b.sigmas, b.stage, b.ws, b.fc, b.frp, b.fdl, b.falpha, b.fcpre, b.fcbd,
+                  b.fcalog, b.fcgz, b.fcwx, b.fminner, b.fdm, b.fgpre, b.fup, b.fkw, b.fdup, b.frz,
+                  b.fgraw, b.fcarry, b.fpart};
   for (void *p : ptrs)
     if (p) cudaFree(p);
   if (ctx->stream && ctx->own_stream) cudaStreamDestroy(ctx->stream);
@@ -620,6 +702,9 @@ int aideen_upload_embedding(aideen_ctx *ctx, const float *emb) {
 int aideen_reset_state(aideen_ctx *ctx) {
   if (!ctx) return AIDEEN_E_INVALID;
   CU(cudaMemsetAsync(ctx->b.mstate, 0,
+                     (size_t)ctx->cfg.max_batch * ctx->cfg.h_slots * ctx->cfg.d_model * 4, ctx->stream));
+  // the TBPTT carry of the FPM backward is cleared with the memory (gpu_deq.rs:3147)
+  CU(cudaMemsetAsync(ctx->b.fcarry, 0,
                      (size_t)ctx->cfg.max_batch * ctx->cfg.h_slots * ctx->cfg.d_model * 4, ctx->stream));
   return AIDEEN_OK;
 }
@@ -794,6 +879,8 @@ static void *buf_ptr(aideen_ctx *ctx, int which, size_t *count) {
     case AIDEEN_BUF_DS_IN: *count = N * d; return b.dS;
     case AIDEEN_BUF_LM_GRADS: *count = ctx->lm_len ? ctx->lm_b + ctx->cfg.vocab + d : 0; return b.Glm;
     case AIDEEN_BUF_PRE: *count = N * h * d; return b.pre;
+    case AIDEEN_BUF_FPM_DM: *count = b.fdm ? N * h * d : 0; return b.fdm;
+    case AIDEEN_BUF_FPM_CARRY: *count = (size_t)ctx->cfg.max_batch * h * d; return b.fcarry;
     default: *count = 0; return nullptr;
   }
 }

@@ -111,4 +111,23 @@ cudaError_t launch_rmsnorm_bwd(const float *dy, const float *P, const float *lrm
                                cudaStream_t st);
 cudaError_t launch_sum(const float *x, int n, float *out, cudaStream_t st);
 
+// FPM memory backward (fpm_bwd.cu).  Row-major [N][h][d] buffers, N = B*T
+// tokens ordered (b, t); v is the adjoint solution [h][N][d].
+struct FpmBwdArgs {
+  int B, T, h, d;
+  const float *W;
+  size_t off_bdelta, off_bret, off_wgate, off_bwrite, off_alog, off_wx;
+  const float *hstar, *hist, *c, *rpre, *dpre, *v;
+  float *alpha, *cpre, *cbd, *calog, *cgz, *cwx, *minner;  // per-element coefficients
+  float *rz, *graw;     // [N][h]
+  float *dm, *gpre;     // scan outputs
+  float *carry;         // [B][h][d] TBPTT carry, in: dL/dM seed, out: dL/dM before the chunk
+  float *part;          // [4][B][h][d] per-sequence partial sums
+};
+cudaError_t launch_fpm_c(const float *hstar, const float *signal, float *c, size_t n, cudaStream_t st);
+cudaError_t launch_fpm_coef(const FpmBwdArgs &a, cudaStream_t st);
+cudaError_t launch_fpm_scan(const FpmBwdArgs &a, cudaStream_t st);
+cudaError_t launch_fpm_gate(const FpmBwdArgs &a, cudaStream_t st);
+cudaError_t launch_fpm_finalize(const FpmBwdArgs &a, float *G, cudaStream_t st);
+
 }  // namespace aideen

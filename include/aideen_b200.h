@@ -121,9 +121,9 @@ uint64_t aideen_launch_count(const aideen_ctx *ctx);
  * milliseconds and launch counts per class. */
 enum { AIDEEN_PROF_PICARD = 0, AIDEEN_PROF_ADJOINT = 1, AIDEEN_PROF_GEMM = 2,
        AIDEEN_PROF_LM_SOFTMAX = 3, AIDEEN_PROF_OPTIMIZER = 4, AIDEEN_PROF_OTHER = 5,
-       AIDEEN_PROF_CLASSES = 6 };
+       AIDEEN_PROF_FPM_BWD = 6, AIDEEN_PROF_CLASSES = 7 };
 int aideen_profile(aideen_ctx *ctx, int enable);
-int aideen_profile_read(aideen_ctx *ctx, float *ms /*[6]*/, uint64_t *launches /*[6], nullable*/,
+int aideen_profile_read(aideen_ctx *ctx, float *ms /*[AIDEEN_PROF_CLASSES]*/, uint64_t *launches /*[AIDEEN_PROF_CLASSES], nullable*/,
                         int reset);
 
 /* Length of AllWeights for (d, h) (deq_bridge.rs:103-137). */
@@ -214,7 +214,9 @@ enum aideen_buf {
   AIDEEN_BUF_S_IN = 12,     /* [N][d] */
   AIDEEN_BUF_DS_IN = 13,    /* [N][d] exact dL/dS_in */
   AIDEEN_BUF_LM_GRADS = 14, /* [vocab*d + vocab + d] */
-  AIDEEN_BUF_PRE = 15       /* [N][h][d] pre = branch + h* of the adjoint */
+  AIDEEN_BUF_PRE = 15,      /* [N][h][d] pre = branch + h* of the adjoint */
+  AIDEEN_BUF_FPM_DM = 16,   /* [N][h][d] dL/dM[t] of the last FPM backward (fpm_dm_buf) */
+  AIDEEN_BUF_FPM_CARRY = 17 /* [max_batch][h][d] FPM TBPTT carry (tbptt_carry_buf) */
 };
 /* Copies the first n_elems elements (4 bytes each) of a buffer to host dst. */
 int aideen_read(aideen_ctx *ctx, int which, void *dst, size_t n_elems);

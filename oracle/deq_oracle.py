@@ -19,6 +19,8 @@ It restates, in float64 numpy, the reference's live GPU semantics:
 * Adam                       `aideen-training-lab/src/optimizer.rs:105-183`
 * clipped SGD apply          `aideen-backbone/src/shaders/fused_deq_update.wgsl:809-823`
 * spectral renorm            `aideen-block/src/shaders/spectral_renorm.wgsl:83-196`
+* FPM backward (TBPTT scan)  `aideen-backbone/src/shaders/fused_fpm_retain_bwd.wgsl:364-2095`
+* FPM W_out / W_x grads      `aideen-backbone/src/shaders/fused_fpm_shared_update.wgsl:129-256`
 
 Weight gradients are derived analytically (implicit-function theorem through
 the map the clean adjoint linearises); the reference's own stage-4 shaders
@@ -538,6 +540,117 @@ def weight_grads(S_flat, signal, A, cache, v, g_pre, pre, r_pre, W, cfg: Cfg):
 
 
 # ---------------------------------------------------------------------------
+# FPM memory backward (reverse scan over the write recurrence)
+# ---------------------------------------------------------------------------
+
+FPM_READ_GRAD_SCALE = 0.5
+
+
+def fpm_backward(hstar, signal, hist, v, W, d, h, carry=None):
+    """Reverse-time backward of the FPM memory write, as the reference computes it
+    (`aideen-backbone/src/shaders/fused_fpm_retain_bwd.wgsl:364-2095`), followed
+    by the shared W_out / diag W_x gradients (`fused_fpm_shared_update.wgsl:
+    129-158, 225-256`, the entry points bound at `gpu_deq.rs:1811,1820`).
+
+    hstar, signal, hist: [B,T,h,d] (hist[t] = memory after the write of token t);
+    v: adjoint solution [B*T,h,d]; carry: dL/dM seed [B,h,d] from the following
+    chunk (TBPTT carry, zero after a state reset).
+
+    The reference's formulas are kept as they are, including where they are not
+    the exact derivative of `fpm_write`: x_proj is rebuilt as
+    h_unit + wx*h_unit + write (no sqrt(z) factor) for m_inner and the a_log term,
+    the novelty gradient is applied per dimension, W_x's carrier gradient omits
+    the (1 - retain) factor, the read path contributes 0.5 * v[t] to dL/dM[t-1],
+    and m_prev is zero at t = 0 of the chunk.  The associative branch (off) and
+    the W_k_write / W_v_write updates (compiled out: ENABLE_FPM_WRITE_BWD = false,
+    FPM_DIRECT_WRITE_SCALE = 0) contribute nothing.
+
+    Gradients are returned as raw sums over all sequences and tokens, in the
+    AllWeights layout; the reference's per-family divisors (B*T for the slot
+    parameters, B*T*h for W_out and W_x) are learning-rate factors left to the
+    update's grad_scale.  Returns dict(G, carry, dm, minner, hunit, gx).
+    """
+    V = View(W, d, h)
+    L = V.L
+    hstar = np.asarray(hstar, np.float64)
+    signal = np.asarray(signal, np.float64)
+    hist = np.asarray(hist, np.float64)
+    B, T = hstar.shape[:2]
+    v = np.asarray(v, np.float64).reshape(B, T, h, d)
+    v = np.where(np.isfinite(v), v, 0.0)
+    g = np.zeros((B, h, d)) if carry is None else np.asarray(carry, np.float64).copy()
+    inv_sqrt_d = 1.0 / math.sqrt(max(1, d))
+    wx = 0.5 * np.tanh(np.diag(V.Wx))[None, None, :]
+    a = 1.0 / (1.0 + np.exp(V.Alog))[None]                      # [1,h,d]
+    gWup = np.zeros((h, d, RANK)); gWdown = np.zeros((h, RANK, d))
+    gbret = np.zeros((h, d)); gbd = np.zeros((h, d)); gwf = np.zeros((h, d))
+    gbw = np.zeros(h); galog = np.zeros((h, d))
+    dm_all = np.zeros((B, T, h, d)); minner_all = np.zeros_like(dm_all)
+    hunit_all = np.zeros_like(dm_all); gx_all = np.zeros_like(dm_all)
+    for t in range(T - 1, -1, -1):
+        c = 0.5 * (hstar[:, t] + signal[:, t])
+        m_prev = hist[:, t - 1] if t > 0 else np.zeros((B, h, d))
+        up = es('bsj,sjr->bsr', c, V.Wup)
+        retain = 1.0 / (1.0 + np.exp(-(V.bret[None] + es('bsr,srd->bsd', up, V.Wdown))))
+        kw = es('bsj,sjr->bsr', c, V.Wkw)
+        prop = np.tanh(V.bdelta[None] + es('bsr,srd->bsd', kw, V.Wvw))
+        raw_z = 1.0 / (1.0 + np.exp(-((c * V.wgate[None]).sum(-1) * inv_sqrt_d + V.bwrite[None] + FPM_GATE_BIAS)))
+        prev_norm = np.sqrt(np.maximum((m_prev * m_prev).sum(-1), 1e-6))
+        diff = prop - m_prev
+        diff_norm = np.sqrt(np.maximum((diff * diff).sum(-1), 1e-6))
+        denom = diff_norm + prev_norm + 1e-6
+        nov = (diff_norm / denom)[..., None]
+        z = np.clip(raw_z, 0.0, 1.0)[..., None]
+        dnov_ddiff = (prev_norm / denom ** 2)[..., None]
+        dnov_dprev = (-diff_norm / denom ** 2)[..., None]
+        h_rms = np.sqrt(np.maximum((hstar[:, t] ** 2).sum(-1) / max(1, d), 1e-6))
+        hu = hstar[:, t] / h_rms[..., None]
+        ret_eff = 1.0 - nov * (1.0 - retain)
+        x_proj = hu + wx * hu + z * FPM_RESIDUAL_SCALE * prop
+        base = a * m_prev + (1.0 - a) * x_proj
+        m_inner = ret_eff * m_prev + (1.0 - ret_eff) * base
+        g_x = (1.0 - a) * (1.0 - ret_eff) * g
+        g_prev = ret_eff * g + (1.0 - ret_eff) * a * g
+        q = nov * retain * (1.0 - retain)
+        g_pre = (m_prev - base) * g * q
+        g_z = (g_x * (FPM_RESIDUAL_SCALE * prop + 0.5 * hu / np.sqrt(np.maximum(z, 1e-6)))).sum(-1)
+        g_raw_z = g_z * raw_z * (1.0 - raw_z)
+        dm_all[:, t], minner_all[:, t], hunit_all[:, t] = g, m_inner, hu
+        gx_all[:, t] = (1.0 - a) * g
+        g_re = g_pre / np.maximum(q, 1e-6)
+        g_nov = -g_re * (1.0 - retain)
+        g_dn = g_nov * dnov_ddiff
+        g_pn = g_nov * dnov_dprev
+        unit_diff = diff / np.maximum(diff_norm, 1e-6)[..., None]
+        g_prop = g_x * z * FPM_RESIDUAL_SCALE + g_dn * unit_diff
+        g_prev = g_prev + g_pn * m_prev / np.maximum(prev_norm, 1e-6)[..., None] - g_dn * unit_diff
+        g_a = (1.0 - ret_eff) * (m_prev - x_proj) * g
+        galog += (-a * (1.0 - a) * g_a).sum(0)
+        gbd += (g_prop * (1.0 - prop * prop)).sum(0)
+        gbret += g_pre.sum(0)
+        dup = es('bsd,srd->bsr', g_pre, V.Wdown)
+        gWdown += es('bsr,bsd->srd', up, g_pre)
+        gWup += es('bsd,bsr->sdr', c, dup)
+        gwf += (g_raw_z[..., None] * c).sum(0) * inv_sqrt_d
+        gbw += g_raw_z.sum(0)
+        g = g_prev + FPM_READ_GRAD_SCALE * v[:, t]
+    G = np.zeros(L.total)
+    G[L.w_retain_up:L.w_retain_up + h * d * RANK] = gWup.ravel()
+    G[L.w_retain_down:L.w_retain_down + h * RANK * d] = gWdown.ravel()
+    G[L.b_retain:L.b_retain + h * d] = gbret.ravel()
+    G[L.b_delta:L.b_delta + h * d] = gbd.ravel()
+    G[L.w_write_gate:L.w_write_gate + h * d] = gwf.ravel()
+    G[L.b_write_mem:L.b_write_mem + h] = gbw
+    G[L.alog:L.alog + h * d] = galog.ravel()
+    gwout = es('btsr,btsc->rc', dm_all, minner_all)
+    G[L.wout:L.wout + d * d] = gwout.ravel()
+    wraw = np.diag(V.Wx)
+    gwx = (gx_all * hunit_all).sum((0, 1, 2)) * 0.5 * (1.0 - np.tanh(wraw) ** 2)
+    G[L.wx + np.arange(d) * (d + 1)] = gwx
+    return dict(G=G, carry=g, dm=dm_all, minner=minner_all, hunit=hunit_all, gx=gx_all)
+
+
+# ---------------------------------------------------------------------------
 # optimizers and spectral renorm
 # ---------------------------------------------------------------------------
 
@@ -607,7 +720,7 @@ def branch_of(fwd: ForwardOut, W, cfg: Cfg):
 
 
 def train_step(S_in, targets, W, lm, cfg: Cfg, adam_state=None, step=1, lr=1e-3,
-               mstate=None):
+               mstate=None, fpm_carry=None):
     """Forward -> LM-head CE -> adjoint -> weight grads -> Adam (DEQ core and LM head).
 
     Returns a dict with every intermediate the GPU path is compared on.
@@ -625,6 +738,10 @@ def train_step(S_in, targets, W, lm, cfg: Cfg, adam_state=None, step=1, lr=1e-3,
     G, dS = weight_grads(np.asarray(S_in, np.float64).reshape(N, d),
                          fwd.signal.reshape(N, h, d), fwd.A.reshape(N, h, d), fwd.attn_cache,
                          v, g_pre, pre, r_pre, W, cfg)
+    fpm_out = None
+    if cfg.fpm:
+        fpm_out = fpm_backward(fwd.hstar, fwd.signal, fwd.hist_ctx, v, W, d, h, carry=fpm_carry)
+        G = G + fpm_out["G"]
     if adam_state is None:
         adam_state = (np.zeros_like(G), np.zeros_like(G))
     Wn, m1, m2 = adam(W, G, adam_state[0], adam_state[1], step, lr=lr)
@@ -632,4 +749,4 @@ def train_step(S_in, targets, W, lm, cfg: Cfg, adam_state=None, step=1, lr=1e-3,
     lm_g = np.concatenate([gW_lm.ravel(), gb_lm, gg_lm])
     lm_new, _, _ = adam(lm_flat, lm_g, np.zeros_like(lm_g), np.zeros_like(lm_g), step, lr=lr)
     return dict(fwd=fwd, loss=loss, dP=dP, v=v, g_pre=g_pre, grads=G, dS=dS, W_new=Wn,
-                adam=(m1, m2), lm_grads=lm_g, lm_new=lm_new)
+                adam=(m1, m2), lm_grads=lm_g, lm_new=lm_new, fpm=fpm_out)

@@ -145,6 +145,12 @@ def test_full_step_gradients_and_update(c):
     blocks = dict(wq=(L.wq, L.q_bias), qb=(L.q_bias, L.wk), wk=(L.wk, L.k_bias), kb=(L.k_bias, L.wv),
                   wv=(L.wv, L.wo), wo=(L.wo, L.win), win=(L.win, L.wx), ns=(L.nscale, L.hist),
                   anchor=(L.slot_anchor, L.w_k_write))
+    if c["fpm"]:
+        blocks.update(wup=(L.w_retain_up, L.w_retain_down), wdown=(L.w_retain_down, L.b_retain),
+                      bret=(L.b_retain, L.w_q_mem), bdelta=(L.b_delta, L.flags),
+                      wgate=(L.w_write_gate, L.b_write_mem), bwrite=(L.b_write_mem, L.hhist_gamma),
+                      alog=(L.alog, L.nscale), wout=(L.wout, L.alog), wx=(L.wx, L.wout))
+        assert np.abs(G[L.w_retain_down:L.b_retain]).max() > 0 and np.abs(G[L.b_retain:L.w_q_mem]).max() > 0
     for name, (a, b) in blocks.items():
         assert rel(Gg[a:b], G[a:b]) < TOL, name
     assert rel(be.read("ds_in", (N, d)), r["dS"]) < TOL
@@ -214,4 +220,46 @@ def test_rejects_sizes_beyond_caps():
         be.run_forward_deq_no_readback(np.zeros((1, 8, 128), np.float32), 1, 8, RunConfig())
     with pytest.raises(AideenError):
         be.upload_weights(np.zeros(10, np.float32))
+    be.close()
+
+
+def _fpm_chunk(be, W, lm, emb, tok, tg, rc, cfg, carry, mstate):
+    B, T = tok.shape
+    d, h = cfg.d, cfg.h
+    be.run_forward_tokens(tok, B, T, rc)
+    be.lm_head_loss(tg)
+    be.run_staged_adjoint_picard_no_readback(0.85, 12)
+    be.weight_grads()
+    r = O.train_step(emb[tok], tg, W, lm, cfg, mstate=mstate, fpm_carry=carry)
+    return r
+
+
+def test_fpm_backward_tbptt_carry_across_chunks():
+    """Two consecutive chunks of the same sequences: the FPM memory and the
+    TBPTT carry both flow into the second chunk's gradients; reset_state clears both."""
+    d, h, B, T, V = 128, 4, 2, 8, 61
+    c = dict(d=d, h=h, B=B, T=T, fpm=True)
+    W, be, S, rc, cfg = _setup(c, vocab=V)
+    cfg.adj_iters = 12
+    lm, emb = init_lm_head(d, V), init_embedding(d, V)
+    be.upload_lm_head(*lm)
+    be.upload_embedding(emb)
+    rng = np.random.default_rng(21)
+    toks = [rng.integers(0, V, (B, T)).astype(np.int32) for _ in range(2)]
+    tgs = [rng.integers(0, V, (B, T)).astype(np.int32) for _ in range(2)]
+    r1 = _fpm_chunk(be, W, lm, emb, toks[0], tgs[0], rc, cfg, None, None)
+    N = B * T
+    assert rel(be.read("fpm_dm", (B, T, h, d)), r1["fpm"]["dm"]) < TOL
+    assert rel(be.read("fpm_carry", (B, h, d)), r1["fpm"]["carry"]) < TOL
+    r2 = _fpm_chunk(be, W, lm, emb, toks[1], tgs[1], rc, cfg, r1["fpm"]["carry"], r1["fwd"].mstate)
+    L = O.Offsets(d, h)
+    Gg = be.read_grads()
+    G = r2["grads"]
+    for name, (a, b) in dict(wup=(L.w_retain_up, L.w_retain_down), wdown=(L.w_retain_down, L.b_retain),
+                             bret=(L.b_retain, L.w_q_mem), alog=(L.alog, L.nscale),
+                             wout=(L.wout, L.alog), wgate=(L.w_write_gate, L.b_write_mem)).items():
+        assert rel(Gg[a:b], G[a:b]) < TOL, name
+    assert rel(be.read("fpm_carry", (B, h, d)), r2["fpm"]["carry"]) < TOL
+    be.reset_state()
+    assert np.abs(be.read("fpm_carry", (B, h, d))).max() == 0.0
     be.close()

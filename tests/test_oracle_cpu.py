@@ -276,3 +276,96 @@ def test_clipped_sgd_clamps_and_decays():
     w = np.array([1.0, 1.0, 1.0]); g = np.array([1e4, -1.0, 1.0])
     out = O.clipped_sgd(w, g, lr=0.1, wd=0.5, main_len=2)
     assert np.allclose(out, [0.95 - 0.5, 0.95 + 0.1, 1.0 - 0.1])
+
+
+# ---------------------------------------------------------------------------
+# FPM backward restatement
+# ---------------------------------------------------------------------------
+
+def _fpm_case(d=16, h=2, B=2, seed=3, bwrite=None):
+    W = init_all_weights(d, h, seed=seed).astype(np.float64)
+    L = O.Offsets(d, h)
+    rng = np.random.default_rng(seed)
+    # non-trivial FPM parameters so every term of the backward is exercised
+    for off, n, s in ((L.w_retain_up, h * d * O.RANK, 0.2), (L.w_retain_down, h * O.RANK * d, 0.2),
+                      (L.b_retain, h * d, 0.5), (L.w_write_gate, h * d, 0.5), (L.b_delta, h * d, 0.3),
+                      (L.w_k_write, h * d * O.RANK, 0.2), (L.w_v_write, h * O.RANK * d, 0.2),
+                      (L.alog, h * d, 0.5)):
+        W[off:off + n] = rng.standard_normal(n) * s
+    W[L.wx + np.arange(d) * (d + 1)] = rng.standard_normal(d) * 0.5
+    W[L.b_write_mem:L.b_write_mem + h] = rng.standard_normal(h) if bwrite is None else bwrite
+    hs = rng.standard_normal((B, 1, h, d))
+    sig = rng.standard_normal((B, 1, h, d))
+    g = rng.standard_normal((B, h, d))
+    return W, hs, sig, g
+
+
+def _write_functional(W, hs, sig, g, d, h):
+    V = O.View(W, d, h)
+    m = O.fpm_write(hs[:, 0], sig[:, 0], np.zeros_like(g), V, np.diag(V.Wx))
+    return float((g * m).sum())
+
+
+def _fd(W, idx, f, eps=1e-6):
+    Wp, Wm = W.copy(), W.copy()
+    Wp[idx] += eps
+    Wm[idx] -= eps
+    return (f(Wp) - f(Wm)) / (2 * eps)
+
+
+@pytest.mark.parametrize("name", ["b_write_mem", "w_write_gate"])
+def test_fpm_backward_gate_terms_are_exact_derivatives(name):
+    """The write-gate terms of the reference FPM backward are the exact derivative
+    of the forward write at any gate value: checked by central differences on
+    <g, m_t> for a one-token chunk seeded with dL/dM_t = g."""
+    d, h = 16, 2
+    W, hs, sig, g = _fpm_case(d, h)
+    out = O.fpm_backward(hs, sig, np.zeros_like(hs), np.zeros((2, h, d)), W, d, h, carry=g)
+    f = lambda w: _write_functional(w, hs, sig, g, d, h)
+    L = O.Offsets(d, h)
+    off = getattr(L, name)
+    idx = list(range(off, off + (h if name == "b_write_mem" else 5)))
+    for i in idx:
+        fd = _fd(W, i, f)
+        assert abs(out["G"][i] - fd) <= 1e-6 * max(1.0, abs(fd)), (name, i, out["G"][i], fd)
+
+
+@pytest.mark.parametrize("name", ["b_retain", "w_retain_up", "w_retain_down", "alog"])
+def test_fpm_backward_retain_terms_exact_when_gate_saturates(name):
+    """With the write gate saturated (z = 1) the reference's rebuilt x_proj equals
+    the forward's, and its retain-gate and decay gradients are exact derivatives."""
+    d, h = 16, 2
+    W, hs, sig, g = _fpm_case(d, h, bwrite=60.0)
+    out = O.fpm_backward(hs, sig, np.zeros_like(hs), np.zeros((2, h, d)), W, d, h, carry=g)
+    f = lambda w: _write_functional(w, hs, sig, g, d, h)
+    L = O.Offsets(d, h)
+    off = getattr(L, name)
+    rng = np.random.default_rng(0)
+    n = {"b_retain": h * d, "w_retain_up": h * d * O.RANK, "w_retain_down": h * O.RANK * d, "alog": h * d}[name]
+    for i in off + rng.choice(n, 8, replace=False):
+        fd = _fd(W, i, f)
+        assert abs(out["G"][i] - fd) <= 1e-6 * max(1.0, abs(fd)), (name, i, out["G"][i], fd)
+
+
+def test_fpm_backward_carry_and_read_seed():
+    """dL/dM flows backward through the chunk: with zero weights on the write path
+    the carry out is the read-path seed 0.5*v[0] plus the propagated carry."""
+    d, h, B, T = 16, 2, 1, 3
+    W, _, _, _ = _fpm_case(d, h, B=B)
+    rng = np.random.default_rng(9)
+    hs = rng.standard_normal((B, T, h, d))
+    sig = rng.standard_normal((B, T, h, d))
+    hist = rng.standard_normal((B, T, h, d)) * 0.3
+    v = rng.standard_normal((B * T, h, d))
+    out0 = O.fpm_backward(hs, sig, hist, v, W, d, h)
+    # linear in (carry, v): doubling both doubles every gradient and the carry
+    c = rng.standard_normal((B, h, d))
+    o1 = O.fpm_backward(hs, sig, hist, v, W, d, h, carry=c)
+    o2 = O.fpm_backward(hs, sig, hist, 2 * v, W, d, h, carry=2 * c)
+    np.testing.assert_allclose(o2["G"], 2 * o1["G"], rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(o2["carry"], 2 * o1["carry"], rtol=1e-10, atol=1e-12)
+    # the last token is seeded by the carry, earlier ones by 0.5*v of the next token
+    np.testing.assert_allclose(o1["dm"][:, T - 1], c)
+    assert np.abs(out0["dm"][:, T - 1]).max() == 0.0
+    assert np.abs(out0["dm"][:, T - 2]).max() > 0.0
+    assert np.all(np.isfinite(o1["G"]))
