@@ -443,6 +443,22 @@ cudaError_t launch_add(float *dst, const float *a, const float *b, size_t n, cud
   return cudaGetLastError();
 }
 
+// dst[r][c] = x[r][c] + bias[c] over rows of `len` floats (len % 4 == 0).
+__global__ void add_rowbias_kernel(float *__restrict__ dst, const float *__restrict__ x,
+                                   const float *__restrict__ bias, size_t n4, size_t len4) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+       i += (size_t)gridDim.x * blockDim.x)
+    st4(dst + 4 * i, ld4(x + 4 * i) + ld4(bias + 4 * (i % len4)));
+}
+
+cudaError_t launch_add_rowbias(float *dst, const float *x, const float *bias, size_t rows, size_t len,
+                               cudaStream_t st) {
+  const size_t n4 = rows * len / 4;
+  if (n4 == 0) return cudaSuccess;
+  add_rowbias_kernel<<<grid_for(n4), 256, 0, st>>>(dst, x, bias, n4, len / 4);
+  return cudaGetLastError();
+}
+
 __global__ void colsum_kernel(const float *__restrict__ X, int rows, int ncols, long ld,
                               float *__restrict__ out, int seg, long ostride, int accumulate) {
   __shared__ float red[32][33];

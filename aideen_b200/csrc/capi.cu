@@ -29,6 +29,7 @@ struct DevBufs {
   float *S_in = nullptr;
   int32_t *tokens = nullptr, *targets = nullptr;
   float *signal = nullptr, *A = nullptr, *amat = nullptr;
+  float *src = nullptr;  // [N][h][d] signal + slot anchor (attention source rows)
   float *Qh = nullptr, *Kh = nullptr, *Vh = nullptr, *alpha = nullptr, *nmix = nullptr,
         *rmix = nullptr, *scale = nullptr, *rho = nullptr, *Rsrc = nullptr;
   float *hstar = nullptr, *pre = nullptr, *pooled = nullptr, *hist = nullptr, *fpmctx = nullptr,
@@ -46,13 +47,12 @@ struct DevBufs {
   float *stage = nullptr;  // packed AllWeights staging for upload/download
   float *ws = nullptr;     // split-K partial sums of the tensor-core GEMM
   // FPM backward (allocated on first use): [N][h][d] unless noted
-  float *fc = nullptr, *frp = nullptr, *fdl = nullptr, *falpha = nullptr, *fcpre = nullptr,
-        *fcbd = nullptr, *fcalog = nullptr, *fcgz = nullptr, *fcwx = nullptr, *fminner = nullptr,
-        *fdm = nullptr, *fgpre = nullptr;
+  float *fc = nullptr, *frp = nullptr, *fdl = nullptr, *fminner = nullptr, *fdm = nullptr,
+        *fgpre = nullptr;
   float *fup = nullptr, *fkw = nullptr, *fdup = nullptr;  // [N][h][32]
-  float *frz = nullptr, *fgraw = nullptr;                 // [N][h]
+  float *fA = nullptr, *fU = nullptr, *fgin = nullptr;    // [max_batch][h][nch][d]
   float *fcarry = nullptr;                                // [max_batch][h][d] TBPTT carry
-  float *fpart = nullptr;                                 // [4][max_batch][h][d]
+  float *fpart = nullptr, *fpart_bw = nullptr;            // [5][max_batch*nch][h][d], [max_batch*nch][h]
 };
 
 }  // namespace
@@ -194,13 +194,14 @@ int run_forward(aideen_ctx *ctx, const aideen_run *r, aideen_stats *stats) {
                      (long)h * d, d, ctx->signal_scale)));
   }
   if (r->slot_coord) {
-    // 32-wide K/V/Q heads of src = signal + anchor (:281-355)
-    KL(gemm_any(ctx, gemm(N, kHeadDim, d, h, b.signal, (long)h * d, d, false, W + L.wk, d, (long)d * d,
-                     false, b.Kh, (long)h * kHeadDim, kHeadDim, 1.f, 0.f, W + L.slot_anchor, d)));
-    KL(gemm_any(ctx, gemm(N, kHeadDim, d, h, b.signal, (long)h * d, d, false, W + L.wv, d, (long)d * d,
-                     false, b.Vh, (long)h * kHeadDim, kHeadDim, 1.f, 0.f, W + L.slot_anchor, d)));
-    KL(gemm_any(ctx, gemm(N, kHeadDim, d, h, b.signal, (long)h * d, d, false, W + L.wq, d, (long)d * d,
-                     false, b.Qh, (long)h * kHeadDim, kHeadDim, 1.f, 0.f, W + L.slot_anchor, d)));
+    // 32-wide K/V/Q heads of src = signal + anchor (:281-355); src is kept for the backward
+    KL(launch_add_rowbias(b.src, b.signal, W + L.slot_anchor, N, (size_t)h * d, st));
+    KL(gemm_any(ctx, gemm(N, kHeadDim, d, h, b.src, (long)h * d, d, false, W + L.wk, d, (long)d * d,
+                     false, b.Kh, (long)h * kHeadDim, kHeadDim)));
+    KL(gemm_any(ctx, gemm(N, kHeadDim, d, h, b.src, (long)h * d, d, false, W + L.wv, d, (long)d * d,
+                     false, b.Vh, (long)h * kHeadDim, kHeadDim)));
+    KL(gemm_any(ctx, gemm(N, kHeadDim, d, h, b.src, (long)h * d, d, false, W + L.wq, d, (long)d * d,
+                     false, b.Qh, (long)h * kHeadDim, kHeadDim)));
     AttnArgs a{};
     a.h = h; a.d = d; a.W = W; a.off_qb = L.q_bias; a.off_kb = L.k_bias; a.off_anchor = L.slot_anchor;
     a.Qh = b.Qh; a.Kh = b.Kh; a.Vh = b.Vh; a.alpha = b.alpha; a.nmix = b.nmix; a.rmix = b.rmix;
@@ -321,8 +322,8 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
     const float *dqkv[3] = {b.dQ, b.dK, b.dV};
     const size_t woff[3] = {L.wq, L.wk, L.wv};
     for (int i = 0; i < 3; ++i)
-      KL(gemm_any(ctx, gemm(d, kHeadDim, N, h, b.signal, (long)h * d, d, true, dqkv[i], H32, kHeadDim,
-                       false, G + woff[i], d, (long)d * d, 1.f, 0.f, W + L.slot_anchor, d)));
+      KL(gemm_any(ctx, gemm(d, kHeadDim, N, h, b.src, (long)h * d, d, true, dqkv[i], H32, kHeadDim,
+                       false, G + woff[i], d, (long)d * d)));
     KL(launch_dsig_init(a, b.dsig, N * h, 1, st));
     // dsrc[n][s][j] += sum_c d{Q,K,V}[n][s][c] W[s][j*d + c]
     for (int i = 0; i < 3; ++i)
@@ -360,14 +361,16 @@ int run_fpm_backward(aideen_ctx *ctx) {
   DevBufs &b = ctx->b;
   cudaStream_t st = ctx->stream;
   const size_t Nhd = ctx->max_tokens * h * d, NH32 = ctx->max_tokens * h * kRank;
+  const int CH = fpm_chunk_len(d);
+  const size_t nch_max = (ctx->cfg.max_seq_len + CH - 1) / CH;
+  const size_t chunk_rows = (size_t)ctx->cfg.max_batch * nch_max;
   if (!b.fc) {
     cudaError_t e = cudaSuccess;
     auto A = [&](float **p, size_t n) { if (e == cudaSuccess) e = dalloc(p, n); };
-    A(&b.fc, Nhd); A(&b.frp, Nhd); A(&b.fdl, Nhd); A(&b.falpha, Nhd); A(&b.fcpre, Nhd);
-    A(&b.fcbd, Nhd); A(&b.fcalog, Nhd); A(&b.fcgz, Nhd); A(&b.fcwx, Nhd); A(&b.fminner, Nhd);
-    A(&b.fdm, Nhd); A(&b.fgpre, Nhd); A(&b.fup, NH32); A(&b.fkw, NH32); A(&b.fdup, NH32);
-    A(&b.frz, ctx->max_tokens * h); A(&b.fgraw, ctx->max_tokens * h);
-    A(&b.fpart, 4 * (size_t)ctx->cfg.max_batch * h * d);
+    A(&b.fc, Nhd); A(&b.frp, Nhd); A(&b.fdl, Nhd); A(&b.fminner, Nhd); A(&b.fdm, Nhd); A(&b.fgpre, Nhd);
+    A(&b.fup, NH32); A(&b.fkw, NH32); A(&b.fdup, NH32);
+    A(&b.fA, chunk_rows * h * d); A(&b.fU, chunk_rows * h * d); A(&b.fgin, chunk_rows * h * d);
+    A(&b.fpart, 5 * chunk_rows * h * d); A(&b.fpart_bw, chunk_rows * h);
     CU(e);
   }
   const float *W = b.W;
@@ -375,13 +378,12 @@ int run_fpm_backward(aideen_ctx *ctx) {
   const int R = kRank, HR = h * kRank;
   const long hd = (long)h * d;
   FpmBwdArgs a{};
-  a.B = B; a.T = T; a.h = h; a.d = d; a.W = W;
+  a.B = B; a.T = T; a.h = h; a.d = d; a.nch = (T + CH - 1) / CH; a.W = W;
   a.off_bdelta = L.b_delta; a.off_bret = L.b_retain; a.off_wgate = L.w_write_gate;
   a.off_bwrite = L.b_write_mem; a.off_alog = L.alog; a.off_wx = L.wx;
   a.hstar = b.hstar; a.hist = b.hist; a.c = b.fc; a.rpre = b.frp; a.dpre = b.fdl; a.v = b.v;
-  a.alpha = b.falpha; a.cpre = b.fcpre; a.cbd = b.fcbd; a.calog = b.fcalog; a.cgz = b.fcgz;
-  a.cwx = b.fcwx; a.minner = b.fminner; a.rz = b.frz; a.graw = b.fgraw; a.dm = b.fdm;
-  a.gpre = b.fgpre; a.carry = b.fcarry; a.part = b.fpart;
+  a.minner = b.fminner; a.cA = b.fA; a.cU = b.fU; a.gin = b.fgin; a.dm = b.fdm; a.gpre = b.fgpre;
+  a.carry = b.fcarry; a.part = b.fpart; a.part_bw = b.fpart_bw;
   ctx->prof_phase = AIDEEN_PROF_FPM_BWD;
   struct PhaseReset { aideen_ctx *c; ~PhaseReset() { c->prof_phase = -1; } } phase_reset{ctx};
   KL(launch_fpm_c(b.hstar, b.signal, b.fc, (size_t)N * h * d, st));
@@ -390,14 +392,14 @@ int run_fpm_backward(aideen_ctx *ctx) {
                    b.fup, HR, R)));
   KL(gemm_any(ctx, gemm(N, R, d, h, b.fc, hd, d, false, W + L.w_k_write, R, (long)d * R, false,
                    b.fkw, HR, R)));
-  // retain / proposal pre-activations (bias added in the coefficient kernel)
+  // retain / proposal pre-activations (biases are added by the chunk kernels)
   KL(gemm_any(ctx, gemm(N, d, R, h, b.fup, HR, R, false, W + L.w_retain_down, d, (long)R * d, false,
                    b.frp, hd, d)));
   KL(gemm_any(ctx, gemm(N, d, R, h, b.fkw, HR, R, false, W + L.w_v_write, d, (long)R * d, false,
                    b.fdl, hd, d)));
-  KL(launch_fpm_coef(a, st));
-  KL(launch_fpm_scan(a, st));
-  KL(launch_fpm_gate(a, st));
+  KL(launch_fpm_composite(a, st));
+  KL(launch_fpm_carry(a, st));
+  KL(launch_fpm_chunks(a, st));
   KL(launch_fpm_finalize(a, G, st));
   // W_retain_down[s][r][k] = sum_n up[n][s][r] g_pre[n][s][k]
   KL(gemm_any(ctx, gemm(R, d, N, h, b.fup, HR, R, true, b.fgpre, hd, d, false, G + L.w_retain_down, d,
@@ -408,10 +410,6 @@ int run_fpm_backward(aideen_ctx *ctx) {
   // W_retain_up[s][j][r] = sum_n c[n][s][j] dup[n][s][r]
   KL(gemm_any(ctx, gemm(d, R, N, h, b.fc, hd, d, true, b.fdup, HR, R, false, G + L.w_retain_up, R,
                    (long)d * R)));
-  // W_write_gate[s][k] = d^-1/2 sum_n graw[n][s] c[n][s][k];  b_write_mem[s] = sum_n graw[n][s]
-  KL(gemm_any(ctx, gemm(1, d, N, h, b.fgraw, h, 1, true, b.fc, hd, d, false, G + L.w_write_gate, d, d,
-                   1.f / std::sqrt((float)d))));
-  KL(launch_colsum(b.fgraw, N, h, h, G + L.b_write_mem, h, 0, false, st));
   // W_out[r][c] = sum_{n,s} dm[n][s][r] m_inner[n][s][c]
   KL(gemm_any(ctx, gemm(d, d, N * h, 1, b.fdm, d, 0, true, b.fminner, d, 0, false, G + L.wout, d, 0)));
   return AIDEEN_OK;
@@ -516,7 +514,7 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   auto A = [&](auto **p, size_t n) { if (e == cudaSuccess) e = dalloc(p, n); };
   A(&b.W, ctx->W_len); A(&b.G, ctx->W_len); A(&b.M1, ctx->W_len); A(&b.M2, ctx->W_len);
   A(&b.S_in, N * d); A(&b.tokens, N); A(&b.targets, N);
-  A(&b.signal, Nhd); A(&b.A, Nhd); A(&b.amat, Nhd);
+  A(&b.signal, Nhd); A(&b.A, Nhd); A(&b.amat, Nhd); A(&b.src, Nhd);
   A(&b.Qh, NH32); A(&b.Kh, NH32); A(&b.Vh, NH32); A(&b.nmix, NH32); A(&b.dn, NH32);
   A(&b.dQ, NH32); A(&b.dK, NH32); A(&b.dV, NH32);
   A(&b.alpha, N * h * h); A(&b.rmix, N * h); A(&b.scale, N * h); A(&b.rho, N * h);
@@ -570,9 +568,8 @@ void aideen_destroy(aideen_ctx *ctx) {
                   b.pooled, b.hist, b.fpmctx, b.mstate, b.iters, b.v, b.gpre, b.dl_dh, b.rhs_slot,
                   b.nsg, b.da, b.dn, b.dQ, b.dK, b.dV, b.dsig, b.dRc, b.dS, b.lmp, b.Glm, b.Mlm1,
                   b.Mlm2, b.y, b.lrms, b.logits, b.dy, b.ggp, b.loss_rows, b.scal, b.emb, b.stats,
-                  b.sigmas, b.stage, b.ws, b.fc, b.frp, b.fdl, b.falpha, b.fcpre, b.fcbd,
-                  b.fcalog, b.fcgz, b.fcwx, b.fminner, b.fdm, b.fgpre, b.fup, b.fkw, b.fdup, b.frz,
-                  b.fgraw, b.fcarry, b.fpart};
+                  b.sigmas, b.stage, b.ws, b.fc, b.frp, b.fdl, b.fminner, b.fdm, b.fgpre, b.fup,
+                  b.fkw, b.fdup, b.fA, b.fU, b.fgin, b.fcarry, b.fpart, b.fpart_bw, b.src};
   for (void *p : ptrs)
     if (p) cudaFree(p);
   if (ctx->stream && ctx->own_stream) cudaStreamDestroy(ctx->stream);

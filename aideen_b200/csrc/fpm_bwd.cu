@@ -10,15 +10,18 @@
 //   * every forward-side quantity of token t (the retain / write-gate
 //     pre-activations, the proposal, novelty and norms) depends only on the
 //     stored h*, signal and memory history, so the low-rank projections are
-//     batched tensor-core GEMMs over all tokens and `fpm_coef_kernel` turns
-//     them into per-element coefficients, fully parallel over (token, slot);
+//     batched tensor-core GEMMs over all tokens and `row_coefs` turns them
+//     into per-element coefficients, one warp per (token, slot);
 //   * in those formulas dL/dM[t-1] is an elementwise-linear function of
 //     dL/dM[t]:  g[t-1] = alpha[t] * g[t] + 0.5 * v[t]  (the reference's
 //     retain, decay and per-dimension novelty terms all act elementwise), so
-//     the serial part is a diagonal linear reverse scan, one thread per
-//     (sequence, slot, dimension): `fpm_scan_kernel`;
-//   * every parameter gradient is linear in g, so after the scan they are
-//     column sums and outer-product GEMMs over all tokens.
+//     the serial part is a diagonal linear reverse scan.  It runs chunked:
+//     every chunk of CH tokens composes its steps into g -> A g + U
+//     (parallel over chunks), a short pass carries g across the chunks, and
+//     every chunk then replays its steps from its entry value;
+//   * every parameter gradient is linear in g, so the elementwise ones are
+//     summed per chunk and reduced deterministically, and the matrix ones are
+//     outer-product GEMMs over all tokens.
 #include <cuda_runtime.h>
 #include <math.h>
 
@@ -41,32 +44,37 @@ __global__ void fpm_c_kernel(const float4 *__restrict__ hs, const float4 *__rest
     c[i] = 0.5f * (hs[i] + sig[i]);
 }
 
-// One warp per (token, slot) row; lane owns float4 columns lane + 32*i.
-template <int NV>
-__global__ void __launch_bounds__(256) fpm_coef_kernel(FpmBwdArgs a) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+// Coefficients of one (token, slot) row, computed by one warp; lane owns the
+// float4 columns lane + 32*i.  Every gradient term of the reference's token
+// step is linear in g = dL/dM[t]:
+//   alpha: g[t-1] = alpha * g + 0.5 v[t]      cpre:  g_pre (b_retain, W_retain_*)
+//   cbd:   b_delta term                       calog: a_log term
+//   cwx:   diag-W_x carrier term (before the tanh chain)
+//   cgz:   per-element weight of the write-gate sum, rz = raw_z (1 - raw_z)
+// and m_inner (the W_out operand) does not depend on g.  FULL = false stores
+// alpha only.
+// prm: the slot's parameters staged in shared memory,
+//   [0,d) b_retain  [d,2d) b_delta  [2d,3d) W_write_gate  [3d,4d) a = sigmoid(-a_log)
+//   [4d,5d) 0.5 tanh(diag W_x)
+template <int NV, bool FULL>
+__device__ __forceinline__ void row_coefs(const FpmBwdArgs &a, const float *prm, int n, int s, int t,
+                                          float *sm_row, size_t plane, float *rz_out) {
   const int lane = threadIdx.x & 31;
-  const int rows = a.B * a.T * a.h;
-  if (warp >= rows) return;
   const int d = a.d, h = a.h;
-  const int n = warp / h, s = warp - n * h;
-  const int t = n % a.T;
-  const size_t row = (size_t)warp * d;
-  const float *W = a.W;
-  float4 hv[NV], cv[NV], mp[NV], pr[NV], rt[NV];
+  const size_t row = ((size_t)n * h + s) * d;
+  float4 hv[NV], mp[NV], pr[NV], rt[NV];
   float hsq = 0.f, gdot = 0.f, psq = 0.f, dsq = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int k = 4 * (lane + 32 * i);
     hv[i] = ld4(a.hstar + row + k);
-    cv[i] = ld4(a.c + row + k);
     mp[i] = t > 0 ? ld4(a.hist + row - (size_t)h * d + k) : f4(0.f);
-    const float4 dl = ld4(a.dpre + row + k) + ld4(W + a.off_bdelta + (size_t)s * d + k);
+    const float4 dl = ld4(a.dpre + row + k) + ld4(prm + d + k);
     pr[i] = tanh4(dl);
-    const float4 rp = ld4(a.rpre + row + k) + ld4(W + a.off_bret + (size_t)s * d + k);
+    const float4 rp = ld4(a.rpre + row + k) + ld4(prm + k);
     rt[i] = make_float4(sigm(rp.x), sigm(rp.y), sigm(rp.z), sigm(rp.w));
     hsq += dot4(hv[i], hv[i]);
-    gdot += dot4(ld4(W + a.off_wgate + (size_t)s * d + k), cv[i]);
+    gdot += dot4(ld4(prm + 2 * d + k), ld4(a.c + row + k));
     psq += dot4(mp[i], mp[i]);
     const float4 df = pr[i] - mp[i];
     dsq += dot4(df, df);
@@ -75,7 +83,7 @@ __global__ void __launch_bounds__(256) fpm_coef_kernel(FpmBwdArgs a) {
   gdot = warp_sum(gdot);
   psq = warp_sum(psq);
   dsq = warp_sum(dsq);
-  const float raw_z = sigm(gdot * rsqrtf((float)d) + W[a.off_bwrite + s] + kGateBias);
+  const float raw_z = sigm(gdot * rsqrtf((float)d) + a.W[a.off_bwrite + s] + kGateBias);
   const float z = fminf(fmaxf(raw_z, 0.f), 1.f);
   const float prev_norm = sqrtf(fmaxf(psq, 1e-6f));
   const float diff_norm = sqrtf(fmaxf(dsq, 1e-6f));
@@ -87,30 +95,29 @@ __global__ void __launch_bounds__(256) fpm_coef_kernel(FpmBwdArgs a) {
   const float inv_dn = 1.f / fmaxf(diff_norm, 1e-6f);
   const float inv_pn = 1.f / fmaxf(prev_norm, 1e-6f);
   const float zs = 0.5f / sqrtf(fmaxf(z, 1e-6f));
-  if (lane == 0) a.rz[warp] = raw_z * (1.f - raw_z);
+  if (FULL && lane == 0) *rz_out = raw_z * (1.f - raw_z);
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int k = 4 * (lane + 32 * i);
-    const float4 alog = ld4(W + a.off_alog + (size_t)s * d + k);
+    const float4 am4 = ld4(prm + 3 * d + k), wx4 = ld4(prm + 4 * d + k);
     float o_alpha[4], o_pre[4], o_bd[4], o_alog[4], o_gz[4], o_wx[4], o_min[4];
     const float hvv[4] = {hv[i].x, hv[i].y, hv[i].z, hv[i].w};
     const float mpv[4] = {mp[i].x, mp[i].y, mp[i].z, mp[i].w};
     const float prv[4] = {pr[i].x, pr[i].y, pr[i].z, pr[i].w};
     const float rtv[4] = {rt[i].x, rt[i].y, rt[i].z, rt[i].w};
-    const float alv[4] = {alog.x, alog.y, alog.z, alog.w};
+    const float amv[4] = {am4.x, am4.y, am4.z, am4.w};
+    const float wxv[4] = {wx4.x, wx4.y, wx4.z, wx4.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int kk = k + e;
-      const float wx = 0.5f * tanhf(W[a.off_wx + (size_t)kk * d + kk]);
-      const float am = 1.f / (1.f + expf(alv[e]));
+      const float wx = wxv[e], am = amv[e];
       const float hu = hvv[e] * inv_hrms;
       const float r = rtv[e], p = prv[e], m = mpv[e];
       const float ret = 1.f - nov * (1.f - r);
       const float xp = hu + wx * hu + z * kResidualScale * p;
       const float base = am * m + (1.f - am) * xp;
       const float q = nov * r * (1.f - r);
-      const float cpre = (m - base) * q;                    // g_pre / g
-      const float cnov = -(cpre / fmaxf(q, 1e-6f)) * (1.f - r);   // g_nov / g
+      const float cpre = (m - base) * q;                          // g_pre / g
+      const float cnov = -(cpre / fmaxf(q, 1e-6f)) * (1.f - r);   // g_novelty / g
       const float udiff = (p - m) * inv_dn;
       const float cdn = cnov * dnov_ddiff;
       const float gx = (1.f - am) * (1.f - ret);
@@ -122,95 +129,178 @@ __global__ void __launch_bounds__(256) fpm_coef_kernel(FpmBwdArgs a) {
       o_wx[e] = (1.f - am) * hu;
       o_min[e] = ret * m + (1.f - ret) * base;
     }
-    st4(a.alpha + row + k, make_float4(o_alpha[0], o_alpha[1], o_alpha[2], o_alpha[3]));
-    st4(a.cpre + row + k, make_float4(o_pre[0], o_pre[1], o_pre[2], o_pre[3]));
-    st4(a.cbd + row + k, make_float4(o_bd[0], o_bd[1], o_bd[2], o_bd[3]));
-    st4(a.calog + row + k, make_float4(o_alog[0], o_alog[1], o_alog[2], o_alog[3]));
-    st4(a.cgz + row + k, make_float4(o_gz[0], o_gz[1], o_gz[2], o_gz[3]));
-    st4(a.cwx + row + k, make_float4(o_wx[0], o_wx[1], o_wx[2], o_wx[3]));
-    st4(a.minner + row + k, make_float4(o_min[0], o_min[1], o_min[2], o_min[3]));
+    st4(sm_row + k, make_float4(o_alpha[0], o_alpha[1], o_alpha[2], o_alpha[3]));
+    if (FULL) {
+      st4(sm_row + plane + k, make_float4(o_pre[0], o_pre[1], o_pre[2], o_pre[3]));
+      st4(sm_row + 2 * plane + k, make_float4(o_bd[0], o_bd[1], o_bd[2], o_bd[3]));
+      st4(sm_row + 3 * plane + k, make_float4(o_alog[0], o_alog[1], o_alog[2], o_alog[3]));
+      st4(sm_row + 4 * plane + k, make_float4(o_wx[0], o_wx[1], o_wx[2], o_wx[3]));
+      st4(sm_row + 5 * plane + k, make_float4(o_gz[0], o_gz[1], o_gz[2], o_gz[3]));
+      st4(a.minner + row + k, make_float4(o_min[0], o_min[1], o_min[2], o_min[3]));
+    }
   }
 }
 
-// Reverse scan, one thread per (sequence b, slot s, dimension k):
-//   dm[t] = g;  g_pre[t] = cpre[t] * g;  g <- alpha[t] * g + 0.5 * v[t]
-// with per-thread sums of the elementwise gradient terms over the chunk.
-__global__ void __launch_bounds__(128) fpm_scan_kernel(FpmBwdArgs a) {
-  const int d = a.d, h = a.h, T = a.T;
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= a.B * h * d) return;
-  const int k = i % d;
-  const int s = (i / d) % h;
-  const int b = i / (d * h);
+// One CTA per (chunk of CH tokens, slot, sequence); warp w computes token w's
+// coefficients into shared memory, then one thread per dimension walks the
+// chunk backwards.
+//   FULL = false: chunk composite  g_in -> A * g_in + U  (alpha products and
+//                 the accumulated read seeds), written to a.cA / a.cU.
+//   FULL = true:  from the chunk's entry value a.gin, emit dm and g_pre, the
+//                 per-chunk sums of every elementwise gradient term, and the
+//                 write-gate terms (W_write_gate, b_write_mem).
+template <int NV, int CH, bool FULL>
+__global__ void __launch_bounds__(32 * CH) fpm_chunk_kernel(FpmBwdArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  const int ch = blockIdx.x, s = blockIdx.y, b = blockIdx.z;
+  const int d = a.d, h = a.h, T = a.T, nch = a.nch;
+  const size_t plane = (size_t)CH * d;
+  float *rz = sm + (FULL ? 6 : 1) * plane;
+  float *graw = rz + CH;
+  float *prm = graw + CH;   // 5 * d staged slot parameters (CH is a multiple of 4)
+  for (int k = threadIdx.x; k < d; k += blockDim.x) {
+    const float *W = a.W;
+    prm[k] = W[a.off_bret + (size_t)s * d + k];
+    prm[d + k] = W[a.off_bdelta + (size_t)s * d + k];
+    prm[2 * d + k] = W[a.off_wgate + (size_t)s * d + k];
+    prm[3 * d + k] = 1.f / (1.f + expf(W[a.off_alog + (size_t)s * d + k]));
+    prm[4 * d + k] = 0.5f * tanhf(W[a.off_wx + (size_t)k * d + k]);
+  }
+  __syncthreads();
+  const int w = threadIdx.x >> 5;
+  const int t0 = ch * CH;
+  const int nt = min(CH, T - t0);
+  if (w < nt) row_coefs<NV, FULL>(a, prm, b * T + t0 + w, s, t0 + w, sm + (size_t)w * d, plane, rz + w);
+  __syncthreads();
   const size_t N = (size_t)a.B * T;
+  const size_t bc = ((size_t)b * nch + ch) * h + s;   // (sequence, chunk, slot) row of the partials
+  const size_t P = (size_t)a.B * nch * h * d;
+  for (int k = threadIdx.x; k < d; k += blockDim.x) {
+    if (!FULL) {
+      float A = 1.f, U = 0.f;
+      for (int tl = nt - 1; tl >= 0; --tl) {
+        const size_t n = (size_t)b * T + t0 + tl;
+        float vv = a.v[((size_t)s * N + n) * d + k];
+        vv = isfinite(vv) ? vv : 0.f;
+        const float al = sm[(size_t)tl * d + k];
+        A = al * A;
+        U = al * U + kReadGradScale * vv;
+      }
+      const size_t o = (((size_t)b * h + s) * nch + ch) * d + k;
+      a.cA[o] = A;
+      a.cU[o] = U;
+    } else {
+      float g = a.gin[(((size_t)b * h + s) * nch + ch) * d + k];
+      float s_pre = 0.f, s_bd = 0.f, s_alog = 0.f, s_wx = 0.f;
+      for (int tl = nt - 1; tl >= 0; --tl) {
+        const size_t n = (size_t)b * T + t0 + tl;
+        const size_t idx = (n * h + s) * d + k;
+        float vv = a.v[((size_t)s * N + n) * d + k];
+        vv = isfinite(vv) ? vv : 0.f;
+        float *c = sm + (size_t)tl * d + k;
+        const float al = c[0];
+        a.dm[idx] = g;
+        c[0] = g;                               // dm, for the write-gate sum below
+        const float gp = c[plane] * g;
+        a.gpre[idx] = gp;
+        s_pre += gp;
+        s_bd += c[2 * plane] * g;
+        s_alog += c[3 * plane] * g;
+        s_wx += c[4 * plane] * g;
+        g = al * g + kReadGradScale * vv;
+      }
+      const size_t o = bc * d + k;
+      a.part[o] = s_pre;
+      a.part[P + o] = s_bd;
+      a.part[2 * P + o] = s_alog;
+      a.part[3 * P + o] = s_wx;
+    }
+  }
+  if (!FULL) return;
+  __syncthreads();
+  if (w < nt) {
+    const int lane = threadIdx.x & 31;
+    const float *dm = sm + (size_t)w * d, *cg = dm + 5 * plane;
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int k = 4 * (lane + 32 * i);
+      acc += dot4(ld4(cg + k), ld4(dm + k));
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) graw[w] = acc * rz[w];
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < d; k += blockDim.x) {
+    float acc = 0.f;
+    for (int tl = 0; tl < nt; ++tl) {
+      const size_t n = (size_t)b * T + t0 + tl;
+      acc += graw[tl] * a.c[(n * h + s) * d + k];
+    }
+    a.part[4 * P + bc * d + k] = acc;
+  }
+  if (threadIdx.x == 0) {
+    float acc = 0.f;
+    for (int tl = 0; tl < nt; ++tl) acc += graw[tl];
+    a.part_bw[bc] = acc;
+  }
+}
+
+// Carry across chunks, one thread per (sequence, slot, dimension):
+// gin[ch] = g;  g <- A[ch] g + U[ch], from the last chunk to the first.
+__global__ void fpm_carry_kernel(FpmBwdArgs a) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int d = a.d, nch = a.nch;
+  if (i >= a.B * a.h * d) return;
+  const int k = i % d;
+  const size_t bs = i / d;
   float g = a.carry[i];
-  float s_pre = 0.f, s_bd = 0.f, s_alog = 0.f, s_wx = 0.f;
-#pragma unroll 4
-  for (int t = T - 1; t >= 0; --t) {
-    const size_t n = (size_t)b * T + t;
-    const size_t idx = (n * h + s) * d + k;
-    const float al = a.alpha[idx];
-    const float cp = a.cpre[idx];
-    float vv = a.v[((size_t)s * N + n) * d + k];
-    vv = isfinite(vv) ? vv : 0.f;
-    a.dm[idx] = g;
-    const float gp = cp * g;
-    a.gpre[idx] = gp;
-    s_pre += gp;
-    s_bd += a.cbd[idx] * g;
-    s_alog += a.calog[idx] * g;
-    s_wx += a.cwx[idx] * g;
-    g = al * g + kReadGradScale * vv;
+  for (int ch = nch - 1; ch >= 0; --ch) {
+    const size_t o = (bs * nch + ch) * d + k;
+    a.gin[o] = g;
+    g = a.cA[o] * g + a.cU[o];
   }
   a.carry[i] = g;
-  const size_t P = (size_t)a.B * h * d;
-  a.part[i] = s_pre;
-  a.part[P + i] = s_bd;
-  a.part[2 * P + i] = s_alog;
-  a.part[3 * P + i] = s_wx;
 }
 
-// Per (token, slot): dL/d(raw gate) = raw_z (1 - raw_z) * sum_k cgz * dm.
-template <int NV>
-__global__ void __launch_bounds__(256) fpm_gate_kernel(FpmBwdArgs a) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= a.B * a.T * a.h) return;
-  const size_t row = (size_t)warp * a.d;
+// Deterministic sums of the per-(sequence, chunk) partials into the gradient
+// vector.  blockIdx.y picks the quantity; each block reduces 32 columns with
+// 32 row-strided threads per column:
+//   0..3: b_retain, b_delta, a_log, W_write_gate over [B*nch] rows of [h*d]
+//   4:    diag W_x over [B*nch*h] rows of [d]     5: b_write_mem over rows of [h]
+__global__ void __launch_bounds__(1024) fpm_finalize_kernel(FpmBwdArgs a, float *G) {
+  __shared__ float red[32][33];
+  const int d = a.d, h = a.h, q = blockIdx.y;
+  const int R = a.B * a.nch;
+  const size_t P = (size_t)R * h * d;
+  const float *X;
+  int rows, ncols;
+  if (q < 4) { X = a.part + (size_t)(q == 3 ? 4 : q) * P; rows = R; ncols = h * d; }
+  else if (q == 4) { X = a.part + 3 * P; rows = R * h; ncols = d; }
+  else { X = a.part_bw; rows = R; ncols = h; }
+  const int c0 = blockIdx.x * 32;
+  if (c0 >= ncols) return;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c = c0 + tx;
   float acc = 0.f;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int k = 4 * (lane + 32 * i);
-    acc += dot4(ld4(a.cgz + row + k), ld4(a.dm + row + k));
-  }
-  acc = warp_sum(acc);
-  if (lane == 0) a.graw[warp] = acc * a.rz[warp];
-}
-
-// Sum the per-sequence partials and scatter into the gradient vector:
-// b_retain, b_delta, a_log per (slot, k) and the diagonal of W_x per k.
-__global__ void fpm_finalize_kernel(FpmBwdArgs a, float *G) {
-  const int d = a.d, h = a.h, B = a.B;
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  const size_t P = (size_t)B * h * d;
-  if (i < h * d) {
-    float sp = 0.f, sb = 0.f, sa = 0.f;
-    for (int b = 0; b < B; ++b) {
-      const size_t j = (size_t)b * h * d + i;
-      sp += a.part[j];
-      sb += a.part[P + j];
-      sa += a.part[2 * P + j];
+  if (c < ncols)
+    for (int r = ty; r < rows; r += 32) acc += X[(size_t)r * ncols + c];
+  red[ty][tx] = acc;
+  __syncthreads();
+  if (ty != 0 || c >= ncols) return;
+  float t = 0.f;
+  for (int i = 0; i < 32; ++i) t += red[i][tx];
+  switch (q) {
+    case 0: G[a.off_bret + c] = t; break;
+    case 1: G[a.off_bdelta + c] = t; break;
+    case 2: G[a.off_alog + c] = t; break;
+    case 3: G[a.off_wgate + c] = t * rsqrtf((float)d); break;
+    case 4: {
+      const float th = tanhf(a.W[a.off_wx + (size_t)c * d + c]);
+      G[a.off_wx + (size_t)c * d + c] = t * 0.5f * (1.f - th * th);
+      break;
     }
-    G[a.off_bret + i] = sp;
-    G[a.off_bdelta + i] = sb;
-    G[a.off_alog + i] = sa;
-  }
-  if (i < d) {
-    float sw = 0.f;
-    for (int b = 0; b < B; ++b)
-      for (int s = 0; s < h; ++s) sw += a.part[3 * P + ((size_t)b * h + s) * d + i];
-    const float th = tanhf(a.W[a.off_wx + (size_t)i * d + i]);
-    G[a.off_wx + (size_t)i * d + i] = sw * 0.5f * (1.f - th * th);
+    default: G[a.off_bwrite + c] = t;
   }
 }
 
@@ -225,41 +315,46 @@ cudaError_t launch_fpm_c(const float *hstar, const float *signal, float *c, size
   return cudaGetLastError();
 }
 
-cudaError_t launch_fpm_coef(const FpmBwdArgs &a, cudaStream_t st) {
-  const int rows = a.B * a.T * a.h;
-  const int blocks = (rows * 32 + 255) / 256;
-  switch (a.d / 128) {
-    case 1: fpm_coef_kernel<1><<<blocks, 256, 0, st>>>(a); break;
-    case 2: fpm_coef_kernel<2><<<blocks, 256, 0, st>>>(a); break;
-    case 4: fpm_coef_kernel<4><<<blocks, 256, 0, st>>>(a); break;
-    case 8: fpm_coef_kernel<8><<<blocks, 256, 0, st>>>(a); break;
-    default: return cudaErrorInvalidValue;
-  }
+int fpm_chunk_len(int d) { return d > 512 ? 4 : 8; }
+
+size_t fpm_chunk_smem(int d, bool full) {
+  const int CH = fpm_chunk_len(d);
+  return ((full ? 6 : 1) * (size_t)CH * d + 2 * CH + 5 * (size_t)d) * sizeof(float);
+}
+
+template <int NV, int CH, bool FULL>
+static cudaError_t chunk_launch(const FpmBwdArgs &a, cudaStream_t st) {
+  const size_t smem = fpm_chunk_smem(a.d, FULL);
+  auto k = fpm_chunk_kernel<NV, CH, FULL>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  k<<<dim3(a.nch, a.h, a.B), 32 * CH, smem, st>>>(a);
   return cudaGetLastError();
 }
 
-cudaError_t launch_fpm_scan(const FpmBwdArgs &a, cudaStream_t st) {
+template <bool FULL>
+static cudaError_t chunk_dispatch(const FpmBwdArgs &a, cudaStream_t st) {
+  if (a.nch != (a.T + fpm_chunk_len(a.d) - 1) / fpm_chunk_len(a.d)) return cudaErrorInvalidValue;
+  switch (a.d / 128) {
+    case 1: return chunk_launch<1, 8, FULL>(a, st);
+    case 2: return chunk_launch<2, 8, FULL>(a, st);
+    case 4: return chunk_launch<4, 8, FULL>(a, st);
+    case 8: return chunk_launch<8, 4, FULL>(a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_fpm_composite(const FpmBwdArgs &a, cudaStream_t st) { return chunk_dispatch<false>(a, st); }
+cudaError_t launch_fpm_chunks(const FpmBwdArgs &a, cudaStream_t st) { return chunk_dispatch<true>(a, st); }
+
+cudaError_t launch_fpm_carry(const FpmBwdArgs &a, cudaStream_t st) {
   const int n = a.B * a.h * a.d;
-  fpm_scan_kernel<<<(n + 127) / 128, 128, 0, st>>>(a);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_fpm_gate(const FpmBwdArgs &a, cudaStream_t st) {
-  const int rows = a.B * a.T * a.h;
-  const int blocks = (rows * 32 + 255) / 256;
-  switch (a.d / 128) {
-    case 1: fpm_gate_kernel<1><<<blocks, 256, 0, st>>>(a); break;
-    case 2: fpm_gate_kernel<2><<<blocks, 256, 0, st>>>(a); break;
-    case 4: fpm_gate_kernel<4><<<blocks, 256, 0, st>>>(a); break;
-    case 8: fpm_gate_kernel<8><<<blocks, 256, 0, st>>>(a); break;
-    default: return cudaErrorInvalidValue;
-  }
+  fpm_carry_kernel<<<(n + 127) / 128, 128, 0, st>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t launch_fpm_finalize(const FpmBwdArgs &a, float *G, cudaStream_t st) {
-  const int n = a.h * a.d;
-  fpm_finalize_kernel<<<(n + 255) / 256, 256, 0, st>>>(a, G);
+  fpm_finalize_kernel<<<dim3((a.h * a.d + 31) / 32, 6), 1024, 0, st>>>(a, G);
   return cudaGetLastError();
 }
 

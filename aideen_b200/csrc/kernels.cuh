@@ -91,6 +91,8 @@ cudaError_t launch_dsig_init(const AttnBwdArgs &a, float *dsig, int rows, int sl
 cudaError_t launch_colsum(const float *X, int rows, int ncols, long ld, float *out, int seg,
                           long ostride, bool accumulate, cudaStream_t st);
 cudaError_t launch_add(float *dst, const float *a, const float *b, size_t n, cudaStream_t st);
+cudaError_t launch_add_rowbias(float *dst, const float *x, const float *bias, size_t rows, size_t len,
+                               cudaStream_t st);
 
 // optimizer / renorm
 cudaError_t launch_adam(float *w, const float *g, float *m1, float *m2, size_t n, float lr,
@@ -112,22 +114,26 @@ cudaError_t launch_rmsnorm_bwd(const float *dy, const float *P, const float *lrm
 cudaError_t launch_sum(const float *x, int n, float *out, cudaStream_t st);
 
 // FPM memory backward (fpm_bwd.cu).  Row-major [N][h][d] buffers, N = B*T
-// tokens ordered (b, t); v is the adjoint solution [h][N][d].
+// tokens ordered (b, t); v is the adjoint solution [h][N][d]; the chunk
+// arrays cA, cU, gin are [B][h][nch][d] with nch = ceil(T / fpm_chunk_len(d)).
 struct FpmBwdArgs {
-  int B, T, h, d;
+  int B, T, h, d, nch;
   const float *W;
   size_t off_bdelta, off_bret, off_wgate, off_bwrite, off_alog, off_wx;
   const float *hstar, *hist, *c, *rpre, *dpre, *v;
-  float *alpha, *cpre, *cbd, *calog, *cgz, *cwx, *minner;  // per-element coefficients
-  float *rz, *graw;     // [N][h]
-  float *dm, *gpre;     // scan outputs
+  float *minner;        // [N][h][d] memory after the write, rebuilt as the reference does
+  float *cA, *cU, *gin; // chunk composites and entry values
+  float *dm, *gpre;     // [N][h][d] dL/dM[t] and the retain-gate pre-activation gradient
   float *carry;         // [B][h][d] TBPTT carry, in: dL/dM seed, out: dL/dM before the chunk
-  float *part;          // [4][B][h][d] per-sequence partial sums
+  float *part;          // [5][B*nch][h][d] per-chunk partial sums
+  float *part_bw;       // [B*nch][h]
 };
+int fpm_chunk_len(int d);
+size_t fpm_chunk_smem(int d, bool full);
 cudaError_t launch_fpm_c(const float *hstar, const float *signal, float *c, size_t n, cudaStream_t st);
-cudaError_t launch_fpm_coef(const FpmBwdArgs &a, cudaStream_t st);
-cudaError_t launch_fpm_scan(const FpmBwdArgs &a, cudaStream_t st);
-cudaError_t launch_fpm_gate(const FpmBwdArgs &a, cudaStream_t st);
+cudaError_t launch_fpm_composite(const FpmBwdArgs &a, cudaStream_t st);
+cudaError_t launch_fpm_carry(const FpmBwdArgs &a, cudaStream_t st);
+cudaError_t launch_fpm_chunks(const FpmBwdArgs &a, cudaStream_t st);
 cudaError_t launch_fpm_finalize(const FpmBwdArgs &a, float *G, cudaStream_t st);
 
 }  // namespace aideen
