@@ -155,9 +155,10 @@ __global__ void __launch_bounds__(32 * CH) fpm_chunk_kernel(FpmBwdArgs a) {
   const int ch = blockIdx.x, s = blockIdx.y, b = blockIdx.z;
   const int d = a.d, h = a.h, T = a.T, nch = a.nch;
   const size_t plane = (size_t)CH * d;
-  float *rz = sm + (FULL ? 6 : 1) * plane;
+  float *vs = sm + (FULL ? 6 : 1) * plane;   // 0.5 * v of the chunk's tokens
+  float *rz = vs + plane;
   float *graw = rz + CH;
-  float *prm = graw + CH;   // 5 * d staged slot parameters (CH is a multiple of 4)
+  float *prm = graw + CH;   // 5 * d staged slot parameters (CH is even)
   for (int k = threadIdx.x; k < d; k += blockDim.x) {
     const float *W = a.W;
     prm[k] = W[a.off_bret + (size_t)s * d + k];
@@ -170,21 +171,32 @@ __global__ void __launch_bounds__(32 * CH) fpm_chunk_kernel(FpmBwdArgs a) {
   const int w = threadIdx.x >> 5;
   const int t0 = ch * CH;
   const int nt = min(CH, T - t0);
-  if (w < nt) row_coefs<NV, FULL>(a, prm, b * T + t0 + w, s, t0 + w, sm + (size_t)w * d, plane, rz + w);
-  __syncthreads();
   const size_t N = (size_t)a.B * T;
+  if (w < nt) {
+    const int lane = threadIdx.x & 31;
+    const size_t n = (size_t)b * T + t0 + w;
+    const float *vrow = a.v + ((size_t)s * N + n) * d;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int k = 4 * (lane + 32 * i);
+      const float4 x = ld4(vrow + k);
+      st4(vs + (size_t)w * d + k, make_float4(isfinite(x.x) ? kReadGradScale * x.x : 0.f,
+                                              isfinite(x.y) ? kReadGradScale * x.y : 0.f,
+                                              isfinite(x.z) ? kReadGradScale * x.z : 0.f,
+                                              isfinite(x.w) ? kReadGradScale * x.w : 0.f));
+    }
+    row_coefs<NV, FULL>(a, prm, (int)n, s, t0 + w, sm + (size_t)w * d, plane, rz + w);
+  }
+  __syncthreads();
   const size_t bc = ((size_t)b * nch + ch) * h + s;   // (sequence, chunk, slot) row of the partials
   const size_t P = (size_t)a.B * nch * h * d;
   for (int k = threadIdx.x; k < d; k += blockDim.x) {
     if (!FULL) {
       float A = 1.f, U = 0.f;
       for (int tl = nt - 1; tl >= 0; --tl) {
-        const size_t n = (size_t)b * T + t0 + tl;
-        float vv = a.v[((size_t)s * N + n) * d + k];
-        vv = isfinite(vv) ? vv : 0.f;
         const float al = sm[(size_t)tl * d + k];
         A = al * A;
-        U = al * U + kReadGradScale * vv;
+        U = al * U + vs[(size_t)tl * d + k];
       }
       const size_t o = (((size_t)b * h + s) * nch + ch) * d + k;
       a.cA[o] = A;
@@ -195,8 +207,6 @@ __global__ void __launch_bounds__(32 * CH) fpm_chunk_kernel(FpmBwdArgs a) {
       for (int tl = nt - 1; tl >= 0; --tl) {
         const size_t n = (size_t)b * T + t0 + tl;
         const size_t idx = (n * h + s) * d + k;
-        float vv = a.v[((size_t)s * N + n) * d + k];
-        vv = isfinite(vv) ? vv : 0.f;
         float *c = sm + (size_t)tl * d + k;
         const float al = c[0];
         a.dm[idx] = g;
@@ -207,7 +217,7 @@ __global__ void __launch_bounds__(32 * CH) fpm_chunk_kernel(FpmBwdArgs a) {
         s_bd += c[2 * plane] * g;
         s_alog += c[3 * plane] * g;
         s_wx += c[4 * plane] * g;
-        g = al * g + kReadGradScale * vv;
+        g = al * g + vs[(size_t)tl * d + k];
       }
       const size_t o = bc * d + k;
       a.part[o] = s_pre;
@@ -233,9 +243,12 @@ __global__ void __launch_bounds__(32 * CH) fpm_chunk_kernel(FpmBwdArgs a) {
   __syncthreads();
   for (int k = threadIdx.x; k < d; k += blockDim.x) {
     float acc = 0.f;
-    for (int tl = 0; tl < nt; ++tl) {
-      const size_t n = (size_t)b * T + t0 + tl;
-      acc += graw[tl] * a.c[(n * h + s) * d + k];
+#pragma unroll
+    for (int tl = 0; tl < CH; ++tl) {
+      if (tl < nt) {
+        const size_t n = (size_t)b * T + t0 + tl;
+        acc += graw[tl] * a.c[(n * h + s) * d + k];
+      }
     }
     a.part[4 * P + bc * d + k] = acc;
   }
@@ -315,11 +328,11 @@ cudaError_t launch_fpm_c(const float *hstar, const float *signal, float *c, size
   return cudaGetLastError();
 }
 
-int fpm_chunk_len(int d) { return d > 512 ? 4 : 8; }
+int fpm_chunk_len(int d) { return d > 512 ? 2 : 4; }
 
 size_t fpm_chunk_smem(int d, bool full) {
   const int CH = fpm_chunk_len(d);
-  return ((full ? 6 : 1) * (size_t)CH * d + 2 * CH + 5 * (size_t)d) * sizeof(float);
+  return ((full ? 7 : 2) * (size_t)CH * d + 2 * CH + 5 * (size_t)d) * sizeof(float);
 }
 
 template <int NV, int CH, bool FULL>
@@ -336,10 +349,10 @@ template <bool FULL>
 static cudaError_t chunk_dispatch(const FpmBwdArgs &a, cudaStream_t st) {
   if (a.nch != (a.T + fpm_chunk_len(a.d) - 1) / fpm_chunk_len(a.d)) return cudaErrorInvalidValue;
   switch (a.d / 128) {
-    case 1: return chunk_launch<1, 8, FULL>(a, st);
-    case 2: return chunk_launch<2, 8, FULL>(a, st);
-    case 4: return chunk_launch<4, 8, FULL>(a, st);
-    case 8: return chunk_launch<8, 4, FULL>(a, st);
+    case 1: return chunk_launch<1, 4, FULL>(a, st);
+    case 2: return chunk_launch<2, 4, FULL>(a, st);
+    case 4: return chunk_launch<4, 4, FULL>(a, st);
+    case 8: return chunk_launch<8, 2, FULL>(a, st);
     default: return cudaErrorInvalidValue;
   }
 }

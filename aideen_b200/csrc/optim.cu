@@ -166,26 +166,46 @@ cudaError_t launch_count_active(const int32_t *tg, int N, float *out, cudaStream
   return cudaGetLastError();
 }
 
-// One block per row: logits += b_lm, online max/sum, then dlogits = (softmax - onehot)/n_active in place.
-__global__ void softmax_ce_kernel(float *__restrict__ logits, const float *__restrict__ bias,
-                                  const int32_t *__restrict__ tg,
-                                  const float *__restrict__ n_active, int V, long ld,
-                                  float *__restrict__ loss_rows) {
+// One block per row, two read passes and one write: pass 1 keeps an online
+// (max, sum) of logits + b_lm in base-2 units; pass 2 re-reads the row (an
+// L2 hit: the rows of the resident blocks fit in L2) and overwrites it with
+// dlogits = (softmax - onehot) / n_active.  Rows start 16-byte aligned
+// (ld % 4 == 0); the bias is read with float4 where its address allows.
+__global__ void __launch_bounds__(1024) softmax_ce_kernel(float *__restrict__ logits,
+                                                          const float *__restrict__ bias,
+                                                          const int32_t *__restrict__ tg,
+                                                          const float *__restrict__ n_active, int V,
+                                                          long ld, float *__restrict__ loss_rows) {
   __shared__ float rm[32], rs[32];
+  constexpr float kLog2e = 1.4426950408889634f;
   const int n = blockIdx.x;
   float *row = logits + (size_t)n * ld;
   const int t = tg[n];
+  const int V4 = V / 4;
+  const bool bias_vec = (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
+  auto load4 = [&](int i) -> float4 {
+    const float4 x = *reinterpret_cast<const float4 *>(row + 4 * i);
+    const float4 b = bias_vec ? *reinterpret_cast<const float4 *>(bias + 4 * i)
+                              : make_float4(bias[4 * i], bias[4 * i + 1], bias[4 * i + 2], bias[4 * i + 3]);
+    return make_float4((x.x + b.x) * kLog2e, (x.y + b.y) * kLog2e, (x.z + b.z) * kLog2e,
+                       (x.w + b.w) * kLog2e);
+  };
   float m = -INFINITY, s = 0.f;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float x = row[i] + bias[i];
-    row[i] = x;
-    if (x > m) { s = s * expf(m - x) + 1.f; m = x; }
-    else s += expf(x - m);
+  for (int i = threadIdx.x; i < V4; i += blockDim.x) {
+    const float4 x = load4(i);
+    const float mx = fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w));
+    if (mx > m) { s *= exp2f(m - mx); m = mx; }
+    s += exp2f(x.x - m) + exp2f(x.y - m) + exp2f(x.z - m) + exp2f(x.w - m);
+  }
+  for (int i = 4 * V4 + threadIdx.x; i < V; i += blockDim.x) {
+    const float x = (row[i] + bias[i]) * kLog2e;
+    if (x > m) { s *= exp2f(m - x); m = x; }
+    s += exp2f(x - m);
   }
   for (int o = 16; o > 0; o >>= 1) {
     const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
     const float mm = fmaxf(m, m2);
-    s = (m == -INFINITY ? 0.f : s * expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * expf(m2 - mm));
+    s = (m == -INFINITY ? 0.f : s * exp2f(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * exp2f(m2 - mm));
     m = mm;
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -194,21 +214,32 @@ __global__ void softmax_ce_kernel(float *__restrict__ logits, const float *__res
   float M = -INFINITY;
   for (int w = 0; w < nw; ++w) M = fmaxf(M, rm[w]);
   float S = 0.f;
-  for (int w = 0; w < nw; ++w) S += (rm[w] == -INFINITY) ? 0.f : rs[w] * expf(rm[w] - M);
+  for (int w = 0; w < nw; ++w) S += (rm[w] == -INFINITY) ? 0.f : rs[w] * exp2f(rm[w] - M);
   const float inv_na = 1.f / *n_active;
   if (t < 0 || t >= V) {
     for (int i = threadIdx.x; i < V; i += blockDim.x) row[i] = 0.f;
     if (threadIdx.x == 0) loss_rows[n] = 0.f;
     return;
   }
-  const float lt = row[t];
+  const float lt = row[t] + bias[t];
   __syncthreads();  // every thread has read row[t] before it is overwritten
-  if (threadIdx.x == 0) loss_rows[n] = -(lt - M - logf(S)) * inv_na;
-  const float invS = 1.f / S;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    float p = expf(row[i] - M) * invS;
-    if (i == t) p -= 1.f;
-    row[i] = p * inv_na;
+  // loss = -(x_t - ln sum exp x) with M, S in base 2: ln sum = (M + log2 S) ln 2
+  if (threadIdx.x == 0) loss_rows[n] = -(lt - (M + log2f(S)) * 0.6931471805599453f) * inv_na;
+  const float scale = inv_na / S;
+  for (int i = threadIdx.x; i < V4; i += blockDim.x) {
+    const float4 x = load4(i);
+    float4 p = make_float4(exp2f(x.x - M) * scale, exp2f(x.y - M) * scale, exp2f(x.z - M) * scale,
+                           exp2f(x.w - M) * scale);
+    if ((t >> 2) == i) {
+      const int j = t & 3;
+      if (j == 0) p.x -= inv_na; else if (j == 1) p.y -= inv_na; else if (j == 2) p.z -= inv_na; else p.w -= inv_na;
+    }
+    *reinterpret_cast<float4 *>(row + 4 * i) = p;
+  }
+  for (int i = 4 * V4 + threadIdx.x; i < V; i += blockDim.x) {
+    float p = exp2f((row[i] + bias[i]) * kLog2e - M) * scale;
+    if (i == t) p -= inv_na;
+    row[i] = p;
   }
 }
 
