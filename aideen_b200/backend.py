@@ -102,7 +102,7 @@ _SIGS = {
     "aideen_device_ptr": (_P, [_P, C.c_int]),
     "aideen_adjoint_noalloc": (C.c_int, [_P, _P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32,
                                          C.c_uint32, C.c_float, C.c_uint32, _P, _P, _P, _P]),
-    "aideen_gemm_selftest": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+    "aideen_gemm_selftest": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                        C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(C.c_float)]),
     "aideen_comm_unique_id": (C.c_int, [_P]),
     "aideen_comm_init": (C.c_int, [_P, _P, C.c_int, C.c_int]),
@@ -367,11 +367,13 @@ class GpuDeqBackend:
     def read_adj_v_out(self):
         return self.read("adj_v", (self.h, self.batch * self.seq_len, self.d))
 
-    def gemm_selftest(self, M, N, K, batch=1, trans_a=False, trans_b=False):
-        """(relative L2 difference, ms tensor-core, ms CUDA-core) on seeded operands."""
+    def gemm_selftest(self, M, N, K, batch=1, trans_a=False, trans_b=False, presplit=False):
+        """(relative L2 difference, ms tensor-core, ms CUDA-core) on seeded operands.
+        presplit=True runs the persistent kernel on pre-split hi/lo operands."""
         e, t1, t2 = C.c_float(), C.c_float(), C.c_float()
         self._check(self.lib.aideen_gemm_selftest(self.ctx, M, N, K, batch, int(trans_a), int(trans_b),
-                                                  C.byref(e), C.byref(t1), C.byref(t2)), "gemm_selftest")
+                                                  int(presplit), C.byref(e), C.byref(t1), C.byref(t2)),
+                    "gemm_selftest")
         return e.value, t1.value, t2.value
 
     # ---- multi-GPU --------------------------------------------------------

@@ -42,6 +42,11 @@ struct DevBufs {
   float *y = nullptr, *lrms = nullptr, *logits = nullptr, *dy = nullptr, *ggp = nullptr,
         *loss_rows = nullptr, *scal = nullptr;  // scal: [n_active, loss]
   float *emb = nullptr;
+  // pre-split LM-head GEMM operands: dlogits remainder [N][Vp]; y and y^T
+  // halves [N][d], [d][N4]; W_lm halves [V][d]
+  float *dlog_lo = nullptr, *yhi = nullptr, *ylo = nullptr, *yThi = nullptr, *yTlo = nullptr;
+  float *whi = nullptr, *wlo = nullptr;
+  float *colpart = nullptr;  // [blocks][Vp] per-block column sums of dlogits
   unsigned long long *stats = nullptr;
   float *sigmas = nullptr;
   float *stage = nullptr;  // packed AllWeights staging for upload/download
@@ -77,6 +82,7 @@ struct aideen_ctx {
   uint32_t adj_N = 0;     // tokens of the last adjoint
   float adj_beta = 0.85f;
   bool lm_ready = false, emb_ready = false;
+  bool lm_split_stale = true;  // W_lm changed since its hi/lo copies were made
   bool use_tc = true;     // tcgen05 GEMMs where the operand shapes allow
   DevBufs b;
   // opt-in per-kernel-class timing (aideen_profile): events around each launch
@@ -106,7 +112,7 @@ int prof_class(const char *expr, int phase) {
   if (phase >= 0) return phase;
   if (strstr(expr, "launch_picard")) return AIDEEN_PROF_PICARD;
   if (strstr(expr, "launch_adjoint")) return AIDEEN_PROF_ADJOINT;
-  if (strstr(expr, "gemm_any")) return AIDEEN_PROF_GEMM;
+  if (strstr(expr, "gemm_any") || strstr(expr, "gemm_split")) return AIDEEN_PROF_GEMM;
   if (strstr(expr, "launch_softmax_ce")) return AIDEEN_PROF_LM_SOFTMAX;
   if (strstr(expr, "launch_adam") || strstr(expr, "launch_clipped_sgd")) return AIDEEN_PROF_OPTIMIZER;
   return AIDEEN_PROF_OTHER;
@@ -161,6 +167,12 @@ GemmArgs gemm(int M, int N, int K, int batch, const float *A, long lda, long sA,
   g.C = C; g.ldc = ldc; g.strideC = sC;
   g.alpha = alpha; g.beta = beta; g.abias = abias; g.strideAbias = sbias;
   return g;
+}
+
+// Pre-split GEMM (operands as tf32 high parts in g.A / g.B plus remainders).
+cudaError_t gemm_split(aideen_ctx *ctx, const GemmArgs &g, const float *A_lo, const float *B_lo) {
+  if (!tc_split_supported(g, A_lo, B_lo)) return cudaErrorInvalidValue;
+  return tc_gemm_split(g, A_lo, B_lo, ctx->stream, ctx->b.ws, ctx->ws_floats);
 }
 
 // GEMM dispatch: tcgen05 (3xTF32) when supported for these operands, else CUDA cores.
@@ -255,15 +267,41 @@ int run_lm_head(aideen_ctx *ctx, int N, float *loss_out) {
   const float *Wlm = b.lmp, *glm = b.lmp + ctx->lm_g;
   const long Vp = ctx->Vp;
   KL(launch_count_active(b.targets, N, b.scal, st));
-  // logits[n][v] = y[n] . W_lm[v]   (K-major A and B)
-  KL(gemm_any(ctx, gemm(N, V, d, 1, b.y, d, 0, false, Wlm, d, 0, true, b.logits, Vp, 0)));
-  KL(launch_softmax_ce(b.logits, b.lmp + ctx->lm_b, b.targets, b.scal, N, V, Vp, b.loss_rows, st));
+  // The three LM-head GEMMs run on pre-split operands: W_lm halves are
+  // refreshed once per change of W_lm, y and y^T halves per call (y^T makes
+  // dW_lm's B operand K-major), and the softmax writes dlogits already split.
+  if (ctx->lm_split_stale) {
+    KL(launch_split_hilo(Wlm, b.whi, b.wlo, (size_t)V * d, st));
+    ctx->lm_split_stale = false;
+  }
+  const long N4 = (N + 3) / 4 * 4;
+  KL(launch_split_hilo(b.y, b.yhi, b.ylo, (size_t)N * d, st));
+  KL(launch_transpose_split(b.y, N, d, d, b.yThi, b.yTlo, N4, st));
+  // logits[n][v] = y[n] . W_lm[v]
+  KL(gemm_split(ctx, gemm(N, V, d, 1, b.yhi, d, 0, false, b.whi, d, 0, true, b.logits, Vp, 0), b.ylo, b.wlo));
+  // vocabularies whose column accumulator fits one block's shared memory fuse
+  // the b_lm column sums into the softmax; larger ones sum dlogits afterwards
+  const bool fused_colsum = Vp * 4 <= 227 * 1024;
+  const int nrb = softmax_rows_blocks(N);
+  if (fused_colsum)
+    KL(launch_softmax_ce_split(b.logits, b.lmp + ctx->lm_b, b.targets, b.scal, N, V, Vp, b.loss_rows,
+                               b.dlog_lo, b.colpart, st));
+  else
+    KL(launch_softmax_ce(b.logits, b.lmp + ctx->lm_b, b.targets, b.scal, N, V, Vp, b.loss_rows, b.dlog_lo, st));
   KL(launch_sum(b.loss_rows, N, b.scal + 1, st));
-  // dy = dlogits . W_lm
-  KL(gemm_any(ctx, gemm(N, d, V, 1, b.logits, Vp, 0, false, Wlm, d, 0, false, b.dy, d, 0)));
-  // dW_lm = dlogits^T . y
-  KL(gemm_any(ctx, gemm(V, d, N, 1, b.logits, Vp, 0, true, b.y, d, 0, false, b.Glm, d, 0)));
-  KL(launch_colsum(b.logits, N, V, Vp, b.Glm + ctx->lm_b, V, 0, false, st));
+  // dy[n][j] = sum_v dlogits[n][v] W_lm[v][j]
+  KL(gemm_split(ctx, gemm(N, d, V, 1, b.logits, Vp, 0, false, b.whi, d, 0, false, b.dy, d, 0), b.dlog_lo,
+                b.wlo));
+  // dW_lm[v][j] = sum_n dlogits[n][v] y^T[j][n]
+  KL(gemm_split(ctx, gemm(V, d, N, 1, b.logits, Vp, 0, true, b.yThi, N4, 0, true, b.Glm, d, 0), b.dlog_lo,
+                b.yTlo));
+  // b_lm gradient: column sums of dlogits from the softmax's per-block partials
+  if (fused_colsum) {
+    KL(launch_colsum(b.colpart, nrb, V, Vp, b.Glm + ctx->lm_b, V, 0, false, st));
+  } else {
+    KL(launch_colsum(b.logits, N, V, Vp, b.Glm + ctx->lm_b, V, 0, false, st));
+    KL(launch_colsum(b.dlog_lo, N, V, Vp, b.Glm + ctx->lm_b, V, 0, true, st));
+  }
   KL(launch_rmsnorm_bwd(b.dy, b.pooled, b.lrms, glm, b.dl_dh, b.ggp, N, d, st));
   KL(launch_colsum(b.ggp, N, d, d, b.Glm + ctx->lm_g, d, 0, false, st));
   if (loss_out) {
@@ -459,14 +497,18 @@ int run_update(aideen_ctx *ctx, const aideen_update *u) {
     const float bc2 = (float)(1.0 - std::pow((double)u->beta2, t));
     KL(launch_adam(b.W, b.G, b.M1, b.M2, ctx->W_len, u->lr, u->beta1, u->beta2, u->eps, bc1, bc2,
                    u->grad_scale, st));
-    if (u->update_lm_head && ctx->lm_ready)
+    if (u->update_lm_head && ctx->lm_ready) {
       KL(launch_adam(b.lmp, b.Glm, b.Mlm1, b.Mlm2, ctx->lm_len, u->lr, u->beta1, u->beta2, u->eps,
                      bc1, bc2, u->grad_scale, st));
+      ctx->lm_split_stale = true;
+    }
   } else if (u->rule == AIDEEN_RULE_CLIPPED_SGD) {
     KL(launch_clipped_sgd(b.W, b.G, ctx->W_len, ctx->P.hist, u->lr, u->weight_decay, u->grad_scale, st));
-    if (u->update_lm_head && ctx->lm_ready)
+    if (u->update_lm_head && ctx->lm_ready) {
       KL(launch_clipped_sgd(b.lmp, b.Glm, ctx->lm_len, ctx->lm_len, u->lr, u->weight_decay,
                             u->grad_scale, st));
+      ctx->lm_split_stale = true;
+    }
   } else {
     return set_err(ctx, AIDEEN_E_INVALID, "unknown update rule");
   }
@@ -523,13 +565,16 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   A(&b.v, Nhd); A(&b.gpre, Nhd); A(&b.dsig, Nhd); A(&b.da, Nhd);
   A(&b.mstate, (size_t)cfg->max_batch * h * d); A(&b.fcarry, (size_t)cfg->max_batch * h * d);
   A(&b.pooled, N * d); A(&b.dl_dh, N * d); A(&b.nsg, N * d); A(&b.dS, N * d);
-  A(&b.y, N * d); A(&b.dy, N * d); A(&b.ggp, N * d); A(&b.lrms, N); A(&b.loss_rows, N);
+  A(&b.y, N * d); A(&b.dy, N * d); A(&b.yhi, N * d); A(&b.ylo, N * d);
+  A(&b.yThi, d * ((N + 3) / 4 * 4)); A(&b.yTlo, d * ((N + 3) / 4 * 4)); A(&b.ggp, N * d); A(&b.lrms, N); A(&b.loss_rows, N);
   A(&b.scal, 4); A(&b.stage, ctx->Lx.total);
   ctx->ws_floats = 16 * N * d;  // up to 16 splits of an [N][d] output
   A(&b.ws, ctx->ws_floats); A(&b.stats, 4); A(&b.sigmas, 5 * h + 2);
   if (V) {
     A(&b.lmp, ctx->lm_len); A(&b.Glm, ctx->lm_len); A(&b.Mlm1, ctx->lm_len); A(&b.Mlm2, ctx->lm_len);
     A(&b.logits, N * (size_t)ctx->Vp); A(&b.emb, V * d);
+    A(&b.dlog_lo, N * (size_t)ctx->Vp); A(&b.whi, V * d); A(&b.wlo, V * d);
+    A(&b.colpart, (size_t)softmax_rows_blocks((int)N) * ctx->Vp);  // <= one row per SM
   }
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
   ctx->own_stream = true;
@@ -569,7 +614,8 @@ void aideen_destroy(aideen_ctx *ctx) {
                   b.nsg, b.da, b.dn, b.dQ, b.dK, b.dV, b.dsig, b.dRc, b.dS, b.lmp, b.Glm, b.Mlm1,
                   b.Mlm2, b.y, b.lrms, b.logits, b.dy, b.ggp, b.loss_rows, b.scal, b.emb, b.stats,
                   b.sigmas, b.stage, b.ws, b.fc, b.frp, b.fdl, b.fminner, b.fdm, b.fgpre, b.fup,
-                  b.fkw, b.fdup, b.fA, b.fU, b.fgin, b.fcarry, b.fpart, b.fpart_bw, b.src};
+                  b.fkw, b.fdup, b.fA, b.fU, b.fgin, b.fcarry, b.fpart, b.fpart_bw, b.src,
+                  b.dlog_lo, b.yhi, b.ylo, b.yThi, b.yTlo, b.whi, b.wlo, b.colpart};
   for (void *p : ptrs)
     if (p) cudaFree(p);
   if (ctx->stream && ctx->own_stream) cudaStreamDestroy(ctx->stream);
@@ -674,6 +720,7 @@ int aideen_upload_lm_head(aideen_ctx *ctx, const float *w_lm, const float *b_lm,
   CHK(copy_in(ctx, ctx->b.lmp + ctx->lm_g, g_lm, d * sizeof(float), AIDEEN_HOST));
   CU(cudaStreamSynchronize(ctx->stream));
   ctx->lm_ready = true;
+  ctx->lm_split_stale = true;
   return AIDEEN_OK;
 }
 
@@ -931,7 +978,7 @@ __global__ void relerr_kernel(const float *a, const float *b, size_t n, double *
 }  // namespace
 
 int aideen_gemm_selftest(aideen_ctx *ctx, int M, int N, int K, int batch, int trans_a, int trans_b,
-                         float *rel_err, float *ms_tc, float *ms_simt) {
+                         int flags, float *rel_err, float *ms_tc, float *ms_simt) {
   if (!ctx || M <= 0 || N <= 0 || K <= 0 || batch <= 0) return AIDEEN_E_INVALID;
   const size_t na = (size_t)M * K * batch, nb = (size_t)K * N * batch, nc = (size_t)M * N * batch;
   float *A = nullptr, *B = nullptr, *C1 = nullptr, *C2 = nullptr;
@@ -946,7 +993,20 @@ int aideen_gemm_selftest(aideen_ctx *ctx, int M, int N, int K, int batch, int tr
   GemmArgs g = gemm(M, N, K, batch, A, lda, (long)M * K, trans_a != 0, B, ldb, (long)K * N, trans_b != 0,
                     C1, N, (long)M * N);
   int rc = AIDEEN_OK;
-  if (!tc_gemm_supported(g)) {
+  const bool presplit = (flags & AIDEEN_SELFTEST_PRESPLIT) != 0;
+  float *Alo = nullptr, *Blo = nullptr, *Ahi = nullptr, *Bhi = nullptr;
+  if (presplit) {
+    CU(cudaMalloc(&Ahi, na * 4)); CU(cudaMalloc(&Alo, na * 4));
+    CU(cudaMalloc(&Bhi, nb * 4)); CU(cudaMalloc(&Blo, nb * 4));
+    CU(launch_split_hilo(A, Ahi, Alo, na, st));
+    CU(launch_split_hilo(B, Bhi, Blo, nb, st));
+  }
+  GemmArgs gs = g;
+  gs.A = Ahi; gs.B = Bhi;
+  auto run_tc = [&](float *wsp, size_t wsn) -> cudaError_t {
+    return presplit ? tc_gemm_split(gs, Alo, Blo, st, wsp, wsn) : tc_gemm(g, st, wsp, wsn);
+  };
+  if (presplit ? !tc_split_supported(gs, Alo, Blo) : !tc_gemm_supported(g)) {
     rc = set_err(ctx, AIDEEN_E_UNSUPPORTED, "shape not supported by the tensor-core GEMM");
   } else {
     cudaEvent_t e0, e1, e2;
@@ -954,9 +1014,9 @@ int aideen_gemm_selftest(aideen_ctx *ctx, int M, int N, int K, int batch, int tr
     float *wsp = nullptr;
     const size_t wsn = 16 * (size_t)M * N;
     cudaMalloc(&wsp, wsn * 4);
-    tc_gemm(g, st, wsp, wsn);  // warm-up
+    run_tc(wsp, wsn);  // warm-up
     cudaEventRecord(e0, st);
-    cudaError_t ce = tc_gemm(g, st, wsp, wsn);
+    cudaError_t ce = run_tc(wsp, wsn);
     cudaEventRecord(e1, st);
     GemmArgs g2 = g;
     g2.C = C2;
@@ -973,7 +1033,7 @@ int aideen_gemm_selftest(aideen_ctx *ctx, int M, int N, int K, int batch, int tr
     cudaFree(wsp);
     if (ce != cudaSuccess || ce2 != cudaSuccess || se != cudaSuccess)
       rc = set_err(ctx, AIDEEN_E_CUDA, "GEMM self-test launch failed");
-    else if (tc_gemm_error(true))
+    else if (presplit ? tc_split_error(true) : tc_gemm_error(true))
       rc = set_err(ctx, AIDEEN_E_TIMEOUT, "tensor-core GEMM pipeline wait timed out");
     if (getenv("AIDEEN_SELFTEST_DUMP")) {
       float a[8], b2[8];
@@ -987,6 +1047,7 @@ int aideen_gemm_selftest(aideen_ctx *ctx, int M, int N, int K, int batch, int tr
     if (ms_simt) *ms_simt = t2;
   }
   cudaFree(A); cudaFree(B); cudaFree(C1); cudaFree(C2); cudaFree(acc);
+  if (presplit) { cudaFree(Ahi); cudaFree(Alo); cudaFree(Bhi); cudaFree(Blo); }
   return rc;
 }
 

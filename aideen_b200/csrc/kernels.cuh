@@ -26,6 +26,18 @@ bool tc_gemm_supported(const GemmArgs &g);
 // ws: optional workspace for split-K partial sums (ws_floats capacity).
 cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t s, float *ws = nullptr, size_t ws_floats = 0);
 unsigned int tc_gemm_error(bool reset);
+// Persistent tcgen05 GEMM on pre-split operands (tcgemm_split.cu): g.A / g.B
+// hold the tf32-exact high parts, A_lo / B_lo the remainders (same strides);
+// beta must be 0 or 1.
+bool tc_split_supported(const GemmArgs &g, const float *A_lo, const float *B_lo);
+cudaError_t tc_gemm_split(const GemmArgs &g, const float *A_lo, const float *B_lo, cudaStream_t s,
+                          float *ws = nullptr, size_t ws_floats = 0);
+unsigned int tc_split_error(bool reset);
+// x -> (hi, lo) with hi exact in tf32 and lo = x - hi (n % 4 == 0).
+cudaError_t launch_split_hilo(const float *x, float *hi, float *lo, size_t n, cudaStream_t st);
+// out[c][r] = split(x[r][c]): transposed hi / lo copies (row stride ldt).
+cudaError_t launch_transpose_split(const float *x, int R, int C, long ldx, float *hiT, float *loT, long ldt,
+                                   cudaStream_t st);
 
 struct AttnArgs {
   int h, d;
@@ -106,8 +118,18 @@ cudaError_t launch_spectral(float *W, int d, int h, const Layout &L, int n_iters
 
 // LM head helpers
 cudaError_t launch_count_active(const int32_t *tg, int N, float *out, cudaStream_t st);
+// dlogits replace the logits in place; with lo != nullptr the row is written
+// pre-split: logits <- tf32-exact high part, lo <- remainder (same strides).
 cudaError_t launch_softmax_ce(float *logits, const float *bias, const int32_t *tg,
-                              const float *n_active, int N, int V, long ld, float *loss_rows, cudaStream_t st);
+                              const float *n_active, int N, int V, long ld, float *loss_rows, float *lo,
+                              cudaStream_t st);
+// Pre-split softmax-CE over blocks of rows that also writes per-block column
+// sums of dlogits: colpart is [softmax_rows_blocks(N)][ld]; ld * 4 bytes must
+// fit in one block's shared memory (vocab <= 58,000).
+int softmax_rows_blocks(int N);
+cudaError_t launch_softmax_ce_split(float *logits, const float *bias, const int32_t *tg,
+                                    const float *n_active, int N, int V, long ld, float *loss_rows,
+                                    float *lo, float *colpart, cudaStream_t st);
 cudaError_t launch_rmsnorm_bwd(const float *dy, const float *P, const float *lrms,
                                const float *g, float *dl_dh, float *ggp, int N, int d,
                                cudaStream_t st);

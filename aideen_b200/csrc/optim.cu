@@ -175,7 +175,8 @@ __global__ void __launch_bounds__(1024) softmax_ce_kernel(float *__restrict__ lo
                                                           const float *__restrict__ bias,
                                                           const int32_t *__restrict__ tg,
                                                           const float *__restrict__ n_active, int V,
-                                                          long ld, float *__restrict__ loss_rows) {
+                                                          long ld, float *__restrict__ loss_rows,
+                                                          float *__restrict__ lo_out) {
   __shared__ float rm[32], rs[32];
   constexpr float kLog2e = 1.4426950408889634f;
   const int n = blockIdx.x;
@@ -216,8 +217,12 @@ __global__ void __launch_bounds__(1024) softmax_ce_kernel(float *__restrict__ lo
   float S = 0.f;
   for (int w = 0; w < nw; ++w) S += (rm[w] == -INFINITY) ? 0.f : rs[w] * exp2f(rm[w] - M);
   const float inv_na = 1.f / *n_active;
+  float *lrow = lo_out ? lo_out + (size_t)n * ld : nullptr;
   if (t < 0 || t >= V) {
-    for (int i = threadIdx.x; i < V; i += blockDim.x) row[i] = 0.f;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      row[i] = 0.f;
+      if (lrow) lrow[i] = 0.f;
+    }
     if (threadIdx.x == 0) loss_rows[n] = 0.f;
     return;
   }
@@ -234,20 +239,176 @@ __global__ void __launch_bounds__(1024) softmax_ce_kernel(float *__restrict__ lo
       const int j = t & 3;
       if (j == 0) p.x -= inv_na; else if (j == 1) p.y -= inv_na; else if (j == 2) p.z -= inv_na; else p.w -= inv_na;
     }
+    if (lrow) {
+      float4 h;
+      h.x = __uint_as_float(__float_as_uint(p.x) & 0xFFFFE000u);
+      h.y = __uint_as_float(__float_as_uint(p.y) & 0xFFFFE000u);
+      h.z = __uint_as_float(__float_as_uint(p.z) & 0xFFFFE000u);
+      h.w = __uint_as_float(__float_as_uint(p.w) & 0xFFFFE000u);
+      *reinterpret_cast<float4 *>(lrow + 4 * i) = make_float4(p.x - h.x, p.y - h.y, p.z - h.z, p.w - h.w);
+      p = h;
+    }
     *reinterpret_cast<float4 *>(row + 4 * i) = p;
   }
   for (int i = 4 * V4 + threadIdx.x; i < V; i += blockDim.x) {
     float p = exp2f((row[i] + bias[i]) * kLog2e - M) * scale;
     if (i == t) p -= inv_na;
+    if (lrow) {
+      const float h = __uint_as_float(__float_as_uint(p) & 0xFFFFE000u);
+      lrow[i] = p - h;
+      p = h;
+    }
     row[i] = p;
   }
 }
 
 cudaError_t launch_softmax_ce(float *logits, const float *bias, const int32_t *tg,
-                              const float *n_active, int N, int V, long ld, float *loss_rows,
+                              const float *n_active, int N, int V, long ld, float *loss_rows, float *lo,
                               cudaStream_t st) {
   if (N <= 0) return cudaSuccess;
-  softmax_ce_kernel<<<N, 1024, 0, st>>>(logits, bias, tg, n_active, V, ld, loss_rows);
+  softmax_ce_kernel<<<N, 1024, 0, st>>>(logits, bias, tg, n_active, V, ld, loss_rows, lo);
+  return cudaGetLastError();
+}
+
+// Pre-split variant that also emits column partial sums of dlogits: one
+// block of 1024 threads walks `rows` consecutive rows (two read passes and
+// one write per row, as softmax_ce_kernel), writes each row as tf32-exact
+// high part (in place) + remainder (lo), and adds the row into a per-block
+// column accumulator held in shared memory (ld floats, each column owned by
+// one thread, so no atomics); the block's sums go to colpart[block][v].
+__global__ void __launch_bounds__(1024) softmax_ce_rows_kernel(float *__restrict__ logits,
+                                                               const float *__restrict__ bias,
+                                                               const int32_t *__restrict__ tg,
+                                                               const float *__restrict__ n_active, int N,
+                                                               int V, long ld, int rows,
+                                                               float *__restrict__ loss_rows,
+                                                               float *__restrict__ lo_out,
+                                                               float *__restrict__ colpart) {
+  extern __shared__ __align__(16) float colacc[];
+  __shared__ float rm[32], rs[32];
+  constexpr float kLog2e = 1.4426950408889634f;
+  const int V4 = V / 4;
+  const int tail = V - 4 * V4;
+  const bool bias_vec = (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const float inv_na = 1.f / *n_active;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) colacc[i] = 0.f;
+  auto bias4 = [&](int i) -> float4 {
+    return bias_vec ? *reinterpret_cast<const float4 *>(bias + 4 * i)
+                    : make_float4(bias[4 * i], bias[4 * i + 1], bias[4 * i + 2], bias[4 * i + 3]);
+  };
+  for (int rr = 0; rr < rows; ++rr) {
+    const int n = blockIdx.x * rows + rr;
+    if (n >= N) break;
+    float *row = logits + (size_t)n * ld;
+    float *lrow = lo_out + (size_t)n * ld;
+    const int t = tg[n];
+    float m = -INFINITY, sacc = 0.f;
+    for (int i = threadIdx.x; i < V4; i += blockDim.x) {
+      const float4 x4 = *reinterpret_cast<const float4 *>(row + 4 * i);
+      const float4 b4 = bias4(i);
+      const float4 x = make_float4((x4.x + b4.x) * kLog2e, (x4.y + b4.y) * kLog2e, (x4.z + b4.z) * kLog2e,
+                                   (x4.w + b4.w) * kLog2e);
+      const float mx = fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w));
+      if (mx > m) { sacc *= exp2f(m - mx); m = mx; }
+      sacc += exp2f(x.x - m) + exp2f(x.y - m) + exp2f(x.z - m) + exp2f(x.w - m);
+    }
+    if ((int)threadIdx.x < tail) {
+      const int i = 4 * V4 + threadIdx.x;
+      const float x = (row[i] + bias[i]) * kLog2e;
+      if (x > m) { sacc *= exp2f(m - x); m = x; }
+      sacc += exp2f(x - m);
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, sacc, o);
+      const float mm = fmaxf(m, m2);
+      sacc = (m == -INFINITY ? 0.f : sacc * exp2f(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * exp2f(m2 - mm));
+      m = mm;
+    }
+    __syncthreads();  // the previous row's readers of rm / rs are done
+    if (lane == 0) { rm[warp] = m; rs[warp] = sacc; }
+    __syncthreads();
+    float M = -INFINITY;
+    for (int w = 0; w < nw; ++w) M = fmaxf(M, rm[w]);
+    float S = 0.f;
+    for (int w = 0; w < nw; ++w) S += (rm[w] == -INFINITY) ? 0.f : rs[w] * exp2f(rm[w] - M);
+    const bool ignore = t < 0 || t >= V;
+    const float lt = ignore ? 0.f : row[t] + bias[t];
+    __syncthreads();  // every thread has read row[t] before it is overwritten
+    if (threadIdx.x == 0)
+      loss_rows[n] = ignore ? 0.f : -(lt - (M + log2f(S)) * 0.6931471805599453f) * inv_na;
+    const float scale = ignore ? 0.f : inv_na / S;
+    for (int i = threadIdx.x; i < V4; i += blockDim.x) {
+      const float4 x4 = *reinterpret_cast<const float4 *>(row + 4 * i);
+      const float4 b4 = bias4(i);
+      float4 p = make_float4(exp2f((x4.x + b4.x) * kLog2e - M) * scale, exp2f((x4.y + b4.y) * kLog2e - M) * scale,
+                             exp2f((x4.z + b4.z) * kLog2e - M) * scale, exp2f((x4.w + b4.w) * kLog2e - M) * scale);
+      if (!ignore && (t >> 2) == i) {
+        const int j = t & 3;
+        if (j == 0) p.x -= inv_na; else if (j == 1) p.y -= inv_na; else if (j == 2) p.z -= inv_na; else p.w -= inv_na;
+      }
+      float4 *ca = reinterpret_cast<float4 *>(colacc + 4 * i);
+      *ca = *ca + p;
+      float4 h;
+      h.x = __uint_as_float(__float_as_uint(p.x) & 0xFFFFE000u);
+      h.y = __uint_as_float(__float_as_uint(p.y) & 0xFFFFE000u);
+      h.z = __uint_as_float(__float_as_uint(p.z) & 0xFFFFE000u);
+      h.w = __uint_as_float(__float_as_uint(p.w) & 0xFFFFE000u);
+      *reinterpret_cast<float4 *>(lrow + 4 * i) = make_float4(p.x - h.x, p.y - h.y, p.z - h.z, p.w - h.w);
+      *reinterpret_cast<float4 *>(row + 4 * i) = h;
+    }
+    if ((int)threadIdx.x < tail) {
+      const int i = 4 * V4 + threadIdx.x;
+      float p = exp2f((row[i] + bias[i]) * kLog2e - M) * scale;
+      if (!ignore && i == t) p -= inv_na;
+      colacc[i] += p;
+      const float h = __uint_as_float(__float_as_uint(p) & 0xFFFFE000u);
+      lrow[i] = p - h;
+      row[i] = h;
+    }
+  }
+  float *prow = colpart + (size_t)blockIdx.x * ld;
+  for (int i = threadIdx.x; i < V4; i += blockDim.x)
+    *reinterpret_cast<float4 *>(prow + 4 * i) = *reinterpret_cast<const float4 *>(colacc + 4 * i);
+  if ((int)threadIdx.x < tail) prow[4 * V4 + threadIdx.x] = colacc[4 * V4 + threadIdx.x];
+}
+
+namespace {
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+}  // namespace
+
+// One wave: as many blocks as SMs (one block per SM: the accumulator takes
+// V floats of shared memory), each with ceil(N / blocks) rows.
+int softmax_rows_per_block(int N) {
+  const int nsm = num_sms();
+  return (N + nsm - 1) / nsm;
+}
+int softmax_rows_blocks(int N) {
+  const int r = softmax_rows_per_block(N);
+  return (N + r - 1) / r;
+}
+
+cudaError_t launch_softmax_ce_split(float *logits, const float *bias, const int32_t *tg,
+                                    const float *n_active, int N, int V, long ld, float *loss_rows,
+                                    float *lo, float *colpart, cudaStream_t st) {
+  if (N <= 0) return cudaSuccess;
+  const size_t smem = (size_t)ld * sizeof(float);
+  if (ld & 3 || smem > 227 * 1024) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(softmax_ce_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  softmax_ce_rows_kernel<<<softmax_rows_blocks(N), 1024, smem, st>>>(logits, bias, tg, n_active, N, V, ld,
+                                                                      softmax_rows_per_block(N), loss_rows, lo,
+                                                                      colpart);
   return cudaGetLastError();
 }
 

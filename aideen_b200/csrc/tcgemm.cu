@@ -26,83 +26,14 @@
 #include <cstring>
 
 #include "kernels.cuh"
+#include "tc_common.cuh"
 
 namespace aideen {
 namespace {
 
 constexpr int BM = 128, BK = 32, STAGES = 3, TC_THREADS = 192;
-constexpr uint32_t kMaxSpin = 1u << 26;
 
 __device__ unsigned int g_tc_error;  // first error code seen by any tcgemm CTA
-
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-
-// Bounded wait for the phase with the given parity; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-  const uint32_t addr = smem_u32(bar);
-  for (uint32_t i = 0; i < kMaxSpin; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    if (done) return true;
-  }
-  return false;
-}
-
-__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x,
-                                            int y, int z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
-
-// Shared-memory matrix descriptor (sm100 version field = 1).  layout 2 =
-// 128-byte swizzle (K-major operands), layout 1 = 128-byte swizzle on 32-byte
-// atoms, the only layout the tf32 MMA accepts for MN-major operands.
-__device__ __forceinline__ uint64_t sdesc(const void *base, uint32_t lbo_bytes, uint32_t sbo_bytes,
-                                          uint32_t layout) {
-  const uint64_t addr = smem_u32(base);
-  return ((addr & 0x3FFFFull) >> 4) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16) |
-         ((uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
-}
-
-__device__ __forceinline__ void umma_tf32(uint32_t tmem_c, uint64_t da, uint64_t db, uint32_t idesc,
-                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_c),
-      "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 
 // x -> (x_hi, x_lo) in place / alongside: x_hi keeps the 10 tf32 mantissa bits.
 __device__ __forceinline__ void split1(float4 *raw, float4 *lo) {
@@ -124,6 +55,8 @@ struct TcParams {
   float alpha, beta;
   int a_batched, b_batched;  // operand map has a batch dimension
   int ksplit, kchunk;        // split-K: blockIdx.z = split index, kchunk K-blocks each
+  int tma_epi;               // 1: epilogue through 32x32 shared-memory boxes + bulk tensor
+                             //    store (beta 0) or reduce-add (beta 1) on mapC
 };
 
 // Warp roles (192 threads): warp 0 lane 0 = TMA producer, warp 1 = TMEM
@@ -131,16 +64,20 @@ struct TcParams {
 // (warp w reads TMEM lanes 32*(w%4)..+31, so the four cover all 128 rows).
 // Per stage s: full[s] (TMA landed) -> conv[s] (split done, 4 warp arrivals)
 // -> empty[s] (MMAs done, tcgen05.commit) -> producer refills.
+constexpr int BOX_BYTES = 32 * 32 * 4;  // one 32x32 fp32 epilogue box
+
 template <int BN>
 __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constant__ CUtensorMap mapA,
                                                             const __grid_constant__ CUtensorMap mapB,
+                                                            const __grid_constant__ CUtensorMap mapC,
                                                             TcParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *sm = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4;
   constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-  uint64_t *full = reinterpret_cast<uint64_t *>(sm + STAGES * STAGE_BYTES);
+  unsigned char *boxes = sm + STAGES * STAGE_BYTES;  // 4 epilogue warps x 2 boxes
+  uint64_t *full = reinterpret_cast<uint64_t *>(boxes + 8 * BOX_BYTES);
   uint64_t *conv = full + STAGES;
   uint64_t *empty = conv + STAGES;
   uint64_t *done = empty + STAGES;
@@ -266,7 +203,48 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
     }
     const bool ok = mbar_wait(done, 0) && !*(volatile uint32_t *)err;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (ok) {
+    if (ok && p.tma_epi) {
+      const int q = warp & 3;  // TMEM lane quadrant this warp may access
+      const int rowbase = m0 + q * 32;
+      unsigned char *mybox = boxes + (warp - 2) * 2 * BOX_BYTES;
+      int nst = 0;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+            "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+            "%28, %29, %30, %31}, [%32];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+              "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+              "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+              "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+              "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        const int col = n0 + c0;
+        if (col >= p.N || rowbase >= p.M) continue;  // box entirely outside C
+        unsigned char *box = mybox + (nst & 1) * BOX_BYTES;
+        if (lane == 0) bulk_wait_read<1>();  // the store issued from this box two boxes ago is done reading
+        __syncwarp();
+        float4 *row = reinterpret_cast<float4 *>(box + lane * 128);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          row[k ^ (lane & 7)] = make_float4(p.alpha * __uint_as_float(r[4 * k]), p.alpha * __uint_as_float(r[4 * k + 1]),
+                                            p.alpha * __uint_as_float(r[4 * k + 2]),
+                                            p.alpha * __uint_as_float(r[4 * k + 3]));
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          if (p.beta != 0.f) tma_reduce_add_3d(&mapC, box, col, rowbase, bz);
+          else tma_store_3d(&mapC, box, col, rowbase, bz);
+          bulk_commit();
+        }
+        ++nst;
+      }
+      if (lane == 0) bulk_wait<0>();  // stores complete before the CTA's shared memory goes away
+    } else if (ok) {
       const int q = warp & 3;  // TMEM lane quadrant this warp may access
       const int row = m0 + q * 32 + lane;
       float *crow = p.C + (long)bz * p.strideC + (long)row * p.ldc;
@@ -316,23 +294,6 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
 }
 
 // ---------------------------------------------------------------- host side
-using EncodeFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                              const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
-                              CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
-                              CUtensorMapFloatOOBfill);
-
-EncodeFn encode_fn() {
-  static EncodeFn fn = nullptr;
-  if (!fn) {
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeFn>(p);
-  }
-  return fn;
-}
-
 // 3-D fp32 map: dim0 contiguous (extent e0), dim1 stride s1 elements, dim2 stride s2.
 bool make_map(CUtensorMap *m, const float *base, uint64_t e0, uint64_t e1, uint64_t e2, uint64_t s1,
               uint64_t s2, uint32_t box0, uint32_t box1, bool kmajor) {
@@ -350,7 +311,8 @@ bool make_map(CUtensorMap *m, const float *base, uint64_t e0, uint64_t e1, uint6
 
 template <int BN>
 size_t tc_smem() {
-  return 1024 + STAGES * (size_t)(2 * BM * BK * 4 + 2 * BN * BK * 4) + 8 * (3 * STAGES + 1) + 16;
+  return 1024 + STAGES * (size_t)(2 * BM * BK * 4 + 2 * BN * BK * 4) + 8 * BOX_BYTES + 8 * (3 * STAGES + 1) +
+         16;
 }
 
 }  // namespace
@@ -398,7 +360,7 @@ cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st, float *ws, size_t ws_flo
     ok = make_map(&mb, g.B, g.N, g.K, b_batched ? g.batch : 1, g.ldb, g.strideB, 32, BK, false);
   if (!ok) return cudaErrorInvalidValue;
   TcParams p{g.M, g.N, g.K, a_k, b_k, g.C, g.ldc, g.strideC, g.alpha, g.beta, a_batched ? 1 : 0,
-             b_batched ? 1 : 0, 1, 0};
+             b_batched ? 1 : 0, 1, 0, 0};
   const int tiles_n = (g.N + BN - 1) / BN, tiles_m = (g.M + BM - 1) / BM;
   const int tiles = tiles_n * tiles_m * g.batch;
   const int kblocks = (g.K + BK - 1) / BK;
@@ -420,15 +382,23 @@ cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st, float *ws, size_t ws_flo
       zdim = splits;
     }
   }
+  // Coalesced epilogue through bulk tensor stores when C allows a tensor map
+  // (16-byte aligned rows) and beta is 0 or 1 (reduce-add in L2).
+  CUtensorMap mc;
+  memset(&mc, 0, sizeof(mc));
+  if ((p.beta == 0.f || p.beta == 1.f) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
+      ((p.ldc | p.strideC) & 3) == 0 &&
+      make_map_sw(&mc, p.C, g.N, g.M, zdim, p.ldc, p.strideC, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B))
+    p.tma_epi = 1;
   dim3 grid(tiles_n, tiles_m, zdim);
   if (BN == 128) {
     const size_t smem = tc_smem<128>();
     cudaFuncSetAttribute(tcgemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    tcgemm_kernel<128><<<grid, TC_THREADS, smem, st>>>(ma, mb, p);
+    tcgemm_kernel<128><<<grid, TC_THREADS, smem, st>>>(ma, mb, mc, p);
   } else {
     const size_t smem = tc_smem<32>();
     cudaFuncSetAttribute(tcgemm_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    tcgemm_kernel<32><<<grid, TC_THREADS, smem, st>>>(ma, mb, p);
+    tcgemm_kernel<32><<<grid, TC_THREADS, smem, st>>>(ma, mb, mc, p);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || p.ksplit <= 1) return e;

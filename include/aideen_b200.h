@@ -246,12 +246,14 @@ int aideen_adjoint_noalloc(const float *hstar, const float *branch, const float 
                            void *stream);
 
 /* ---- diagnostics (no counterpart in the reference) --------------------------
- * Runs the tcgen05 3xTF32 GEMM and the CUDA-core fp32 GEMM on the same seeded
+ * Runs a tcgen05 3xTF32 GEMM and the CUDA-core fp32 GEMM on the same seeded
  * device operands (C = op(A) op(B), row-major, `batch` independent problems)
- * and reports the relative L2 difference and both kernel times.  Allocates
- * its own temporaries. */
+ * and reports the relative L2 difference and both kernel times.  flags bit 0
+ * selects the persistent kernel on pre-split (hi/lo) operands instead of the
+ * in-kernel-split one.  Allocates its own temporaries. */
+#define AIDEEN_SELFTEST_PRESPLIT 1
 int aideen_gemm_selftest(aideen_ctx *ctx, int M, int N, int K, int batch, int trans_a, int trans_b,
-                         float *rel_err, float *ms_tc, float *ms_simt);
+                         int flags, float *rel_err, float *ms_tc, float *ms_simt);
 
 /* ---- multi-GPU (one process per GPU; NCCL over NVLink) ----------------- */
 #define AIDEEN_UNIQUE_ID_BYTES 128

@@ -27,3 +27,23 @@ def test_tensor_core_gemm_matches_fp32(shape):
     print(f"{shape}: rel {err:.2e}  tc {t_tc:.3f} ms  simt {t_simt:.3f} ms")
     assert err < 5e-5   # fp32-level: both kernels round differently over K
     be.close()
+
+
+SPLIT_SHAPES = [
+    # the LM-head shapes (vocab rounded to 4) and smaller / ragged / batched cases
+    (2048, 50260, 512, 1, False, True),    # logits = y . W_lm^T
+    (2048, 512, 50260, 1, False, False),   # dy = dlogits . W_lm (split-K)
+    (50260, 512, 2048, 1, True, False),    # dW_lm = dlogits^T . y
+    (300, 520, 100, 2, False, False),      # ragged M / N / K, batched
+    (256, 256, 64, 3, True, True),         # both operands transposed
+]
+
+
+@pytest.mark.parametrize("shape", SPLIT_SHAPES, ids=lambda s: "x".join(map(str, s[:4])) + f"_t{int(s[4])}{int(s[5])}")
+def test_presplit_persistent_gemm_matches_fp32(shape):
+    M, N, K, B, ta, tb = shape
+    be = GpuDeqBackend(128, 2, 1, 1)
+    err, t_tc, t_simt = be.gemm_selftest(M, N, K, B, ta, tb, presplit=True)
+    print(f"{shape}: rel {err:.2e}  tc {t_tc:.3f} ms  simt {t_simt:.3f} ms")
+    assert err < 5e-5
+    be.close()
