@@ -13,6 +13,7 @@
 //                      + the LM-head RMSNorm input (lm_train.wgsl:100-125)
 //   solve_stats        iteration / non-finite counters
 #include <cooperative_groups.h>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -132,12 +133,23 @@ __device__ __forceinline__ void mv_d_to_32(const float *M0, const float *M1, flo
 #pragma unroll
   for (int q = 0; q < Q; ++q) acc[q] = f4(0.f);
   const int j0 = warp * 128 + g;
+  if (Q == 1) {  // two accumulator chains for latency
+    float4 acc1 = f4(0.f);
 #pragma unroll 8
-  for (int i = 0; i < 32; ++i) {
-    const int j = j0 + 4 * i;
-    const float xj = xs[j];
-    acc[0] = acc[0] + xj * ld4(M0 + (size_t)j * kRank + rq);
-    if (Q > 1) acc[Q - 1] = acc[Q - 1] + xj * ld4(M1 + (size_t)j * kRank + rq);
+    for (int i = 0; i < 32; i += 2) {
+      const int j = j0 + 4 * i;
+      acc[0] = acc[0] + xs[j] * ld4(M0 + (size_t)j * kRank + rq);
+      acc1 = acc1 + xs[j + 4] * ld4(M0 + (size_t)(j + 4) * kRank + rq);
+    }
+    acc[0] = acc[0] + acc1;
+  } else {
+#pragma unroll 8
+    for (int i = 0; i < 32; ++i) {
+      const int j = j0 + 4 * i;
+      const float xj = xs[j];
+      acc[0] = acc[0] + xj * ld4(M0 + (size_t)j * kRank + rq);
+      acc[Q - 1] = acc[Q - 1] + xj * ld4(M1 + (size_t)j * kRank + rq);
+    }
   }
 #pragma unroll
   for (int q = 0; q < Q; ++q) {
@@ -182,6 +194,144 @@ __device__ __forceinline__ void mv2_32_to_d(const float *Ma, const float *ina, c
   yb = b;
 }
 
+// ---- tensor-memory staging of rank-32 FPM matrices (d = 512) ---------------
+// Thread t of the 128-thread block owns TMEM lane t.  A d->32 matrix M[j][r]
+// occupies 128 columns: column 32e + r of lane t holds M[4t+e][r]; a 32->d
+// matrix M[r][o] occupies 128 columns: column 32q + 4rr + e holds
+// M[8q+rr][4t+e].  Loads complete at tmem_wait (which also orders the
+// destination registers after the wait).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+                 "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]),
+                 "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]),
+                 "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// Copy a rank-32 matrix from global memory into this thread's TMEM lane
+// (layouts above); `rows_d` = true for d->32 matrices.
+__device__ __forceinline__ void tmem_stage(uint32_t tlane, const float *M, int d, bool rows_d) {
+  const int t = threadIdx.x;
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t v[32];
+    if (rows_d) {
+      const float *row = M + (size_t)(4 * t + c) * kRank;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 x = ld4(row + 4 * i);
+        v[4 * i] = __float_as_uint(x.x); v[4 * i + 1] = __float_as_uint(x.y);
+        v[4 * i + 2] = __float_as_uint(x.z); v[4 * i + 3] = __float_as_uint(x.w);
+      }
+    } else {
+#pragma unroll
+      for (int rr = 0; rr < 8; ++rr) {
+        const float4 x = ld4(M + (size_t)(8 * c + rr) * d + 4 * t);
+        v[4 * rr] = __float_as_uint(x.x); v[4 * rr + 1] = __float_as_uint(x.y);
+        v[4 * rr + 2] = __float_as_uint(x.z); v[4 * rr + 3] = __float_as_uint(x.w);
+      }
+    }
+    tmem_st32(tlane + 32 * c, v);
+  }
+}
+
+// out[0..32) = Ms . x with Ms in shared memory (mv_d_to_32 layout) and
+// out[32..64) = Mt . x with Mt (d->32) in TMEM at lane-relative column tcol.
+__device__ __forceinline__ void mv_d_to_32_smem_tmem(const float *Ms, uint32_t tcol, float4 x, float *xs,
+                                                     float *out, float *part) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  st4(xs + threadIdx.x * 4, x);
+  __syncthreads();
+  const int g = lane >> 3, rq = (lane & 7) * 4;
+  float4 acc = f4(0.f), acc1 = f4(0.f);  // two chains for latency
+  const int j0 = warp * 128 + g;
+#pragma unroll 8
+  for (int i = 0; i < 32; i += 2) {
+    const int j = j0 + 4 * i;
+    acc = acc + xs[j] * ld4(Ms + (size_t)j * kRank + rq);
+    acc1 = acc1 + xs[j + 4] * ld4(Ms + (size_t)(j + 4) * kRank + rq);
+  }
+  acc = acc + acc1;
+#pragma unroll
+  for (int o = 8; o <= 16; o <<= 1) {
+    acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+    acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
+    acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
+    acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
+  }
+  if (g == 0) st4(part + warp * 64 + rq, acc);
+  float p[32];
+  const float xe[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    uint32_t w[32];
+    tmem_ld32(tcol + 32 * e, w);
+    tmem_wait(w);
+#pragma unroll
+    for (int r = 0; r < 32; ++r) p[r] = (e == 0 ? 0.f : p[r]) + xe[e] * __uint_as_float(w[r]);
+  }
+  part[warp * 64 + 32 + lane] = warp_transpose_reduce32(p);
+  __syncthreads();
+  if (threadIdx.x < 64) {
+    float t = 0.f;
+    for (int w = 0; w < nw; ++w) t += part[w * 64 + threadIdx.x];
+    out[threadIdx.x] = t;
+  }
+  __syncthreads();
+}
+
+// ya = Ma . ina, yb = Mb . inb for two 32->d matrices in TMEM (thread's 4 outputs).
+__device__ __forceinline__ void mv2_32_to_d_tmem(uint32_t ta, const float *ina, uint32_t tb, const float *inb,
+                                                 float4 &ya, float4 &yb) {
+  float4 a = f4(0.f), b = f4(0.f);
+#pragma unroll 1
+  for (int q = 0; q < 4; ++q) {
+    uint32_t wa[32], wb[32];
+    tmem_ld32(ta + 32 * q, wa);
+    tmem_ld32(tb + 32 * q, wb);
+    tmem_wait(wa);
+    tmem_wait(wb);
+#pragma unroll
+    for (int rr = 0; rr < 8; ++rr) {
+      const float xa = ina[8 * q + rr], xb = inb[8 * q + rr];
+      a.x += xa * __uint_as_float(wa[4 * rr]); a.y += xa * __uint_as_float(wa[4 * rr + 1]);
+      a.z += xa * __uint_as_float(wa[4 * rr + 2]); a.w += xa * __uint_as_float(wa[4 * rr + 3]);
+      b.x += xb * __uint_as_float(wb[4 * rr]); b.y += xb * __uint_as_float(wb[4 * rr + 1]);
+      b.z += xb * __uint_as_float(wb[4 * rr + 2]); b.w += xb * __uint_as_float(wb[4 * rr + 3]);
+    }
+  }
+  ya = a;
+  yb = b;
+}
+
 __device__ __forceinline__ float4 sigmoid4(float4 x) {
   return make_float4(1.f / (1.f + expf(-x.x)), 1.f / (1.f + expf(-x.y)), 1.f / (1.f + expf(-x.z)),
                      1.f / (1.f + expf(-x.w)));
@@ -215,7 +365,21 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
   // 0 W_k_mem, 1 W_q_mem, 2 W_k_write, 3 W_retain_up ([d][32]); 4 W_v_write,
   // 5 W_retain_down ([32][d]).  The rest stay in global memory (L2-resident).
   const float *mat[6];
+  uint32_t tmem = 0;
+  __shared__ uint32_t tmem_slot;
   if constexpr (FPM) {
+    if (a.use_tmem) {  // matrices 3..5 in tensor memory, 128 columns each
+      if (threadIdx.x < 32) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         (uint32_t)__cvta_generic_to_shared(&tmem_slot)),
+                     "r"(512u));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncthreads();
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      tmem = tmem_slot + ((uint32_t)(threadIdx.x & ~31) << 16);  // this warp's lane quadrant
+    }
     const size_t ms = (size_t)s * d * kRank;
     const float *src[6] = {W + a.off_wkm + ms, W + a.off_wqm + ms, W + a.off_wkw + ms,
                            W + a.off_wup + ms, W + a.off_wvw + ms, W + a.off_wdown + ms};
@@ -226,6 +390,12 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
       if (res)
         for (int q = threadIdx.x * 4; q < d * kRank; q += blockDim.x * 4) st4(dst + q, ld4(src[i] + q));
       mat[i] = res ? dst : src[i];
+    }
+    if (a.use_tmem) {
+      tmem_stage(tmem + 0, mat[3], d, true);     // W_retain_up  [d][32]
+      tmem_stage(tmem + 128, mat[4], d, false);  // W_v_write    [32][d]
+      tmem_stage(tmem + 256, mat[5], d, false);  // W_retain_down [32][d]
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     }
     m = ld4(a.mstate + ((size_t)b * h + s) * d + j0);
     st4(mbuf + j0, m);
@@ -244,37 +414,64 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
     mv_d_to_32<1>(mat[0], nullptr, m + hs4 * tanh4(m) + hb4, xs, keybuf, part);
   }
   const float band = fmaxf(a.eps, 0.15f * 0.2f);
+  // loop-invariant FPM write parameters of this slot
+  if constexpr (FPM) {
+    // the prologue's memory and read key are published: split cluster barrier,
+    // waited on before the first remote read
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  }
 #ifdef AIDEEN_PICARD_PROF
   long long _pt = clock64();
   long long _pacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #endif
+  // rows of the next token, loaded one token ahead
+  const size_t e0 = ((size_t)b * T * h + s) * d + j0;
+  float4 sig_nx = ld4(a.signal + e0);
+  float4 A4_nx = a.slot_coord ? ld4(a.A + e0) : f4(0.f);
+  // sum of squares of the next token's iteration-0 `dep` and `signal`,
+  // reduced together with the previous token's last block reduction
+  float dep0_sq = 0.f, sig_sq = 0.f;
   for (int t = 0; t < T; ++t) {
     const size_t n = (size_t)b * T + t;
     const size_t e = (n * h + s) * d + j0;
-    const float4 sig = ld4(a.signal + e);
-    const float4 A4 = a.slot_coord ? ld4(a.A + e) : f4(0.f);
+    const float4 sig = sig_nx;
+    const float4 A4 = A4_nx;
+    if (t + 1 < T) {
+      sig_nx = ld4(a.signal + e + (size_t)h * d);
+      if (a.slot_coord) A4_nx = ld4(a.A + e + (size_t)h * d);
+    }
     if (t == 0) {
       float v[1] = {dot4(sig, sig)};
       R.sum(v);
       const float den = fmaxf(sqrtf(v[0] * inv_d + 1e-6f), 1e-6f);
       hcur = make_float4(sig.x / den, sig.y / den, sig.z / den, sig.w / den);
+      sig_sq = v[0];
+    }
+    if (t == 0 || !FPM) {
+      const float4 dep0 = sig + hcur + anc + A4;
+      float v[1] = {dot4(dep0, dep0)};
+      R.sum(v);
+      dep0_sq = v[0];
+      if (!FPM && t > 0) sig_sq = 0.f;  // only the FPM read uses it
     }
     float4 ctx = f4(0.f);
-    if constexpr (FPM) {
-      cg::this_cluster().sync();  // every slot's key + memory for this token is visible
-    }
+    bool waited = false;  // this token's cluster-barrier wait
     PT(0);
     float prev = 1.f;
     int it = 0;
     bool conv = false;
+    float rr = sqrtf(dep0_sq * inv_d + 1e-6f);
+    float hq_sq = 0.f;
     while (it < a.max_iters && !conv) {
       if constexpr (FPM) {
         if (it == 1) {
+          // every slot's key + memory for this token is visible past this wait
+          asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+          waited = true;
+          PT(0);
           // Model-A memory read from the first structured state (:1031-1200)
-          float v2[2] = {dot4(hcur, hcur), dot4(sig, sig)};
-          R.sum(v2);
-          const float hq = sqrtf(fmaxf(v2[0], 1e-6f));
-          const float sig_norm = sqrtf(fmaxf(v2[1], 1e-6f));
+          const float hq = sqrtf(fmaxf(hq_sq, 1e-6f));
+          const float sig_norm = sqrtf(fmaxf(sig_sq, 1e-6f));
           mv_d_to_32<1>(mat[1], nullptr,
                         make_float4(hcur.x / hq, hcur.y / hq, hcur.z / hq, hcur.w / hq), xs, vec, part);
           PT(6);
@@ -337,20 +534,28 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
           PT(2);
         }
       }
-      float4 dep = sig + hcur + anc;
-      if (it == 0) dep = dep + A4;
-      float4 pre = dep;
+      float4 pre = sig + hcur + anc;
+      if (it == 0) pre = pre + A4;
       if (FPM && it >= 1) pre = pre + ctx;
-      float v1[1] = {dot4(dep, dep)};
-      R.sum(v1);
-      const float rr = sqrtf(v1[0] * inv_d + 1e-6f);
       const float4 f = make_float4(NS.x * (pre.x / rr), NS.y * (pre.y / rr), NS.z * (pre.z / rr),
                                    NS.w * (pre.w / rr));
       const float4 hn = a.blend * f + (1.f - a.blend) * hcur;
       const float4 dh = hn - hcur;
-      float v2[1] = {dot4(dh, dh)};
-      R.sum(v2);
+      // one reduction per iteration: |dh|^2 of this iteration, |dep|^2 of the
+      // next one (dep has no attention term after iteration 0) and, after
+      // iteration 0 with FPM, |h|^2 for the memory read's query
+      const float4 dep_nx = sig + hn + anc;
+      float v2[3] = {dot4(dh, dh), dot4(dep_nx, dep_nx), dot4(hn, hn)};
+      if (FPM && it == 0) R.sum(v2);
+      else {
+        float v2b[2] = {v2[0], v2[1]};
+        R.sum(v2b);
+        v2[0] = v2b[0];
+        v2[1] = v2b[1];
+      }
       const float err = sqrtf(v2[0] * inv_d + 1e-12f) / fmaxf(rr, 1e-6f);
+      rr = sqrtf(v2[1] * inv_d + 1e-6f);
+      hq_sq = v2[2];
       hcur = hn;
       const bool strict = err < a.eps;
       const float plateau = fabsf(err - prev) / fmaxf(prev, a.eps);
@@ -367,20 +572,34 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
     if (threadIdx.x == 0) a.iters[n * h + s] = it;
     PT(3);
     if constexpr (FPM) {
+      if (!waited) {  // solve stopped before the memory read: still consume this token's barrier phase
+        asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+        PT(0);
+      }
       st4(a.fpmctx + e, ctx);
       // post-solve memory write (:1965-2140)
       const float4 c = 0.5f * (hcur + sig);
       PT(4);
-      mv_d_to_32<2>(mat[2], mat[3], c, xs, vec, part);   // bottleneck | retain-up
-      PT(5);
       float4 pv, dv;
-      mv2_32_to_d(mat[4], vec, mat[5], vec + 32, d, pv, dv);
+      if (a.use_tmem) {
+        mv_d_to_32_smem_tmem(mat[2], tmem + 0, c, xs, vec, part);   // bottleneck | retain-up
+        PT(5);
+        mv2_32_to_d_tmem(tmem + 128, vec, tmem + 256, vec + 32, pv, dv);
+      } else {
+        mv_d_to_32<2>(mat[2], mat[3], c, xs, vec, part);   // bottleneck | retain-up
+        PT(5);
+        mv2_32_to_d(mat[4], vec, mat[5], vec + 32, d, pv, dv);
+      }
       PT(6);
       const float4 prop = tanh4(ld4(W + a.off_bdelta + (size_t)s * d + j0) + pv);
       const float4 df = prop - m;
-      float v3[4] = {dot4(m, m), dot4(df, df), dot4(hcur, hcur),
-                     dot4(ld4(W + a.off_wgate + (size_t)s * d + j0), c)};
+      // the next token's iteration-0 |dep|^2 and |signal|^2 ride along
+      const float4 dep0n = sig_nx + hcur + anc + A4_nx;
+      float v3[6] = {dot4(m, m), dot4(df, df), dot4(hcur, hcur), dot4(ld4(W + a.off_wgate + (size_t)s * d + j0), c), dot4(dep0n, dep0n),
+                     dot4(sig_nx, sig_nx)};
       R.sum(v3);
+      dep0_sq = v3[4];
+      sig_sq = v3[5];
       const float h_rms = sqrtf(fmaxf(v3[2] * inv_d, 1e-6f));
       const float4 hu = make_float4(hcur.x / h_rms, hcur.y / h_rms, hcur.z / h_rms, hcur.w / h_rms);
       const float raw_z = 1.f / (1.f + expf(-(v3[3] * rsqrtf((float)d) + W[a.off_bwrite + s] - 1.5f)));
@@ -402,6 +621,8 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
       mv_d_to_32<1>(mat[0], nullptr, m + hs4 * tanh4(m) + hb4, xs, keybuf + (cur ^ 1) * 32, part);
       PT(7);
       cur ^= 1;
+      // publish this token's memory and key to the cluster
+      asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
       PT(4);
     }
   }
@@ -411,7 +632,14 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
 #endif
   if constexpr (FPM) {
     st4(a.mstate + ((size_t)b * h + s) * d + j0, m);
-    cg::this_cluster().sync();  // keep shared memory alive for remote readers
+    // match the last arrive: peers may read this block's memory until they pass it
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (a.use_tmem) {
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncthreads();
+      if (threadIdx.x < 32)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_slot), "r"(512u));
+    }
   }
 }
 
@@ -498,6 +726,9 @@ cudaError_t launch_picard(const PicardArgs &a, bool fpm, cudaStream_t st) {
     smem += mat_bytes;
     ++p.n_resident;
   }
+  // d = 512: the three matrices that do not fit in shared memory go to tensor
+  // memory (one 128-thread block per SM owns all 512 columns)
+  p.use_tmem = (a.d == 512 && p.n_resident == 3 && !getenv("AIDEEN_PICARD_NO_TMEM")) ? 1 : 0;
   e = cudaFuncSetAttribute(picard_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};

@@ -52,6 +52,7 @@ struct AttnArgs {
 struct PicardArgs {
   int B, T, h, d, max_iters, slot_coord;
   int n_resident;  // FPM matrices staged in shared memory (set by the launcher)
+  int use_tmem;    // 1: matrices 3..5 live in tensor memory (d = 512, n_resident = 3)
   float eps, blend, alpha_m, tau, gate_min;
   const float *W;
   size_t off_ns, off_anchor, off_hscale, off_hbias, off_wkm, off_wqm, off_bread, off_wgate,
