@@ -76,6 +76,7 @@ _SIGS = {
     "aideen_sync": (C.c_int, [_P]),
     "aideen_launch_count": (C.c_uint64, [_P]),
     "aideen_profile": (C.c_int, [_P, C.c_int]),
+    "aideen_join": (C.c_int, [_P]),
     "aideen_profile_read": (C.c_int, [_P, _P, _P, C.c_int]),
     "aideen_all_weights_len": (C.c_size_t, [C.c_uint32, C.c_uint32]),
     "aideen_upload_weights": (C.c_int, [_P, _P, C.c_size_t, C.c_int]),
@@ -192,6 +193,10 @@ class GpuDeqBackend:
             self.close()
         except Exception:
             pass
+
+    def join(self):
+        """Order the deferred LM-head update before later work on the context stream."""
+        self._check(self.lib.aideen_join(self.ctx), "join")
 
     def sync(self):
         self._check(self.lib.aideen_sync(self.ctx), "sync")

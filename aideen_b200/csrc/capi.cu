@@ -67,6 +67,11 @@ struct aideen_ctx {
   int device = 0;
   cudaStream_t stream = nullptr;
   bool own_stream = false;
+  // side stream for the LM-head update (+ its hi/lo split), which only the
+  // next LM-head call needs: it overlaps the next step's forward
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_grads = nullptr, ev_lm_done = nullptr;
+  bool lm_pending = false;
   ncclComm_t comm = nullptr;
   int nranks = 1, rank = 0;
   std::string err;
@@ -100,6 +105,13 @@ namespace {
 int set_err(aideen_ctx *c, int code, const std::string &msg) {
   if (c) c->err = msg;
   return code;
+}
+
+// Make the context stream wait for a deferred LM-head update on the side stream.
+cudaError_t join_side(aideen_ctx *c) {
+  if (!c->lm_pending) return cudaSuccess;
+  c->lm_pending = false;
+  return cudaStreamWaitEvent(c->stream, c->ev_lm_done, 0);
 }
 
 #define CU(expr)                                                                       \
@@ -266,6 +278,7 @@ int run_lm_head(aideen_ctx *ctx, int N, float *loss_out) {
   cudaStream_t st = ctx->stream;
   const float *Wlm = b.lmp, *glm = b.lmp + ctx->lm_g;
   const long Vp = ctx->Vp;
+  CU(join_side(ctx));
   KL(launch_count_active(b.targets, N, b.scal, st));
   // The three LM-head GEMMs run on pre-split operands: W_lm halves are
   // refreshed once per change of W_lm, y and y^T halves per call (y^T makes
@@ -486,6 +499,32 @@ int run_allreduce(aideen_ctx *ctx, int timeout_ms) {
   }
 }
 
+// LM-head update and the refresh of its pre-split copies.  Without profiling
+// it runs on the side stream, ordered after the gradients (and their
+// allreduce) on the context stream; the next LM-head call joins it.
+int run_lm_update(aideen_ctx *ctx, const aideen_update *u, float bc1, float bc2) {
+  DevBufs &b = ctx->b;
+  const bool deferred = !ctx->prof;
+  cudaStream_t ls = deferred ? ctx->side : ctx->stream;
+  CU(join_side(ctx));
+  if (deferred) {
+    CU(cudaEventRecord(ctx->ev_grads, ctx->stream));
+    CU(cudaStreamWaitEvent(ctx->side, ctx->ev_grads, 0));
+  }
+  if (u->rule == AIDEEN_RULE_ADAM)
+    KL(launch_adam(b.lmp, b.Glm, b.Mlm1, b.Mlm2, ctx->lm_len, u->lr, u->beta1, u->beta2, u->eps, bc1, bc2,
+                   u->grad_scale, ls));
+  else
+    KL(launch_clipped_sgd(b.lmp, b.Glm, ctx->lm_len, ctx->lm_len, u->lr, u->weight_decay, u->grad_scale, ls));
+  KL(launch_split_hilo(b.lmp, b.whi, b.wlo, (size_t)ctx->cfg.vocab * ctx->cfg.d_model, ls));
+  ctx->lm_split_stale = false;
+  if (deferred) {
+    CU(cudaEventRecord(ctx->ev_lm_done, ctx->side));
+    ctx->lm_pending = true;
+  }
+  return AIDEEN_OK;
+}
+
 int run_update(aideen_ctx *ctx, const aideen_update *u) {
   if (!u) return set_err(ctx, AIDEEN_E_INVALID, "null update");
   if (u->allreduce) CHK(run_allreduce(ctx, 0));
@@ -497,18 +536,10 @@ int run_update(aideen_ctx *ctx, const aideen_update *u) {
     const float bc2 = (float)(1.0 - std::pow((double)u->beta2, t));
     KL(launch_adam(b.W, b.G, b.M1, b.M2, ctx->W_len, u->lr, u->beta1, u->beta2, u->eps, bc1, bc2,
                    u->grad_scale, st));
-    if (u->update_lm_head && ctx->lm_ready) {
-      KL(launch_adam(b.lmp, b.Glm, b.Mlm1, b.Mlm2, ctx->lm_len, u->lr, u->beta1, u->beta2, u->eps,
-                     bc1, bc2, u->grad_scale, st));
-      ctx->lm_split_stale = true;
-    }
+    if (u->update_lm_head && ctx->lm_ready) CHK(run_lm_update(ctx, u, bc1, bc2));
   } else if (u->rule == AIDEEN_RULE_CLIPPED_SGD) {
     KL(launch_clipped_sgd(b.W, b.G, ctx->W_len, ctx->P.hist, u->lr, u->weight_decay, u->grad_scale, st));
-    if (u->update_lm_head && ctx->lm_ready) {
-      KL(launch_clipped_sgd(b.lmp, b.Glm, ctx->lm_len, ctx->lm_len, u->lr, u->weight_decay,
-                            u->grad_scale, st));
-      ctx->lm_split_stale = true;
-    }
+    if (u->update_lm_head && ctx->lm_ready) CHK(run_lm_update(ctx, u, 0.f, 0.f));
   } else {
     return set_err(ctx, AIDEEN_E_INVALID, "unknown update rule");
   }
@@ -578,6 +609,9 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   }
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
   ctx->own_stream = true;
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_grads, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_lm_done, cudaEventDisableTiming);
   if (e != cudaSuccess) {
     aideen_destroy(ctx);
     return fail(AIDEEN_E_CUDA);
@@ -618,12 +652,17 @@ void aideen_destroy(aideen_ctx *ctx) {
                   b.dlog_lo, b.yhi, b.ylo, b.yThi, b.yTlo, b.whi, b.wlo, b.colpart};
   for (void *p : ptrs)
     if (p) cudaFree(p);
+  if (ctx->side) cudaStreamSynchronize(ctx->side);
   if (ctx->stream && ctx->own_stream) cudaStreamDestroy(ctx->stream);
+  if (ctx->side) cudaStreamDestroy(ctx->side);
+  if (ctx->ev_grads) cudaEventDestroy(ctx->ev_grads);
+  if (ctx->ev_lm_done) cudaEventDestroy(ctx->ev_lm_done);
   delete ctx;
 }
 
 int aideen_set_stream(aideen_ctx *ctx, void *s) {
   if (!ctx) return AIDEEN_E_INVALID;
+  CU(join_side(ctx));
   CU(cudaStreamSynchronize(ctx->stream));
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   ctx->stream = (cudaStream_t)s;
@@ -657,8 +696,15 @@ int aideen_profile_read(aideen_ctx *ctx, float *ms, uint64_t *launches, int rese
   return AIDEEN_OK;
 }
 
+int aideen_join(aideen_ctx *ctx) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  CU(join_side(ctx));
+  return AIDEEN_OK;
+}
+
 int aideen_sync(aideen_ctx *ctx) {
   if (!ctx) return AIDEEN_E_INVALID;
+  CU(join_side(ctx));
   CU(cudaStreamSynchronize(ctx->stream));
   return AIDEEN_OK;
 }
@@ -715,6 +761,7 @@ int aideen_upload_lm_head(aideen_ctx *ctx, const float *w_lm, const float *b_lm,
   if (!ctx) return AIDEEN_E_INVALID;
   const size_t V = ctx->cfg.vocab, d = ctx->cfg.d_model;
   if (!V) return set_err(ctx, AIDEEN_E_INVALID, "context created with vocab = 0");
+  CU(join_side(ctx));
   CHK(copy_in(ctx, ctx->b.lmp, w_lm, V * d * sizeof(float), AIDEEN_HOST));
   CHK(copy_in(ctx, ctx->b.lmp + ctx->lm_b, b_lm, V * sizeof(float), AIDEEN_HOST));
   CHK(copy_in(ctx, ctx->b.lmp + ctx->lm_g, g_lm, d * sizeof(float), AIDEEN_HOST));
@@ -726,6 +773,7 @@ int aideen_upload_lm_head(aideen_ctx *ctx, const float *w_lm, const float *b_lm,
 
 int aideen_download_lm_head(aideen_ctx *ctx, float *w_lm, float *b_lm, float *g_lm) {
   if (!ctx || !ctx->lm_ready) return set_err(ctx, AIDEEN_E_INVALID, "no LM head");
+  CU(join_side(ctx));
   const size_t V = ctx->cfg.vocab, d = ctx->cfg.d_model;
   if (w_lm) CU(cudaMemcpyAsync(w_lm, ctx->b.lmp, V * d * 4, cudaMemcpyDeviceToHost, ctx->stream));
   if (b_lm) CU(cudaMemcpyAsync(b_lm, ctx->b.lmp + ctx->lm_b, V * 4, cudaMemcpyDeviceToHost, ctx->stream));
@@ -755,6 +803,7 @@ int aideen_reset_state(aideen_ctx *ctx) {
 
 int aideen_reset_optimizer(aideen_ctx *ctx) {
   if (!ctx) return AIDEEN_E_INVALID;
+  CU(join_side(ctx));
   CU(cudaMemsetAsync(ctx->b.M1, 0, ctx->W_len * 4, ctx->stream));
   CU(cudaMemsetAsync(ctx->b.M2, 0, ctx->W_len * 4, ctx->stream));
   if (ctx->lm_len) {
@@ -931,6 +980,7 @@ static void *buf_ptr(aideen_ctx *ctx, int which, size_t *count) {
 
 int aideen_read(aideen_ctx *ctx, int which, void *dst, size_t n) {
   if (!ctx || !dst) return AIDEEN_E_INVALID;
+  CU(join_side(ctx));
   size_t count = 0;
   void *p = buf_ptr(ctx, which, &count);
   if (!p) return set_err(ctx, AIDEEN_E_INVALID, "unknown or absent buffer");
@@ -953,6 +1003,7 @@ int aideen_read(aideen_ctx *ctx, int which, void *dst, size_t n) {
 
 void *aideen_device_ptr(aideen_ctx *ctx, int which) {
   if (!ctx) return nullptr;
+  join_side(ctx);
   size_t count = 0;
   return buf_ptr(ctx, which, &count);
 }

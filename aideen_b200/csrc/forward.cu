@@ -460,7 +460,8 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
     float prev = 1.f;
     int it = 0;
     bool conv = false;
-    float rr = sqrtf(dep0_sq * inv_d + 1e-6f);
+    // 1 / rms(dep) of the current iteration (one reciprocal instead of 4 divisions)
+    float irr = 1.f / sqrtf(dep0_sq * inv_d + 1e-6f);
     float hq_sq = 0.f;
     while (it < a.max_iters && !conv) {
       if constexpr (FPM) {
@@ -470,10 +471,9 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
           waited = true;
           PT(0);
           // Model-A memory read from the first structured state (:1031-1200)
-          const float hq = sqrtf(fmaxf(hq_sq, 1e-6f));
+          const float ihq = 1.f / sqrtf(fmaxf(hq_sq, 1e-6f));
           const float sig_norm = sqrtf(fmaxf(sig_sq, 1e-6f));
-          mv_d_to_32<1>(mat[1], nullptr,
-                        make_float4(hcur.x / hq, hcur.y / hq, hcur.z / hq, hcur.w / hq), xs, vec, part);
+          mv_d_to_32<1>(mat[1], nullptr, ihq * hcur, xs, vec, part);
           PT(6);
           cg::cluster_group cl = cg::this_cluster();
           if (threadIdx.x < 32) {
@@ -537,8 +537,7 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
       float4 pre = sig + hcur + anc;
       if (it == 0) pre = pre + A4;
       if (FPM && it >= 1) pre = pre + ctx;
-      const float4 f = make_float4(NS.x * (pre.x / rr), NS.y * (pre.y / rr), NS.z * (pre.z / rr),
-                                   NS.w * (pre.w / rr));
+      const float4 f = NS * (irr * pre);
       const float4 hn = a.blend * f + (1.f - a.blend) * hcur;
       const float4 dh = hn - hcur;
       // one reduction per iteration: |dh|^2 of this iteration, |dep|^2 of the
@@ -553,13 +552,14 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
         v2[0] = v2b[0];
         v2[1] = v2b[1];
       }
-      const float err = sqrtf(v2[0] * inv_d + 1e-12f) / fmaxf(rr, 1e-6f);
-      rr = sqrtf(v2[1] * inv_d + 1e-6f);
+      // rms(dep) >= 1e-3 always (the 1e-6 floor), so max(rms, 1e-6) = rms
+      const float err = sqrtf(v2[0] * inv_d + 1e-12f) * irr;
+      irr = 1.f / sqrtf(v2[1] * inv_d + 1e-6f);
       hq_sq = v2[2];
       hcur = hn;
       const bool strict = err < a.eps;
-      const float plateau = fabsf(err - prev) / fmaxf(prev, a.eps);
-      const bool homeo = (it + 1 >= 4) && (err <= band) && (plateau <= 0.10f);
+      // plateau = |err - prev| / max(prev, eps) <= 0.10, without the division
+      const bool homeo = (it + 1 >= 4) && (err <= band) && (fabsf(err - prev) <= 0.10f * fmaxf(prev, a.eps));
       conv = strict || homeo;
       prev = err;
       ++it;
@@ -600,8 +600,7 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
       R.sum(v3);
       dep0_sq = v3[4];
       sig_sq = v3[5];
-      const float h_rms = sqrtf(fmaxf(v3[2] * inv_d, 1e-6f));
-      const float4 hu = make_float4(hcur.x / h_rms, hcur.y / h_rms, hcur.z / h_rms, hcur.w / h_rms);
+      const float4 hu = (1.f / sqrtf(fmaxf(v3[2] * inv_d, 1e-6f))) * hcur;
       const float raw_z = 1.f / (1.f + expf(-(v3[3] * rsqrtf((float)d) + W[a.off_bwrite + s] - 1.5f)));
       const float z = fminf(fmaxf(raw_z, 0.f), 1.f);
       const float prev_norm = sqrtf(fmaxf(v3[0], 1e-6f));

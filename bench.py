@@ -248,21 +248,27 @@ def main():
     torch.cuda.synchronize()
 
     def timed(where):
-        ev = []
+        # One timed region over all K steps, so the LM-head update the library
+        # defers to its side stream (it overlaps the next step's forward) is
+        # counted; the L2 flush between consecutive steps sits inside the region
+        # and its time counts against the steps.
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
-        for _ in range(args.steps):
-            with torch.cuda.stream(stream):
-                flush.zero_()
-                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                s.record(stream)
+        with torch.cuda.stream(stream):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+        for k in range(args.steps):
+            if k:
+                with torch.cuda.stream(stream):
+                    flush.zero_()
             step(where)
-            with torch.cuda.stream(stream):
-                e.record(stream)
-            ev.append((s, e))
+        be.join()
+        with torch.cuda.stream(stream):
+            e.record(stream)
         torch.cuda.synchronize()
-        ms = sum(s.elapsed_time(e) for s, e in ev)
+        ms = s.elapsed_time(e)
         if world > 1:
             t = torch.tensor([ms], device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -332,7 +338,7 @@ def main():
                            "d_r": D, "h_slots": H, "ctx": T, "batch_per_gpu": B_PER_GPU,
                            "global_batch": B_PER_GPU * world, "vocab": VOCAB,
                            "max_iters": MAX_ITERS, "adj_iters": ADJ_ITERS, "anderson_m": ANDERSON_M,
-                           "parallelism": f"dp{world}", "l2": "256 MB buffer flushed before every timed step"},
+                           "parallelism": f"dp{world}", "l2": "256 MB buffer written before every step, inside the timed region"},
                 "e2e": {"value": e2e, "unit": "tokens/s",
                         "h2d_bytes_per_step": int(tok.nbytes + tg.nbytes), "d2h_bytes_per_step": 4},
                 "gpu_launches": int(launches),

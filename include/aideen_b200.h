@@ -110,6 +110,11 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status);
 void aideen_destroy(aideen_ctx *ctx);
 const char *aideen_last_error(const aideen_ctx *ctx);
 int aideen_set_stream(aideen_ctx *ctx, void *cuda_stream);
+/* Make the context stream wait for work the library deferred to its side
+ * stream (the LM-head update of the last apply, which otherwise overlaps the
+ * next forward).  Stream-ordered, no host wait; aideen_sync and every read
+ * of LM-head state do it implicitly. */
+int aideen_join(aideen_ctx *ctx);
 int aideen_sync(aideen_ctx *ctx);
 /* Number of this library's own kernel launches issued since create. */
 uint64_t aideen_launch_count(const aideen_ctx *ctx);
