@@ -1,3 +1,4 @@
+#include <cooperative_groups.h>
 // Fused optimizer sweeps, spectral renormalisation and LM-head helpers.
 //
 //   adam        bias-corrected Adam, one float4 pass over w, g, m, v
@@ -10,6 +11,8 @@
 //               (lm_train.wgsl:79-130, 327-395)
 #include "common.cuh"
 #include "kernels.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace aideen {
 
@@ -139,11 +142,130 @@ __global__ void __launch_bounds__(1024) spectral_kernel(SpecArgs a) {
   }
 }
 
+// Cluster variant for d <= 512: a cluster of 8 CTAs per matrix, CTA q of the
+// cluster keeping rows [q*R, (q+1)*R) (R = d/8) in shared memory for all the
+// power iterations.  Per iteration: v = A^T u from per-CTA partials summed
+// through distributed shared memory (each CTA owns a column slice), then
+// u = A v on the local rows; the norms are summed across the cluster.  The
+// arithmetic is the single-CTA kernel's (same sums, same normalisations).
+constexpr int kSpecCluster = 8;
+
+__global__ void __launch_bounds__(256) spectral_cluster_kernel(SpecArgs a) {
+  extern __shared__ __align__(16) float smc[];
+  cg::cluster_group cl = cg::this_cluster();
+  const int d = a.d, h = a.h, R = d / kSpecCluster;
+  const int q = (int)cl.block_rank();
+  const int mi = blockIdx.x / kSpecCluster;
+  float *Ms = smc;                 // R x d
+  float *vpart = Ms + (size_t)R * d;  // d   partial A^T u over local rows
+  float *vslice = vpart + d;       // R   reduced column slice [q*R, (q+1)*R)
+  float *vfull = vslice + R;       // d
+  float *uloc = vfull + d;         // R
+  float *nrm = uloc + R;           // [0] slice |v|^2, [1] local |u|^2
+  float *red = nrm + 4;            // 32
+  size_t off;
+  float thr;
+  if (mi < h) { off = a.wq + (size_t)mi * d * d; thr = a.attn; }
+  else if (mi < 2 * h) { off = a.wk + (size_t)(mi - h) * d * d; thr = a.attn; }
+  else if (mi < 3 * h) { off = a.wv + (size_t)(mi - 2 * h) * d * d; thr = a.wvth; }
+  else if (mi < 4 * h) { off = a.wo + (size_t)(mi - 3 * h) * d * d; thr = a.woth; }
+  else if (mi < 5 * h) { off = a.win + (size_t)(mi - 4 * h) * d * d; thr = a.winth; }
+  else if (mi == 5 * h) { off = a.wx; thr = a.fpm; }
+  else { off = a.wout; thr = a.fpm; }
+  float *M = a.W + off + (size_t)q * R * d;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  for (int i = tid * 4; i < R * d; i += blockDim.x * 4) st4(Ms + i, ld4(M + i));
+  const float u0 = 1.f / sqrtf((float)d);
+  for (int i = tid; i < R; i += blockDim.x) uloc[i] = u0;
+  __syncthreads();
+  float sigma = 1.f;
+  for (int it = 0; it < a.n_iters; ++it) {
+    // partial v over the local rows
+    for (int c = tid; c < d; c += blockDim.x) {
+      float acc = 0.f;
+      for (int r = 0; r < R; ++r) acc += Ms[(size_t)r * d + c] * uloc[r];
+      vpart[c] = acc;
+    }
+    cl.sync();
+    // this CTA's column slice, summed over the cluster in rank order
+    float part = 0.f;
+    for (int i = tid; i < R; i += blockDim.x) {
+      float acc = 0.f;
+      for (int p = 0; p < kSpecCluster; ++p) acc += cl.map_shared_rank(vpart, p)[q * R + i];
+      vslice[i] = acc;
+      part += acc * acc;
+    }
+    part = warp_sum(part);
+    if (lane == 0) red[warp] = part;
+    __syncthreads();
+    if (tid == 0) {
+      float t = 0.f;
+      for (int w = 0; w < nw; ++w) t += red[w];
+      nrm[0] = t;
+    }
+    cl.sync();
+    float vn2 = 0.f;
+    for (int p = 0; p < kSpecCluster; ++p) vn2 += cl.map_shared_rank(nrm, p)[0];
+    const float vn = sqrtf(vn2 + 1e-12f);
+    for (int c = tid; c < d; c += blockDim.x) vfull[c] = cl.map_shared_rank(vslice, c / R)[c % R] / vn;
+    __syncthreads();
+    // u = A v on the local rows, warp per row
+    float upart = 0.f;
+    for (int r = warp; r < R; r += nw) {
+      float acc = 0.f;
+      for (int c = lane; c < d; c += 32) acc += Ms[(size_t)r * d + c] * vfull[c];
+      acc = warp_sum(acc);
+      if (lane == 0) { uloc[r] = acc; upart += acc * acc; }
+    }
+    if (lane == 0) red[warp] = upart;
+    __syncthreads();
+    if (tid == 0) {
+      float t = 0.f;
+      for (int w = 0; w < nw; ++w) t += red[w];
+      nrm[1] = t;
+    }
+    cl.sync();
+    float un2 = 0.f;
+    for (int p = 0; p < kSpecCluster; ++p) un2 += cl.map_shared_rank(nrm, p)[1];
+    sigma = sqrtf(un2 + 1e-12f);
+    for (int r = tid; r < R; r += blockDim.x) uloc[r] /= sigma;
+    __syncthreads();
+  }
+  if (tid == 0 && q == 0 && a.sigmas) a.sigmas[mi] = sigma;
+  if (sigma > thr) {
+    const float sc = thr / sigma;
+    for (int i = tid * 4; i < R * d; i += blockDim.x * 4) st4(M + i, sc * ld4(Ms + i));
+  }
+  cl.sync();  // peers' last remote reads of this CTA's norms are done
+}
+
 cudaError_t launch_spectral(float *W, int d, int h, const Layout &L, int n_iters, float attn,
                             float win, float fpm, float wv, float wo, float *sigmas,
                             cudaStream_t st) {
   SpecArgs a{W, d, h, n_iters, L.wq, L.wk, L.wv, L.wo, L.win, L.wx, L.wout,
              attn, win, fpm, wv, wo, sigmas};
+  if (d % kSpecCluster == 0 && d <= 512) {
+    const int R = d / kSpecCluster;
+    const size_t smem = ((size_t)R * d + 2 * (size_t)d + 2 * (size_t)R + 4 + 32) * sizeof(float);
+    cudaError_t e = cudaFuncSetAttribute(spectral_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((5 * h + 2) * kSpecCluster);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kSpecCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, spectral_cluster_kernel, a);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+  }
   const size_t smem = (2 * (size_t)d + 64) * sizeof(float);
   spectral_kernel<<<5 * h + 2, 1024, smem, st>>>(a);
   return cudaGetLastError();
