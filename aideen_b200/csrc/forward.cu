@@ -117,35 +117,44 @@ __global__ void attn_scale_kernel(AttnArgs a, int rows) {
   if (lane == 0) { a.scale[w] = sc; a.rho[w] = rho; a.Rsrc[w] = R; }
 }
 
+// ---- Picard element ownership ---------------------------------------------
+// The block has d/2 threads; thread t = hf * (d/4) + l (hf = 0, 1) owns the
+// float2 at j0 = 4 l + 2 hf.  With d = 512 this pairs warps w and w + 4 on the
+// same TMEM lane quadrant (lane l), each using half of the lane's columns.
+__device__ __forceinline__ int picard_j0() {
+  const int th = blockDim.x >> 1;
+  return 4 * (threadIdx.x % th) + 2 * (threadIdx.x / th);
+}
+
 // y_q[r] = sum_j Mq[j*32 + r] x[j], r < 32, for Q (1 or 2) matrices sharing x.
-// Each thread stages its float4 of x in xs; then lane l of warp w reads rows
-// j = w*128 + 4*i + (l>>3), columns 4*(l&7)..+3, so one warp load covers four
-// whole 128-byte rows (coalesced, conflict-free in shared memory).  Results
-// land in out[q*32 + r].  Three block barriers.
+// Each thread stages its float2 of x in xs; then lane l of warp w reads rows
+// j = 64 w + 4 i + (l >> 3), columns 4 (l & 7)..+3, so one warp load covers
+// four whole 128-byte rows (coalesced, conflict-free in shared memory); every
+// warp covers 64 rows.  Results land in out[q*32 + r].  Three block barriers.
 template <int Q>
-__device__ __forceinline__ void mv_d_to_32(const float *M0, const float *M1, float4 x, float *xs,
+__device__ __forceinline__ void mv_d_to_32(const float *M0, const float *M1, float2 x, int j0, float *xs,
                                            float *out, float *part) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  st4(xs + threadIdx.x * 4, x);
+  st2(xs + j0, x);
   __syncthreads();
   const int g = lane >> 3, rq = (lane & 7) * 4;
   float4 acc[Q];
 #pragma unroll
   for (int q = 0; q < Q; ++q) acc[q] = f4(0.f);
-  const int j0 = warp * 128 + g;
+  const int jb = warp * 64 + g;
   if (Q == 1) {  // two accumulator chains for latency
     float4 acc1 = f4(0.f);
-#pragma unroll 8
-    for (int i = 0; i < 32; i += 2) {
-      const int j = j0 + 4 * i;
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      const int j = jb + 4 * i;
       acc[0] = acc[0] + xs[j] * ld4(M0 + (size_t)j * kRank + rq);
       acc1 = acc1 + xs[j + 4] * ld4(M0 + (size_t)(j + 4) * kRank + rq);
     }
     acc[0] = acc[0] + acc1;
   } else {
-#pragma unroll 8
-    for (int i = 0; i < 32; ++i) {
-      const int j = j0 + 4 * i;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int j = jb + 4 * i;
       const float xj = xs[j];
       acc[0] = acc[0] + xj * ld4(M0 + (size_t)j * kRank + rq);
       acc[Q - 1] = acc[Q - 1] + xj * ld4(M1 + (size_t)j * kRank + rq);
@@ -171,35 +180,26 @@ __device__ __forceinline__ void mv_d_to_32(const float *M0, const float *M1, flo
   __syncthreads();
 }
 
-// out[o] = sum_r M[r*d + o] in[r] for the thread's 4 outputs.
-__device__ __forceinline__ float4 mv_32_to_d(const float *__restrict__ M, const float *in, int d) {
-  float4 acc = f4(0.f);
-  const float *col = M + threadIdx.x * 4;
-#pragma unroll 8
-  for (int r = 0; r < kRank; ++r) acc = acc + in[r] * ld4(col + (size_t)r * d);
-  return acc;
-}
-
-// Two 32->d products in one pass: ya = Ma . ina, yb = Mb . inb (thread's 4 outputs).
+// Two 32->d products in one pass: ya = Ma . ina, yb = Mb . inb (thread's 2 outputs).
 __device__ __forceinline__ void mv2_32_to_d(const float *Ma, const float *ina, const float *Mb,
-                                            const float *inb, int d, float4 &ya, float4 &yb) {
-  float4 a = f4(0.f), b = f4(0.f);
-  const size_t c = threadIdx.x * 4;
+                                            const float *inb, int d, int j0, float2 &ya, float2 &yb) {
+  float2 a = f2(0.f), b = f2(0.f);
 #pragma unroll
   for (int r = 0; r < kRank; ++r) {
-    a = a + ina[r] * ld4(Ma + (size_t)r * d + c);
-    b = b + inb[r] * ld4(Mb + (size_t)r * d + c);
+    a = a + ina[r] * ld2(Ma + (size_t)r * d + j0);
+    b = b + inb[r] * ld2(Mb + (size_t)r * d + j0);
   }
   ya = a;
   yb = b;
 }
 
 // ---- tensor-memory staging of rank-32 FPM matrices (d = 512) ---------------
-// Thread t of the 128-thread block owns TMEM lane t.  A d->32 matrix M[j][r]
-// occupies 128 columns: column 32e + r of lane t holds M[4t+e][r]; a 32->d
-// matrix M[r][o] occupies 128 columns: column 32q + 4rr + e holds
-// M[8q+rr][4t+e].  Loads complete at tmem_wait (which also orders the
-// destination registers after the wait).
+// TMEM lane l holds the rows / outputs of both threads owning l; the thread
+// with half hf uses the lane's columns [64 hf, 64 hf + 64) of every matrix
+// (128 columns per matrix).  A d->32 matrix M[j][r]: column 64 hf + 32 k + r
+// holds M[j0 + k][r].  A 32->d matrix M[r][o]: column 64 hf + 32 c + 2 rr + k
+// holds M[16 c + rr][j0 + k].  Loads complete at tmem_wait (which also orders
+// the destination registers after the wait).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
@@ -236,15 +236,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
-// Copy a rank-32 matrix from global memory into this thread's TMEM lane
-// (layouts above); `rows_d` = true for d->32 matrices.
-__device__ __forceinline__ void tmem_stage(uint32_t tlane, const float *M, int d, bool rows_d) {
-  const int t = threadIdx.x;
+// Copy this thread's part of a rank-32 matrix from global memory into TMEM
+// (layouts above; tcol already includes the 64 hf column offset).
+__device__ __forceinline__ void tmem_stage(uint32_t tcol, const float *M, int d, int j0, bool rows_d) {
 #pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < 2; ++c) {
     uint32_t v[32];
     if (rows_d) {
-      const float *row = M + (size_t)(4 * t + c) * kRank;
+      const float *row = M + (size_t)(j0 + c) * kRank;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float4 x = ld4(row + 4 * i);
@@ -253,29 +252,29 @@ __device__ __forceinline__ void tmem_stage(uint32_t tlane, const float *M, int d
       }
     } else {
 #pragma unroll
-      for (int rr = 0; rr < 8; ++rr) {
-        const float4 x = ld4(M + (size_t)(8 * c + rr) * d + 4 * t);
-        v[4 * rr] = __float_as_uint(x.x); v[4 * rr + 1] = __float_as_uint(x.y);
-        v[4 * rr + 2] = __float_as_uint(x.z); v[4 * rr + 3] = __float_as_uint(x.w);
+      for (int rr = 0; rr < 16; ++rr) {
+        const float2 x = ld2(M + (size_t)(16 * c + rr) * d + j0);
+        v[2 * rr] = __float_as_uint(x.x);
+        v[2 * rr + 1] = __float_as_uint(x.y);
       }
     }
-    tmem_st32(tlane + 32 * c, v);
+    tmem_st32(tcol + 32 * c, v);
   }
 }
 
 // out[0..32) = Ms . x with Ms in shared memory (mv_d_to_32 layout) and
 // out[32..64) = Mt . x with Mt (d->32) in TMEM at lane-relative column tcol.
-__device__ __forceinline__ void mv_d_to_32_smem_tmem(const float *Ms, uint32_t tcol, float4 x, float *xs,
-                                                     float *out, float *part) {
+__device__ __forceinline__ void mv_d_to_32_smem_tmem(const float *Ms, uint32_t tcol, float2 x, int j0,
+                                                     float *xs, float *out, float *part) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  st4(xs + threadIdx.x * 4, x);
+  st2(xs + j0, x);
   __syncthreads();
   const int g = lane >> 3, rq = (lane & 7) * 4;
   float4 acc = f4(0.f), acc1 = f4(0.f);  // two chains for latency
-  const int j0 = warp * 128 + g;
-#pragma unroll 8
-  for (int i = 0; i < 32; i += 2) {
-    const int j = j0 + 4 * i;
+  const int jb = warp * 64 + g;
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) {
+    const int j = jb + 4 * i;
     acc = acc + xs[j] * ld4(Ms + (size_t)j * kRank + rq);
     acc1 = acc1 + xs[j + 4] * ld4(Ms + (size_t)(j + 4) * kRank + rq);
   }
@@ -289,14 +288,16 @@ __device__ __forceinline__ void mv_d_to_32_smem_tmem(const float *Ms, uint32_t t
   }
   if (g == 0) st4(part + warp * 64 + rq, acc);
   float p[32];
-  const float xe[4] = {x.x, x.y, x.z, x.w};
+  {
+    uint32_t w0[32];
+    tmem_ld32(tcol, w0);
+    tmem_wait(w0);
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    uint32_t w[32];
-    tmem_ld32(tcol + 32 * e, w);
-    tmem_wait(w);
+    for (int r = 0; r < 32; ++r) p[r] = x.x * __uint_as_float(w0[r]);
+    tmem_ld32(tcol + 32, w0);
+    tmem_wait(w0);
 #pragma unroll
-    for (int r = 0; r < 32; ++r) p[r] = (e == 0 ? 0.f : p[r]) + xe[e] * __uint_as_float(w[r]);
+    for (int r = 0; r < 32; ++r) p[r] += x.y * __uint_as_float(w0[r]);
   }
   part[warp * 64 + 32 + lane] = warp_transpose_reduce32(p);
   __syncthreads();
@@ -308,68 +309,67 @@ __device__ __forceinline__ void mv_d_to_32_smem_tmem(const float *Ms, uint32_t t
   __syncthreads();
 }
 
-// ya = Ma . ina, yb = Mb . inb for two 32->d matrices in TMEM (thread's 4 outputs).
+// ya = Ma . ina, yb = Mb . inb for two 32->d matrices in TMEM (thread's 2 outputs).
 __device__ __forceinline__ void mv2_32_to_d_tmem(uint32_t ta, const float *ina, uint32_t tb, const float *inb,
-                                                 float4 &ya, float4 &yb) {
-  float4 a = f4(0.f), b = f4(0.f);
+                                                 float2 &ya, float2 &yb) {
+  float2 a = f2(0.f), b = f2(0.f);
 #pragma unroll 1
-  for (int q = 0; q < 4; ++q) {
+  for (int c = 0; c < 2; ++c) {
     uint32_t wa[32], wb[32];
-    tmem_ld32(ta + 32 * q, wa);
-    tmem_ld32(tb + 32 * q, wb);
+    tmem_ld32(ta + 32 * c, wa);
+    tmem_ld32(tb + 32 * c, wb);
     tmem_wait(wa);
     tmem_wait(wb);
 #pragma unroll
-    for (int rr = 0; rr < 8; ++rr) {
-      const float xa = ina[8 * q + rr], xb = inb[8 * q + rr];
-      a.x += xa * __uint_as_float(wa[4 * rr]); a.y += xa * __uint_as_float(wa[4 * rr + 1]);
-      a.z += xa * __uint_as_float(wa[4 * rr + 2]); a.w += xa * __uint_as_float(wa[4 * rr + 3]);
-      b.x += xb * __uint_as_float(wb[4 * rr]); b.y += xb * __uint_as_float(wb[4 * rr + 1]);
-      b.z += xb * __uint_as_float(wb[4 * rr + 2]); b.w += xb * __uint_as_float(wb[4 * rr + 3]);
+    for (int rr = 0; rr < 16; ++rr) {
+      const float xa = ina[16 * c + rr], xb = inb[16 * c + rr];
+      a.x += xa * __uint_as_float(wa[2 * rr]); a.y += xa * __uint_as_float(wa[2 * rr + 1]);
+      b.x += xb * __uint_as_float(wb[2 * rr]); b.y += xb * __uint_as_float(wb[2 * rr + 1]);
     }
   }
   ya = a;
   yb = b;
 }
 
-__device__ __forceinline__ float4 sigmoid4(float4 x) {
-  return make_float4(1.f / (1.f + expf(-x.x)), 1.f / (1.f + expf(-x.y)), 1.f / (1.f + expf(-x.z)),
-                     1.f / (1.f + expf(-x.w)));
+__device__ __forceinline__ float2 sigmoid2(float2 x) {
+  return make_float2(1.f / (1.f + expf(-x.x)), 1.f / (1.f + expf(-x.y)));
 }
 
-// Persistent token-serial solve.  blockDim = d/4 (one float4 per thread),
-// grid = B*h, block = b*h + s.  FPM=true requires a cluster of h CTAs.
-template <bool FPM>
-__global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
+// Persistent token-serial solve.  blockDim = d/2 (one float2 per thread, see
+// picard_j0), grid = B*h, block = b*h + s.  FPM=true requires a cluster of h CTAs.
+template <bool FPM, int MAXT>
+__global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
   extern __shared__ float4 sm4[];
   float *sm = reinterpret_cast<float *>(sm4);
   float *red = sm;               // 512
   float *vec = red + 512;        // 64   (q / bottleneck | retain-up)
-  float *part = vec + 64;        // 512  (8 warps x 64)
-  float *wsm = part + 512;       // 64   ([0,16) read weights, [16] gate, [17,33) b_read_mem)
+  float *part = vec + 64;        // 1024 (up to 16 warps x 64)
+  float *wsm = part + 1024;      // 64   ([0,16) read weights, [16] gate, [17,33) b_read_mem)
   float *keybuf = wsm + 64;      // 2 x 32
   float *mbuf = keybuf + 64;     // 2 x d
   float *xs = mbuf + 2 * a.d;    // d    (matvec input staging)
   float *wres = xs + a.d;        // n_resident x (d x 32) staged FPM matrices
   const int d = a.d, h = a.h, T = a.T;
   const int b = blockIdx.x / h, s = blockIdx.x % h;
-  const int j0 = threadIdx.x * 4;
+  const int j0 = picard_j0();
+  const int warp = threadIdx.x >> 5;
   const float inv_d = 1.f / (float)d;
   const float *W = a.W;
-  const float4 NS = ld4(W + a.off_ns + j0);
-  const float4 anc = ld4(W + a.off_anchor + (size_t)s * d + j0);
+  const float2 NS = ld2(W + a.off_ns + j0);
+  const float2 anc = ld2(W + a.off_anchor + (size_t)s * d + j0);
   BlockReducer R(red);
-  float4 hcur = f4(0.f), m = f4(0.f), hs4 = f4(0.f), hb4 = f4(0.f), wx4 = f4(0.f), ad4 = f4(0.f);
+  float2 hcur = f2(0.f), m = f2(0.f), hsv = f2(0.f), hbv = f2(0.f), wxv = f2(0.f), adv = f2(0.f);
   int cur = 0;
   // Per-slot rank-32 FPM matrices, staged in shared memory as far as they fit:
   // 0 W_k_mem, 1 W_q_mem, 2 W_k_write, 3 W_retain_up ([d][32]); 4 W_v_write,
-  // 5 W_retain_down ([32][d]).  The rest stay in global memory (L2-resident).
+  // 5 W_retain_down ([32][d]).  The rest stay in global memory (L2-resident),
+  // or, at d = 512, in tensor memory.
   const float *mat[6];
   uint32_t tmem = 0;
   __shared__ uint32_t tmem_slot;
   if constexpr (FPM) {
     if (a.use_tmem) {  // matrices 3..5 in tensor memory, 128 columns each
-      if (threadIdx.x < 32) {
+      if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          (uint32_t)__cvta_generic_to_shared(&tmem_slot)),
                      "r"(512u));
@@ -378,7 +378,9 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncthreads();
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      tmem = tmem_slot + ((uint32_t)(threadIdx.x & ~31) << 16);  // this warp's lane quadrant
+      // this warp's lane quadrant, this thread's half of the lane's columns
+      tmem = tmem_slot + ((uint32_t)(32 * (warp & 3)) << 16) +
+             64u * (uint32_t)(threadIdx.x / (blockDim.x >> 1));
     }
     const size_t ms = (size_t)s * d * kRank;
     const float *src[6] = {W + a.off_wkm + ms, W + a.off_wqm + ms, W + a.off_wkw + ms,
@@ -392,29 +394,25 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
       mat[i] = res ? dst : src[i];
     }
     if (a.use_tmem) {
-      tmem_stage(tmem + 0, mat[3], d, true);     // W_retain_up  [d][32]
-      tmem_stage(tmem + 128, mat[4], d, false);  // W_v_write    [32][d]
-      tmem_stage(tmem + 256, mat[5], d, false);  // W_retain_down [32][d]
+      tmem_stage(tmem + 0, mat[3], d, j0, true);     // W_retain_up   [d][32]
+      tmem_stage(tmem + 128, mat[4], d, j0, false);  // W_v_write     [32][d]
+      tmem_stage(tmem + 256, mat[5], d, j0, false);  // W_retain_down [32][d]
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     }
-    m = ld4(a.mstate + ((size_t)b * h + s) * d + j0);
-    st4(mbuf + j0, m);
+    m = ld2(a.mstate + ((size_t)b * h + s) * d + j0);
+    st2(mbuf + j0, m);
     if (threadIdx.x < h) wsm[17 + threadIdx.x] = W[a.off_bread + threadIdx.x];  // b_read_mem
-    hs4 = ld4(W + a.off_hscale + (size_t)s * d + j0);
-    hb4 = ld4(W + a.off_hbias + (size_t)s * d + j0);
-    wx4 = make_float4(0.5f * tanhf(W[a.off_wx + (size_t)(j0 + 0) * d + j0 + 0]),
-                      0.5f * tanhf(W[a.off_wx + (size_t)(j0 + 1) * d + j0 + 1]),
-                      0.5f * tanhf(W[a.off_wx + (size_t)(j0 + 2) * d + j0 + 2]),
-                      0.5f * tanhf(W[a.off_wx + (size_t)(j0 + 3) * d + j0 + 3]));
-    const float4 al = ld4(W + a.off_alog + (size_t)s * d + j0);
-    ad4 = make_float4(1.f / (1.f + expf(al.x)), 1.f / (1.f + expf(al.y)), 1.f / (1.f + expf(al.z)),
-                      1.f / (1.f + expf(al.w)));
+    hsv = ld2(W + a.off_hscale + (size_t)s * d + j0);
+    hbv = ld2(W + a.off_hbias + (size_t)s * d + j0);
+    wxv = make_float2(0.5f * tanhf(W[a.off_wx + (size_t)(j0 + 0) * d + j0 + 0]),
+                      0.5f * tanhf(W[a.off_wx + (size_t)(j0 + 1) * d + j0 + 1]));
+    const float2 al = ld2(W + a.off_alog + (size_t)s * d + j0);
+    adv = make_float2(1.f / (1.f + expf(al.x)), 1.f / (1.f + expf(al.y)));
     __syncthreads();
     // read key of the carried memory for the first token (:855-883)
-    mv_d_to_32<1>(mat[0], nullptr, m + hs4 * tanh4(m) + hb4, xs, keybuf, part);
+    mv_d_to_32<1>(mat[0], nullptr, m + hsv * tanh2(m) + hbv, j0, xs, keybuf, part);
   }
   const float band = fmaxf(a.eps, 0.15f * 0.2f);
-  // loop-invariant FPM write parameters of this slot
   if constexpr (FPM) {
     // the prologue's memory and read key are published: split cluster barrier,
     // waited on before the first remote read
@@ -426,41 +424,41 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
 #endif
   // rows of the next token, loaded one token ahead
   const size_t e0 = ((size_t)b * T * h + s) * d + j0;
-  float4 sig_nx = ld4(a.signal + e0);
-  float4 A4_nx = a.slot_coord ? ld4(a.A + e0) : f4(0.f);
+  float2 sig_nx = ld2(a.signal + e0);
+  float2 Av_nx = a.slot_coord ? ld2(a.A + e0) : f2(0.f);
   // sum of squares of the next token's iteration-0 `dep` and `signal`,
   // reduced together with the previous token's last block reduction
   float dep0_sq = 0.f, sig_sq = 0.f;
   for (int t = 0; t < T; ++t) {
     const size_t n = (size_t)b * T + t;
     const size_t e = (n * h + s) * d + j0;
-    const float4 sig = sig_nx;
-    const float4 A4 = A4_nx;
+    const float2 sig = sig_nx;
+    const float2 Av = Av_nx;
     if (t + 1 < T) {
-      sig_nx = ld4(a.signal + e + (size_t)h * d);
-      if (a.slot_coord) A4_nx = ld4(a.A + e + (size_t)h * d);
+      sig_nx = ld2(a.signal + e + (size_t)h * d);
+      if (a.slot_coord) Av_nx = ld2(a.A + e + (size_t)h * d);
     }
     if (t == 0) {
-      float v[1] = {dot4(sig, sig)};
+      float v[1] = {dot2(sig, sig)};
       R.sum(v);
       const float den = fmaxf(sqrtf(v[0] * inv_d + 1e-6f), 1e-6f);
-      hcur = make_float4(sig.x / den, sig.y / den, sig.z / den, sig.w / den);
+      hcur = make_float2(sig.x / den, sig.y / den);
       sig_sq = v[0];
     }
     if (t == 0 || !FPM) {
-      const float4 dep0 = sig + hcur + anc + A4;
-      float v[1] = {dot4(dep0, dep0)};
+      const float2 dep0 = sig + hcur + anc + Av;
+      float v[1] = {dot2(dep0, dep0)};
       R.sum(v);
       dep0_sq = v[0];
       if (!FPM && t > 0) sig_sq = 0.f;  // only the FPM read uses it
     }
-    float4 ctx = f4(0.f);
+    float2 ctx = f2(0.f);
     bool waited = false;  // this token's cluster-barrier wait
     PT(0);
     float prev = 1.f;
     int it = 0;
     bool conv = false;
-    // 1 / rms(dep) of the current iteration (one reciprocal instead of 4 divisions)
+    // 1 / rms(dep) of the current iteration (one reciprocal instead of per-element divisions)
     float irr = 1.f / sqrtf(dep0_sq * inv_d + 1e-6f);
     float hq_sq = 0.f;
     while (it < a.max_iters && !conv) {
@@ -473,7 +471,7 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
           // Model-A memory read from the first structured state (:1031-1200)
           const float ihq = 1.f / sqrtf(fmaxf(hq_sq, 1e-6f));
           const float sig_norm = sqrtf(fmaxf(sig_sq, 1e-6f));
-          mv_d_to_32<1>(mat[1], nullptr, ihq * hcur, xs, vec, part);
+          mv_d_to_32<1>(mat[1], nullptr, ihq * hcur, j0, xs, vec, part);
           PT(6);
           cg::cluster_group cl = cg::this_cluster();
           if (threadIdx.x < 32) {
@@ -515,18 +513,18 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
           }
           __syncthreads();
           PT(7);
-          float4 mr = f4(0.f);
+          float2 mr = f2(0.f);
           for (int base = 0; base < h; base += 8) {   // 8 remote loads in flight at a time
-            float4 mm[8];
+            float2 mm[8];
 #pragma unroll
             for (int q = 0; q < 8; ++q)
-              if (base + q < h) mm[q] = ld4(cl.map_shared_rank(mbuf + cur * d, base + q) + j0);
+              if (base + q < h) mm[q] = ld2(cl.map_shared_rank(mbuf + cur * d, base + q) + j0);
 #pragma unroll
             for (int q = 0; q < 8; ++q)
               if (base + q < h) mr = mr + wsm[base + q] * mm[q];
           }
-          const float4 mu = tanh4(mr);
-          float v1[1] = {dot4(mu, mu)};
+          const float2 mu = tanh2(mr);
+          float v1[1] = {dot2(mu, mu)};
           R.sum(v1);
           const float mu_norm = sqrtf(fmaxf(v1[0], 1e-6f));
           const float coef = sig_norm * fmaxf(a.alpha_m, 0.001f) / fmaxf(mu_norm, 1e-6f) * wsm[16];
@@ -534,17 +532,17 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
           PT(2);
         }
       }
-      float4 pre = sig + hcur + anc;
-      if (it == 0) pre = pre + A4;
+      float2 pre = sig + hcur + anc;
+      if (it == 0) pre = pre + Av;
       if (FPM && it >= 1) pre = pre + ctx;
-      const float4 f = NS * (irr * pre);
-      const float4 hn = a.blend * f + (1.f - a.blend) * hcur;
-      const float4 dh = hn - hcur;
+      const float2 f = NS * (irr * pre);
+      const float2 hn = a.blend * f + (1.f - a.blend) * hcur;
+      const float2 dh = hn - hcur;
       // one reduction per iteration: |dh|^2 of this iteration, |dep|^2 of the
       // next one (dep has no attention term after iteration 0) and, after
       // iteration 0 with FPM, |h|^2 for the memory read's query
-      const float4 dep_nx = sig + hn + anc;
-      float v2[3] = {dot4(dh, dh), dot4(dep_nx, dep_nx), dot4(hn, hn)};
+      const float2 dep_nx = sig + hn + anc;
+      float v2[3] = {dot2(dh, dh), dot2(dep_nx, dep_nx), dot2(hn, hn)};
       if (FPM && it == 0) R.sum(v2);
       else {
         float v2b[2] = {v2[0], v2[1]};
@@ -565,10 +563,10 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
       ++it;
       PT(1);
     }
-    st4(a.hstar + e, hcur);
-    float4 pre_adj = sig + hcur;
-    if (a.slot_coord) pre_adj = pre_adj + A4 + anc;
-    st4(a.pre + e, pre_adj);
+    st2(a.hstar + e, hcur);
+    float2 pre_adj = sig + hcur;
+    if (a.slot_coord) pre_adj = pre_adj + Av + anc;
+    st2(a.pre + e, pre_adj);
     if (threadIdx.x == 0) a.iters[n * h + s] = it;
     PT(3);
     if constexpr (FPM) {
@@ -576,48 +574,48 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
         asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
         PT(0);
       }
-      st4(a.fpmctx + e, ctx);
+      st2(a.fpmctx + e, ctx);
       // post-solve memory write (:1965-2140)
-      const float4 c = 0.5f * (hcur + sig);
+      const float2 c = 0.5f * (hcur + sig);
       PT(4);
-      float4 pv, dv;
+      float2 pv, dv;
       if (a.use_tmem) {
-        mv_d_to_32_smem_tmem(mat[2], tmem + 0, c, xs, vec, part);   // bottleneck | retain-up
+        mv_d_to_32_smem_tmem(mat[2], tmem + 0, c, j0, xs, vec, part);   // bottleneck | retain-up
         PT(5);
         mv2_32_to_d_tmem(tmem + 128, vec, tmem + 256, vec + 32, pv, dv);
       } else {
-        mv_d_to_32<2>(mat[2], mat[3], c, xs, vec, part);   // bottleneck | retain-up
+        mv_d_to_32<2>(mat[2], mat[3], c, j0, xs, vec, part);   // bottleneck | retain-up
         PT(5);
-        mv2_32_to_d(mat[4], vec, mat[5], vec + 32, d, pv, dv);
+        mv2_32_to_d(mat[4], vec, mat[5], vec + 32, d, j0, pv, dv);
       }
       PT(6);
-      const float4 prop = tanh4(ld4(W + a.off_bdelta + (size_t)s * d + j0) + pv);
-      const float4 df = prop - m;
+      const float2 prop = tanh2(ld2(W + a.off_bdelta + (size_t)s * d + j0) + pv);
+      const float2 df = prop - m;
       // the next token's iteration-0 |dep|^2 and |signal|^2 ride along
-      const float4 dep0n = sig_nx + hcur + anc + A4_nx;
-      float v3[6] = {dot4(m, m), dot4(df, df), dot4(hcur, hcur), dot4(ld4(W + a.off_wgate + (size_t)s * d + j0), c), dot4(dep0n, dep0n),
-                     dot4(sig_nx, sig_nx)};
+      const float2 dep0n = sig_nx + hcur + anc + Av_nx;
+      float v3[6] = {dot2(m, m), dot2(df, df), dot2(hcur, hcur), dot2(ld2(W + a.off_wgate + (size_t)s * d + j0), c),
+                     dot2(dep0n, dep0n), dot2(sig_nx, sig_nx)};
       R.sum(v3);
       dep0_sq = v3[4];
       sig_sq = v3[5];
-      const float4 hu = (1.f / sqrtf(fmaxf(v3[2] * inv_d, 1e-6f))) * hcur;
+      const float2 hu = (1.f / sqrtf(fmaxf(v3[2] * inv_d, 1e-6f))) * hcur;
       const float raw_z = 1.f / (1.f + expf(-(v3[3] * rsqrtf((float)d) + W[a.off_bwrite + s] - 1.5f)));
       const float z = fminf(fmaxf(raw_z, 0.f), 1.f);
       const float prev_norm = sqrtf(fmaxf(v3[0], 1e-6f));
       const float diff_norm = sqrtf(fmaxf(v3[1], 1e-6f));
       const float novelty = diff_norm / (diff_norm + prev_norm + 1e-6f);
-      const float4 rr4 = sigmoid4(ld4(W + a.off_bret + (size_t)s * d + j0) + dv);
-      const float4 retain = f4(1.f) - novelty * (f4(1.f) - rr4);
-      const float4 write = (z * 0.1f) * prop;
-      const float4 x = sqrtf(fmaxf(z, 1e-6f)) * hu + wx4 * hu + write;
-      const float4 base = ad4 * m + (f4(1.f) - ad4) * x;
-      const float4 mn = retain * m + (f4(1.f) - retain) * base;
-      st4(a.hist + e, mn);
-      st4(mbuf + (cur ^ 1) * d + j0, mn);
+      const float2 rrv = sigmoid2(ld2(W + a.off_bret + (size_t)s * d + j0) + dv);
+      const float2 retain = f2(1.f) - novelty * (f2(1.f) - rrv);
+      const float2 write = (z * 0.1f) * prop;
+      const float2 x = sqrtf(fmaxf(z, 1e-6f)) * hu + wxv * hu + write;
+      const float2 base = adv * m + (f2(1.f) - adv) * x;
+      const float2 mn = retain * m + (f2(1.f) - retain) * base;
+      st2(a.hist + e, mn);
+      st2(mbuf + (cur ^ 1) * d + j0, mn);
       m = mn;
       PT(4);
       // read key of the new memory, used by every slot at the next token
-      mv_d_to_32<1>(mat[0], nullptr, m + hs4 * tanh4(m) + hb4, xs, keybuf + (cur ^ 1) * 32, part);
+      mv_d_to_32<1>(mat[0], nullptr, m + hsv * tanh2(m) + hbv, j0, xs, keybuf + (cur ^ 1) * 32, part);
       PT(7);
       cur ^= 1;
       // publish this token's memory and key to the cluster
@@ -630,13 +628,13 @@ __global__ void __launch_bounds__(256) picard_kernel(PicardArgs a) {
     for (int i = 0; i < 8; ++i) g_picard_prof[blockIdx.x * 8 + i] += _pacc[i];
 #endif
   if constexpr (FPM) {
-    st4(a.mstate + ((size_t)b * h + s) * d + j0, m);
+    st2(a.mstate + ((size_t)b * h + s) * d + j0, m);
     // match the last arrive: peers may read this block's memory until they pass it
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
     if (a.use_tmem) {
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncthreads();
-      if (threadIdx.x < 32)
+      if (warp == 0)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_slot), "r"(512u));
     }
   }
@@ -701,19 +699,21 @@ cudaError_t launch_attn_scale(const AttnArgs &a, int rows, cudaStream_t st) {
 }
 
 static size_t picard_smem_base(int d) {
-  return (size_t)(512 + 64 + 512 + 64 + 64 + 3 * d) * sizeof(float);
+  return (size_t)(512 + 64 + 1024 + 64 + 64 + 3 * d) * sizeof(float);
 }
 
-cudaError_t launch_picard(const PicardArgs &a, bool fpm, cudaStream_t st) {
-  if (a.B <= 0 || a.T <= 0) return cudaSuccess;
-  const int threads = a.d / 4;
+template <bool FPM, int MAXT>
+static cudaError_t picard_launch(const PicardArgs &a, cudaStream_t st) {
+  const int threads = a.d / 2;
   size_t smem = picard_smem_base(a.d);
-  if (!fpm) {
-    picard_kernel<false><<<a.B * a.h, threads, smem, st>>>(a);
+  if (!FPM) {
+    cudaError_t e = cudaFuncSetAttribute(picard_kernel<false, MAXT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    picard_kernel<false, MAXT><<<a.B * a.h, threads, smem, st>>>(a);
     return cudaGetLastError();
   }
-  cudaError_t e = cudaFuncSetAttribute(picard_kernel<true>,
-                                       cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaError_t e = cudaFuncSetAttribute(picard_kernel<true, MAXT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e != cudaSuccess) return e;
   int dev = 0, optin = 0;
   cudaGetDevice(&dev);
@@ -726,9 +726,9 @@ cudaError_t launch_picard(const PicardArgs &a, bool fpm, cudaStream_t st) {
     ++p.n_resident;
   }
   // d = 512: the three matrices that do not fit in shared memory go to tensor
-  // memory (one 128-thread block per SM owns all 512 columns)
+  // memory (one 256-thread block per SM owns all 512 columns)
   p.use_tmem = (a.d == 512 && p.n_resident == 3 && !getenv("AIDEEN_PICARD_NO_TMEM")) ? 1 : 0;
-  e = cudaFuncSetAttribute(picard_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  e = cudaFuncSetAttribute(picard_kernel<true, MAXT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.B * a.h);
@@ -742,9 +742,15 @@ cudaError_t launch_picard(const PicardArgs &a, bool fpm, cudaStream_t st) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, picard_kernel<true>, p);
+  e = cudaLaunchKernelEx(&cfg, picard_kernel<true, MAXT>, p);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
+}
+
+cudaError_t launch_picard(const PicardArgs &a, bool fpm, cudaStream_t st) {
+  if (a.B <= 0 || a.T <= 0) return cudaSuccess;
+  if (a.d > 512) return fpm ? picard_launch<true, 512>(a, st) : picard_launch<false, 512>(a, st);
+  return fpm ? picard_launch<true, 256>(a, st) : picard_launch<false, 256>(a, st);
 }
 
 cudaError_t launch_pool_rmsnorm(const float *hstar, const float *g, float *pooled, float *y,
