@@ -563,18 +563,19 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       ++it;
       PT(1);
     }
-    st2(a.hstar + e, hcur);
     float2 pre_adj = sig + hcur;
     if (a.slot_coord) pre_adj = pre_adj + Av + anc;
-    st2(a.pre + e, pre_adj);
-    if (threadIdx.x == 0) a.iters[n * h + s] = it;
+    if (!FPM) {
+      st2(a.hstar + e, hcur);
+      st2(a.pre + e, pre_adj);
+      if (threadIdx.x == 0) a.iters[n * h + s] = it;
+    }
     PT(3);
     if constexpr (FPM) {
       if (!waited) {  // solve stopped before the memory read: still consume this token's barrier phase
         asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
         PT(0);
       }
-      st2(a.fpmctx + e, ctx);
       // post-solve memory write (:1965-2140)
       const float2 c = 0.5f * (hcur + sig);
       PT(4);
@@ -610,7 +611,6 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       const float2 x = sqrtf(fmaxf(z, 1e-6f)) * hu + wxv * hu + write;
       const float2 base = adv * m + (f2(1.f) - adv) * x;
       const float2 mn = retain * m + (f2(1.f) - retain) * base;
-      st2(a.hist + e, mn);
       st2(mbuf + (cur ^ 1) * d + j0, mn);
       m = mn;
       PT(4);
@@ -618,8 +618,15 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       mv_d_to_32<1>(mat[0], nullptr, m + hsv * tanh2(m) + hbv, j0, xs, keybuf + (cur ^ 1) * 32, part);
       PT(7);
       cur ^= 1;
-      // publish this token's memory and key to the cluster
+      // publish this token's memory and key to the cluster; the global stores
+      // (no reader inside this kernel) come after the arrive, so its release
+      // orders only the shared-memory writes
       asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+      st2(a.hist + e, mn);
+      st2(a.hstar + e, hcur);
+      st2(a.pre + e, pre_adj);
+      st2(a.fpmctx + e, ctx);
+      if (threadIdx.x == 0) a.iters[n * h + s] = it;
       PT(4);
     }
   }

@@ -266,12 +266,16 @@ __global__ void fpm_carry_kernel(FpmBwdArgs a) {
   const int d = a.d, nch = a.nch;
   if (i >= a.B * a.h * d) return;
   const int k = i % d;
-  const size_t bs = i / d;
+  const size_t base = (size_t)(i / d) * nch * d + k;
+  const float *__restrict__ cA = a.cA;
+  const float *__restrict__ cU = a.cU;
+  float *__restrict__ gin = a.gin;
   float g = a.carry[i];
+#pragma unroll 8
   for (int ch = nch - 1; ch >= 0; --ch) {
-    const size_t o = (bs * nch + ch) * d + k;
-    a.gin[o] = g;
-    g = a.cA[o] * g + a.cU[o];
+    const size_t o = base + (size_t)ch * d;
+    gin[o] = g;
+    g = cA[o] * g + cU[o];
   }
   a.carry[i] = g;
 }

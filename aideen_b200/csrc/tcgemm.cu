@@ -85,9 +85,10 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
   uint32_t *err = tmem_slot + 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, bz = blockIdx.z;
-  // with split-K, z selects the K range (operands unbatched) and the output slice
-  const int zab = p.ksplit > 1 ? 0 : bz;
-  const int kb0 = p.ksplit > 1 ? bz * p.kchunk : 0;
+  // with split-K, z = batch * ksplit + split: the split selects the K range,
+  // the output slice is z itself (workspace [batch][ksplit][M][N])
+  const int zab = p.ksplit > 1 ? bz / p.ksplit : bz;
+  const int kb0 = p.ksplit > 1 ? (bz % p.ksplit) * p.kchunk : 0;
   const int ktot = (p.K + BK - 1) / BK;
   const int kblocks = p.ksplit > 1 ? min(p.kchunk, ktot - kb0) : ktot;
 
@@ -326,16 +327,17 @@ bool tc_gemm_supported(const GemmArgs &g) {
 }
 
 namespace {
-// C = alpha * sum_s ws[s] + beta * C, summed in split order (deterministic).
-__global__ void splitk_reduce_kernel(const float *__restrict__ ws, int splits, int M, int N, float *C,
-                                     long ldc, float alpha, float beta) {
-  const size_t total = (size_t)M * N;
+// C[b] = alpha * sum_s ws[b][s] + beta * C[b], summed in split order (deterministic).
+__global__ void splitk_reduce_kernel(const float *__restrict__ ws, int splits, int batch, int M, int N,
+                                     float *C, long ldc, long strideC, float alpha, float beta) {
+  const size_t mn = (size_t)M * N, total = mn * batch;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
        i += (size_t)gridDim.x * blockDim.x) {
+    const size_t bb = i / mn, r = i % mn;
     float acc = 0.f;
-    for (int s = 0; s < splits; ++s) acc += ws[(size_t)s * total + i];
-    const size_t m = i / N, n = i % N;
-    float *c = C + m * ldc + n;
+    for (int s = 0; s < splits; ++s) acc += ws[(bb * splits + s) * mn + r];
+    const size_t m = r / N, n = r % N;
+    float *c = C + bb * strideC + m * ldc + n;
     *c = beta != 0.f ? alpha * acc + beta * *c : alpha * acc;
   }
 }
@@ -365,13 +367,15 @@ cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st, float *ws, size_t ws_flo
   const int tiles = tiles_n * tiles_m * g.batch;
   const int kblocks = (g.K + BK - 1) / BK;
   int zdim = g.batch;
-  // Split K when the output has too few tiles to fill the GPU and K is long.
-  if (ws && g.batch == 1 && tiles < 148 && kblocks >= 64) {
+  // Split K when the output (all batches) has too few tiles to fill the GPU
+  // and K is long enough; the partial sums go to the workspace.
+  if (ws && tiles < 148 && kblocks >= 64) {
     int splits = (2 * 148 + tiles - 1) / tiles;
     if (splits > 16) splits = 16;
+    if (splits > kblocks / 4) splits = kblocks / 4;
     const int chunk = (kblocks + splits - 1) / splits;
     splits = (kblocks + chunk - 1) / chunk;
-    if ((size_t)splits * g.M * g.N <= ws_floats && splits > 1) {
+    if ((size_t)splits * g.batch * g.M * g.N <= ws_floats && splits > 1) {
       p.ksplit = splits;
       p.kchunk = chunk;
       p.C = ws;
@@ -379,7 +383,7 @@ cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st, float *ws, size_t ws_flo
       p.strideC = (long)g.M * g.N;
       p.alpha = 1.f;
       p.beta = 0.f;
-      zdim = splits;
+      zdim = splits * g.batch;
     }
   }
   // Coalesced epilogue through bulk tensor stores when C allows a tensor map
@@ -402,7 +406,8 @@ cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st, float *ws, size_t ws_flo
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || p.ksplit <= 1) return e;
-  splitk_reduce_kernel<<<148 * 4, 256, 0, st>>>(ws, p.ksplit, g.M, g.N, g.C, g.ldc, g.alpha, g.beta);
+  splitk_reduce_kernel<<<148 * 4, 256, 0, st>>>(ws, p.ksplit, g.batch, g.M, g.N, g.C, g.ldc,
+                                                g.batch > 1 ? g.strideC : 0, g.alpha, g.beta);
   return cudaGetLastError();
 }
 
