@@ -131,7 +131,9 @@ __device__ __forceinline__ int picard_j0() {
 // j = 64 w + 4 i + (l >> 3), columns 4 (l & 7)..+3, so one warp load covers
 // four whole 128-byte rows (coalesced, conflict-free in shared memory); every
 // warp covers 64 rows.  Results land in out[q*32 + r].  Three block barriers.
-template <int Q>
+// SYNC_OUT = false skips the last barrier: for results that only the writing
+// warp (warp 0) reads, or that peers read after a cluster barrier.
+template <int Q, bool SYNC_OUT = true>
 __device__ __forceinline__ void mv_d_to_32(const float *M0, const float *M1, float2 x, int j0, float *xs,
                                            float *out, float *part) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -177,7 +179,7 @@ __device__ __forceinline__ void mv_d_to_32(const float *M0, const float *M1, flo
     for (int w = 0; w < nw; ++w) t += part[w * 64 + threadIdx.x];
     out[threadIdx.x] = t;
   }
-  __syncthreads();
+  if (SYNC_OUT) __syncthreads();
 }
 
 // Two 32->d products in one pass: ya = Ma . ina, yb = Mb . inb (thread's 2 outputs).
@@ -410,7 +412,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
     adv = make_float2(1.f / (1.f + expf(al.x)), 1.f / (1.f + expf(al.y)));
     __syncthreads();
     // read key of the carried memory for the first token (:855-883)
-    mv_d_to_32<1>(mat[0], nullptr, m + hsv * tanh2(m) + hbv, j0, xs, keybuf, part);
+    mv_d_to_32<1, false>(mat[0], nullptr, m + hsv * tanh2(m) + hbv, j0, xs, keybuf, part);
   }
   const float band = fmaxf(a.eps, 0.15f * 0.2f);
   if constexpr (FPM) {
@@ -471,11 +473,13 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
           // Model-A memory read from the first structured state (:1031-1200)
           const float ihq = 1.f / sqrtf(fmaxf(hq_sq, 1e-6f));
           const float sig_norm = sqrtf(fmaxf(sig_sq, 1e-6f));
-          mv_d_to_32<1>(mat[1], nullptr, ihq * hcur, j0, xs, vec, part);
+          // the query lands in vec[0..32), written and read by warp 0 only
+          mv_d_to_32<1, false>(mat[1], nullptr, ihq * hcur, j0, xs, vec, part);
           PT(6);
           cg::cluster_group cl = cg::this_cluster();
           if (threadIdx.x < 32) {
             const int lane = threadIdx.x;
+            __syncwarp();
             float kr[16];
 #pragma unroll
             for (int ms = 0; ms < 16; ++ms)
@@ -490,14 +494,25 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
             }
 #endif
             const float qv = vec[lane];
-            float sc = -1e30f;
+            // 16 dot products over the warp in 16 shuffles: halving exchanges
+            // (xor 16, 8, 4, 2) leave lane l with slot (l >> 1)'s partial, one
+            // more xor-1 sum completes it
+            float p[16];
 #pragma unroll
-            for (int ms = 0; ms < 16; ++ms) {
-              if (ms < h) {
-                const float dot = warp_sum(qv * kr[ms]);
-                if (lane == ms) sc = dot;
+            for (int ms = 0; ms < 16; ++ms) p[ms] = qv * kr[ms];
+#pragma unroll
+            for (int off = 16, nv = 8; off >= 2; off >>= 1, nv >>= 1) {
+              const bool upper = (lane & off) != 0;
+#pragma unroll
+              for (int i = 0; i < nv; ++i) {
+                const float send = upper ? p[i] : p[i + nv];
+                const float keep = upper ? p[i + nv] : p[i];
+                p[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
               }
             }
+            const float part_dot = p[0] + __shfl_xor_sync(0xffffffffu, p[0], 1);
+            float sc = __shfl_sync(0xffffffffu, part_dot, (lane & 15) << 1);
+            if (lane >= h) sc = -1e30f;
             if (lane < h) sc = (sc + wsm[17 + lane]) * rsqrtf((float)kRank) / fmaxf(a.tau, 1e-3f);
             const float mx = warp_max(sc);
             const float ex = lane < h ? expf(sc - mx) : 0.f;
@@ -615,7 +630,8 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       m = mn;
       PT(4);
       // read key of the new memory, used by every slot at the next token
-      mv_d_to_32<1>(mat[0], nullptr, m + hsv * tanh2(m) + hbv, j0, xs, keybuf + (cur ^ 1) * 32, part);
+      // peers read the key after the cluster barrier below; no block barrier needed
+      mv_d_to_32<1, false>(mat[0], nullptr, m + hsv * tanh2(m) + hbv, j0, xs, keybuf + (cur ^ 1) * 32, part);
       PT(7);
       cur ^= 1;
       // publish this token's memory and key to the cluster; the global stores
