@@ -443,6 +443,35 @@ cudaError_t launch_add(float *dst, const float *a, const float *b, size_t n, cud
   return cudaGetLastError();
 }
 
+__global__ void permute_rows_kernel(const uint32_t *__restrict__ src, uint32_t *__restrict__ dst, int B, int T,
+                                    size_t len, int to_internal) {
+  const size_t N = (size_t)B * T;
+  const size_t r = blockIdx.x % N, blk = blockIdx.x / N;  // destination row
+  // destination row r in the target order -> source row in the other order
+  size_t sr;
+  if (to_internal) { const size_t t = r / B, b = r % B; sr = b * T + t; }
+  else { const size_t b = r / T, t = r % T; sr = t * B + b; }
+  const uint32_t *s = src + (blk * N + sr) * len;
+  uint32_t *dd = dst + (blk * N + r) * len;
+  if ((len & 3) == 0 && ((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(dd)) & 15) == 0) {
+    for (size_t i = threadIdx.x; i < len / 4; i += blockDim.x)
+      reinterpret_cast<uint4 *>(dd)[i] = reinterpret_cast<const uint4 *>(s)[i];
+  } else {
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) dd[i] = s[i];
+  }
+}
+
+cudaError_t launch_permute_rows(const void *src, void *dst, int B, int T, int blocks, size_t len,
+                                bool to_internal, cudaStream_t st) {
+  const size_t rows = (size_t)B * T * blocks;
+  if (rows == 0 || len == 0) return cudaSuccess;
+  const int threads = len >= 512 ? 128 : 32;
+  permute_rows_kernel<<<(unsigned)rows, threads, 0, st>>>(reinterpret_cast<const uint32_t *>(src),
+                                                         reinterpret_cast<uint32_t *>(dst), B, T, len,
+                                                         to_internal ? 1 : 0);
+  return cudaGetLastError();
+}
+
 // dst[r][c] = x[r][c] + bias[c] over rows of `len` floats (len % 4 == 0).
 __global__ void add_rowbias_kernel(float *__restrict__ dst, const float *__restrict__ x,
                                    const float *__restrict__ bias, size_t n4, size_t len4) {

@@ -30,6 +30,7 @@ struct DevBufs {
   int32_t *tokens = nullptr, *targets = nullptr;
   float *signal = nullptr, *A = nullptr, *amat = nullptr;
   float *src = nullptr;  // [N][h][d] signal + slot anchor (attention source rows)
+  float *perm = nullptr;  // row-permutation scratch, max_tokens * h * d floats (on first use)
   float *Qh = nullptr, *Kh = nullptr, *Vh = nullptr, *alpha = nullptr, *nmix = nullptr,
         *rmix = nullptr, *scale = nullptr, *rho = nullptr, *Rsrc = nullptr;
   float *hstar = nullptr, *pre = nullptr, *pooled = nullptr, *hist = nullptr, *fpmctx = nullptr,
@@ -84,6 +85,11 @@ struct aideen_ctx {
   bool signal_zero = false;
   aideen_run last_run{};
   uint32_t N = 0;         // tokens of the last forward (B*T)
+  // Activation rows are token-major inside the library (row t*B + b) so that a
+  // run of tokens is a contiguous row range; the ABI keeps the caller's order
+  // (row b*T + t) and permutes at the boundary.  (perm_B, perm_T) describe the
+  // rows currently held (perm_B = 1: caller order, e.g. after aideen_adjoint_on).
+  int perm_B = 1, perm_T = 0;
   uint32_t adj_N = 0;     // tokens of the last adjoint
   float adj_beta = 0.85f;
   bool lm_ready = false, emb_ready = false;
@@ -169,6 +175,28 @@ int copy_in(aideen_ctx *ctx, void *dst, const void *src, size_t bytes, int where
   return AIDEEN_OK;
 }
 
+cudaError_t ensure_perm(aideen_ctx *ctx) {
+  if (ctx->b.perm) return cudaSuccess;
+  return dalloc(&ctx->b.perm, ctx->max_tokens * ctx->cfg.h_slots * ctx->cfg.d_model);
+}
+
+// Copy `blocks` sets of B*T rows (len 4-byte words each) from the caller's
+// order into the library's token-major order.
+int copy_in_rows(aideen_ctx *ctx, void *dst, const void *src, int B, int T, int blocks, size_t len, int where) {
+  const size_t bytes = (size_t)B * T * blocks * len * 4;
+  if (bytes == 0) return AIDEEN_OK;
+  if (!src) return set_err(ctx, AIDEEN_E_INVALID, "null input pointer");
+  if (B == 1 || T == 1) return copy_in(ctx, dst, src, bytes, where);
+  const void *from = src;
+  if (where != AIDEEN_DEVICE) {
+    CU(ensure_perm(ctx));
+    CU(cudaMemcpyAsync(ctx->b.perm, src, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    from = ctx->b.perm;
+  }
+  KL(launch_permute_rows(from, dst, B, T, blocks, len, true, ctx->stream));
+  return AIDEEN_OK;
+}
+
 GemmArgs gemm(int M, int N, int K, int batch, const float *A, long lda, long sA, bool tA,
               const float *B, long ldb, long sB, bool tB, float *C, long ldc, long sC,
               float alpha = 1.f, float beta = 0.f, const float *abias = nullptr, long sbias = 0) {
@@ -206,6 +234,8 @@ int check_run(aideen_ctx *ctx, const aideen_run *r) {
 int run_forward(aideen_ctx *ctx, const aideen_run *r, aideen_stats *stats) {
   const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
   const int N = r->batch * r->seq_len;
+  ctx->perm_B = r->batch;
+  ctx->perm_T = r->seq_len;
   const Layout &L = ctx->P;
   DevBufs &b = ctx->b;
   cudaStream_t st = ctx->stream;
@@ -649,7 +679,7 @@ void aideen_destroy(aideen_ctx *ctx) {
                   b.Mlm2, b.y, b.lrms, b.logits, b.dy, b.ggp, b.loss_rows, b.scal, b.emb, b.stats,
                   b.sigmas, b.stage, b.ws, b.fc, b.frp, b.fdl, b.fminner, b.fdm, b.fgpre, b.fup,
                   b.fkw, b.fdup, b.fA, b.fU, b.fgin, b.fcarry, b.fpart, b.fpart_bw, b.src,
-                  b.dlog_lo, b.yhi, b.ylo, b.yThi, b.yTlo, b.whi, b.wlo, b.colpart};
+                  b.dlog_lo, b.yhi, b.ylo, b.yThi, b.yTlo, b.whi, b.wlo, b.colpart, b.perm};
   for (void *p : ptrs)
     if (p) cudaFree(p);
   if (ctx->side) cudaStreamSynchronize(ctx->side);
@@ -818,7 +848,8 @@ int aideen_forward(aideen_ctx *ctx, const aideen_run *run, const float *s_in, in
   if (!ctx) return AIDEEN_E_INVALID;
   CHK(check_run(ctx, run));
   const size_t N = (size_t)run->batch * run->seq_len;
-  CHK(copy_in(ctx, ctx->b.S_in, s_in, N * ctx->cfg.d_model * 4, where));
+  CHK(copy_in_rows(ctx, ctx->b.S_in, s_in, run->batch, run->seq_len, 1, ctx->cfg.d_model, where));
+  (void)N;
   return run_forward(ctx, run, stats);
 }
 
@@ -828,7 +859,7 @@ int aideen_forward_tokens(aideen_ctx *ctx, const aideen_run *run, const int32_t 
   CHK(check_run(ctx, run));
   if (!ctx->emb_ready) return set_err(ctx, AIDEEN_E_INVALID, "embedding not uploaded");
   const int N = run->batch * run->seq_len;
-  CHK(copy_in(ctx, ctx->b.tokens, tokens, (size_t)N * 4, where));
+  CHK(copy_in_rows(ctx, ctx->b.tokens, tokens, run->batch, run->seq_len, 1, 1, where));
   KL(launch_embed(ctx->b.tokens, ctx->b.emb, ctx->b.S_in, N, ctx->cfg.d_model, ctx->cfg.vocab, ctx->stream));
   return run_forward(ctx, run, stats);
 }
@@ -838,7 +869,7 @@ int aideen_lm_head_loss(aideen_ctx *ctx, uint32_t batch, uint32_t seq_len, const
   if (!ctx) return AIDEEN_E_INVALID;
   const uint32_t N = batch * seq_len;
   if (N == 0 || N != ctx->N) return set_err(ctx, AIDEEN_E_INVALID, "LM head must follow a forward of the same shape");
-  CHK(copy_in(ctx, ctx->b.targets, targets, (size_t)N * 4, where));
+  CHK(copy_in_rows(ctx, ctx->b.targets, targets, ctx->perm_B, ctx->perm_T, 1, 1, where));
   return run_lm_head(ctx, N, loss_out);
 }
 
@@ -848,11 +879,11 @@ int aideen_adjoint(aideen_ctx *ctx, const aideen_adjoint_args *a, const float *d
   const uint32_t N = a->batch * a->seq_len;
   if (N == 0 || N != ctx->N) return set_err(ctx, AIDEEN_E_INVALID, "adjoint must follow a forward of the same shape");
   const size_t d = ctx->cfg.d_model, h = ctx->cfg.h_slots;
-  if (dl_dh) CHK(copy_in(ctx, ctx->b.dl_dh, dl_dh, (size_t)N * d * 4, where));
+  if (dl_dh) CHK(copy_in_rows(ctx, ctx->b.dl_dh, dl_dh, ctx->perm_B, ctx->perm_T, 1, d, where));
   const float *rs = nullptr;
   if (rhs_slot) {
     if (!ctx->b.rhs_slot) CU(dalloc(&ctx->b.rhs_slot, ctx->max_tokens * h * d));
-    CHK(copy_in(ctx, ctx->b.rhs_slot, rhs_slot, (size_t)N * h * d * 4, where));
+    CHK(copy_in_rows(ctx, ctx->b.rhs_slot, rhs_slot, ctx->perm_B, ctx->perm_T, 1, h * d, where));
     rs = ctx->b.rhs_slot;
   }
   return run_adjoint(ctx, N, ctx->b.pre, nullptr, ctx->b.dl_dh, rs, a->iters, a->damping, a->anderson_m);
@@ -886,6 +917,8 @@ int aideen_adjoint_on(aideen_ctx *ctx, const aideen_adjoint_args *a, const float
     }
   }
   ctx->N = 0;  // the forward state no longer matches this adjoint
+  ctx->perm_B = 1;  // rows in the caller's order
+  ctx->perm_T = (int)N;
   return run_adjoint(ctx, N, pa, pb, rt, rs, a->iters, a->damping, a->anderson_m);
 }
 
@@ -893,11 +926,20 @@ int aideen_source_grad(aideen_ctx *ctx, float *out, int where) {
   if (!ctx || !out) return AIDEEN_E_INVALID;
   const int N = ctx->adj_N, h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
   if (N == 0) return set_err(ctx, AIDEEN_E_INVALID, "no adjoint has run");
-  float *dst = where == AIDEEN_DEVICE ? out : ctx->b.dS;  // dS doubles as host staging
-  KL(launch_source_grad(ctx->b.gpre, dst, N, h, d, ctx->stream));
+  KL(launch_source_grad(ctx->b.gpre, ctx->b.dS, N, h, d, ctx->stream));  // dS doubles as staging
+  const bool perm = ctx->perm_B > 1 && ctx->perm_T > 1;
+  const float *res = ctx->b.dS;
+  if (perm) {
+    CU(ensure_perm(ctx));
+    float *dst = where == AIDEEN_DEVICE ? out : ctx->b.perm;
+    KL(launch_permute_rows(ctx->b.dS, dst, ctx->perm_B, ctx->perm_T, 1, d, false, ctx->stream));
+    res = dst;
+  }
   if (where != AIDEEN_DEVICE) {
-    CU(cudaMemcpyAsync(out, dst, (size_t)N * d * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    CU(cudaMemcpyAsync(out, res, (size_t)N * d * 4, cudaMemcpyDeviceToHost, ctx->stream));
     CU(cudaStreamSynchronize(ctx->stream));
+  } else if (!perm) {
+    CU(cudaMemcpyAsync(out, res, (size_t)N * d * 4, cudaMemcpyDeviceToDevice, ctx->stream));
   }
   return AIDEEN_OK;
 }
@@ -932,8 +974,8 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
   if (!ctx->emb_ready || !ctx->lm_ready)
     return set_err(ctx, AIDEEN_E_INVALID, "train step needs the embedding and the LM head");
   const int N = a->run.batch * a->run.seq_len;
-  CHK(copy_in(ctx, ctx->b.tokens, tokens, (size_t)N * 4, where));
-  CHK(copy_in(ctx, ctx->b.targets, targets, (size_t)N * 4, where));
+  CHK(copy_in_rows(ctx, ctx->b.tokens, tokens, a->run.batch, a->run.seq_len, 1, 1, where));
+  CHK(copy_in_rows(ctx, ctx->b.targets, targets, a->run.batch, a->run.seq_len, 1, 1, where));
   KL(launch_embed(ctx->b.tokens, ctx->b.emb, ctx->b.S_in, N, ctx->cfg.d_model, ctx->cfg.vocab, ctx->stream));
   CHK(run_forward(ctx, &a->run, stats));
   CHK(run_lm_head(ctx, N, nullptr));
@@ -995,6 +1037,27 @@ int aideen_read(aideen_ctx *ctx, int which, void *dst, size_t n) {
     }
     CU(cudaStreamSynchronize(ctx->stream));
     return AIDEEN_OK;
+  }
+  // row-indexed buffers come back in the caller's row order
+  size_t len = 0;
+  int blocks = 1;
+  const size_t hh = ctx->cfg.h_slots, dd = ctx->cfg.d_model;
+  switch (which) {
+    case AIDEEN_BUF_HSTAR: case AIDEEN_BUF_SIGNAL: case AIDEEN_BUF_ATTN: case AIDEEN_BUF_GPRE:
+    case AIDEEN_BUF_HIST_CTX: case AIDEEN_BUF_FPM_CTX: case AIDEEN_BUF_PRE: case AIDEEN_BUF_FPM_DM:
+      len = hh * dd; break;
+    case AIDEEN_BUF_POOLED: case AIDEEN_BUF_DL_DH: case AIDEEN_BUF_S_IN: case AIDEEN_BUF_DS_IN:
+      len = dd; break;
+    case AIDEEN_BUF_ITERS: len = hh; break;
+    case AIDEEN_BUF_ALPHA: len = hh * hh; break;
+    case AIDEEN_BUF_ADJ_V: len = dd; blocks = (int)hh; break;
+    default: break;
+  }
+  const int PB = ctx->perm_B, PT = ctx->perm_T;
+  if (len && PB > 1 && PT > 1 && count == (size_t)PB * PT * blocks * len) {
+    CU(ensure_perm(ctx));
+    KL(launch_permute_rows(p, ctx->b.perm, PB, PT, blocks, len, false, ctx->stream));
+    p = ctx->b.perm;
   }
   CU(cudaMemcpyAsync(dst, p, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
   CU(cudaStreamSynchronize(ctx->stream));

@@ -425,20 +425,22 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
   long long _pacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #endif
   // rows of the next token, loaded one token ahead
-  const size_t e0 = ((size_t)b * T * h + s) * d + j0;
+  // rows are token-major: row (t, b) = t * B + b
+  const size_t e0 = ((size_t)b * h + s) * d + j0;
+  const size_t tstride = (size_t)a.B * h * d;  // one token step in a row-major [N][h][d] buffer
   float2 sig_nx = ld2(a.signal + e0);
   float2 Av_nx = a.slot_coord ? ld2(a.A + e0) : f2(0.f);
   // sum of squares of the next token's iteration-0 `dep` and `signal`,
   // reduced together with the previous token's last block reduction
   float dep0_sq = 0.f, sig_sq = 0.f;
   for (int t = 0; t < T; ++t) {
-    const size_t n = (size_t)b * T + t;
+    const size_t n = (size_t)t * a.B + b;
     const size_t e = (n * h + s) * d + j0;
     const float2 sig = sig_nx;
     const float2 Av = Av_nx;
     if (t + 1 < T) {
-      sig_nx = ld2(a.signal + e + (size_t)h * d);
-      if (a.slot_coord) Av_nx = ld2(a.A + e + (size_t)h * d);
+      sig_nx = ld2(a.signal + e + tstride);
+      if (a.slot_coord) Av_nx = ld2(a.A + e + tstride);
     }
     if (t == 0) {
       float v[1] = {dot2(sig, sig)};

@@ -1,4 +1,4 @@
-// FPM memory backward: the reverse-time pass through the post-solve memory
+// FPM memory backward (token-major rows: row (t, b) = t * B + b): the reverse-time pass through the post-solve memory
 // write, with the reference's gradient formulas
 // (aideen-backbone/src/shaders/fused_fpm_retain_bwd.wgsl:364-2095) and its
 // shared W_out / diag W_x gradients (fused_fpm_shared_update.wgsl:129-256).
@@ -68,7 +68,7 @@ __device__ __forceinline__ void row_coefs(const FpmBwdArgs &a, const float *prm,
   for (int i = 0; i < NV; ++i) {
     const int k = 4 * (lane + 32 * i);
     hv[i] = ld4(a.hstar + row + k);
-    mp[i] = t > 0 ? ld4(a.hist + row - (size_t)h * d + k) : f4(0.f);
+    mp[i] = t > 0 ? ld4(a.hist + row - (size_t)a.B * h * d + k) : f4(0.f);  // token t-1, token-major rows
     const float4 dl = ld4(a.dpre + row + k) + ld4(prm + d + k);
     pr[i] = tanh4(dl);
     const float4 rp = ld4(a.rpre + row + k) + ld4(prm + k);
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(32 * CH) fpm_chunk_kernel(FpmBwdArgs a) {
   const size_t N = (size_t)a.B * T;
   if (w < nt) {
     const int lane = threadIdx.x & 31;
-    const size_t n = (size_t)b * T + t0 + w;
+    const size_t n = (size_t)(t0 + w) * a.B + b;
     const float *vrow = a.v + ((size_t)s * N + n) * d;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(32 * CH) fpm_chunk_kernel(FpmBwdArgs a) {
       float g = a.gin[(((size_t)b * h + s) * nch + ch) * d + k];
       float s_pre = 0.f, s_bd = 0.f, s_alog = 0.f, s_wx = 0.f;
       for (int tl = nt - 1; tl >= 0; --tl) {
-        const size_t n = (size_t)b * T + t0 + tl;
+        const size_t n = (size_t)(t0 + tl) * a.B + b;
         const size_t idx = (n * h + s) * d + k;
         float *c = sm + (size_t)tl * d + k;
         const float al = c[0];
@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(32 * CH) fpm_chunk_kernel(FpmBwdArgs a) {
 #pragma unroll
     for (int tl = 0; tl < CH; ++tl) {
       if (tl < nt) {
-        const size_t n = (size_t)b * T + t0 + tl;
+        const size_t n = (size_t)(t0 + tl) * a.B + b;
         acc += graw[tl] * a.c[(n * h + s) * d + k];
       }
     }

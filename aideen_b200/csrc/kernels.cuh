@@ -104,6 +104,11 @@ cudaError_t launch_dsig_init(const AttnBwdArgs &a, float *dsig, int rows, int sl
 cudaError_t launch_colsum(const float *X, int rows, int ncols, long ld, float *out, int seg,
                           long ostride, bool accumulate, cudaStream_t st);
 cudaError_t launch_add(float *dst, const float *a, const float *b, size_t n, cudaStream_t st);
+// Row permutation between the caller's order (row b*T + t) and the library's
+// token-major order (row t*B + b), for `blocks` consecutive sets of B*T rows of
+// `len` 4-byte words each (to_internal: caller -> library).
+cudaError_t launch_permute_rows(const void *src, void *dst, int B, int T, int blocks, size_t len,
+                                bool to_internal, cudaStream_t st);
 cudaError_t launch_add_rowbias(float *dst, const float *x, const float *bias, size_t rows, size_t len,
                                cudaStream_t st);
 
@@ -137,7 +142,8 @@ cudaError_t launch_rmsnorm_bwd(const float *dy, const float *P, const float *lrm
 cudaError_t launch_sum(const float *x, int n, float *out, cudaStream_t st);
 
 // FPM memory backward (fpm_bwd.cu).  Row-major [N][h][d] buffers, N = B*T
-// tokens ordered (b, t); v is the adjoint solution [h][N][d]; the chunk
+// tokens in the library's token-major order (row t*B + b); v is the adjoint
+// solution [h][N][d]; the chunk
 // arrays cA, cU, gin are [B][h][nch][d] with nch = ceil(T / fpm_chunk_len(d)).
 struct FpmBwdArgs {
   int B, T, h, d, nch;

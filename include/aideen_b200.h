@@ -223,9 +223,12 @@ enum aideen_buf {
   AIDEEN_BUF_FPM_DM = 16,   /* [N][h][d] dL/dM[t] of the last FPM backward (fpm_dm_buf) */
   AIDEEN_BUF_FPM_CARRY = 17 /* [max_batch][h][d] FPM TBPTT carry (tbptt_carry_buf) */
 };
-/* Copies the first n_elems elements (4 bytes each) of a buffer to host dst. */
+/* Copies the first n_elems elements (4 bytes each) of a buffer to host dst,
+ * token rows in the caller's order (row b*T + t). */
 int aideen_read(aideen_ctx *ctx, int which, void *dst, size_t n_elems);
-/* Device pointer of a buffer (zero-copy consumers); NULL if absent. */
+/* Device pointer of a buffer (zero-copy consumers); NULL if absent.  After a
+ * forward the token rows of activation buffers are in the library's
+ * token-major order (row t*B + b), not the caller's. */
 void *aideen_device_ptr(aideen_ctx *ctx, int which);
 
 /* ---- allocation-free adjoint (no counterpart in the reference) -------------
