@@ -237,7 +237,7 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
   #pragma unroll
     for (int f = 0; f < F; ++f) c += dot4(wv[f], v[f]);
     const float cs = warp_sum(c) / den;
-    const size_t vbase = ((size_t)s * a.N + n) * d;
+    const size_t vbase = ((size_t)s * (a.v_ld ? a.v_ld : a.N) + n) * d;
   #pragma unroll
     for (int f = 0; f < F; ++f) {
       const int j = (f * 32 + lane) * 4;
@@ -275,7 +275,8 @@ static cudaError_t adjoint_launch(const AdjointArgs &a, cudaStream_t st) {
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, 32 * a.h, smem);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
-  const int grid = a.N < sms * per_sm ? a.N : sms * per_sm;
+  const int cap = (a.max_ctas > 0 && a.max_ctas < sms ? a.max_ctas : sms) * per_sm;
+  const int grid = a.N < cap ? a.N : cap;
   k<<<grid, 32 * a.h, smem, st>>>(a);
   return cudaGetLastError();
 }

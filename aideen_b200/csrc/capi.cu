@@ -73,6 +73,12 @@ struct aideen_ctx {
   cudaStream_t side = nullptr;
   cudaEvent_t ev_grads = nullptr, ev_lm_done = nullptr;
   bool lm_pending = false;
+  // training-step pipeline: Picard token chunks on a high-priority stream,
+  // the LM head and adjoint of each finished chunk on the context stream
+  static constexpr int kMaxChunks = 8;
+  cudaStream_t pic = nullptr;
+  cudaEvent_t ev_prep = nullptr, ev_pic[kMaxChunks] = {};
+  int sm_budget = 0;      // SMs the GEMM / softmax / adjoint launches may use (0: all)
   ncclComm_t comm = nullptr;
   int nranks = 1, rank = 0;
   std::string err;
@@ -212,7 +218,7 @@ GemmArgs gemm(int M, int N, int K, int batch, const float *A, long lda, long sA,
 // Pre-split GEMM (operands as tf32 high parts in g.A / g.B plus remainders).
 cudaError_t gemm_split(aideen_ctx *ctx, const GemmArgs &g, const float *A_lo, const float *B_lo) {
   if (!tc_split_supported(g, A_lo, B_lo)) return cudaErrorInvalidValue;
-  return tc_gemm_split(g, A_lo, B_lo, ctx->stream, ctx->b.ws, ctx->ws_floats);
+  return tc_gemm_split(g, A_lo, B_lo, ctx->stream, ctx->b.ws, ctx->ws_floats, ctx->sm_budget);
 }
 
 // GEMM dispatch: tcgen05 (3xTF32) when supported for these operands, else CUDA cores.
@@ -231,7 +237,8 @@ int check_run(aideen_ctx *ctx, const aideen_run *r) {
 }
 
 // Everything after S_in is resident: projection, slot attention, Picard, pool.
-int run_forward(aideen_ctx *ctx, const aideen_run *r, aideen_stats *stats) {
+// Projection and slot attention of a forward (everything before the Picard solve).
+int run_forward_prep(aideen_ctx *ctx, const aideen_run *r) {
   const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
   const int N = r->batch * r->seq_len;
   ctx->perm_B = r->batch;
@@ -267,6 +274,14 @@ int run_forward(aideen_ctx *ctx, const aideen_run *r, aideen_stats *stats) {
     KL(launch_attn_scale(a, N * h, st));
   }
   if (!r->fpm) CU(cudaMemsetAsync(b.hist, 0, (size_t)N * h * d * sizeof(float), st));
+  return AIDEEN_OK;
+}
+
+PicardArgs picard_args(aideen_ctx *ctx, const aideen_run *r) {
+  const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
+  const Layout &L = ctx->P;
+  DevBufs &b = ctx->b;
+  const float *W = b.W;
   PicardArgs p{};
   p.B = r->batch; p.T = r->seq_len; p.h = h; p.d = d; p.max_iters = r->max_iters;
   p.slot_coord = r->slot_coord ? 1 : 0;
@@ -281,24 +296,42 @@ int run_forward(aideen_ctx *ctx, const aideen_run *r, aideen_stats *stats) {
   p.signal = b.signal; p.A = b.A;
   p.hstar = b.hstar; p.pre = b.pre; p.hist = b.hist; p.fpmctx = b.fpmctx; p.mstate = b.mstate;
   p.iters = b.iters;
+  p.t0 = 0;
+  p.t1 = r->seq_len;
+  return p;
+}
+
+int read_solve_stats(aideen_ctx *ctx, const aideen_run *r, aideen_stats *stats) {
+  const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
+  const int N = r->batch * r->seq_len;
+  DevBufs &b = ctx->b;
+  cudaStream_t st = ctx->stream;
+  CU(cudaMemsetAsync(b.stats, 0, 4 * sizeof(unsigned long long), st));
+  KL(launch_solve_stats(b.iters, b.hstar, N * h, d, r->max_iters, b.stats, st));
+  unsigned long long hs[4];
+  CU(cudaMemcpyAsync(hs, b.stats, sizeof(hs), cudaMemcpyDeviceToHost, st));
+  CU(cudaStreamSynchronize(st));
+  stats->total_iters = hs[0];
+  stats->max_iters_seen = (uint32_t)hs[1];
+  stats->unconverged = (uint32_t)hs[2];
+  stats->nonfinite = (uint32_t)hs[3];
+  stats->solves = (uint32_t)(N * h);
+  return AIDEEN_OK;
+}
+
+int run_forward(aideen_ctx *ctx, const aideen_run *r, aideen_stats *stats) {
+  const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
+  const int N = r->batch * r->seq_len;
+  DevBufs &b = ctx->b;
+  cudaStream_t st = ctx->stream;
+  CHK(run_forward_prep(ctx, r));
+  const PicardArgs p = picard_args(ctx, r);
   KL(launch_picard(p, r->fpm != 0, st));
   KL(launch_pool_rmsnorm(b.hstar, ctx->lm_ready ? b.lmp + ctx->lm_g : nullptr,
                          b.pooled, ctx->lm_ready ? b.y : nullptr, b.lrms, N, h, d, st));
   ctx->last_run = *r;
   ctx->N = N;
-  if (stats) {
-    CU(cudaMemsetAsync(b.stats, 0, 4 * sizeof(unsigned long long), st));
-    KL(launch_solve_stats(b.iters, b.hstar, N * h, d, r->max_iters, b.stats, st));
-    unsigned long long hs[4];
-    CU(cudaMemcpyAsync(hs, b.stats, sizeof(hs), cudaMemcpyDeviceToHost, st));
-    CU(cudaStreamSynchronize(st));
-    stats->total_iters = hs[0];
-    stats->max_iters_seen = (uint32_t)hs[1];
-    stats->unconverged = (uint32_t)hs[2];
-    stats->nonfinite = (uint32_t)hs[3];
-    stats->solves = (uint32_t)(N * h);
-  }
-  return AIDEEN_OK;
+  return stats ? read_solve_stats(ctx, r, stats) : AIDEEN_OK;
 }
 
 int run_lm_head(aideen_ctx *ctx, int N, float *loss_out) {
@@ -496,6 +529,112 @@ int run_fpm_backward(aideen_ctx *ctx) {
   return AIDEEN_OK;
 }
 
+// Token chunks of the training step for the pipelined schedule (0: run the
+// step sequentially).  Pipelining pays when the Picard solve leaves SMs idle.
+int pipeline_chunks(aideen_ctx *ctx, const aideen_run *r) {
+  if (ctx->prof || getenv("AIDEEN_NO_PIPELINE")) return 0;
+  int nsm = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const int picard_ctas = (int)(r->batch * ctx->cfg.h_slots);
+  if (nsm - picard_ctas < 32) return 0;
+  if (r->batch % 4 != 0) return 0;  // chunk row offsets must keep 16-byte alignment of y^T columns
+  int nch = 4;
+  if (const char *e = getenv("AIDEEN_PIPELINE_CHUNKS")) nch = atoi(e);
+  if (nch > aideen_ctx::kMaxChunks) nch = aideen_ctx::kMaxChunks;
+  if (nch < 2 || (int)r->seq_len < 2 * nch) return 0;
+  return nch;
+}
+
+// Forward, LM head and adjoint of one training step with the Picard solve cut
+// into token chunks on the high-priority stream: when chunk j's fixed points
+// exist, pooling, the LM head (logits, softmax-CE, dy, dW_lm accumulated) and
+// the adjoint of its rows run on the context stream, capped to the SMs the
+// solve leaves free, while the solve continues with chunk j+1.  Results equal
+// the sequential schedule's (each stage is row-local or a sum over rows).
+int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aideen_stats *stats) {
+  const aideen_run *r = &a->run;
+  const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model, V = ctx->cfg.vocab;
+  const int B = r->batch, T = r->seq_len, N = B * T;
+  const long Vp = ctx->Vp, N4 = (N + 3) / 4 * 4;
+  DevBufs &b = ctx->b;
+  cudaStream_t st = ctx->stream;
+  const float *glm = b.lmp + ctx->lm_g, *Wlm = b.lmp;
+  CHK(run_forward_prep(ctx, r));
+  ctx->last_run = *r;
+  ctx->N = N;
+  // LM-head prerequisites
+  CU(join_side(ctx));
+  KL(launch_count_active(b.targets, N, b.scal, st));
+  if (ctx->lm_split_stale) {
+    KL(launch_split_hilo(Wlm, b.whi, b.wlo, (size_t)V * d, st));
+    ctx->lm_split_stale = false;
+  }
+  int nsm = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const int budget = nsm - B * h;
+  CU(cudaMemsetAsync(b.colpart, 0, (size_t)nsm * Vp * sizeof(float), st));
+  // the last chunk's consumers run after the solve has finished: all SMs
+  const bool cap_last = getenv("AIDEEN_PIPELINE_CAP_LAST") != nullptr;
+  // Picard chunks on the high-priority stream
+  CU(cudaEventRecord(ctx->ev_prep, st));
+  CU(cudaStreamWaitEvent(ctx->pic, ctx->ev_prep, 0));
+  PicardArgs p = picard_args(ctx, r);
+  for (int j = 0; j < nch; ++j) {
+    p.t0 = (int)((long)j * T / nch);
+    p.t1 = (int)((long)(j + 1) * T / nch);
+    ctx->launches++;
+    CU(launch_picard(p, r->fpm != 0, ctx->pic));
+    CU(cudaEventRecord(ctx->ev_pic[j], ctx->pic));
+  }
+  // per-chunk consumers on the context stream, within the SMs the solve leaves
+  int colpart_rows = 0;
+  for (int j = 0; j < nch; ++j) {
+    const int t0 = (int)((long)j * T / nch), t1 = (int)((long)(j + 1) * T / nch);
+    const int bud = (j + 1 < nch || cap_last) ? budget : 0;
+    ctx->sm_budget = bud;
+    const long r0 = (long)t0 * B;
+    const int R = (t1 - t0) * B;
+    CU(cudaStreamWaitEvent(st, ctx->ev_pic[j], 0));
+    KL(launch_pool_rmsnorm(b.hstar + r0 * h * d, glm, b.pooled + r0 * d, b.y + r0 * d, b.lrms + r0, R, h, d, st));
+    KL(launch_split_hilo(b.y + r0 * d, b.yhi + r0 * d, b.ylo + r0 * d, (size_t)R * d, st));
+    KL(launch_transpose_split(b.y + r0 * d, R, d, d, b.yThi + r0, b.yTlo + r0, N4, st));
+    // logits[n][v] = y[n] . W_lm[v]
+    KL(gemm_split(ctx, gemm(R, V, d, 1, b.yhi + r0 * d, d, 0, false, b.whi, d, 0, true, b.logits + r0 * Vp, Vp, 0),
+                  b.ylo + r0 * d, b.wlo));
+    KL(launch_softmax_ce_split(b.logits + r0 * Vp, b.lmp + ctx->lm_b, b.targets + r0, b.scal, R, V, Vp,
+                               b.loss_rows + r0, b.dlog_lo + r0 * Vp, b.colpart, st, bud, true));
+    const int blocks = softmax_rows_blocks(R, bud);
+    colpart_rows = blocks > colpart_rows ? blocks : colpart_rows;
+    // dy[n][j] = sum_v dlogits[n][v] W_lm[v][j]
+    KL(gemm_split(ctx, gemm(R, d, V, 1, b.logits + r0 * Vp, Vp, 0, false, b.whi, d, 0, false, b.dy + r0 * d, d, 0),
+                  b.dlog_lo + r0 * Vp, b.wlo));
+    KL(launch_rmsnorm_bwd(b.dy + r0 * d, b.pooled + r0 * d, b.lrms + r0, glm, b.dl_dh + r0 * d,
+                          b.ggp + r0 * d, R, d, st));
+    // dW_lm[v][j] += sum_{n in chunk} dlogits[n][v] y^T[j][n]
+    KL(gemm_split(ctx, gemm(V, d, R, 1, b.logits + r0 * Vp, Vp, 0, true, b.yThi + r0, N4, 0, true, b.Glm, d, 0,
+                            1.f, j > 0 ? 1.f : 0.f),
+                  b.dlog_lo + r0 * Vp, b.yTlo + r0));
+    // adjoint of the chunk's rows
+    AdjointArgs aa{};
+    aa.N = R; aa.h = h; aa.d = d; aa.iters = a->adj_iters; aa.anderson_m = a->anderson_m;
+    aa.beta = r->damping;
+    aa.pre_a = b.pre + r0 * h * d; aa.pre_b = nullptr; aa.rhs_tok = b.dl_dh + r0 * d; aa.rhs_slot = nullptr;
+    aa.NS = b.W + ctx->P.nscale; aa.v = b.v + r0 * d; aa.v_ld = N; aa.gpre = b.gpre + r0 * h * d;
+    aa.nsg = b.nsg + r0 * d; aa.max_ctas = bud;
+    if (a->anderson_m > 4) { ctx->sm_budget = 0; return set_err(ctx, AIDEEN_E_UNSUPPORTED, "anderson_m > 4"); }
+    KL(launch_adjoint(aa, st));
+  }
+  ctx->sm_budget = 0;
+  ctx->adj_N = N;
+  ctx->adj_beta = r->damping;
+  KL(launch_sum(b.loss_rows, N, b.scal + 1, st));
+  KL(launch_colsum(b.colpart, colpart_rows, V, Vp, b.Glm + ctx->lm_b, V, 0, false, st));
+  KL(launch_colsum(b.ggp, N, d, d, b.Glm + ctx->lm_g, d, 0, false, st));
+  return stats ? read_solve_stats(ctx, r, stats) : AIDEEN_OK;
+}
+
 int run_allreduce(aideen_ctx *ctx, int timeout_ms) {
   if (!ctx->comm || ctx->nranks <= 1) return AIDEEN_OK;
   ncclResult_t r = ncclGroupStart();
@@ -635,13 +774,23 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
     A(&b.lmp, ctx->lm_len); A(&b.Glm, ctx->lm_len); A(&b.Mlm1, ctx->lm_len); A(&b.Mlm2, ctx->lm_len);
     A(&b.logits, N * (size_t)ctx->Vp); A(&b.emb, V * d);
     A(&b.dlog_lo, N * (size_t)ctx->Vp); A(&b.whi, V * d); A(&b.wlo, V * d);
-    A(&b.colpart, (size_t)softmax_rows_blocks((int)N) * ctx->Vp);  // <= one row per SM
+    int nsm_dev = 0;
+    cudaDeviceGetAttribute(&nsm_dev, cudaDevAttrMultiProcessorCount, device);
+    A(&b.colpart, (size_t)(nsm_dev > 0 ? nsm_dev : 148) * ctx->Vp);  // <= one row per SM
   }
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
   ctx->own_stream = true;
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_grads, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_lm_done, cudaEventDisableTiming);
+  if (e == cudaSuccess) {
+    int lo = 0, hi = 0;
+    cudaDeviceGetStreamPriorityRange(&lo, &hi);
+    e = cudaStreamCreateWithPriority(&ctx->pic, cudaStreamNonBlocking, hi);
+  }
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_prep, cudaEventDisableTiming);
+  for (int i = 0; i < aideen_ctx::kMaxChunks && e == cudaSuccess; ++i)
+    e = cudaEventCreateWithFlags(&ctx->ev_pic[i], cudaEventDisableTiming);
   if (e != cudaSuccess) {
     aideen_destroy(ctx);
     return fail(AIDEEN_E_CUDA);
@@ -685,6 +834,10 @@ void aideen_destroy(aideen_ctx *ctx) {
   if (ctx->side) cudaStreamSynchronize(ctx->side);
   if (ctx->stream && ctx->own_stream) cudaStreamDestroy(ctx->stream);
   if (ctx->side) cudaStreamDestroy(ctx->side);
+  if (ctx->pic) { cudaStreamSynchronize(ctx->pic); cudaStreamDestroy(ctx->pic); }
+  if (ctx->ev_prep) cudaEventDestroy(ctx->ev_prep);
+  for (auto &ev : ctx->ev_pic)
+    if (ev) cudaEventDestroy(ev);
   if (ctx->ev_grads) cudaEventDestroy(ctx->ev_grads);
   if (ctx->ev_lm_done) cudaEventDestroy(ctx->ev_lm_done);
   delete ctx;
@@ -977,10 +1130,15 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
   CHK(copy_in_rows(ctx, ctx->b.tokens, tokens, a->run.batch, a->run.seq_len, 1, 1, where));
   CHK(copy_in_rows(ctx, ctx->b.targets, targets, a->run.batch, a->run.seq_len, 1, 1, where));
   KL(launch_embed(ctx->b.tokens, ctx->b.emb, ctx->b.S_in, N, ctx->cfg.d_model, ctx->cfg.vocab, ctx->stream));
-  CHK(run_forward(ctx, &a->run, stats));
-  CHK(run_lm_head(ctx, N, nullptr));
-  CHK(run_adjoint(ctx, N, ctx->b.pre, nullptr, ctx->b.dl_dh, nullptr, a->adj_iters, a->run.damping,
-                  a->anderson_m));
+  const int nch = pipeline_chunks(ctx, &a->run);
+  if (nch > 1) {
+    CHK(run_step_pipelined(ctx, a, nch, stats));
+  } else {
+    CHK(run_forward(ctx, &a->run, stats));
+    CHK(run_lm_head(ctx, N, nullptr));
+    CHK(run_adjoint(ctx, N, ctx->b.pre, nullptr, ctx->b.dl_dh, nullptr, a->adj_iters, a->run.damping,
+                    a->anderson_m));
+  }
   CHK(run_weight_grads(ctx, false));
   CHK(run_update(ctx, &a->update));
   if (a->renorm)

@@ -426,19 +426,19 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
 #endif
   // rows of the next token, loaded one token ahead
   // rows are token-major: row (t, b) = t * B + b
-  const size_t e0 = ((size_t)b * h + s) * d + j0;
+  const size_t e0 = (((size_t)a.t0 * a.B + b) * h + s) * d + j0;
   const size_t tstride = (size_t)a.B * h * d;  // one token step in a row-major [N][h][d] buffer
   float2 sig_nx = ld2(a.signal + e0);
   float2 Av_nx = a.slot_coord ? ld2(a.A + e0) : f2(0.f);
   // sum of squares of the next token's iteration-0 `dep` and `signal`,
   // reduced together with the previous token's last block reduction
   float dep0_sq = 0.f, sig_sq = 0.f;
-  for (int t = 0; t < T; ++t) {
+  for (int t = a.t0; t < a.t1; ++t) {
     const size_t n = (size_t)t * a.B + b;
     const size_t e = (n * h + s) * d + j0;
     const float2 sig = sig_nx;
     const float2 Av = Av_nx;
-    if (t + 1 < T) {
+    if (t + 1 < a.t1) {
       sig_nx = ld2(a.signal + e + tstride);
       if (a.slot_coord) Av_nx = ld2(a.A + e + tstride);
     }
@@ -449,12 +449,15 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       hcur = make_float2(sig.x / den, sig.y / den);
       sig_sq = v[0];
     }
-    if (t == 0 || !FPM) {
+    if (t > 0 && t == a.t0) {  // a later token range: continue from the stored fixed point
+      hcur = ld2(a.hstar + e - tstride);
+    }
+    if (t == a.t0 || !FPM) {
       const float2 dep0 = sig + hcur + anc + Av;
-      float v[1] = {dot2(dep0, dep0)};
+      float v[2] = {dot2(dep0, dep0), dot2(sig, sig)};
       R.sum(v);
       dep0_sq = v[0];
-      if (!FPM && t > 0) sig_sq = 0.f;  // only the FPM read uses it
+      if (t > 0) sig_sq = v[1];  // (t == 0 computed it above; only the FPM read uses it)
     }
     float2 ctx = f2(0.f);
     bool waited = false;  // this token's cluster-barrier wait
@@ -773,7 +776,7 @@ static cudaError_t picard_launch(const PicardArgs &a, cudaStream_t st) {
 }
 
 cudaError_t launch_picard(const PicardArgs &a, bool fpm, cudaStream_t st) {
-  if (a.B <= 0 || a.T <= 0) return cudaSuccess;
+  if (a.B <= 0 || a.T <= 0 || a.t1 <= a.t0) return cudaSuccess;
   if (a.d > 512) return fpm ? picard_launch<true, 512>(a, st) : picard_launch<false, 512>(a, st);
   return fpm ? picard_launch<true, 256>(a, st) : picard_launch<false, 256>(a, st);
 }

@@ -31,7 +31,7 @@ unsigned int tc_gemm_error(bool reset);
 // beta must be 0 or 1.
 bool tc_split_supported(const GemmArgs &g, const float *A_lo, const float *B_lo);
 cudaError_t tc_gemm_split(const GemmArgs &g, const float *A_lo, const float *B_lo, cudaStream_t s,
-                          float *ws = nullptr, size_t ws_floats = 0);
+                          float *ws = nullptr, size_t ws_floats = 0, int max_ctas = 0);
 unsigned int tc_split_error(bool reset);
 // x -> (hi, lo) with hi exact in tf32 and lo = x - hi (n % 4 == 0).
 cudaError_t launch_split_hilo(const float *x, float *hi, float *lo, size_t n, cudaStream_t st);
@@ -51,6 +51,7 @@ struct AttnArgs {
 
 struct PicardArgs {
   int B, T, h, d, max_iters, slot_coord;
+  int t0, t1;      // token range of this launch (state carried in hstar / mstate)
   int n_resident;  // FPM matrices staged in shared memory (set by the launcher)
   int use_tmem;    // 1: matrices 3..5 live in tensor memory (d = 512, n_resident = 3)
   float eps, blend, alpha_m, tau, gate_min;
@@ -69,7 +70,9 @@ struct AdjointArgs {
   const float *rhs_tok;        // [N][d] or null (scaled 1/h per slot)
   const float *rhs_slot;       // [N][h][d] or null
   const float *NS;
-  float *v;                    // [h][N][d]
+  float *v;                    // [h][v_ld][d] (rows n of slot s at (s * v_ld + n) * d)
+  int v_ld;                    // rows per slot block of v (0: N)
+  int max_ctas;                // SMs to use (0: every SM), at full occupancy each
   float *gpre;                 // [N][h][d]
   float *nsg;                  // [N][d] per-token NormScale-gradient partials or null
 };
@@ -132,10 +135,12 @@ cudaError_t launch_softmax_ce(float *logits, const float *bias, const int32_t *t
 // Pre-split softmax-CE over blocks of rows that also writes per-block column
 // sums of dlogits: colpart is [softmax_rows_blocks(N)][ld]; ld * 4 bytes must
 // fit in one block's shared memory (vocab <= 58,000).
-int softmax_rows_blocks(int N);
+int softmax_rows_blocks(int N, int max_blocks = 0);
+// max_blocks caps the grid (0: one block per SM); accumulate adds into colpart.
 cudaError_t launch_softmax_ce_split(float *logits, const float *bias, const int32_t *tg,
                                     const float *n_active, int N, int V, long ld, float *loss_rows,
-                                    float *lo, float *colpart, cudaStream_t st);
+                                    float *lo, float *colpart, cudaStream_t st, int max_blocks = 0,
+                                    bool accumulate = false);
 cudaError_t launch_rmsnorm_bwd(const float *dy, const float *P, const float *lrms,
                                const float *g, float *dl_dh, float *ggp, int N, int d,
                                cudaStream_t st);

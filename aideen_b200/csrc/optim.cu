@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(1024) softmax_ce_rows_kernel(float *__restrict
                                                                int V, long ld, int rows,
                                                                float *__restrict__ loss_rows,
                                                                float *__restrict__ lo_out,
-                                                               float *__restrict__ colpart) {
+                                                               float *__restrict__ colpart, int accumulate) {
   extern __shared__ __align__(16) float colacc[];
   __shared__ float rm[32], rs[32];
   constexpr float kLog2e = 1.4426950408889634f;
@@ -490,9 +490,13 @@ __global__ void __launch_bounds__(1024) softmax_ce_rows_kernel(float *__restrict
     }
   }
   float *prow = colpart + (size_t)blockIdx.x * ld;
-  for (int i = threadIdx.x; i < V4; i += blockDim.x)
-    *reinterpret_cast<float4 *>(prow + 4 * i) = *reinterpret_cast<const float4 *>(colacc + 4 * i);
-  if ((int)threadIdx.x < tail) prow[4 * V4 + threadIdx.x] = colacc[4 * V4 + threadIdx.x];
+  for (int i = threadIdx.x; i < V4; i += blockDim.x) {
+    float4 v = *reinterpret_cast<const float4 *>(colacc + 4 * i);
+    if (accumulate) v = v + *reinterpret_cast<const float4 *>(prow + 4 * i);
+    *reinterpret_cast<float4 *>(prow + 4 * i) = v;
+  }
+  if ((int)threadIdx.x < tail)
+    prow[4 * V4 + threadIdx.x] = colacc[4 * V4 + threadIdx.x] + (accumulate ? prow[4 * V4 + threadIdx.x] : 0.f);
 }
 
 namespace {
@@ -510,27 +514,28 @@ int num_sms() {
 
 // One wave: as many blocks as SMs (one block per SM: the accumulator takes
 // V floats of shared memory), each with ceil(N / blocks) rows.
-int softmax_rows_per_block(int N) {
-  const int nsm = num_sms();
+int softmax_rows_per_block(int N, int max_blocks) {
+  const int nsm = max_blocks > 0 && max_blocks < num_sms() ? max_blocks : num_sms();
   return (N + nsm - 1) / nsm;
 }
-int softmax_rows_blocks(int N) {
-  const int r = softmax_rows_per_block(N);
+int softmax_rows_blocks(int N, int max_blocks) {
+  const int r = softmax_rows_per_block(N, max_blocks);
   return (N + r - 1) / r;
 }
 
 cudaError_t launch_softmax_ce_split(float *logits, const float *bias, const int32_t *tg,
                                     const float *n_active, int N, int V, long ld, float *loss_rows,
-                                    float *lo, float *colpart, cudaStream_t st) {
+                                    float *lo, float *colpart, cudaStream_t st, int max_blocks,
+                                    bool accumulate) {
   if (N <= 0) return cudaSuccess;
   const size_t smem = (size_t)ld * sizeof(float);
   if (ld & 3 || smem > 227 * 1024) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(softmax_ce_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
-  softmax_ce_rows_kernel<<<softmax_rows_blocks(N), 1024, smem, st>>>(logits, bias, tg, n_active, N, V, ld,
-                                                                      softmax_rows_per_block(N), loss_rows, lo,
-                                                                      colpart);
+  softmax_ce_rows_kernel<<<softmax_rows_blocks(N, max_blocks), 1024, smem, st>>>(
+      logits, bias, tg, n_active, N, V, ld, softmax_rows_per_block(N, max_blocks), loss_rows, lo, colpart,
+      accumulate ? 1 : 0);
   return cudaGetLastError();
 }
 

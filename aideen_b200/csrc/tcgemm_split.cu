@@ -300,7 +300,7 @@ bool tc_split_supported(const GemmArgs &g, const float *A_lo, const float *B_lo)
 }
 
 cudaError_t tc_gemm_split(const GemmArgs &g, const float *A_lo, const float *B_lo, cudaStream_t st,
-                          float *ws, size_t ws_floats) {
+                          float *ws, size_t ws_floats, int max_ctas) {
   if (!tc_split_supported(g, A_lo, B_lo)) return cudaErrorInvalidValue;
   const bool a_k = !g.transA, b_k = g.transB;
   const bool a_b = g.strideA != 0 && g.batch > 1, b_b = g.strideB != 0 && g.batch > 1;
@@ -334,7 +334,7 @@ cudaError_t tc_gemm_split(const GemmArgs &g, const float *A_lo, const float *B_l
   p.ksplit = 1; p.kchunk = 0;
   p.alpha = g.alpha;
   p.reduce_add = g.beta == 1.f ? 1 : 0;
-  const int nsm = sm_count();
+  const int nsm = max_ctas > 0 && max_ctas < sm_count() ? max_ctas : sm_count();
   const int tiles = p.tiles_m * p.tiles_n;
   const int kblocks = (g.K + PK - 1) / PK;
   float *Cmap = g.C;

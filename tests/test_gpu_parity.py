@@ -263,3 +263,41 @@ def test_fpm_backward_tbptt_carry_across_chunks():
     be.reset_state()
     assert np.abs(be.read("fpm_carry", (B, h, d))).max() == 0.0
     be.close()
+
+
+def test_pipelined_train_step_matches_sequential_and_oracle():
+    """The chunked training step (Picard token chunks overlapped with the LM head
+    and adjoint) gives the sequential step's loss, gradients and update."""
+    import os
+    d, h, B, T, V = 128, 4, 4, 16, 61
+    c = dict(d=d, h=h, B=B, T=T, fpm=True)
+    W, _, _, rc, cfg = _setup(c, vocab=V)
+    lm, emb = init_lm_head(d, V), init_embedding(d, V)
+    rng = np.random.default_rng(31)
+    tok = rng.integers(0, V, (B, T)).astype(np.int32)
+    tg = rng.integers(0, V, (B, T)).astype(np.int32)
+    tg[1, 3] = -1
+    out = {}
+    for mode in ("seq", "pipe"):
+        if mode == "seq":
+            os.environ["AIDEEN_NO_PIPELINE"] = "1"
+        else:
+            os.environ.pop("AIDEEN_NO_PIPELINE", None)
+        be = GpuDeqBackend(d, h, max_batch=B, max_seq_len=T, vocab=V)
+        be.upload_weights(W)
+        be.upload_lm_head(*lm)
+        be.upload_embedding(emb)
+        loss = be.train_step(tok, tg, B, T, rc, adj_iters=12, lr=1e-3, step=1)
+        out[mode] = (loss, be.read_grads(), be.read("lm_grads", (V * d + V + d,)), be.read_weights(),
+                     be.read("iters", (B, T, h), np.int32))
+        be.close()
+    os.environ.pop("AIDEEN_NO_PIPELINE", None)
+    ls, gs, lgs, ws, its = out["seq"]
+    lp, gp, lgp, wp, itp = out["pipe"]
+    assert np.array_equal(its, itp)
+    assert abs(lp - ls) <= 1e-6 * abs(ls)
+    assert rel(gp, gs) < 1e-5 and rel(lgp, lgs) < 1e-5
+    cfg.adj_iters = 12
+    r = O.train_step(emb[tok], tg, W, lm, cfg)
+    assert abs(lp - r["loss"]) / r["loss"] < TOL
+    assert rel(wp.astype(np.float64) - W, r["W_new"] - W) < 5e-3
