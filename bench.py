@@ -325,8 +325,9 @@ def main():
                 "bound": "hbm", "achieved": ach, "peak": hbm, "peak_source": src, "unit": "GB/s",
                 "frac": ach / hbm, "traffic": None, "ms_per_launch": kms,
                 "algorithmic_bytes_per_launch": bytes_of[dominant],
-                "note": "latency-bound serial chain (token x iteration); HBM is not the limit"
-                        if dominant == "picard" else ""}
+                "note": (f"latency-bound serial chain: {T} tokens per launch, {1e3 * kms / T:.2f} us per token "
+                         f"(all slots of a sequence advance one token together; ~20 barrier-separated phases "
+                         f"per token); HBM is not the limit") if dominant == "picard" else ""}
     c4 = adjoint_micro(torch, hbm, src, local) if world == 1 and not args.no_micro else None
 
     if rank == 0:
@@ -344,6 +345,9 @@ def main():
                 "gpu_launches": int(launches),
                 "roofline": roof,
                 "kernel_ms_per_step": {k: round(v[0], 4) for k, v in kprof.items()},
+                "kernel_ms_note": "per-class device time from a profiled pass (CUDA events around each launch), "
+                                  "which runs the step's kernels one after another; the timed steps overlap "
+                                  "the Picard token chunks with the LM head and adjoint",
                 "roofline_adjoint_c4": c4,
                 "clocks": clk.summary()}
         if not args.no_cpu_baseline and world == 1:
