@@ -238,43 +238,53 @@ int check_run(aideen_ctx *ctx, const aideen_run *r) {
 
 // Everything after S_in is resident: projection, slot attention, Picard, pool.
 // Projection and slot attention of a forward (everything before the Picard solve).
-int run_forward_prep(aideen_ctx *ctx, const aideen_run *r) {
+// Projection and slot attention of rows [r0, r0 + R) (every op is row-local).
+int run_forward_prep_rows(aideen_ctx *ctx, const aideen_run *r, long r0, int R) {
   const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
-  const int N = r->batch * r->seq_len;
-  ctx->perm_B = r->batch;
-  ctx->perm_T = r->seq_len;
   const Layout &L = ctx->P;
   DevBufs &b = ctx->b;
   cudaStream_t st = ctx->stream;
   const float *W = b.W;
+  const long hd = (long)h * d, H32 = (long)h * kHeadDim;
+  float *signal = b.signal + r0 * hd;
   if (ctx->signal_zero) {
-    CU(cudaMemsetAsync(b.signal, 0, (size_t)N * h * d * sizeof(float), st));
+    CU(cudaMemsetAsync(signal, 0, (size_t)R * hd * sizeof(float), st));
   } else {
     // signal[n][s][:] = sigma * S_in[n] . W_in[s]   (deq_slot_attn_unified_clean.wgsl:762-804)
-    KL(gemm_any(ctx, gemm(N, d, d, h, b.S_in, d, 0, false, W + L.win, d, (long)d * d, false, b.signal,
-                     (long)h * d, d, ctx->signal_scale)));
+    KL(gemm_any(ctx, gemm(R, d, d, h, b.S_in + r0 * d, d, 0, false, W + L.win, d, (long)d * d, false, signal,
+                     hd, d, ctx->signal_scale)));
   }
   if (r->slot_coord) {
     // 32-wide K/V/Q heads of src = signal + anchor (:281-355); src is kept for the backward
-    KL(launch_add_rowbias(b.src, b.signal, W + L.slot_anchor, N, (size_t)h * d, st));
-    KL(gemm_any(ctx, gemm(N, kHeadDim, d, h, b.src, (long)h * d, d, false, W + L.wk, d, (long)d * d,
-                     false, b.Kh, (long)h * kHeadDim, kHeadDim)));
-    KL(gemm_any(ctx, gemm(N, kHeadDim, d, h, b.src, (long)h * d, d, false, W + L.wv, d, (long)d * d,
-                     false, b.Vh, (long)h * kHeadDim, kHeadDim)));
-    KL(gemm_any(ctx, gemm(N, kHeadDim, d, h, b.src, (long)h * d, d, false, W + L.wq, d, (long)d * d,
-                     false, b.Qh, (long)h * kHeadDim, kHeadDim)));
+    float *src = b.src + r0 * hd;
+    KL(launch_add_rowbias(src, signal, W + L.slot_anchor, R, (size_t)hd, st));
+    KL(gemm_any(ctx, gemm(R, kHeadDim, d, h, src, hd, d, false, W + L.wk, d, (long)d * d,
+                     false, b.Kh + r0 * H32, H32, kHeadDim)));
+    KL(gemm_any(ctx, gemm(R, kHeadDim, d, h, src, hd, d, false, W + L.wv, d, (long)d * d,
+                     false, b.Vh + r0 * H32, H32, kHeadDim)));
+    KL(gemm_any(ctx, gemm(R, kHeadDim, d, h, src, hd, d, false, W + L.wq, d, (long)d * d,
+                     false, b.Qh + r0 * H32, H32, kHeadDim)));
     AttnArgs a{};
     a.h = h; a.d = d; a.W = W; a.off_qb = L.q_bias; a.off_kb = L.k_bias; a.off_anchor = L.slot_anchor;
-    a.Qh = b.Qh; a.Kh = b.Kh; a.Vh = b.Vh; a.alpha = b.alpha; a.nmix = b.nmix; a.rmix = b.rmix;
-    a.signal = b.signal; a.amat = b.amat; a.A = b.A; a.scale = b.scale; a.rho = b.rho; a.Rsrc = b.Rsrc;
-    KL(launch_attn_softmax(a, N, st));
+    a.Qh = b.Qh + r0 * H32; a.Kh = b.Kh + r0 * H32; a.Vh = b.Vh + r0 * H32;
+    a.alpha = b.alpha + r0 * h * h; a.nmix = b.nmix + r0 * H32; a.rmix = b.rmix + r0 * h;
+    a.signal = signal; a.amat = b.amat + r0 * hd; a.A = b.A + r0 * hd;
+    a.scale = b.scale + r0 * h; a.rho = b.rho + r0 * h; a.Rsrc = b.Rsrc + r0 * h;
+    KL(launch_attn_softmax(a, R, st));
     // attn[o] = sum_k W_o[s][k*d + o] n[k]  (:452-470)
-    KL(gemm_any(ctx, gemm(N, d, kHeadDim, h, b.nmix, (long)h * kHeadDim, kHeadDim, false, W + L.wo, d,
-                     (long)d * d, false, b.amat, (long)h * d, d)));
-    KL(launch_attn_scale(a, N * h, st));
+    KL(gemm_any(ctx, gemm(R, d, kHeadDim, h, a.nmix, H32, kHeadDim, false, W + L.wo, d,
+                     (long)d * d, false, b.amat + r0 * hd, hd, d)));
+    KL(launch_attn_scale(a, R * h, st));
   }
-  if (!r->fpm) CU(cudaMemsetAsync(b.hist, 0, (size_t)N * h * d * sizeof(float), st));
+  if (!r->fpm) CU(cudaMemsetAsync(b.hist + r0 * hd, 0, (size_t)R * hd * sizeof(float), st));
   return AIDEEN_OK;
+}
+
+// Projection and slot attention of a forward (everything before the Picard solve).
+int run_forward_prep(aideen_ctx *ctx, const aideen_run *r) {
+  ctx->perm_B = r->batch;
+  ctx->perm_T = r->seq_len;
+  return run_forward_prep_rows(ctx, r, 0, r->batch * r->seq_len);
 }
 
 PicardArgs picard_args(aideen_ctx *ctx, const aideen_run *r) {
@@ -560,16 +570,16 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   DevBufs &b = ctx->b;
   cudaStream_t st = ctx->stream;
   const float *glm = b.lmp + ctx->lm_g, *Wlm = b.lmp;
-  CHK(run_forward_prep(ctx, r));
+  // forward prep of the first chunk's rows; the rest is prepared while the
+  // solve runs the first chunk
+  ctx->perm_B = B;
+  ctx->perm_T = T;
+  const int R0 = (int)((long)T / nch) * B;
+  CHK(run_forward_prep_rows(ctx, r, 0, R0));
+  CU(cudaEventRecord(ctx->ev_prep, st));
   ctx->last_run = *r;
   ctx->N = N;
-  // LM-head prerequisites
-  CU(join_side(ctx));
   KL(launch_count_active(b.targets, N, b.scal, st));
-  if (ctx->lm_split_stale) {
-    KL(launch_split_hilo(Wlm, b.whi, b.wlo, (size_t)V * d, st));
-    ctx->lm_split_stale = false;
-  }
   int nsm = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
@@ -577,11 +587,19 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   CU(cudaMemsetAsync(b.colpart, 0, (size_t)nsm * Vp * sizeof(float), st));
   // the last chunk's consumers run after the solve has finished: all SMs
   const bool cap_last = getenv("AIDEEN_PIPELINE_CAP_LAST") != nullptr;
-  // Picard chunks on the high-priority stream
-  CU(cudaEventRecord(ctx->ev_prep, st));
+  // Picard chunks on the high-priority stream: chunk 0 after its rows' prep,
+  // the others after the remaining rows' prep
   CU(cudaStreamWaitEvent(ctx->pic, ctx->ev_prep, 0));
   PicardArgs p = picard_args(ctx, r);
-  for (int j = 0; j < nch; ++j) {
+  p.t0 = 0;
+  p.t1 = (int)((long)T / nch);
+  ctx->launches++;
+  CU(launch_picard(p, r->fpm != 0, ctx->pic));
+  CU(cudaEventRecord(ctx->ev_pic[0], ctx->pic));
+  CHK(run_forward_prep_rows(ctx, r, R0, N - R0));
+  CU(cudaEventRecord(ctx->ev_prep, st));
+  CU(cudaStreamWaitEvent(ctx->pic, ctx->ev_prep, 0));
+  for (int j = 1; j < nch; ++j) {
     p.t0 = (int)((long)j * T / nch);
     p.t1 = (int)((long)(j + 1) * T / nch);
     ctx->launches++;
@@ -597,6 +615,13 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
     const long r0 = (long)t0 * B;
     const int R = (t1 - t0) * B;
     CU(cudaStreamWaitEvent(st, ctx->ev_pic[j], 0));
+    if (j == 0) {  // the previous step's deferred LM-head update must be done before the logits
+      CU(join_side(ctx));
+      if (ctx->lm_split_stale) {
+        KL(launch_split_hilo(Wlm, b.whi, b.wlo, (size_t)V * d, st));
+        ctx->lm_split_stale = false;
+      }
+    }
     KL(launch_pool_rmsnorm(b.hstar + r0 * h * d, glm, b.pooled + r0 * d, b.y + r0 * d, b.lrms + r0, R, h, d, st));
     KL(launch_split_hilo(b.y + r0 * d, b.yhi + r0 * d, b.ylo + r0 * d, (size_t)R * d, st));
     KL(launch_transpose_split(b.y + r0 * d, R, d, d, b.yThi + r0, b.yTlo + r0, N4, st));
