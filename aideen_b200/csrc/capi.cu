@@ -79,6 +79,8 @@ struct aideen_ctx {
   cudaStream_t pic = nullptr;
   cudaEvent_t ev_prep = nullptr, ev_pic[kMaxChunks] = {};
   int sm_budget = 0;      // SMs the GEMM / softmax / adjoint launches may use (0: all)
+  // optional stage timeline of the pipelined step (AIDEEN_PIPE_TIMELINE=1, stderr)
+  std::vector<std::pair<std::string, cudaEvent_t>> tl;
   ncclComm_t comm = nullptr;
   int nranks = 1, rank = 0;
   std::string err;
@@ -539,6 +541,53 @@ int run_fpm_backward(aideen_ctx *ctx) {
   return AIDEEN_OK;
 }
 
+void tl_mark(aideen_ctx *ctx, const char *name, cudaStream_t s) {
+  static const bool on = getenv("AIDEEN_PIPE_TIMELINE") != nullptr;
+  if (!on) return;
+  cudaEvent_t e;
+  cudaEventCreate(&e);
+  cudaEventRecord(e, s);
+  ctx->tl.push_back({name, e});
+}
+
+void tl_flush(aideen_ctx *ctx) {
+  if (ctx->tl.empty()) return;
+  cudaDeviceSynchronize();
+  fprintf(stderr, "[timeline]");
+  for (auto &m : ctx->tl) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, ctx->tl.front().second, m.second);
+    fprintf(stderr, " %s=%.3f", m.first.c_str(), ms);
+  }
+  fprintf(stderr, "\n");
+  for (auto &m : ctx->tl) cudaEventDestroy(m.second);
+  ctx->tl.clear();
+}
+
+// Token boundary of chunk j of nch: proportional to cumulative weights.  A
+// small first chunk lets the consumers start early; the default weights for
+// four chunks are 1,2,3,3 (measured best of the tried splits at the bench
+// shape; AIDEEN_PIPELINE_WEIGHTS overrides, comma-separated).
+int chunk_bound(int j, int nch, int T) {
+  int w[aideen_ctx::kMaxChunks] = {0};
+  int tot = 0;
+  const char *e = getenv("AIDEEN_PIPELINE_WEIGHTS");
+  for (int i = 0; i < nch; ++i) {
+    static const int kDefault4[4] = {1, 2, 3, 3};
+    int wi = (nch == 4) ? kDefault4[i] : 1;
+    if (e && *e) {
+      wi = atoi(e);
+      while (*e && *e != ',') ++e;
+      if (*e == ',') ++e;
+    }
+    w[i] = wi > 0 ? wi : 1;
+    tot += w[i];
+  }
+  int acc = 0;
+  for (int i = 0; i < j; ++i) acc += w[i];
+  return (int)((long)acc * T / tot);
+}
+
 // Token chunks of the training step for the pipelined schedule (0: run the
 // step sequentially).  Pipelining pays when the Picard solve leaves SMs idle.
 int pipeline_chunks(aideen_ctx *ctx, const aideen_run *r) {
@@ -552,7 +601,9 @@ int pipeline_chunks(aideen_ctx *ctx, const aideen_run *r) {
   int nch = 4;
   if (const char *e = getenv("AIDEEN_PIPELINE_CHUNKS")) nch = atoi(e);
   if (nch > aideen_ctx::kMaxChunks) nch = aideen_ctx::kMaxChunks;
-  if (nch < 2 || (int)r->seq_len < 2 * nch) return 0;
+  if (nch < 2) return 0;
+  for (int j = 0; j < nch; ++j)  // every chunk holds at least one token
+    if (chunk_bound(j + 1, nch, r->seq_len) <= chunk_bound(j, nch, r->seq_len)) return 0;
   return nch;
 }
 
@@ -570,11 +621,12 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   DevBufs &b = ctx->b;
   cudaStream_t st = ctx->stream;
   const float *glm = b.lmp + ctx->lm_g, *Wlm = b.lmp;
+  tl_mark(ctx, "start", st);
   // forward prep of the first chunk's rows; the rest is prepared while the
   // solve runs the first chunk
   ctx->perm_B = B;
   ctx->perm_T = T;
-  const int R0 = (int)((long)T / nch) * B;
+  const int R0 = chunk_bound(1, nch, T) * B;
   CHK(run_forward_prep_rows(ctx, r, 0, R0));
   CU(cudaEventRecord(ctx->ev_prep, st));
   ctx->last_run = *r;
@@ -592,24 +644,27 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   CU(cudaStreamWaitEvent(ctx->pic, ctx->ev_prep, 0));
   PicardArgs p = picard_args(ctx, r);
   p.t0 = 0;
-  p.t1 = (int)((long)T / nch);
+  p.t1 = chunk_bound(1, nch, T);
   ctx->launches++;
   CU(launch_picard(p, r->fpm != 0, ctx->pic));
   CU(cudaEventRecord(ctx->ev_pic[0], ctx->pic));
+  tl_mark(ctx, "pic0", ctx->pic);
   CHK(run_forward_prep_rows(ctx, r, R0, N - R0));
+  tl_mark(ctx, "prep", st);
   CU(cudaEventRecord(ctx->ev_prep, st));
   CU(cudaStreamWaitEvent(ctx->pic, ctx->ev_prep, 0));
   for (int j = 1; j < nch; ++j) {
-    p.t0 = (int)((long)j * T / nch);
-    p.t1 = (int)((long)(j + 1) * T / nch);
+    p.t0 = chunk_bound(j, nch, T);
+    p.t1 = chunk_bound(j + 1, nch, T);
     ctx->launches++;
     CU(launch_picard(p, r->fpm != 0, ctx->pic));
     CU(cudaEventRecord(ctx->ev_pic[j], ctx->pic));
+    tl_mark(ctx, ("pic" + std::to_string(j)).c_str(), ctx->pic);
   }
   // per-chunk consumers on the context stream, within the SMs the solve leaves
   int colpart_rows = 0;
   for (int j = 0; j < nch; ++j) {
-    const int t0 = (int)((long)j * T / nch), t1 = (int)((long)(j + 1) * T / nch);
+    const int t0 = chunk_bound(j, nch, T), t1 = chunk_bound(j + 1, nch, T);
     const int bud = (j + 1 < nch || cap_last) ? budget : 0;
     ctx->sm_budget = bud;
     const long r0 = (long)t0 * B;
@@ -650,6 +705,7 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
     aa.nsg = b.nsg + r0 * d; aa.max_ctas = bud;
     if (a->anderson_m > 4) { ctx->sm_budget = 0; return set_err(ctx, AIDEEN_E_UNSUPPORTED, "anderson_m > 4"); }
     KL(launch_adjoint(aa, st));
+    tl_mark(ctx, ("cons" + std::to_string(j)).c_str(), st);
   }
   ctx->sm_budget = 0;
   ctx->adj_N = N;
@@ -1165,7 +1221,10 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
                     a->anderson_m));
   }
   CHK(run_weight_grads(ctx, false));
+  tl_mark(ctx, "wgrads", ctx->stream);
   CHK(run_update(ctx, &a->update));
+  tl_mark(ctx, "update", ctx->stream);
+  tl_flush(ctx);
   if (a->renorm)
     KL(launch_spectral(ctx->b.W, ctx->cfg.d_model, ctx->cfg.h_slots, ctx->P, 12, 0.10f, 0.30f, 0.70f,
                        0.50f, 0.50f, ctx->b.sigmas, ctx->stream));
