@@ -588,6 +588,16 @@ int chunk_bound(int j, int nch, int T) {
   return (int)((long)acc * T / tot);
 }
 
+// chunk_bound rounded so every chunk's rows (tokens x B) fill whole 128-row
+// GEMM tiles where B divides 128 (the first and last bounds stay 0 and T)
+int chunk_bound_aligned(int j, int nch, int T, int B) {
+  const int t = chunk_bound(j, nch, T);
+  if (j == 0 || j == nch || B <= 0 || 128 % B != 0) return t;
+  const int q = 128 / B;
+  const int r = (t + q / 2) / q * q;
+  return r > 0 && r < T ? r : t;
+}
+
 // Token chunks of the training step for the pipelined schedule (0: run the
 // step sequentially).  Pipelining pays when the Picard solve leaves SMs idle.
 int pipeline_chunks(aideen_ctx *ctx, const aideen_run *r) {
@@ -603,7 +613,9 @@ int pipeline_chunks(aideen_ctx *ctx, const aideen_run *r) {
   if (nch > aideen_ctx::kMaxChunks) nch = aideen_ctx::kMaxChunks;
   if (nch < 2) return 0;
   for (int j = 0; j < nch; ++j)  // every chunk holds at least one token
-    if (chunk_bound(j + 1, nch, r->seq_len) <= chunk_bound(j, nch, r->seq_len)) return 0;
+    if (chunk_bound_aligned(j + 1, nch, r->seq_len, r->batch) <=
+        chunk_bound_aligned(j, nch, r->seq_len, r->batch))
+      return 0;
   return nch;
 }
 
@@ -626,7 +638,7 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   // solve runs the first chunk
   ctx->perm_B = B;
   ctx->perm_T = T;
-  const int R0 = chunk_bound(1, nch, T) * B;
+  const int R0 = chunk_bound_aligned(1, nch, T, B) * B;
   CHK(run_forward_prep_rows(ctx, r, 0, R0));
   CU(cudaEventRecord(ctx->ev_prep, st));
   ctx->last_run = *r;
@@ -644,7 +656,7 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   CU(cudaStreamWaitEvent(ctx->pic, ctx->ev_prep, 0));
   PicardArgs p = picard_args(ctx, r);
   p.t0 = 0;
-  p.t1 = chunk_bound(1, nch, T);
+  p.t1 = chunk_bound_aligned(1, nch, T, B);
   ctx->launches++;
   CU(launch_picard(p, r->fpm != 0, ctx->pic));
   CU(cudaEventRecord(ctx->ev_pic[0], ctx->pic));
@@ -654,8 +666,8 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   CU(cudaEventRecord(ctx->ev_prep, st));
   CU(cudaStreamWaitEvent(ctx->pic, ctx->ev_prep, 0));
   for (int j = 1; j < nch; ++j) {
-    p.t0 = chunk_bound(j, nch, T);
-    p.t1 = chunk_bound(j + 1, nch, T);
+    p.t0 = chunk_bound_aligned(j, nch, T, B);
+    p.t1 = chunk_bound_aligned(j + 1, nch, T, B);
     ctx->launches++;
     CU(launch_picard(p, r->fpm != 0, ctx->pic));
     CU(cudaEventRecord(ctx->ev_pic[j], ctx->pic));
@@ -664,7 +676,7 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   // per-chunk consumers on the context stream, within the SMs the solve leaves
   int colpart_rows = 0;
   for (int j = 0; j < nch; ++j) {
-    const int t0 = chunk_bound(j, nch, T), t1 = chunk_bound(j + 1, nch, T);
+    const int t0 = chunk_bound_aligned(j, nch, T, B), t1 = chunk_bound_aligned(j + 1, nch, T, B);
     const int bud = (j + 1 < nch || cap_last) ? budget : 0;
     ctx->sm_budget = bud;
     const long r0 = (long)t0 * B;
