@@ -52,6 +52,7 @@ struct DevBufs {
   float *sigmas = nullptr;
   float *stage = nullptr;  // packed AllWeights staging for upload/download
   float *ws = nullptr;     // split-K partial sums of the tensor-core GEMM
+  float *ws2 = nullptr;    // the same for GEMMs on the FPM-backward stream
   // FPM backward (allocated on first use): [N][h][d] unless noted
   float *fc = nullptr, *frp = nullptr, *fdl = nullptr, *fminner = nullptr, *fdm = nullptr,
         *fgpre = nullptr;
@@ -78,6 +79,9 @@ struct aideen_ctx {
   static constexpr int kMaxChunks = 8;
   cudaStream_t pic = nullptr;
   cudaEvent_t ev_prep = nullptr, ev_pic[kMaxChunks] = {};
+  // FPM backward stream: runs beside the attention-branch weight gradients
+  cudaStream_t fst = nullptr;
+  cudaEvent_t ev_g0 = nullptr, ev_fdone = nullptr;
   int sm_budget = 0;      // SMs the GEMM / softmax / adjoint launches may use (0: all)
   // optional stage timeline of the pipelined step (AIDEEN_PIPE_TIMELINE=1, stderr)
   std::vector<std::pair<std::string, cudaEvent_t>> tl;
@@ -429,6 +433,23 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   const bool sc = ctx->last_run.slot_coord != 0;
   const int H32 = h * kHeadDim;
   CU(cudaMemsetAsync(G, 0, ctx->W_len * sizeof(float), st));
+  // The FPM backward writes only its own gradient segments: without
+  // profiling it runs on its own stream (and split-K workspace) beside the
+  // attention-branch gradients below.
+  const bool fork_fpm = ctx->last_run.fpm && !ctx->prof && ctx->fst;
+  if (fork_fpm) {
+    CU(cudaEventRecord(ctx->ev_g0, st));
+    CU(cudaStreamWaitEvent(ctx->fst, ctx->ev_g0, 0));
+    cudaStream_t keep_st = ctx->stream;
+    float *keep_ws = ctx->b.ws;
+    ctx->stream = ctx->fst;
+    ctx->b.ws = ctx->b.ws2;
+    const int rc = run_fpm_backward(ctx);
+    ctx->stream = keep_st;
+    ctx->b.ws = keep_ws;
+    CHK(rc);
+    CU(cudaEventRecord(ctx->ev_fdone, ctx->fst));
+  }
   KL(launch_colsum(b.nsg, N, d, d, G + L.nscale, d, 0, false, st));
   AttnBwdArgs a{};
   a.h = h; a.d = d; a.W = W; a.off_qb = L.q_bias; a.off_kb = L.k_bias; a.off_anchor = L.slot_anchor;
@@ -474,7 +495,8 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   } else if (want_ds) {
     CU(cudaMemsetAsync(b.dS, 0, (size_t)N * d * sizeof(float), st));
   }
-  if (ctx->last_run.fpm) CHK(run_fpm_backward(ctx));
+  if (fork_fpm) CU(cudaStreamWaitEvent(st, ctx->ev_fdone, 0));
+  else if (ctx->last_run.fpm) CHK(run_fpm_backward(ctx));
   return AIDEEN_OK;
 }
 
@@ -862,7 +884,7 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   A(&b.yThi, d * ((N + 3) / 4 * 4)); A(&b.yTlo, d * ((N + 3) / 4 * 4)); A(&b.ggp, N * d); A(&b.lrms, N); A(&b.loss_rows, N);
   A(&b.scal, 4); A(&b.stage, ctx->Lx.total);
   ctx->ws_floats = 16 * N * d;  // up to 16 splits of an [N][d] output
-  A(&b.ws, ctx->ws_floats); A(&b.stats, 4); A(&b.sigmas, 5 * h + 2);
+  A(&b.ws, ctx->ws_floats); A(&b.ws2, ctx->ws_floats); A(&b.stats, 4); A(&b.sigmas, 5 * h + 2);
   if (V) {
     A(&b.lmp, ctx->lm_len); A(&b.Glm, ctx->lm_len); A(&b.Mlm1, ctx->lm_len); A(&b.Mlm2, ctx->lm_len);
     A(&b.logits, N * (size_t)ctx->Vp); A(&b.emb, V * d);
@@ -882,6 +904,9 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
     e = cudaStreamCreateWithPriority(&ctx->pic, cudaStreamNonBlocking, hi);
   }
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_prep, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->fst, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_g0, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_fdone, cudaEventDisableTiming);
   for (int i = 0; i < aideen_ctx::kMaxChunks && e == cudaSuccess; ++i)
     e = cudaEventCreateWithFlags(&ctx->ev_pic[i], cudaEventDisableTiming);
   if (e != cudaSuccess) {
@@ -921,7 +946,7 @@ void aideen_destroy(aideen_ctx *ctx) {
                   b.Mlm2, b.y, b.lrms, b.logits, b.dy, b.ggp, b.loss_rows, b.scal, b.emb, b.stats,
                   b.sigmas, b.stage, b.ws, b.fc, b.frp, b.fdl, b.fminner, b.fdm, b.fgpre, b.fup,
                   b.fkw, b.fdup, b.fA, b.fU, b.fgin, b.fcarry, b.fpart, b.fpart_bw, b.src,
-                  b.dlog_lo, b.yhi, b.ylo, b.yThi, b.yTlo, b.whi, b.wlo, b.colpart, b.perm};
+                  b.dlog_lo, b.yhi, b.ylo, b.yThi, b.yTlo, b.whi, b.wlo, b.colpart, b.perm, b.ws2};
   for (void *p : ptrs)
     if (p) cudaFree(p);
   if (ctx->side) cudaStreamSynchronize(ctx->side);
@@ -929,6 +954,9 @@ void aideen_destroy(aideen_ctx *ctx) {
   if (ctx->side) cudaStreamDestroy(ctx->side);
   if (ctx->pic) { cudaStreamSynchronize(ctx->pic); cudaStreamDestroy(ctx->pic); }
   if (ctx->ev_prep) cudaEventDestroy(ctx->ev_prep);
+  if (ctx->fst) { cudaStreamSynchronize(ctx->fst); cudaStreamDestroy(ctx->fst); }
+  if (ctx->ev_g0) cudaEventDestroy(ctx->ev_g0);
+  if (ctx->ev_fdone) cudaEventDestroy(ctx->ev_fdone);
   for (auto &ev : ctx->ev_pic)
     if (ev) cudaEventDestroy(ev);
   if (ctx->ev_grads) cudaEventDestroy(ctx->ev_grads);
