@@ -82,6 +82,7 @@ struct aideen_ctx {
   // FPM backward stream: runs beside the attention-branch weight gradients
   cudaStream_t fst = nullptr;
   cudaEvent_t ev_g0 = nullptr, ev_fdone = nullptr;
+  bool fpm_prepared = false;  // the FPM backward's forward-only stage already ran this step
   int sm_budget = 0;      // SMs the GEMM / softmax / adjoint launches may use (0: all)
   // optional stage timeline of the pipelined step (AIDEEN_PIPE_TIMELINE=1, stderr)
   std::vector<std::pair<std::string, cudaEvent_t>> tl;
@@ -418,7 +419,7 @@ int run_adjoint(aideen_ctx *ctx, int N, const float *pre_a, const float *pre_b,
   return AIDEEN_OK;
 }
 
-int run_fpm_backward(aideen_ctx *ctx);
+int run_fpm_backward(aideen_ctx *ctx, bool prepare_only = false);
 
 int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
@@ -502,7 +503,7 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
 
 // FPM memory backward over the last forward's chunk (fpm_bwd.cu); adds the
 // FPM parameters' gradients to G and advances the TBPTT carry.
-int run_fpm_backward(aideen_ctx *ctx) {
+int run_fpm_backward(aideen_ctx *ctx, bool prepare_only) {
   const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
   const int B = ctx->last_run.batch, T = ctx->last_run.seq_len, N = B * T;
   const Layout &L = ctx->P;
@@ -534,6 +535,8 @@ int run_fpm_backward(aideen_ctx *ctx) {
   a.carry = b.fcarry; a.part = b.fpart; a.part_bw = b.fpart_bw;
   ctx->prof_phase = AIDEEN_PROF_FPM_BWD;
   struct PhaseReset { aideen_ctx *c; ~PhaseReset() { c->prof_phase = -1; } } phase_reset{ctx};
+  if (!ctx->fpm_prepared || prepare_only) {
+  // forward-only stage: c and the rank-32 projections (needs h*, not v)
   KL(launch_fpm_c(b.hstar, b.signal, b.fc, (size_t)N * h * d, st));
   // up[n][s][r] = sum_j c W_retain_up[s][j][r];  kw = same with W_k_write
   KL(gemm_any(ctx, gemm(N, R, d, h, b.fc, hd, d, false, W + L.w_retain_up, R, (long)d * R, false,
@@ -545,6 +548,12 @@ int run_fpm_backward(aideen_ctx *ctx) {
                    b.frp, hd, d)));
   KL(gemm_any(ctx, gemm(N, d, R, h, b.fkw, HR, R, false, W + L.w_v_write, d, (long)R * d, false,
                    b.fdl, hd, d)));
+  }
+  if (prepare_only) {
+    ctx->fpm_prepared = true;
+    return AIDEEN_OK;
+  }
+  ctx->fpm_prepared = false;
   KL(launch_fpm_composite(a, st));
   KL(launch_fpm_carry(a, st));
   KL(launch_fpm_chunks(a, st));
@@ -694,6 +703,18 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
     CU(launch_picard(p, r->fpm != 0, ctx->pic));
     CU(cudaEventRecord(ctx->ev_pic[j], ctx->pic));
     tl_mark(ctx, ("pic" + std::to_string(j)).c_str(), ctx->pic);
+  }
+  // the FPM backward's forward-only stage once the solve is done, on its stream
+  if (r->fpm && ctx->fst) {
+    CU(cudaStreamWaitEvent(ctx->fst, ctx->ev_pic[nch - 1], 0));
+    cudaStream_t keep_st = ctx->stream;
+    float *keep_ws = ctx->b.ws;
+    ctx->stream = ctx->fst;
+    ctx->b.ws = ctx->b.ws2;
+    const int rc = run_fpm_backward(ctx, true);
+    ctx->stream = keep_st;
+    ctx->b.ws = keep_ws;
+    CHK(rc);
   }
   // per-chunk consumers on the context stream, within the SMs the solve leaves
   int colpart_rows = 0;
