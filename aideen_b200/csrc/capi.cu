@@ -48,6 +48,7 @@ struct DevBufs {
   float *dlog_lo = nullptr, *yhi = nullptr, *ylo = nullptr, *yThi = nullptr, *yTlo = nullptr;
   float *whi = nullptr, *wlo = nullptr;
   float *colpart = nullptr;  // [blocks][Vp] per-block column sums of dlogits
+  float2 *rowstats = nullptr;  // [N][ceil(V / 256)] softmax statistics from the logits GEMM
   unsigned long long *stats = nullptr;
   float *sigmas = nullptr;
   float *stage = nullptr;  // packed AllWeights staging for upload/download
@@ -223,9 +224,11 @@ GemmArgs gemm(int M, int N, int K, int batch, const float *A, long lda, long sA,
 }
 
 // Pre-split GEMM (operands as tf32 high parts in g.A / g.B plus remainders).
-cudaError_t gemm_split(aideen_ctx *ctx, const GemmArgs &g, const float *A_lo, const float *B_lo) {
+cudaError_t gemm_split(aideen_ctx *ctx, const GemmArgs &g, const float *A_lo, const float *B_lo,
+                       const float *row_bias = nullptr, float2 *row_stats = nullptr) {
   if (!tc_split_supported(g, A_lo, B_lo)) return cudaErrorInvalidValue;
-  return tc_gemm_split(g, A_lo, B_lo, ctx->stream, ctx->b.ws, ctx->ws_floats, ctx->sm_budget);
+  return tc_gemm_split(g, A_lo, B_lo, ctx->stream, ctx->b.ws, ctx->ws_floats, ctx->sm_budget, row_bias,
+                       row_stats);
 }
 
 // GEMM dispatch: tcgen05 (3xTF32) when supported for these operands, else CUDA cores.
@@ -736,10 +739,12 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
     KL(launch_split_hilo(b.y + r0 * d, b.yhi + r0 * d, b.ylo + r0 * d, (size_t)R * d, st));
     KL(launch_transpose_split(b.y + r0 * d, R, d, d, b.yThi + r0, b.yTlo + r0, N4, st));
     // logits[n][v] = y[n] . W_lm[v]
+    const long NT = (V + 255) / 256;
     KL(gemm_split(ctx, gemm(R, V, d, 1, b.yhi + r0 * d, d, 0, false, b.whi, d, 0, true, b.logits + r0 * Vp, Vp, 0),
-                  b.ylo + r0 * d, b.wlo));
+                  b.ylo + r0 * d, b.wlo, b.lmp + ctx->lm_b, b.rowstats + r0 * NT));
     KL(launch_softmax_ce_split(b.logits + r0 * Vp, b.lmp + ctx->lm_b, b.targets + r0, b.scal, R, V, Vp,
-                               b.loss_rows + r0, b.dlog_lo + r0 * Vp, b.colpart, st, bud, true));
+                               b.loss_rows + r0, b.dlog_lo + r0 * Vp, b.colpart, st, bud, true,
+                               b.rowstats + r0 * NT));
     const int blocks = softmax_rows_blocks(R, bud);
     colpart_rows = blocks > colpart_rows ? blocks : colpart_rows;
     // dy[n][j] = sum_v dlogits[n][v] W_lm[v][j]
@@ -913,6 +918,7 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
     int nsm_dev = 0;
     cudaDeviceGetAttribute(&nsm_dev, cudaDevAttrMultiProcessorCount, device);
     A(&b.colpart, (size_t)(nsm_dev > 0 ? nsm_dev : 148) * ctx->Vp);  // <= one row per SM
+    A(&b.rowstats, N * ((V + 255) / 256));
   }
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
   ctx->own_stream = true;
@@ -967,7 +973,7 @@ void aideen_destroy(aideen_ctx *ctx) {
                   b.Mlm2, b.y, b.lrms, b.logits, b.dy, b.ggp, b.loss_rows, b.scal, b.emb, b.stats,
                   b.sigmas, b.stage, b.ws, b.fc, b.frp, b.fdl, b.fminner, b.fdm, b.fgpre, b.fup,
                   b.fkw, b.fdup, b.fA, b.fU, b.fgin, b.fcarry, b.fpart, b.fpart_bw, b.src,
-                  b.dlog_lo, b.yhi, b.ylo, b.yThi, b.yTlo, b.whi, b.wlo, b.colpart, b.perm, b.ws2};
+                  b.dlog_lo, b.yhi, b.ylo, b.yThi, b.yTlo, b.whi, b.wlo, b.colpart, b.perm, b.ws2, b.rowstats};
   for (void *p : ptrs)
     if (p) cudaFree(p);
   if (ctx->side) cudaStreamSynchronize(ctx->side);

@@ -30,8 +30,11 @@ unsigned int tc_gemm_error(bool reset);
 // hold the tf32-exact high parts, A_lo / B_lo the remainders (same strides);
 // beta must be 0 or 1.
 bool tc_split_supported(const GemmArgs &g, const float *A_lo, const float *B_lo);
+// row_stats (with row_bias): per-(row, 256-column tile) softmax statistics of
+// C + bias in base 2, (max, sum exp2(z - max)), [M][ceil(N / 256)] (batch 1).
 cudaError_t tc_gemm_split(const GemmArgs &g, const float *A_lo, const float *B_lo, cudaStream_t s,
-                          float *ws = nullptr, size_t ws_floats = 0, int max_ctas = 0);
+                          float *ws = nullptr, size_t ws_floats = 0, int max_ctas = 0,
+                          const float *row_bias = nullptr, float2 *row_stats = nullptr);
 unsigned int tc_split_error(bool reset);
 // x -> (hi, lo) with hi exact in tf32 and lo = x - hi (n % 4 == 0).
 cudaError_t launch_split_hilo(const float *x, float *hi, float *lo, size_t n, cudaStream_t st);
@@ -137,10 +140,12 @@ cudaError_t launch_softmax_ce(float *logits, const float *bias, const int32_t *t
 // fit in one block's shared memory (vocab <= 58,000).
 int softmax_rows_blocks(int N, int max_blocks = 0);
 // max_blocks caps the grid (0: one block per SM); accumulate adds into colpart.
+// stats: optional per-(row, 256-column tile) statistics from the logits GEMM
+// ([N][ceil(V / 256)]); with them the row's max / sum need no read pass.
 cudaError_t launch_softmax_ce_split(float *logits, const float *bias, const int32_t *tg,
                                     const float *n_active, int N, int V, long ld, float *loss_rows,
                                     float *lo, float *colpart, cudaStream_t st, int max_blocks = 0,
-                                    bool accumulate = false);
+                                    bool accumulate = false, const float2 *stats = nullptr);
 cudaError_t launch_rmsnorm_bwd(const float *dy, const float *P, const float *lrms,
                                const float *g, float *dl_dh, float *ggp, int N, int d,
                                cudaStream_t st);

@@ -405,7 +405,8 @@ __global__ void __launch_bounds__(1024) softmax_ce_rows_kernel(float *__restrict
                                                                int V, long ld, int rows,
                                                                float *__restrict__ loss_rows,
                                                                float *__restrict__ lo_out,
-                                                               float *__restrict__ colpart, int accumulate) {
+                                                               float *__restrict__ colpart, int accumulate,
+                                                               const float2 *__restrict__ stats) {
   extern __shared__ __align__(16) float colacc[];
   __shared__ float rm[32], rs[32];
   constexpr float kLog2e = 1.4426950408889634f;
@@ -426,20 +427,30 @@ __global__ void __launch_bounds__(1024) softmax_ce_rows_kernel(float *__restrict
     float *lrow = lo_out + (size_t)n * ld;
     const int t = tg[n];
     float m = -INFINITY, sacc = 0.f;
-    for (int i = threadIdx.x; i < V4; i += blockDim.x) {
-      const float4 x4 = *reinterpret_cast<const float4 *>(row + 4 * i);
-      const float4 b4 = bias4(i);
-      const float4 x = make_float4((x4.x + b4.x) * kLog2e, (x4.y + b4.y) * kLog2e, (x4.z + b4.z) * kLog2e,
-                                   (x4.w + b4.w) * kLog2e);
-      const float mx = fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w));
-      if (mx > m) { sacc *= exp2f(m - mx); m = mx; }
-      sacc += exp2f(x.x - m) + exp2f(x.y - m) + exp2f(x.z - m) + exp2f(x.w - m);
-    }
-    if ((int)threadIdx.x < tail) {
-      const int i = 4 * V4 + threadIdx.x;
-      const float x = (row[i] + bias[i]) * kLog2e;
-      if (x > m) { sacc *= exp2f(m - x); m = x; }
-      sacc += exp2f(x - m);
+    if (stats) {  // combine the GEMM epilogue's per-tile statistics
+      const int nt = (V + 255) / 256;
+      for (int i = threadIdx.x; i < nt; i += blockDim.x) {
+        const float2 tsm = stats[(size_t)n * nt + i];
+        if (tsm.x == -INFINITY) continue;
+        if (tsm.x > m) { sacc = sacc * exp2f(m - tsm.x) + tsm.y; m = tsm.x; }
+        else sacc += tsm.y * exp2f(tsm.x - m);
+      }
+    } else {
+      for (int i = threadIdx.x; i < V4; i += blockDim.x) {
+        const float4 x4 = *reinterpret_cast<const float4 *>(row + 4 * i);
+        const float4 b4 = bias4(i);
+        const float4 x = make_float4((x4.x + b4.x) * kLog2e, (x4.y + b4.y) * kLog2e, (x4.z + b4.z) * kLog2e,
+                                     (x4.w + b4.w) * kLog2e);
+        const float mx = fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w));
+        if (mx > m) { sacc *= exp2f(m - mx); m = mx; }
+        sacc += exp2f(x.x - m) + exp2f(x.y - m) + exp2f(x.z - m) + exp2f(x.w - m);
+      }
+      if ((int)threadIdx.x < tail) {
+        const int i = 4 * V4 + threadIdx.x;
+        const float x = (row[i] + bias[i]) * kLog2e;
+        if (x > m) { sacc *= exp2f(m - x); m = x; }
+        sacc += exp2f(x - m);
+      }
     }
     for (int o = 16; o > 0; o >>= 1) {
       const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, sacc, o);
@@ -526,7 +537,7 @@ int softmax_rows_blocks(int N, int max_blocks) {
 cudaError_t launch_softmax_ce_split(float *logits, const float *bias, const int32_t *tg,
                                     const float *n_active, int N, int V, long ld, float *loss_rows,
                                     float *lo, float *colpart, cudaStream_t st, int max_blocks,
-                                    bool accumulate) {
+                                    bool accumulate, const float2 *stats) {
   if (N <= 0) return cudaSuccess;
   const size_t smem = (size_t)ld * sizeof(float);
   if (ld & 3 || smem > 227 * 1024) return cudaErrorInvalidValue;
@@ -535,7 +546,7 @@ cudaError_t launch_softmax_ce_split(float *logits, const float *bias, const int3
   if (e != cudaSuccess) return e;
   softmax_ce_rows_kernel<<<softmax_rows_blocks(N, max_blocks), 1024, smem, st>>>(
       logits, bias, tg, n_active, N, V, ld, softmax_rows_per_block(N, max_blocks), loss_rows, lo, colpart,
-      accumulate ? 1 : 0);
+      accumulate ? 1 : 0, stats);
   return cudaGetLastError();
 }
 

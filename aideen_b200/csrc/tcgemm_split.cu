@@ -47,6 +47,11 @@ struct SplitParams {
   int ksplit, kchunk;          // split-K when ksplit > 1 (z = split index, operands unbatched)
   float alpha;
   int reduce_add;
+  // optional per-(row, 256-column tile) softmax statistics of (C + bias) in
+  // base 2: row_stats[row * tiles_n + tile] = (max z, sum exp2(z - max)),
+  // z = (alpha * acc + bias[col]) * log2(e)
+  const float *row_bias;
+  float2 *row_stats;
 };
 
 __global__ void __launch_bounds__(P_THREADS, 1)
@@ -211,6 +216,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int rowbase = m0 + q * 32;
+      float st_m = -INFINITY, st_s = 0.f;  // this lane's row: running softmax statistics
 #pragma unroll 1
       for (int c = 0; c < PN / 32; ++c) {
         uint32_t r[32];
@@ -232,6 +238,24 @@ __global__ void __launch_bounds__(P_THREADS, 1)
           if (lane == 0) mbar_arrive(&tempty[a]);
         }
         const int col = n0 + c * 32;
+        if (p.row_stats) {
+          constexpr float kLog2e = 1.4426950408889634f;
+          float zc[32];
+          float mc = -INFINITY;
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            zc[k] = col + k < p.N ? (p.alpha * __uint_as_float(r[k]) + __ldg(p.row_bias + col + k)) * kLog2e
+                                  : -INFINITY;
+            mc = fmaxf(mc, zc[k]);
+          }
+          if (mc > -INFINITY) {
+            float sc = 0.f;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) sc += exp2f(zc[k] - mc);
+            if (mc > st_m) { st_s = st_s * exp2f(st_m - mc) + sc; st_m = mc; }
+            else st_s += sc * exp2f(mc - st_m);
+          }
+        }
         if (col >= p.N || rowbase >= p.M) continue;  // box entirely outside C
         unsigned char *box = mybox + (nst & 1) * PBOX_BYTES;
         if (lane == 0) bulk_wait_read<1>();  // the store issued from this box two boxes ago is done reading
@@ -251,6 +275,8 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         }
         ++nst;
       }
+      if (p.row_stats && rowbase + lane < p.M)
+        p.row_stats[(size_t)(rowbase + lane) * p.tiles_n + n0 / PN] = make_float2(st_m, st_s);
     }
     if (lane == 0) bulk_wait<0>();  // stores complete before the CTA's shared memory goes away
   }
@@ -300,8 +326,10 @@ bool tc_split_supported(const GemmArgs &g, const float *A_lo, const float *B_lo)
 }
 
 cudaError_t tc_gemm_split(const GemmArgs &g, const float *A_lo, const float *B_lo, cudaStream_t st,
-                          float *ws, size_t ws_floats, int max_ctas) {
+                          float *ws, size_t ws_floats, int max_ctas, const float *row_bias,
+                          float2 *row_stats) {
   if (!tc_split_supported(g, A_lo, B_lo)) return cudaErrorInvalidValue;
+  if (row_stats && (g.batch != 1 || !row_bias)) return cudaErrorInvalidValue;
   const bool a_k = !g.transA, b_k = g.transB;
   const bool a_b = g.strideA != 0 && g.batch > 1, b_b = g.strideB != 0 && g.batch > 1;
   CUtensorMap mah, mal, mbh, mbl, mc;
@@ -334,6 +362,8 @@ cudaError_t tc_gemm_split(const GemmArgs &g, const float *A_lo, const float *B_l
   p.ksplit = 1; p.kchunk = 0;
   p.alpha = g.alpha;
   p.reduce_add = g.beta == 1.f ? 1 : 0;
+  p.row_bias = row_bias;
+  p.row_stats = row_stats;
   const int nsm = max_ctas > 0 && max_ctas < sm_count() ? max_ctas : sm_count();
   const int tiles = p.tiles_m * p.tiles_n;
   const int kblocks = (g.K + PK - 1) / PK;
@@ -342,7 +372,7 @@ cudaError_t tc_gemm_split(const GemmArgs &g, const float *A_lo, const float *B_l
   int cz = g.batch;
   // Split K when the output has too few tiles to keep every SM busy: pick the
   // split count (<= 16) that minimises the per-CTA share of K blocks.
-  if (ws && g.batch == 1 && tiles < nsm && kblocks >= 128) {
+  if (ws && g.batch == 1 && tiles < nsm && kblocks >= 128 && !row_stats) {
     int best = 1;
     double best_cost = (double)kblocks;  // one unit of all K blocks per CTA
     for (int s = 2; s <= 16; ++s) {
