@@ -600,14 +600,14 @@ void tl_flush(aideen_ctx *ctx) {
 
 // Token boundary of chunk j of nch: proportional to cumulative weights.  A
 // small first chunk lets the consumers start early; the default weights for
-// four chunks are 1,2,3,3 (measured best of the tried splits at the bench
+// four chunks are 1,2,3,4 (measured best of the tried splits at the bench
 // shape; AIDEEN_PIPELINE_WEIGHTS overrides, comma-separated).
 int chunk_bound(int j, int nch, int T) {
   int w[aideen_ctx::kMaxChunks] = {0};
   int tot = 0;
   const char *e = getenv("AIDEEN_PIPELINE_WEIGHTS");
   for (int i = 0; i < nch; ++i) {
-    static const int kDefault4[4] = {1, 2, 3, 3};
+    static const int kDefault4[4] = {1, 2, 3, 4};
     int wi = (nch == 4) ? kDefault4[i] : 1;
     if (e && *e) {
       wi = atoi(e);
