@@ -415,6 +415,17 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
     mv_d_to_32<1, false>(mat[0], nullptr, m + hsv * tanh2(m) + hbv, j0, xs, keybuf, part);
   }
   const float band = fmaxf(a.eps, 0.15f * 0.2f);
+  // loop-invariant write parameters of this slot, staged in shared memory so
+  // the token loop issues no global parameter loads: [0,d) b_delta,
+  // [d,2d) W_write_gate, [2d,3d) b_retain (b_write_mem sits in wsm[40])
+  float *wprm = wres + (size_t)a.n_resident * d * kRank;
+  if constexpr (FPM) {
+    st2(wprm + j0, ld2(W + a.off_bdelta + (size_t)s * d + j0));
+    st2(wprm + d + j0, ld2(W + a.off_wgate + (size_t)s * d + j0));
+    st2(wprm + 2 * d + j0, ld2(W + a.off_bret + (size_t)s * d + j0));
+    if (threadIdx.x == 0) wsm[40] = W[a.off_bwrite + s];
+    __syncthreads();
+  }
   if constexpr (FPM) {
     // the prologue's memory and read key are published: split cluster barrier,
     // waited on before the first remote read
@@ -494,7 +505,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
               float chk = 0.f;
 #pragma unroll
               for (int ms = 0; ms < 16; ++ms) chk += kr[ms];
-              if (chk == 12345.678f) wsm[40] = chk;
+              if (chk == 12345.678f) wsm[41] = chk;
               PT(5);
             }
 #endif
@@ -610,22 +621,22 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
         mv2_32_to_d(mat[4], vec, mat[5], vec + 32, d, j0, pv, dv);
       }
       PT(6);
-      const float2 prop = tanh2(ld2(W + a.off_bdelta + (size_t)s * d + j0) + pv);
+      const float2 prop = tanh2(ld2(wprm + j0) + pv);
       const float2 df = prop - m;
       // the next token's iteration-0 |dep|^2 and |signal|^2 ride along
       const float2 dep0n = sig_nx + hcur + anc + Av_nx;
-      float v3[6] = {dot2(m, m), dot2(df, df), dot2(hcur, hcur), dot2(ld2(W + a.off_wgate + (size_t)s * d + j0), c),
-                     dot2(dep0n, dep0n), dot2(sig_nx, sig_nx)};
+      float v3[6] = {dot2(m, m), dot2(df, df), dot2(hcur, hcur), dot2(ld2(wprm + d + j0), c), dot2(dep0n, dep0n),
+                     dot2(sig_nx, sig_nx)};
       R.sum(v3);
       dep0_sq = v3[4];
       sig_sq = v3[5];
       const float2 hu = (1.f / sqrtf(fmaxf(v3[2] * inv_d, 1e-6f))) * hcur;
-      const float raw_z = 1.f / (1.f + expf(-(v3[3] * rsqrtf((float)d) + W[a.off_bwrite + s] - 1.5f)));
+      const float raw_z = 1.f / (1.f + expf(-(v3[3] * rsqrtf((float)d) + wsm[40] - 1.5f)));
       const float z = fminf(fmaxf(raw_z, 0.f), 1.f);
       const float prev_norm = sqrtf(fmaxf(v3[0], 1e-6f));
       const float diff_norm = sqrtf(fmaxf(v3[1], 1e-6f));
       const float novelty = diff_norm / (diff_norm + prev_norm + 1e-6f);
-      const float2 rrv = sigmoid2(ld2(W + a.off_bret + (size_t)s * d + j0) + dv);
+      const float2 rrv = sigmoid2(ld2(wprm + 2 * d + j0) + dv);
       const float2 retain = f2(1.f) - novelty * (f2(1.f) - rrv);
       const float2 write = (z * 0.1f) * prop;
       const float2 x = sqrtf(fmaxf(z, 1e-6f)) * hu + wxv * hu + write;
@@ -727,7 +738,8 @@ cudaError_t launch_attn_scale(const AttnArgs &a, int rows, cudaStream_t st) {
 }
 
 static size_t picard_smem_base(int d) {
-  return (size_t)(512 + 64 + 1024 + 64 + 64 + 3 * d) * sizeof(float);
+  // red, vec, part, wsm, keybuf, mbuf (2d), xs (d), write parameters (3d)
+  return (size_t)(512 + 64 + 1024 + 64 + 64 + 6 * d) * sizeof(float);
 }
 
 template <bool FPM, int MAXT>
