@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
     int it = 0;
     bool conv = false;
     // 1 / rms(dep) of the current iteration (one reciprocal instead of per-element divisions)
-    float irr = 1.f / sqrtf(dep0_sq * inv_d + 1e-6f);
+    float irr = rsqrtf(dep0_sq * inv_d + 1e-6f);
     float hq_sq = 0.f;
     while (it < a.max_iters && !conv) {
       if constexpr (FPM) {
@@ -487,7 +487,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
           waited = true;
           PT(0);
           // Model-A memory read from the first structured state (:1031-1200)
-          const float ihq = 1.f / sqrtf(fmaxf(hq_sq, 1e-6f));
+          const float ihq = rsqrtf(fmaxf(hq_sq, 1e-6f));
           const float sig_norm = sqrtf(fmaxf(sig_sq, 1e-6f));
           // the query lands in vec[0..32), written and read by warp 0 only
           mv_d_to_32<1, false>(mat[1], nullptr, ihq * hcur, j0, xs, vec, part);
@@ -583,7 +583,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       }
       // rms(dep) >= 1e-3 always (the 1e-6 floor), so max(rms, 1e-6) = rms
       const float err = sqrtf(v2[0] * inv_d + 1e-12f) * irr;
-      irr = 1.f / sqrtf(v2[1] * inv_d + 1e-6f);
+      irr = rsqrtf(v2[1] * inv_d + 1e-6f);
       hq_sq = v2[2];
       hcur = hn;
       const bool strict = err < a.eps;
@@ -630,7 +630,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       R.sum(v3);
       dep0_sq = v3[4];
       sig_sq = v3[5];
-      const float2 hu = (1.f / sqrtf(fmaxf(v3[2] * inv_d, 1e-6f))) * hcur;
+      const float2 hu = rsqrtf(fmaxf(v3[2] * inv_d, 1e-6f)) * hcur;
       const float raw_z = 1.f / (1.f + expf(-(v3[3] * rsqrtf((float)d) + wsm[40] - 1.5f)));
       const float z = fminf(fmaxf(raw_z, 0.f), 1.f);
       const float prev_norm = sqrtf(fmaxf(v3[0], 1e-6f));
