@@ -333,8 +333,9 @@ __device__ __forceinline__ void mv2_32_to_d_tmem(uint32_t ta, const float *ina, 
   yb = b;
 }
 
+// (fast reciprocal: ~2 ulp, on the Picard write's dependency chain)
 __device__ __forceinline__ float2 sigmoid2(float2 x) {
-  return make_float2(1.f / (1.f + expf(-x.x)), 1.f / (1.f + expf(-x.y)));
+  return make_float2(__fdividef(1.f, 1.f + expf(-x.x)), __fdividef(1.f, 1.f + expf(-x.y)));
 }
 
 // Persistent token-serial solve.  blockDim = d/2 (one float2 per thread, see
@@ -533,7 +534,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
             const float mx = warp_max(sc);
             const float ex = lane < h ? expf(sc - mx) : 0.f;
             const float se = fmaxf(warp_sum(ex), 1e-12f);
-            const float w = ex / se;
+            const float w = __fdividef(ex, se);
             const float peak = warp_max(lane < h ? w : 0.f);
             if (lane < h) wsm[lane] = w;
             if (lane == 0) {
@@ -631,11 +632,11 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       dep0_sq = v3[4];
       sig_sq = v3[5];
       const float2 hu = rsqrtf(fmaxf(v3[2] * inv_d, 1e-6f)) * hcur;
-      const float raw_z = 1.f / (1.f + expf(-(v3[3] * rsqrtf((float)d) + wsm[40] - 1.5f)));
+      const float raw_z = __fdividef(1.f, 1.f + expf(-(v3[3] * rsqrtf((float)d) + wsm[40] - 1.5f)));
       const float z = fminf(fmaxf(raw_z, 0.f), 1.f);
       const float prev_norm = sqrtf(fmaxf(v3[0], 1e-6f));
       const float diff_norm = sqrtf(fmaxf(v3[1], 1e-6f));
-      const float novelty = diff_norm / (diff_norm + prev_norm + 1e-6f);
+      const float novelty = __fdividef(diff_norm, diff_norm + prev_norm + 1e-6f);
       const float2 rrv = sigmoid2(ld2(wprm + 2 * d + j0) + dv);
       const float2 retain = f2(1.f) - novelty * (f2(1.f) - rrv);
       const float2 write = (z * 0.1f) * prop;
