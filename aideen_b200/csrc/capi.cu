@@ -330,7 +330,10 @@ int read_solve_stats(aideen_ctx *ctx, const aideen_run *r, aideen_stats *stats) 
   KL(launch_solve_stats(b.iters, b.hstar, N * h, d, r->max_iters, b.stats, st));
   unsigned long long hs[4];
   CU(cudaMemcpyAsync(hs, b.stats, sizeof(hs), cudaMemcpyDeviceToHost, st));
+  unsigned int pic_err = 0;
+  CU(picard_error_async(&pic_err, st));
   CU(cudaStreamSynchronize(st));
+  if (pic_err) return set_err(ctx, AIDEEN_E_TIMEOUT, "Picard memory-row exchange: a bounded wait ran out");
   stats->total_iters = hs[0];
   stats->max_iters_seen = (uint32_t)hs[1];
   stats->unconverged = (uint32_t)hs[2];

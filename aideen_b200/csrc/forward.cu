@@ -334,6 +334,86 @@ __device__ __forceinline__ void mv2_32_to_d_tmem(uint32_t ta, const float *ina, 
 }
 
 // (fast reciprocal: ~2 ulp, on the Picard write's dependency chain)
+// out[0..32) = Ma . x, out[32..64) = Mb . x for two d->32 matrices in TMEM.
+__device__ __forceinline__ void mv2_d_to_32_tmem(uint32_t ta, uint32_t tb, float2 x, float *out, float *part) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  float pa[32], pb[32];
+  {
+    uint32_t w0[32];
+    tmem_ld32(ta, w0);
+    tmem_wait(w0);
+#pragma unroll
+    for (int r = 0; r < 32; ++r) pa[r] = x.x * __uint_as_float(w0[r]);
+    tmem_ld32(ta + 32, w0);
+    tmem_wait(w0);
+#pragma unroll
+    for (int r = 0; r < 32; ++r) pa[r] += x.y * __uint_as_float(w0[r]);
+  }
+  part[warp * 64 + lane] = warp_transpose_reduce32(pa);
+  {
+    uint32_t w0[32];
+    tmem_ld32(tb, w0);
+    tmem_wait(w0);
+#pragma unroll
+    for (int r = 0; r < 32; ++r) pb[r] = x.x * __uint_as_float(w0[r]);
+    tmem_ld32(tb + 32, w0);
+    tmem_wait(w0);
+#pragma unroll
+    for (int r = 0; r < 32; ++r) pb[r] += x.y * __uint_as_float(w0[r]);
+  }
+  part[warp * 64 + 32 + lane] = warp_transpose_reduce32(pb);
+  __syncthreads();
+  if (threadIdx.x < 64) {
+    float t = 0.f;
+    for (int w = 0; w < nw; ++w) t += part[w * 64 + threadIdx.x];
+    out[threadIdx.x] = t;
+  }
+  __syncthreads();
+}
+
+// ---- inbox exchange of the FPM memory rows and read keys -------------------
+__device__ unsigned int g_picard_error;  // a bounded inbox wait gave up (data of that token invalid)
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void inbox_arm(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+// Bounded wait for phase `parity`; false if it gave up.
+__device__ __forceinline__ bool inbox_wait(uint64_t *bar, uint32_t parity) {
+  const uint32_t addr = smem_addr(bar);
+  for (uint32_t i = 0; i < (1u << 24); ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+// Copy `bytes` of this CTA's shared memory to the same-layout slot in CTA
+// `rank`, completing on that CTA's mbarrier.
+__device__ __forceinline__ void push_to(const void *src, const void *dst_local, uint64_t *bar_local,
+                                        uint32_t rank, uint32_t bytes) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          cluster_addr(smem_addr(dst_local), rank)),
+      "r"(smem_addr(src)), "r"(bytes), "r"(cluster_addr(smem_addr(bar_local), rank))
+      : "memory");
+}
+
+// (fast reciprocal: ~2 ulp, on the Picard write's dependency chain)
 __device__ __forceinline__ float2 sigmoid2(float2 x) {
   return make_float2(__fdividef(1.f, 1.f + expf(-x.x)), __fdividef(1.f, 1.f + expf(-x.y)));
 }
@@ -396,7 +476,13 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
         for (int q = threadIdx.x * 4; q < d * kRank; q += blockDim.x * 4) st4(dst + q, ld4(src[i] + q));
       mat[i] = res ? dst : src[i];
     }
-    if (a.use_tmem) {
+    if (a.use_tmem && a.push) {
+      tmem_stage(tmem + 0, mat[2], d, j0, true);     // W_k_write     [d][32]
+      tmem_stage(tmem + 128, mat[3], d, j0, true);   // W_retain_up   [d][32]
+      tmem_stage(tmem + 256, mat[4], d, j0, false);  // W_v_write     [32][d]
+      tmem_stage(tmem + 384, mat[5], d, j0, false);  // W_retain_down [32][d]
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    } else if (a.use_tmem) {
       tmem_stage(tmem + 0, mat[3], d, j0, true);     // W_retain_up   [d][32]
       tmem_stage(tmem + 128, mat[4], d, j0, false);  // W_v_write     [32][d]
       tmem_stage(tmem + 256, mat[5], d, j0, false);  // W_retain_down [32][d]
@@ -427,10 +513,36 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
     if (threadIdx.x == 0) wsm[40] = W[a.off_bwrite + s];
     __syncthreads();
   }
+  // push mode inbox: [2][h][d] memory rows and [2][h][32] read keys of every
+  // slot, double-buffered by token parity, one mbarrier per buffer
+  float *inbox_m = wprm + 3 * d;
+  float *inbox_k = inbox_m + 2 * (size_t)h * d;
+  uint64_t *inbar = reinterpret_cast<uint64_t *>(inbox_k + 2 * (size_t)h * kRank);
+  const uint32_t inbox_bytes = (uint32_t)h * (uint32_t)(d + kRank) * 4u;
   if constexpr (FPM) {
-    // the prologue's memory and read key are published: split cluster barrier,
-    // waited on before the first remote read
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    if (a.push) {
+      if (threadIdx.x == 0) {
+        for (int q = 0; q < 2; ++q)
+          asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&inbar[q])));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      }
+      // every CTA's inbox barriers exist before anyone pushes
+      asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+      asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+      __syncthreads();  // keybuf[0] / mbuf[0] of the prologue are complete
+      if (threadIdx.x == 0) {
+        inbox_arm(&inbar[0], inbox_bytes);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        for (int q = 0; q < h; ++q) {
+          push_to(mbuf, inbox_m + (size_t)s * d, &inbar[0], q, (uint32_t)d * 4u);
+          push_to(keybuf, inbox_k + (size_t)s * kRank, &inbar[0], q, kRank * 4u);
+        }
+      }
+    } else {
+      // the prologue's memory and read key are published: split cluster barrier,
+      // waited on before the first remote read
+      asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    }
   }
 #ifdef AIDEEN_PICARD_PROF
   long long _pt = clock64();
@@ -484,7 +596,16 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       if constexpr (FPM) {
         if (it == 1) {
           // every slot's key + memory for this token is visible past this wait
-          asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+          if (a.push) {
+            if (threadIdx.x == 0) {
+              const int tl = t - a.t0;
+              if (!inbox_wait(&inbar[tl & 1], (tl >> 1) & 1)) atomicExch(&g_picard_error, 1u);
+              if (t + 1 < a.t1) inbox_arm(&inbar[(tl + 1) & 1], inbox_bytes);
+            }
+            // the next block barrier (inside the query product) orders the inbox reads
+          } else {
+            asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+          }
           waited = true;
           PT(0);
           // Model-A memory read from the first structured state (:1031-1200)
@@ -498,9 +619,15 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
             const int lane = threadIdx.x;
             __syncwarp();
             float kr[16];
+            if (a.push) {
+              const float *kb = inbox_k + (size_t)((t - a.t0) & 1) * h * kRank;
 #pragma unroll
-            for (int ms = 0; ms < 16; ++ms)
-              kr[ms] = ms < h ? cl.map_shared_rank(keybuf + cur * 32, ms)[lane] : 0.f;
+              for (int ms = 0; ms < 16; ++ms) kr[ms] = ms < h ? kb[ms * kRank + lane] : 0.f;
+            } else {
+#pragma unroll
+              for (int ms = 0; ms < 16; ++ms)
+                kr[ms] = ms < h ? cl.map_shared_rank(keybuf + cur * 32, ms)[lane] : 0.f;
+            }
 #ifdef AIDEEN_PICARD_PROF
             {
               float chk = 0.f;
@@ -546,14 +673,19 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
           __syncthreads();
           PT(7);
           float2 mr = f2(0.f);
-          for (int base = 0; base < h; base += 8) {   // 8 remote loads in flight at a time
-            float2 mm[8];
+          if (a.push) {
+            const float *mb = inbox_m + (size_t)((t - a.t0) & 1) * h * d + j0;
+            for (int q = 0; q < h; ++q) mr = mr + wsm[q] * ld2(mb + (size_t)q * d);
+          } else {
+            for (int base = 0; base < h; base += 8) {   // 8 remote loads in flight at a time
+              float2 mm[8];
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-              if (base + q < h) mm[q] = ld2(cl.map_shared_rank(mbuf + cur * d, base + q) + j0);
+              for (int q = 0; q < 8; ++q)
+                if (base + q < h) mm[q] = ld2(cl.map_shared_rank(mbuf + cur * d, base + q) + j0);
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-              if (base + q < h) mr = mr + wsm[base + q] * mm[q];
+              for (int q = 0; q < 8; ++q)
+                if (base + q < h) mr = mr + wsm[base + q] * mm[q];
+            }
           }
           const float2 mu = tanh2(mr);
           float v1[1] = {dot2(mu, mu)};
@@ -604,15 +736,27 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
     }
     PT(3);
     if constexpr (FPM) {
-      if (!waited) {  // solve stopped before the memory read: still consume this token's barrier phase
-        asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+      if (!waited) {  // solve stopped before the memory read: still consume this token's phase
+        if (a.push) {
+          if (threadIdx.x == 0) {
+            const int tl = t - a.t0;
+            if (!inbox_wait(&inbar[tl & 1], (tl >> 1) & 1)) atomicExch(&g_picard_error, 1u);
+            if (t + 1 < a.t1) inbox_arm(&inbar[(tl + 1) & 1], inbox_bytes);
+          }
+        } else {
+          asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+        }
         PT(0);
       }
       // post-solve memory write (:1965-2140)
       const float2 c = 0.5f * (hcur + sig);
       PT(4);
       float2 pv, dv;
-      if (a.use_tmem) {
+      if (a.use_tmem && a.push) {
+        mv2_d_to_32_tmem(tmem + 0, tmem + 128, c, vec, part);   // bottleneck | retain-up
+        PT(5);
+        mv2_32_to_d_tmem(tmem + 256, vec, tmem + 384, vec + 32, pv, dv);
+      } else if (a.use_tmem) {
         mv_d_to_32_smem_tmem(mat[2], tmem + 0, c, j0, xs, vec, part);   // bottleneck | retain-up
         PT(5);
         mv2_32_to_d_tmem(tmem + 128, vec, tmem + 256, vec + 32, pv, dv);
@@ -650,11 +794,29 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       // peers read the key after the cluster barrier below; no block barrier needed
       mv_d_to_32<1, false>(mat[0], nullptr, m + hsv * tanh2(m) + hbv, j0, xs, keybuf + (cur ^ 1) * 32, part);
       PT(7);
-      cur ^= 1;
-      // publish this token's memory and key to the cluster; the global stores
-      // (no reader inside this kernel) come after the arrive, so its release
-      // orders only the shared-memory writes
-      asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+      if (a.push) {
+        // push this token's memory row and key into every slot's inbox for the
+        // next token (none after the last token of the launch)
+        if (t + 1 < a.t1) {
+          __syncthreads();  // mbuf row and key complete
+          if (threadIdx.x == 0) {
+            const int nb = (t - a.t0 + 1) & 1;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            for (int q = 0; q < h; ++q) {
+              push_to(mbuf + (cur ^ 1) * d, inbox_m + ((size_t)nb * h + s) * d, &inbar[nb], q, (uint32_t)d * 4u);
+              push_to(keybuf + (cur ^ 1) * 32, inbox_k + ((size_t)nb * h + s) * kRank, &inbar[nb], q,
+                      kRank * 4u);
+            }
+          }
+        }
+        cur ^= 1;
+      } else {
+        cur ^= 1;
+        // publish this token's memory and key to the cluster; the global stores
+        // (no reader inside this kernel) come after the arrive, so its release
+        // orders only the shared-memory writes
+        asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+      }
       st2(a.hist + e, mn);
       st2(a.hstar + e, hcur);
       st2(a.pre + e, pre_adj);
@@ -669,8 +831,13 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
 #endif
   if constexpr (FPM) {
     st2(a.mstate + ((size_t)b * h + s) * d + j0, m);
-    // match the last arrive: peers may read this block's memory until they pass it
-    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (a.push) {  // no CTA leaves while a peer may still push into it
+      asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+      asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    } else {
+      // match the last arrive: peers may read this block's memory until they pass it
+      asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    }
     if (a.use_tmem) {
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncthreads();
@@ -738,6 +905,16 @@ cudaError_t launch_attn_scale(const AttnArgs &a, int rows, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// Reads (and clears) the flag a Picard launch sets when a bounded inbox wait
+// gave up; ordered on `st` after the solve.
+cudaError_t picard_error_async(unsigned int *host_flag, cudaStream_t st) {
+  static const unsigned int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(host_flag, g_picard_error, sizeof(unsigned int), 0,
+                                            cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) return e;
+  return cudaMemcpyToSymbolAsync(g_picard_error, &zero, sizeof(unsigned int), 0, cudaMemcpyHostToDevice, st);
+}
+
 static size_t picard_smem_base(int d) {
   // red, vec, part, wsm, keybuf, mbuf (2d), xs (d), write parameters (3d)
   return (size_t)(512 + 64 + 1024 + 64 + 64 + 6 * d) * sizeof(float);
@@ -767,8 +944,16 @@ static cudaError_t picard_launch(const PicardArgs &a, cudaStream_t st) {
     ++p.n_resident;
   }
   // d = 512: the three matrices that do not fit in shared memory go to tensor
-  // memory (one 256-thread block per SM owns all 512 columns)
+  // memory (one 256-thread block per SM owns all 512 columns); with h <= 8 a
+  // fourth one moves there too, and the freed shared memory holds the inbox of
+  // the pushed memory rows / read keys
   p.use_tmem = (a.d == 512 && p.n_resident == 3 && !getenv("AIDEEN_PICARD_NO_TMEM")) ? 1 : 0;
+  p.push = (p.use_tmem && a.h <= 8 && !getenv("AIDEEN_PICARD_NO_PUSH")) ? 1 : 0;
+  if (p.push) {
+    p.n_resident = 2;
+    smem -= mat_bytes;
+    smem += (2 * (size_t)a.h * (a.d + kRank) + 4) * sizeof(float);
+  }
   e = cudaFuncSetAttribute(picard_kernel<true, MAXT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};

@@ -36,6 +36,7 @@ cudaError_t tc_gemm_split(const GemmArgs &g, const float *A_lo, const float *B_l
                           float *ws = nullptr, size_t ws_floats = 0, int max_ctas = 0,
                           const float *row_bias = nullptr, float2 *row_stats = nullptr);
 unsigned int tc_split_error(bool reset);
+cudaError_t picard_error_async(unsigned int *host_flag, cudaStream_t st);
 // x -> (hi, lo) with hi exact in tf32 and lo = x - hi (n % 4 == 0).
 cudaError_t launch_split_hilo(const float *x, float *hi, float *lo, size_t n, cudaStream_t st);
 // out[c][r] = split(x[r][c]): transposed hi / lo copies (row stride ldt).
@@ -56,7 +57,8 @@ struct PicardArgs {
   int B, T, h, d, max_iters, slot_coord;
   int t0, t1;      // token range of this launch (state carried in hstar / mstate)
   int n_resident;  // FPM matrices staged in shared memory (set by the launcher)
-  int use_tmem;    // 1: matrices 3..5 live in tensor memory (d = 512, n_resident = 3)
+  int use_tmem;    // 1: rank-32 matrices in tensor memory (d = 512): 3..5, or 2..5 with push
+  int push;        // 1: memory rows / read keys pushed into every peer's inbox by bulk copy
   float eps, blend, alpha_m, tau, gate_min;
   const float *W;
   size_t off_ns, off_anchor, off_hscale, off_hbias, off_wkm, off_wqm, off_bread, off_wgate,
