@@ -9,6 +9,10 @@
 //   * one CTA per SM loops over 128 x 256 output tiles (m fastest, so the CTAs
 //     running together share the B tile in L2), with split-K units when the
 //     output has too few tiles to fill the GPU;
+//   * wide mode (no row statistics): 256 x 256 tiles as two M = 128 MMAs that
+//     share each B stage (3 stages of 64 KB, both accumulators in the 512 TMEM
+//     columns, epilogue not overlapped), which cuts the L2 -> SM traffic of
+//     the re-read B slices by half for the long-K and tall-M LM-head GEMMs;
 //   * warp 0 / lane 0 streams A_hi, A_lo, B_hi, B_lo K-slices (BK = 16) by TMA
 //     into a 4-stage ring (64-byte swizzle for K-major operands, 128-byte
 //     swizzle on 32-byte atoms for MN-major ones);
@@ -22,6 +26,7 @@
 //
 // Every mbarrier wait is bounded; on a timeout the kernel records an error,
 // stops issuing, waits for its own copies and MMAs, frees TMEM and returns.
+#include <cstdlib>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -35,6 +40,9 @@ constexpr int PM = 128, PN = 256, PK = 16, PSTAGES = 4, P_THREADS = 192;
 constexpr int PA_BYTES = PM * PK * 4;                     // one A tile (hi or lo): 8 KB
 constexpr int PB_BYTES = PN * PK * 4;                     // one B tile: 16 KB
 constexpr int PSTAGE_BYTES = 2 * PA_BYTES + 2 * PB_BYTES;  // 48 KB
+constexpr int PWSTAGES = 3;                                  // wide mode: 3 stages of
+constexpr int PWSTAGE_BYTES = 4 * PA_BYTES + 2 * PB_BYTES;  // 64 KB (2 A sub-tiles)
+static_assert(PWSTAGES * PWSTAGE_BYTES == PSTAGES * PSTAGE_BYTES, "ring size shared by both modes");
 constexpr int PBOX_BYTES = 32 * 32 * 4;                   // one 32x32 epilogue box
 constexpr size_t P_SMEM = 1024 + (size_t)PSTAGES * PSTAGE_BYTES + 8 * PBOX_BYTES + 16 * 8 + 16;
 
@@ -47,6 +55,7 @@ struct SplitParams {
   int ksplit, kchunk;          // split-K when ksplit > 1 (z = split index, operands unbatched)
   float alpha;
   int reduce_add;
+  int wide;  // 256-row tiles (two 128-row sub-tiles sharing the B stage)
   // optional per-(row, 256-column tile) softmax statistics of (C + bias) in
   // base 2: row_stats[row * tiles_n + tile] = (max z, sum exp2(z - max)),
   // z = (alpha * acc + bias[col]) * log2(e)
@@ -73,6 +82,11 @@ __global__ void __launch_bounds__(P_THREADS, 1)
   const int per_z = p.tiles_m * p.tiles_n;
   const int units = per_z * p.zdim;
   const int ktot = (p.K + PK - 1) / PK;
+  const int nsub = p.wide ? 2 : 1;                   // 128-row sub-tiles per tile
+  const int TM = PM * nsub;                          // tile rows
+  const int nstage = p.wide ? PWSTAGES : PSTAGES;
+  const int stage_bytes = p.wide ? PWSTAGE_BYTES : PSTAGE_BYTES;
+  const int nacc = p.wide ? 1 : 2;                   // TMEM accumulator sets (nsub x 256 columns each)
 
   if (tid == 0) {
     for (int s = 0; s < PSTAGES; ++s) {
@@ -103,7 +117,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     z = u / per_z;
     const int rem = u - z * per_z;
     n0 = (rem / p.tiles_m) * PN;
-    m0 = (rem % p.tiles_m) * PM;
+    m0 = (rem % p.tiles_m) * TM;
     if (p.ksplit > 1) {
       kb0 = z * p.kchunk;
       nkb = min(p.kchunk, ktot - kb0);
@@ -123,23 +137,27 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         const int zo = p.ksplit > 1 ? 0 : z;
         const int za = p.a_batched ? zo : 0, zb = p.b_batched ? zo : 0;
         for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int s = it % PSTAGES;
-          if (it >= PSTAGES && !mbar_wait(&empty[s], ((it / PSTAGES) - 1) & 1)) { ok = false; break; }
+          const int s = it % nstage;
+          if (it >= (uint32_t)nstage && !mbar_wait(&empty[s], ((it / nstage) - 1) & 1)) { ok = false; break; }
           if (*(volatile uint32_t *)err) { ok = false; break; }
           const int k0 = (kb0 + kb) * PK;
-          unsigned char *st = sm + s * PSTAGE_BYTES;
-          mbar_expect_tx(&full[s], PSTAGE_BYTES);
-          if (p.a_kmajor) {
-            tma_load_3d(st, &mAh, &full[s], k0, m0, za);
-            tma_load_3d(st + PA_BYTES, &mAl, &full[s], k0, m0, za);
-          } else {
+          unsigned char *st = sm + s * stage_bytes;
+          mbar_expect_tx(&full[s], stage_bytes);
+          for (int sub = 0; sub < nsub; ++sub) {  // A sub-tile: hi then lo
+            unsigned char *sa = st + sub * 2 * PA_BYTES;
+            const int ms = m0 + sub * PM;
+            if (p.a_kmajor) {
+              tma_load_3d(sa, &mAh, &full[s], k0, ms, za);
+              tma_load_3d(sa + PA_BYTES, &mAl, &full[s], k0, ms, za);
+            } else {
 #pragma unroll
-            for (int c = 0; c < PM / 32; ++c) {
-              tma_load_3d(st + c * (PK * 128), &mAh, &full[s], m0 + 32 * c, k0, za);
-              tma_load_3d(st + PA_BYTES + c * (PK * 128), &mAl, &full[s], m0 + 32 * c, k0, za);
+              for (int c = 0; c < PM / 32; ++c) {
+                tma_load_3d(sa + c * (PK * 128), &mAh, &full[s], ms + 32 * c, k0, za);
+                tma_load_3d(sa + PA_BYTES + c * (PK * 128), &mAl, &full[s], ms + 32 * c, k0, za);
+              }
             }
           }
-          unsigned char *sb = st + 2 * PA_BYTES;
+          unsigned char *sb = st + nsub * 2 * PA_BYTES;
           if (p.b_kmajor) {
             tma_load_3d(sb, &mBh, &full[s], k0, n0, zb);
             tma_load_3d(sb + PB_BYTES, &mBl, &full[s], k0, n0, zb);
@@ -154,8 +172,8 @@ __global__ void __launch_bounds__(P_THREADS, 1)
       }
       if (!ok) atomicExch(err, 1u);
       // every issued copy must land before the CTA can exit (bounded)
-      const uint32_t first = it > (uint32_t)PSTAGES ? it - PSTAGES : 0;
-      for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % PSTAGES], (j / PSTAGES) & 1);
+      const uint32_t first = it > (uint32_t)nstage ? it - nstage : 0;
+      for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % nstage], (j / nstage) & 1);
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---------------- MMA issuer
@@ -172,26 +190,29 @@ __global__ void __launch_bounds__(P_THREADS, 1)
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++j) {
         int m0, n0, z, kb0, nkb;
         coords(u, m0, n0, z, kb0, nkb);
-        const int a = j & 1;
-        if (j >= 2 && !mbar_wait(&tempty[a], ((j >> 1) - 1) & 1)) { ok = false; break; }
+        const int a = j % nacc;
+        if (j >= nacc && !mbar_wait(&tempty[a], ((j / nacc) - 1) & 1)) { ok = false; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t tacc = tmem + (uint32_t)(a * PN);
         for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int s = it % PSTAGES;
-          if (!mbar_wait(&full[s], (it / PSTAGES) & 1) || *(volatile uint32_t *)err) { ok = false; break; }
+          const int s = it % nstage;
+          if (!mbar_wait(&full[s], (it / nstage) & 1) || *(volatile uint32_t *)err) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          unsigned char *st = sm + s * PSTAGE_BYTES;
+          unsigned char *st = sm + s * stage_bytes;
+          unsigned char *sb = st + nsub * 2 * PA_BYTES;
 #pragma unroll
           for (int k8 = 0; k8 < PK / 8; ++k8) {
             const uint32_t koffA = p.a_kmajor ? k8 * 32 : k8 * 1024;
             const uint32_t koffB = p.b_kmajor ? k8 * 32 : k8 * 1024;
-            const uint64_t ahi = sdesc(st + koffA, lboA, 512u, layA);
-            const uint64_t alo = sdesc(st + PA_BYTES + koffA, lboA, 512u, layA);
-            const uint64_t bhi = sdesc(st + 2 * PA_BYTES + koffB, lboB, 512u, layB);
-            const uint64_t blo = sdesc(st + 2 * PA_BYTES + PB_BYTES + koffB, lboB, 512u, layB);
-            umma_tf32(tacc, ahi, bhi, idesc, (kb > 0 || k8 > 0) ? 1u : 0u);
-            umma_tf32(tacc, ahi, blo, idesc, 1u);
-            umma_tf32(tacc, alo, bhi, idesc, 1u);
+            const uint64_t bhi = sdesc(sb + koffB, lboB, 512u, layB);
+            const uint64_t blo = sdesc(sb + PB_BYTES + koffB, lboB, 512u, layB);
+            for (int sub = 0; sub < nsub; ++sub) {
+              const uint32_t tacc = tmem + (uint32_t)((a + sub) * PN);
+              const uint64_t ahi = sdesc(st + sub * 2 * PA_BYTES + koffA, lboA, 512u, layA);
+              const uint64_t alo = sdesc(st + sub * 2 * PA_BYTES + PA_BYTES + koffA, lboA, 512u, layA);
+              umma_tf32(tacc, ahi, bhi, idesc, (kb > 0 || k8 > 0) ? 1u : 0u);
+              umma_tf32(tacc, ahi, blo, idesc, 1u);
+              umma_tf32(tacc, alo, bhi, idesc, 1u);
+            }
           }
           umma_commit(&empty[s]);
         }
@@ -209,18 +230,19 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
       int m0, n0, z, kb0, nkb;
       coords(u, m0, n0, z, kb0, nkb);
-      const int a = j & 1;
-      if (!mbar_wait(&tfull[a], (j >> 1) & 1) || *(volatile uint32_t *)err) {
+      const int a = j % nacc;
+      if (!mbar_wait(&tfull[a], (j / nacc) & 1) || *(volatile uint32_t *)err) {
         atomicExch(err, 1u);
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int rowbase = m0 + q * 32;
+      for (int sub = 0; sub < nsub; ++sub) {
+      const int rowbase = m0 + sub * PM + q * 32;
       float st_m = -INFINITY, st_s = 0.f;  // this lane's row: running softmax statistics
 #pragma unroll 1
       for (int c = 0; c < PN / 32; ++c) {
         uint32_t r[32];
-        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * PN + c * 32);
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((a + sub) * PN + c * 32);
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
             "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
@@ -232,7 +254,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
               "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
             : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (c == PN / 32 - 1) {  // accumulator fully read: hand it back to the MMA warp
+        if (sub == nsub - 1 && c == PN / 32 - 1) {  // accumulators fully read: hand them back
           asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty[a]);
@@ -277,6 +299,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
       }
       if (p.row_stats && rowbase + lane < p.M)
         p.row_stats[(size_t)(rowbase + lane) * p.tiles_n + n0 / PN] = make_float2(st_m, st_s);
+      }
     }
     if (lane == 0) bulk_wait<0>();  // stores complete before the CTA's shared memory goes away
   }
@@ -356,7 +379,11 @@ cudaError_t tc_gemm_split(const GemmArgs &g, const float *A_lo, const float *B_l
   SplitParams p{};
   p.M = g.M; p.N = g.N; p.K = g.K;
   p.a_kmajor = a_k; p.b_kmajor = b_k; p.a_batched = a_b; p.b_batched = b_b;
-  p.tiles_m = (g.M + PM - 1) / PM;
+  // wide tiles for the GEMMs without row statistics (AIDEEN_SPLIT_NARROW forces 128-row tiles)
+  // (the logits GEMM with row statistics keeps 128-row tiles: its short K makes
+  // the overlapped epilogue worth more than the saved B traffic, measured)
+  p.wide = (!row_stats && g.M > PM && !getenv("AIDEEN_SPLIT_NARROW")) ? 1 : 0;
+  p.tiles_m = (g.M + PM * (1 + p.wide) - 1) / (PM * (1 + p.wide));
   p.tiles_n = (g.N + PN - 1) / PN;
   p.zdim = g.batch;
   p.ksplit = 1; p.kchunk = 0;

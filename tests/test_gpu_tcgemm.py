@@ -47,3 +47,16 @@ def test_presplit_persistent_gemm_matches_fp32(shape):
     print(f"{shape}: rel {err:.2e}  tc {t_tc:.3f} ms  simt {t_simt:.3f} ms")
     assert err < 5e-5
     be.close()
+
+
+@pytest.mark.parametrize("shape", [SPLIT_SHAPES[1], SPLIT_SHAPES[3], SPLIT_SHAPES[4]],
+                         ids=lambda s: "x".join(map(str, s[:4])) + f"_t{int(s[4])}{int(s[5])}")
+def test_presplit_narrow_tiles_match_fp32(shape, monkeypatch):
+    """128-row tiles (the mode the logits GEMM with row statistics uses) on shapes
+    that otherwise take the 256-row tiles."""
+    monkeypatch.setenv("AIDEEN_SPLIT_NARROW", "1")
+    M, N, K, B, ta, tb = shape
+    be = GpuDeqBackend(128, 2, 1, 1)
+    err, t_tc, t_simt = be.gemm_selftest(M, N, K, B, ta, tb, presplit=True)
+    assert err < 5e-5
+    be.close()
