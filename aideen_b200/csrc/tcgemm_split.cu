@@ -398,15 +398,18 @@ cudaError_t tc_gemm_split(const GemmArgs &g, const float *A_lo, const float *B_l
   long cld = g.ldc, cstride = g.strideC;
   int cz = g.batch;
   // Split K when the output has too few tiles to keep every SM busy: pick the
-  // split count (<= 16) that minimises the per-CTA share of K blocks.
+  // split count (<= 64, within the workspace) that minimises the per-CTA share
+  // of K blocks plus the partial sums' round trip (about 1.6e-6 K-block times
+  // per output element and split: written once, read once by the reduction).
   if (ws && g.batch == 1 && tiles < nsm && kblocks >= 128 && !row_stats) {
     int best = 1;
     double best_cost = (double)kblocks;  // one unit of all K blocks per CTA
-    for (int s = 2; s <= 16; ++s) {
+    const double per_split = 1.6e-6 * (double)g.M * g.N * (p.wide ? 0.5 : 1.0);
+    for (int s = 2; s <= 64; ++s) {
       const int chunk = (kblocks + s - 1) / s;
       const int splits = (kblocks + chunk - 1) / chunk;
       const int rounds = (tiles * splits + nsm - 1) / nsm;
-      const double cost = (double)rounds * chunk + 0.02 * kblocks * splits / 16.0;
+      const double cost = (double)rounds * chunk + per_split * splits;
       if ((size_t)splits * g.M * g.N <= ws_floats && cost < best_cost) { best_cost = cost; best = s; }
     }
     if (best > 1) {
