@@ -602,16 +602,15 @@ void tl_flush(aideen_ctx *ctx) {
 }
 
 // Token boundary of chunk j of nch: proportional to cumulative weights.  A
-// small first chunk lets the consumers start early; the default weights for
-// four chunks are 1,2,3,4 (measured best of the tried splits at the bench
+// small first chunk lets the consumers start early; the default weights are
+// 1,2,3,... (three chunks 1,2,3 measured best of the tried splits at the bench
 // shape; AIDEEN_PIPELINE_WEIGHTS overrides, comma-separated).
 int chunk_bound(int j, int nch, int T) {
   int w[aideen_ctx::kMaxChunks] = {0};
   int tot = 0;
   const char *e = getenv("AIDEEN_PIPELINE_WEIGHTS");
   for (int i = 0; i < nch; ++i) {
-    static const int kDefault4[4] = {1, 2, 3, 4};
-    int wi = (nch == 4) ? kDefault4[i] : 1;
+    int wi = i + 1;
     if (e && *e) {
       wi = atoi(e);
       while (*e && *e != ',') ++e;
@@ -645,7 +644,7 @@ int pipeline_chunks(aideen_ctx *ctx, const aideen_run *r) {
   const int picard_ctas = (int)(r->batch * ctx->cfg.h_slots);
   if (nsm - picard_ctas < 32) return 0;
   if (r->batch % 4 != 0) return 0;  // chunk row offsets must keep 16-byte alignment of y^T columns
-  int nch = 4;
+  int nch = 3;
   if (const char *e = getenv("AIDEEN_PIPELINE_CHUNKS")) nch = atoi(e);
   if (nch > aideen_ctx::kMaxChunks) nch = aideen_ctx::kMaxChunks;
   if (nch < 2) return 0;
