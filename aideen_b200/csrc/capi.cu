@@ -426,6 +426,7 @@ int run_adjoint(aideen_ctx *ctx, int N, const float *pre_a, const float *pre_b,
 }
 
 int run_fpm_backward(aideen_ctx *ctx, bool prepare_only = false);
+void tl_mark(aideen_ctx *ctx, const char *name, cudaStream_t s);
 
 int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
@@ -455,6 +456,7 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
     ctx->stream = keep_st;
     ctx->b.ws = keep_ws;
     CHK(rc);
+    tl_mark(ctx, "fpm_bwd", ctx->fst);
     CU(cudaEventRecord(ctx->ev_fdone, ctx->fst));
   }
   KL(launch_colsum(b.nsg, N, d, d, G + L.nscale, d, 0, false, st));
@@ -471,6 +473,7 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
     // gW_o[s][c][o] = sum_n n[n][s][c] da[n][s][o]
     KL(gemm_any(ctx, gemm(kHeadDim, d, N, h, b.nmix, H32, kHeadDim, true, b.da, (long)h * d, d, false,
                      G + L.wo, d, (long)d * d)));
+    tl_mark(ctx, "wg_o", st);
     KL(launch_attn_bwd_softmax(a, N, st));
     // gW_{q,k,v}[s][j][c] = sum_n src[n][s][j] d{Q,K,V}[n][s][c]
     const float *dqkv[3] = {b.dQ, b.dK, b.dV};
@@ -478,11 +481,13 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
     for (int i = 0; i < 3; ++i)
       KL(gemm_any(ctx, gemm(d, kHeadDim, N, h, b.src, (long)h * d, d, true, dqkv[i], H32, kHeadDim,
                        false, G + woff[i], d, (long)d * d)));
+    tl_mark(ctx, "wg_qkv", st);
     KL(launch_dsig_init(a, b.dsig, N * h, 1, st));
     // dsrc[n][s][j] += sum_c d{Q,K,V}[n][s][c] W[s][j*d + c]
     for (int i = 0; i < 3; ++i)
       KL(gemm_any(ctx, gemm(N, d, kHeadDim, h, dqkv[i], H32, kHeadDim, false, W + woff[i], d, (long)d * d,
                        true, b.dsig, (long)h * d, d, 1.f, 1.f)));
+    tl_mark(ctx, "dsrc", st);
     KL(launch_colsum(b.dQ, N, H32, H32, G + L.q_bias, kHeadDim, d, false, st));
     KL(launch_colsum(b.dK, N, H32, H32, G + L.k_bias, kHeadDim, d, false, st));
     KL(launch_colsum(b.dsig, N, h * d, (long)h * d, G + L.slot_anchor, h * d, 0, false, st));
@@ -493,6 +498,7 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
     // gW_in[s][j][o] = sigma * sum_n S_in[n][j] dsig[n][s][o]
     KL(gemm_any(ctx, gemm(d, d, N, h, b.S_in, d, 0, true, b.dsig, (long)h * d, d, false, G + L.win, d,
                      (long)d * d, ctx->signal_scale)));
+    tl_mark(ctx, "wg_in", st);
     if (want_ds) {
       for (int s = 0; s < h; ++s)
         KL(gemm_any(ctx, gemm(N, d, d, 1, b.dsig + (size_t)s * d, (long)h * d, 0, false,
@@ -502,6 +508,7 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   } else if (want_ds) {
     CU(cudaMemsetAsync(b.dS, 0, (size_t)N * d * sizeof(float), st));
   }
+  tl_mark(ctx, "attn_grads", st);
   if (fork_fpm) CU(cudaStreamWaitEvent(st, ctx->ev_fdone, 0));
   else if (ctx->last_run.fpm) CHK(run_fpm_backward(ctx));
   return AIDEEN_OK;

@@ -850,7 +850,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
 __global__ void pool_rmsnorm_kernel(const float *__restrict__ hstar, const float *__restrict__ g,
                                     float *__restrict__ pooled, float *__restrict__ y,
                                     float *__restrict__ lrms, int h, int d) {
-  __shared__ float red[512];
+  __shared__ __align__(16) float red[512];
   const int n = blockIdx.x, j0 = threadIdx.x * 4;
   float4 p = f4(0.f);
   for (int s = 0; s < h; ++s) p = p + ld4(hstar + ((size_t)n * h + s) * d + j0);

@@ -554,7 +554,7 @@ cudaError_t launch_softmax_ce_split(float *logits, const float *bias, const int3
 __global__ void rmsnorm_bwd_kernel(const float *__restrict__ dy, const float *__restrict__ P,
                                    const float *__restrict__ lrms, const float *__restrict__ g,
                                    float *__restrict__ dl_dh, float *__restrict__ ggp, int d) {
-  __shared__ float red[512];
+  __shared__ __align__(16) float red[512];
   const int n = blockIdx.x, j0 = threadIdx.x * 4;
   const float4 dd = ld4(dy + (size_t)n * d + j0), p = ld4(P + (size_t)n * d + j0), gg = ld4(g + j0);
   const float r = lrms[n];
@@ -576,7 +576,7 @@ cudaError_t launch_rmsnorm_bwd(const float *dy, const float *P, const float *lrm
 }
 
 __global__ void sum_kernel(const float *__restrict__ x, int n, float *out) {
-  __shared__ float red[512];
+  __shared__ __align__(16) float red[512];
   float s = 0.f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
   BlockReducer R(red);
