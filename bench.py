@@ -351,7 +351,7 @@ def main():
                 "roofline_adjoint_c4": c4,
                 "clocks": clk.summary()}
         if not args.no_cpu_baseline and world == 1:
-            line["cpu_baseline"] = cpu_baseline(16)
+            line["cpu_baseline"] = cpu_baseline(128)
         print(json.dumps(line), flush=True)
     be.close()
     if world > 1:
