@@ -683,6 +683,7 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   ctx->perm_T = T;
   const int R0 = chunk_bound_aligned(1, nch, T, B) * B;
   CHK(run_forward_prep_rows(ctx, r, 0, R0));
+  tl_mark(ctx, "prep0", st);
   CU(cudaEventRecord(ctx->ev_prep, st));
   ctx->last_run = *r;
   ctx->N = N;

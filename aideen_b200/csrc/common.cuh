@@ -48,6 +48,32 @@ struct BlockReducer {
 };
 
 // Same protocol for doubles; `red` holds 2 * 8 * 32 doubles.
+// Block sum with the warp count known at compile time (blockDim = 32 * NW,
+// NW a multiple of 4): the warp partials come back as NW/4 float4 loads.
+template <int NW, int K>
+__device__ __forceinline__ void block_sum_static(float *red, int &parity, float (&v)[K]) {
+  static_assert(NW % 4 == 0 && NW <= 32 && K <= 8, "static block sum shape");
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float *buf = red + parity * 8 * 32;
+  parity ^= 1;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const float x = warp_sum(v[k]);
+    if (lane == 0) buf[k * 32 + warp] = x;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    float4 acc = reinterpret_cast<const float4 *>(buf + k * 32)[0];
+#pragma unroll
+    for (int w = 4; w < NW; w += 4) {
+      const float4 q = reinterpret_cast<const float4 *>(buf + k * 32 + w)[0];
+      acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
+    }
+    v[k] = (acc.x + acc.y) + (acc.z + acc.w);
+  }
+}
+
 struct BlockReducerD {
   double *red;
   int parity;

@@ -420,7 +420,14 @@ __device__ __forceinline__ float2 sigmoid2(float2 x) {
 
 // Persistent token-serial solve.  blockDim = d/2 (one float2 per thread, see
 // picard_j0), grid = B*h, block = b*h + s.  FPM=true requires a cluster of h CTAs.
-template <bool FPM, int MAXT>
+template <int NW, int K>
+__device__ __forceinline__ void bsum(BlockReducer &R, float (&v)[K]) {
+  if constexpr (NW > 0) block_sum_static<NW>(R.red, R.parity, v);
+  else R.sum(v);
+}
+
+// NW > 0: blockDim = 32 * NW fixed at compile time (static block reductions).
+template <bool FPM, int MAXT, int NW>
 __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
   extern __shared__ float4 sm4[];
   float *sm = reinterpret_cast<float *>(sm4);
@@ -568,7 +575,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
     }
     if (t == 0) {
       float v[1] = {dot2(sig, sig)};
-      R.sum(v);
+      bsum<NW>(R, v);
       const float den = fmaxf(sqrtf(v[0] * inv_d + 1e-6f), 1e-6f);
       hcur = make_float2(sig.x / den, sig.y / den);
       sig_sq = v[0];
@@ -579,7 +586,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
     if (t == a.t0 || !FPM) {
       const float2 dep0 = sig + hcur + anc + Av;
       float v[2] = {dot2(dep0, dep0), dot2(sig, sig)};
-      R.sum(v);
+      bsum<NW>(R, v);
       dep0_sq = v[0];
       if (t > 0) sig_sq = v[1];  // (t == 0 computed it above; only the FPM read uses it)
     }
@@ -689,7 +696,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
           }
           const float2 mu = tanh2(mr);
           float v1[1] = {dot2(mu, mu)};
-          R.sum(v1);
+          bsum<NW>(R, v1);
           const float mu_norm = sqrtf(fmaxf(v1[0], 1e-6f));
           const float coef = sig_norm * fmaxf(a.alpha_m, 0.001f) / fmaxf(mu_norm, 1e-6f) * wsm[16];
           ctx = coef * mu;
@@ -707,10 +714,10 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       // iteration 0 with FPM, |h|^2 for the memory read's query
       const float2 dep_nx = sig + hn + anc;
       float v2[3] = {dot2(dh, dh), dot2(dep_nx, dep_nx), dot2(hn, hn)};
-      if (FPM && it == 0) R.sum(v2);
+      if (FPM && it == 0) bsum<NW>(R, v2);
       else {
         float v2b[2] = {v2[0], v2[1]};
-        R.sum(v2b);
+        bsum<NW>(R, v2b);
         v2[0] = v2b[0];
         v2[1] = v2b[1];
       }
@@ -772,7 +779,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       const float2 dep0n = sig_nx + hcur + anc + Av_nx;
       float v3[6] = {dot2(m, m), dot2(df, df), dot2(hcur, hcur), dot2(ld2(wprm + d + j0), c), dot2(dep0n, dep0n),
                      dot2(sig_nx, sig_nx)};
-      R.sum(v3);
+      bsum<NW>(R, v3);
       dep0_sq = v3[4];
       sig_sq = v3[5];
       const float2 hu = rsqrtf(fmaxf(v3[2] * inv_d, 1e-6f)) * hcur;
@@ -920,18 +927,18 @@ static size_t picard_smem_base(int d) {
   return (size_t)(512 + 64 + 1024 + 64 + 64 + 6 * d) * sizeof(float);
 }
 
-template <bool FPM, int MAXT>
+template <bool FPM, int MAXT, int NW = 0>
 static cudaError_t picard_launch(const PicardArgs &a, cudaStream_t st) {
   const int threads = a.d / 2;
   size_t smem = picard_smem_base(a.d);
   if (!FPM) {
-    cudaError_t e = cudaFuncSetAttribute(picard_kernel<false, MAXT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(picard_kernel<false, MAXT, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
-    picard_kernel<false, MAXT><<<a.B * a.h, threads, smem, st>>>(a);
+    picard_kernel<false, MAXT, NW><<<a.B * a.h, threads, smem, st>>>(a);
     return cudaGetLastError();
   }
-  cudaError_t e = cudaFuncSetAttribute(picard_kernel<true, MAXT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaError_t e = cudaFuncSetAttribute(picard_kernel<true, MAXT, NW>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e != cudaSuccess) return e;
   int dev = 0, optin = 0;
   cudaGetDevice(&dev);
@@ -954,7 +961,7 @@ static cudaError_t picard_launch(const PicardArgs &a, cudaStream_t st) {
     smem -= mat_bytes;
     smem += (2 * (size_t)a.h * (a.d + kRank) + 4) * sizeof(float);
   }
-  e = cudaFuncSetAttribute(picard_kernel<true, MAXT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  e = cudaFuncSetAttribute(picard_kernel<true, MAXT, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.B * a.h);
@@ -968,7 +975,7 @@ static cudaError_t picard_launch(const PicardArgs &a, cudaStream_t st) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, picard_kernel<true, MAXT>, p);
+  e = cudaLaunchKernelEx(&cfg, picard_kernel<true, MAXT, NW>, p);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
@@ -976,6 +983,8 @@ static cudaError_t picard_launch(const PicardArgs &a, cudaStream_t st) {
 cudaError_t launch_picard(const PicardArgs &a, bool fpm, cudaStream_t st) {
   if (a.B <= 0 || a.T <= 0 || a.t1 <= a.t0) return cudaSuccess;
   if (a.d > 512) return fpm ? picard_launch<true, 512>(a, st) : picard_launch<false, 512>(a, st);
+  if (a.d == 512)  // 256 threads: eight warps, static reductions
+    return fpm ? picard_launch<true, 256, 8>(a, st) : picard_launch<false, 256, 8>(a, st);
   return fpm ? picard_launch<true, 256>(a, st) : picard_launch<false, 256>(a, st);
 }
 
