@@ -83,6 +83,11 @@ struct aideen_ctx {
   // FPM backward stream: runs beside the attention-branch weight gradients
   cudaStream_t fst = nullptr;
   cudaEvent_t ev_g0 = nullptr, ev_fdone = nullptr;
+  // last pipeline chunk: dW_lm and the LM-head bias / gain sums on their own
+  // stream beside the weight gradients; joined before the gradients are used
+  cudaStream_t lmst = nullptr;
+  cudaEvent_t ev_adj = nullptr, ev_lmg = nullptr;
+  bool lmg_pending = false;
   bool fpm_prepared = false;  // the FPM backward's forward-only stage already ran this step
   int sm_budget = 0;      // SMs the GEMM / softmax / adjoint launches may use (0: all)
   // optional stage timeline of the pipelined step (AIDEEN_PIPE_TIMELINE=1, stderr)
@@ -762,10 +767,15 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
                   b.dlog_lo + r0 * Vp, b.wlo));
     KL(launch_rmsnorm_bwd(b.dy + r0 * d, b.pooled + r0 * d, b.lrms + r0, glm, b.dl_dh + r0 * d,
                           b.ggp + r0 * d, R, d, st));
-    // dW_lm[v][j] += sum_{n in chunk} dlogits[n][v] y^T[j][n]
-    KL(gemm_split(ctx, gemm(V, d, R, 1, b.logits + r0 * Vp, Vp, 0, true, b.yThi + r0, N4, 0, true, b.Glm, d, 0,
-                            1.f, j > 0 ? 1.f : 0.f),
-                  b.dlog_lo + r0 * Vp, b.yTlo + r0));
+    // dW_lm[v][j] += sum_{n in chunk} dlogits[n][v] y^T[j][n]; the last chunk's
+    // runs after its adjoint, on its own stream (below)
+    const bool tail_lm = j == nch - 1 && ctx->lmst && !ctx->prof;
+    auto dwlm = [&]() {
+      return gemm_split(ctx, gemm(V, d, R, 1, b.logits + r0 * Vp, Vp, 0, true, b.yThi + r0, N4, 0, true, b.Glm,
+                                  d, 0, 1.f, j > 0 ? 1.f : 0.f),
+                        b.dlog_lo + r0 * Vp, b.yTlo + r0);
+    };
+    if (!tail_lm) KL(dwlm());
     // adjoint of the chunk's rows
     AdjointArgs aa{};
     aa.N = R; aa.h = h; aa.d = d; aa.iters = a->adj_iters; aa.anderson_m = a->anderson_m;
@@ -776,13 +786,28 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
     if (a->anderson_m > 4) { ctx->sm_budget = 0; return set_err(ctx, AIDEEN_E_UNSUPPORTED, "anderson_m > 4"); }
     KL(launch_adjoint(aa, st));
     tl_mark(ctx, ("cons" + std::to_string(j)).c_str(), st);
+    if (tail_lm) {
+      CU(cudaEventRecord(ctx->ev_adj, st));
+      CU(cudaStreamWaitEvent(ctx->lmst, ctx->ev_adj, 0));
+      ctx->stream = ctx->lmst;
+      ctx->sm_budget = 0;
+      const cudaError_t e = dwlm();
+      ctx->stream = st;
+      KL(e);
+    }
   }
   ctx->sm_budget = 0;
   ctx->adj_N = N;
   ctx->adj_beta = r->damping;
   KL(launch_sum(b.loss_rows, N, b.scal + 1, st));
-  KL(launch_colsum(b.colpart, colpart_rows, V, Vp, b.Glm + ctx->lm_b, V, 0, false, st));
-  KL(launch_colsum(b.ggp, N, d, d, b.Glm + ctx->lm_g, d, 0, false, st));
+  const bool tail_lm = ctx->lmst && !ctx->prof;
+  cudaStream_t lst = tail_lm ? ctx->lmst : st;
+  KL(launch_colsum(b.colpart, colpart_rows, V, Vp, b.Glm + ctx->lm_b, V, 0, false, lst));
+  KL(launch_colsum(b.ggp, N, d, d, b.Glm + ctx->lm_g, d, 0, false, lst));
+  if (tail_lm) {
+    CU(cudaEventRecord(ctx->ev_lmg, ctx->lmst));
+    ctx->lmg_pending = true;
+  }
   return stats ? read_solve_stats(ctx, r, stats) : AIDEEN_OK;
 }
 
@@ -944,6 +969,9 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->fst, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_g0, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_fdone, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->lmst, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_adj, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_lmg, cudaEventDisableTiming);
   for (int i = 0; i < aideen_ctx::kMaxChunks && e == cudaSuccess; ++i)
     e = cudaEventCreateWithFlags(&ctx->ev_pic[i], cudaEventDisableTiming);
   if (e != cudaSuccess) {
@@ -994,6 +1022,9 @@ void aideen_destroy(aideen_ctx *ctx) {
   if (ctx->fst) { cudaStreamSynchronize(ctx->fst); cudaStreamDestroy(ctx->fst); }
   if (ctx->ev_g0) cudaEventDestroy(ctx->ev_g0);
   if (ctx->ev_fdone) cudaEventDestroy(ctx->ev_fdone);
+  if (ctx->lmst) { cudaStreamSynchronize(ctx->lmst); cudaStreamDestroy(ctx->lmst); }
+  if (ctx->ev_adj) cudaEventDestroy(ctx->ev_adj);
+  if (ctx->ev_lmg) cudaEventDestroy(ctx->ev_lmg);
   for (auto &ev : ctx->ev_pic)
     if (ev) cudaEventDestroy(ev);
   if (ctx->ev_grads) cudaEventDestroy(ctx->ev_grads);
@@ -1298,6 +1329,10 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
                     a->anderson_m));
   }
   CHK(run_weight_grads(ctx, false));
+  if (ctx->lmg_pending) {  // the last chunk's dW_lm and LM-head sums
+    CU(cudaStreamWaitEvent(ctx->stream, ctx->ev_lmg, 0));
+    ctx->lmg_pending = false;
+  }
   tl_mark(ctx, "wgrads", ctx->stream);
   CHK(run_update(ctx, &a->update));
   tl_mark(ctx, "update", ctx->stream);
