@@ -182,6 +182,45 @@ __device__ __forceinline__ void mv_d_to_32(const float *M0, const float *M1, flo
   if (SYNC_OUT) __syncthreads();
 }
 
+// Warp partials of out = M . x for x already staged in xs (all of it visible to
+// every thread): each warp's 64 rows, reduced over the warp, into part[warp *
+// 64 + 0..31].  No block barrier: the caller's next one publishes part.
+__device__ __forceinline__ void mv_d_to_32_partials(const float *M0, const float *xs, float *part) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 3, rq = (lane & 7) * 4;
+  const int jb = warp * 64 + g;
+  float4 acc = f4(0.f), acc1 = f4(0.f);
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) {
+    const int j = jb + 4 * i;
+    acc = acc + xs[j] * ld4(M0 + (size_t)j * kRank + rq);
+    acc1 = acc1 + xs[j + 4] * ld4(M0 + (size_t)(j + 4) * kRank + rq);
+  }
+  acc = acc + acc1;
+#pragma unroll
+  for (int o = 8; o <= 16; o <<= 1) {
+    acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+    acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
+    acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
+    acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
+  }
+  if (g == 0) st4(part + warp * 64 + rq, acc);
+}
+
+// Lane l of the calling warp: sum over the NW warps of part[w * 64 + l].
+template <int NW>
+__device__ __forceinline__ float sum_partials32(const float *part) {
+  const int lane = threadIdx.x & 31;
+  const int nw = NW > 0 ? NW : (int)(blockDim.x >> 5);
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < (NW > 0 ? NW : 32); ++w) {
+    if (NW == 0 && w >= nw) break;
+    t += part[w * 64 + lane];
+  }
+  return t;
+}
+
 // Two 32->d products in one pass: ya = Ma . ina, yb = Mb . inb (thread's 2 outputs).
 __device__ __forceinline__ void mv2_32_to_d(const float *Ma, const float *ina, const float *Mb,
                                             const float *inb, int d, int j0, float2 &ya, float2 &yb) {
@@ -619,7 +658,10 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
           const float ihq = rsqrtf(fmaxf(hq_sq, 1e-6f));
           const float sig_norm = sqrtf(fmaxf(sig_sq, 1e-6f));
           // the query lands in vec[0..32), written and read by warp 0 only
-          mv_d_to_32<1, false>(mat[1], nullptr, ihq * hcur, j0, xs, vec, part);
+          // (q = W_q_mem . h / |h|: the staged h is unscaled, the sum is scaled)
+          mv_d_to_32_partials(mat[1], xs, part);
+          __syncthreads();
+          if (threadIdx.x < 32) vec[threadIdx.x] = ihq * sum_partials32<NW>(part);
           PT(6);
           cg::cluster_group cl = cg::this_cluster();
           if (threadIdx.x < 32) {
@@ -713,6 +755,9 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       // next one (dep has no attention term after iteration 0) and, after
       // iteration 0 with FPM, |h|^2 for the memory read's query
       const float2 dep_nx = sig + hn + anc;
+      // the memory read's query input (h after iteration 0), published by this
+      // iteration's reduction barrier
+      if (FPM && it == 0) st2(xs + j0, hn);
       float v2[3] = {dot2(dh, dh), dot2(dep_nx, dep_nx), dot2(hn, hn)};
       if (FPM && it == 0) bsum<NW>(R, v2);
       else {
@@ -799,25 +844,34 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       PT(4);
       // read key of the new memory, used by every slot at the next token
       // peers read the key after the cluster barrier below; no block barrier needed
-      mv_d_to_32<1, false>(mat[0], nullptr, m + hsv * tanh2(m) + hbv, j0, xs, keybuf + (cur ^ 1) * 32, part);
-      PT(7);
       if (a.push) {
         // push this token's memory row and key into every slot's inbox for the
-        // next token (none after the last token of the launch)
+        // next token (none, and no key, after the last token of the launch)
         if (t + 1 < a.t1) {
-          __syncthreads();  // mbuf row and key complete
-          if (threadIdx.x == 0) {
-            const int nb = (t - a.t0 + 1) & 1;
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            for (int q = 0; q < h; ++q) {
-              push_to(mbuf + (cur ^ 1) * d, inbox_m + ((size_t)nb * h + s) * d, &inbar[nb], q, (uint32_t)d * 4u);
-              push_to(keybuf + (cur ^ 1) * 32, inbox_k + ((size_t)nb * h + s) * kRank, &inbar[nb], q,
-                      kRank * 4u);
+          st2(xs + j0, m + hsv * tanh2(m) + hbv);
+          __syncthreads();
+          mv_d_to_32_partials(mat[0], xs, part);
+          PT(7);
+          __syncthreads();  // key partials and the mbuf row complete
+          if (warp == 0) {
+            const int lane = threadIdx.x & 31;
+            keybuf[(cur ^ 1) * 32 + lane] = sum_partials32<NW>(part);
+            __syncwarp();
+            if (lane == 0) {
+              const int nb = (t - a.t0 + 1) & 1;
+              asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+              for (int q = 0; q < h; ++q) {
+                push_to(mbuf + (cur ^ 1) * d, inbox_m + ((size_t)nb * h + s) * d, &inbar[nb], q, (uint32_t)d * 4u);
+                push_to(keybuf + (cur ^ 1) * 32, inbox_k + ((size_t)nb * h + s) * kRank, &inbar[nb], q,
+                        kRank * 4u);
+              }
             }
           }
         }
         cur ^= 1;
       } else {
+        mv_d_to_32<1, false>(mat[0], nullptr, m + hsv * tanh2(m) + hbv, j0, xs, keybuf + (cur ^ 1) * 32, part);
+        PT(7);
         cur ^= 1;
         // publish this token's memory and key to the cluster; the global stores
         // (no reader inside this kernel) come after the arrive, so its release
