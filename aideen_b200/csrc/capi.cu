@@ -54,6 +54,7 @@ struct DevBufs {
   float *stage = nullptr;  // packed AllWeights staging for upload/download
   float *ws = nullptr;     // split-K partial sums of the tensor-core GEMM
   float *ws2 = nullptr;    // the same for GEMMs on the FPM-backward stream
+  float *ws3 = nullptr;    // and for the attention-gradient side stream
   // FPM backward (allocated on first use): [N][h][d] unless noted
   float *fc = nullptr, *frp = nullptr, *fdl = nullptr, *fminner = nullptr, *fdm = nullptr,
         *fgpre = nullptr;
@@ -87,6 +88,9 @@ struct aideen_ctx {
   // stream beside the weight gradients; joined before the gradients are used
   cudaStream_t lmst = nullptr;
   cudaEvent_t ev_adj = nullptr, ev_lmg = nullptr;
+  // attention-branch weight gradients: the GEMMs off the dsig chain run on ast
+  cudaStream_t ast = nullptr;
+  cudaEvent_t ev_da = nullptr, ev_dqkv = nullptr, ev_adone = nullptr;
   bool lmg_pending = false;
   bool fpm_prepared = false;  // the FPM backward's forward-only stage already ran this step
   int sm_budget = 0;      // SMs the GEMM / softmax / adjoint launches may use (0: all)
@@ -464,7 +468,26 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
     tl_mark(ctx, "fpm_bwd", ctx->fst);
     CU(cudaEventRecord(ctx->ev_fdone, ctx->fst));
   }
-  KL(launch_colsum(b.nsg, N, d, d, G + L.nscale, d, 0, false, st));
+  // Off the dsig chain (attn scale -> dn -> softmax backward -> dsig -> dsrc
+  // -> W_in gradient), the W_o / W_q,k,v gradient GEMMs and the bias sums run
+  // on a side stream with their own split-K workspace.
+  const bool fork_attn = sc && !ctx->prof && ctx->ast;
+  cudaStream_t sst = fork_attn ? ctx->ast : st;
+  auto on_side = [&](auto &&f) -> cudaError_t {
+    if (!fork_attn) return f();
+    float *keep_ws = b.ws;
+    ctx->stream = ctx->ast;
+    b.ws = b.ws3;
+    const cudaError_t e = f();
+    ctx->stream = st;
+    b.ws = keep_ws;
+    return e;
+  };
+  if (fork_attn) {
+    if (!fork_fpm) CU(cudaEventRecord(ctx->ev_g0, st));
+    CU(cudaStreamWaitEvent(ctx->ast, ctx->ev_g0, 0));
+  }
+  KL(launch_colsum(b.nsg, N, d, d, G + L.nscale, d, 0, false, sst));
   AttnBwdArgs a{};
   a.h = h; a.d = d; a.W = W; a.off_qb = L.q_bias; a.off_kb = L.k_bias; a.off_anchor = L.slot_anchor;
   a.gpre = b.gpre; a.amat = b.amat; a.scale = b.scale; a.rho = b.rho; a.Rsrc = b.Rsrc;
@@ -472,20 +495,35 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   a.alpha = b.alpha; a.Qh = b.Qh; a.Kh = b.Kh; a.Vh = b.Vh; a.dQ = b.dQ; a.dK = b.dK; a.dV = b.dV;
   if (sc) {
     KL(launch_attn_bwd_scale(a, N * h, st));
+    if (fork_attn) {
+      CU(cudaEventRecord(ctx->ev_da, st));
+      CU(cudaStreamWaitEvent(ctx->ast, ctx->ev_da, 0));
+    }
+    // gW_o[s][c][o] = sum_n n[n][s][c] da[n][s][o]
+    KL(on_side([&] {
+      return gemm_any(ctx, gemm(kHeadDim, d, N, h, b.nmix, H32, kHeadDim, true, b.da, (long)h * d, d, false,
+                                G + L.wo, d, (long)d * d));
+    }));
     // dn[n][s][c] = sum_o da[n][s][o] W_o[s][c*d + o]
     KL(gemm_any(ctx, gemm(N, kHeadDim, d, h, b.da, (long)h * d, d, false, W + L.wo, d, (long)d * d, true,
                      b.dn, H32, kHeadDim)));
-    // gW_o[s][c][o] = sum_n n[n][s][c] da[n][s][o]
-    KL(gemm_any(ctx, gemm(kHeadDim, d, N, h, b.nmix, H32, kHeadDim, true, b.da, (long)h * d, d, false,
-                     G + L.wo, d, (long)d * d)));
     tl_mark(ctx, "wg_o", st);
     KL(launch_attn_bwd_softmax(a, N, st));
+    if (fork_attn) {
+      CU(cudaEventRecord(ctx->ev_dqkv, st));
+      CU(cudaStreamWaitEvent(ctx->ast, ctx->ev_dqkv, 0));
+    }
     // gW_{q,k,v}[s][j][c] = sum_n src[n][s][j] d{Q,K,V}[n][s][c]
     const float *dqkv[3] = {b.dQ, b.dK, b.dV};
     const size_t woff[3] = {L.wq, L.wk, L.wv};
     for (int i = 0; i < 3; ++i)
-      KL(gemm_any(ctx, gemm(d, kHeadDim, N, h, b.src, (long)h * d, d, true, dqkv[i], H32, kHeadDim,
-                       false, G + woff[i], d, (long)d * d)));
+      KL(on_side([&] {
+        return gemm_any(ctx, gemm(d, kHeadDim, N, h, b.src, (long)h * d, d, true, dqkv[i], H32, kHeadDim,
+                                  false, G + woff[i], d, (long)d * d));
+      }));
+    KL(launch_colsum(b.dQ, N, H32, H32, G + L.q_bias, kHeadDim, d, false, sst));
+    KL(launch_colsum(b.dK, N, H32, H32, G + L.k_bias, kHeadDim, d, false, sst));
+    if (fork_attn) CU(cudaEventRecord(ctx->ev_adone, ctx->ast));
     tl_mark(ctx, "wg_qkv", st);
     KL(launch_dsig_init(a, b.dsig, N * h, 1, st));
     // dsrc[n][s][j] += sum_c d{Q,K,V}[n][s][c] W[s][j*d + c]
@@ -493,8 +531,6 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
       KL(gemm_any(ctx, gemm(N, d, kHeadDim, h, dqkv[i], H32, kHeadDim, false, W + woff[i], d, (long)d * d,
                        true, b.dsig, (long)h * d, d, 1.f, 1.f)));
     tl_mark(ctx, "dsrc", st);
-    KL(launch_colsum(b.dQ, N, H32, H32, G + L.q_bias, kHeadDim, d, false, st));
-    KL(launch_colsum(b.dK, N, H32, H32, G + L.k_bias, kHeadDim, d, false, st));
     KL(launch_colsum(b.dsig, N, h * d, (long)h * d, G + L.slot_anchor, h * d, 0, false, st));
   } else {
     KL(launch_dsig_init(a, b.dsig, N * h, 0, st));
@@ -513,6 +549,7 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   } else if (want_ds) {
     CU(cudaMemsetAsync(b.dS, 0, (size_t)N * d * sizeof(float), st));
   }
+  if (fork_attn) CU(cudaStreamWaitEvent(st, ctx->ev_adone, 0));
   tl_mark(ctx, "attn_grads", st);
   if (fork_fpm) CU(cudaStreamWaitEvent(st, ctx->ev_fdone, 0));
   else if (ctx->last_run.fpm) CHK(run_fpm_backward(ctx));
@@ -791,7 +828,10 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
       CU(cudaStreamWaitEvent(ctx->lmst, ctx->ev_adj, 0));
       ctx->stream = ctx->lmst;
       ctx->sm_budget = 0;
+      float *keep_ws = b.ws;
+      b.ws = nullptr;  // no split-K here: the context stream's GEMMs own the workspace meanwhile
       const cudaError_t e = dwlm();
+      b.ws = keep_ws;
       ctx->stream = st;
       KL(e);
     }
@@ -945,7 +985,7 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   A(&b.yThi, d * ((N + 3) / 4 * 4)); A(&b.yTlo, d * ((N + 3) / 4 * 4)); A(&b.ggp, N * d); A(&b.lrms, N); A(&b.loss_rows, N);
   A(&b.scal, 4); A(&b.stage, ctx->Lx.total);
   ctx->ws_floats = 16 * N * d;  // up to 16 splits of an [N][d] output
-  A(&b.ws, ctx->ws_floats); A(&b.ws2, ctx->ws_floats); A(&b.stats, 4); A(&b.sigmas, 5 * h + 2);
+  A(&b.ws, ctx->ws_floats); A(&b.ws2, ctx->ws_floats); A(&b.ws3, ctx->ws_floats); A(&b.stats, 4); A(&b.sigmas, 5 * h + 2);
   if (V) {
     A(&b.lmp, ctx->lm_len); A(&b.Glm, ctx->lm_len); A(&b.Mlm1, ctx->lm_len); A(&b.Mlm2, ctx->lm_len);
     A(&b.logits, N * (size_t)ctx->Vp); A(&b.emb, V * d);
@@ -970,6 +1010,10 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_g0, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_fdone, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->lmst, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->ast, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_da, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_dqkv, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_adone, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_adj, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_lmg, cudaEventDisableTiming);
   for (int i = 0; i < aideen_ctx::kMaxChunks && e == cudaSuccess; ++i)
@@ -1011,7 +1055,7 @@ void aideen_destroy(aideen_ctx *ctx) {
                   b.Mlm2, b.y, b.lrms, b.logits, b.dy, b.ggp, b.loss_rows, b.scal, b.emb, b.stats,
                   b.sigmas, b.stage, b.ws, b.fc, b.frp, b.fdl, b.fminner, b.fdm, b.fgpre, b.fup,
                   b.fkw, b.fdup, b.fA, b.fU, b.fgin, b.fcarry, b.fpart, b.fpart_bw, b.src,
-                  b.dlog_lo, b.yhi, b.ylo, b.yThi, b.yTlo, b.whi, b.wlo, b.colpart, b.perm, b.ws2, b.rowstats};
+                  b.dlog_lo, b.yhi, b.ylo, b.yThi, b.yTlo, b.whi, b.wlo, b.colpart, b.perm, b.ws2, b.ws3, b.rowstats};
   for (void *p : ptrs)
     if (p) cudaFree(p);
   if (ctx->side) cudaStreamSynchronize(ctx->side);
@@ -1023,6 +1067,10 @@ void aideen_destroy(aideen_ctx *ctx) {
   if (ctx->ev_g0) cudaEventDestroy(ctx->ev_g0);
   if (ctx->ev_fdone) cudaEventDestroy(ctx->ev_fdone);
   if (ctx->lmst) { cudaStreamSynchronize(ctx->lmst); cudaStreamDestroy(ctx->lmst); }
+  if (ctx->ast) { cudaStreamSynchronize(ctx->ast); cudaStreamDestroy(ctx->ast); }
+  if (ctx->ev_da) cudaEventDestroy(ctx->ev_da);
+  if (ctx->ev_dqkv) cudaEventDestroy(ctx->ev_dqkv);
+  if (ctx->ev_adone) cudaEventDestroy(ctx->ev_adone);
   if (ctx->ev_adj) cudaEventDestroy(ctx->ev_adj);
   if (ctx->ev_lmg) cudaEventDestroy(ctx->ev_lmg);
   for (auto &ev : ctx->ev_pic)
