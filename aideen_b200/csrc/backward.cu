@@ -11,6 +11,8 @@
 //   attn_bwd_softmax per-token softmax / mean-subtracted mix backward
 //   dsig_init        dL/dsignal = g_pre + dL/dR * dR/dsrc
 //   colsum           column sums (bias / anchor / NormScale gradients)
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -50,7 +52,65 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 // (pre parts, per-slot RHS, pooled RHS row) streaming into the other half of a
 // double-buffered shared-memory stage with cp.async.bulk, so HBM traffic
 // overlaps the on-chip iterations.  Waits are bounded.
-template <int F, int MA, int MAXT, int MINB>
+// Anderson weights of one token: block-reduce the Gram of the pseudo-residuals
+// (g6 = this warp's partials <d0,d0>, <d0,d1>, <d0,d2>, <d1,d1>, <d1,d2>,
+// <d2,d2>), then the regularised Cramer solve, clamp and renormalisation of
+// staged_adjoint_picard_clean.wgsl:1022-1135.  buf: 96 floats of shared memory.
+template <int MA>
+__device__ __forceinline__ void anderson_coefs(float (&g6)[6], int n_res, float *buf, int s, int lane, int h,
+                                               float &b0, float &b1, float &b2) {
+  b2 = 0.f;
+#pragma unroll
+  for (int q = 0; q < 6; ++q) {
+    const float x = warp_sum(g6[q]);
+    if (lane == 0) buf[q * 16 + s] = x;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < 6; ++q) {
+    float t = 0.f;
+    for (int w = 0; w < h; ++w) t += buf[q * 16 + w];
+    g6[q] = t;
+  }
+  if (n_res == 2) {
+    float g00 = g6[0], g01 = g6[1], g10 = g6[1], g11 = g6[3];
+    const float reg = fmaxf(1e-8f, 1e-4f * (fabsf(g00) + fabsf(g11)));
+    g00 += reg;
+    g11 += reg;
+    const float det = g00 * g11 - g01 * g10;
+    const float sdet = det < 0.f ? fminf(det, -1e-10f) : fmaxf(det, 1e-10f);
+    b0 = (g11 - g01) / sdet;
+    b1 = (g00 - g10) / sdet;
+  } else {
+    float g00 = g6[0], g01 = g6[1], g02 = g6[2];
+    float g10 = g6[1], g11 = g6[3], g12 = g6[4];
+    float g20 = g6[2], g21 = g6[4], g22 = g6[5];
+    const float reg = fmaxf(1e-8f, 1e-4f * (fabsf(g00) + fabsf(g11) + fabsf(g22)));
+    g00 += reg;
+    g11 += reg;
+    g22 += reg;
+    const float det = g00 * (g11 * g22 - g12 * g21) - g01 * (g10 * g22 - g12 * g20) +
+                      g02 * (g10 * g21 - g11 * g20);
+    const float sdet = det < 0.f ? fminf(det, -1e-8f) : fmaxf(det, 1e-8f);
+    b0 = ((g11 * g22 - g12 * g21) - g01 * (g22 - g12) + g02 * (g21 - g11)) / sdet;
+    b1 = (g00 * (g22 - g12) - (g10 * g22 - g12 * g20) + g02 * (g10 - g20)) / sdet;
+    b2 = (g00 * (g11 - g21) - g01 * (g10 - g20) + (g10 * g21 - g11 * g20)) / sdet;
+  }
+  b0 = fminf(fmaxf(b0, -2.f), 3.f);
+  b1 = fminf(fmaxf(b1, -2.f), 3.f);
+  if (n_res == 3) b2 = fminf(fmaxf(b2, -2.f), 3.f);
+  const float ssum = b0 + b1 + (n_res == 3 ? b2 : 0.f);
+  if (fabsf(ssum) < 1e-6f) {
+    b0 = 1.f; b1 = 0.f; b2 = 0.f;
+  } else {
+    b0 /= ssum; b1 /= ssum; b2 = n_res == 3 ? b2 / ssum : 0.f;
+  }
+}
+
+// HS: the Anderson iterates live in a shared-memory ring ([MA][h][d], each
+// thread touching only its own elements) instead of registers, which leaves
+// room for two CTAs (two tokens) per SM.
+template <int F, int MA, int MAXT, int MINB, bool HS = false>
 __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
   extern __shared__ __align__(128) unsigned char smraw[];
   uint64_t *bar = reinterpret_cast<uint64_t *>(smraw);  // [2]
@@ -131,7 +191,8 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
       av[f] = (beta * inv) * ns[f] + f4(1.f - beta);
       wv[f] = beta * (ns[f] * pre[f]);
     }
-    float4 hist[MA > 0 ? MA : 1][F];
+    float4 hist[(MA > 0 && !HS) ? MA : 1][F];
+    float *ring = stage0 + 2 * stage_f + (size_t)s * d;  // HS: iterate slot q at ring + q * hd
     for (int k = 0; k < a.iters; ++k) {
       float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;  // independent partial sums (ILP)
 #pragma unroll
@@ -151,7 +212,43 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
         x.w = fmaf(ncs, pre[f].w, fmaf(av[f].w, v[f].w, rhs[f].w));
         v[f] = x;
       }
-      if constexpr (MA > 0) {
+      if constexpr (MA > 0 && HS) {
+        // hist i steps ago = ring slot (k - i) mod MA; this iterate goes to slot k mod MA
+#pragma unroll
+        for (int f = 0; f < F; ++f) st4(ring + (size_t)(k % MA) * hd + (f * 32 + lane) * 4, v[f]);
+        const int n_res = k < MA - 1 ? k : MA - 1;
+        if (k >= 2 && n_res >= 2) {
+          const float *r1 = ring + (size_t)((k + MA - 1) % MA) * hd;
+          const float *r2 = ring + (size_t)((k + MA - 2) % MA) * hd;
+          const float *r3 = ring + (size_t)((k + MA - 3) % MA) * hd;
+          float g6[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  #pragma unroll
+          for (int f = 0; f < F; ++f) {
+            const int j = (f * 32 + lane) * 4;
+            const float4 h1 = ld4(r1 + j), h2 = ld4(r2 + j);
+            const float4 d0 = v[f] - h1;
+            const float4 d1 = h1 - h2;
+            g6[0] += dot4(d0, d0);
+            g6[1] += dot4(d0, d1);
+            g6[3] += dot4(d1, d1);
+            if (MA > 3 && n_res == 3) {
+              const float4 d2 = h2 - ld4(r3 + j);
+              g6[2] += dot4(d0, d2);
+              g6[4] += dot4(d1, d2);
+              g6[5] += dot4(d2, d2);
+            }
+          }
+          float b0, b1, b2;
+          anderson_coefs<MA>(g6, n_res, gram + (k & 1) * 96, s, lane, h, b0, b1, b2);
+  #pragma unroll
+          for (int f = 0; f < F; ++f) {
+            const int j = (f * 32 + lane) * 4;
+            float4 mixed = b0 * v[f] + b1 * ld4(r1 + j);
+            if (MA > 3 && n_res == 3) mixed = mixed + b2 * ld4(r2 + j);
+            v[f] = mixed;
+          }
+        }
+      } else if constexpr (MA > 0) {
         // ring buffer as a shift register: hist[i] = iterate stored i steps ago
   #pragma unroll
         for (int i = MA - 1; i > 0; --i)
@@ -177,53 +274,8 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
               g6[5] += dot4(d2, d2);
             }
           }
-          float *buf = gram + (k & 1) * 96;
-  #pragma unroll
-          for (int q = 0; q < 6; ++q) {
-            const float x = warp_sum(g6[q]);
-            if (lane == 0) buf[q * 16 + s] = x;
-          }
-          __syncthreads();
-  #pragma unroll
-          for (int q = 0; q < 6; ++q) {
-            float t = 0.f;
-            for (int w = 0; w < h; ++w) t += buf[q * 16 + w];
-            g6[q] = t;
-          }
-          float b0, b1, b2 = 0.f;
-          if (n_res == 2) {
-            float g00 = g6[0], g01 = g6[1], g10 = g6[1], g11 = g6[3];
-            const float reg = fmaxf(1e-8f, 1e-4f * (fabsf(g00) + fabsf(g11)));
-            g00 += reg;
-            g11 += reg;
-            const float det = g00 * g11 - g01 * g10;
-            const float sdet = det < 0.f ? fminf(det, -1e-10f) : fmaxf(det, 1e-10f);
-            b0 = (g11 - g01) / sdet;
-            b1 = (g00 - g10) / sdet;
-          } else {
-            float g00 = g6[0], g01 = g6[1], g02 = g6[2];
-            float g10 = g6[1], g11 = g6[3], g12 = g6[4];
-            float g20 = g6[2], g21 = g6[4], g22 = g6[5];
-            const float reg = fmaxf(1e-8f, 1e-4f * (fabsf(g00) + fabsf(g11) + fabsf(g22)));
-            g00 += reg;
-            g11 += reg;
-            g22 += reg;
-            const float det = g00 * (g11 * g22 - g12 * g21) - g01 * (g10 * g22 - g12 * g20) +
-                              g02 * (g10 * g21 - g11 * g20);
-            const float sdet = det < 0.f ? fminf(det, -1e-8f) : fmaxf(det, 1e-8f);
-            b0 = ((g11 * g22 - g12 * g21) - g01 * (g22 - g12) + g02 * (g21 - g11)) / sdet;
-            b1 = (g00 * (g22 - g12) - (g10 * g22 - g12 * g20) + g02 * (g10 - g20)) / sdet;
-            b2 = (g00 * (g11 - g21) - g01 * (g10 - g20) + (g10 * g21 - g11 * g20)) / sdet;
-          }
-          b0 = fminf(fmaxf(b0, -2.f), 3.f);
-          b1 = fminf(fmaxf(b1, -2.f), 3.f);
-          if (n_res == 3) b2 = fminf(fmaxf(b2, -2.f), 3.f);
-          const float ssum = b0 + b1 + (n_res == 3 ? b2 : 0.f);
-          if (fabsf(ssum) < 1e-6f) {
-            b0 = 1.f; b1 = 0.f; b2 = 0.f;
-          } else {
-            b0 /= ssum; b1 /= ssum; b2 = n_res == 3 ? b2 / ssum : 0.f;
-          }
+          float b0, b1, b2;
+          anderson_coefs<MA>(g6, n_res, gram + (k & 1) * 96, s, lane, h, b0, b1, b2);
   #pragma unroll
           for (int f = 0; f < F; ++f) {
             float4 mixed = b0 * hist[0][f] + b1 * hist[1][f];
@@ -260,13 +312,13 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
   if (threadIdx.x == 0 && pending && it < 1 << 30) mbar_wait_bounded(&bar[(it + 1) & 1], ((it + 1) >> 1) & 1);
 }
 
-template <int F, int MA, int MAXT, int MINB>
+template <int F, int MA, int MAXT, int MINB, bool HS = false>
 static cudaError_t adjoint_launch(const AdjointArgs &a, cudaStream_t st) {
   const size_t hd = (size_t)a.h * a.d;
   const size_t stage_f = hd * (1 + (a.pre_b != nullptr) + (a.rhs_slot != nullptr)) +
                          (a.rhs_tok ? (size_t)a.d : 0);
-  const size_t smem = 128 + 192 * 4 + 2 * stage_f * 4;
-  auto k = adjoint_kernel<F, MA, MAXT, MINB>;
+  const size_t smem = 128 + 192 * 4 + 2 * stage_f * 4 + (HS ? (size_t)MA * hd * 4 : 0);
+  auto k = adjoint_kernel<F, MA, MAXT, MINB, HS>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   int per_sm = 0, dev = 0, sms = 0;
@@ -288,7 +340,12 @@ static cudaError_t adjoint_dispatch_m(const AdjointArgs &a, cudaStream_t st) {
   switch (ma) {
     case 0: return small ? adjoint_launch<F, 0, 256, 2>(a, st) : adjoint_launch<F, 0, 512, 1>(a, st);
     case 3: return small ? adjoint_launch<F, 3, 256, 1>(a, st) : adjoint_launch<F, 3, 512, 1>(a, st);
-    case 4: return small ? adjoint_launch<F, 4, 256, 1>(a, st) : adjoint_launch<F, 4, 512, 1>(a, st);
+    case 4:
+      // iterates in shared memory (two tokens per SM) while two CTAs' rings and
+      // stages fit: 4 x h x d floats of ring per CTA
+      if (small && 4 * (size_t)a.h * a.d <= 16384 && !getenv("AIDEEN_ADJ_REG_HIST"))
+        return adjoint_launch<F, 4, 256, 2, true>(a, st);
+      return small ? adjoint_launch<F, 4, 256, 1>(a, st) : adjoint_launch<F, 4, 512, 1>(a, st);
     default: return cudaErrorInvalidValue;
   }
 }
