@@ -61,6 +61,7 @@ struct DevBufs {
   float *fup = nullptr, *fkw = nullptr, *fdup = nullptr;  // [N][h][32]
   float *fA = nullptr, *fU = nullptr, *fgin = nullptr;    // [max_batch][h][nch][d]
   float *fcarry = nullptr;                                // [max_batch][h][d] TBPTT carry
+  float *fprm = nullptr;                                   // [h][5][d] FPM slot parameters
   float *fpart = nullptr, *fpart_bw = nullptr;            // [5][max_batch*nch][h][d], [max_batch*nch][h]
 };
 
@@ -574,7 +575,7 @@ int run_fpm_backward(aideen_ctx *ctx, bool prepare_only) {
     A(&b.fc, Nhd); A(&b.frp, Nhd); A(&b.fdl, Nhd); A(&b.fminner, Nhd); A(&b.fdm, Nhd); A(&b.fgpre, Nhd);
     A(&b.fup, NH32); A(&b.fkw, NH32); A(&b.fdup, NH32);
     A(&b.fA, chunk_rows * h * d); A(&b.fU, chunk_rows * h * d); A(&b.fgin, chunk_rows * h * d);
-    A(&b.fpart, 5 * chunk_rows * h * d); A(&b.fpart_bw, chunk_rows * h);
+    A(&b.fpart, 5 * chunk_rows * h * d); A(&b.fpart_bw, chunk_rows * h); A(&b.fprm, (size_t)5 * h * d);
     CU(e);
   }
   const float *W = b.W;
@@ -587,7 +588,7 @@ int run_fpm_backward(aideen_ctx *ctx, bool prepare_only) {
   a.off_bwrite = L.b_write_mem; a.off_alog = L.alog; a.off_wx = L.wx;
   a.hstar = b.hstar; a.hist = b.hist; a.c = b.fc; a.rpre = b.frp; a.dpre = b.fdl; a.v = b.v;
   a.minner = b.fminner; a.cA = b.fA; a.cU = b.fU; a.gin = b.fgin; a.dm = b.fdm; a.gpre = b.fgpre;
-  a.carry = b.fcarry; a.part = b.fpart; a.part_bw = b.fpart_bw;
+  a.carry = b.fcarry; a.part = b.fpart; a.part_bw = b.fpart_bw; a.slot_prm = b.fprm;
   ctx->prof_phase = AIDEEN_PROF_FPM_BWD;
   struct PhaseReset { aideen_ctx *c; ~PhaseReset() { c->prof_phase = -1; } } phase_reset{ctx};
   if (!ctx->fpm_prepared || prepare_only) {
@@ -609,6 +610,7 @@ int run_fpm_backward(aideen_ctx *ctx, bool prepare_only) {
     return AIDEEN_OK;
   }
   ctx->fpm_prepared = false;
+  KL(launch_fpm_slot_params(a, st));
   KL(launch_fpm_composite(a, st));
   KL(launch_fpm_carry(a, st));
   KL(launch_fpm_chunks(a, st));
@@ -1054,7 +1056,7 @@ void aideen_destroy(aideen_ctx *ctx) {
                   b.nsg, b.da, b.dn, b.dQ, b.dK, b.dV, b.dsig, b.dRc, b.dS, b.lmp, b.Glm, b.Mlm1,
                   b.Mlm2, b.y, b.lrms, b.logits, b.dy, b.ggp, b.loss_rows, b.scal, b.emb, b.stats,
                   b.sigmas, b.stage, b.ws, b.fc, b.frp, b.fdl, b.fminner, b.fdm, b.fgpre, b.fup,
-                  b.fkw, b.fdup, b.fA, b.fU, b.fgin, b.fcarry, b.fpart, b.fpart_bw, b.src,
+                  b.fkw, b.fdup, b.fA, b.fU, b.fgin, b.fcarry, b.fpart, b.fpart_bw, b.fprm, b.src,
                   b.dlog_lo, b.yhi, b.ylo, b.yThi, b.yTlo, b.whi, b.wlo, b.colpart, b.perm, b.ws2, b.ws3, b.rowstats};
   for (void *p : ptrs)
     if (p) cudaFree(p);

@@ -159,13 +159,9 @@ __global__ void __launch_bounds__(32 * CH) fpm_chunk_kernel(FpmBwdArgs a) {
   float *rz = vs + plane;
   float *graw = rz + CH;
   float *prm = graw + CH;   // 5 * d staged slot parameters (CH is even)
-  for (int k = threadIdx.x; k < d; k += blockDim.x) {
-    const float *W = a.W;
-    prm[k] = W[a.off_bret + (size_t)s * d + k];
-    prm[d + k] = W[a.off_bdelta + (size_t)s * d + k];
-    prm[2 * d + k] = W[a.off_wgate + (size_t)s * d + k];
-    prm[3 * d + k] = 1.f / (1.f + expf(W[a.off_alog + (size_t)s * d + k]));
-    prm[4 * d + k] = 0.5f * tanhf(W[a.off_wx + (size_t)k * d + k]);
+  {
+    const float4 *src = reinterpret_cast<const float4 *>(a.slot_prm + (size_t)s * 5 * d);
+    for (int k = threadIdx.x; k < 5 * d / 4; k += blockDim.x) reinterpret_cast<float4 *>(prm)[k] = src[k];
   }
   __syncthreads();
   const int w = threadIdx.x >> 5;
@@ -323,6 +319,22 @@ __global__ void __launch_bounds__(1024) fpm_finalize_kernel(FpmBwdArgs a, float 
 
 }  // namespace
 
+// The slot parameters every chunk CTA stages, once per backward:
+//   [0,d) b_retain  [d,2d) b_delta  [2d,3d) W_write_gate  [3d,4d) sigmoid(-a_log)
+//   [4d,5d) 0.5 tanh(diag W_x)
+__global__ void fpm_slot_params_kernel(FpmBwdArgs a) {
+  const int s = blockIdx.x, d = a.d;
+  const float *W = a.W;
+  float *o = a.slot_prm + (size_t)s * 5 * d;
+  for (int k = threadIdx.x; k < d; k += blockDim.x) {
+    o[k] = W[a.off_bret + (size_t)s * d + k];
+    o[d + k] = W[a.off_bdelta + (size_t)s * d + k];
+    o[2 * d + k] = W[a.off_wgate + (size_t)s * d + k];
+    o[3 * d + k] = 1.f / (1.f + expf(W[a.off_alog + (size_t)s * d + k]));
+    o[4 * d + k] = 0.5f * tanhf(W[a.off_wx + (size_t)k * d + k]);
+  }
+}
+
 cudaError_t launch_fpm_c(const float *hstar, const float *signal, float *c, size_t n, cudaStream_t st) {
   const size_t n4 = n / 4;
   const int blocks = (int)((n4 + 255) / 256 < 148 * 16 ? (n4 + 255) / 256 : 148 * 16);
@@ -361,6 +373,10 @@ static cudaError_t chunk_dispatch(const FpmBwdArgs &a, cudaStream_t st) {
   }
 }
 
+cudaError_t launch_fpm_slot_params(const FpmBwdArgs &a, cudaStream_t st) {
+  fpm_slot_params_kernel<<<a.h, 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
 cudaError_t launch_fpm_composite(const FpmBwdArgs &a, cudaStream_t st) { return chunk_dispatch<false>(a, st); }
 cudaError_t launch_fpm_chunks(const FpmBwdArgs &a, cudaStream_t st) { return chunk_dispatch<true>(a, st); }
 

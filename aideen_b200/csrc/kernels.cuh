@@ -168,10 +168,12 @@ struct FpmBwdArgs {
   float *carry;         // [B][h][d] TBPTT carry, in: dL/dM seed, out: dL/dM before the chunk
   float *part;          // [5][B*nch][h][d] per-chunk partial sums
   float *part_bw;       // [B*nch][h]
+  float *slot_prm;      // [h][5][d] per-slot parameters (launch_fpm_slot_params)
 };
 int fpm_chunk_len(int d);
 size_t fpm_chunk_smem(int d, bool full);
 cudaError_t launch_fpm_c(const float *hstar, const float *signal, float *c, size_t n, cudaStream_t st);
+cudaError_t launch_fpm_slot_params(const FpmBwdArgs &a, cudaStream_t st);
 cudaError_t launch_fpm_composite(const FpmBwdArgs &a, cudaStream_t st);
 cudaError_t launch_fpm_carry(const FpmBwdArgs &a, cudaStream_t st);
 cudaError_t launch_fpm_chunks(const FpmBwdArgs &a, cudaStream_t st);
