@@ -93,7 +93,8 @@ struct aideen_ctx {
   cudaStream_t ast = nullptr;
   cudaEvent_t ev_da = nullptr, ev_dqkv = nullptr, ev_adone = nullptr;
   bool lmg_pending = false;
-  bool fpm_prepared = false;  // the FPM backward's forward-only stage already ran this step
+  bool fpm_prepared = false;
+  int fpm_comp_done = 0;      // FPM chunk composites [0, this) already formed this step  // the FPM backward's forward-only stage already ran this step
   int sm_budget = 0;      // SMs the GEMM / softmax / adjoint launches may use (0: all)
   // optional stage timeline of the pipelined step (AIDEEN_PIPE_TIMELINE=1, stderr)
   std::vector<std::pair<std::string, cudaEvent_t>> tl;
@@ -436,6 +437,7 @@ int run_adjoint(aideen_ctx *ctx, int N, const float *pre_a, const float *pre_b,
 }
 
 int run_fpm_backward(aideen_ctx *ctx, bool prepare_only = false);
+int fpm_args(aideen_ctx *ctx, FpmBwdArgs &a);
 void tl_mark(aideen_ctx *ctx, const char *name, cudaStream_t s);
 
 int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
@@ -557,14 +559,12 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   return AIDEEN_OK;
 }
 
-// FPM memory backward over the last forward's chunk (fpm_bwd.cu); adds the
-// FPM parameters' gradients to G and advances the TBPTT carry.
-int run_fpm_backward(aideen_ctx *ctx, bool prepare_only) {
+// FPM backward arguments over the last forward (allocates the FPM buffers once).
+int fpm_args(aideen_ctx *ctx, FpmBwdArgs &a) {
   const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
-  const int B = ctx->last_run.batch, T = ctx->last_run.seq_len, N = B * T;
+  const int B = ctx->last_run.batch, T = ctx->last_run.seq_len;
   const Layout &L = ctx->P;
   DevBufs &b = ctx->b;
-  cudaStream_t st = ctx->stream;
   const size_t Nhd = ctx->max_tokens * h * d, NH32 = ctx->max_tokens * h * kRank;
   const int CH = fpm_chunk_len(d);
   const size_t nch_max = (ctx->cfg.max_seq_len + CH - 1) / CH;
@@ -579,16 +579,32 @@ int run_fpm_backward(aideen_ctx *ctx, bool prepare_only) {
     CU(e);
   }
   const float *W = b.W;
-  float *G = b.G;
-  const int R = kRank, HR = h * kRank;
-  const long hd = (long)h * d;
-  FpmBwdArgs a{};
+  a = FpmBwdArgs{};
   a.B = B; a.T = T; a.h = h; a.d = d; a.nch = (T + CH - 1) / CH; a.W = W;
   a.off_bdelta = L.b_delta; a.off_bret = L.b_retain; a.off_wgate = L.w_write_gate;
   a.off_bwrite = L.b_write_mem; a.off_alog = L.alog; a.off_wx = L.wx;
   a.hstar = b.hstar; a.hist = b.hist; a.c = b.fc; a.rpre = b.frp; a.dpre = b.fdl; a.v = b.v;
   a.minner = b.fminner; a.cA = b.fA; a.cU = b.fU; a.gin = b.fgin; a.dm = b.fdm; a.gpre = b.fgpre;
   a.carry = b.fcarry; a.part = b.fpart; a.part_bw = b.fpart_bw; a.slot_prm = b.fprm;
+  a.ch0 = 0;
+  a.ch1 = 0;
+  return AIDEEN_OK;
+}
+
+// FPM memory backward over the last forward's chunk (fpm_bwd.cu); adds the
+// FPM parameters' gradients to G and advances the TBPTT carry.
+int run_fpm_backward(aideen_ctx *ctx, bool prepare_only) {
+  const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
+  const int B = ctx->last_run.batch, T = ctx->last_run.seq_len, N = B * T;
+  const Layout &L = ctx->P;
+  DevBufs &b = ctx->b;
+  cudaStream_t st = ctx->stream;
+  FpmBwdArgs a;
+  CHK(fpm_args(ctx, a));
+  const float *W = b.W;
+  float *G = b.G;
+  const int R = kRank, HR = h * kRank;
+  const long hd = (long)h * d;
   ctx->prof_phase = AIDEEN_PROF_FPM_BWD;
   struct PhaseReset { aideen_ctx *c; ~PhaseReset() { c->prof_phase = -1; } } phase_reset{ctx};
   if (!ctx->fpm_prepared || prepare_only) {
@@ -610,17 +626,27 @@ int run_fpm_backward(aideen_ctx *ctx, bool prepare_only) {
     return AIDEEN_OK;
   }
   ctx->fpm_prepared = false;
-  KL(launch_fpm_slot_params(a, st));
+  if (ctx->fpm_comp_done == 0) KL(launch_fpm_slot_params(a, st));
+  // chunk composites not already formed during the pipelined step
+  a.ch0 = ctx->fpm_comp_done;
+  a.ch1 = a.nch;
   KL(launch_fpm_composite(a, st));
+  a.ch0 = 0;
+  a.ch1 = 0;
+  ctx->fpm_comp_done = 0;
+  tl_mark(ctx, "f_comp", st);
   KL(launch_fpm_carry(a, st));
   KL(launch_fpm_chunks(a, st));
+  tl_mark(ctx, "f_chunks", st);
   KL(launch_fpm_finalize(a, G, st));
+  tl_mark(ctx, "f_fin", st);
   // W_retain_down[s][r][k] = sum_n up[n][s][r] g_pre[n][s][k]
   KL(gemm_any(ctx, gemm(R, d, N, h, b.fup, HR, R, true, b.fgpre, hd, d, false, G + L.w_retain_down, d,
                    (long)R * d)));
   // dup[n][s][r] = sum_k g_pre[n][s][k] W_retain_down[s][r][k]
   KL(gemm_any(ctx, gemm(N, R, d, h, b.fgpre, hd, d, false, W + L.w_retain_down, d, (long)R * d, true,
                    b.fdup, HR, R)));
+  tl_mark(ctx, "f_dup", st);
   // W_retain_up[s][j][r] = sum_n c[n][s][j] dup[n][s][r]
   KL(gemm_any(ctx, gemm(d, R, N, h, b.fc, hd, d, true, b.fdup, HR, R, false, G + L.w_retain_up, R,
                    (long)d * R)));
@@ -825,11 +851,31 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
     if (a->anderson_m > 4) { ctx->sm_budget = 0; return set_err(ctx, AIDEEN_E_UNSUPPORTED, "anderson_m > 4"); }
     KL(launch_adjoint(aa, st));
     tl_mark(ctx, ("cons" + std::to_string(j)).c_str(), st);
+    // the FPM backward's chunk composites need only the forward and this
+    // chunk's adjoint: form them on the FPM stream now (not for the last chunk,
+    // whose composites start the backward proper)
+    if (r->fpm && ctx->fst && ctx->fpm_prepared && j + 1 < nch && !ctx->prof) {
+      FpmBwdArgs fa;
+      CHK(fpm_args(ctx, fa));
+      const int CH = fpm_chunk_len(d);
+      if (t0 % CH == 0 && t1 % CH == 0 && t0 / CH == ctx->fpm_comp_done) {
+        CU(cudaEventRecord(ctx->ev_adj, st));
+        CU(cudaStreamWaitEvent(ctx->fst, ctx->ev_adj, 0));
+        if (ctx->fpm_comp_done == 0) KL(launch_fpm_slot_params(fa, ctx->fst));
+        fa.ch0 = t0 / CH;
+        fa.ch1 = t1 / CH;
+        KL(launch_fpm_composite(fa, ctx->fst));
+        ctx->fpm_comp_done = t1 / CH;
+      }
+    }
     if (tail_lm) {
       CU(cudaEventRecord(ctx->ev_adj, st));
       CU(cudaStreamWaitEvent(ctx->lmst, ctx->ev_adj, 0));
       ctx->stream = ctx->lmst;
-      ctx->sm_budget = 0;
+      // leave SMs to the FPM backward and attention-gradient chains that run
+      // beside it (their kernels cannot share an SM with this GEMM's CTAs)
+      // (48 SMs: best of the tried caps at the bench shape; AIDEEN_TAIL_LM_CAP overrides)
+      ctx->sm_budget = getenv("AIDEEN_TAIL_LM_CAP") ? atoi(getenv("AIDEEN_TAIL_LM_CAP")) : nsm - 48;
       float *keep_ws = b.ws;
       b.ws = nullptr;  // no split-K here: the context stream's GEMMs own the workspace meanwhile
       const cudaError_t e = dwlm();

@@ -152,7 +152,7 @@ __device__ __forceinline__ void row_coefs(const FpmBwdArgs &a, const float *prm,
 template <int NV, int CH, bool FULL>
 __global__ void __launch_bounds__(32 * CH) fpm_chunk_kernel(FpmBwdArgs a) {
   extern __shared__ __align__(16) float sm[];
-  const int ch = blockIdx.x, s = blockIdx.y, b = blockIdx.z;
+  const int ch = (FULL ? 0 : a.ch0) + blockIdx.x, s = blockIdx.y, b = blockIdx.z;
   const int d = a.d, h = a.h, T = a.T, nch = a.nch;
   const size_t plane = (size_t)CH * d;
   float *vs = sm + (FULL ? 6 : 1) * plane;   // 0.5 * v of the chunk's tokens
@@ -357,7 +357,11 @@ static cudaError_t chunk_launch(const FpmBwdArgs &a, cudaStream_t st) {
   auto k = fpm_chunk_kernel<NV, CH, FULL>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  k<<<dim3(a.nch, a.h, a.B), 32 * CH, smem, st>>>(a);
+  const int nx = (!FULL && a.ch1 > 0) ? a.ch1 - a.ch0 : a.nch;
+  if (nx <= 0) return cudaSuccess;
+  FpmBwdArgs b = a;
+  if (FULL || a.ch1 <= 0) b.ch0 = 0;
+  k<<<dim3(nx, a.h, a.B), 32 * CH, smem, st>>>(b);
   return cudaGetLastError();
 }
 

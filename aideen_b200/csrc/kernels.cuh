@@ -169,6 +169,7 @@ struct FpmBwdArgs {
   float *part;          // [5][B*nch][h][d] per-chunk partial sums
   float *part_bw;       // [B*nch][h]
   float *slot_prm;      // [h][5][d] per-slot parameters (launch_fpm_slot_params)
+  int ch0, ch1;         // composite: chunk range [ch0, ch1) (ch1 = 0: all chunks)
 };
 int fpm_chunk_len(int d);
 size_t fpm_chunk_smem(int d, bool full);
