@@ -832,15 +832,24 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
                   b.dlog_lo + r0 * Vp, b.wlo));
     KL(launch_rmsnorm_bwd(b.dy + r0 * d, b.pooled + r0 * d, b.lrms + r0, glm, b.dl_dh + r0 * d,
                           b.ggp + r0 * d, R, d, st));
-    // dW_lm[v][j] += sum_{n in chunk} dlogits[n][v] y^T[j][n]; the last chunk's
-    // runs after its adjoint, on its own stream (below)
+    // dW_lm[v][j] = sum_n dlogits[n][v] y^T[j][n], after the last chunk's
+    // adjoint on its own stream (below)
     const bool tail_lm = j == nch - 1 && ctx->lmst && !ctx->prof;
+    // dW_lm is not formed per chunk: one GEMM over every row runs after the last
+    // adjoint, beside the weight gradients (measured ahead of per-chunk GEMMs,
+    // which compete with the solve-capped consumers); AIDEEN_PER_CHUNK_DWLM=1
+    // restores the per-chunk form
+    static const bool defer = getenv("AIDEEN_PER_CHUNK_DWLM") == nullptr;
+    const bool deferred = defer && ctx->lmst && !ctx->prof;
     auto dwlm = [&]() {
-      return gemm_split(ctx, gemm(V, d, R, 1, b.logits + r0 * Vp, Vp, 0, true, b.yThi + r0, N4, 0, true, b.Glm,
-                                  d, 0, 1.f, j > 0 ? 1.f : 0.f),
-                        b.dlog_lo + r0 * Vp, b.yTlo + r0);
+      const long rr0 = deferred ? 0 : r0;
+      const int RR = (int)((deferred ? N : r0 + R) - rr0);
+      const bool first = deferred || j == 0;
+      return gemm_split(ctx, gemm(V, d, RR, 1, b.logits + rr0 * Vp, Vp, 0, true, b.yThi + rr0, N4, 0, true, b.Glm,
+                                  d, 0, 1.f, first ? 0.f : 1.f),
+                        b.dlog_lo + rr0 * Vp, b.yTlo + rr0);
     };
-    if (!tail_lm) KL(dwlm());
+    if (!tail_lm && !deferred) KL(dwlm());
     // adjoint of the chunk's rows
     AdjointArgs aa{};
     aa.N = R; aa.h = h; aa.d = d; aa.iters = a->adj_iters; aa.anderson_m = a->anderson_m;
