@@ -835,21 +835,21 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
     // dW_lm[v][j] = sum_n dlogits[n][v] y^T[j][n], after the last chunk's
     // adjoint on its own stream (below)
     const bool tail_lm = j == nch - 1 && ctx->lmst && !ctx->prof;
-    // dW_lm is not formed per chunk: one GEMM over every row runs after the last
-    // adjoint, beside the weight gradients (measured ahead of per-chunk GEMMs,
-    // which compete with the solve-capped consumers); AIDEEN_PER_CHUNK_DWLM=1
-    // restores the per-chunk form
-    static const bool defer = getenv("AIDEEN_PER_CHUNK_DWLM") == nullptr;
-    const bool deferred = defer && ctx->lmst && !ctx->prof;
+    // dW_lm: the first `early` chunks' rows as each chunk's consumers finish
+    // (they fill the consumers' slack while the solve runs), every later row in
+    // one GEMM after the last adjoint, beside the weight gradients
+    // (AIDEEN_DWLM_EARLY overrides the count; nch - 1 is fully per chunk)
+    static const int early_env = getenv("AIDEEN_DWLM_EARLY") ? atoi(getenv("AIDEEN_DWLM_EARLY")) : 1;
+    const int early = (ctx->lmst && !ctx->prof) ? (early_env < nch - 1 ? early_env : nch - 1) : nch;
     auto dwlm = [&]() {
-      const long rr0 = deferred ? 0 : r0;
-      const int RR = (int)((deferred ? N : r0 + R) - rr0);
-      const bool first = deferred || j == 0;
+      const long rr0 = tail_lm ? (long)chunk_bound_aligned(early, nch, T, B) * B : r0;
+      const int RR = (int)((tail_lm ? N : r0 + R) - rr0);
+      const bool first = rr0 == 0;
       return gemm_split(ctx, gemm(V, d, RR, 1, b.logits + rr0 * Vp, Vp, 0, true, b.yThi + rr0, N4, 0, true, b.Glm,
                                   d, 0, 1.f, first ? 0.f : 1.f),
                         b.dlog_lo + rr0 * Vp, b.yTlo + rr0);
     };
-    if (!tail_lm && !deferred) KL(dwlm());
+    if (!tail_lm && j < early) KL(dwlm());
     // adjoint of the chunk's rows
     AdjointArgs aa{};
     aa.N = R; aa.h = h; aa.d = d; aa.iters = a->adj_iters; aa.anderson_m = a->anderson_m;
