@@ -767,7 +767,8 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
         v2[1] = v2b[1];
       }
       // rms(dep) >= 1e-3 always (the 1e-6 floor), so max(rms, 1e-6) = rms
-      const float err = sqrtf(v2[0] * inv_d + 1e-12f) * irr;
+      const float ex = v2[0] * inv_d + 1e-12f;  // > 0
+      const float err = ex * rsqrtf(ex) * irr;  // sqrt(ex) off the IEEE square-root path
       irr = rsqrtf(v2[1] * inv_d + 1e-6f);
       hq_sq = v2[2];
       hcur = hn;
