@@ -656,7 +656,8 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
           PT(0);
           // Model-A memory read from the first structured state (:1031-1200)
           const float ihq = rsqrtf(fmaxf(hq_sq, 1e-6f));
-          const float sig_norm = sqrtf(fmaxf(sig_sq, 1e-6f));
+          const float sig_c = fmaxf(sig_sq, 1e-6f);
+          const float sig_norm = sig_c * rsqrtf(sig_c);
           // the query lands in vec[0..32), written and read by warp 0 only
           // (q = W_q_mem . h / |h|: the staged h is unscaled, the sum is scaled)
           mv_d_to_32_partials(mat[1], xs, part);
@@ -715,8 +716,8 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
             if (lane < h) wsm[lane] = w;
             if (lane == 0) {
               const float uni = 1.f / (float)(h > 1 ? h : 1);
-              const float conf = fminf(fmaxf((peak - uni) / fmaxf(1e-6f, 1.f - uni), 0.f), 1.f);
-              wsm[16] = fmaxf(sqrtf(conf), a.gate_min);
+              const float conf = fminf(fmaxf(__fdividef(peak - uni, fmaxf(1e-6f, 1.f - uni)), 0.f), 1.f);
+              wsm[16] = fmaxf(conf * rsqrtf(fmaxf(conf, 1e-30f)), a.gate_min);
             }
           }
           __syncthreads();
@@ -739,8 +740,8 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
           const float2 mu = tanh2(mr);
           float v1[1] = {dot2(mu, mu)};
           bsum<NW>(R, v1);
-          const float mu_norm = sqrtf(fmaxf(v1[0], 1e-6f));
-          const float coef = sig_norm * fmaxf(a.alpha_m, 0.001f) / fmaxf(mu_norm, 1e-6f) * wsm[16];
+          // |mu| >= 1e-3 (the 1e-6 floor on |mu|^2), so 1 / max(|mu|, 1e-6) = rsqrt(|mu|^2)
+          const float coef = sig_norm * fmaxf(a.alpha_m, 0.001f) * rsqrtf(fmaxf(v1[0], 1e-6f)) * wsm[16];
           ctx = coef * mu;
           PT(2);
         }
@@ -831,13 +832,15 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       const float2 hu = rsqrtf(fmaxf(v3[2] * inv_d, 1e-6f)) * hcur;
       const float raw_z = __fdividef(1.f, 1.f + expf(-(v3[3] * rsqrtf((float)d) + wsm[40] - 1.5f)));
       const float z = fminf(fmaxf(raw_z, 0.f), 1.f);
-      const float prev_norm = sqrtf(fmaxf(v3[0], 1e-6f));
-      const float diff_norm = sqrtf(fmaxf(v3[1], 1e-6f));
+      const float pq = fmaxf(v3[0], 1e-6f), dq = fmaxf(v3[1], 1e-6f);
+      const float prev_norm = pq * rsqrtf(pq);
+      const float diff_norm = dq * rsqrtf(dq);
       const float novelty = __fdividef(diff_norm, diff_norm + prev_norm + 1e-6f);
       const float2 rrv = sigmoid2(ld2(wprm + 2 * d + j0) + dv);
       const float2 retain = f2(1.f) - novelty * (f2(1.f) - rrv);
       const float2 write = (z * 0.1f) * prop;
-      const float2 x = sqrtf(fmaxf(z, 1e-6f)) * hu + wxv * hu + write;
+      const float zq = fmaxf(z, 1e-6f);
+      const float2 x = (zq * rsqrtf(zq)) * hu + wxv * hu + write;
       const float2 base = adv * m + (f2(1.f) - adv) * x;
       const float2 mn = retain * m + (f2(1.f) - retain) * base;
       st2(mbuf + (cur ^ 1) * d + j0, mn);
