@@ -454,7 +454,7 @@ __device__ __forceinline__ void push_to(const void *src, const void *dst_local, 
 
 // (fast reciprocal: ~2 ulp, on the Picard write's dependency chain)
 __device__ __forceinline__ float2 sigmoid2(float2 x) {
-  return make_float2(__fdividef(1.f, 1.f + expf(-x.x)), __fdividef(1.f, 1.f + expf(-x.y)));
+  return make_float2(__fdividef(1.f, 1.f + __expf(-x.x)), __fdividef(1.f, 1.f + __expf(-x.y)));
 }
 
 // Persistent token-serial solve.  blockDim = d/2 (one float2 per thread, see
@@ -709,7 +709,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
             if (lane >= h) sc = -1e30f;
             if (lane < h) sc = (sc + wsm[17 + lane]) * rsqrtf((float)kRank) / fmaxf(a.tau, 1e-3f);
             const float mx = warp_max(sc);
-            const float ex = lane < h ? expf(sc - mx) : 0.f;
+            const float ex = lane < h ? __expf(sc - mx) : 0.f;
             const float se = fmaxf(warp_sum(ex), 1e-12f);
             const float w = __fdividef(ex, se);
             const float peak = warp_max(lane < h ? w : 0.f);
@@ -830,7 +830,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       dep0_sq = v3[4];
       sig_sq = v3[5];
       const float2 hu = rsqrtf(fmaxf(v3[2] * inv_d, 1e-6f)) * hcur;
-      const float raw_z = __fdividef(1.f, 1.f + expf(-(v3[3] * rsqrtf((float)d) + wsm[40] - 1.5f)));
+      const float raw_z = __fdividef(1.f, 1.f + __expf(-(v3[3] * rsqrtf((float)d) + wsm[40] - 1.5f)));
       const float z = fminf(fmaxf(raw_z, 0.f), 1.f);
       const float pq = fmaxf(v3[0], 1e-6f), dq = fmaxf(v3[1], 1e-6f);
       const float prev_norm = pq * rsqrtf(pq);
