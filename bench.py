@@ -103,22 +103,22 @@ def make_tokens(rank: int, B: int):
     return np.ascontiguousarray(ids[:, :-1]), np.ascontiguousarray(ids[:, 1:])
 
 
-def cpu_baseline(sample_tokens: int = 16):
-    """Oracle (CPU restatement of the reference math) on a bounded sample of the
-    same workload: one sequence of `sample_tokens` tokens at the full model size."""
+def cpu_baseline(n_seq: int = B_PER_GPU):
+    """Oracle (CPU restatement of the reference math) on `n_seq` sequences of the
+    bench workload at the full model size (n_seq = B_PER_GPU: one GPU's whole step)."""
     from oracle import deq_oracle as O
     from aideen_b200.weights import init_all_weights, init_embedding, init_lm_head
     W = init_all_weights(D, H, seed=0)
     lm = init_lm_head(D, VOCAB)
     emb = init_embedding(D, VOCAB)
-    tok, tg = make_tokens(0, 1)
-    tok, tg = tok[:, :sample_tokens], tg[:, :sample_tokens]
+    tok, tg = make_tokens(0, B_PER_GPU)
+    tok, tg = tok[:n_seq], tg[:n_seq]
     cfg = O.Cfg(d=D, h=H, fpm=True, max_iters=MAX_ITERS, adj_iters=ADJ_ITERS, anderson_m=ANDERSON_M)
     t0 = time.perf_counter()
     O.train_step(emb[tok], tg, W, lm, cfg)
     dt = time.perf_counter() - t0
-    return {"value": sample_tokens / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"1 sequence x {sample_tokens} tokens of the d512/h8/vocab50257 step "
+    return {"value": n_seq * T / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n_seq} sequence(s) x {T} tokens of the d512/h8/vocab50257 step "
                       f"(numpy float64 oracle, BLAS threads = host cores), {dt:.1f} s"}
 
 
@@ -169,7 +169,7 @@ def run_reference(args, rank, world):
         return
     times = []
     for i in range(args.warmup + args.steps):
-        cb = cpu_baseline(16)
+        cb = cpu_baseline(2)
         if i >= args.warmup:
             times.append(cb["value"])
     v = float(np.mean(times))
@@ -351,7 +351,7 @@ def main():
                 "roofline_adjoint_c4": c4,
                 "clocks": clk.summary()}
         if not args.no_cpu_baseline and world == 1:
-            line["cpu_baseline"] = cpu_baseline(128)
+            line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
     be.close()
     if world > 1:
