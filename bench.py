@@ -64,10 +64,16 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi takes longer to start than a short timed region lasts:
+            # wait for its first sample, then keep only the samples taken inside
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.01)
+            self.n0 = len(self.rows)
         except OSError:
             self.proc = None
         return self
@@ -85,6 +91,10 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        inside = self.rows[getattr(self, "n0", 0):]
+        # a region shorter than the sampling period may hold no sample: then the
+        # sample just before it (same process, GPU already under load) stands in
+        self.rows = inside if inside else self.rows[-1:]
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
