@@ -93,6 +93,7 @@ struct aideen_ctx {
   cudaStream_t ast = nullptr;
   cudaEvent_t ev_da = nullptr, ev_dqkv = nullptr, ev_adone = nullptr;
   bool lmg_pending = false;
+  bool lm_reduced = false;  // this step's LM-head gradients were already summed over ranks
   bool fpm_prepared = false;
   int fpm_comp_done = 0;      // FPM chunk composites [0, this) already formed this step  // the FPM backward's forward-only stage already ran this step
   int sm_budget = 0;      // SMs the GEMM / softmax / adjoint launches may use (0: all)
@@ -902,6 +903,15 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   KL(launch_colsum(b.colpart, colpart_rows, V, Vp, b.Glm + ctx->lm_b, V, 0, false, lst));
   KL(launch_colsum(b.ggp, N, d, d, b.Glm + ctx->lm_g, d, 0, false, lst));
   if (tail_lm) {
+    // data parallel: the LM-head gradients are final here, so their sum over
+    // ranks runs on the same stream, beside the weight gradients (every rank
+    // issues it before the core-gradient allreduce, so the order matches)
+    if (a->update.allreduce && ctx->comm && ctx->nranks > 1 && ctx->lm_ready) {
+      const ncclResult_t nr =
+          ncclAllReduce(b.Glm, b.Glm, ctx->lm_len, ncclFloat, ncclSum, ctx->comm, ctx->lmst);
+      if (nr != ncclSuccess) return set_err(ctx, AIDEEN_E_NCCL, std::string("ncclAllReduce: ") + ncclGetErrorString(nr));
+      ctx->lm_reduced = true;
+    }
     CU(cudaEventRecord(ctx->ev_lmg, ctx->lmst));
     ctx->lmg_pending = true;
   }
@@ -913,8 +923,9 @@ int run_allreduce(aideen_ctx *ctx, int timeout_ms) {
   ncclResult_t r = ncclGroupStart();
   if (r == ncclSuccess)
     r = ncclAllReduce(ctx->b.G, ctx->b.G, ctx->W_len, ncclFloat, ncclSum, ctx->comm, ctx->stream);
-  if (r == ncclSuccess && ctx->lm_ready)
+  if (r == ncclSuccess && ctx->lm_ready && !ctx->lm_reduced)
     r = ncclAllReduce(ctx->b.Glm, ctx->b.Glm, ctx->lm_len, ncclFloat, ncclSum, ctx->comm, ctx->stream);
+  ctx->lm_reduced = false;
   ncclResult_t r2 = ncclGroupEnd();
   if (r != ncclSuccess || r2 != ncclSuccess)
     return set_err(ctx, AIDEEN_E_NCCL, std::string("ncclAllReduce: ") +
