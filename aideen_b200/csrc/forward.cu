@@ -548,6 +548,11 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
     mv_d_to_32<1, false>(mat[0], nullptr, m + hsv * tanh2(m) + hbv, j0, xs, keybuf, part);
   }
   const float band = fmaxf(a.eps, 0.15f * 0.2f);
+  // loop-invariant factors of the memory read: score scale 1 / (sqrt(32) tau),
+  // the uniform weight 1 / h and 1 / max(1 - 1/h, 1e-6) of the confidence gate
+  const float score_scale = rsqrtf((float)kRank) / fmaxf(a.tau, 1e-3f);
+  const float uni = 1.f / (float)(h > 1 ? h : 1);
+  const float inv_conf = 1.f / fmaxf(1e-6f, 1.f - uni);
   // loop-invariant write parameters of this slot, staged in shared memory so
   // the token loop issues no global parameter loads: [0,d) b_delta,
   // [d,2d) W_write_gate, [2d,3d) b_retain (b_write_mem sits in wsm[40])
@@ -707,7 +712,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
             const float part_dot = p[0] + __shfl_xor_sync(0xffffffffu, p[0], 1);
             float sc = __shfl_sync(0xffffffffu, part_dot, (lane & 15) << 1);
             if (lane >= h) sc = -1e30f;
-            if (lane < h) sc = (sc + wsm[17 + lane]) * rsqrtf((float)kRank) / fmaxf(a.tau, 1e-3f);
+            if (lane < h) sc = (sc + wsm[17 + lane]) * score_scale;
             const float mx = warp_max(sc);
             const float ex = lane < h ? __expf(sc - mx) : 0.f;
             const float se = fmaxf(warp_sum(ex), 1e-12f);
@@ -715,8 +720,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
             const float peak = warp_max(lane < h ? w : 0.f);
             if (lane < h) wsm[lane] = w;
             if (lane == 0) {
-              const float uni = 1.f / (float)(h > 1 ? h : 1);
-              const float conf = fminf(fmaxf(__fdividef(peak - uni, fmaxf(1e-6f, 1.f - uni)), 0.f), 1.f);
+              const float conf = fminf(fmaxf((peak - uni) * inv_conf, 0.f), 1.f);
               wsm[16] = fmaxf(conf * rsqrtf(fmaxf(conf, 1e-30f)), a.gate_min);
             }
           }
