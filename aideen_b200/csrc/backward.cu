@@ -22,9 +22,16 @@ __device__ __forceinline__ uint32_t smem_addr(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+constexpr uint32_t kSpinLimit = 1u << 26;
+
+// Set when a bounded wait of the adjoint ran out (the rows of that CTA's
+// remaining tokens were not written); read and cleared by adjoint_error_async.
+__device__ unsigned int g_adjoint_error;
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
+                                                  uint32_t limit = kSpinLimit) {
   const uint32_t addr = smem_addr(bar);
-  for (uint32_t i = 0; i < (1u << 26); ++i) {
+  for (uint32_t i = 0; i < limit; ++i) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -143,7 +150,6 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
   };
   if (threadIdx.x == 0 && (int)blockIdx.x < a.N) issue(blockIdx.x, 0);
   int it = 0;
-  bool pending = (int)blockIdx.x < a.N;
   for (int n = blockIdx.x; n < a.N; n += gridDim.x, ++it) {
     const int b = it & 1;
     const int nn = n + (int)gridDim.x;
@@ -151,9 +157,17 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       issue(nn, b ^ 1);
     }
-    const bool ok = mbar_wait_bounded(&bar[b], (it >> 1) & 1);
-    if (!__syncthreads_and(ok)) break;
-    pending = nn < a.N;
+    const bool ok = mbar_wait_bounded(&bar[b], (it >> 1) & 1, a.spin_limit);
+    if (!__syncthreads_and(ok)) {
+      // Give up on this CTA's remaining tokens: record the error, then let the
+      // copies already issued into both stages land (bounded) before exiting.
+      if (threadIdx.x == 0) {
+        atomicExch(&g_adjoint_error, 1u);
+        mbar_wait_bounded(&bar[b], (it >> 1) & 1);
+        if (nn < a.N) mbar_wait_bounded(&bar[b ^ 1], ((it + 1) >> 1) & 1);
+      }
+      return;
+    }
     const float *sa = stage0 + b * stage_f;
     float *nsacc = stage0 + b * stage_f;
     const float *sb = sa + hd;
@@ -308,8 +322,6 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
       __syncthreads();  // nsacc (this stage) is read before thread 0 refills it
     }
   }
-  // a copy issued for a token this CTA did not reach (timeout path) must land first
-  if (threadIdx.x == 0 && pending && it < 1 << 30) mbar_wait_bounded(&bar[(it + 1) & 1], ((it + 1) >> 1) & 1);
 }
 
 template <int F, int MA, int MAXT, int MINB, bool HS = false>
@@ -350,8 +362,13 @@ static cudaError_t adjoint_dispatch_m(const AdjointArgs &a, cudaStream_t st) {
   }
 }
 
-cudaError_t launch_adjoint(const AdjointArgs &a, cudaStream_t st) {
-  if (a.N <= 0) return cudaSuccess;
+cudaError_t launch_adjoint(const AdjointArgs &a0, cudaStream_t st) {
+  if (a0.N <= 0) return cudaSuccess;
+  AdjointArgs a = a0;
+  // AIDEEN_ADJ_SPIN_LIMIT shortens the stage waits (0: every first wait gives
+  // up at once), so tests can drive the timeout path without a fault
+  a.spin_limit = kSpinLimit;
+  if (const char *e = getenv("AIDEEN_ADJ_SPIN_LIMIT")) a.spin_limit = (uint32_t)strtoul(e, nullptr, 10);
   switch (a.d) {
     case 128: return adjoint_dispatch_m<1>(a, st);
     case 256: return adjoint_dispatch_m<2>(a, st);
@@ -359,6 +376,21 @@ cudaError_t launch_adjoint(const AdjointArgs &a, cudaStream_t st) {
     case 1024: return adjoint_dispatch_m<8>(a, st);
     default: return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t adjoint_error_async(unsigned int *host_flag, cudaStream_t st) {
+  cudaError_t e = cudaMemcpyFromSymbolAsync(host_flag, g_adjoint_error, sizeof(unsigned int), 0,
+                                            cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) return e;
+  static const unsigned int zero = 0;
+  return cudaMemcpyToSymbolAsync(g_adjoint_error, &zero, sizeof(unsigned int), 0, cudaMemcpyHostToDevice, st);
+}
+
+size_t adjoint_smem_bytes(int h, int d, bool has_b, bool has_rs, bool has_tok, int anderson_m) {
+  const size_t hd = (size_t)h * d;
+  const size_t stage_f = hd * (1 + has_b + has_rs) + (has_tok ? (size_t)d : 0);
+  const bool hs = anderson_m == 4 && h <= 8 && 4 * hd <= 16384 && !getenv("AIDEEN_ADJ_REG_HIST");
+  return 128 + 192 * 4 + 2 * stage_f * 4 + (hs ? 4 * hd * 4 : 0);
 }
 
 __global__ void source_grad_kernel(const float *__restrict__ gpre, float *__restrict__ out, int h,

@@ -94,8 +94,8 @@ struct aideen_ctx {
   cudaEvent_t ev_da = nullptr, ev_dqkv = nullptr, ev_adone = nullptr;
   bool lmg_pending = false;
   bool lm_reduced = false;  // this step's LM-head gradients were already summed over ranks
-  bool fpm_prepared = false;
-  int fpm_comp_done = 0;      // FPM chunk composites [0, this) already formed this step  // the FPM backward's forward-only stage already ran this step
+  bool fpm_prepared = false;  // the FPM backward's forward-only stage already ran this step
+  int fpm_comp_done = 0;  // FPM chunk composites [0, this) already formed this step
   int sm_budget = 0;      // SMs the GEMM / softmax / adjoint launches may use (0: all)
   // optional stage timeline of the pipelined step (AIDEEN_PIPE_TIMELINE=1, stderr)
   std::vector<std::pair<std::string, cudaEvent_t>> tl;
@@ -104,9 +104,9 @@ struct aideen_ctx {
   std::string err;
   unsigned long long launches = 0;
   size_t W_len = 0, lm_len = 0, max_tokens = 0;
-  size_t lm_b = 0, lm_g = 0;
-  long Vp = 0;
-  size_t ws_floats = 0;                 // logits row stride (vocab rounded up to 4 floats)   // offsets of b_lm and g_lm in the padded LM block
+  size_t lm_b = 0, lm_g = 0;  // offsets of b_lm and g_lm in the padded LM block
+  long Vp = 0;            // logits row stride (vocab rounded up to 4 floats)
+  size_t ws_floats = 0;   // capacity of each split-K workspace
   float signal_scale = 1.f;
   bool signal_zero = false;
   aideen_run last_run{};
@@ -137,6 +137,21 @@ namespace {
 int set_err(aideen_ctx *c, int code, const std::string &msg) {
   if (c) c->err = msg;
   return code;
+}
+
+// Wait for the context stream, then report a bounded device-side wait that ran
+// out since the last check (adjoint stage loads, Picard memory-row exchange).
+// The flags are per device, so a context also sees another context's timeout
+// on the same device.
+int sync_and_check(aideen_ctx *ctx) {
+  unsigned int adj = 0, pic = 0;
+  cudaError_t e = adjoint_error_async(&adj, ctx->stream);
+  if (e == cudaSuccess) e = picard_error_async(&pic, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return set_err(ctx, AIDEEN_E_CUDA, std::string("sync: ") + cudaGetErrorString(e));
+  if (adj) return set_err(ctx, AIDEEN_E_TIMEOUT, "adjoint: a bounded stage wait ran out (its outputs are invalid)");
+  if (pic) return set_err(ctx, AIDEEN_E_TIMEOUT, "Picard memory-row exchange: a bounded wait ran out");
+  return AIDEEN_OK;
 }
 
 // Make the context stream wait for a deferred LM-head update on the side stream.
@@ -1193,8 +1208,7 @@ int aideen_join(aideen_ctx *ctx) {
 int aideen_sync(aideen_ctx *ctx) {
   if (!ctx) return AIDEEN_E_INVALID;
   CU(join_side(ctx));
-  CU(cudaStreamSynchronize(ctx->stream));
-  return AIDEEN_OK;
+  return sync_and_check(ctx);
 }
 
 // Packed reference layout <-> padded device layout, one copy per tensor.
@@ -1395,7 +1409,7 @@ int aideen_source_grad(aideen_ctx *ctx, float *out, int where) {
   }
   if (where != AIDEEN_DEVICE) {
     CU(cudaMemcpyAsync(out, res, (size_t)N * d * 4, cudaMemcpyDeviceToHost, ctx->stream));
-    CU(cudaStreamSynchronize(ctx->stream));
+    CHK(sync_and_check(ctx));
   } else if (!perm) {
     CU(cudaMemcpyAsync(out, res, (size_t)N * d * 4, cudaMemcpyDeviceToDevice, ctx->stream));
   }
@@ -1432,6 +1446,9 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
   if (!ctx->emb_ready || !ctx->lm_ready)
     return set_err(ctx, AIDEEN_E_INVALID, "train step needs the embedding and the LM head");
   const int N = a->run.batch * a->run.seq_len;
+  // a step that failed after summing its LM-head gradients must not make this
+  // step skip the sum
+  ctx->lm_reduced = false;
   CHK(copy_in_rows(ctx, ctx->b.tokens, tokens, a->run.batch, a->run.seq_len, 1, 1, where));
   CHK(copy_in_rows(ctx, ctx->b.targets, targets, a->run.batch, a->run.seq_len, 1, 1, where));
   KL(launch_embed(ctx->b.tokens, ctx->b.emb, ctx->b.S_in, N, ctx->cfg.d_model, ctx->cfg.vocab, ctx->stream));
@@ -1458,7 +1475,7 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
                        0.50f, 0.50f, ctx->b.sigmas, ctx->stream));
   if (loss_out) {
     CU(cudaMemcpyAsync(loss_out, ctx->b.scal + 1, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-    CU(cudaStreamSynchronize(ctx->stream));
+    CHK(sync_and_check(ctx));
   }
   return AIDEEN_OK;
 }
@@ -1530,8 +1547,7 @@ int aideen_read(aideen_ctx *ctx, int which, void *dst, size_t n) {
     p = ctx->b.perm;
   }
   CU(cudaMemcpyAsync(dst, p, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
-  CU(cudaStreamSynchronize(ctx->stream));
-  return AIDEEN_OK;
+  return sync_and_check(ctx);
 }
 
 void *aideen_device_ptr(aideen_ctx *ctx, int which) {

@@ -80,7 +80,13 @@ struct AdjointArgs {
   int max_ctas;                // SMs to use (0: every SM), at full occupancy each
   float *gpre;                 // [N][h][d]
   float *nsg;                  // [N][d] per-token NormScale-gradient partials or null
+  uint32_t spin_limit;         // bound of each stage wait (set by launch_adjoint)
 };
+// Reads and clears the adjoint's timeout flag (stream-ordered copy into host_flag).
+cudaError_t adjoint_error_async(unsigned int *host_flag, cudaStream_t st);
+// Dynamic shared memory of one adjoint CTA for these inputs (h*d floats per
+// staged tensor, double-buffered; plus the Anderson ring where it is used).
+size_t adjoint_smem_bytes(int h, int d, bool has_b, bool has_rs, bool has_tok, int anderson_m);
 
 struct AttnBwdArgs {
   int h, d;

@@ -1,14 +1,16 @@
 // Allocation-free variant of the fused clean adjoint.
 //
-// Some callers cannot allocate device memory: code running while a CUDA graph
-// is being captured by someone else's framework, allocators that forbid
-// cudaMalloc after start-up, or embedders that hand over pre-sized buffers and
-// own every other byte.  aideen_adjoint_noalloc serves them: the caller passes
-// every input and output as a device pointer, no context is created, and the
-// only extra memory the computation needs (per-token partial sums of the
-// NormScale gradient) lives in the fixed array below.
+// Some callers cannot allocate device memory: allocators that forbid
+// cudaMalloc once start-up is over, embedders that hand over pre-sized
+// buffers and own every other byte of the device, or host code that must not
+// take the allocator's lock on its latency path.  aideen_adjoint_noalloc
+// serves them: the caller passes every input and output as a device pointer,
+// no context is created, and the only extra memory the computation needs
+// (per-token partial sums of the NormScale gradient) lives in the fixed array
+// below.
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <mutex>
 
 #include "../../include/aideen_b200.h"
@@ -58,6 +60,24 @@ extern "C" int aideen_adjoint_noalloc(const float *hstar, const float *branch, c
   if (h_slots < 1 || h_slots > 16 || n_tokens == 0 || anderson_m > 4) return AIDEEN_E_INVALID;
   if (ns_grad_out && (size_t)n_tokens * d_model > kNoAllocScratchFloats)
     return AIDEEN_E_INVALID;  // beyond the fixed scratch: split the tokens over several calls
+  // The kernel stages its inputs with 16-byte bulk copies and float4 accesses:
+  // a misaligned pointer (e.g. a view at an odd element offset) is refused
+  // here instead of faulting on the device.
+  const void *ptrs[] = {hstar, branch, dl_dh, rhs_slot, norm_scale, v_out, gpre_out, ns_grad_out};
+  for (const void *p : ptrs)
+    if (reinterpret_cast<uintptr_t>(p) & 15) return AIDEEN_E_INVALID;
+  // One CTA double-buffers every staged input of a token (h_slots * d_model
+  // floats each for hstar, branch and rhs_slot): shapes whose two stages exceed
+  // the device's shared memory per block are refused.
+  {
+    int dev = 0, optin = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+      return AIDEEN_E_CUDA;
+    if (adjoint_smem_bytes((int)h_slots, (int)d_model, true, rhs_slot != nullptr, dl_dh != nullptr,
+                           (int)anderson_m) > (size_t)optin)
+      return AIDEEN_E_INVALID;
+  }
   float *scratch = nullptr;
   if (ns_grad_out) {
     const int rc = scratch_for_current_device(&scratch);
@@ -77,5 +97,14 @@ extern "C" int aideen_adjoint_noalloc(const float *hstar, const float *branch, c
       launch_colsum(scratch, (int)n_tokens, (int)d_model, d_model, ns_grad_out, (int)d_model, 0,
                     false, st) != cudaSuccess)
     return AIDEEN_E_CUDA;
-  return AIDEEN_OK;
+  // Wait for the work and report a bounded stage wait of the kernel that ran
+  // out.  A stream that is being captured cannot be waited on; its check is
+  // left to the first later call that can wait.
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) return AIDEEN_E_CUDA;
+  if (cap != cudaStreamCaptureStatusNone) return AIDEEN_OK;
+  unsigned int timed_out = 0;
+  if (adjoint_error_async(&timed_out, st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess)
+    return AIDEEN_E_CUDA;
+  return timed_out ? AIDEEN_E_TIMEOUT : AIDEEN_OK;
 }

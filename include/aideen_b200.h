@@ -232,21 +232,29 @@ int aideen_read(aideen_ctx *ctx, int which, void *dst, size_t n_elems);
 void *aideen_device_ptr(aideen_ctx *ctx, int which);
 
 /* ---- allocation-free adjoint (no counterpart in the reference) -------------
- * For callers that cannot allocate device memory (inside someone else's stream
- * capture, under allocators that forbid cudaMalloc after start-up, or in
- * embedders that own every buffer): the same fused clean adjoint as
- * aideen_adjoint_on, with no context and no allocation.  All pointers are
- * device pointers on the current device, 16-byte aligned; layouts as
+ * For callers that cannot allocate device memory (allocators that forbid
+ * cudaMalloc once start-up is over, embedders that own every byte of the
+ * device, host code that must not take the allocator's lock on its latency
+ * path): the same fused clean adjoint as aideen_adjoint_on, with no context
+ * and no allocation.  All pointers are device pointers on the current device
+ * and must be 16-byte aligned (AIDEEN_E_INVALID otherwise); layouts as
  * aideen_adjoint_on (hstar, branch, rhs_slot [N][h][d]; dl_dh [N][d] or NULL;
- * norm_scale [d]; v_out [h][N][d]; gpre_out [N][h][d]).  ns_grad_out (nullable,
- * [d]) receives sum over tokens and slots of beta*v*pre/rms(pre), the NormScale
- * gradient.  Its per-token partials live in a fixed device array of 2^22 floats
- * (16 MiB) that every GPU loading the library holds until exit, so
- * n_tokens * d_model must be <= 4194304 when ns_grad_out is given
- * (AIDEEN_E_INVALID otherwise).  The first call on a device looks up that
- * array's address; make that first call before any stream capture.  All calls
- * share the array: calls that overlap on the GPU (different streams or
- * devices' contexts sharing a device) race.  Nothing in it needs zeroing. */
+ * norm_scale [d]; v_out [h][N][d]; gpre_out [N][h][d]).  One CTA
+ * double-buffers the staged inputs of a token in shared memory, so
+ * 8 * h_slots * d_model * (2 + (rhs_slot != NULL)) bytes must fit in one
+ * block's shared memory (227 KB on B200: h_slots * d_model <= 9600 with
+ * rhs_slot, <= 14400 without, less with the anderson_m = 4 ring); larger
+ * shapes return AIDEEN_E_INVALID.
+ * ns_grad_out (nullable, [d]) receives sum over tokens and slots of
+ * beta*v*pre/rms(pre), the NormScale gradient.  Its per-token partials live in
+ * a fixed device array of 2^22 floats (16 MiB) that every GPU loading the
+ * library holds until exit, so n_tokens * d_model must be <= 4194304 when
+ * ns_grad_out is given (AIDEEN_E_INVALID otherwise).  The first call on a
+ * device looks up that array's address; make that first call before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU
+ * (different streams, or several threads on one device) race.  Nothing in it
+ * needs zeroing.  The call waits for its work on `stream` and returns
+ * AIDEEN_E_TIMEOUT if a bounded wait of the kernel ran out (outputs invalid). */
 int aideen_adjoint_noalloc(const float *hstar, const float *branch, const float *dl_dh,
                            const float *rhs_slot, const float *norm_scale, uint32_t n_tokens,
                            uint32_t h_slots, uint32_t d_model, uint32_t iters, float damping,

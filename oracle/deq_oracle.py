@@ -150,7 +150,8 @@ class Cfg:
     fpm_tau: float = 0.5
     fpm_read_gate_min: float = 0.0
     adj_iters: int = 12
-    anderson_m: int = 0
+    anderson_m: int = 0            # adjoint Anderson depth (0 = off)
+    fwd_anderson_m: int = 0        # forward Anderson depth (0 = plain Picard)
 
 
 def rms(x, axis=-1, eps=1e-6):
@@ -302,6 +303,7 @@ def forward(S_in, W, cfg: Cfg, mstate=None) -> ForwardOut:
     hist = np.zeros((B, T, h, d))
     ctx_all = np.zeros((B, T, h, d))
     hcur = None
+    am = cfg.fwd_anderson_m
     for t in range(T):
         sig = signal[:, t]
         if t == 0:
@@ -311,6 +313,7 @@ def forward(S_in, W, cfg: Cfg, mstate=None) -> ForwardOut:
         active = np.ones((B, h), bool)
         prev = np.ones((B, h))
         it_count = np.zeros((B, h), np.int64)
+        h1 = h2 = h3 = None    # Picard outputs 1, 2, 3 iterations ago (Anderson ring)
         for it in range(cfg.max_iters):
             if not active.any():
                 break
@@ -325,7 +328,25 @@ def forward(S_in, W, cfg: Cfg, mstate=None) -> ForwardOut:
             dh = hn - hcur
             err = np.sqrt(np.mean(dh * dh, -1) + 1e-12) / np.maximum(r, 1e-6)
             conv = _converged(err, prev, it, cfg.eps)
-            hcur = np.where(active[..., None], hn, hcur)
+            hnext = hn
+            if am >= 3 and it >= 2:
+                # type-II Anderson mixing of the slot's iterate, the adjoint's
+                # mixing rule (staged_adjoint_picard_clean.wgsl:1022-1135) applied
+                # per (sequence, slot) solve: each slot's fixed-point problem is
+                # independent once the token's iteration-0 inputs are fixed
+                n_res = min(it, am - 1)
+                D = [hn - h1, h1 - h2] + ([h2 - h3] if n_res == 3 else [])
+                G = np.zeros((B, h, 3, 3))
+                for i in range(n_res):
+                    for j in range(i, n_res):
+                        G[..., i, j] = G[..., j, i] = (D[i] * D[j]).sum(-1)
+                beta = _anderson_coefs(G, n_res)
+                mixed = beta[..., 0, None] * hn + beta[..., 1, None] * h1
+                if n_res == 3:
+                    mixed = mixed + beta[..., 2, None] * h2
+                hnext = np.where(conv[..., None], hn, mixed)
+            h3, h2, h1 = h2, h1, hn
+            hcur = np.where(active[..., None], hnext, hcur)
             prev = np.where(active, err, prev)
             it_count = it_count + active
             active = active & ~conv
@@ -425,7 +446,46 @@ def adjoint(hstar, branch, rhs_tok, NS, cfg: Cfg, rhs_slot=None):
     return v, norm_grad(v), pre, r
 
 
+def _anderson_coefs(G, n_res):
+    """Mixing weights from the Gram matrix of pseudo-residuals G [..., 3, 3]:
+    Tikhonov term 1e-4*trace, Cramer solve with a floored determinant, clamp
+    to [-2, 3], renormalise to sum 1 with a most-recent fallback
+    (`staged_adjoint_picard_clean.wgsl:1075-1124`).  Returns [..., 3]."""
+    beta = np.zeros(G.shape[:-2] + (3,))
+    if n_res == 2:
+        g00, g01, g10, g11 = G[..., 0, 0], G[..., 0, 1], G[..., 1, 0], G[..., 1, 1]
+        reg = np.maximum(1e-8, 1e-4 * (np.abs(g00) + np.abs(g11)))
+        g00 = g00 + reg
+        g11 = g11 + reg
+        det = g00 * g11 - g01 * g10
+        sdet = np.where(det < 0, np.minimum(det, -1e-10), np.maximum(det, 1e-10))
+        beta[..., 0] = (g11 - g01) / sdet
+        beta[..., 1] = (g00 - g10) / sdet
+    else:
+        g = G.copy()
+        reg = np.maximum(1e-8, 1e-4 * (np.abs(g[..., 0, 0]) + np.abs(g[..., 1, 1]) + np.abs(g[..., 2, 2])))
+        for i in range(3):
+            g[..., i, i] += reg
+        g00, g01, g02 = g[..., 0, 0], g[..., 0, 1], g[..., 0, 2]
+        g10, g11, g12 = g[..., 1, 0], g[..., 1, 1], g[..., 1, 2]
+        g20, g21, g22 = g[..., 2, 0], g[..., 2, 1], g[..., 2, 2]
+        det = (g00 * (g11 * g22 - g12 * g21) - g01 * (g10 * g22 - g12 * g20)
+               + g02 * (g10 * g21 - g11 * g20))
+        sdet = np.where(det < 0, np.minimum(det, -1e-8), np.maximum(det, 1e-8))
+        beta[..., 0] = ((g11 * g22 - g12 * g21) - g01 * (g22 - g12) + g02 * (g21 - g11)) / sdet
+        beta[..., 1] = (g00 * (g22 - g12) - (g10 * g22 - g12 * g20) + g02 * (g10 - g20)) / sdet
+        beta[..., 2] = (g00 * (g11 - g21) - g01 * (g10 - g20) + (g10 * g21 - g11 * g20)) / sdet
+    beta[..., :n_res] = np.clip(beta[..., :n_res], -2.0, 3.0)
+    beta[..., n_res:] = 0.0
+    ssum = beta.sum(-1)
+    small = np.abs(ssum) < 1e-6
+    beta = np.where(small[..., None], 0.0, beta / np.where(small, 1.0, ssum)[..., None])
+    beta[small, 0] = 1.0
+    return beta
+
+
 def _anderson_mix(hist, k, m, n_res):
+    """Adjoint mixing: per-token Gram over all h*d of the token (`:1049-1074`)."""
     N = hist[0].shape[0]
     deltas = [hist[(k + m - i) % m] - hist[(k + m - i - 1) % m] for i in range(n_res)]
     G = np.zeros((N, 3, 3))
@@ -434,35 +494,7 @@ def _anderson_mix(hist, k, m, n_res):
             dot = (deltas[i] * deltas[j]).sum(axis=(1, 2))
             G[:, i, j] = dot
             G[:, j, i] = dot
-    beta = np.zeros((N, 3))
-    if n_res == 2:
-        g00, g01, g10, g11 = G[:, 0, 0], G[:, 0, 1], G[:, 1, 0], G[:, 1, 1]
-        reg = np.maximum(1e-8, 1e-4 * (np.abs(g00) + np.abs(g11)))
-        g00 = g00 + reg
-        g11 = g11 + reg
-        det = g00 * g11 - g01 * g10
-        sdet = np.where(det < 0, np.minimum(det, -1e-10), np.maximum(det, 1e-10))
-        beta[:, 0] = (g11 - g01) / sdet
-        beta[:, 1] = (g00 - g10) / sdet
-    else:
-        g = G.copy()
-        reg = np.maximum(1e-8, 1e-4 * (np.abs(g[:, 0, 0]) + np.abs(g[:, 1, 1]) + np.abs(g[:, 2, 2])))
-        for i in range(3):
-            g[:, i, i] += reg
-        g00, g01, g02 = g[:, 0, 0], g[:, 0, 1], g[:, 0, 2]
-        g10, g11, g12 = g[:, 1, 0], g[:, 1, 1], g[:, 1, 2]
-        g20, g21, g22 = g[:, 2, 0], g[:, 2, 1], g[:, 2, 2]
-        det = (g00 * (g11 * g22 - g12 * g21) - g01 * (g10 * g22 - g12 * g20)
-               + g02 * (g10 * g21 - g11 * g20))
-        sdet = np.where(det < 0, np.minimum(det, -1e-8), np.maximum(det, 1e-8))
-        beta[:, 0] = ((g11 * g22 - g12 * g21) - g01 * (g22 - g12) + g02 * (g21 - g11)) / sdet
-        beta[:, 1] = (g00 * (g22 - g12) - (g10 * g22 - g12 * g20) + g02 * (g10 - g20)) / sdet
-        beta[:, 2] = (g00 * (g11 - g21) - g01 * (g10 - g20) + (g10 * g21 - g11 * g20)) / sdet
-    beta = np.clip(beta[:, :n_res], -2.0, 3.0)
-    s = beta.sum(1)
-    small = np.abs(s) < 1e-6
-    beta = np.where(small[:, None], 0.0, beta / np.where(small, 1.0, s)[:, None])
-    beta[small, 0] = 1.0
+    beta = _anderson_coefs(G, n_res)
     out = np.zeros_like(hist[0])
     for i in range(n_res):
         out += beta[:, i][:, None, None] * hist[(k + m - i) % m]

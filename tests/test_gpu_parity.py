@@ -9,6 +9,7 @@ import pytest
 from oracle import deq_oracle as O
 from aideen_b200.backend import GpuDeqBackend, RunConfig, RULE_ADAM, RULE_CLIPPED_SGD, AideenError
 from aideen_b200.weights import init_all_weights, init_lm_head, init_embedding
+from parity_util import assert_step, step_errors
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-3
@@ -58,7 +59,7 @@ def test_forward_parity(c):
     if c["fpm"]:
         assert rel(be.read("hist_ctx", (B, T, h, d)), ref.hist_ctx) < TOL
         assert rel(be.read("mstate", (B, h, d)), ref.mstate) < TOL
-        assert rel(be.read("fpm_ctx", (B, T, h, d)), ref.fpm_ctx) < 1e-2 * max(1, 1)
+        assert rel(be.read("fpm_ctx", (B, T, h, d)), ref.fpm_ctx) < TOL
     assert st.solves == B * T * h and st.nonfinite == 0
     assert st.total_iters == int(ref.iters.sum())
     be.close()
@@ -155,15 +156,14 @@ def test_full_step_gradients_and_update(c):
         assert rel(Gg[a:b], G[a:b]) < TOL, name
     assert rel(be.read("ds_in", (N, d)), r["dS"]) < TOL
     assert rel(be.read("lm_grads", (r["lm_grads"].size,)), r["lm_grads"]) < TOL
-    # Adam step on both parameter sets
+    # Adam step on both parameter sets: the kernel against the oracle's Adam on
+    # the GPU's own gradients (fp32 rounding only); the gradients feeding it
+    # were compared at 1e-3 above (parity_util.step_errors says why the update
+    # W_new - W is not itself a 1e-3 quantity)
     be.apply_update(rule=RULE_ADAM, lr=1e-3, step=1, lm_head=True)
-    Wn = be.read_weights()
-    # compare the update itself (W_new - W) to keep the tolerance meaningful
-    assert rel(Wn.astype(np.float64) - W, r["W_new"] - W) < 5e-3
-    lw, lb, lg = be.read_lm_head()
-    lm_new = np.concatenate([lw.ravel(), lb, lg])
-    lm_old = np.concatenate([np.ravel(x) for x in lm])
-    assert rel(lm_new.astype(np.float64) - lm_old, r["lm_new"] - lm_old) < 5e-3
+    e = step_errors(be, r, W, lm, B, T)
+    assert e["adam_kernel"] < 1e-4 and e["lm_adam_kernel"] < 1e-4, e
+    assert e["update"] < 5e-3, e
     be.close()
 
 
@@ -208,8 +208,7 @@ def test_train_step_api_matches_oracle():
     loss = be.train_step(tok, tg, B, T, rc, adj_iters=12, lr=1e-3, step=1)
     cfg.adj_iters = 12
     r = O.train_step(emb[tok], tg, W, lm, cfg)
-    assert abs(loss - r["loss"]) / r["loss"] < TOL
-    assert rel(be.read_weights().astype(np.float64) - W, r["W_new"] - W) < 5e-3
+    assert_step(step_errors(be, r, W, lm, B, T), loss, r)
     be.close()
 
 
@@ -300,4 +299,6 @@ def test_pipelined_train_step_matches_sequential_and_oracle():
     cfg.adj_iters = 12
     r = O.train_step(emb[tok], tg, W, lm, cfg)
     assert abs(lp - r["loss"]) / r["loss"] < TOL
-    assert rel(wp.astype(np.float64) - W, r["W_new"] - W) < 5e-3
+    assert rel(gp, r["grads"]) < TOL and rel(lgp, r["lm_grads"]) < TOL
+    W_kernel, _, _ = O.adam(W, gp, np.zeros_like(W, np.float64), np.zeros_like(W, np.float64), 1, lr=1e-3)
+    assert rel(wp.astype(np.float64) - W, W_kernel.astype(np.float32).astype(np.float64) - W) < 1e-4
