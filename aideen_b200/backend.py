@@ -21,7 +21,7 @@ HOST, DEVICE = 0, 1
 
 BUF = dict(hstar=0, pooled=1, signal=2, attn=3, iters=4, adj_v=5, gpre=6, dl_dh=7, hist_ctx=8,
            mstate=9, fpm_ctx=10, alpha=11, s_in=12, ds_in=13, lm_grads=14, pre=15, fpm_dm=16,
-           fpm_carry=17)
+           fpm_carry=17, lm_samples=18)
 
 RULE_ADAM, RULE_CLIPPED_SGD = 0, 1
 
@@ -40,7 +40,7 @@ class Run(C.Structure):
     _fields_ = [("batch", C.c_uint32), ("seq_len", C.c_uint32), ("max_iters", C.c_uint32),
                 ("epsilon", C.c_float), ("damping", C.c_float), ("slot_coord", C.c_uint32),
                 ("fpm", C.c_uint32), ("fpm_alpha_m", C.c_float), ("fpm_tau", C.c_float),
-                ("fpm_read_gate_min", C.c_float)]
+                ("fpm_read_gate_min", C.c_float), ("anderson_m", C.c_uint32)]
 
 
 class Stats(C.Structure):
@@ -61,7 +61,8 @@ class Update(C.Structure):
 
 class StepArgs(C.Structure):
     _fields_ = [("run", Run), ("adj_iters", C.c_uint32), ("anderson_m", C.c_uint32),
-                ("update", Update), ("renorm", C.c_uint32)]
+                ("update", Update), ("renorm", C.c_uint32), ("lm_samples", C.c_uint32),
+                ("emb_update", C.c_uint32), ("emb_lr", C.c_float), ("sample_seed", C.c_uint64)]
 
 
 _LIB = None
@@ -84,6 +85,7 @@ _SIGS = {
     "aideen_download_grads": (C.c_int, [_P, _P, C.c_size_t]),
     "aideen_upload_lm_head": (C.c_int, [_P, _P, _P, _P]),
     "aideen_download_lm_head": (C.c_int, [_P, _P, _P, _P]),
+    "aideen_download_embedding": (C.c_int, [_P, _P]),
     "aideen_upload_embedding": (C.c_int, [_P, _P]),
     "aideen_reset_state": (C.c_int, [_P]),
     "aideen_reset_optimizer": (C.c_int, [_P]),
@@ -155,10 +157,11 @@ class RunConfig:
     fpm_alpha_m: float = 0.01
     fpm_tau: float = 0.5
     fpm_read_gate_min: float = 0.0
+    anderson_m: int = 0            # forward Anderson depth (0 = plain Picard)
 
     def run(self, batch: int, seq_len: int) -> Run:
         return Run(batch, seq_len, self.max_iters, self.epsilon, self.damping, int(self.slot_coord),
-                   int(self.fpm), self.fpm_alpha_m, self.fpm_tau, self.fpm_read_gate_min)
+                   int(self.fpm), self.fpm_alpha_m, self.fpm_tau, self.fpm_read_gate_min, self.anderson_m)
 
 
 class GpuDeqBackend:
@@ -208,7 +211,7 @@ class GpuDeqBackend:
     def launch_count(self) -> int:
         return int(self.lib.aideen_launch_count(self.ctx))
 
-    PROF_CLASSES = ("picard", "adjoint", "gemm", "lm_softmax", "optimizer", "other", "fpm_bwd")
+    PROF_CLASSES = ("picard", "adjoint", "gemm", "lm_head", "optimizer", "other", "fpm_bwd")
 
     def profile(self, enable: bool = True):
         """Bracket every kernel launch with CUDA events (per-class device time)."""
@@ -252,6 +255,11 @@ class GpuDeqBackend:
         c = np.empty(self.d, np.float32)
         self._check(self.lib.aideen_download_lm_head(self.ctx, _ptr(a), _ptr(b), _ptr(c)), "read_lm_head")
         return a, b, c
+
+    def read_embedding(self):
+        out = np.empty((self.vocab, self.d), np.float32)
+        self._check(self.lib.aideen_download_embedding(self.ctx, _ptr(out)), "read_embedding")
+        return out
 
     def upload_embedding(self, emb):
         e = _f32(emb)
@@ -338,13 +346,16 @@ class GpuDeqBackend:
 
     def train_step(self, tokens, targets, batch, seq_len, cfg: RunConfig, adj_iters=12,
                    anderson_m=0, lr=1e-3, step=1, rule=RULE_ADAM, renorm=False, allreduce=False,
-                   grad_scale=1.0, where=HOST, want_loss=True, raw_ptr=False):
+                   grad_scale=1.0, where=HOST, want_loss=True, raw_ptr=False, lm_samples=0,
+                   emb_update=0, emb_lr=0.0, sample_seed=0):
         """One full step.  With raw_ptr=True, `tokens`/`targets` are integer
         addresses (device memory when where=DEVICE, pinned host memory when
-        where=HOST) instead of arrays."""
+        where=HOST) instead of arrays.  lm_samples > 0 selects the reference's
+        sampled-softmax LM head; emb_update 1 / 2 trains the embedding rows
+        from dL/dpooled / dL/dS_in (see aideen_step_args)."""
         a = StepArgs(cfg.run(batch, seq_len), adj_iters, anderson_m,
                      Update(rule, lr, 0.9, 0.999, 1e-8, 0.0, grad_scale, step, int(allreduce), 1),
-                     int(renorm))
+                     int(renorm), lm_samples, emb_update, emb_lr, sample_seed)
         loss = C.c_float(0.0)
         if not raw_ptr:
             t, g = _i32(tokens), _i32(targets)

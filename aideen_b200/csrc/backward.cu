@@ -61,8 +61,8 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 // overlaps the on-chip iterations.  Waits are bounded.
 // Anderson weights of one token: block-reduce the Gram of the pseudo-residuals
 // (g6 = this warp's partials <d0,d0>, <d0,d1>, <d0,d2>, <d1,d1>, <d1,d2>,
-// <d2,d2>), then the regularised Cramer solve, clamp and renormalisation of
-// staged_adjoint_picard_clean.wgsl:1022-1135.  buf: 96 floats of shared memory.
+// <d2,d2>) over the token's h*d iterate, then anderson_solve
+// (staged_adjoint_picard_clean.wgsl:1022-1135).  buf: 96 floats of shared memory.
 template <int MA>
 __device__ __forceinline__ void anderson_coefs(float (&g6)[6], int n_res, float *buf, int s, int lane, int h,
                                                float &b0, float &b1, float &b2) {
@@ -79,39 +79,7 @@ __device__ __forceinline__ void anderson_coefs(float (&g6)[6], int n_res, float 
     for (int w = 0; w < h; ++w) t += buf[q * 16 + w];
     g6[q] = t;
   }
-  if (n_res == 2) {
-    float g00 = g6[0], g01 = g6[1], g10 = g6[1], g11 = g6[3];
-    const float reg = fmaxf(1e-8f, 1e-4f * (fabsf(g00) + fabsf(g11)));
-    g00 += reg;
-    g11 += reg;
-    const float det = g00 * g11 - g01 * g10;
-    const float sdet = det < 0.f ? fminf(det, -1e-10f) : fmaxf(det, 1e-10f);
-    b0 = (g11 - g01) / sdet;
-    b1 = (g00 - g10) / sdet;
-  } else {
-    float g00 = g6[0], g01 = g6[1], g02 = g6[2];
-    float g10 = g6[1], g11 = g6[3], g12 = g6[4];
-    float g20 = g6[2], g21 = g6[4], g22 = g6[5];
-    const float reg = fmaxf(1e-8f, 1e-4f * (fabsf(g00) + fabsf(g11) + fabsf(g22)));
-    g00 += reg;
-    g11 += reg;
-    g22 += reg;
-    const float det = g00 * (g11 * g22 - g12 * g21) - g01 * (g10 * g22 - g12 * g20) +
-                      g02 * (g10 * g21 - g11 * g20);
-    const float sdet = det < 0.f ? fminf(det, -1e-8f) : fmaxf(det, 1e-8f);
-    b0 = ((g11 * g22 - g12 * g21) - g01 * (g22 - g12) + g02 * (g21 - g11)) / sdet;
-    b1 = (g00 * (g22 - g12) - (g10 * g22 - g12 * g20) + g02 * (g10 - g20)) / sdet;
-    b2 = (g00 * (g11 - g21) - g01 * (g10 - g20) + (g10 * g21 - g11 * g20)) / sdet;
-  }
-  b0 = fminf(fmaxf(b0, -2.f), 3.f);
-  b1 = fminf(fmaxf(b1, -2.f), 3.f);
-  if (n_res == 3) b2 = fminf(fmaxf(b2, -2.f), 3.f);
-  const float ssum = b0 + b1 + (n_res == 3 ? b2 : 0.f);
-  if (fabsf(ssum) < 1e-6f) {
-    b0 = 1.f; b1 = 0.f; b2 = 0.f;
-  } else {
-    b0 /= ssum; b1 /= ssum; b2 = n_res == 3 ? b2 / ssum : 0.f;
-  }
+  anderson_solve(g6, n_res, b0, b1, b2);
 }
 
 // HS: the Anderson iterates live in a shared-memory ring ([MA][h][d], each
@@ -150,6 +118,11 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
   };
   if (threadIdx.x == 0 && (int)blockIdx.x < a.N) issue(blockIdx.x, 0);
   int it = 0;
+  // per-CTA NormScale-gradient partial of this warp's slot, summed over the
+  // CTA's tokens (nsg_cta mode)
+  float4 nsv[F];
+#pragma unroll
+  for (int f = 0; f < F; ++f) nsv[f] = f4(0.f);
   for (int n = blockIdx.x; n < a.N; n += gridDim.x, ++it) {
     const int b = it & 1;
     const int nn = n + (int)gridDim.x;
@@ -207,25 +180,19 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
     }
     float4 hist[(MA > 0 && !HS) ? MA : 1][F];
     float *ring = stage0 + 2 * stage_f + (size_t)s * d;  // HS: iterate slot q at ring + q * hd
-    for (int k = 0; k < a.iters; ++k) {
-      float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;  // independent partial sums (ILP)
+    int k0 = 0;
+    for (int k = k0; k < a.iters; ++k) {
+      // w . v in two float4 partial sums (ILP), packed FMAs throughout
+      float4 c0 = f4(0.f), c1 = f4(0.f);
 #pragma unroll
       for (int f = 0; f < F; ++f) {
-        c0 = fmaf(wv[f].x, v[f].x, c0);
-        c1 = fmaf(wv[f].y, v[f].y, c1);
-        c2 = fmaf(wv[f].z, v[f].z, c2);
-        c3 = fmaf(wv[f].w, v[f].w, c3);
+        if (f & 1) c1 = dot4_acc(c1, wv[f], v[f]);
+        else c0 = dot4_acc(c0, wv[f], v[f]);
       }
-      const float ncs = -warp_sum((c0 + c1) + (c2 + c3)) * inv_den;
+      const float ncs = -warp_sum(hsum4(c0) + hsum4(c1)) * inv_den;
+      const float4 nc4 = f4(ncs);
   #pragma unroll
-      for (int f = 0; f < F; ++f) {
-        float4 x;
-        x.x = fmaf(ncs, pre[f].x, fmaf(av[f].x, v[f].x, rhs[f].x));
-        x.y = fmaf(ncs, pre[f].y, fmaf(av[f].y, v[f].y, rhs[f].y));
-        x.z = fmaf(ncs, pre[f].z, fmaf(av[f].z, v[f].z, rhs[f].z));
-        x.w = fmaf(ncs, pre[f].w, fmaf(av[f].w, v[f].w, rhs[f].w));
-        v[f] = x;
-      }
+      for (int f = 0; f < F; ++f) v[f] = fma4(nc4, pre[f], fma4(av[f], v[f], rhs[f]));
       if constexpr (MA > 0 && HS) {
         // hist i steps ago = ring slot (k - i) mod MA; this iterate goes to slot k mod MA
 #pragma unroll
@@ -309,8 +276,9 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
       const int j = (f * 32 + lane) * 4;
       st4(a.v + vbase + j, v[f]);
       // g_pre = beta*J_norm^T v = (a - (1 - beta)) * v - (w . v / den) * pre
-      st4(a.gpre + e + j, (av[f] - f4(1.f - beta)) * v[f] - cs * pre[f]);
+      if (a.gpre) st4(a.gpre + e + j, (av[f] - f4(1.f - beta)) * v[f] - cs * pre[f]);
       if (a.nsg) st4(nsacc + (size_t)s * d + j, (beta * inv) * (v[f] * pre[f]));
+      if (a.nsg_cta) nsv[f] = fma4(f4(beta * inv), v[f] * pre[f], nsv[f]);
     }
     if (a.nsg) {
       __syncthreads();
@@ -322,10 +290,22 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
       __syncthreads();  // nsacc (this stage) is read before thread 0 refills it
     }
   }
+  if (a.nsg_cta) {
+    // sum the slots' partials through shared memory (every stage is consumed)
+    __syncthreads();
+#pragma unroll
+    for (int f = 0; f < F; ++f) st4(stage0 + (size_t)s * d + (f * 32 + lane) * 4, nsv[f]);
+    __syncthreads();
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+      float t = 0.f;
+      for (int q = 0; q < h; ++q) t += stage0[(size_t)q * d + j];
+      a.nsg_cta[(size_t)blockIdx.x * d + j] = t;
+    }
+  }
 }
 
 template <int F, int MA, int MAXT, int MINB, bool HS = false>
-static cudaError_t adjoint_launch(const AdjointArgs &a, cudaStream_t st) {
+static cudaError_t adjoint_launch(const AdjointArgs &a, cudaStream_t st, int *grid_out) {
   const size_t hd = (size_t)a.h * a.d;
   const size_t stage_f = hd * (1 + (a.pre_b != nullptr) + (a.rhs_slot != nullptr)) +
                          (a.rhs_tok ? (size_t)a.d : 0);
@@ -341,28 +321,30 @@ static cudaError_t adjoint_launch(const AdjointArgs &a, cudaStream_t st) {
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
   const int cap = (a.max_ctas > 0 && a.max_ctas < sms ? a.max_ctas : sms) * per_sm;
   const int grid = a.N < cap ? a.N : cap;
+  if (grid_out) *grid_out = grid;
   k<<<grid, 32 * a.h, smem, st>>>(a);
   return cudaGetLastError();
 }
 
 template <int F>
-static cudaError_t adjoint_dispatch_m(const AdjointArgs &a, cudaStream_t st) {
+static cudaError_t adjoint_dispatch_m(const AdjointArgs &a, cudaStream_t st, int *g) {
   const int ma = a.anderson_m <= 2 ? 0 : a.anderson_m;  // m <= 2 never mixes (n_res < 2)
   const bool small = a.h <= 8;
   switch (ma) {
-    case 0: return small ? adjoint_launch<F, 0, 256, 2>(a, st) : adjoint_launch<F, 0, 512, 1>(a, st);
-    case 3: return small ? adjoint_launch<F, 3, 256, 1>(a, st) : adjoint_launch<F, 3, 512, 1>(a, st);
+    case 0: return small ? adjoint_launch<F, 0, 256, 2>(a, st, g) : adjoint_launch<F, 0, 512, 1>(a, st, g);
+    case 3: return small ? adjoint_launch<F, 3, 256, 1>(a, st, g) : adjoint_launch<F, 3, 512, 1>(a, st, g);
     case 4:
       // iterates in shared memory (two tokens per SM) while two CTAs' rings and
       // stages fit: 4 x h x d floats of ring per CTA
       if (small && 4 * (size_t)a.h * a.d <= 16384 && !getenv("AIDEEN_ADJ_REG_HIST"))
-        return adjoint_launch<F, 4, 256, 2, true>(a, st);
-      return small ? adjoint_launch<F, 4, 256, 1>(a, st) : adjoint_launch<F, 4, 512, 1>(a, st);
+        return adjoint_launch<F, 4, 256, 2, true>(a, st, g);
+      return small ? adjoint_launch<F, 4, 256, 1>(a, st, g) : adjoint_launch<F, 4, 512, 1>(a, st, g);
     default: return cudaErrorInvalidValue;
   }
 }
 
-cudaError_t launch_adjoint(const AdjointArgs &a0, cudaStream_t st) {
+cudaError_t launch_adjoint(const AdjointArgs &a0, cudaStream_t st, int *g) {
+  if (g) *g = 0;
   if (a0.N <= 0) return cudaSuccess;
   AdjointArgs a = a0;
   // AIDEEN_ADJ_SPIN_LIMIT shortens the stage waits (0: every first wait gives
@@ -370,10 +352,10 @@ cudaError_t launch_adjoint(const AdjointArgs &a0, cudaStream_t st) {
   a.spin_limit = kSpinLimit;
   if (const char *e = getenv("AIDEEN_ADJ_SPIN_LIMIT")) a.spin_limit = (uint32_t)strtoul(e, nullptr, 10);
   switch (a.d) {
-    case 128: return adjoint_dispatch_m<1>(a, st);
-    case 256: return adjoint_dispatch_m<2>(a, st);
-    case 512: return adjoint_dispatch_m<4>(a, st);
-    case 1024: return adjoint_dispatch_m<8>(a, st);
+    case 128: return adjoint_dispatch_m<1>(a, st, g);
+    case 256: return adjoint_dispatch_m<2>(a, st, g);
+    case 512: return adjoint_dispatch_m<4>(a, st, g);
+    case 1024: return adjoint_dispatch_m<8>(a, st, g);
     default: return cudaErrorInvalidValue;
   }
 }

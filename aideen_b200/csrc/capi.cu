@@ -63,6 +63,15 @@ struct DevBufs {
   float *fcarry = nullptr;                                // [max_batch][h][d] TBPTT carry
   float *fprm = nullptr;                                   // [h][5][d] FPM slot parameters
   float *fpart = nullptr, *fpart_bw = nullptr;            // [5][max_batch*nch][h][d], [max_batch*nch][h]
+  // sampled-softmax LM head and embedding update (allocated on first use)
+  int32_t *lS = nullptr;     // [lcap] sampled vocabulary ids
+  float *lWS = nullptr;      // [lcap][d] gathered (then updated) W_lm rows
+  int *ints = nullptr;       // [0] K, [1] distinct tokens U
+  unsigned int *lerr = nullptr;
+  int32_t *tg_all = nullptr, *tok_all = nullptr;  // allgathered targets / tokens (data parallel)
+  float *grad_all = nullptr;                       // allgathered embedding-gradient rows
+  int32_t *cuniq = nullptr, *coff = nullptr, *cpos = nullptr;  // token CSR
+  float *Me1 = nullptr, *Me2 = nullptr;             // embedding Adam moments [V][d]
 };
 
 }  // namespace
@@ -117,8 +126,10 @@ struct aideen_ctx {
   // rows currently held (perm_B = 1: caller order, e.g. after aideen_adjoint_on).
   int perm_B = 1, perm_T = 0;
   uint32_t adj_N = 0;     // tokens of the last adjoint
+  int nsg_rows = 0;       // rows of per-CTA NormScale-gradient partials the last adjoint wrote
   float adj_beta = 0.85f;
   bool lm_ready = false, emb_ready = false;
+  size_t lcap = 0, gcap = 0;  // capacity of the sampled-set buffers / allgather buffers (rows)
   bool lm_split_stale = true;  // W_lm changed since its hi/lo copies were made
   bool use_tc = true;     // tcgen05 GEMMs where the operand shapes allow
   DevBufs b;
@@ -270,6 +281,7 @@ int check_run(aideen_ctx *ctx, const aideen_run *r) {
       r->seq_len > ctx->cfg.max_seq_len)
     return set_err(ctx, AIDEEN_E_INVALID, "batch/seq_len outside the context caps");
   if (r->max_iters == 0) return set_err(ctx, AIDEEN_E_INVALID, "max_iters must be >= 1");
+  if (r->anderson_m > 3) return set_err(ctx, AIDEEN_E_UNSUPPORTED, "forward anderson_m > 3");
   return AIDEEN_OK;
 }
 
@@ -345,6 +357,7 @@ PicardArgs picard_args(aideen_ctx *ctx, const aideen_run *r) {
   p.iters = b.iters;
   p.t0 = 0;
   p.t1 = r->seq_len;
+  p.anderson_m = r->anderson_m >= 2 ? (int)r->anderson_m : 0;  // depth 1 never mixes
   return p;
 }
 
@@ -386,6 +399,8 @@ int run_forward(aideen_ctx *ctx, const aideen_run *r, aideen_stats *stats) {
 
 int run_lm_head(aideen_ctx *ctx, int N, float *loss_out) {
   if (!ctx->lm_ready) return set_err(ctx, AIDEEN_E_INVALID, "LM head not uploaded");
+  ctx->prof_phase = AIDEEN_PROF_LM_SOFTMAX;  // every LM-head launch in one profile class
+  struct PhaseReset { aideen_ctx *c; ~PhaseReset() { c->prof_phase = -1; } } phase_reset{ctx};
   const int d = ctx->cfg.d_model, V = ctx->cfg.vocab;
   DevBufs &b = ctx->b;
   cudaStream_t st = ctx->stream;
@@ -445,8 +460,10 @@ int run_adjoint(aideen_ctx *ctx, int N, const float *pre_a, const float *pre_b,
   a.N = N; a.h = ctx->cfg.h_slots; a.d = ctx->cfg.d_model; a.iters = iters;
   a.anderson_m = anderson_m; a.beta = beta;
   a.pre_a = pre_a; a.pre_b = pre_b; a.rhs_tok = rhs_tok; a.rhs_slot = rhs_slot;
-  a.NS = ctx->b.W + ctx->P.nscale; a.v = ctx->b.v; a.gpre = ctx->b.gpre; a.nsg = ctx->b.nsg;
-  KL(launch_adjoint(a, ctx->stream));
+  a.NS = ctx->b.W + ctx->P.nscale; a.v = ctx->b.v; a.gpre = ctx->b.gpre; a.nsg_cta = ctx->b.nsg;
+  int grid = 0;
+  KL(launch_adjoint(a, ctx->stream, &grid));
+  ctx->nsg_rows = grid;
   ctx->adj_N = N;
   ctx->adj_beta = beta;
   return AIDEEN_OK;
@@ -506,7 +523,7 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
     if (!fork_fpm) CU(cudaEventRecord(ctx->ev_g0, st));
     CU(cudaStreamWaitEvent(ctx->ast, ctx->ev_g0, 0));
   }
-  KL(launch_colsum(b.nsg, N, d, d, G + L.nscale, d, 0, false, sst));
+  KL(launch_colsum(b.nsg, ctx->nsg_rows, d, d, G + L.nscale, d, 0, false, sst));
   AttnBwdArgs a{};
   a.h = h; a.d = d; a.W = W; a.off_qb = L.q_bias; a.off_kb = L.k_bias; a.off_anchor = L.slot_anchor;
   a.gpre = b.gpre; a.amat = b.amat; a.scale = b.scale; a.rho = b.rho; a.Rsrc = b.Rsrc;
@@ -817,6 +834,7 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   }
   // per-chunk consumers on the context stream, within the SMs the solve leaves
   int colpart_rows = 0;
+  int nsg_rows = 0;
   for (int j = 0; j < nch; ++j) {
     const int t0 = chunk_bound_aligned(j, nch, T, B), t1 = chunk_bound_aligned(j + 1, nch, T, B);
     const int bud = (j + 1 < nch || cap_last) ? budget : 0;
@@ -872,9 +890,13 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
     aa.beta = r->damping;
     aa.pre_a = b.pre + r0 * h * d; aa.pre_b = nullptr; aa.rhs_tok = b.dl_dh + r0 * d; aa.rhs_slot = nullptr;
     aa.NS = b.W + ctx->P.nscale; aa.v = b.v + r0 * d; aa.v_ld = N; aa.gpre = b.gpre + r0 * h * d;
-    aa.nsg = b.nsg + r0 * d; aa.max_ctas = bud;
+    // per-CTA NormScale-gradient partials, the chunks' rows one after another
+    // (a launch has at most as many CTAs as tokens, so N rows always suffice)
+    aa.nsg_cta = b.nsg + (size_t)nsg_rows * d; aa.max_ctas = bud;
     if (a->anderson_m > 4) { ctx->sm_budget = 0; return set_err(ctx, AIDEEN_E_UNSUPPORTED, "anderson_m > 4"); }
-    KL(launch_adjoint(aa, st));
+    int grid = 0;
+    KL(launch_adjoint(aa, st, &grid));
+    nsg_rows += grid;
     tl_mark(ctx, ("cons" + std::to_string(j)).c_str(), st);
     // the FPM backward's chunk composites need only the forward and this
     // chunk's adjoint: form them on the FPM stream now (not for the last chunk,
@@ -912,6 +934,7 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   ctx->sm_budget = 0;
   ctx->adj_N = N;
   ctx->adj_beta = r->damping;
+  ctx->nsg_rows = nsg_rows;
   KL(launch_sum(b.loss_rows, N, b.scal + 1, st));
   const bool tail_lm = ctx->lmst && !ctx->prof;
   cudaStream_t lst = tail_lm ? ctx->lmst : st;
@@ -931,6 +954,145 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
     ctx->lmg_pending = true;
   }
   return stats ? read_solve_stats(ctx, r, stats) : AIDEEN_OK;
+}
+
+// Sampled-softmax LM head over the last forward's pooled rows (the
+// reference's lm_probs -> lm_update -> lm_backprop_h_t order): its Adam step
+// on the sampled rows happens here, before dL/dh is formed from them.  With a
+// communicator the sampled set is built from every rank's targets and the
+// sampled-row gradients are summed over ranks before the clamp and the step,
+// so every rank applies the same update.
+int run_lm_head_sampled(aideen_ctx *ctx, int N, const aideen_step_args *a) {
+  if (!ctx->lm_ready) return set_err(ctx, AIDEEN_E_INVALID, "LM head not uploaded");
+  ctx->prof_phase = AIDEEN_PROF_LM_SOFTMAX;  // every LM-head launch in one profile class
+  struct PhaseReset { aideen_ctx *c; ~PhaseReset() { c->prof_phase = -1; } } phase_reset{ctx};
+  const int d = ctx->cfg.d_model, V = ctx->cfg.vocab;
+  DevBufs &b = ctx->b;
+  cudaStream_t st = ctx->stream;
+  const bool dp = ctx->comm && ctx->nranks > 1;
+  const int Ng = dp ? N * ctx->nranks : N;
+  const int ns = (int)a->lm_samples;
+  // K <= max(min(max(ns, Ng), V, 2048), distinct targets) <= min(V, max(ns, Ng))
+  size_t cap = (size_t)(ns > Ng ? ns : Ng);
+  if (cap > (size_t)V) cap = V;
+  cap = (cap + 3) / 4 * 4;
+  if (cap > (size_t)ctx->Vp) return set_err(ctx, AIDEEN_E_INVALID, "sampled set larger than the logits rows");
+  if (cap > ctx->lcap) {
+    if (b.lS) { cudaFree(b.lS); cudaFree(b.lWS); b.lS = nullptr; b.lWS = nullptr; }
+    CU(dalloc(&b.lS, cap));
+    CU(dalloc(&b.lWS, cap * d));
+    ctx->lcap = cap;
+  }
+  if (!b.ints) {
+    CU(dalloc(&b.ints, 8));
+    CU(dalloc(&b.lerr, 1));
+    CU(cudaMemsetAsync(b.lerr, 0, sizeof(unsigned int), st));
+  }
+  const int32_t *tg = b.targets;
+  if (dp) {
+    if ((size_t)Ng > ctx->gcap) {
+      if (b.tg_all) { cudaFree(b.tg_all); cudaFree(b.tok_all); b.tg_all = b.tok_all = nullptr; }
+      CU(dalloc(&b.tg_all, (size_t)Ng));
+      CU(dalloc(&b.tok_all, (size_t)Ng));
+      ctx->gcap = Ng;
+    }
+    const ncclResult_t nr = ncclAllGather(b.targets, b.tg_all, N, ncclInt32, ctx->comm, st);
+    if (nr != ncclSuccess) return set_err(ctx, AIDEEN_E_NCCL, std::string("ncclAllGather: ") + ncclGetErrorString(nr));
+    tg = b.tg_all;
+  }
+  CU(join_side(ctx));
+  const unsigned long long seed = a->sample_seed ? (unsigned long long)a->sample_seed : 0xA1DEEE5A4D5EED5Eull;
+  const uint32_t step = a->update.step;
+  int *Kd = b.ints;
+  KL(launch_sample_set(tg, Ng, V, ns, 2048, seed, step, b.lS, Kd, b.scal, (int)cap, b.lerr, st));
+  const float *Wlm = b.lmp, *blm = b.lmp + ctx->lm_b, *glm = b.lmp + ctx->lm_g;
+  KL(launch_gather_rows(Wlm, b.lS, Kd, (int)cap, d, b.lWS, st));
+  const long ld = (long)cap;
+  // logits[n][k] = y[n] . W_lm[S_k]
+  KL(gemm_any(ctx, gemm(N, (int)cap, d, 1, b.y, d, 0, false, b.lWS, d, 0, true, b.logits, ld, 0)));
+  KL(launch_softmax_sampled(b.logits, ld, blm, b.lS, Kd, b.targets, V, b.scal, b.loss_rows, N, st));
+  KL(launch_sum(b.loss_rows, N, b.scal + 1, st));
+  // dW_S[k][j] = sum_n coef[n][k] y[n][j]; db_S[k] = sum_n coef[n][k]
+  float *dW = b.Glm, *db = b.Glm + ctx->lm_b;
+  KL(gemm_any(ctx, gemm((int)cap, d, N, 1, b.logits, ld, 0, true, b.y, d, 0, false, dW, d, 0)));
+  KL(launch_colsum(b.logits, N, (int)cap, ld, db, (int)cap, 0, false, st));
+  if (dp) {
+    ncclResult_t nr = ncclGroupStart();
+    if (nr == ncclSuccess) nr = ncclAllReduce(dW, dW, cap * d, ncclFloat, ncclSum, ctx->comm, st);
+    if (nr == ncclSuccess) nr = ncclAllReduce(db, db, cap, ncclFloat, ncclSum, ctx->comm, st);
+    const ncclResult_t n2 = ncclGroupEnd();
+    if (nr != ncclSuccess || n2 != ncclSuccess)
+      return set_err(ctx, AIDEEN_E_NCCL, std::string("ncclAllReduce: ") +
+                                             ncclGetErrorString(nr != ncclSuccess ? nr : n2));
+  }
+  const aideen_update *u = &a->update;
+  const double t = u->step < 1 ? 1.0 : (double)u->step;
+  const float bc1 = (float)(1.0 - std::pow((double)u->beta1, t));
+  const float bc2 = (float)(1.0 - std::pow((double)u->beta2, t));
+  KL(launch_lm_sampled_adam(b.lmp, b.lmp + ctx->lm_b, b.Mlm1, b.Mlm2, ctx->lm_b, dW, db, b.lS, Kd, (int)cap, d,
+                            b.lWS, u->lr, u->beta1, u->beta2, u->eps, bc1, bc2, st));
+  ctx->lm_split_stale = true;
+  // dL/dy[n][j] = sum_k coef[n][k] W_lm'[S_k][j], then through the RMSNorm
+  KL(gemm_any(ctx, gemm(N, d, (int)cap, 1, b.logits, ld, 0, false, b.lWS, d, 0, false, b.dy, d, 0)));
+  KL(launch_rmsnorm_bwd(b.dy, b.pooled, b.lrms, glm, b.dl_dh, b.ggp, N, d, st));
+  return AIDEEN_OK;
+}
+
+// Embedding rows of the step's tokens: the mean gradient row of every
+// distinct token (dL/dpooled, or dL/dS_in with source 2), then Adam on that
+// row.  With a communicator every rank gathers all ranks' tokens and rows, so
+// every rank applies the same update.
+int run_emb_update(aideen_ctx *ctx, int N, const aideen_step_args *a) {
+  const int d = ctx->cfg.d_model, V = ctx->cfg.vocab;
+  DevBufs &b = ctx->b;
+  cudaStream_t st = ctx->stream;
+  const bool dp = ctx->comm && ctx->nranks > 1;
+  const int Ng = dp ? N * ctx->nranks : N;
+  if (Ng > emb_csr_max_tokens())
+    return set_err(ctx, AIDEEN_E_UNSUPPORTED, "embedding update: more tokens per step than the CSR sort holds");
+  if (!b.Me1) {
+    CU(dalloc(&b.Me1, (size_t)V * d));
+    CU(dalloc(&b.Me2, (size_t)V * d));
+    CU(cudaMemsetAsync(b.Me1, 0, (size_t)V * d * 4, st));
+    CU(cudaMemsetAsync(b.Me2, 0, (size_t)V * d * 4, st));
+  }
+  if (!b.cuniq || (size_t)Ng > ctx->gcap) {
+    if (b.cuniq) { cudaFree(b.cuniq); cudaFree(b.coff); cudaFree(b.cpos); }
+    if (b.tg_all) { cudaFree(b.tg_all); cudaFree(b.tok_all); b.tg_all = b.tok_all = nullptr; }
+    if (b.grad_all) { cudaFree(b.grad_all); b.grad_all = nullptr; }
+    const size_t n = (size_t)Ng > ctx->gcap ? (size_t)Ng : ctx->gcap;
+    CU(dalloc(&b.cuniq, n)); CU(dalloc(&b.coff, n + 1)); CU(dalloc(&b.cpos, n));
+    CU(dalloc(&b.tg_all, n)); CU(dalloc(&b.tok_all, n));
+    ctx->gcap = n;
+  }
+  if (!b.ints) {
+    CU(dalloc(&b.ints, 8));
+    CU(dalloc(&b.lerr, 1));
+    CU(cudaMemsetAsync(b.lerr, 0, sizeof(unsigned int), st));
+  }
+  const float *grad = a->emb_update == 2 ? b.dS : b.dl_dh;
+  const int32_t *tok = b.tokens;
+  if (dp) {
+    if (!b.grad_all) CU(dalloc(&b.grad_all, ctx->gcap * d));
+    ncclResult_t nr = ncclGroupStart();
+    if (nr == ncclSuccess) nr = ncclAllGather(b.tokens, b.tok_all, N, ncclInt32, ctx->comm, st);
+    if (nr == ncclSuccess) nr = ncclAllGather(grad, b.grad_all, (size_t)N * d, ncclFloat, ctx->comm, st);
+    const ncclResult_t n2 = ncclGroupEnd();
+    if (nr != ncclSuccess || n2 != ncclSuccess)
+      return set_err(ctx, AIDEEN_E_NCCL, std::string("ncclAllGather: ") +
+                                             ncclGetErrorString(nr != ncclSuccess ? nr : n2));
+    tok = b.tok_all;
+    grad = b.grad_all;
+  }
+  const aideen_update *u = &a->update;
+  const double t = u->step < 1 ? 1.0 : (double)u->step;
+  const float bc1 = (float)(1.0 - std::pow((double)u->beta1, t));
+  const float bc2 = (float)(1.0 - std::pow((double)u->beta2, t));
+  const float lr = a->emb_lr > 0.f ? a->emb_lr : u->lr;
+  KL(launch_emb_csr(tok, Ng, V, b.cuniq, b.coff, b.cpos, b.ints + 1, st));
+  KL(launch_emb_adam(b.emb, b.Me1, b.Me2, grad, b.cuniq, b.coff, b.cpos, b.ints + 1, Ng, d, lr, u->beta1,
+                     u->beta2, u->eps, bc1, bc2, st));
+  return AIDEEN_OK;
 }
 
 int run_allreduce(aideen_ctx *ctx, int timeout_ms) {
@@ -1138,7 +1300,9 @@ void aideen_destroy(aideen_ctx *ctx) {
                   b.Mlm2, b.y, b.lrms, b.logits, b.dy, b.ggp, b.loss_rows, b.scal, b.emb, b.stats,
                   b.sigmas, b.stage, b.ws, b.fc, b.frp, b.fdl, b.fminner, b.fdm, b.fgpre, b.fup,
                   b.fkw, b.fdup, b.fA, b.fU, b.fgin, b.fcarry, b.fpart, b.fpart_bw, b.fprm, b.src,
-                  b.dlog_lo, b.yhi, b.ylo, b.yThi, b.yTlo, b.whi, b.wlo, b.colpart, b.perm, b.ws2, b.ws3, b.rowstats};
+                  b.dlog_lo, b.yhi, b.ylo, b.yThi, b.yTlo, b.whi, b.wlo, b.colpart, b.perm, b.ws2, b.ws3, b.rowstats,
+                  b.lS, b.lWS, b.ints, b.lerr, b.tg_all, b.tok_all, b.grad_all, b.cuniq, b.coff, b.cpos,
+                  b.Me1, b.Me2};
   for (void *p : ptrs)
     if (p) cudaFree(p);
   if (ctx->side) cudaStreamSynchronize(ctx->side);
@@ -1291,6 +1455,14 @@ int aideen_upload_embedding(aideen_ctx *ctx, const float *emb) {
   CU(cudaStreamSynchronize(ctx->stream));
   ctx->emb_ready = true;
   return AIDEEN_OK;
+}
+
+int aideen_download_embedding(aideen_ctx *ctx, float *emb) {
+  if (!ctx || !emb) return AIDEEN_E_INVALID;
+  if (!ctx->emb_ready) return set_err(ctx, AIDEEN_E_INVALID, "embedding not uploaded");
+  CU(cudaMemcpyAsync(emb, ctx->b.emb, (size_t)ctx->cfg.vocab * ctx->cfg.d_model * 4, cudaMemcpyDeviceToHost,
+                     ctx->stream));
+  return sync_and_check(ctx);
 }
 
 int aideen_reset_state(aideen_ctx *ctx) {
@@ -1452,27 +1624,36 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
   CHK(copy_in_rows(ctx, ctx->b.tokens, tokens, a->run.batch, a->run.seq_len, 1, 1, where));
   CHK(copy_in_rows(ctx, ctx->b.targets, targets, a->run.batch, a->run.seq_len, 1, 1, where));
   KL(launch_embed(ctx->b.tokens, ctx->b.emb, ctx->b.S_in, N, ctx->cfg.d_model, ctx->cfg.vocab, ctx->stream));
-  const int nch = pipeline_chunks(ctx, &a->run);
+  if (a->emb_update > 2) return set_err(ctx, AIDEEN_E_INVALID, "emb_update must be 0, 1 or 2");
+  const bool sampled = a->lm_samples > 0;
+  // the sampled head updates its rows before dL/dh exists: no overlap of the
+  // adjoint with the solve, so the sequential schedule
+  const int nch = sampled ? 0 : pipeline_chunks(ctx, &a->run);
   if (nch > 1) {
     CHK(run_step_pipelined(ctx, a, nch, stats));
   } else {
     CHK(run_forward(ctx, &a->run, stats));
-    CHK(run_lm_head(ctx, N, nullptr));
+    if (sampled) CHK(run_lm_head_sampled(ctx, N, a));
+    else CHK(run_lm_head(ctx, N, nullptr));
     CHK(run_adjoint(ctx, N, ctx->b.pre, nullptr, ctx->b.dl_dh, nullptr, a->adj_iters, a->run.damping,
                     a->anderson_m));
   }
-  CHK(run_weight_grads(ctx, false));
+  CHK(run_weight_grads(ctx, a->emb_update == 2));
   if (ctx->lmg_pending) {  // the last chunk's dW_lm and LM-head sums
     CU(cudaStreamWaitEvent(ctx->stream, ctx->ev_lmg, 0));
     ctx->lmg_pending = false;
   }
   tl_mark(ctx, "wgrads", ctx->stream);
-  CHK(run_update(ctx, &a->update));
+  aideen_update up = a->update;
+  if (sampled) up.update_lm_head = 0;  // its rows were updated inside the LM stage
+  CHK(run_update(ctx, &up));
   tl_mark(ctx, "update", ctx->stream);
   tl_flush(ctx);
   if (a->renorm)
     KL(launch_spectral(ctx->b.W, ctx->cfg.d_model, ctx->cfg.h_slots, ctx->P, 12, 0.10f, 0.30f, 0.70f,
                        0.50f, 0.50f, ctx->b.sigmas, ctx->stream));
+  // the reference updates the embedding rows last (trainer.rs:3282-3300)
+  if (a->emb_update) CHK(run_emb_update(ctx, N, a));
   if (loss_out) {
     CU(cudaMemcpyAsync(loss_out, ctx->b.scal + 1, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
     CHK(sync_and_check(ctx));
@@ -1500,6 +1681,7 @@ static void *buf_ptr(aideen_ctx *ctx, int which, size_t *count) {
     case AIDEEN_BUF_S_IN: *count = N * d; return b.S_in;
     case AIDEEN_BUF_DS_IN: *count = N * d; return b.dS;
     case AIDEEN_BUF_LM_GRADS: *count = ctx->lm_len ? ctx->lm_b + ctx->cfg.vocab + d : 0; return b.Glm;
+    case AIDEEN_BUF_LM_SAMPLES: *count = ctx->lcap; return b.lS;
     case AIDEEN_BUF_PRE: *count = N * h * d; return b.pre;
     case AIDEEN_BUF_FPM_DM: *count = b.fdm ? N * h * d : 0; return b.fdm;
     case AIDEEN_BUF_FPM_CARRY: *count = (size_t)ctx->cfg.max_batch * h * d; return b.fcarry;

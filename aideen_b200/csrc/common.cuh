@@ -16,6 +16,49 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Type-II Anderson mixing weights from the Gram of n_res (2 or 3) pseudo-
+// residuals, g6 = <d0,d0>, <d0,d1>, <d0,d2>, <d1,d1>, <d1,d2>, <d2,d2>:
+// Tikhonov term 1e-4*trace, Cramer solve with a floored determinant, clamp to
+// [-2, 3] and renormalisation to sum 1 with a most-recent fallback
+// (staged_adjoint_picard_clean.wgsl:1075-1124).
+__device__ __forceinline__ void anderson_solve(const float (&g6)[6], int n_res, float &b0, float &b1,
+                                               float &b2) {
+  b2 = 0.f;
+  if (n_res == 2) {
+    float g00 = g6[0], g01 = g6[1], g10 = g6[1], g11 = g6[3];
+    const float reg = fmaxf(1e-8f, 1e-4f * (fabsf(g00) + fabsf(g11)));
+    g00 += reg;
+    g11 += reg;
+    const float det = g00 * g11 - g01 * g10;
+    const float sdet = det < 0.f ? fminf(det, -1e-10f) : fmaxf(det, 1e-10f);
+    b0 = (g11 - g01) / sdet;
+    b1 = (g00 - g10) / sdet;
+  } else {
+    float g00 = g6[0], g01 = g6[1], g02 = g6[2];
+    float g10 = g6[1], g11 = g6[3], g12 = g6[4];
+    float g20 = g6[2], g21 = g6[4], g22 = g6[5];
+    const float reg = fmaxf(1e-8f, 1e-4f * (fabsf(g00) + fabsf(g11) + fabsf(g22)));
+    g00 += reg;
+    g11 += reg;
+    g22 += reg;
+    const float det = g00 * (g11 * g22 - g12 * g21) - g01 * (g10 * g22 - g12 * g20) +
+                      g02 * (g10 * g21 - g11 * g20);
+    const float sdet = det < 0.f ? fminf(det, -1e-8f) : fmaxf(det, 1e-8f);
+    b0 = ((g11 * g22 - g12 * g21) - g01 * (g22 - g12) + g02 * (g21 - g11)) / sdet;
+    b1 = (g00 * (g22 - g12) - (g10 * g22 - g12 * g20) + g02 * (g10 - g20)) / sdet;
+    b2 = (g00 * (g11 - g21) - g01 * (g10 - g20) + (g10 * g21 - g11 * g20)) / sdet;
+  }
+  b0 = fminf(fmaxf(b0, -2.f), 3.f);
+  b1 = fminf(fmaxf(b1, -2.f), 3.f);
+  if (n_res == 3) b2 = fminf(fmaxf(b2, -2.f), 3.f);
+  const float ssum = b0 + b1 + (n_res == 3 ? b2 : 0.f);
+  if (fabsf(ssum) < 1e-6f) {
+    b0 = 1.f; b1 = 0.f; b2 = 0.f;
+  } else {
+    b0 /= ssum; b1 /= ssum; b2 = n_res == 3 ? b2 / ssum : 0.f;
+  }
+}
+
 // Block-wide sums of K (<= 8) values per thread; every thread receives the
 // totals.  `red` is shared scratch of 2 * 8 * 32 floats.  Consecutive calls
 // alternate halves of `red`, so one __syncthreads per call suffices: a thread
@@ -145,6 +188,24 @@ __device__ __forceinline__ float4 tanh4(float4 a) {
 __device__ __forceinline__ bool finite4(float4 a) {
   return isfinite(a.x) && isfinite(a.y) && isfinite(a.z) && isfinite(a.w);
 }
+
+// Packed fp32 FMA (sm_100 FFMA2: two lanes of fp32 per instruction issue),
+// each component rounded like fmaf.  AIDEEN_NO_FFMA2 builds the scalar form.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+#ifdef AIDEEN_NO_FFMA2
+  return make_float2(fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y));
+#else
+  return __ffma2_rn(a, b, c);
+#endif
+}
+__device__ __forceinline__ float4 fma4(float4 a, float4 b, float4 c) {
+  const float2 lo = fma2(make_float2(a.x, a.y), make_float2(b.x, b.y), make_float2(c.x, c.y));
+  const float2 hi = fma2(make_float2(a.z, a.w), make_float2(b.z, b.w), make_float2(c.z, c.w));
+  return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+// acc + a * b accumulated per component (a float4 dot product's partial sums)
+__device__ __forceinline__ float4 dot4_acc(float4 acc, float4 a, float4 b) { return fma4(a, b, acc); }
+__device__ __forceinline__ float hsum4(float4 a) { return (a.x + a.y) + (a.z + a.w); }
 
 // float2 counterparts (the Picard kernel's per-thread vectors)
 __device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }

@@ -372,7 +372,32 @@ __device__ __forceinline__ void mv2_32_to_d_tmem(uint32_t ta, const float *ina, 
   yb = b;
 }
 
-// (fast reciprocal: ~2 ulp, on the Picard write's dependency chain)
+// Forward Anderson step (type-II Anderson acceleration in the difference
+// form of Walker & Ni, SIAM J. Numer. Anal. 49(4), 2011): with residuals f_i
+// of the last n + 1 iterations and D_i = f_i - f_{i+1}, gamma minimises
+// |f_0 - sum_i gamma_i D_i|.  q = <D0,D0>, <D0,D1>, <D1,D1>, <D0,f0>, <D1,f0>
+// (n = 1 or 2), ridge 1e-3 * trace on the diagonal.  False (plain Picard
+// step) for a zero trace or any |gamma_i| > 20.
+__device__ __forceinline__ bool anderson_fwd_gamma(const float (&q)[5], int n, float &g0, float &g1) {
+  if (n == 1) {
+    const float tr = q[0];
+    if (!(tr > 0.f)) return false;
+    g0 = q[3] / (q[0] + 1e-3f * tr);
+    g1 = 0.f;
+  } else {
+    const float tr = q[0] + q[2];
+    if (!(tr > 0.f)) return false;
+    const float lam = 1e-3f * tr;
+    const float a = q[0] + lam, b = q[1], c = q[2] + lam;
+    const float det = a * c - b * b;
+    if (!(det > 0.f)) return false;
+    const float idet = 1.f / det;
+    g0 = (c * q[3] - b * q[4]) * idet;
+    g1 = (a * q[4] - b * q[3]) * idet;
+  }
+  return fmaxf(fabsf(g0), fabsf(g1)) <= 20.f;
+}
+
 // out[0..32) = Ma . x, out[32..64) = Mb . x for two d->32 matrices in TMEM.
 __device__ __forceinline__ void mv2_d_to_32_tmem(uint32_t ta, uint32_t tb, float2 x, float *out, float *part) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -643,6 +668,9 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
     // 1 / rms(dep) of the current iteration (one reciprocal instead of per-element divisions)
     float irr = rsqrtf(dep0_sq * inv_d + 1e-6f);
     float hq_sq = 0.f;
+    // forward Anderson ring: Picard outputs g and residuals f = g - x of the
+    // last two iterations of this token
+    float2 ag1 = f2(0.f), ag2 = f2(0.f), af1 = f2(0.f), af2 = f2(0.f);
     while (it < a.max_iters && !conv) {
       if constexpr (FPM) {
         if (it == 1) {
@@ -764,8 +792,24 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       // iteration's reduction barrier
       if (FPM && it == 0) st2(xs + j0, hn);
       float v2[3] = {dot2(dh, dh), dot2(dep_nx, dep_nx), dot2(hn, hn)};
-      if (FPM && it == 0) bsum<NW>(R, v2);
-      else {
+      // Anderson mixing from the third iteration on, over the residuals of
+      // iterations >= 1 (the map is fixed within the token from there); the
+      // slot's normal equations ride along in this iteration's reduction
+      const bool mix = a.anderson_m >= 2 && it >= 2;
+      const int n_res = it < a.anderson_m ? it : a.anderson_m;
+      float q5[5];
+      if (mix) {
+        const float2 D0 = dh - af1;
+        const float2 D1 = n_res == 3 ? af1 - af2 : f2(0.f);
+        float v7[7] = {v2[0], v2[1], dot2(D0, D0), dot2(D0, D1), dot2(D1, D1), dot2(D0, dh), dot2(D1, dh)};
+        bsum<NW>(R, v7);
+        v2[0] = v7[0];
+        v2[1] = v7[1];
+#pragma unroll
+        for (int q = 0; q < 5; ++q) q5[q] = v7[2 + q];
+      } else if (FPM && it == 0) {
+        bsum<NW>(R, v2);
+      } else {
         float v2b[2] = {v2[0], v2[1]};
         bsum<NW>(R, v2b);
         v2[0] = v2b[0];
@@ -781,6 +825,22 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
       // plateau = |err - prev| / max(prev, eps) <= 0.10, without the division
       const bool homeo = (it + 1 >= 4) && (err <= band) && (fabsf(err - prev) <= 0.10f * fmaxf(prev, a.eps));
       conv = strict || homeo;
+      if (mix && !conv) {
+        float g0, g1;
+        if (anderson_fwd_gamma(q5, n_res - 1, g0, g1)) {
+          // next iterate g_0 - sum gamma_i (g_i - g_{i+1}); its |dep|^2 needs
+          // one more reduction
+          hcur = hn - g0 * (hn - ag1) - g1 * (ag1 - ag2);
+          const float2 depm = sig + hcur + anc;
+          float v1[1] = {dot2(depm, depm)};
+          bsum<NW>(R, v1);
+          irr = rsqrtf(v1[0] * inv_d + 1e-6f);
+        }
+      }
+      af2 = af1;
+      af1 = dh;
+      ag2 = ag1;
+      ag1 = hn;
       prev = err;
       ++it;
       PT(1);

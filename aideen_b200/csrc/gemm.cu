@@ -1,8 +1,9 @@
 // Strided-batched fp32 GEMM on CUDA cores (exact fp32 FMA accumulation).
 //
-// Used for the slot projections and their weight gradients; every operand /
-// transposition pattern of the hot path is expressed through GemmArgs
-// (see kernels.cuh).
+// The fallback for operand shapes the tcgen05 kernels cannot describe with
+// TMA (strides or extents that are not 16-byte multiples); the hot path's
+// shapes never take it.  Also the comparator of the tensor-core GEMM
+// self-test (aideen_gemm_selftest).
 #include "kernels.cuh"
 
 namespace aideen {

@@ -59,6 +59,7 @@ struct PicardArgs {
   int n_resident;  // FPM matrices staged in shared memory (set by the launcher)
   int use_tmem;    // 1: rank-32 matrices in tensor memory (d = 512): 3..5, or 2..5 with push
   int push;        // 1: memory rows / read keys pushed into every peer's inbox by bulk copy
+  int anderson_m;  // forward Anderson residuals mixed: 0 (plain Picard), 2 or 3
   float eps, blend, alpha_m, tau, gate_min;
   const float *W;
   size_t off_ns, off_anchor, off_hscale, off_hbias, off_wkm, off_wqm, off_bread, off_wgate,
@@ -80,6 +81,7 @@ struct AdjointArgs {
   int max_ctas;                // SMs to use (0: every SM), at full occupancy each
   float *gpre;                 // [N][h][d]
   float *nsg;                  // [N][d] per-token NormScale-gradient partials or null
+  float *nsg_cta;              // [grid][d] per-CTA NormScale-gradient partials or null
   uint32_t spin_limit;         // bound of each stage wait (set by launch_adjoint)
 };
 // Reads and clears the adjoint's timeout flag (stream-ordered copy into host_flag).
@@ -108,7 +110,8 @@ cudaError_t launch_pool_rmsnorm(const float *hstar, const float *g, float *poole
 cudaError_t launch_solve_stats(const int32_t *iters, const float *hstar, int rows, int d,
                                int max_iters, unsigned long long *st4p, cudaStream_t st);
 
-cudaError_t launch_adjoint(const AdjointArgs &a, cudaStream_t st);
+// grid_out (optional): CTAs launched, i.e. the rows of nsg_cta written.
+cudaError_t launch_adjoint(const AdjointArgs &a, cudaStream_t st, int *grid_out = nullptr);
 cudaError_t launch_source_grad(const float *gpre, float *out, int N, int h, int d, cudaStream_t st);
 cudaError_t launch_attn_bwd_scale(const AttnBwdArgs &a, int rows, cudaStream_t st);
 cudaError_t launch_attn_bwd_softmax(const AttnBwdArgs &a, int N, cudaStream_t st);
@@ -158,6 +161,27 @@ cudaError_t launch_rmsnorm_bwd(const float *dy, const float *P, const float *lrm
                                const float *g, float *dl_dh, float *ggp, int N, int d,
                                cudaStream_t st);
 cudaError_t launch_sum(const float *x, int n, float *out, cudaStream_t st);
+
+// Sampled-softmax LM head and embedding update (lm_sampled.cu).
+// S[cap] <- sampled vocabulary of the targets (K = *K entries used), *active <-
+// valid target count (>= 1); err bit 1: candidate draws exhausted, bit 2: K > cap.
+cudaError_t launch_sample_set(const int32_t *tg, int N, int V, int num_samples, int max_samples,
+                              unsigned long long seed, uint32_t step, int32_t *S, int *K, float *active, int cap,
+                              unsigned int *err, cudaStream_t st);
+cudaError_t launch_gather_rows(const float *W, const int32_t *S, const int *K, int cap, int d, float *WS,
+                               cudaStream_t st);
+cudaError_t launch_softmax_sampled(float *logits, long ld, const float *b_lm, const int32_t *S, const int *K,
+                                   const int32_t *tg, int V, const float *active, float *loss_rows, int N,
+                                   cudaStream_t st);
+cudaError_t launch_lm_sampled_adam(float *W, float *b, float *M1, float *M2, size_t off_b, const float *dW,
+                                   const float *db, const int32_t *S, const int *K, int cap, int d, float *WS,
+                                   float lr, float b1, float b2, float eps, float bc1, float bc2, cudaStream_t st);
+int emb_csr_max_tokens();
+cudaError_t launch_emb_csr(const int32_t *tok, int N, int V, int32_t *uniq, int32_t *off, int32_t *pos, int *U,
+                           cudaStream_t st);
+cudaError_t launch_emb_adam(float *emb, float *M1, float *M2, const float *grad, const int32_t *uniq,
+                            const int32_t *off, const int32_t *pos, const int *U, int ucap, int d, float lr,
+                            float b1, float b2, float eps, float bc1, float bc2, cudaStream_t st);
 
 // FPM memory backward (fpm_bwd.cu).  Row-major [N][h][d] buffers, N = B*T
 // tokens in the library's token-major order (row t*B + b); v is the adjoint

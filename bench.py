@@ -2,11 +2,13 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-One step = embedding gather -> forward Picard solve with FPM memory (d_r=512,
-h_slots=8, ctx=256) -> dense LM-head CE -> clean Picard adjoint (Anderson m=4)
--> weight gradients -> [NCCL allreduce] -> Adam on DEQ core + LM head
-(+ spectral renorm every 4th step).  Per GPU: 8 sequences x 256 tokens of
-Zipf(1.1) ids over vocab 50257 (weak scaling: per-GPU work fixed).
+One step is the reference trainer's step: embedding gather -> forward Picard
+solve with FPM memory (d_r=512, h_slots=8, ctx=256) -> sampled-softmax LM head
+(num_samples 512) with its own Adam step -> clean Picard adjoint (Anderson m=4)
+-> weight gradients -> [NCCL allreduce] -> Adam on the DEQ core (+ spectral
+renorm every 4th step) -> Adam on the embedding rows of the step's tokens.  Per
+GPU: 8 sequences x 256 tokens of Zipf(1.1) ids over vocab 50257 (weak scaling:
+per-GPU work fixed).  --dense-lm times the dense full-vocabulary CE variant.
 
 `value` times the step with token ids already in HBM; `e2e` times the same
 step through the public C ABI from pinned host buffers (H2D of ids/targets and
@@ -31,6 +33,7 @@ sys.path.insert(0, ROOT)
 
 D, H, T, B_PER_GPU, VOCAB = 512, 8, 256, 8, 50257
 MAX_ITERS, ADJ_ITERS, ANDERSON_M = 20, 12, 4
+LM_SAMPLES = 512          # the reference's ArchitectureConfig num_samples default (state.rs:54)
 METRIC = "train tokens/s @d_r=512,h_slots=8,ctx=256"
 
 
@@ -125,17 +128,19 @@ def cpu_baseline(n_seq: int = B_PER_GPU):
     tok, tg = tok[:n_seq], tg[:n_seq]
     cfg = O.Cfg(d=D, h=H, fpm=True, max_iters=MAX_ITERS, adj_iters=ADJ_ITERS, anderson_m=ANDERSON_M)
     t0 = time.perf_counter()
-    O.train_step(emb[tok], tg, W, lm, cfg)
+    O.train_step(emb[tok], tg, W, lm, cfg, lm_samples=LM_SAMPLES, tokens=tok, emb=emb)
     dt = time.perf_counter() - t0
     return {"value": n_seq * T / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{n_seq} sequence(s) x {T} tokens of the d512/h8/vocab50257 step "
-                      f"(numpy float64 oracle, BLAS threads = host cores), {dt:.1f} s"}
+            "sample": f"{n_seq} sequence(s) x {T} tokens of the d512/h8/vocab50257 reference step "
+                      f"(sampled LM head, embedding update; numpy float64 oracle, BLAS threads = host "
+                      f"cores), {dt:.1f} s"}
 
 
 def adjoint_micro(torch, hbm, src, device):
     """isolated clean adjoint on a given fixed point, B*T = 16384
-    tokens x 8 slots x d 512, h* and upstream dL/dh ~ N(0,1) per slot, 20 iterations,
-    through the C ABI with device pointers (inputs resident in HBM, each 268 MB > L2)."""
+    tokens x 8 slots x d 512, h* and branch ~ N(0,1), per-slot RHS ~ N(0,1), exactly 20
+    iterations, through the C ABI with device pointers (inputs resident in HBM, each
+    268 MB > L2).  Algorithmic bytes 16*E*d (h*, branch, RHS in; v out)."""
     from aideen_b200.backend import GpuDeqBackend
     from aideen_b200.weights import init_all_weights
     n_tok, iters = 16384, 20
@@ -167,11 +172,81 @@ def adjoint_micro(torch, hbm, src, device):
     be.close()
     ms = kp[0] / max(kp[1], 1)
     E = n_tok * H
-    nbytes = 4 * (5 * E * D + n_tok * D)  # h*, branch, rhs in; v, g_pre out; NormScale partials out
+    nbytes = 16 * E * D          # 4 tensors of E*d floats: h*, branch, RHS in; v out
+    moved = 4 * (5 * E * D)      # + the g_pre output the weight gradients read
     ach = nbytes / (ms / 1e3) / 1e9
     return {"kernel": "adjoint_kernel<F=4, m=0>", "workload": "16384 tokens x 8 slots x 512, 20 iterations",
             "bound": "hbm", "achieved": ach, "peak": hbm, "peak_source": src, "unit": "GB/s",
-            "frac": ach / hbm, "ms_per_launch": ms, "algorithmic_bytes_per_launch": nbytes}
+            "frac": ach / hbm, "ms_per_launch": ms, "algorithmic_bytes_per_launch": nbytes,
+            "bytes_moved_per_launch": moved,
+            "traffic": None,
+            "note": "algorithmic bytes per the 16*E*d definition; the kernel also writes g_pre (E*d) and "
+                    "per-CTA NormScale partials, which the weight gradients read"}
+
+
+def weight_grad_micro(torch, device):
+    """configs[3]'s second half: the weight-gradient accumulation into every
+    per-slot W_q, W_k, W_v (32-column heads), W_o (32-row heads) and W_in of an
+    N = 16384-token step (64 sequences x 256 tokens, FPM off), after its forward
+    and a 20-iteration adjoint.  Algorithmic FLOPs h*(2*N*d^2 + 4*2*N*d*32) =
+    85.9 GFLOP; timed as the GEMM class of aideen_weight_grads (which also holds
+    the backward GEMMs dn and dsrc, so the figure is conservative)."""
+    from aideen_b200.backend import GpuDeqBackend, RunConfig
+    from aideen_b200.weights import init_all_weights
+    Bm, Tm = 64, 256
+    N = Bm * Tm
+    be = GpuDeqBackend(D, H, max_batch=Bm, max_seq_len=Tm, device=device)
+    be.upload_weights(init_all_weights(D, H, seed=0, attn_sigma=0.8, win_sigma=0.8))
+    rng = np.random.default_rng(0)
+    S = rng.uniform(-1, 1, (Bm, Tm, D)).astype(np.float32)
+    dl = rng.standard_normal((N, D)).astype(np.float32)
+    be.run_forward_deq_no_readback(S, Bm, Tm, RunConfig(max_iters=12, fpm=False))
+    be.run_staged_adjoint_picard_no_readback(0.85, 20, dl_dh=dl)
+    be.weight_grads()
+    be.sync()
+    be.profile(True)
+    be.profile_read(reset=True)
+    reps = 5
+    for _ in range(reps):
+        be.weight_grads()
+    kp = be.profile_read(reset=True)
+    be.close()
+    ms = kp["gemm"][0] / reps
+    flops = H * (2 * N * D * D + 4 * 2 * N * D * 32)
+    tf, tsrc = peaks_tensor()
+    tf32 = tf / 2.0
+    ach = flops / (ms / 1e3) / 1e12
+    return {"kernels": "tcgemm_kernel (3xTF32 tcgen05)", "workload": "N=16384 tokens x 8 slots x 512",
+            "algorithmic_flops": flops, "ms": ms, "achieved_tflops": ach, "tf32_peak": tf32,
+            "peak_source": "half of " + tsrc, "tensor_util_of_tf32": ach / tf32,
+            "note": "fp32-accurate 3xTF32 issues 3 tf32 MMAs per algorithmic product, so 1/3 of "
+                    "the TF32 rate is the ceiling of this accounting"}
+
+
+def configs1_step(device, steps=20, warmup=3):
+    """one sequence of 256 tokens, Anderson-accelerated forward
+    (3 residuals, max 20 iterations, tol 1e-4), Anderson adjoint, sampled LM head,
+    embedding update: train tokens/s through the C ABI from host ids."""
+    import torch
+    from aideen_b200.backend import GpuDeqBackend, RunConfig, HOST
+    from aideen_b200.weights import init_all_weights, init_embedding, init_lm_head
+    be = GpuDeqBackend(D, H, max_batch=1, max_seq_len=T, vocab=VOCAB, device=device)
+    be.upload_weights(init_all_weights(D, H, seed=0))
+    be.upload_lm_head(*init_lm_head(D, VOCAB))
+    be.upload_embedding(init_embedding(D, VOCAB))
+    tok, tg = make_tokens(0, 1)
+    rc = RunConfig(max_iters=MAX_ITERS, fpm=True, anderson_m=3)
+    for k in range(warmup + steps):
+        if k == warmup:
+            be.sync()
+            t0 = time.perf_counter()
+        be.train_step(tok, tg, 1, T, rc, adj_iters=ADJ_ITERS, anderson_m=ANDERSON_M, step=k + 1,
+                      lm_samples=LM_SAMPLES, emb_update=1)
+    be.sync()
+    dt = (time.perf_counter() - t0) / steps
+    be.close()
+    return {"workload": "configs[1]: 1 x 256 tokens, Anderson forward (3 residuals)", "tokens_per_s": T / dt,
+            "ms_per_step": dt * 1e3, "timing": "host wall clock around synchronous C-ABI steps (loss read back)"}
 
 
 def run_reference(args, rank, world):
@@ -197,11 +272,13 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-micro", action="store_true", help="skip the isolated-adjoint microbenchmark")
+    ap.add_argument("--no-micro", action="store_true", help="skip the configs[1] / configs[3] extras")
+    ap.add_argument("--dense-lm", action="store_true",
+                    help="time the dense full-vocabulary CE head instead of the reference's sampled softmax")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -209,7 +286,7 @@ def main():
     if args.impl == "reference":
         return run_reference(args, rank, world)
 
-    # load the library (and the CUDA toolkit's cuBLAS it links) before torch
+    # load the library (it links the CUDA runtime and NCCL) before torch
     from aideen_b200.backend import DEVICE, HOST, GpuDeqBackend, RunConfig, load_library
     load_library()
     import torch
@@ -239,27 +316,26 @@ def main():
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MB > L2
     gs = 1.0 / world
     step_no = [0]
+    lm_samples = 0 if args.dense_lm else LM_SAMPLES
+    emb_update = 0 if args.dense_lm else 1
 
-    def step(where):
+    def step(where, lm=None):
         step_no[0] += 1
         renorm = step_no[0] % 4 == 0
-        if where == DEVICE:
-            return be.train_step(tok_d.data_ptr(), tg_d.data_ptr(), B_PER_GPU, T, rc, adj_iters=ADJ_ITERS,
-                                 anderson_m=ANDERSON_M, step=step_no[0], renorm=renorm,
-                                 allreduce=world > 1, grad_scale=gs, where=DEVICE, want_loss=False,
-                                 raw_ptr=True)
-        return be.train_step(tok_h.data_ptr(), tg_h.data_ptr(), B_PER_GPU, T, rc, adj_iters=ADJ_ITERS,
-                             anderson_m=ANDERSON_M, step=step_no[0], renorm=renorm,
-                             allreduce=world > 1, grad_scale=gs, where=HOST, want_loss=True,
-                             raw_ptr=True)
+        ns = lm_samples if lm is None else lm
+        ptrs = (tok_d.data_ptr(), tg_d.data_ptr()) if where == DEVICE else (tok_h.data_ptr(), tg_h.data_ptr())
+        return be.train_step(*ptrs, B_PER_GPU, T, rc, adj_iters=ADJ_ITERS, anderson_m=ANDERSON_M,
+                             step=step_no[0], renorm=renorm, allreduce=world > 1, grad_scale=gs, where=where,
+                             want_loss=where != DEVICE, raw_ptr=True, lm_samples=ns,
+                             emb_update=emb_update if ns else 0)
 
     for _ in range(args.warmup):
         step(DEVICE)
     torch.cuda.synchronize()
 
-    def timed(where):
-        # One timed region over all K steps, so the LM-head update the library
-        # defers to its side stream (it overlaps the next step's forward) is
+    def timed(where, steps, lm=None):
+        # One timed region over all K steps, so work the library defers to its
+        # side stream (the dense head's update overlaps the next forward) is
         # counted; the L2 flush between consecutive steps sits inside the region
         # and its time counts against the steps.
         if world > 1:
@@ -269,11 +345,11 @@ def main():
             flush.zero_()
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record(stream)
-        for k in range(args.steps):
+        for k in range(steps):
             if k:
                 with torch.cuda.stream(stream):
                     flush.zero_()
-            step(where)
+            step(where, lm)
         be.join()
         with torch.cuda.stream(stream):
             e.record(stream)
@@ -287,12 +363,38 @@ def main():
 
     l0 = be.launch_count
     with ClockSampler(local) as clk:
-        ms = timed(DEVICE)
+        ms = timed(DEVICE, args.steps)
     launches = (be.launch_count - l0) // args.steps
-    ms_e2e = timed(HOST)
+    ms_e2e = timed(HOST, args.steps)
     tokens = world * B_PER_GPU * T * args.steps
     value = tokens / (ms / 1e3)
     e2e = tokens / (ms_e2e / 1e3)
+    # the dense full-vocabulary head (the previous default), for comparison
+    dense = None
+    if not args.dense_lm:
+        nd = max(10, args.steps // 10)
+        for _ in range(3):
+            step(DEVICE, 0)
+        msd = timed(DEVICE, nd, 0)
+        dense = {"value": world * B_PER_GPU * T * nd / (msd / 1e3), "unit": "tokens/s", "steps": nd,
+                 "ms_per_step": msd / nd, "note": "same step with the dense full-vocabulary CE head "
+                 "(LM-head gradients in the common Adam step, pipelined schedule), no embedding update"}
+
+    # data parallel: every rank must hold the same weights after the timed steps
+    agree = None
+    if world > 1:
+        be.sync()
+        wsum = np.float64(be.read_weights().astype(np.float64).sum())
+        lw, lb, lg = be.read_lm_head()
+        lsum = np.float64(lw.astype(np.float64).sum() + lb.sum() + lg.sum())
+        esum = np.float64(be.read_embedding().astype(np.float64).sum())
+        t = torch.tensor([wsum, lsum, esum], device="cuda", dtype=torch.float64)
+        tmax, tmin = t.clone(), t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tmin, op=dist.ReduceOp.MIN)
+        agree = {"core_checksum": float(wsum), "lm_checksum": float(lsum), "emb_checksum": float(esum),
+                 "max_spread_over_ranks": float((tmax - tmin).abs().max().item()),
+                 "identical": bool(torch.equal(tmax, tmin))}
 
     # per-kernel-class device time of the same step (profiled, outside the timed region)
     be.profile(True)
@@ -309,25 +411,10 @@ def main():
     # algorithmic bytes of the Picard solve per launch: signal + attention injection in,
     # h*, pre, FPM memory and FPM context out (the rank-32 FPM weights are read once).
     picard_bytes = 4 * 6 * E * D + 4 * 6 * H * D * 32
-    adj_bytes = 4 * (3 * E * D + 2 * N * D)  # pre in; v, g_pre out; dl_dh in; NormScale partials out
+    adj_bytes = 4 * (3 * E * D + 2 * N * D)  # pre in; v, g_pre out; dl_dh in (per-CTA partials are small)
     bytes_of = {"picard": picard_bytes, "adjoint": adj_bytes}
-    # algorithmic fp32 GEMM FLOPs of one step (LM head + slot projections + weight grads)
-    hd32 = H * 32
-    gemm_flops = (3 * 2 * N * D * VOCAB                      # logits, dy, dW_lm
-                  + 2 * 2 * N * D * D * H                     # signal, gW_in
-                  + 3 * 2 * N * D * hd32 * 2                  # K/V/Q heads and their weight grads
-                  + 2 * N * hd32 * D * 5)                     # attn out, gW_o, dn, 3x dsrc
     roof = None
-    if dominant == "gemm":
-        kms = kprof["gemm"][0]
-        tf, tsrc = peaks_tensor()
-        ach = gemm_flops / (kms / 1e3) / 1e12
-        roof = {"kernel": "tcgemm_kernel (3xTF32 tcgen05 GEMM) + CUDA-core GEMMs with column bias",
-                "bound": "tensor", "achieved": ach, "peak": tf, "peak_source": tsrc, "unit": "TFLOP/s",
-                "frac": ach / tf, "traffic": None, "ms_per_step": kms, "algorithmic_flops_per_step": gemm_flops,
-                "note": "fp32-accurate 3xTF32: each algorithmic FLOP costs 3 tf32 MMA FLOPs, and tf32 runs "
-                        "at half the bf16 rate, so the ceiling is peak/6"}
-    elif dominant in bytes_of:
+    if dominant in bytes_of:
         kms = kprof[dominant][0] / max(kprof[dominant][1], 1)
         ach = bytes_of[dominant] / (kms / 1e3) / 1e9
         roof = {"kernel": {"picard": "picard_kernel<FPM> (token-serial Picard solve + FPM scan)",
@@ -338,27 +425,54 @@ def main():
                 "note": (f"latency-bound serial chain: {T} tokens per launch, {1e3 * kms / T:.2f} us per token "
                          f"(all slots of a sequence advance one token together; ~20 barrier-separated phases "
                          f"per token); HBM is not the limit") if dominant == "picard" else ""}
+    else:
+        roof = {"kernel": dominant, "ms_per_step": kprof[dominant][0], "bound": None, "achieved": None,
+                "peak": None, "unit": None, "frac": None, "traffic": None}
+    # the slot-projection and weight-gradient GEMMs of one step (LM head and FPM
+    # backward excluded): signal and its W_in gradient, the K/V/Q heads and their
+    # gradients, the W_o head and its gradient, dn and the three dsrc GEMMs
+    hd32 = H * 32
+    proj_flops = (2 * 2 * N * D * D * H                   # signal, gW_in
+                  + 3 * 2 * N * D * hd32 * 2              # K/V/Q heads and their weight grads
+                  + 2 * N * hd32 * D * 5)                 # attn out, gW_o, dn, 3x dsrc
+    tf, tsrc = peaks_tensor()
+    gms = kprof["gemm"][0]
+    gach = proj_flops / (gms / 1e3) / 1e12
+    roof_gemm = {"kernels": "tcgemm_kernel (3xTF32 tcgen05)", "algorithmic_flops_per_step": proj_flops,
+                 "ms_per_step": gms, "achieved_tflops": gach, "tf32_peak": tf / 2, "peak_source": "half of " + tsrc,
+                 "frac_of_tf32": gach / (tf / 2),
+                 "note": "profiled pass, one launch after another; 3xTF32 issues 3 tf32 MMAs per "
+                         "algorithmic product (ceiling 1/3 of the TF32 rate in this accounting)"}
     c4 = adjoint_micro(torch, hbm, src, local) if world == 1 and not args.no_micro else None
+    c4g = weight_grad_micro(torch, local) if world == 1 and not args.no_micro else None
+    c1 = configs1_step(local) if world == 1 and not args.no_micro else None
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (Zipf(1.1) token ids, seeded; random-init weights)",
-                "config": {"workload": "DEQ+FPM train step (BASELINE configs[2] per-GPU shard)",
+                "config": {"workload": "DEQ+FPM train step (BASELINE configs[2] per-GPU shard), the reference's "
+                                       + ("dense-CE variant" if args.dense_lm else
+                                          "full step: sampled-softmax LM head (num_samples 512) with its Adam "
+                                          "step, embedding-row Adam update"),
                            "d_r": D, "h_slots": H, "ctx": T, "batch_per_gpu": B_PER_GPU,
-                           "global_batch": B_PER_GPU * world, "vocab": VOCAB,
+                           "global_batch": B_PER_GPU * world, "vocab": VOCAB, "lm_samples": lm_samples,
                            "max_iters": MAX_ITERS, "adj_iters": ADJ_ITERS, "anderson_m": ANDERSON_M,
                            "parallelism": f"dp{world}", "l2": "256 MB buffer written before every step, inside the timed region"},
                 "e2e": {"value": e2e, "unit": "tokens/s",
                         "h2d_bytes_per_step": int(tok.nbytes + tg.nbytes), "d2h_bytes_per_step": 4},
                 "gpu_launches": int(launches),
                 "roofline": roof,
+                "roofline_gemm_proj": roof_gemm,
                 "kernel_ms_per_step": {k: round(v[0], 4) for k, v in kprof.items()},
                 "kernel_ms_note": "per-class device time from a profiled pass (CUDA events around each launch), "
-                                  "which runs the step's kernels one after another; the timed steps overlap "
-                                  "the Picard token chunks with the LM head and adjoint",
+                                  "which runs the step's kernels one after another",
+                "dense_lm": dense,
                 "roofline_adjoint_c4": c4,
+                "weight_grads_c4": c4g,
+                "configs1": c1,
+                "weights_agree": agree,
                 "clocks": clk.summary()}
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline()

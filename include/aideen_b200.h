@@ -70,6 +70,12 @@ typedef struct aideen_run {
   float fpm_alpha_m;
   float fpm_tau;
   float fpm_read_gate_min;
+  /* Anderson acceleration of each (sequence, slot) Picard solve (no
+   * counterpart in the reference forward): 0 or 1 = plain Picard; 2 or 3 =
+   * type-II Anderson over the last 2 or 3 residuals f = G(h) - h of the slot's
+   * d-vector, from the third iteration on (the residuals of iterations >= 1,
+   * whose map is fixed within the token).  The stop rule is unchanged. */
+  uint32_t anderson_m;
 } aideen_run;
 
 /* Forward convergence statistics (DebugLog[13..17] equivalents). */
@@ -124,6 +130,10 @@ uint64_t aideen_launch_count(const aideen_ctx *ctx);
  * clocks).  When enabled, every launch is bracketed by CUDA events on the
  * context's stream; aideen_profile_read synchronises and returns cumulative
  * milliseconds and launch counts per class. */
+/* Classes: Picard solve; adjoint; GEMMs of the slot projections and weight
+ * gradients; every kernel of the LM head (its GEMMs, softmax, reductions, and
+ * the sampled head's Adam step); the optimizer sweeps; the FPM backward (its
+ * GEMMs included); everything else. */
 enum { AIDEEN_PROF_PICARD = 0, AIDEEN_PROF_ADJOINT = 1, AIDEEN_PROF_GEMM = 2,
        AIDEEN_PROF_LM_SOFTMAX = 3, AIDEEN_PROF_OPTIMIZER = 4, AIDEEN_PROF_OTHER = 5,
        AIDEEN_PROF_FPM_BWD = 6, AIDEEN_PROF_CLASSES = 7 };
@@ -143,6 +153,9 @@ int aideen_upload_lm_head(aideen_ctx *ctx, const float *w_lm, const float *b_lm,
                           const float *g_lm);
 int aideen_download_lm_head(aideen_ctx *ctx, float *w_lm, float *b_lm, float *g_lm);
 int aideen_upload_embedding(aideen_ctx *ctx, const float *emb /*[vocab][d]*/);
+/* Embedding table back to the host (GpuEmbeddingTrainer's weights readback,
+ * gpu_embedding.rs weights_buffer). */
+int aideen_download_embedding(aideen_ctx *ctx, float *emb /*[vocab][d]*/);
 /* Zero the carried FPM memory MState (reset_state gpu_deq.rs:3127). */
 int aideen_reset_state(aideen_ctx *ctx);
 /* Zero the Adam moments of the DEQ core and LM head. */
@@ -196,6 +209,21 @@ typedef struct aideen_step_args {
   uint32_t anderson_m;
   aideen_update update;
   uint32_t renorm;           /* 1 = spectral renorm after the update (reference thresholds) */
+  /* LM head: 0 = dense full-vocabulary CE, its gradients in the common update;
+   * > 0 = the reference's sampled softmax with this num_samples (ArchitectureConfig
+   * default 512, state.rs:54): the step's sampled vocabulary (distinct targets
+   * plus deterministic candidates, up to min(max(num_samples, B*T), vocab, 2048),
+   * gpu_lm_head.rs:244-281), softmax over it, and its own Adam step on the
+   * sampled rows with dW, db clamped to +-0.1 before dL/dh is formed from the
+   * updated rows (lm_train.wgsl:79-395; g_lm is not trained). */
+  uint32_t lm_samples;
+  /* Embedding rows of the step's tokens: 0 = frozen; 1 = Adam on the mean
+   * dL/dpooled row of each distinct token (the reference trainer's default
+   * source, trainer.rs:3285-3289; embedding_train.wgsl:100-147); 2 = the same
+   * from the exact dL/dS_in. */
+  uint32_t emb_update;
+  float emb_lr;              /* embedding learning rate (0 = update.lr) */
+  uint64_t sample_seed;      /* 0 = the reference's default seed 0xA1DEEE5A4D5EED5E */
 } aideen_step_args;
 int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *args, const int32_t *tokens,
                       const int32_t *targets, int where, float *loss_out /*host, nullable*/,
@@ -221,7 +249,11 @@ enum aideen_buf {
   AIDEEN_BUF_LM_GRADS = 14, /* [vocab*d + vocab + d] */
   AIDEEN_BUF_PRE = 15,      /* [N][h][d] pre = branch + h* of the adjoint */
   AIDEEN_BUF_FPM_DM = 16,   /* [N][h][d] dL/dM[t] of the last FPM backward (fpm_dm_buf) */
-  AIDEEN_BUF_FPM_CARRY = 17 /* [max_batch][h][d] FPM TBPTT carry (tbptt_carry_buf) */
+  AIDEEN_BUF_FPM_CARRY = 17, /* [max_batch][h][d] FPM TBPTT carry (tbptt_carry_buf) */
+  AIDEEN_BUF_LM_SAMPLES = 18  /* int32 sampled vocabulary of the last sampled LM head, ascending
+                               * (last_sampled_indices, gpu_lm_head.rs:2604); with it the
+                               * LM_GRADS buffer holds the sampled rows' dW [K][d] and, at
+                               * offset vocab*d, db [K] */
 };
 /* Copies the first n_elems elements (4 bytes each) of a buffer to host dst,
  * token rows in the caller's order (row b*T + t). */

@@ -313,7 +313,8 @@ def forward(S_in, W, cfg: Cfg, mstate=None) -> ForwardOut:
         active = np.ones((B, h), bool)
         prev = np.ones((B, h))
         it_count = np.zeros((B, h), np.int64)
-        h1 = h2 = h3 = None    # Picard outputs 1, 2, 3 iterations ago (Anderson ring)
+        # Anderson ring: Picard outputs g and residuals f of the last two iterations
+        g1 = g2 = f1 = f2 = None
         for it in range(cfg.max_iters):
             if not active.any():
                 break
@@ -329,23 +330,25 @@ def forward(S_in, W, cfg: Cfg, mstate=None) -> ForwardOut:
             err = np.sqrt(np.mean(dh * dh, -1) + 1e-12) / np.maximum(r, 1e-6)
             conv = _converged(err, prev, it, cfg.eps)
             hnext = hn
-            if am >= 3 and it >= 2:
-                # type-II Anderson mixing of the slot's iterate, the adjoint's
-                # mixing rule (staged_adjoint_picard_clean.wgsl:1022-1135) applied
-                # per (sequence, slot) solve: each slot's fixed-point problem is
-                # independent once the token's iteration-0 inputs are fixed
-                n_res = min(it, am - 1)
-                D = [hn - h1, h1 - h2] + ([h2 - h3] if n_res == 3 else [])
-                G = np.zeros((B, h, 3, 3))
-                for i in range(n_res):
-                    for j in range(i, n_res):
-                        G[..., i, j] = G[..., j, i] = (D[i] * D[j]).sum(-1)
-                beta = _anderson_coefs(G, n_res)
-                mixed = beta[..., 0, None] * hn + beta[..., 1, None] * h1
+            f0 = hn - hcur
+            if am >= 2 and it >= 2:
+                # Anderson (type II) over the residuals f = g(x) - x of the
+                # iterations >= 1, whose map is fixed within the token
+                n_res = min(it, am)
+                D = [f0 - f1] + ([f1 - f2] if n_res == 3 else [])
+                DtD = np.zeros((B, h, 2, 2))
+                Dtf = np.zeros((B, h, 2))
+                for i in range(n_res - 1):
+                    Dtf[..., i] = (D[i] * f0).sum(-1)
+                    for j in range(i, n_res - 1):
+                        DtD[..., i, j] = DtD[..., j, i] = (D[i] * D[j]).sum(-1)
+                gam, ok = anderson_fwd_gamma(DtD, Dtf, n_res - 1)
+                mixed = hn - gam[..., 0, None] * (hn - g1)
                 if n_res == 3:
-                    mixed = mixed + beta[..., 2, None] * h2
-                hnext = np.where(conv[..., None], hn, mixed)
-            h3, h2, h1 = h2, h1, hn
+                    mixed = mixed - gam[..., 1, None] * (g1 - g2)
+                hnext = np.where((conv | ~ok)[..., None], hn, mixed)
+            f2, f1 = f1, f0
+            g2, g1 = g1, hn
             hcur = np.where(active[..., None], hnext, hcur)
             prev = np.where(active, err, prev)
             it_count = it_count + active
@@ -402,6 +405,115 @@ def lm_head(pooled, targets, w_lm, b_lm, g_lm):
     return loss, dP, gW, gb, gg
 
 
+LM_SAMPLE_SEED = 0xA1DEEE5A4D5EED5E   # gpu_lm_head.rs:1492-1494 default
+LM_MAX_SAMPLES = 2048                 # MAX_SHADER_SAMPLES, gpu_lm_head.rs:247
+_M64 = (1 << 64) - 1
+
+
+def sample_candidate(seed, step_t, draw, vocab):
+    """`deterministic_sample_candidate` (gpu_lm_head.rs:213-223): the seed mixed
+    with the step and the draw index, then the splitmix64 finaliser."""
+    x = (seed ^ ((step_t * 0x9E3779B97F4A7C15) & _M64) ^ ((draw * 0xD1B54A32D192ED03) & _M64)) & _M64
+    x ^= x >> 30
+    x = (x * 0xBF58476D1CE4E5B9) & _M64
+    x ^= x >> 27
+    x = (x * 0x94D049BB133111EB) & _M64
+    x ^= x >> 31
+    return x % vocab
+
+
+def sampled_indices(targets, step_t, vocab, num_samples=512, seed=LM_SAMPLE_SEED):
+    """`build_sampled_indices` (gpu_lm_head.rs:244-281): the distinct valid
+    targets, filled with deterministic candidates in draw order (skipping ones
+    already present) up to min(max(num_samples, len(targets)), vocab, 2048),
+    sorted ascending.  (The reference's buffer capacity, at least 1024 x batch,
+    never binds at these sizes.)"""
+    tg = [int(t) for t in np.asarray(targets).ravel()]
+    desired = min(max(num_samples, len(tg)), vocab, LM_MAX_SAMPLES)
+    S = sorted({t for t in tg if 0 <= t < vocab})
+    seen = set(S)
+    draw = 0
+    while len(S) < desired:
+        c = sample_candidate(seed, step_t, draw, vocab)
+        draw += 1
+        if c not in seen:
+            seen.add(c)
+            S.append(c)
+    return np.array(sorted(S), np.int64)
+
+
+def lm_head_sampled(pooled, targets, w_lm, b_lm, g_lm, S, state, step, lr=1e-3, b1=0.9, b2=0.999,
+                    eps=1e-8):
+    """Sampled-softmax LM head with its fused Adam step, in the reference's
+    order (`lm_train.wgsl`): lm_probs_main (:79-217) -> lm_update_main (:224-290,
+    dW and db clamped to +-0.1 after the 1/active scaling, Adam on the sampled
+    rows only) -> lm_backprop_h_t_main (:327-395, dL/dh from the *updated*
+    rows, through the RMSNorm).  g_lm is not trained here.
+
+    state: dict of Adam moments mW, vW [V,d], mb, vb [V] (updated in place).
+    Returns loss (mean over valid targets), dL/dpooled [N,d], new W_lm, new
+    b_lm, and the unclamped sampled-row gradients dW [K,d], db [K].
+    """
+    P = np.asarray(pooled, np.float64)
+    W = np.asarray(w_lm, np.float64).copy()
+    b = np.asarray(b_lm, np.float64).copy()
+    g = np.asarray(g_lm, np.float64)
+    N, d = P.shape
+    V = W.shape[0]
+    tg = np.asarray(targets).astype(np.int64).ravel()
+    valid = (tg >= 0) & (tg < V)
+    active = max(1, int(valid.sum()))
+    r = np.sqrt(np.mean(P * P, -1) + 1e-5)
+    y = P / r[:, None] * g[None]
+    logits = y @ W[S].T + b[S][None]
+    mx = logits.max(-1, keepdims=True)
+    e = np.exp(logits - mx)
+    p = e / np.maximum(e.sum(-1, keepdims=True), 1e-10)
+    onehot = (S[None, :] == tg[:, None]).astype(np.float64)
+    pt = (p * onehot).sum(-1)
+    loss = float(-(np.log(np.maximum(pt[valid], 1e-10))).sum()) / active
+    coef = (p - onehot) * valid[:, None] / active
+    dW_raw, db_raw = coef.T @ y, coef.sum(0)
+    dW = np.clip(dW_raw, -0.1, 0.1)
+    db = np.clip(db_raw, -0.1, 0.1)
+    t = max(1, step)
+    bc1, bc2 = 1 - b1 ** t, 1 - b2 ** t
+    for (w_arr, m_key, v_key, gr) in ((W, "mW", "vW", dW), (b, "mb", "vb", db)):
+        m = state[m_key][S] * b1 + (1 - b1) * gr
+        v = state[v_key][S] * b2 + (1 - b2) * gr * gr
+        state[m_key][S] = m
+        state[v_key][S] = v
+        w_arr[S] -= lr * (m / bc1) / (np.sqrt(v / bc2) + eps)
+    dldy = coef @ W[S]
+    dot = (dldy * g[None] * P).sum(-1)
+    dP = dldy * g[None] / r[:, None] - P * (dot / (d * r ** 3))[:, None]
+    return loss, dP, W, b, dW_raw, db_raw
+
+
+def embedding_update(emb, tokens, grad_rows, state, step, lr=1e-3, b1=0.9, b2=0.999, eps=1e-8):
+    """`apply_embedding_update_from_buffer` (gpu_embedding.rs:775-857) with
+    `embedding_adamw_update` (embedding_train.wgsl:100-147): per distinct token
+    (ids clamped to vocab - 1, `build_unique_token_csr` gpu_embedding.rs:47-70)
+    the mean of its positions' gradient rows, then Adam on that row only.
+    state: dict with m, v [V,d] (updated in place).  Returns the new table."""
+    E = np.asarray(emb, np.float64).copy()
+    V = E.shape[0]
+    tok = np.minimum(np.asarray(tokens).astype(np.int64).ravel(), V - 1)
+    G = np.asarray(grad_rows, np.float64)
+    uniq, inv = np.unique(tok, return_inverse=True)
+    sums = np.zeros((len(uniq), E.shape[1]))
+    np.add.at(sums, inv, G)
+    cnt = np.bincount(inv, minlength=len(uniq)).astype(np.float64)
+    gr = sums / cnt[:, None]
+    t = max(1, step)
+    m = state["m"][uniq] * b1 + (1 - b1) * gr
+    v = state["v"][uniq] * b2 + (1 - b2) * gr * gr
+    state["m"][uniq] = m
+    state["v"][uniq] = v
+    E[uniq] -= lr * (m / (1 - b1 ** t)) / (np.sqrt(v / (1 - b2 ** t)) + eps)
+    return E
+
+
 # ---------------------------------------------------------------------------
 # adjoint
 # ---------------------------------------------------------------------------
@@ -444,6 +556,38 @@ def adjoint(hstar, branch, rhs_tok, NS, cfg: Cfg, rhs_slot=None):
             if k >= 2 and n_res >= 2:
                 v = _anderson_mix(hist, k, m, n_res)
     return v, norm_grad(v), pre, r
+
+
+def anderson_fwd_gamma(A, rhs, n):
+    """Forward Anderson step (no counterpart in the reference forward).
+
+    Type-II Anderson acceleration in the difference form of Walker & Ni
+    (SIAM J. Numer. Anal. 49(4), 2011): with residuals f_i = g(x_i) - x_i of
+    the last n + 1 iterations and differences D_i = f_i - f_{i+1}, gamma
+    minimises |f_0 - sum_i gamma_i D_i| (normal equations A gamma = rhs,
+    A = D^T D [..., 2, 2], rhs = D^T f_0 [..., 2], n = 1 or 2), regularised with
+    1e-3 * trace(A) on the diagonal; the next iterate is
+    g_0 - sum_i gamma_i (g_i - g_{i+1}).  Returns (gamma [..., 2], ok): ok is
+    False (plain Picard step) for a zero trace or any |gamma_i| > 20.
+    """
+    if n == 1:
+        tr = A[..., 0, 0]
+        ok = tr > 0
+        a = A[..., 0, 0] + 1e-3 * tr
+        gam = np.zeros(A.shape[:-2] + (2,))
+        gam[..., 0] = rhs[..., 0] / np.where(ok, a, 1.0)
+    else:
+        tr = A[..., 0, 0] + A[..., 1, 1]
+        ok = tr > 0
+        lam = 1e-3 * tr
+        a, b, c = A[..., 0, 0] + lam, A[..., 0, 1], A[..., 1, 1] + lam
+        det = a * c - b * b
+        ok &= det > 0
+        idet = 1.0 / np.where(ok, det, 1.0)
+        gam = np.stack([(c * rhs[..., 0] - b * rhs[..., 1]) * idet,
+                        (a * rhs[..., 1] - b * rhs[..., 0]) * idet], -1)
+    ok &= np.abs(gam).max(-1) <= 20.0
+    return gam, ok
 
 
 def _anderson_coefs(G, n_res):
@@ -752,8 +896,17 @@ def branch_of(fwd: ForwardOut, W, cfg: Cfg):
 
 
 def train_step(S_in, targets, W, lm, cfg: Cfg, adam_state=None, step=1, lr=1e-3,
-               mstate=None, fpm_carry=None):
-    """Forward -> LM-head CE -> adjoint -> weight grads -> Adam (DEQ core and LM head).
+               mstate=None, fpm_carry=None, lm_samples=0, sample_seed=LM_SAMPLE_SEED,
+               lm_state=None, tokens=None, emb=None, emb_state=None, emb_grad="dl_dh"):
+    """Forward -> LM head -> adjoint -> weight grads -> Adam (DEQ core and LM head).
+
+    lm_samples = 0: dense full-vocabulary CE; the LM-head gradients join the
+    common Adam step.  lm_samples > 0: the reference's sampled-softmax head with
+    its own fused Adam step inside the LM stage (`lm_head_sampled`, sampled set
+    from `sampled_indices`).  With `emb` and `tokens`, the embedding rows of the
+    step's tokens get the reference's Adam update (`embedding_update`) from
+    the LM head's dL/dpooled rows (emb_grad="dl_dh", trainer.rs:3285-3289
+    default) or the exact dL/dS_in (emb_grad="ds_in").
 
     Returns a dict with every intermediate the GPU path is compared on.
     """
@@ -762,11 +915,22 @@ def train_step(S_in, targets, W, lm, cfg: Cfg, adam_state=None, step=1, lr=1e-3,
     N = B * T
     fwd = forward(S_in, W, cfg, mstate)
     w_lm, b_lm, g_lm = lm
-    loss, dP, gW_lm, gb_lm, gg_lm = lm_head(fwd.pooled.reshape(N, d), np.asarray(targets).reshape(N),
-                                             w_lm, b_lm, g_lm)
+    tg = np.asarray(targets).reshape(N)
+    sampled = None
+    if lm_samples > 0:
+        V = np.asarray(w_lm).shape[0]
+        if lm_state is None:
+            lm_state = dict(mW=np.zeros((V, d)), vW=np.zeros((V, d)), mb=np.zeros(V), vb=np.zeros(V))
+        sampled = sampled_indices(tg, step, V, lm_samples, sample_seed)
+        loss, dP, w_new, b_new, dW_s, db_s = lm_head_sampled(fwd.pooled.reshape(N, d), tg, w_lm, b_lm, g_lm,
+                                                             sampled, lm_state, step, lr=lr)
+        lm_new = np.concatenate([w_new.ravel(), b_new, np.asarray(g_lm, np.float64)])
+        lm_g = (dW_s, db_s)
+    else:
+        loss, dP, gW_lm, gb_lm, gg_lm = lm_head(fwd.pooled.reshape(N, d), tg, w_lm, b_lm, g_lm)
     br = branch_of(fwd, W, cfg).reshape(N, h, d)
-    V = View(W, d, h)
-    v, g_pre, pre, r_pre = adjoint(fwd.hstar.reshape(N, h, d), br, dP, V.NS, cfg)
+    V_ = View(W, d, h)
+    v, g_pre, pre, r_pre = adjoint(fwd.hstar.reshape(N, h, d), br, dP, V_.NS, cfg)
     G, dS = weight_grads(np.asarray(S_in, np.float64).reshape(N, d),
                          fwd.signal.reshape(N, h, d), fwd.A.reshape(N, h, d), fwd.attn_cache,
                          v, g_pre, pre, r_pre, W, cfg)
@@ -777,8 +941,16 @@ def train_step(S_in, targets, W, lm, cfg: Cfg, adam_state=None, step=1, lr=1e-3,
     if adam_state is None:
         adam_state = (np.zeros_like(G), np.zeros_like(G))
     Wn, m1, m2 = adam(W, G, adam_state[0], adam_state[1], step, lr=lr)
-    lm_flat = np.concatenate([np.ravel(w_lm), np.ravel(b_lm), np.ravel(g_lm)]).astype(np.float64)
-    lm_g = np.concatenate([gW_lm.ravel(), gb_lm, gg_lm])
-    lm_new, _, _ = adam(lm_flat, lm_g, np.zeros_like(lm_g), np.zeros_like(lm_g), step, lr=lr)
+    if lm_samples <= 0:
+        lm_flat = np.concatenate([np.ravel(w_lm), np.ravel(b_lm), np.ravel(g_lm)]).astype(np.float64)
+        lm_g = np.concatenate([gW_lm.ravel(), gb_lm, gg_lm])
+        lm_new, _, _ = adam(lm_flat, lm_g, np.zeros_like(lm_g), np.zeros_like(lm_g), step, lr=lr)
+    emb_new = None
+    if emb is not None and tokens is not None:
+        if emb_state is None:
+            emb_state = dict(m=np.zeros(np.shape(emb)), v=np.zeros(np.shape(emb)))
+        rows = dP if emb_grad == "dl_dh" else dS
+        emb_new = embedding_update(emb, np.asarray(tokens).reshape(N), rows, emb_state, step, lr=lr)
     return dict(fwd=fwd, loss=loss, dP=dP, v=v, g_pre=g_pre, grads=G, dS=dS, W_new=Wn,
-                adam=(m1, m2), lm_grads=lm_g, lm_new=lm_new, fpm=fpm_out)
+                adam=(m1, m2), lm_grads=lm_g, lm_new=lm_new, fpm=fpm_out, sampled=sampled,
+                emb_new=emb_new)

