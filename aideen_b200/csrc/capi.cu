@@ -102,6 +102,11 @@ struct aideen_ctx {
   cudaStream_t ast = nullptr;
   cudaEvent_t ev_da = nullptr, ev_dqkv = nullptr, ev_adone = nullptr;
   bool lmg_pending = false;
+  // embedding update on its own stream (one GPU): the token CSR from the step's
+  // start, the row Adam once dL/dpooled exists; the next gather joins it
+  cudaStream_t est = nullptr;
+  cudaEvent_t ev_e0 = nullptr, ev_emb = nullptr;
+  bool emb_pending = false, emb_csr_ready = false;
   bool lm_reduced = false;  // this step's LM-head gradients were already summed over ranks
   bool fpm_prepared = false;  // the FPM backward's forward-only stage already ran this step
   int fpm_comp_done = 0;  // FPM chunk composites [0, this) already formed this step
@@ -130,6 +135,7 @@ struct aideen_ctx {
   float adj_beta = 0.85f;
   bool lm_ready = false, emb_ready = false;
   size_t lcap = 0, gcap = 0;  // capacity of the sampled-set buffers / allgather buffers (rows)
+  size_t lcur = 0;            // sampled-set bound of the current step (row stride of its logits)
   bool lm_split_stale = true;  // W_lm changed since its hi/lo copies were made
   bool use_tc = true;     // tcgen05 GEMMs where the operand shapes allow
   DevBufs b;
@@ -163,6 +169,13 @@ int sync_and_check(aideen_ctx *ctx) {
   if (adj) return set_err(ctx, AIDEEN_E_TIMEOUT, "adjoint: a bounded stage wait ran out (its outputs are invalid)");
   if (pic) return set_err(ctx, AIDEEN_E_TIMEOUT, "Picard memory-row exchange: a bounded wait ran out");
   return AIDEEN_OK;
+}
+
+// Make the context stream wait for a deferred embedding update.
+cudaError_t join_emb(aideen_ctx *c) {
+  if (!c->emb_pending) return cudaSuccess;
+  c->emb_pending = false;
+  return cudaStreamWaitEvent(c->stream, c->ev_emb, 0);
 }
 
 // Make the context stream wait for a deferred LM-head update on the side stream.
@@ -771,8 +784,16 @@ int pipeline_chunks(aideen_ctx *ctx, const aideen_run *r) {
 // the adjoint of its rows run on the context stream, capped to the SMs the
 // solve leaves free, while the solve continues with chunk j+1.  Results equal
 // the sequential schedule's (each stage is row-local or a sum over rows).
+int lm_sampled_prepare(aideen_ctx *ctx, int N, const aideen_step_args *a);
+int lm_sampled_rows(aideen_ctx *ctx, long r0, int R, bool first);
+int lm_sampled_finish(aideen_ctx *ctx, int N, const aideen_step_args *a);
+
 int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aideen_stats *stats) {
   const aideen_run *r = &a->run;
+  // sampled head: per chunk only its logits / softmax / dW_S share; its Adam
+  // step, dL/dh and the adjoint follow the last chunk (dL/dh needs the
+  // updated rows, which need every row's coef)
+  const bool sampled = a->lm_samples > 0;
   const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model, V = ctx->cfg.vocab;
   const int B = r->batch, T = r->seq_len, N = B * T;
   const long Vp = ctx->Vp, N4 = (N + 3) / 4 * 4;
@@ -790,7 +811,8 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   CU(cudaEventRecord(ctx->ev_prep, st));
   ctx->last_run = *r;
   ctx->N = N;
-  KL(launch_count_active(b.targets, N, b.scal, st));
+  if (sampled) CHK(lm_sampled_prepare(ctx, N, a));
+  else KL(launch_count_active(b.targets, N, b.scal, st));
   int nsm = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
@@ -842,6 +864,13 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
     const long r0 = (long)t0 * B;
     const int R = (t1 - t0) * B;
     CU(cudaStreamWaitEvent(st, ctx->ev_pic[j], 0));
+    if (sampled) {
+      KL(launch_pool_rmsnorm(b.hstar + r0 * h * d, glm, b.pooled + r0 * d, b.y + r0 * d, b.lrms + r0, R, h, d,
+                             st));
+      CHK(lm_sampled_rows(ctx, r0, R, j == 0));
+      tl_mark(ctx, ("cons" + std::to_string(j)).c_str(), st);
+      continue;
+    }
     if (j == 0) {  // the previous step's deferred LM-head update must be done before the logits
       CU(join_side(ctx));
       if (ctx->lm_split_stale) {
@@ -932,6 +961,23 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
     }
   }
   ctx->sm_budget = 0;
+  if (sampled) {
+    CHK(lm_sampled_finish(ctx, N, a));
+    tl_mark(ctx, "lm_fin", st);
+    AdjointArgs aa{};
+    aa.N = N; aa.h = h; aa.d = d; aa.iters = a->adj_iters; aa.anderson_m = a->anderson_m;
+    aa.beta = r->damping;
+    aa.pre_a = b.pre; aa.rhs_tok = b.dl_dh;
+    aa.NS = b.W + ctx->P.nscale; aa.v = b.v; aa.gpre = b.gpre; aa.nsg_cta = b.nsg;
+    if (a->anderson_m > 4) return set_err(ctx, AIDEEN_E_UNSUPPORTED, "anderson_m > 4");
+    int grid = 0;
+    KL(launch_adjoint(aa, st, &grid));
+    tl_mark(ctx, "adjoint", st);
+    ctx->adj_N = N;
+    ctx->adj_beta = r->damping;
+    ctx->nsg_rows = grid;
+    return stats ? read_solve_stats(ctx, r, stats) : AIDEEN_OK;
+  }
   ctx->adj_N = N;
   ctx->adj_beta = r->damping;
   ctx->nsg_rows = nsg_rows;
@@ -962,7 +1008,10 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
 // communicator the sampled set is built from every rank's targets and the
 // sampled-row gradients are summed over ranks before the clamp and the step,
 // so every rank applies the same update.
-int run_lm_head_sampled(aideen_ctx *ctx, int N, const aideen_step_args *a) {
+// Sampled head, stage 1: the sampled set (from every rank's targets with a
+// communicator) and the gathered rows W_S.  Depends only on the targets and
+// W_lm, so it can run before the forward's rows exist.
+int lm_sampled_prepare(aideen_ctx *ctx, int N, const aideen_step_args *a) {
   if (!ctx->lm_ready) return set_err(ctx, AIDEEN_E_INVALID, "LM head not uploaded");
   ctx->prof_phase = AIDEEN_PROF_LM_SOFTMAX;  // every LM-head launch in one profile class
   struct PhaseReset { aideen_ctx *c; ~PhaseReset() { c->prof_phase = -1; } } phase_reset{ctx};
@@ -983,6 +1032,7 @@ int run_lm_head_sampled(aideen_ctx *ctx, int N, const aideen_step_args *a) {
     CU(dalloc(&b.lWS, cap * d));
     ctx->lcap = cap;
   }
+  ctx->lcur = cap;
   if (!b.ints) {
     CU(dalloc(&b.ints, 8));
     CU(dalloc(&b.lerr, 1));
@@ -1002,23 +1052,50 @@ int run_lm_head_sampled(aideen_ctx *ctx, int N, const aideen_step_args *a) {
   }
   CU(join_side(ctx));
   const unsigned long long seed = a->sample_seed ? (unsigned long long)a->sample_seed : 0xA1DEEE5A4D5EED5Eull;
-  const uint32_t step = a->update.step;
-  int *Kd = b.ints;
-  KL(launch_sample_set(tg, Ng, V, ns, 2048, seed, step, b.lS, Kd, b.scal, (int)cap, b.lerr, st));
-  const float *Wlm = b.lmp, *blm = b.lmp + ctx->lm_b, *glm = b.lmp + ctx->lm_g;
-  KL(launch_gather_rows(Wlm, b.lS, Kd, (int)cap, d, b.lWS, st));
-  const long ld = (long)cap;
+  KL(launch_sample_set(tg, Ng, V, ns, 2048, seed, a->update.step, b.lS, b.ints, b.scal, (int)cap, b.lerr, st));
+  KL(launch_gather_rows(b.lmp, b.lS, b.ints, (int)cap, d, b.lWS, st));
+  return AIDEEN_OK;
+}
+
+// Stage 2, for token rows [r0, r0 + R) whose pooled state exists: sampled
+// logits, softmax and coef in place, loss rows, and their share of dW_S and
+// db_S (accumulated after the first row range).
+int lm_sampled_rows(aideen_ctx *ctx, long r0, int R, bool first) {
+  ctx->prof_phase = AIDEEN_PROF_LM_SOFTMAX;
+  struct PhaseReset { aideen_ctx *c; ~PhaseReset() { c->prof_phase = -1; } } phase_reset{ctx};
+  const int d = ctx->cfg.d_model, V = ctx->cfg.vocab;
+  DevBufs &b = ctx->b;
+  cudaStream_t st = ctx->stream;
+  const int cap = (int)ctx->lcur;
+  const long ld = cap;
+  float *lg = b.logits + r0 * ld;
+  const float *y = b.y + r0 * d;
   // logits[n][k] = y[n] . W_lm[S_k]
-  KL(gemm_any(ctx, gemm(N, (int)cap, d, 1, b.y, d, 0, false, b.lWS, d, 0, true, b.logits, ld, 0)));
-  KL(launch_softmax_sampled(b.logits, ld, blm, b.lS, Kd, b.targets, V, b.scal, b.loss_rows, N, st));
-  KL(launch_sum(b.loss_rows, N, b.scal + 1, st));
-  // dW_S[k][j] = sum_n coef[n][k] y[n][j]; db_S[k] = sum_n coef[n][k]
+  KL(gemm_any(ctx, gemm(R, cap, d, 1, y, d, 0, false, b.lWS, d, 0, true, lg, ld, 0)));
+  KL(launch_softmax_sampled(lg, ld, b.lmp + ctx->lm_b, b.lS, b.ints, b.targets + r0, V, b.scal,
+                            b.loss_rows + r0, R, st));
+  // dW_S[k][j] += sum_n coef[n][k] y[n][j]; db_S[k] += sum_n coef[n][k]
+  KL(gemm_any(ctx, gemm(cap, d, R, 1, lg, ld, 0, true, y, d, 0, false, b.Glm, d, 0, 1.f, first ? 0.f : 1.f)));
+  KL(launch_colsum(lg, R, cap, ld, b.Glm + ctx->lm_b, cap, 0, !first, st));
+  return AIDEEN_OK;
+}
+
+// Stage 3, once every row's coef exists: (sum over ranks,) the clamped Adam
+// step on the sampled rows, then dL/dy from the updated rows and the RMSNorm
+// backward into dl_dh, and the loss.
+int lm_sampled_finish(aideen_ctx *ctx, int N, const aideen_step_args *a) {
+  ctx->prof_phase = AIDEEN_PROF_LM_SOFTMAX;
+  struct PhaseReset { aideen_ctx *c; ~PhaseReset() { c->prof_phase = -1; } } phase_reset{ctx};
+  const int d = ctx->cfg.d_model;
+  DevBufs &b = ctx->b;
+  cudaStream_t st = ctx->stream;
+  const int cap = (int)ctx->lcur;
+  const long ld = cap;
   float *dW = b.Glm, *db = b.Glm + ctx->lm_b;
-  KL(gemm_any(ctx, gemm((int)cap, d, N, 1, b.logits, ld, 0, true, b.y, d, 0, false, dW, d, 0)));
-  KL(launch_colsum(b.logits, N, (int)cap, ld, db, (int)cap, 0, false, st));
-  if (dp) {
+  KL(launch_sum(b.loss_rows, N, b.scal + 1, st));
+  if (ctx->comm && ctx->nranks > 1) {
     ncclResult_t nr = ncclGroupStart();
-    if (nr == ncclSuccess) nr = ncclAllReduce(dW, dW, cap * d, ncclFloat, ncclSum, ctx->comm, st);
+    if (nr == ncclSuccess) nr = ncclAllReduce(dW, dW, (size_t)cap * d, ncclFloat, ncclSum, ctx->comm, st);
     if (nr == ncclSuccess) nr = ncclAllReduce(db, db, cap, ncclFloat, ncclSum, ctx->comm, st);
     const ncclResult_t n2 = ncclGroupEnd();
     if (nr != ncclSuccess || n2 != ncclSuccess)
@@ -1029,13 +1106,25 @@ int run_lm_head_sampled(aideen_ctx *ctx, int N, const aideen_step_args *a) {
   const double t = u->step < 1 ? 1.0 : (double)u->step;
   const float bc1 = (float)(1.0 - std::pow((double)u->beta1, t));
   const float bc2 = (float)(1.0 - std::pow((double)u->beta2, t));
-  KL(launch_lm_sampled_adam(b.lmp, b.lmp + ctx->lm_b, b.Mlm1, b.Mlm2, ctx->lm_b, dW, db, b.lS, Kd, (int)cap, d,
+  KL(launch_lm_sampled_adam(b.lmp, b.lmp + ctx->lm_b, b.Mlm1, b.Mlm2, ctx->lm_b, dW, db, b.lS, b.ints, cap, d,
                             b.lWS, u->lr, u->beta1, u->beta2, u->eps, bc1, bc2, st));
   ctx->lm_split_stale = true;
   // dL/dy[n][j] = sum_k coef[n][k] W_lm'[S_k][j], then through the RMSNorm
-  KL(gemm_any(ctx, gemm(N, d, (int)cap, 1, b.logits, ld, 0, false, b.lWS, d, 0, false, b.dy, d, 0)));
-  KL(launch_rmsnorm_bwd(b.dy, b.pooled, b.lrms, glm, b.dl_dh, b.ggp, N, d, st));
+  KL(gemm_any(ctx, gemm(N, d, cap, 1, b.logits, ld, 0, false, b.lWS, d, 0, false, b.dy, d, 0)));
+  KL(launch_rmsnorm_bwd(b.dy, b.pooled, b.lrms, b.lmp + ctx->lm_g, b.dl_dh, b.ggp, N, d, st));
   return AIDEEN_OK;
+}
+
+// Sampled-softmax LM head over the last forward's pooled rows (the
+// reference's lm_probs -> lm_update -> lm_backprop_h_t order): its Adam step
+// on the sampled rows happens here, before dL/dh is formed from them.  With a
+// communicator the sampled set is built from every rank's targets and the
+// sampled-row gradients are summed over ranks before the clamp and the step,
+// so every rank applies the same update.
+int run_lm_head_sampled(aideen_ctx *ctx, int N, const aideen_step_args *a) {
+  CHK(lm_sampled_prepare(ctx, N, a));
+  CHK(lm_sampled_rows(ctx, 0, N, true));
+  return lm_sampled_finish(ctx, N, a);
 }
 
 // Embedding rows of the step's tokens: the mean gradient row of every
@@ -1089,9 +1178,37 @@ int run_emb_update(aideen_ctx *ctx, int N, const aideen_step_args *a) {
   const float bc1 = (float)(1.0 - std::pow((double)u->beta1, t));
   const float bc2 = (float)(1.0 - std::pow((double)u->beta2, t));
   const float lr = a->emb_lr > 0.f ? a->emb_lr : u->lr;
+  if (ctx->emb_csr_ready) {
+    // the CSR was built on the embedding stream at the step's start; the row
+    // update follows the gradient rows there and the next gather joins it
+    ctx->emb_csr_ready = false;
+    CU(cudaEventRecord(ctx->ev_e0, st));
+    CU(cudaStreamWaitEvent(ctx->est, ctx->ev_e0, 0));
+    ctx->launches++;
+    CU(launch_emb_adam(b.emb, b.Me1, b.Me2, grad, b.cuniq, b.coff, b.cpos, b.ints + 1, Ng, d, lr, u->beta1,
+                       u->beta2, u->eps, bc1, bc2, ctx->est));
+    CU(cudaEventRecord(ctx->ev_emb, ctx->est));
+    ctx->emb_pending = true;
+    return AIDEEN_OK;
+  }
   KL(launch_emb_csr(tok, Ng, V, b.cuniq, b.coff, b.cpos, b.ints + 1, st));
   KL(launch_emb_adam(b.emb, b.Me1, b.Me2, grad, b.cuniq, b.coff, b.cpos, b.ints + 1, Ng, d, lr, u->beta1,
                      u->beta2, u->eps, bc1, bc2, st));
+  return AIDEEN_OK;
+}
+
+// One GPU, no profiling: the step's token CSR on the embedding stream while
+// the forward runs (it needs only the token ids).
+int emb_csr_early(aideen_ctx *ctx, int N) {
+  DevBufs &b = ctx->b;
+  if (ctx->prof || (ctx->comm && ctx->nranks > 1) || !ctx->est || !b.cuniq || (size_t)N > ctx->gcap ||
+      N > emb_csr_max_tokens())
+    return AIDEEN_OK;  // the update builds it itself (first step, data parallel, profiling)
+  CU(cudaEventRecord(ctx->ev_e0, ctx->stream));
+  CU(cudaStreamWaitEvent(ctx->est, ctx->ev_e0, 0));
+  ctx->launches++;
+  CU(launch_emb_csr(b.tokens, N, (int)ctx->cfg.vocab, b.cuniq, b.coff, b.cpos, b.ints + 1, ctx->est));
+  ctx->emb_csr_ready = true;
   return AIDEEN_OK;
 }
 
@@ -1256,6 +1373,9 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_fdone, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->lmst, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->ast, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->est, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_e0, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_emb, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_da, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_dqkv, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_adone, cudaEventDisableTiming);
@@ -1291,6 +1411,7 @@ void aideen_destroy(aideen_ctx *ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->est) cudaStreamSynchronize(ctx->est);
   if (ctx->comm) ncclCommDestroy(ctx->comm);
   DevBufs &b = ctx->b;
   void *ptrs[] = {b.W, b.G, b.M1, b.M2, b.S_in, b.tokens, b.targets, b.signal, b.A, b.amat, b.Qh,
@@ -1315,6 +1436,9 @@ void aideen_destroy(aideen_ctx *ctx) {
   if (ctx->ev_fdone) cudaEventDestroy(ctx->ev_fdone);
   if (ctx->lmst) { cudaStreamSynchronize(ctx->lmst); cudaStreamDestroy(ctx->lmst); }
   if (ctx->ast) { cudaStreamSynchronize(ctx->ast); cudaStreamDestroy(ctx->ast); }
+  if (ctx->est) cudaStreamDestroy(ctx->est);
+  if (ctx->ev_e0) cudaEventDestroy(ctx->ev_e0);
+  if (ctx->ev_emb) cudaEventDestroy(ctx->ev_emb);
   if (ctx->ev_da) cudaEventDestroy(ctx->ev_da);
   if (ctx->ev_dqkv) cudaEventDestroy(ctx->ev_dqkv);
   if (ctx->ev_adone) cudaEventDestroy(ctx->ev_adone);
@@ -1330,6 +1454,7 @@ void aideen_destroy(aideen_ctx *ctx) {
 int aideen_set_stream(aideen_ctx *ctx, void *s) {
   if (!ctx) return AIDEEN_E_INVALID;
   CU(join_side(ctx));
+  CU(join_emb(ctx));
   CU(cudaStreamSynchronize(ctx->stream));
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   ctx->stream = (cudaStream_t)s;
@@ -1366,12 +1491,14 @@ int aideen_profile_read(aideen_ctx *ctx, float *ms, uint64_t *launches, int rese
 int aideen_join(aideen_ctx *ctx) {
   if (!ctx) return AIDEEN_E_INVALID;
   CU(join_side(ctx));
+  CU(join_emb(ctx));
   return AIDEEN_OK;
 }
 
 int aideen_sync(aideen_ctx *ctx) {
   if (!ctx) return AIDEEN_E_INVALID;
   CU(join_side(ctx));
+  CU(join_emb(ctx));
   return sync_and_check(ctx);
 }
 
@@ -1451,6 +1578,7 @@ int aideen_download_lm_head(aideen_ctx *ctx, float *w_lm, float *b_lm, float *g_
 int aideen_upload_embedding(aideen_ctx *ctx, const float *emb) {
   if (!ctx) return AIDEEN_E_INVALID;
   if (!ctx->cfg.vocab) return set_err(ctx, AIDEEN_E_INVALID, "context created with vocab = 0");
+  CU(join_emb(ctx));
   CHK(copy_in(ctx, ctx->b.emb, emb, (size_t)ctx->cfg.vocab * ctx->cfg.d_model * 4, AIDEEN_HOST));
   CU(cudaStreamSynchronize(ctx->stream));
   ctx->emb_ready = true;
@@ -1460,6 +1588,7 @@ int aideen_upload_embedding(aideen_ctx *ctx, const float *emb) {
 int aideen_download_embedding(aideen_ctx *ctx, float *emb) {
   if (!ctx || !emb) return AIDEEN_E_INVALID;
   if (!ctx->emb_ready) return set_err(ctx, AIDEEN_E_INVALID, "embedding not uploaded");
+  CU(join_emb(ctx));
   CU(cudaMemcpyAsync(emb, ctx->b.emb, (size_t)ctx->cfg.vocab * ctx->cfg.d_model * 4, cudaMemcpyDeviceToHost,
                      ctx->stream));
   return sync_and_check(ctx);
@@ -1504,6 +1633,7 @@ int aideen_forward_tokens(aideen_ctx *ctx, const aideen_run *run, const int32_t 
   if (!ctx->emb_ready) return set_err(ctx, AIDEEN_E_INVALID, "embedding not uploaded");
   const int N = run->batch * run->seq_len;
   CHK(copy_in_rows(ctx, ctx->b.tokens, tokens, run->batch, run->seq_len, 1, 1, where));
+  CU(join_emb(ctx));
   KL(launch_embed(ctx->b.tokens, ctx->b.emb, ctx->b.S_in, N, ctx->cfg.d_model, ctx->cfg.vocab, ctx->stream));
   return run_forward(ctx, run, stats);
 }
@@ -1623,12 +1753,12 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
   ctx->lm_reduced = false;
   CHK(copy_in_rows(ctx, ctx->b.tokens, tokens, a->run.batch, a->run.seq_len, 1, 1, where));
   CHK(copy_in_rows(ctx, ctx->b.targets, targets, a->run.batch, a->run.seq_len, 1, 1, where));
-  KL(launch_embed(ctx->b.tokens, ctx->b.emb, ctx->b.S_in, N, ctx->cfg.d_model, ctx->cfg.vocab, ctx->stream));
   if (a->emb_update > 2) return set_err(ctx, AIDEEN_E_INVALID, "emb_update must be 0, 1 or 2");
+  CU(join_emb(ctx));
+  KL(launch_embed(ctx->b.tokens, ctx->b.emb, ctx->b.S_in, N, ctx->cfg.d_model, ctx->cfg.vocab, ctx->stream));
+  if (a->emb_update) CHK(emb_csr_early(ctx, N));
   const bool sampled = a->lm_samples > 0;
-  // the sampled head updates its rows before dL/dh exists: no overlap of the
-  // adjoint with the solve, so the sequential schedule
-  const int nch = sampled ? 0 : pipeline_chunks(ctx, &a->run);
+  const int nch = pipeline_chunks(ctx, &a->run);
   if (nch > 1) {
     CHK(run_step_pipelined(ctx, a, nch, stats));
   } else {
