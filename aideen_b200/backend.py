@@ -86,6 +86,7 @@ _SIGS = {
     "aideen_upload_lm_head": (C.c_int, [_P, _P, _P, _P]),
     "aideen_download_lm_head": (C.c_int, [_P, _P, _P, _P]),
     "aideen_download_embedding": (C.c_int, [_P, _P]),
+    "aideen_temporal_scan": (C.c_int, [_P, C.c_uint32, C.c_uint32, _P, C.c_int]),
     "aideen_upload_embedding": (C.c_int, [_P, _P]),
     "aideen_reset_state": (C.c_int, [_P]),
     "aideen_reset_optimizer": (C.c_int, [_P]),
@@ -255,6 +256,14 @@ class GpuDeqBackend:
         c = np.empty(self.d, np.float32)
         self._check(self.lib.aideen_download_lm_head(self.ctx, _ptr(a), _ptr(b), _ptr(c)), "read_lm_head")
         return a, b, c
+
+    def temporal_scan(self, batch, seq_len, hstar=None):
+        """The simple temporal carrier (`temporal_step`) over a chunk of fixed
+        points (default: the last forward's); memory rows land in hist_ctx."""
+        hs = _f32(hstar) if hstar is not None else None
+        self._check(self.lib.aideen_temporal_scan(self.ctx, batch, seq_len, _ptr(hs) if hs is not None else None,
+                                                  HOST), "temporal_scan")
+        self.batch, self.seq_len = batch, seq_len
 
     def read_embedding(self):
         out = np.empty((self.vocab, self.d), np.float32)

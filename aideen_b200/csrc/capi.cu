@@ -1696,6 +1696,27 @@ int aideen_adjoint_on(aideen_ctx *ctx, const aideen_adjoint_args *a, const float
   return run_adjoint(ctx, N, pa, pb, rt, rs, a->iters, a->damping, a->anderson_m);
 }
 
+int aideen_temporal_scan(aideen_ctx *ctx, uint32_t batch, uint32_t seq_len, const float *hstar, int where) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
+  if (batch == 0 || seq_len == 0 || batch > ctx->cfg.max_batch || seq_len > ctx->cfg.max_seq_len)
+    return set_err(ctx, AIDEEN_E_INVALID, "batch/seq_len outside the context caps");
+  if (hstar) {
+    CHK(copy_in_rows(ctx, ctx->b.hstar, hstar, (int)batch, (int)seq_len, 1, (size_t)h * d, where));
+    ctx->perm_B = (int)batch;
+    ctx->perm_T = (int)seq_len;
+    ctx->N = batch * seq_len;
+  } else if (ctx->N != batch * seq_len || ctx->last_run.batch != batch) {
+    return set_err(ctx, AIDEEN_E_INVALID, "no h* given and the last forward has another shape");
+  }
+  TemporalArgs a{};
+  a.B = (int)batch; a.T = (int)seq_len; a.h = h; a.d = d; a.W = ctx->b.W;
+  a.off_alog = ctx->P.alog; a.off_wx = ctx->P.wx; a.off_wout = ctx->P.wout;
+  a.hstar = ctx->b.hstar; a.hist = ctx->b.hist; a.mstate = ctx->b.mstate;
+  KL(launch_temporal_scan(a, ctx->stream));
+  return AIDEEN_OK;
+}
+
 int aideen_source_grad(aideen_ctx *ctx, float *out, int where) {
   if (!ctx || !out) return AIDEEN_E_INVALID;
   const int N = ctx->adj_N, h = ctx->cfg.h_slots, d = ctx->cfg.d_model;

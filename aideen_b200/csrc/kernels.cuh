@@ -183,6 +183,17 @@ cudaError_t launch_emb_adam(float *emb, float *M1, float *M2, const float *grad,
                             const int32_t *off, const int32_t *pos, const int *U, int ucap, int d, float lr,
                             float b1, float b2, float eps, float bc1, float bc2, cudaStream_t st);
 
+// Simple temporal carrier over a token chunk (temporal.cu): rows token-major
+// (row t*B + b) [N][h][d]; mstate [B][h][d] in/out.
+struct TemporalArgs {
+  int B, T, h, d;
+  const float *W;
+  size_t off_alog, off_wx, off_wout;
+  const float *hstar;
+  float *hist, *mstate;
+};
+cudaError_t launch_temporal_scan(const TemporalArgs &a, cudaStream_t st);
+
 // FPM memory backward (fpm_bwd.cu).  Row-major [N][h][d] buffers, N = B*T
 // tokens in the library's token-major order (row t*B + b); v is the adjoint
 // solution [h][N][d]; the chunk

@@ -314,7 +314,10 @@ def main():
     tg_h = torch.from_numpy(tg).pin_memory()
     rc = RunConfig(max_iters=MAX_ITERS, fpm=True)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MB > L2
-    gs = 1.0 / world
+    # the dense head normalises each rank's loss by its own token count, so
+    # the summed gradients are scaled by 1/world; the sampled head normalises
+    # by the count over every rank already
+    gs = 1.0 / world if args.dense_lm else 1.0
     step_no = [0]
     lm_samples = 0 if args.dense_lm else LM_SAMPLES
     emb_update = 0 if args.dense_lm else 1
@@ -325,7 +328,8 @@ def main():
         ns = lm_samples if lm is None else lm
         ptrs = (tok_d.data_ptr(), tg_d.data_ptr()) if where == DEVICE else (tok_h.data_ptr(), tg_h.data_ptr())
         return be.train_step(*ptrs, B_PER_GPU, T, rc, adj_iters=ADJ_ITERS, anderson_m=ANDERSON_M,
-                             step=step_no[0], renorm=renorm, allreduce=world > 1, grad_scale=gs, where=where,
+                             step=step_no[0], renorm=renorm, allreduce=world > 1,
+                             grad_scale=gs if ns else 1.0 / world, where=where,
                              want_loss=where != DEVICE, raw_ptr=True, lm_samples=ns,
                              emb_update=emb_update if ns else 0)
 

@@ -186,6 +186,16 @@ int aideen_adjoint(aideen_ctx *ctx, const aideen_adjoint_args *args, const float
 int aideen_adjoint_on(aideen_ctx *ctx, const aideen_adjoint_args *args, const float *hstar,
                       const float *branch, const float *dl_dh, const float *rhs_slot,
                       int where);
+/* ---- simple temporal carrier (temporal_step, fixed_point_memory_reasoning.rs:1455-1486;
+ *      hist_v2_temporal_main, hist_v2_temporal.wgsl:40-110) ----------------
+ * Token by token over a chunk of fixed points h* ([B*T][h][d], caller order;
+ * NULL = the last forward's), starting from the carried MState:
+ *   M_t = (I + W_out^T)(a*M_{t-1} + (1-a)*(1 + 0.5 tanh(diag W_x))*h_t/rms(h_t)),
+ *   a = sigmoid(-a_log[slot]).
+ * Leaves every M_t in the HIST_CTX buffer and the last one in MState (the FPM
+ * memory scan's buffers; this is the reference's non-default simpler carrier). */
+int aideen_temporal_scan(aideen_ctx *ctx, uint32_t batch, uint32_t seq_len, const float *hstar, int where);
+
 /* reduce_clean_adjoint_to_source_grad_no_readback (gpu_deq.rs:4922):
  * out[B*T][d] = sum_s beta*J_norm^T v. */
 int aideen_source_grad(aideen_ctx *ctx, float *out, int where);

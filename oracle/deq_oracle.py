@@ -21,6 +21,9 @@ It restates, in float64 numpy, the reference's live GPU semantics:
 * spectral renorm            `aideen-block/src/shaders/spectral_renorm.wgsl:83-196`
 * FPM backward (TBPTT scan)  `aideen-backbone/src/shaders/fused_fpm_retain_bwd.wgsl:364-2095`
 * FPM W_out / W_x grads      `aideen-backbone/src/shaders/fused_fpm_shared_update.wgsl:129-256`
+* temporal carrier (simple)  `aideen-backbone/src/fixed_point_memory_reasoning.rs:1455-1486`
+* sampled-softmax LM head    `aideen-backbone/src/shaders/lm_train.wgsl:79-395`, `gpu_lm_head.rs:213-281`
+* embedding-row Adam         `aideen-backbone/src/shaders/embedding_train.wgsl:100-147`
 
 Weight gradients are derived analytically (implicit-function theorem through
 the map the clean adjoint linearises); the reference's own stage-4 shaders
@@ -266,6 +269,34 @@ def fpm_write(h_star, sig_t, m_prev, V: View, Wx_diag):
     a = 1.0 / (1.0 + np.exp(V.Alog))[None]
     base = a * m_prev + (1.0 - a) * x
     return retain * m_prev + (1.0 - retain) * base
+
+
+def temporal_step(m_prev, h_star, V: View):
+    """The simple temporal carrier `temporal_step` (fixed_point_memory_reasoning.rs:1455-1486;
+    GPU form hist_v2_temporal.wgsl:60-108): per slot,
+    M' = (I + W_out^T)(a * M + (1 - a) * (1 + 0.5 tanh(diag W_x)) * h / rms(h)),
+    a = sigmoid(-a_log[slot]), W_out read as [j][d_out] like the shader.
+    m_prev, h_star: [B,h,d]."""
+    hr = np.sqrt((h_star * h_star).mean(-1) + 1e-6)
+    hu = h_star / np.maximum(hr, 1e-6)[..., None]
+    a = 1.0 / (1.0 + np.exp(V.Alog))[None]
+    x = hu + 0.5 * np.tanh(np.diag(V.Wx))[None, None, :] * hu
+    mn = a * m_prev + (1.0 - a) * x
+    return mn + es('bsj,jo->bso', mn, V.Wout)
+
+
+def temporal_scan(hstar, W, d, h, mstate=None):
+    """The carrier over a [B,T,h,d] chunk of fixed points, token by token:
+    returns the memory after every token [B,T,h,d] and the carried state [B,h,d]."""
+    V = View(W, d, h)
+    hs = np.asarray(hstar, np.float64)
+    B, T = hs.shape[:2]
+    m = np.zeros((B, h, d)) if mstate is None else np.asarray(mstate, np.float64).copy()
+    out = np.zeros_like(hs)
+    for t in range(T):
+        m = temporal_step(m, hs[:, t], V)
+        out[:, t] = m
+    return out, m
 
 
 @dataclass

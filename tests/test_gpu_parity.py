@@ -322,3 +322,25 @@ def test_pipelined_train_step_matches_sequential_and_oracle():
     assert rel(gp, r["grads"]) < TOL and rel(lgp, r["lm_grads"]) < TOL
     W_kernel, _, _ = O.adam(W, gp, np.zeros_like(W, np.float64), np.zeros_like(W, np.float64), 1, lr=1e-3)
     assert rel(wp.astype(np.float64) - W, W_kernel.astype(np.float32).astype(np.float64) - W) < 1e-4
+
+
+@pytest.mark.parametrize("d,h", [(128, 4), (512, 8), (1024, 16)])
+def test_temporal_carrier_scan(d, h):
+    """The simple temporal carrier over two consecutive chunks of fixed points
+    (the carried MState links them) against the oracle's `temporal_scan`."""
+    B, T = 2, 6
+    W = init_all_weights(d, h, seed=4)
+    rng = np.random.default_rng(6)
+    L = O.Offsets(d, h)
+    W[L.wout:L.wout + d * d] = (0.02 * rng.standard_normal(d * d)).astype(np.float32)
+    W[L.wx:L.wx + d * d] = (0.5 * rng.standard_normal(d * d)).astype(np.float32)
+    be = GpuDeqBackend(d, h, max_batch=B, max_seq_len=T)
+    be.upload_weights(W)
+    m = None
+    for chunk in range(2):
+        hs = rng.standard_normal((B, T, h, d)).astype(np.float32)
+        be.temporal_scan(B, T, hs)
+        hist, m = O.temporal_scan(hs, W, d, h, mstate=m)
+        assert rel(be.read("hist_ctx", (B, T, h, d)), hist) < 1e-5
+        assert rel(be.read("mstate", (B, h, d)), m) < 1e-5
+    be.close()

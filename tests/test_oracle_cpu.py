@@ -466,3 +466,97 @@ def test_embedding_update_is_adam_on_mean_rows():
         gm = G[rows].mean(0)
         ref[t] -= 0.1 * gm / (np.abs(gm) + 1e-8)          # Adam's first step
     assert np.allclose(E1, ref)
+
+
+def test_pin_single_map_against_reference_cpu_forward_map():
+    """With attention weights zero and the self-feedback term removed, the
+    oracle's Picard map is the reference test's `cpu_forward_map_no_fpm` at that
+    test's constants (d 16, h 2, W_in 0.01, s 0.1, damping 0.9): the input
+    projection's orientation, the RMS floor and the damping blend agree exactly."""
+    from reference_maps import cpu_forward_map_no_fpm
+    d, h = 16, 2
+    rng = np.random.default_rng(0)
+    w_in = np.full(d * d, 0.01) + 0.002 * rng.standard_normal(d * d)
+    s_in = np.full(d, 0.1) + 0.01 * rng.standard_normal(d)
+    norm = 1.0 + 0.1 * rng.standard_normal(d)
+    hcur = rng.standard_normal((h, d))
+    z = np.zeros(d * d)
+    ref = cpu_forward_map_no_fpm(hcur.ravel(), s_in, z, z, z, z, w_in, norm, 0.9, h, d).reshape(h, d)
+    W = np.zeros(O.Offsets(d, h).total)
+    L = O.Offsets(d, h)
+    W[L.win:L.win + h * d * d] = np.tile(w_in, h)
+    W[L.nscale:L.nscale + d] = norm
+    W[L.signal_scale] = 1.0
+    V = O.View(W, d, h)
+    sig = O.project_signal(s_in[None], V)[0]          # [h, d]
+    dep = sig + 0.0 * hcur                              # self-feedback removed, no anchor / attention
+    r = O.rms(dep)
+    ours = 0.9 * (V.NS * dep / r[:, None]) + 0.1 * hcur
+    assert np.abs(ours - ref).max() < 1e-12
+
+
+def test_pin_temporal_carrier_against_reference_hist_gated_map():
+    """The oracle's temporal carrier (`temporal_step`) reproduces the memory
+    update of the reference test's `cpu_hist_gated_forward_no_attn` wherever the
+    two coincide: diagonal-free W_x (W_x = 0, so both carriers use h_u alone),
+    any W_out (read as [j][d_out] by both), any a_log."""
+    from reference_maps import cpu_hist_gated_forward_no_attn
+    d, h, T = 16, 2, 3
+    rng = np.random.default_rng(3)
+    s_in = rng.uniform(-1, 1, T * d)
+    w_in = 0.2 * rng.standard_normal(d * d)
+    w_out = 0.05 * rng.standard_normal(d * d)
+    a_log = rng.uniform(-1, 1, d)
+    norm = np.ones(d)
+    h_out, m_last = cpu_hist_gated_forward_no_attn(
+        s_in, w_in, np.zeros(d * d), np.zeros(h * d), np.full(h, -1.0986123), np.zeros(h * d),
+        np.zeros(d * d), w_out, a_log, norm, 0.9, h, d)
+    W = np.zeros(O.Offsets(d, h).total)
+    L = O.Offsets(d, h)
+    W[L.wout:L.wout + d * d] = w_out
+    W[L.alog:L.alog + h * d] = np.tile(a_log, h)
+    hs = h_out.reshape(1, T, h, d)
+    hist, m = O.temporal_scan(hs, W, d, h)
+    assert np.abs(m[0] - m_last.reshape(h, d)).max() < 1e-12
+
+
+def test_adjoint_matches_numeric_picard_on_the_live_map_tightly():
+    """The reference's numeric-adjoint case (picard_pipeline_test.rs:1859-1935:
+    d 16, h 2, one token, the same constant weights, beta 0.9, 8 iterations), with
+    J^T built by central differences of the map the clean adjoint linearises
+    (h -> beta*NS*(branch + h)/rms(branch + h) + (1 - beta)*h, branch frozen at
+    the fixed point, staged_adjoint_picard_clean.wgsl:169-248): where the maps
+    agree the adjoint is exact, so the bar is 1e-6 relative L2 instead of the
+    reference's cosine 0.80 against its different CPU map."""
+    d, h = 16, 2
+    beta = 0.9
+    W = np.zeros(O.Offsets(d, h).total)
+    L = O.Offsets(d, h)
+    for off, c in ((L.wq, 0.02), (L.wk, 0.015), (L.wv, 0.01), (L.wo, 0.012), (L.win, 0.01)):
+        W[off:off + h * d * d] = c
+    W[L.nscale:L.nscale + d] = 1.0
+    W[L.signal_scale] = 1.0
+    s_in = np.full((1, 1, d), 0.1)
+    cfg = O.Cfg(d=d, h=h, max_iters=4, damping=beta, adj_iters=8)
+    fwd = O.forward(s_in, W, cfg)
+    hs = fwd.hstar.reshape(1, h, d)
+    br = O.branch_of(fwd, W, cfg).reshape(1, h, d)
+    NS = O.View(W, d, h).NS
+    dl = np.full((1, d), 0.05)
+    v, *_ = O.adjoint(hs, br, dl, NS, cfg)
+
+    def live_map(hh):
+        pre = br[0] + hh
+        r = np.sqrt(np.mean(pre * pre, -1) + 1e-6)
+        return beta * NS * pre / r[:, None] + (1 - beta) * hh
+
+    b_rep = np.full((h, d), 0.05 / h)
+    v_ref = b_rep.copy()
+    for _ in range(8):
+        jt = np.zeros_like(v_ref)
+        for idx in range(h * d):
+            hp = hs[0].copy().ravel(); hm = hs[0].copy().ravel()
+            hp[idx] += 1e-5; hm[idx] -= 1e-5
+            jt.ravel()[idx] = ((live_map(hp.reshape(h, d)) - live_map(hm.reshape(h, d))) * v_ref).sum() / 2e-5
+        v_ref = b_rep + jt
+    assert np.linalg.norm(v[0] - v_ref) / np.linalg.norm(v_ref) < 1e-6
