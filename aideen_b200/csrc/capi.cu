@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdio>
@@ -108,6 +109,11 @@ struct aideen_ctx {
   cudaEvent_t ev_e0 = nullptr, ev_emb = nullptr;
   bool emb_pending = false, emb_csr_ready = false;
   bool lm_reduced = false;  // this step's LM-head gradients were already summed over ranks
+  // data-parallel train step with Adam: the core gradients are reduce-scattered
+  // in two buckets (the attention-branch block as soon as its chain ends,
+  // beside the FPM backward; the rest after it), each rank steps its own shard,
+  // and the weights are all-gathered
+  bool shard_step = false;
   bool fpm_prepared = false;  // the FPM backward's forward-only stage already ran this step
   int fpm_comp_done = 0;  // FPM chunk composites [0, this) already formed this step
   int sm_budget = 0;      // SMs the GEMM / softmax / adjoint launches may use (0: all)
@@ -136,6 +142,9 @@ struct aideen_ctx {
   bool lm_ready = false, emb_ready = false;
   size_t lcap = 0, gcap = 0;  // capacity of the sampled-set buffers / allgather buffers (rows)
   size_t lcur = 0;            // sampled-set bound of the current step (row stride of its logits)
+  int *hK = nullptr;          // pinned host copy of the sampled-set size
+  bool lk_pending = false;    // hK's copy is in flight
+  cudaEvent_t ev_K = nullptr;
   bool lm_split_stale = true;  // W_lm changed since its hi/lo copies were made
   bool use_tc = true;     // tcgen05 GEMMs where the operand shapes allow
   DevBufs b;
@@ -486,6 +495,32 @@ int run_fpm_backward(aideen_ctx *ctx, bool prepare_only = false);
 int fpm_args(aideen_ctx *ctx, FpmBwdArgs &a);
 void tl_mark(aideen_ctx *ctx, const char *name, cudaStream_t s);
 
+// Gradient buckets of the sharded update: [0, W_x) holds W_q..W_in and their
+// biases (the attention-branch chain writes them), [W_x, end) the rest.
+void grad_buckets(const aideen_ctx *ctx, size_t off[2], size_t len[2]) {
+  off[0] = 0;
+  len[0] = ctx->P.wx;
+  off[1] = ctx->P.wx;
+  len[1] = ctx->W_len - ctx->P.wx;
+}
+
+// Sum bucket [off, off + len) of the gradients over ranks, leaving this rank's
+// shard [off + rank*cnt, +cnt) summed (cnt = len / nranks) and the remainder
+// past cnt*nranks summed on every rank.
+int reduce_scatter_bucket(aideen_ctx *ctx, size_t off, size_t len) {
+  const size_t n = (size_t)ctx->nranks, cnt = len / n, rem = len - cnt * n;
+  float *G = ctx->b.G + off;
+  ncclResult_t r = ncclGroupStart();
+  if (r == ncclSuccess && cnt)
+    r = ncclReduceScatter(G, G + (size_t)ctx->rank * cnt, cnt, ncclFloat, ncclSum, ctx->comm, ctx->stream);
+  if (r == ncclSuccess && rem) r = ncclAllReduce(G + cnt * n, G + cnt * n, rem, ncclFloat, ncclSum, ctx->comm, ctx->stream);
+  const ncclResult_t r2 = ncclGroupEnd();
+  if (r != ncclSuccess || r2 != ncclSuccess)
+    return set_err(ctx, AIDEEN_E_NCCL, std::string("ncclReduceScatter: ") +
+                                           ncclGetErrorString(r != ncclSuccess ? r : r2));
+  return AIDEEN_OK;
+}
+
 int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   const int h = ctx->cfg.h_slots, d = ctx->cfg.d_model;
   const int N = ctx->N;
@@ -600,8 +635,12 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   }
   if (fork_attn) CU(cudaStreamWaitEvent(st, ctx->ev_adone, 0));
   tl_mark(ctx, "attn_grads", st);
+  size_t boff[2], blen[2];
+  grad_buckets(ctx, boff, blen);
+  if (ctx->shard_step) CHK(reduce_scatter_bucket(ctx, boff[0], blen[0]));  // beside the FPM backward
   if (fork_fpm) CU(cudaStreamWaitEvent(st, ctx->ev_fdone, 0));
   else if (ctx->last_run.fpm) CHK(run_fpm_backward(ctx));
+  if (ctx->shard_step) CHK(reduce_scatter_bucket(ctx, boff[1], blen[1]));
   return AIDEEN_OK;
 }
 
@@ -1054,6 +1093,31 @@ int lm_sampled_prepare(aideen_ctx *ctx, int N, const aideen_step_args *a) {
   const unsigned long long seed = a->sample_seed ? (unsigned long long)a->sample_seed : 0xA1DEEE5A4D5EED5Eull;
   KL(launch_sample_set(tg, Ng, V, ns, 2048, seed, a->update.step, b.lS, b.ints, b.scal, (int)cap, b.lerr, st));
   KL(launch_gather_rows(b.lmp, b.lS, b.ints, (int)cap, d, b.lWS, st));
+  if (!ctx->hK) {
+    CU(cudaMallocHost((void **)&ctx->hK, sizeof(int)));
+    CU(cudaEventCreateWithFlags(&ctx->ev_K, cudaEventDisableTiming));
+  }
+  // the set holds max(desired, distinct targets) ids with desired =
+  // min(max(ns, Ng), V, 2048): when desired already reaches the bound, that is
+  // the size; otherwise the host reads it back to trim the GEMM width
+  const int desired = std::min(std::min(ns > Ng ? ns : Ng, V), 2048);
+  if ((size_t)(desired + 3) / 4 * 4 < cap) {
+    CU(cudaMemcpyAsync(ctx->hK, b.ints, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CU(cudaEventRecord(ctx->ev_K, st));
+    ctx->lk_pending = true;
+  }
+  return AIDEEN_OK;
+}
+
+// The sampled set's size as the GEMMs' width: the host waits for the set
+// (built before the forward's rows exist; the caller has enqueued the solve
+// by now, so the device keeps working) and trims the bound to it.
+int lm_sampled_width(aideen_ctx *ctx) {
+  if (!ctx->lk_pending) return AIDEEN_OK;
+  ctx->lk_pending = false;
+  CU(cudaEventSynchronize(ctx->ev_K));
+  const size_t k = ((size_t)(*ctx->hK > 0 ? *ctx->hK : 1) + 3) / 4 * 4;
+  if (k < ctx->lcur) ctx->lcur = k;
   return AIDEEN_OK;
 }
 
@@ -1061,6 +1125,7 @@ int lm_sampled_prepare(aideen_ctx *ctx, int N, const aideen_step_args *a) {
 // logits, softmax and coef in place, loss rows, and their share of dW_S and
 // db_S (accumulated after the first row range).
 int lm_sampled_rows(aideen_ctx *ctx, long r0, int R, bool first) {
+  CHK(lm_sampled_width(ctx));
   ctx->prof_phase = AIDEEN_PROF_LM_SOFTMAX;
   struct PhaseReset { aideen_ctx *c; ~PhaseReset() { c->prof_phase = -1; } } phase_reset{ctx};
   const int d = ctx->cfg.d_model, V = ctx->cfg.vocab;
@@ -1094,6 +1159,9 @@ int lm_sampled_finish(aideen_ctx *ctx, int N, const aideen_step_args *a) {
   float *dW = b.Glm, *db = b.Glm + ctx->lm_b;
   KL(launch_sum(b.loss_rows, N, b.scal + 1, st));
   if (ctx->comm && ctx->nranks > 1) {
+    // the sampled rows' gradients are the only LM-head gradients of the step:
+    // the core-gradient sum must not sum the LM-head block again
+    ctx->lm_reduced = true;
     ncclResult_t nr = ncclGroupStart();
     if (nr == ncclSuccess) nr = ncclAllReduce(dW, dW, (size_t)cap * d, ncclFloat, ncclSum, ctx->comm, st);
     if (nr == ncclSuccess) nr = ncclAllReduce(db, db, cap, ncclFloat, ncclSum, ctx->comm, st);
@@ -1164,7 +1232,9 @@ int run_emb_update(aideen_ctx *ctx, int N, const aideen_step_args *a) {
   if (dp) {
     if (!b.grad_all) CU(dalloc(&b.grad_all, ctx->gcap * d));
     ncclResult_t nr = ncclGroupStart();
-    if (nr == ncclSuccess) nr = ncclAllGather(b.tokens, b.tok_all, N, ncclInt32, ctx->comm, st);
+    // (with the CSR built early, every rank's tokens were gathered then)
+    if (nr == ncclSuccess && !ctx->emb_csr_ready)
+      nr = ncclAllGather(b.tokens, b.tok_all, N, ncclInt32, ctx->comm, st);
     if (nr == ncclSuccess) nr = ncclAllGather(grad, b.grad_all, (size_t)N * d, ncclFloat, ctx->comm, st);
     const ncclResult_t n2 = ncclGroupEnd();
     if (nr != ncclSuccess || n2 != ncclSuccess)
@@ -1197,17 +1267,25 @@ int run_emb_update(aideen_ctx *ctx, int N, const aideen_step_args *a) {
   return AIDEEN_OK;
 }
 
-// One GPU, no profiling: the step's token CSR on the embedding stream while
-// the forward runs (it needs only the token ids).
+// No profiling: the step's token CSR on the embedding stream while the forward
+// runs (it needs only the token ids; with a communicator, every rank's ids,
+// gathered here on the context stream).
 int emb_csr_early(aideen_ctx *ctx, int N) {
   DevBufs &b = ctx->b;
-  if (ctx->prof || (ctx->comm && ctx->nranks > 1) || !ctx->est || !b.cuniq || (size_t)N > ctx->gcap ||
-      N > emb_csr_max_tokens())
-    return AIDEEN_OK;  // the update builds it itself (first step, data parallel, profiling)
+  const bool dp = ctx->comm && ctx->nranks > 1;
+  const int Ng = dp ? N * ctx->nranks : N;
+  if (ctx->prof || !ctx->est || !b.cuniq || (size_t)Ng > ctx->gcap || Ng > emb_csr_max_tokens())
+    return AIDEEN_OK;  // the update builds it itself (first step, profiling)
+  const int32_t *tok = b.tokens;
+  if (dp) {
+    const ncclResult_t nr = ncclAllGather(b.tokens, b.tok_all, N, ncclInt32, ctx->comm, ctx->stream);
+    if (nr != ncclSuccess) return set_err(ctx, AIDEEN_E_NCCL, std::string("ncclAllGather: ") + ncclGetErrorString(nr));
+    tok = b.tok_all;
+  }
   CU(cudaEventRecord(ctx->ev_e0, ctx->stream));
   CU(cudaStreamWaitEvent(ctx->est, ctx->ev_e0, 0));
   ctx->launches++;
-  CU(launch_emb_csr(b.tokens, N, (int)ctx->cfg.vocab, b.cuniq, b.coff, b.cpos, b.ints + 1, ctx->est));
+  CU(launch_emb_csr(tok, Ng, (int)ctx->cfg.vocab, b.cuniq, b.coff, b.cpos, b.ints + 1, ctx->est));
   ctx->emb_csr_ready = true;
   return AIDEEN_OK;
 }
@@ -1272,8 +1350,54 @@ int run_lm_update(aideen_ctx *ctx, const aideen_update *u, float bc1, float bc2)
   return AIDEEN_OK;
 }
 
+// Adam on this rank's shard of both reduce-scattered buckets (and on the
+// small remainders every rank holds summed), then the weights all-gathered.
+int run_update_sharded(aideen_ctx *ctx, const aideen_update *u, float bc1, float bc2) {
+  DevBufs &b = ctx->b;
+  cudaStream_t st = ctx->stream;
+  size_t boff[2], blen[2];
+  grad_buckets(ctx, boff, blen);
+  const size_t n = (size_t)ctx->nranks;
+  for (int k = 0; k < 2; ++k) {
+    const size_t cnt = blen[k] / n, rem = blen[k] - cnt * n;
+    const size_t o = boff[k] + (size_t)ctx->rank * cnt, orr = boff[k] + cnt * n;
+    if (cnt) KL(launch_adam(b.W + o, b.G + o, b.M1 + o, b.M2 + o, cnt, u->lr, u->beta1, u->beta2, u->eps, bc1, bc2,
+                            u->grad_scale, st));
+    if (rem) KL(launch_adam(b.W + orr, b.G + orr, b.M1 + orr, b.M2 + orr, rem, u->lr, u->beta1, u->beta2, u->eps,
+                            bc1, bc2, u->grad_scale, st));
+  }
+  ncclResult_t r = ncclGroupStart();
+  for (int k = 0; k < 2 && r == ncclSuccess; ++k) {
+    const size_t cnt = blen[k] / n;
+    if (cnt)
+      r = ncclAllGather(b.W + boff[k] + (size_t)ctx->rank * cnt, b.W + boff[k], cnt, ncclFloat, ctx->comm, st);
+  }
+  const ncclResult_t r2 = ncclGroupEnd();
+  if (r != ncclSuccess || r2 != ncclSuccess)
+    return set_err(ctx, AIDEEN_E_NCCL, std::string("ncclAllGather: ") +
+                                           ncclGetErrorString(r != ncclSuccess ? r : r2));
+  return AIDEEN_OK;
+}
+
 int run_update(aideen_ctx *ctx, const aideen_update *u) {
   if (!u) return set_err(ctx, AIDEEN_E_INVALID, "null update");
+  if (ctx->shard_step) {
+    // the core gradients were reduce-scattered during the weight gradients;
+    // the LM head's sum is still owed in dense mode
+    ctx->shard_step = false;
+    if (ctx->lm_ready && !ctx->lm_reduced && u->update_lm_head) {
+      const ncclResult_t nr = ncclAllReduce(ctx->b.Glm, ctx->b.Glm, ctx->lm_len, ncclFloat, ncclSum, ctx->comm,
+                                            ctx->stream);
+      if (nr != ncclSuccess) return set_err(ctx, AIDEEN_E_NCCL, std::string("ncclAllReduce: ") + ncclGetErrorString(nr));
+    }
+    ctx->lm_reduced = false;
+    const double t = u->step < 1 ? 1.0 : (double)u->step;
+    const float bc1 = (float)(1.0 - std::pow((double)u->beta1, t));
+    const float bc2 = (float)(1.0 - std::pow((double)u->beta2, t));
+    CHK(run_update_sharded(ctx, u, bc1, bc2));
+    if (u->update_lm_head && ctx->lm_ready) CHK(run_lm_update(ctx, u, bc1, bc2));
+    return AIDEEN_OK;
+  }
   if (u->allreduce) CHK(run_allreduce(ctx, 0));
   DevBufs &b = ctx->b;
   cudaStream_t st = ctx->stream;
@@ -1437,6 +1561,8 @@ void aideen_destroy(aideen_ctx *ctx) {
   if (ctx->lmst) { cudaStreamSynchronize(ctx->lmst); cudaStreamDestroy(ctx->lmst); }
   if (ctx->ast) { cudaStreamSynchronize(ctx->ast); cudaStreamDestroy(ctx->ast); }
   if (ctx->est) cudaStreamDestroy(ctx->est);
+  if (ctx->hK) cudaFreeHost(ctx->hK);
+  if (ctx->ev_K) cudaEventDestroy(ctx->ev_K);
   if (ctx->ev_e0) cudaEventDestroy(ctx->ev_e0);
   if (ctx->ev_emb) cudaEventDestroy(ctx->ev_emb);
   if (ctx->ev_da) cudaEventDestroy(ctx->ev_da);
@@ -1789,7 +1915,15 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
     CHK(run_adjoint(ctx, N, ctx->b.pre, nullptr, ctx->b.dl_dh, nullptr, a->adj_iters, a->run.damping,
                     a->anderson_m));
   }
-  CHK(run_weight_grads(ctx, a->emb_update == 2));
+  // data parallel with Adam: sharded update (no profiling: its per-class
+  // timing assumes one stream)
+  ctx->shard_step = a->update.allreduce && ctx->comm && ctx->nranks > 1 && a->update.rule == AIDEEN_RULE_ADAM &&
+                    !ctx->prof && !getenv("AIDEEN_NO_SHARDED_UPDATE");
+  const int wg = run_weight_grads(ctx, a->emb_update == 2);
+  if (wg != AIDEEN_OK) {
+    ctx->shard_step = false;
+    return wg;
+  }
   if (ctx->lmg_pending) {  // the last chunk's dW_lm and LM-head sums
     CU(cudaStreamWaitEvent(ctx->stream, ctx->ev_lmg, 0));
     ctx->lmg_pending = false;

@@ -56,7 +56,7 @@ def test_nccl_gradient_allreduce_two_gpus():
 DP, HP, BP, TP = 128, 4, 4, 16   # the pipelined step's shape in the parity tests
 
 
-def _rank_step(rank, uid, q):
+def _rank_step(rank, uid, uid2, q):
     """One data-parallel training step per rank, through the pipelined path
     (where the LM-head gradients are summed on their own stream)."""
     from aideen_b200.backend import GpuDeqBackend, RunConfig
@@ -64,28 +64,35 @@ def _rank_step(rank, uid, q):
     rng = np.random.default_rng(200 + rank)
     tok = rng.integers(0, V, (BP, TP)).astype(np.int32)
     tg = rng.integers(0, V, (BP, TP)).astype(np.int32)
+    import os
     res = {}
-    for dp in (False, True):
+    for dp in (False, True, "sharded"):
+        # the gradient sum is read back from the plain allreduce; the default
+        # sharded update must give the same weights
+        if dp is True:
+            os.environ["AIDEEN_NO_SHARDED_UPDATE"] = "1"
+        else:
+            os.environ.pop("AIDEEN_NO_SHARDED_UPDATE", None)
         be = GpuDeqBackend(DP, HP, max_batch=BP, max_seq_len=TP, vocab=V, device=rank)
         be.upload_weights(init_all_weights(DP, HP, seed=6))
         be.upload_lm_head(*init_lm_head(DP, V))
         be.upload_embedding(init_embedding(DP, V))
         if dp:
-            be.comm_init(uid, 2, rank)
+            be.comm_init(uid if dp is True else uid2, 2, rank)
         be.train_step(tok, tg, BP, TP, RunConfig(fpm=True), adj_iters=12, lr=1e-3, step=1,
-                      allreduce=dp, grad_scale=0.5 if dp else 1.0)
+                      allreduce=bool(dp), grad_scale=0.5 if dp else 1.0)
         res[dp] = (be.read("lm_grads", (V * DP + V + DP,)), be.read_grads(), be.read_weights())
         be.close()
-    q.put((rank, res[False][0], res[False][1], res[True]))
+    q.put((rank, res[False][0], res[False][1], res[True], res["sharded"][2]))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_pipelined_train_step_two_gpus_sums_all_gradients():
     from aideen_b200.backend import GpuDeqBackend
-    uid = GpuDeqBackend.comm_unique_id()
+    uid, uid2 = GpuDeqBackend.comm_unique_id(), GpuDeqBackend.comm_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    ps = [ctx.Process(target=_rank_step, args=(r, uid, q)) for r in range(2)]
+    ps = [ctx.Process(target=_rank_step, args=(r, uid, uid2, q)) for r in range(2)]
     for p in ps:
         p.start()
     out = {r: rest for r, *rest in (q.get(timeout=300) for _ in range(2))}
@@ -99,6 +106,9 @@ def test_pipelined_train_step_two_gpus_sums_all_gradients():
         assert np.linalg.norm(lm - lm_sum) / np.linalg.norm(lm_sum) < 1e-6
         assert np.linalg.norm(g - g_sum) / np.linalg.norm(g_sum) < 1e-6
     assert np.array_equal(out[0][2][2], out[1][2][2])   # identical update on both ranks
+    # the sharded update (reduce-scatter, Adam per shard, all-gather) gives the same weights
+    for r in range(2):
+        np.testing.assert_allclose(out[r][3], out[r][2][2], rtol=0, atol=1e-6)
 
 
 DR, HR, BR, TR, VR, NSR = 128, 4, 2, 16, 97, 24   # the reference-step case
@@ -117,9 +127,12 @@ def _rank_ref_step(rank, uid, q):
     be.upload_weights(init_all_weights(DR, HR, seed=7))
     be.upload_lm_head(*init_lm_head(DR, VR))
     be.upload_embedding(init_embedding(DR, VR))
+    import os
+    os.environ["AIDEEN_NO_SHARDED_UPDATE"] = "1"   # the summed gradients stay readable
     be.comm_init(uid, 2, rank)
     loss = be.train_step(tok, tg, BR, TR, RunConfig(fpm=True), adj_iters=12, lr=1e-3, step=1,
                          allreduce=True, grad_scale=1.0, lm_samples=NSR, emb_update=1)
+    os.environ.pop("AIDEEN_NO_SHARDED_UPDATE")
     out = dict(tok=tok, tg=tg, loss=loss, grads=be.read_grads(), W=be.read_weights(),
                lm=be.read_lm_head(), emb=be.read_embedding(), dl=be.read("dl_dh", (BR * TR, DR)),
                lmg=be.read("lm_grads", (VR * DR + VR + DR,)))
