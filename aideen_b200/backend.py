@@ -87,6 +87,8 @@ _SIGS = {
     "aideen_download_lm_head": (C.c_int, [_P, _P, _P, _P]),
     "aideen_download_embedding": (C.c_int, [_P, _P]),
     "aideen_temporal_scan": (C.c_int, [_P, C.c_uint32, C.c_uint32, _P, C.c_int]),
+    "aideen_download_adam": (C.c_int, [_P, _P, _P, C.c_size_t, _P, _P]),
+    "aideen_upload_adam": (C.c_int, [_P, _P, _P, C.c_size_t, _P, _P]),
     "aideen_upload_embedding": (C.c_int, [_P, _P]),
     "aideen_reset_state": (C.c_int, [_P]),
     "aideen_reset_optimizer": (C.c_int, [_P]),
@@ -264,6 +266,26 @@ class GpuDeqBackend:
         self._check(self.lib.aideen_temporal_scan(self.ctx, batch, seq_len, _ptr(hs) if hs is not None else None,
                                                   HOST), "temporal_scan")
         self.batch, self.seq_len = batch, seq_len
+
+    def read_adam(self):
+        """(m_core, v_core, m_lm, v_lm): core moments in the packed AllWeights
+        layout, LM-head moments as [vocab*d + vocab + d] (None without a head)."""
+        n = self.layout.total
+        mc, vc = np.empty(n, np.float32), np.empty(n, np.float32)
+        nl = self.vocab * self.d + self.vocab + self.d if self.vocab else 0
+        ml = np.empty(nl, np.float32) if nl else None
+        vl = np.empty(nl, np.float32) if nl else None
+        self._check(self.lib.aideen_download_adam(self.ctx, _ptr(mc), _ptr(vc), n,
+                                                  _ptr(ml) if nl else None, _ptr(vl) if nl else None), "read_adam")
+        return mc, vc, ml, vl
+
+    def upload_adam(self, m_core, v_core, m_lm=None, v_lm=None):
+        mc, vc = _f32(m_core), _f32(v_core)
+        ml = _f32(m_lm) if m_lm is not None else None
+        vl = _f32(v_lm) if v_lm is not None else None
+        self._check(self.lib.aideen_upload_adam(self.ctx, _ptr(mc), _ptr(vc), mc.size,
+                                                _ptr(ml) if ml is not None else None,
+                                                _ptr(vl) if vl is not None else None), "upload_adam")
 
     def read_embedding(self):
         out = np.empty((self.vocab, self.d), np.float32)

@@ -1676,6 +1676,49 @@ int aideen_download_grads(aideen_ctx *ctx, float *out, size_t n) {
   return download_packed(ctx, ctx->b.G, out, n);
 }
 
+// LM-head block [V*d | V (padded) | d] <-> packed [V*d + V + d] host array.
+static int lm_block_copy(aideen_ctx *ctx, float *dev, float *host, bool to_host) {
+  const size_t V = ctx->cfg.vocab, d = ctx->cfg.d_model;
+  const size_t seg[3][2] = {{0, V * d}, {ctx->lm_b, V}, {ctx->lm_g, d}};
+  size_t o = 0;
+  for (auto &sg : seg) {
+    if (to_host) CU(cudaMemcpyAsync(host + o, dev + sg[0], sg[1] * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    else CU(cudaMemcpyAsync(dev + sg[0], host + o, sg[1] * 4, cudaMemcpyHostToDevice, ctx->stream));
+    o += sg[1];
+  }
+  return AIDEEN_OK;
+}
+
+int aideen_download_adam(aideen_ctx *ctx, float *m_core, float *v_core, size_t n_core, float *m_lm, float *v_lm) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  CU(join_side(ctx));
+  if (m_core) CHK(download_packed(ctx, ctx->b.M1, m_core, n_core));
+  if (v_core) CHK(download_packed(ctx, ctx->b.M2, v_core, n_core));
+  if (ctx->lm_len) {
+    if (m_lm) CHK(lm_block_copy(ctx, ctx->b.Mlm1, m_lm, true));
+    if (v_lm) CHK(lm_block_copy(ctx, ctx->b.Mlm2, v_lm, true));
+  }
+  return sync_and_check(ctx);
+}
+
+int aideen_upload_adam(aideen_ctx *ctx, const float *m_core, const float *v_core, size_t n_core, const float *m_lm,
+                       const float *v_lm) {
+  if (!ctx) return AIDEEN_E_INVALID;
+  if ((m_core || v_core) && n_core != ctx->Lx.total) return set_err(ctx, AIDEEN_E_INVALID, "bad moment length");
+  CU(join_side(ctx));
+  for (int i = 0; i < 2; ++i) {
+    const float *src = i ? v_core : m_core;
+    if (!src) continue;
+    CU(cudaMemcpyAsync(ctx->b.stage, src, n_core * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CHK(repack(ctx, i ? ctx->b.M2 : ctx->b.M1, ctx->b.stage, true, cudaMemcpyDeviceToDevice));
+  }
+  if (ctx->lm_len) {
+    if (m_lm) CHK(lm_block_copy(ctx, ctx->b.Mlm1, const_cast<float *>(m_lm), false));
+    if (v_lm) CHK(lm_block_copy(ctx, ctx->b.Mlm2, const_cast<float *>(v_lm), false));
+  }
+  return sync_and_check(ctx);
+}
+
 int aideen_upload_lm_head(aideen_ctx *ctx, const float *w_lm, const float *b_lm, const float *g_lm) {
   if (!ctx) return AIDEEN_E_INVALID;
   const size_t V = ctx->cfg.vocab, d = ctx->cfg.d_model;

@@ -156,6 +156,14 @@ int aideen_upload_embedding(aideen_ctx *ctx, const float *emb /*[vocab][d]*/);
 /* Embedding table back to the host (GpuEmbeddingTrainer's weights readback,
  * gpu_embedding.rs weights_buffer). */
 int aideen_download_embedding(aideen_ctx *ctx, float *emb /*[vocab][d]*/);
+/* Adam moments for checkpoints (the reference's Adam::save_state / load_state,
+ * optimizer.rs:246-325): DEQ core in the packed AllWeights layout (n_core =
+ * aideen_all_weights_len) and the LM head as [vocab*d + vocab + d]; NULL
+ * skips a part.  After data-parallel train steps every rank holds current
+ * moments only for its own shard of the core (the sharded update). */
+int aideen_download_adam(aideen_ctx *ctx, float *m_core, float *v_core, size_t n_core, float *m_lm, float *v_lm);
+int aideen_upload_adam(aideen_ctx *ctx, const float *m_core, const float *v_core, size_t n_core,
+                       const float *m_lm, const float *v_lm);
 /* Zero the carried FPM memory MState (reset_state gpu_deq.rs:3127). */
 int aideen_reset_state(aideen_ctx *ctx);
 /* Zero the Adam moments of the DEQ core and LM head. */

@@ -344,3 +344,47 @@ def test_temporal_carrier_scan(d, h):
         assert rel(be.read("hist_ctx", (B, T, h, d)), hist) < 1e-5
         assert rel(be.read("mstate", (B, h, d)), m) < 1e-5
     be.close()
+
+
+def test_checkpoint_resume_continues_identically(tmp_path):
+    """Save the weights (.aidn) and Adam state (.opt) after two steps, load them
+    into a fresh context: the third step (from a reset memory state) is the
+    same on both."""
+    from aideen_b200 import checkpoint as ck
+    d, h, B, T, V = 128, 4, 2, 8, 61
+    W = init_all_weights(d, h, seed=3)
+    lm, emb = init_lm_head(d, V), init_embedding(d, V)
+    rng = np.random.default_rng(4)
+    toks = [rng.integers(0, V, (B, T)).astype(np.int32) for _ in range(3)]
+    rc = RunConfig(fpm=True)
+
+    def fresh():
+        be = GpuDeqBackend(d, h, max_batch=B, max_seq_len=T, vocab=V)
+        return be
+
+    a = fresh()
+    a.upload_weights(W)
+    a.upload_lm_head(*lm)
+    a.upload_embedding(emb)
+    for k in range(2):
+        a.train_step(toks[k], toks[k], B, T, rc, adj_iters=8, step=k + 1)
+    ck.full_model(a.read_weights(), d, h, a.read_lm_head(), a.read_embedding()).save(str(tmp_path / "m.aidn"))
+    ck.save_opt(str(tmp_path / "m.opt"), 2, ck.adam_tensors(*a.read_adam()[:2], d, h, *a.read_adam()[2:]))
+    b = fresh()
+    w, lmb, e = ck.unpack_full_model(ck.AidenModel.load(str(tmp_path / "m.aidn")))
+    b.upload_weights(w)
+    b.upload_lm_head(*lmb)
+    b.upload_embedding(e)
+    step, t = ck.load_opt(str(tmp_path / "m.opt"))
+    b.upload_adam(*ck.adam_from_tensors(t, d, h))
+    # the carried FPM memory and TBPTT carry are run state, not checkpointed:
+    # both contexts start the next step from zero
+    a.reset_state()
+    b.reset_state()
+    la = a.train_step(toks[2], toks[2], B, T, rc, adj_iters=8, step=3)
+    lb = b.train_step(toks[2], toks[2], B, T, rc, adj_iters=8, step=step + 1)
+    assert la == lb
+    assert np.array_equal(a.read_weights(), b.read_weights())
+    assert all(np.array_equal(x, y) for x, y in zip(a.read_lm_head(), b.read_lm_head()))
+    a.close()
+    b.close()
