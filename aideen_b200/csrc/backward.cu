@@ -181,6 +181,53 @@ __global__ void __launch_bounds__(MAXT, MINB) adjoint_kernel(AdjointArgs a) {
     float4 hist[(MA > 0 && !HS) ? MA : 1][F];
     float *ring = stage0 + 2 * stage_f + (size_t)s * d;  // HS: iterate slot q at ring + q * hd
     int k0 = 0;
+    if constexpr (MA == 0) {
+      // Two iterations per warp reduction.  With u = w (*) a,
+      //   c_k     = w . v_k,
+      //   c_{k+1} = w . v_{k+1} = w.rhs + u . v_k + ncs_k * w.pre,
+      // so w . v_k and u . v_k, reduced together (one exchange splits the two
+      // sums between the half-warps, four more finish them, one more shares
+      // them back), give both steps' scalars: about half the reduction
+      // instructions per iteration, which with the FMAs bounds this kernel at
+      // 20 iterations (the FMA pipe and the issue slots, not HBM).
+      float wr = 0.f, wp = 0.f;
+#pragma unroll
+      for (int f = 0; f < F; ++f) {
+        wr += dot4(wv[f], rhs[f]);
+        wp += dot4(wv[f], pre[f]);
+      }
+      wr = warp_sum(wr);
+      wp = warp_sum(wp);
+      float4 u[F];
+#pragma unroll
+      for (int f = 0; f < F; ++f) u[f] = wv[f] * av[f];
+      const bool upper = (lane & 16) != 0;
+      for (; k0 + 2 <= a.iters; k0 += 2) {
+        float A0 = 0.f, A1 = 0.f, B0 = 0.f, B1 = 0.f;
+#pragma unroll
+        for (int f = 0; f < F; ++f) {
+          A0 = fmaf(wv[f].x, v[f].x, A0); A1 = fmaf(wv[f].y, v[f].y, A1);
+          A0 = fmaf(wv[f].z, v[f].z, A0); A1 = fmaf(wv[f].w, v[f].w, A1);
+          B0 = fmaf(u[f].x, v[f].x, B0); B1 = fmaf(u[f].y, v[f].y, B1);
+          B0 = fmaf(u[f].z, v[f].z, B0); B1 = fmaf(u[f].w, v[f].w, B1);
+        }
+        const float A = A0 + A1, Bq = B0 + B1;
+        // lanes < 16 keep A, lanes >= 16 keep B; each sends the other half's value
+        float x = (upper ? Bq : A) + __shfl_xor_sync(0xffffffffu, upper ? A : Bq, 16);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+        const float y = __shfl_xor_sync(0xffffffffu, x, 16);
+        const float Asum = upper ? y : x, Bsum = upper ? x : y;
+        const float ncs0 = -Asum * inv_den;
+        const float ncs1 = -(wr + Bsum + ncs0 * wp) * inv_den;
+        const float4 n0 = f4(ncs0), n1 = f4(ncs1);
+#pragma unroll
+        for (int f = 0; f < F; ++f) {
+          const float4 v1 = fma4(n0, pre[f], fma4(av[f], v[f], rhs[f]));
+          v[f] = fma4(n1, pre[f], fma4(av[f], v1, rhs[f]));
+        }
+      }
+    }
     for (int k = k0; k < a.iters; ++k) {
       // w . v in two float4 partial sums (ILP), packed FMAs throughout
       float4 c0 = f4(0.f), c1 = f4(0.f);
