@@ -474,9 +474,10 @@ __global__ void attn_bwd_softmax_kernel(AttnBwdArgs a) {
   const int n = blockIdx.x, s = threadIdx.x >> 5, c = threadIdx.x & 31;
   const int h = a.h, d = a.d;
   const size_t row = ((size_t)n * h + s) * kHeadDim + c;
-  Ks[s][c] = a.Kh[row] + a.W[a.off_kb + (size_t)s * d + c];
-  Qs[s][c] = a.Qh[row] + a.W[a.off_qb + (size_t)s * d + c];
-  Vs[s][c] = a.Vh[row];
+  const size_t qrow = ((size_t)n * h + s) * a.qkv_ld + c;
+  Ks[s][c] = a.Kh[qrow] + a.W[a.off_kb + (size_t)s * d + c];
+  Qs[s][c] = a.Qh[qrow] + a.W[a.off_qb + (size_t)s * d + c];
+  Vs[s][c] = a.Vh[qrow];
   if (c < h) al[s][c] = a.alpha[((size_t)n * h + s) * h + c];
   const float nn = a.nmix[row], dnn = a.dn[row], r = a.rmix[(size_t)n * h + s];
   const float ndn = warp_sum(nn * dnn);
@@ -500,7 +501,7 @@ __global__ void attn_bwd_softmax_kernel(AttnBwdArgs a) {
       dq += dl * Ks[k][c];
       if (c == 0) dlg[s][k] = dl;
     }
-  a.dQ[row] = gain * dq;
+  a.dQ[qrow] = gain * dq;
   __syncthreads();
   // key/value slot s
   float dk = 0.f, dv = 0.f;
@@ -509,8 +510,8 @@ __global__ void attn_bwd_softmax_kernel(AttnBwdArgs a) {
     dk += dlg[q][s] * Qs[q][c];
     dv += (al[q][s] - ih) * dmix[q][c];
   }
-  a.dK[row] = gain * dk;
-  a.dV[row] = dv;
+  a.dK[qrow] = gain * dk;
+  a.dV[qrow] = dv;
 }
 
 cudaError_t launch_attn_bwd_softmax(const AttnBwdArgs &a, int N, cudaStream_t st) {
@@ -608,13 +609,14 @@ cudaError_t launch_add_rowbias(float *dst, const float *x, const float *bias, si
 }
 
 __global__ void colsum_kernel(const float *__restrict__ X, int rows, int ncols, long ld,
-                              float *__restrict__ out, int seg, long ostride, int accumulate) {
+                              float *__restrict__ out, int seg, long ostride, int accumulate, long istride) {
   __shared__ float red[32][33];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + tx;
+  const long ic = (long)(c / seg) * istride + c % seg;
   float acc = 0.f;
   if (c < ncols)
-    for (int r = ty; r < rows; r += 32) acc += X[(size_t)r * ld + c];
+    for (int r = ty; r < rows; r += 32) acc += X[(size_t)r * ld + ic];
   red[ty][tx] = acc;
   __syncthreads();
   if (ty == 0 && c < ncols) {
@@ -626,10 +628,10 @@ __global__ void colsum_kernel(const float *__restrict__ X, int rows, int ncols, 
 }
 
 cudaError_t launch_colsum(const float *X, int rows, int ncols, long ld, float *out, int seg,
-                          long ostride, bool accumulate, cudaStream_t st) {
+                          long ostride, bool accumulate, cudaStream_t st, long istride) {
   if (ncols <= 0) return cudaSuccess;
   colsum_kernel<<<(ncols + 31) / 32, 1024, 0, st>>>(X, rows, ncols, ld, out, seg, ostride,
-                                                     accumulate ? 1 : 0);
+                                                     accumulate ? 1 : 0, istride > 0 ? istride : seg);
   return cudaGetLastError();
 }
 

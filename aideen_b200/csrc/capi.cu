@@ -38,6 +38,10 @@ struct DevBufs {
         *mstate = nullptr;
   int32_t *iters = nullptr;
   float *v = nullptr, *gpre = nullptr, *dl_dh = nullptr, *rhs_slot = nullptr, *nsg = nullptr;
+  // Q | K | V head projections (and their gradients) of a (token, slot) row side
+  // by side, [N][h][96]; Qh..Vh / dQ..dV point into them; Wcat [h][d][96] is
+  // the matching operand of W_q | W_k | W_v (refreshed at every forward)
+  float *qkv = nullptr, *dqkv = nullptr, *Wcat = nullptr;
   float *da = nullptr, *dn = nullptr, *dQ = nullptr, *dK = nullptr, *dV = nullptr,
         *dsig = nullptr, *dRc = nullptr, *dS = nullptr;
   float *lmp = nullptr, *Glm = nullptr, *Mlm1 = nullptr, *Mlm2 = nullptr;  // [V*d | V | d]
@@ -329,15 +333,14 @@ int run_forward_prep_rows(aideen_ctx *ctx, const aideen_run *r, long r0, int R) 
     // 32-wide K/V/Q heads of src = signal + anchor (:281-355); src is kept for the backward
     float *src = b.src + r0 * hd;
     KL(launch_add_rowbias(src, signal, W + L.slot_anchor, R, (size_t)hd, st));
-    KL(gemm_any(ctx, gemm(R, kHeadDim, d, h, src, hd, d, false, W + L.wk, d, (long)d * d,
-                     false, b.Kh + r0 * H32, H32, kHeadDim)));
-    KL(gemm_any(ctx, gemm(R, kHeadDim, d, h, src, hd, d, false, W + L.wv, d, (long)d * d,
-                     false, b.Vh + r0 * H32, H32, kHeadDim)));
-    KL(gemm_any(ctx, gemm(R, kHeadDim, d, h, src, hd, d, false, W + L.wq, d, (long)d * d,
-                     false, b.Qh + r0 * H32, H32, kHeadDim)));
+    // Q | K | V heads in one GEMM against the packed [d][96] operand
+    const long H96 = (long)h * 96;
+    if (r0 == 0) KL(launch_pack_qkv(W, L.wq, L.wk, L.wv, h, d, b.Wcat, st));
+    KL(gemm_any(ctx, gemm(R, 96, d, h, src, hd, d, false, b.Wcat, 96, (long)d * 96, false, b.qkv + r0 * H96, H96,
+                          96)));
     AttnArgs a{};
     a.h = h; a.d = d; a.W = W; a.off_qb = L.q_bias; a.off_kb = L.k_bias; a.off_anchor = L.slot_anchor;
-    a.Qh = b.Qh + r0 * H32; a.Kh = b.Kh + r0 * H32; a.Vh = b.Vh + r0 * H32;
+    a.Qh = b.Qh + r0 * H96; a.Kh = b.Kh + r0 * H96; a.Vh = b.Vh + r0 * H96; a.qkv_ld = 96;
     a.alpha = b.alpha + r0 * h * h; a.nmix = b.nmix + r0 * H32; a.rmix = b.rmix + r0 * h;
     a.signal = signal; a.amat = b.amat + r0 * hd; a.A = b.A + r0 * hd;
     a.scale = b.scale + r0 * h; a.rho = b.rho + r0 * h; a.Rsrc = b.Rsrc + r0 * h;
@@ -577,6 +580,8 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   a.gpre = b.gpre; a.amat = b.amat; a.scale = b.scale; a.rho = b.rho; a.Rsrc = b.Rsrc;
   a.signal = b.signal; a.da = b.da; a.dRc = b.dRc; a.dn = b.dn; a.nmix = b.nmix; a.rmix = b.rmix;
   a.alpha = b.alpha; a.Qh = b.Qh; a.Kh = b.Kh; a.Vh = b.Vh; a.dQ = b.dQ; a.dK = b.dK; a.dV = b.dV;
+  a.qkv_ld = 96;
+  const long H96 = (long)h * 96;
   if (sc) {
     KL(launch_attn_bwd_scale(a, N * h, st));
     if (fork_attn) {
@@ -602,18 +607,17 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
     const size_t woff[3] = {L.wq, L.wk, L.wv};
     for (int i = 0; i < 3; ++i)
       KL(on_side([&] {
-        return gemm_any(ctx, gemm(d, kHeadDim, N, h, b.src, (long)h * d, d, true, dqkv[i], H32, kHeadDim,
+        return gemm_any(ctx, gemm(d, kHeadDim, N, h, b.src, (long)h * d, d, true, dqkv[i], H96, 96,
                                   false, G + woff[i], d, (long)d * d));
       }));
-    KL(launch_colsum(b.dQ, N, H32, H32, G + L.q_bias, kHeadDim, d, false, sst));
-    KL(launch_colsum(b.dK, N, H32, H32, G + L.k_bias, kHeadDim, d, false, sst));
+    KL(launch_colsum(b.dQ, N, H32, H96, G + L.q_bias, kHeadDim, d, false, sst, 96));
+    KL(launch_colsum(b.dK, N, H32, H96, G + L.k_bias, kHeadDim, d, false, sst, 96));
     if (fork_attn) CU(cudaEventRecord(ctx->ev_adone, ctx->ast));
     tl_mark(ctx, "wg_qkv", st);
     KL(launch_dsig_init(a, b.dsig, N * h, 1, st));
-    // dsrc[n][s][j] += sum_c d{Q,K,V}[n][s][c] W[s][j*d + c]
-    for (int i = 0; i < 3; ++i)
-      KL(gemm_any(ctx, gemm(N, d, kHeadDim, h, dqkv[i], H32, kHeadDim, false, W + woff[i], d, (long)d * d,
-                       true, b.dsig, (long)h * d, d, 1.f, 1.f)));
+    // dsrc[n][s][j] += sum_c d{Q|K|V}[n][s][c] Wcat[s][j][c], one GEMM of depth 96
+    KL(gemm_any(ctx, gemm(N, d, 96, h, b.dqkv, H96, 96, false, b.Wcat, 96, (long)d * 96, true, b.dsig,
+                          (long)h * d, d, 1.f, 1.f)));
     tl_mark(ctx, "dsrc", st);
     KL(launch_colsum(b.dsig, N, h * d, (long)h * d, G + L.slot_anchor, h * d, 0, false, st));
   } else {
@@ -1459,8 +1463,10 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   A(&b.W, ctx->W_len); A(&b.G, ctx->W_len); A(&b.M1, ctx->W_len); A(&b.M2, ctx->W_len);
   A(&b.S_in, N * d); A(&b.tokens, N); A(&b.targets, N);
   A(&b.signal, Nhd); A(&b.A, Nhd); A(&b.amat, Nhd); A(&b.src, Nhd);
-  A(&b.Qh, NH32); A(&b.Kh, NH32); A(&b.Vh, NH32); A(&b.nmix, NH32); A(&b.dn, NH32);
-  A(&b.dQ, NH32); A(&b.dK, NH32); A(&b.dV, NH32);
+  A(&b.qkv, 3 * NH32); A(&b.dqkv, 3 * NH32); A(&b.Wcat, (size_t)h * d * 96);
+  A(&b.nmix, NH32); A(&b.dn, NH32);
+  b.Qh = b.qkv; b.Kh = b.qkv + 32; b.Vh = b.qkv + 64;
+  b.dQ = b.dqkv; b.dK = b.dqkv + 32; b.dV = b.dqkv + 64;
   A(&b.alpha, N * h * h); A(&b.rmix, N * h); A(&b.scale, N * h); A(&b.rho, N * h);
   A(&b.Rsrc, N * h); A(&b.dRc, N * h); A(&b.iters, N * h);
   A(&b.hstar, Nhd); A(&b.pre, Nhd); A(&b.hist, Nhd); A(&b.fpmctx, Nhd);
@@ -1492,7 +1498,13 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
     e = cudaStreamCreateWithPriority(&ctx->pic, cudaStreamNonBlocking, hi);
   }
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_prep, cudaEventDisableTiming);
-  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->fst, cudaStreamNonBlocking);
+  if (e == cudaSuccess) {
+    // the FPM backward is the longest chain after the adjoint: its CTAs go
+    // ahead of the attention-branch GEMMs that run beside it
+    int lo = 0, hi = 0;
+    cudaDeviceGetStreamPriorityRange(&lo, &hi);
+    e = cudaStreamCreateWithPriority(&ctx->fst, cudaStreamNonBlocking, hi);
+  }
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_g0, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_fdone, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->lmst, cudaStreamNonBlocking);
@@ -1538,10 +1550,10 @@ void aideen_destroy(aideen_ctx *ctx) {
   if (ctx->est) cudaStreamSynchronize(ctx->est);
   if (ctx->comm) ncclCommDestroy(ctx->comm);
   DevBufs &b = ctx->b;
-  void *ptrs[] = {b.W, b.G, b.M1, b.M2, b.S_in, b.tokens, b.targets, b.signal, b.A, b.amat, b.Qh,
-                  b.Kh, b.Vh, b.alpha, b.nmix, b.rmix, b.scale, b.rho, b.Rsrc, b.hstar, b.pre,
+  void *ptrs[] = {b.W, b.G, b.M1, b.M2, b.S_in, b.tokens, b.targets, b.signal, b.A, b.amat, b.qkv,
+                  b.dqkv, b.Wcat, b.alpha, b.nmix, b.rmix, b.scale, b.rho, b.Rsrc, b.hstar, b.pre,
                   b.pooled, b.hist, b.fpmctx, b.mstate, b.iters, b.v, b.gpre, b.dl_dh, b.rhs_slot,
-                  b.nsg, b.da, b.dn, b.dQ, b.dK, b.dV, b.dsig, b.dRc, b.dS, b.lmp, b.Glm, b.Mlm1,
+                  b.nsg, b.da, b.dn, b.dsig, b.dRc, b.dS, b.lmp, b.Glm, b.Mlm1,
                   b.Mlm2, b.y, b.lrms, b.logits, b.dy, b.ggp, b.loss_rows, b.scal, b.emb, b.stats,
                   b.sigmas, b.stage, b.ws, b.fc, b.frp, b.fdl, b.fminner, b.fdm, b.fgpre, b.fup,
                   b.fkw, b.fdup, b.fA, b.fU, b.fgin, b.fcarry, b.fpart, b.fpart_bw, b.fprm, b.src,

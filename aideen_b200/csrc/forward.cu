@@ -53,9 +53,10 @@ __global__ void attn_softmax_kernel(AttnArgs a) {
   const int s = threadIdx.x >> 5, c = threadIdx.x & 31;
   const int h = a.h, d = a.d;
   const size_t row = ((size_t)n * h + s) * kHeadDim + c;
-  Ks[s][c] = a.Kh[row] + a.W[a.off_kb + (size_t)s * d + c];
-  Vs[s][c] = a.Vh[row];
-  const float q = a.Qh[row] + a.W[a.off_qb + (size_t)s * d + c];
+  const size_t qrow = ((size_t)n * h + s) * a.qkv_ld + c;
+  Ks[s][c] = a.Kh[qrow] + a.W[a.off_kb + (size_t)s * d + c];
+  Vs[s][c] = a.Vh[qrow];
+  const float q = a.Qh[qrow] + a.W[a.off_qb + (size_t)s * d + c];
   __syncthreads();
   const float gain = 2.0f * rsqrtf((float)kHeadDim);
   float logit[16];
@@ -1025,6 +1026,23 @@ cudaError_t launch_embed(const int32_t *tok, const float *emb, float *S, int N, 
 cudaError_t launch_attn_softmax(const AttnArgs &a, int N, cudaStream_t st) {
   if (N <= 0) return cudaSuccess;
   attn_softmax_kernel<<<N, 32 * a.h, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+__global__ void pack_qkv_kernel(const float *__restrict__ W, size_t oq, size_t ok, size_t ov, int h, int d,
+                                float *__restrict__ Wcat) {
+  const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;  // over h*d*96
+  if (i >= (size_t)h * d * 96) return;
+  const int c = (int)(i % 96);
+  const size_t sj = i / 96;  // s*d + j
+  const size_t src = (c < 32 ? oq : c < 64 ? ok : ov) + (sj / d) * (size_t)d * d + (sj % d) * d + (c % 32);
+  Wcat[i] = W[src];
+}
+
+cudaError_t launch_pack_qkv(const float *W, size_t oq, size_t ok, size_t ov, int h, int d, float *Wcat,
+                            cudaStream_t st) {
+  const size_t n = (size_t)h * d * 96;
+  pack_qkv_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(W, oq, ok, ov, h, d, Wcat);
   return cudaGetLastError();
 }
 

@@ -47,7 +47,8 @@ struct AttnArgs {
   int h, d;
   const float *W;
   size_t off_qb, off_kb, off_anchor;
-  const float *Qh, *Kh, *Vh;      // [N][h][32] projections without bias
+  const float *Qh, *Kh, *Vh;      // [N][h] rows of 32 projections without bias, row stride qkv_ld
+  int qkv_ld;                     // floats between consecutive (token, slot) rows of Qh / Kh / Vh
   float *alpha, *nmix, *rmix;     // [N][h][h], [N][h][32], [N][h]
   const float *signal, *amat;     // [N][h][d]
   float *A, *scale, *rho, *Rsrc;  // [N][h][d], [N][h] x3
@@ -98,6 +99,7 @@ struct AttnBwdArgs {
   float *da, *dRc;
   const float *dn, *nmix, *rmix, *alpha, *Qh, *Kh, *Vh;
   float *dQ, *dK, *dV;
+  int qkv_ld;                     // row stride of Qh / Kh / Vh and of dQ / dK / dV
 };
 
 cudaError_t launch_embed(const int32_t *tok, const float *emb, float *S, int N, int d, int vocab,
@@ -118,8 +120,14 @@ cudaError_t launch_attn_bwd_softmax(const AttnBwdArgs &a, int N, cudaStream_t st
 cudaError_t launch_dsig_init(const AttnBwdArgs &a, float *dsig, int rows, int slot_coord,
                              cudaStream_t st);
 // out[map(c)] (+)= sum_r X[r*ld + c], c < ncols; map(c) = (c/seg)*ostride + c%seg.
+// istride (0: seg) spaces the input columns the same way: input column of c
+// is (c/seg)*istride + c%seg.
 cudaError_t launch_colsum(const float *X, int rows, int ncols, long ld, float *out, int seg,
-                          long ostride, bool accumulate, cudaStream_t st);
+                          long ostride, bool accumulate, cudaStream_t st, long istride = 0);
+// Wcat[s][j][0:32 | 32:64 | 64:96] = W_q / W_k / W_v[s][j][0:32]: the three
+// head projections as one [d][96] operand per slot.
+cudaError_t launch_pack_qkv(const float *W, size_t off_q, size_t off_k, size_t off_v, int h, int d, float *Wcat,
+                            cudaStream_t st);
 cudaError_t launch_add(float *dst, const float *a, const float *b, size_t n, cudaStream_t st);
 // Row permutation between the caller's order (row b*T + t) and the library's
 // token-major order (row t*B + b), for `blocks` consecutive sets of B*T rows of
