@@ -614,9 +614,19 @@ __global__ void colsum_kernel(const float *__restrict__ X, int rows, int ncols, 
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + tx;
   const long ic = (long)(c / seg) * istride + c % seg;
+  // eight independent partial sums per thread: the row loads of a thread are in
+  // flight together instead of one after another
   float acc = 0.f;
-  if (c < ncols)
-    for (int r = ty; r < rows; r += 32) acc += X[(size_t)r * ld + ic];
+  if (c < ncols) {
+    float p[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    int r = ty;
+    for (; r + 7 * 32 < rows; r += 8 * 32) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) p[q] += X[(size_t)(r + q * 32) * ld + ic];
+    }
+    for (; r < rows; r += 32) p[0] += X[(size_t)r * ld + ic];
+    acc = ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
+  }
   red[ty][tx] = acc;
   __syncthreads();
   if (ty == 0 && c < ncols) {

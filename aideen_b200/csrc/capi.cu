@@ -275,6 +275,11 @@ int copy_in_rows(aideen_ctx *ctx, void *dst, const void *src, int B, int T, int 
   return AIDEEN_OK;
 }
 
+bool tf32_grads_enabled() {
+  static const bool on = getenv("AIDEEN_GRAD_3XTF32") == nullptr;
+  return on;
+}
+
 GemmArgs gemm(int M, int N, int K, int batch, const float *A, long lda, long sA, bool tA,
               const float *B, long ldb, long sB, bool tB, float *C, long ldc, long sC,
               float alpha = 1.f, float beta = 0.f, const float *abias = nullptr, long sbias = 0) {
@@ -284,6 +289,14 @@ GemmArgs gemm(int M, int N, int K, int batch, const float *A, long lda, long sA,
   g.B = B; g.ldb = ldb; g.strideB = sB; g.transB = tB;
   g.C = C; g.ldc = ldc; g.strideC = sC;
   g.alpha = alpha; g.beta = beta; g.abias = abias; g.strideAbias = sbias;
+  g.tf32 = false;
+  return g;
+}
+
+// The same GEMM with single TF32 products (weight gradients, whose 1e-3
+// accuracy bar TF32 rounding meets; the forward keeps 3xTF32)
+GemmArgs tf32(GemmArgs g) {
+  g.tf32 = tf32_grads_enabled();
   return g;
 }
 
@@ -590,8 +603,8 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
     }
     // gW_o[s][c][o] = sum_n n[n][s][c] da[n][s][o]
     KL(on_side([&] {
-      return gemm_any(ctx, gemm(kHeadDim, d, N, h, b.nmix, H32, kHeadDim, true, b.da, (long)h * d, d, false,
-                                G + L.wo, d, (long)d * d));
+      return gemm_any(ctx, tf32(gemm(kHeadDim, d, N, h, b.nmix, H32, kHeadDim, true, b.da, (long)h * d, d, false,
+                                     G + L.wo, d, (long)d * d)));
     }));
     // dn[n][s][c] = sum_o da[n][s][o] W_o[s][c*d + o]
     KL(gemm_any(ctx, gemm(N, kHeadDim, d, h, b.da, (long)h * d, d, false, W + L.wo, d, (long)d * d, true,
@@ -607,8 +620,8 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
     const size_t woff[3] = {L.wq, L.wk, L.wv};
     for (int i = 0; i < 3; ++i)
       KL(on_side([&] {
-        return gemm_any(ctx, gemm(d, kHeadDim, N, h, b.src, (long)h * d, d, true, dqkv[i], H96, 96,
-                                  false, G + woff[i], d, (long)d * d));
+        return gemm_any(ctx, tf32(gemm(d, kHeadDim, N, h, b.src, (long)h * d, d, true, dqkv[i], H96, 96,
+                                       false, G + woff[i], d, (long)d * d)));
       }));
     KL(launch_colsum(b.dQ, N, H32, H96, G + L.q_bias, kHeadDim, d, false, sst, 96));
     KL(launch_colsum(b.dK, N, H32, H96, G + L.k_bias, kHeadDim, d, false, sst, 96));
@@ -625,8 +638,8 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   }
   if (!ctx->signal_zero) {
     // gW_in[s][j][o] = sigma * sum_n S_in[n][j] dsig[n][s][o]
-    KL(gemm_any(ctx, gemm(d, d, N, h, b.S_in, d, 0, true, b.dsig, (long)h * d, d, false, G + L.win, d,
-                     (long)d * d, ctx->signal_scale)));
+    KL(gemm_any(ctx, tf32(gemm(d, d, N, h, b.S_in, d, 0, true, b.dsig, (long)h * d, d, false, G + L.win, d,
+                               (long)d * d, ctx->signal_scale))));
     tl_mark(ctx, "wg_in", st);
     if (want_ds) {
       for (int s = 0; s < h; ++s)
@@ -730,17 +743,17 @@ int run_fpm_backward(aideen_ctx *ctx, bool prepare_only) {
   KL(launch_fpm_finalize(a, G, st));
   tl_mark(ctx, "f_fin", st);
   // W_retain_down[s][r][k] = sum_n up[n][s][r] g_pre[n][s][k]
-  KL(gemm_any(ctx, gemm(R, d, N, h, b.fup, HR, R, true, b.fgpre, hd, d, false, G + L.w_retain_down, d,
-                   (long)R * d)));
+  KL(gemm_any(ctx, tf32(gemm(R, d, N, h, b.fup, HR, R, true, b.fgpre, hd, d, false, G + L.w_retain_down, d,
+                             (long)R * d))));
   // dup[n][s][r] = sum_k g_pre[n][s][k] W_retain_down[s][r][k]
   KL(gemm_any(ctx, gemm(N, R, d, h, b.fgpre, hd, d, false, W + L.w_retain_down, d, (long)R * d, true,
                    b.fdup, HR, R)));
   tl_mark(ctx, "f_dup", st);
   // W_retain_up[s][j][r] = sum_n c[n][s][j] dup[n][s][r]
-  KL(gemm_any(ctx, gemm(d, R, N, h, b.fc, hd, d, true, b.fdup, HR, R, false, G + L.w_retain_up, R,
-                   (long)d * R)));
+  KL(gemm_any(ctx, tf32(gemm(d, R, N, h, b.fc, hd, d, true, b.fdup, HR, R, false, G + L.w_retain_up, R,
+                             (long)d * R))));
   // W_out[r][c] = sum_{n,s} dm[n][s][r] m_inner[n][s][c]
-  KL(gemm_any(ctx, gemm(d, d, N * h, 1, b.fdm, d, 0, true, b.fminner, d, 0, false, G + L.wout, d, 0)));
+  KL(gemm_any(ctx, tf32(gemm(d, d, N * h, 1, b.fdm, d, 0, true, b.fminner, d, 0, false, G + L.wout, d, 0))));
   return AIDEEN_OK;
 }
 
@@ -1144,7 +1157,7 @@ int lm_sampled_rows(aideen_ctx *ctx, long r0, int R, bool first) {
   KL(launch_softmax_sampled(lg, ld, b.lmp + ctx->lm_b, b.lS, b.ints, b.targets + r0, V, b.scal,
                             b.loss_rows + r0, R, st));
   // dW_S[k][j] += sum_n coef[n][k] y[n][j]; db_S[k] += sum_n coef[n][k]
-  KL(gemm_any(ctx, gemm(cap, d, R, 1, lg, ld, 0, true, y, d, 0, false, b.Glm, d, 0, 1.f, first ? 0.f : 1.f)));
+  KL(gemm_any(ctx, tf32(gemm(cap, d, R, 1, lg, ld, 0, true, y, d, 0, false, b.Glm, d, 0, 1.f, first ? 0.f : 1.f))));
   KL(launch_colsum(lg, R, cap, ld, b.Glm + ctx->lm_b, cap, 0, !first, st));
   return AIDEEN_OK;
 }

@@ -19,6 +19,9 @@ struct GemmArgs {
   float *C; long ldc, strideC;
   float alpha, beta;
   const float *abias; long strideAbias;
+  // tensor-core kernel only: one TF32 product per term (operands rounded to
+  // tf32, fp32 accumulation) instead of the fp32-accurate 3xTF32 split
+  bool tf32;
 };
 cudaError_t gemm_f32(const GemmArgs &g, cudaStream_t s);
 // Same contract on tcgen05 tensor cores (3xTF32, fp32-accurate); no abias.

@@ -35,6 +35,20 @@ constexpr int BM = 128, BK = 32, STAGES = 3, TC_THREADS = 192;
 
 __device__ unsigned int g_tc_error;  // first error code seen by any tcgemm CTA
 
+// x -> tf32 in place, rounded to nearest (ties to even) instead of the
+// truncation the tensor core applies to fp32 bit patterns.
+__device__ __forceinline__ uint32_t tf32_rn(uint32_t u) {
+  return (u + 0x0FFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
+}
+__device__ __forceinline__ void round1(float4 *raw) {
+  float4 v = *raw;
+  v.x = __uint_as_float(tf32_rn(__float_as_uint(v.x)));
+  v.y = __uint_as_float(tf32_rn(__float_as_uint(v.y)));
+  v.z = __uint_as_float(tf32_rn(__float_as_uint(v.z)));
+  v.w = __uint_as_float(tf32_rn(__float_as_uint(v.w)));
+  *raw = v;
+}
+
 // x -> (x_hi, x_lo) in place / alongside: x_hi keeps the 10 tf32 mantissa bits.
 __device__ __forceinline__ void split1(float4 *raw, float4 *lo) {
   const float4 v = *raw;
@@ -57,6 +71,7 @@ struct TcParams {
   int ksplit, kchunk;        // split-K: blockIdx.z = split index, kchunk K-blocks each
   int tma_epi;               // 1: epilogue through 32x32 shared-memory boxes + bulk tensor
                              //    store (beta 0) or reduce-add (beta 1) on mapC
+  int single;                // 1: one TF32 product per term (operands rounded to tf32)
 };
 
 // Warp roles (192 threads): warp 0 lane 0 = TMA producer, warp 1 = TMEM
@@ -176,8 +191,10 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
           const uint64_t bhi = sdesc(stage_ptr(s, 2) + koffB, lboB, sboB, layB);
           const uint64_t blo = sdesc(stage_ptr(s, 3) + koffB, lboB, sboB, layB);
           umma_tf32(tmem, ahi, bhi, idesc, (kb > 0 || k8 > 0) ? 1u : 0u);
-          umma_tf32(tmem, ahi, blo, idesc, 1u);
-          umma_tf32(tmem, alo, bhi, idesc, 1u);
+          if (!p.single) {
+            umma_tf32(tmem, ahi, blo, idesc, 1u);
+            umma_tf32(tmem, alo, bhi, idesc, 1u);
+          }
         }
         umma_commit(&empty[s]);
       }
@@ -194,10 +211,17 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
       float4 *la = reinterpret_cast<float4 *>(stage_ptr(s, 1));
       float4 *rb = reinterpret_cast<float4 *>(stage_ptr(s, 2));
       float4 *lb = reinterpret_cast<float4 *>(stage_ptr(s, 3));
+      if (p.single) {
 #pragma unroll 4
-      for (int i = ct; i < A_BYTES / 16; i += 128) split1(ra + i, la + i);
+        for (int i = ct; i < A_BYTES / 16; i += 128) round1(ra + i);
 #pragma unroll 4
-      for (int i = ct; i < B_BYTES / 16; i += 128) split1(rb + i, lb + i);
+        for (int i = ct; i < B_BYTES / 16; i += 128) round1(rb + i);
+      } else {
+#pragma unroll 4
+        for (int i = ct; i < A_BYTES / 16; i += 128) split1(ra + i, la + i);
+#pragma unroll 4
+        for (int i = ct; i < B_BYTES / 16; i += 128) split1(rb + i, lb + i);
+      }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&conv[s]);
@@ -362,7 +386,7 @@ cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st, float *ws, size_t ws_flo
     ok = make_map(&mb, g.B, g.N, g.K, b_batched ? g.batch : 1, g.ldb, g.strideB, 32, BK, false);
   if (!ok) return cudaErrorInvalidValue;
   TcParams p{g.M, g.N, g.K, a_k, b_k, g.C, g.ldc, g.strideC, g.alpha, g.beta, a_batched ? 1 : 0,
-             b_batched ? 1 : 0, 1, 0, 0};
+             b_batched ? 1 : 0, 1, 0, 0, g.tf32 ? 1 : 0};
   const int tiles_n = (g.N + BN - 1) / BN, tiles_m = (g.M + BM - 1) / BM;
   const int tiles = tiles_n * tiles_m * g.batch;
   const int kblocks = (g.K + BK - 1) / BK;

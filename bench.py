@@ -249,6 +249,49 @@ def configs1_step(device, steps=20, warmup=3):
             "ms_per_step": dt * 1e3, "timing": "host wall clock around synchronous C-ABI steps (loss read back)"}
 
 
+def configs4_step(device, steps=2, warmup=1):
+    """BASELINE configs[4]'s per-GPU shard: d_r 1024, 16 slots, 4 sequences x
+    2048 tokens (32 sequences over 8 GPUs), vocab 50257, Zipf ids, FPM scan over
+    2048 steps, Anderson forward (max 30) and adjoint (max 30), sampled LM head,
+    embedding update.  Train tokens/s of the whole step, device-timed."""
+    import torch
+    from aideen_b200.backend import GpuDeqBackend, RunConfig, DEVICE
+    from aideen_b200.weights import init_all_weights, init_embedding, init_lm_head, zipf_tokens
+    d, h, B, Tl = 1024, 16, 4, 2048
+    be = GpuDeqBackend(d, h, max_batch=B, max_seq_len=Tl, vocab=VOCAB, device=device)
+    be.upload_weights(init_all_weights(d, h, seed=0))
+    be.upload_lm_head(*init_lm_head(d, VOCAB))
+    be.upload_embedding(init_embedding(d, VOCAB))
+    ids = zipf_tokens(B * (Tl + 1), VOCAB, seed=7).reshape(B, Tl + 1)
+    tok = torch.from_numpy(np.ascontiguousarray(ids[:, :-1])).cuda()
+    tg = torch.from_numpy(np.ascontiguousarray(ids[:, 1:])).cuda()
+    rc = RunConfig(max_iters=30, fpm=True, anderson_m=3)
+    stream = torch.cuda.Stream()
+    be.set_stream(stream.cuda_stream)
+
+    def one(k):
+        be.train_step(tok.data_ptr(), tg.data_ptr(), B, Tl, rc, adj_iters=30, anderson_m=4, step=k + 1,
+                      where=DEVICE, want_loss=False, raw_ptr=True, lm_samples=LM_SAMPLES, emb_update=1)
+
+    for k in range(warmup):
+        one(k)
+    be.sync()
+    with torch.cuda.stream(stream):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+    for k in range(steps):
+        one(warmup + k)
+    be.join()
+    with torch.cuda.stream(stream):
+        e.record(stream)
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    st = be.solve_stats() if hasattr(be, "solve_stats") else None
+    be.close()
+    return {"workload": "configs[4] per-GPU shard: d 1024, h 16, 4 x 2048 tokens, Anderson fwd/adj max 30",
+            "tokens_per_s": B * Tl / (ms / 1e3), "ms_per_step": ms, "steps": steps}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -277,6 +320,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-micro", action="store_true", help="skip the configs[1] / configs[3] extras")
+    ap.add_argument("--no-dense", action="store_true", help="skip the dense-CE comparison run")
+    ap.add_argument("--micro-only", action="store_true",
+                    help="only the configs[3] adjoint and weight-gradient microbenchmarks (for profiling)")
     ap.add_argument("--dense-lm", action="store_true",
                     help="time the dense full-vocabulary CE head instead of the reference's sampled softmax")
     args = ap.parse_args()
@@ -294,6 +340,11 @@ def main():
     from aideen_b200.weights import init_all_weights, init_embedding, init_lm_head
 
     torch.cuda.set_device(local)
+    if args.micro_only:
+        hbm, src = peaks()
+        print(json.dumps({"roofline_adjoint_c4": adjoint_micro(torch, hbm, src, local),
+                          "weight_grads_c4": weight_grad_micro(torch, local)}), flush=True)
+        return
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     be = GpuDeqBackend(D, H, max_batch=B_PER_GPU, max_seq_len=T, vocab=VOCAB, device=local)
@@ -375,7 +426,7 @@ def main():
     e2e = tokens / (ms_e2e / 1e3)
     # the dense full-vocabulary head (the previous default), for comparison
     dense = None
-    if not args.dense_lm:
+    if not args.dense_lm and not args.no_dense:
         nd = max(10, args.steps // 10)
         for _ in range(3):
             step(DEVICE, 0)
@@ -450,6 +501,7 @@ def main():
     c4 = adjoint_micro(torch, hbm, src, local) if world == 1 and not args.no_micro else None
     c4g = weight_grad_micro(torch, local) if world == 1 and not args.no_micro else None
     c1 = configs1_step(local) if world == 1 and not args.no_micro else None
+    c5 = configs4_step(local) if world == 1 and not args.no_micro else None
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -476,6 +528,7 @@ def main():
                 "roofline_adjoint_c4": c4,
                 "weight_grads_c4": c4g,
                 "configs1": c1,
+                "configs4": c5,
                 "weights_agree": agree,
                 "clocks": clk.summary()}
         if not args.no_cpu_baseline and world == 1:

@@ -183,7 +183,6 @@ def test_full_step_gradients_and_update(c):
     be.apply_update(rule=RULE_ADAM, lr=1e-3, step=1, lm_head=True)
     e = step_errors(be, r, W, lm, B, T)
     assert e["adam_kernel"] < 1e-4 and e["lm_adam_kernel"] < 1e-4, e
-    assert e["update"] < 5e-3, e
     be.close()
 
 
