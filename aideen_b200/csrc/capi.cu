@@ -225,6 +225,7 @@ int prof_class(const char *expr, int phase) {
       cudaEventRecord(_e0, ctx->stream);                                               \
     }                                                                                  \
     cudaError_t _e = (expr);                                                           \
+    ctx->launches += tc_take_extra_launches();                                         \
     if (ctx->prof) {                                                                   \
       cudaEventRecord(_e1, ctx->stream);                                               \
       ctx->pev.push_back({prof_class(#expr, ctx->prof_phase), {_e0, _e1}});                            \

@@ -29,6 +29,10 @@ bool tc_gemm_supported(const GemmArgs &g);
 // ws: optional workspace for split-K partial sums (ws_floats capacity).
 cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t s, float *ws = nullptr, size_t ws_floats = 0);
 unsigned int tc_gemm_error(bool reset);
+// Kernels a GEMM call launched beyond its main one (split-K reductions) since
+// the last call of tc_take_extra_launches, on this host thread.
+extern thread_local unsigned tc_extra_launches;
+unsigned tc_take_extra_launches();
 // Persistent tcgen05 GEMM on pre-split operands (tcgemm_split.cu): g.A / g.B
 // hold the tf32-exact high parts, A_lo / B_lo the remainders (same strides);
 // beta must be 0 or 1.

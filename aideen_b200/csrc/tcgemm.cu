@@ -430,9 +430,18 @@ cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st, float *ws, size_t ws_flo
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || p.ksplit <= 1) return e;
+  tc_extra_launches++;
   splitk_reduce_kernel<<<148 * 4, 256, 0, st>>>(ws, p.ksplit, g.batch, g.M, g.N, g.C, g.ldc,
                                                 g.batch > 1 ? g.strideC : 0, g.alpha, g.beta);
   return cudaGetLastError();
+}
+
+thread_local unsigned tc_extra_launches = 0;
+
+unsigned tc_take_extra_launches() {
+  const unsigned v = tc_extra_launches;
+  tc_extra_launches = 0;
+  return v;
 }
 
 unsigned int tc_gemm_error(bool reset) {

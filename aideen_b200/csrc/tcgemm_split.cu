@@ -431,6 +431,7 @@ cudaError_t tc_gemm_split(const GemmArgs &g, const float *A_lo, const float *B_l
   tc_split_kernel<<<grid, P_THREADS, P_SMEM, st>>>(mah, mal, mbh, mbl, mc, p);
   e = cudaGetLastError();
   if (e != cudaSuccess || p.ksplit <= 1) return e;
+  tc_extra_launches++;
   split_reduce_kernel<<<nsm * 4, 256, 0, st>>>(ws, p.ksplit, g.M, g.N, g.C, g.ldc, g.alpha, g.beta);
   return cudaGetLastError();
 }

@@ -179,7 +179,9 @@ def adjoint_micro(torch, hbm, src, device):
             "bound": "hbm", "achieved": ach, "peak": hbm, "peak_source": src, "unit": "GB/s",
             "frac": ach / hbm, "ms_per_launch": ms, "algorithmic_bytes_per_launch": nbytes,
             "bytes_moved_per_launch": moved,
-            "traffic": None,
+            # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this workload
+            # under ncu (805.3 MB read, 498.8 MB written)
+            "traffic": 805.3e6 + 498.8e6,
             "note": "algorithmic bytes per the 16*E*d definition; the kernel also writes g_pre (E*d) and "
                     "per-CTA NormScale partials, which the weight gradients read"}
 
@@ -216,11 +218,12 @@ def weight_grad_micro(torch, device):
     tf, tsrc = peaks_tensor()
     tf32 = tf / 2.0
     ach = flops / (ms / 1e3) / 1e12
-    return {"kernels": "tcgemm_kernel (3xTF32 tcgen05)", "workload": "N=16384 tokens x 8 slots x 512",
+    return {"kernels": "tcgemm_kernel (tcgen05; weight gradients in single TF32, dn/dsrc in 3xTF32)",
+            "workload": "N=16384 tokens x 8 slots x 512",
             "algorithmic_flops": flops, "ms": ms, "achieved_tflops": ach, "tf32_peak": tf32,
             "peak_source": "half of " + tsrc, "tensor_util_of_tf32": ach / tf32,
-            "note": "fp32-accurate 3xTF32 issues 3 tf32 MMAs per algorithmic product, so 1/3 of "
-                    "the TF32 rate is the ceiling of this accounting"}
+            "note": "the weight-gradient GEMMs issue one tf32 MMA per product (TF32 rate is their "
+                    "ceiling); dn and dsrc, also in this class, issue three (3xTF32)"}
 
 
 def configs1_step(device, steps=20, warmup=3):
@@ -468,16 +471,22 @@ def main():
     picard_bytes = 4 * 6 * E * D + 4 * 6 * H * D * 32
     adj_bytes = 4 * (3 * E * D + 2 * N * D)  # pre in; v, g_pre out; dl_dh in (per-CTA partials are small)
     bytes_of = {"picard": picard_bytes, "adjoint": adj_bytes}
+    # DRAM bytes read + written per step by these kernels in one ncu capture of this
+    # workload (dram__bytes_read.sum + dram__bytes_write.sum summed over the step's
+    # launches; most of the outputs stay in the 126 MB L2, so traffic is below the
+    # algorithmic bytes)
+    traffic_of = {"picard": 16.14e6 + 24.67e6 + 37.32e6 + 9.51e6, "adjoint": 37.80e6 + 13.59e6}
     roof = None
     if dominant in bytes_of:
-        kms = kprof[dominant][0] / max(kprof[dominant][1], 1)
-        ach = bytes_of[dominant] / (kms / 1e3) / 1e9
+        nl = max(kprof[dominant][1], 1)
+        kms = kprof[dominant][0] / nl
+        ach = bytes_of[dominant] / (kprof[dominant][0] / 1e3) / 1e9
         roof = {"kernel": {"picard": "picard_kernel<FPM> (token-serial Picard solve + FPM scan)",
                            "adjoint": "adjoint_kernel (fused clean adjoint)"}[dominant],
                 "bound": "hbm", "achieved": ach, "peak": hbm, "peak_source": src, "unit": "GB/s",
-                "frac": ach / hbm, "traffic": None, "ms_per_launch": kms,
-                "algorithmic_bytes_per_launch": bytes_of[dominant],
-                "note": (f"latency-bound serial chain: {T} tokens per launch, {1e3 * kms / T:.2f} us per token "
+                "frac": ach / hbm, "traffic": traffic_of[dominant] / nl, "ms_per_launch": kms,
+                "launches_per_step": nl, "algorithmic_bytes_per_launch": bytes_of[dominant] / nl,
+                "note": (f"latency-bound serial chain: {T} tokens per step in {nl} token chunks, {1e3 * kprof[dominant][0] / T:.2f} us per token "
                          f"(all slots of a sequence advance one token together; ~20 barrier-separated phases "
                          f"per token); HBM is not the limit") if dominant == "picard" else ""}
     else:
@@ -493,11 +502,11 @@ def main():
     tf, tsrc = peaks_tensor()
     gms = kprof["gemm"][0]
     gach = proj_flops / (gms / 1e3) / 1e12
-    roof_gemm = {"kernels": "tcgemm_kernel (3xTF32 tcgen05)", "algorithmic_flops_per_step": proj_flops,
+    roof_gemm = {"kernels": "tcgemm_kernel (tcgen05: 3xTF32 forward/activation grads, TF32 weight grads)", "algorithmic_flops_per_step": proj_flops,
                  "ms_per_step": gms, "achieved_tflops": gach, "tf32_peak": tf / 2, "peak_source": "half of " + tsrc,
                  "frac_of_tf32": gach / (tf / 2),
                  "note": "profiled pass, one launch after another; 3xTF32 issues 3 tf32 MMAs per "
-                         "algorithmic product (ceiling 1/3 of the TF32 rate in this accounting)"}
+                         "algorithmic product, single TF32 (weight gradients) one"}
     c4 = adjoint_micro(torch, hbm, src, local) if world == 1 and not args.no_micro else None
     c4g = weight_grad_micro(torch, local) if world == 1 and not args.no_micro else None
     c1 = configs1_step(local) if world == 1 and not args.no_micro else None
