@@ -414,12 +414,14 @@ class GpuDeqBackend:
     def read_adj_v_out(self):
         return self.read("adj_v", (self.h, self.batch * self.seq_len, self.d))
 
-    def gemm_selftest(self, M, N, K, batch=1, trans_a=False, trans_b=False, presplit=False):
+    def gemm_selftest(self, M, N, K, batch=1, trans_a=False, trans_b=False, presplit=False, tf32=False):
         """(relative L2 difference, ms tensor-core, ms CUDA-core) on seeded operands.
-        presplit=True runs the persistent kernel on pre-split hi/lo operands."""
+        presplit=True runs the persistent kernel on pre-split hi/lo operands;
+        tf32=True single TF32 products instead of 3xTF32."""
         e, t1, t2 = C.c_float(), C.c_float(), C.c_float()
+        flags = (1 if presplit else 0) | (2 if tf32 else 0)
         self._check(self.lib.aideen_gemm_selftest(self.ctx, M, N, K, batch, int(trans_a), int(trans_b),
-                                                  int(presplit), C.byref(e), C.byref(t1), C.byref(t2)),
+                                                  flags, C.byref(e), C.byref(t1), C.byref(t2)),
                     "gemm_selftest")
         return e.value, t1.value, t2.value
 

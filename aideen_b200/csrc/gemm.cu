@@ -72,7 +72,8 @@ __global__ void __launch_bounds__(256) gemm_kernel(GemmArgs g) {
     for (int j = 0; j < TN; ++j) {
       const int n = n0 + tx + 16 * j;
       if (n >= g.N) continue;
-      float *c = C + (long)m * g.ldc + n;
+      float *c = C + (long)m * g.ldc +
+                 (g.col_group > 0 ? (long)(n / g.col_group) * g.group_stride + n % g.col_group : n);
       float r = g.alpha * acc[i][j];
       if (g.beta != 0.f) r += g.beta * *c;
       *c = r;

@@ -22,6 +22,11 @@ struct GemmArgs {
   // tensor-core kernel only: one TF32 product per term (operands rounded to
   // tf32, fp32 accumulation) instead of the fp32-accurate 3xTF32 split
   bool tf32;
+  // col_group > 0: C's columns come in groups of col_group that live
+  // group_stride floats apart (column n is stored at
+  // (n / col_group) * group_stride + n % col_group of the row), e.g. the
+  // Q, K and V blocks of one 96-column product
+  int col_group; long group_stride;
 };
 cudaError_t gemm_f32(const GemmArgs &g, cudaStream_t s);
 // Same contract on tcgen05 tensor cores (3xTF32, fp32-accurate); no abias.

@@ -1,18 +1,25 @@
 // fp32-accurate GEMM on the 5th-generation tensor cores (tcgen05, sm_100a).
 //
 // C[b] = alpha * opA(A[b]) * opB(B[b]) + beta * C[b], row-major, the same
-// contract as gemm_f32 (kernels.cuh).  One CTA computes a 128 x BN tile:
+// contract as gemm_f32 (kernels.cuh).  One CTA computes a 128 x BN tile
+// (BN = 32, 64, 128 or 256):
 //
 //   * TMA (cp.async.bulk.tensor, no multicast) brings fp32 tiles of A and B
-//     into 128-byte-swizzled shared memory, BK = 32 along K per stage;
-//   * all threads split each staged value x into x_hi = x with the low 13
-//     mantissa bits cleared (exactly representable in tf32) and
-//     x_lo = x - x_hi, in the same swizzled layout;
+//     into 128-byte-swizzled shared memory, BK = 32 along K per stage, in a
+//     ring of as many stages as fit (the stage size depends on the mode);
+//   * eight warps convert each staged value x in place: 3xTF32 splits it into
+//     x_hi = x with the low 13 mantissa bits cleared (exact in tf32) and
+//     x_lo = x - x_hi; single TF32 rounds it to the nearest tf32 value;
 //   * one thread issues, per K=8 step, three tcgen05.mma kind::tf32
-//     (hi*hi + hi*lo + lo*hi) accumulating in TMEM (fp32), then
-//     tcgen05.commit releases the stage to the TMA producer;
+//     (hi*hi + hi*lo + lo*hi; one in single mode) accumulating in TMEM
+//     (fp32), then tcgen05.commit releases the stage to the TMA producer;
 //   * the epilogue reads the accumulator with tcgen05.ld (warp w owns TMEM
-//     lanes 32w..32w+31 = tile rows) and applies alpha/beta.
+//     lanes 32w..32w+31 = tile rows), stages 32x32 boxes in the (now idle)
+//     stage ring and writes them with bulk tensor stores / reduce-adds.
+//
+// The shared-memory traffic per K block (TMA writes, the conversion pass,
+// the MMA operand reads) bounds this kernel before the tensor pipe does, so
+// wide tiles (fewer A re-reads per product) and deep rings pay.
 //
 // The 3-term split keeps the product error at ~2^-21 relative, i.e. fp32
 // level, which the DEQ forward needs (its stop rule compares residuals near
@@ -31,21 +38,37 @@
 namespace aideen {
 namespace {
 
-constexpr int BM = 128, BK = 32, STAGES = 3, TC_THREADS = 192;
+// 2 role warps + NCONV converter / epilogue warps
+constexpr int BM = 128, BK = 32, MAX_STAGES = 8, NCONV = 8, TC_THREADS = 64 + 32 * NCONV;
+constexpr int SMEM_LIMIT = 232448;  // opt-in dynamic shared memory per block on sm_100
 
 __device__ unsigned int g_tc_error;  // first error code seen by any tcgemm CTA
 
-// x -> tf32 in place, rounded to nearest (ties to even) instead of the
-// truncation the tensor core applies to fp32 bit patterns.
-__device__ __forceinline__ uint32_t tf32_rn(uint32_t u) {
-  return (u + 0x0FFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
+#ifdef AIDEEN_TC_PROF
+// Per-CTA timeline of the launches since the last reset (profiling builds
+// only), clock64 cycles after the CTA's start: [0] setup done, [1] first stage
+// converted, [2] last stage converted, [3] accumulator complete, [4] end,
+// [5] converter wait on full (warp 2), [6] MMA wait on conv, [7] producer
+// wait on empty.
+__device__ unsigned long long g_tc_prof[4096 * 8];
+#define TCP(i, v) if (prof_row) prof_row[i] = (v)
+#else
+#define TCP(i, v)
+#endif
+
+// x -> tf32 in place, rounded to nearest (cvt.rna: ties away from zero)
+// instead of the truncation the tensor core applies to fp32 bit patterns.
+__device__ __forceinline__ float tf32_rn(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
 }
 __device__ __forceinline__ void round1(float4 *raw) {
   float4 v = *raw;
-  v.x = __uint_as_float(tf32_rn(__float_as_uint(v.x)));
-  v.y = __uint_as_float(tf32_rn(__float_as_uint(v.y)));
-  v.z = __uint_as_float(tf32_rn(__float_as_uint(v.z)));
-  v.w = __uint_as_float(tf32_rn(__float_as_uint(v.w)));
+  v.x = tf32_rn(v.x);
+  v.y = tf32_rn(v.y);
+  v.z = tf32_rn(v.z);
+  v.w = tf32_rn(v.w);
   *raw = v;
 }
 
@@ -71,17 +94,25 @@ struct TcParams {
   int ksplit, kchunk;        // split-K: blockIdx.z = split index, kchunk K-blocks each
   int tma_epi;               // 1: epilogue through 32x32 shared-memory boxes + bulk tensor
                              //    store (beta 0) or reduce-add (beta 1) on mapC
-  int single;                // 1: one TF32 product per term (operands rounded to tf32)
+  int stages;                // depth of the TMA ring (2..MAX_STAGES)
 };
 
-// Warp roles (192 threads): warp 0 lane 0 = TMA producer, warp 1 = TMEM
-// owner + MMA issuer (lane 0), warps 2..5 = hi/lo splitters and epilogue
-// (warp w reads TMEM lanes 32*(w%4)..+31, so the four cover all 128 rows).
-// Per stage s: full[s] (TMA landed) -> conv[s] (split done, 4 warp arrivals)
-// -> empty[s] (MMAs done, tcgen05.commit) -> producer refills.
 constexpr int BOX_BYTES = 32 * 32 * 4;  // one 32x32 fp32 epilogue box
 
-template <int BN>
+template <int BN, bool SPLIT3>
+__host__ __device__ constexpr int stage_bytes() {
+  return (SPLIT3 ? 2 : 1) * (BM * BK * 4 + BN * BK * 4);
+}
+constexpr size_t ring_offset_bytes = 1024;                      // alignment slack
+constexpr size_t bar_bytes = 8 * (3 * MAX_STAGES + 1) + 16;  // mbarriers, TMEM slot, error word
+size_t tc_smem(int stage_b, int stages) { return ring_offset_bytes + (size_t)stages * stage_b + bar_bytes; }
+
+// Warp roles: warp 0 lane 0 = TMA producer, warp 1 = TMEM owner + MMA
+// issuer (lane 0), warps 2..2+NCONV-1 = converters and epilogue (warp w reads
+// TMEM lanes 32*(w%4)..+31; warps w and w+4 take alternate 32-column chunks).
+// Per stage s: full[s] (TMA landed) -> conv[s] (converted, NCONV warp
+// arrivals) -> empty[s] (MMAs done, tcgen05.commit) -> producer refills.
+template <int BN, bool SPLIT3>
 __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constant__ CUtensorMap mapA,
                                                             const __grid_constant__ CUtensorMap mapB,
                                                             const __grid_constant__ CUtensorMap mapC,
@@ -90,12 +121,16 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
   unsigned char *sm = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4;
-  constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-  unsigned char *boxes = sm + STAGES * STAGE_BYTES;  // 4 epilogue warps x 2 boxes
-  uint64_t *full = reinterpret_cast<uint64_t *>(boxes + 8 * BOX_BYTES);
-  uint64_t *conv = full + STAGES;
-  uint64_t *empty = conv + STAGES;
-  uint64_t *done = empty + STAGES;
+  constexpr int STAGE_BYTES = stage_bytes<BN, SPLIT3>();
+  constexpr uint32_t TMEM_COLS = BN;  // a power of two >= 32
+  const int S = p.stages;
+  // the epilogue boxes (NCONV warps x 2) reuse the ring: every MMA has completed
+  // (and so every copy has landed) before the first box is written
+  unsigned char *boxes = sm;
+  uint64_t *full = reinterpret_cast<uint64_t *>(sm + (size_t)S * STAGE_BYTES);
+  uint64_t *conv = full + MAX_STAGES;
+  uint64_t *empty = conv + MAX_STAGES;
+  uint64_t *done = empty + MAX_STAGES;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
   uint32_t *err = tmem_slot + 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -106,30 +141,45 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
   const int kb0 = p.ksplit > 1 ? (bz % p.ksplit) * p.kchunk : 0;
   const int ktot = (p.K + BK - 1) / BK;
   const int kblocks = p.ksplit > 1 ? min(p.kchunk, ktot - kb0) : ktot;
+#ifdef AIDEEN_TC_PROF
+  const long long t_start = clock64();
+  const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  unsigned long long *prof_row = cta < 4096 ? g_tc_prof + 8 * cta : nullptr;
+#endif
 
   if (tid == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&conv[s], 4);
+      mbar_init(&conv[s], NCONV);
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, 1);
     *err = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mapA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mapB)) : "memory");
+  }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"((uint32_t)BN));
+                 "r"(TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
+#ifdef AIDEEN_TC_PROF
+  if (tid == 0) TCP(0, clock64() - t_start);
+  long long w_acc = 0;
+#endif
 
+  // 0 A (hi), 1 A lo, 2 B (hi), 3 B lo; single mode holds only 0 and 2
   auto stage_ptr = [&](int s, int which) -> unsigned char * {
-    unsigned char *base = sm + s * STAGE_BYTES;  // 0 A hi, 1 A lo, 2 B hi, 3 B lo
+    unsigned char *base = sm + (size_t)s * STAGE_BYTES;
+    if (!SPLIT3) return which == 0 ? base : base + A_BYTES;
     return which == 0 ? base : which == 1 ? base + A_BYTES : which == 2 ? base + 2 * A_BYTES
                                                                         : base + 2 * A_BYTES + B_BYTES;
   };
@@ -139,8 +189,14 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
       int issued = 0;
       bool ok = true;
       for (int kb = 0; kb < kblocks && ok; ++kb) {
-        const int s = kb % STAGES;
-        if (kb >= STAGES && !mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { ok = false; break; }
+        const int s = kb % S;
+#ifdef AIDEEN_TC_PROF
+        const long long w0 = clock64();
+#endif
+        if (kb >= S && !mbar_wait(&empty[s], ((kb / S) - 1) & 1)) { ok = false; break; }
+#ifdef AIDEEN_TC_PROF
+        w_acc += clock64() - w0;
+#endif
         if (*(volatile uint32_t *)err) { ok = false; break; }
         const int k0 = (kb0 + kb) * BK;
         mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
@@ -162,9 +218,10 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
         issued = kb + 1;
       }
       if (!ok) atomicExch(err, 1u);
+      TCP(7, w_acc);
       // every issued copy must land before the CTA can exit (bounded)
-      for (int kb = issued - STAGES < 0 ? 0 : issued - STAGES; kb < issued; ++kb)
-        mbar_wait(&full[kb % STAGES], (kb / STAGES) & 1);
+      for (int kb = issued - S < 0 ? 0 : issued - S; kb < issued; ++kb)
+        mbar_wait(&full[kb % S], (kb / S) & 1);
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---------------- MMA issuer
@@ -178,8 +235,14 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
       const uint32_t layA = p.a_kmajor ? 2u : 1u, layB = p.b_kmajor ? 2u : 1u;
       bool ok = true;
       for (int kb = 0; kb < kblocks; ++kb) {
-        const int s = kb % STAGES;
-        if (!mbar_wait(&conv[s], (kb / STAGES) & 1) || *(volatile uint32_t *)err) { ok = false; break; }
+        const int s = kb % S;
+#ifdef AIDEEN_TC_PROF
+        const long long w0 = clock64();
+#endif
+        if (!mbar_wait(&conv[s], (kb / S) & 1) || *(volatile uint32_t *)err) { ok = false; break; }
+#ifdef AIDEEN_TC_PROF
+        w_acc += clock64() - w0;
+#endif
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
         for (int k8 = 0; k8 < BK / 8; ++k8) {
@@ -187,11 +250,11 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
           const uint32_t koffA = p.a_kmajor ? k8 * 32 : k8 * 1024;
           const uint32_t koffB = p.b_kmajor ? k8 * 32 : k8 * 1024;
           const uint64_t ahi = sdesc(stage_ptr(s, 0) + koffA, lboA, sboA, layA);
-          const uint64_t alo = sdesc(stage_ptr(s, 1) + koffA, lboA, sboA, layA);
           const uint64_t bhi = sdesc(stage_ptr(s, 2) + koffB, lboB, sboB, layB);
-          const uint64_t blo = sdesc(stage_ptr(s, 3) + koffB, lboB, sboB, layB);
           umma_tf32(tmem, ahi, bhi, idesc, (kb > 0 || k8 > 0) ? 1u : 0u);
-          if (!p.single) {
+          if (SPLIT3) {
+            const uint64_t alo = sdesc(stage_ptr(s, 1) + koffA, lboA, sboA, layA);
+            const uint64_t blo = sdesc(stage_ptr(s, 3) + koffB, lboB, sboB, layB);
             umma_tf32(tmem, ahi, blo, idesc, 1u);
             umma_tf32(tmem, alo, bhi, idesc, 1u);
           }
@@ -199,42 +262,58 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
         umma_commit(&empty[s]);
       }
       if (!ok) atomicExch(err, 1u);
+      TCP(6, w_acc);
       umma_commit(done);  // arrives once every MMA issued so far has completed
     }
-  } else {  // ---------------- splitters (128 threads) + epilogue
+  } else {  // ---------------- converters (32 * NCONV threads) + epilogue
+    constexpr int NCT = 32 * NCONV;
     const int ct = tid - 64;
     for (int kb = 0; kb < kblocks; ++kb) {
-      const int s = kb % STAGES;
-      if (!mbar_wait(&full[s], (kb / STAGES) & 1)) { atomicExch(err, 1u); break; }
+      const int s = kb % S;
+#ifdef AIDEEN_TC_PROF
+      const long long w0 = clock64();
+#endif
+      if (!mbar_wait(&full[s], (kb / S) & 1)) { atomicExch(err, 1u); break; }
       if (*(volatile uint32_t *)err) break;
+#ifdef AIDEEN_TC_PROF
+      w_acc += clock64() - w0;
+#endif
       float4 *ra = reinterpret_cast<float4 *>(stage_ptr(s, 0));
-      float4 *la = reinterpret_cast<float4 *>(stage_ptr(s, 1));
       float4 *rb = reinterpret_cast<float4 *>(stage_ptr(s, 2));
-      float4 *lb = reinterpret_cast<float4 *>(stage_ptr(s, 3));
-      if (p.single) {
+      if (!SPLIT3) {
 #pragma unroll 4
-        for (int i = ct; i < A_BYTES / 16; i += 128) round1(ra + i);
+        for (int i = ct; i < A_BYTES / 16; i += NCT) round1(ra + i);
 #pragma unroll 4
-        for (int i = ct; i < B_BYTES / 16; i += 128) round1(rb + i);
+        for (int i = ct; i < B_BYTES / 16; i += NCT) round1(rb + i);
       } else {
+        float4 *la = reinterpret_cast<float4 *>(stage_ptr(s, 1));
+        float4 *lb = reinterpret_cast<float4 *>(stage_ptr(s, 3));
 #pragma unroll 4
-        for (int i = ct; i < A_BYTES / 16; i += 128) split1(ra + i, la + i);
+        for (int i = ct; i < A_BYTES / 16; i += NCT) split1(ra + i, la + i);
 #pragma unroll 4
-        for (int i = ct; i < B_BYTES / 16; i += 128) split1(rb + i, lb + i);
+        for (int i = ct; i < B_BYTES / 16; i += NCT) split1(rb + i, lb + i);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&conv[s]);
+#ifdef AIDEEN_TC_PROF
+      if (tid == 64 && kb == 0) TCP(1, clock64() - t_start);
+      if (tid == 64 && kb == kblocks - 1) TCP(2, clock64() - t_start);
+#endif
     }
     const bool ok = mbar_wait(done, 0) && !*(volatile uint32_t *)err;
+#ifdef AIDEEN_TC_PROF
+    if (tid == 64) { TCP(3, clock64() - t_start); TCP(5, w_acc); }
+#endif
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (ok && p.tma_epi) {
       const int q = warp & 3;  // TMEM lane quadrant this warp may access
+      const int half = (warp - 2) >> 2;  // which alternate 32-column chunks
       const int rowbase = m0 + q * 32;
       unsigned char *mybox = boxes + (warp - 2) * 2 * BOX_BYTES;
       int nst = 0;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = 32 * half; c0 < BN; c0 += 32 * (NCONV / 4)) {
         uint32_t r[32];
         const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
         asm volatile(
@@ -271,10 +350,11 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
       if (lane == 0) bulk_wait<0>();  // stores complete before the CTA's shared memory goes away
     } else if (ok) {
       const int q = warp & 3;  // TMEM lane quadrant this warp may access
+      const int half = (warp - 2) >> 2;
       const int row = m0 + q * 32 + lane;
       float *crow = p.C + (long)bz * p.strideC + (long)row * p.ldc;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = 32 * half; c0 < BN; c0 += 32 * (NCONV / 4)) {
         uint32_t r[32];
         const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
         asm volatile(
@@ -315,7 +395,10 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
   __syncthreads();
   if (tid == 0 && *(volatile uint32_t *)err) atomicCAS(&g_tc_error, 0u, 1u);
   if (warp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+#ifdef AIDEEN_TC_PROF
+  if (tid == 0) TCP(4, clock64() - t_start);
+#endif
 }
 
 // ---------------------------------------------------------------- host side
@@ -334,10 +417,106 @@ bool make_map(CUtensorMap *m, const float *base, uint64_t e0, uint64_t e1, uint6
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN>
-size_t tc_smem() {
-  return 1024 + STAGES * (size_t)(2 * BM * BK * 4 + 2 * BN * BK * 4) + 8 * BOX_BYTES + 8 * (3 * STAGES + 1) +
-         16;
+// Tuning knobs read once from the environment (0 = the built-in choice):
+// AIDEEN_TC_BN (32, 64, 128, 256), AIDEEN_TC_STAGES (2..8), AIDEEN_TC_CPS
+// (CTAs per SM the ring is sized for, 1 or 2).
+int env_int(const char *name) {
+  const char *v = getenv(name);
+  return v ? atoi(v) : 0;
+}
+struct TcTuning {
+  int bn = env_int("AIDEEN_TC_BN"), stages = env_int("AIDEEN_TC_STAGES"), cps = env_int("AIDEEN_TC_CPS");
+};
+const TcTuning &tuning() {
+  static TcTuning t;
+  return t;
+}
+
+// Ring depth: as many stages as fit the shared memory of `cps` CTAs per SM,
+// no more than the K blocks one CTA walks (a short-K GEMM then holds a small
+// ring and more CTAs share an SM), and at least the bytes of the epilogue
+// boxes that reuse it (2 per epilogue warp: 4 warps when BN = 32, else 8).
+int ring_stages(int stage_b, int cps, int kblocks = MAX_STAGES, int bn = 128) {
+  const TcTuning &t = tuning();
+  const long budget = SMEM_LIMIT / cps - 1024 * (cps - 1) - (long)ring_offset_bytes - (long)bar_bytes;
+  int st = (int)(budget / stage_b);
+  if (st > MAX_STAGES) st = MAX_STAGES;
+  if (t.stages >= 2 && t.stages < st) st = t.stages;
+  if (kblocks < st) st = kblocks;
+  const int box_bytes = 2 * (bn == 32 ? 4 : NCONV) * BOX_BYTES;
+  if (st < 1) st = 1;
+  while (st * stage_b < box_bytes) ++st;
+  return st;
+}
+
+template <int BN, bool SPLIT3>
+cudaError_t launch_tc(dim3 grid, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc, TcParams p,
+                      int cps, cudaStream_t st) {
+  static bool attr_set = false;
+  const int kb_cta = p.ksplit > 1 ? p.kchunk : (p.K + BK - 1) / BK;
+  p.stages = ring_stages(stage_bytes<BN, SPLIT3>(), cps, kb_cta, BN);
+  if (tc_smem(stage_bytes<BN, SPLIT3>(), p.stages) > (size_t)SMEM_LIMIT) return cudaErrorInvalidValue;
+  if (!attr_set) {
+    const cudaError_t e = cudaFuncSetAttribute(tcgemm_kernel<BN, SPLIT3>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  tcgemm_kernel<BN, SPLIT3><<<grid, TC_THREADS, tc_smem(stage_bytes<BN, SPLIT3>(), p.stages), st>>>(ma, mb, mc, p);
+  return cudaGetLastError();
+}
+
+// C = alpha * sum_s ws[b][s] + beta * C over one split-K product of R x Cc
+// outputs per batch entry, summed in split order (deterministic).  trans:
+// workspace (r, c) is C's (c, r) (the product was formed with A and B
+// swapped); col_group: C's column n sits at (n / col_group) * group_stride +
+// n % col_group of its row.  Each thread sums 4 adjacent workspace columns.
+__global__ void splitk_reduce_kernel(const float *__restrict__ ws, int splits, int batch, int R, int Cc,
+                                     float *C, long ldc, long strideC, float alpha, float beta, int trans,
+                                     int col_group, long group_stride) {
+  const int c4n = (Cc + 3) >> 2;
+  const long per_b = (long)R * c4n, total = per_b * batch;
+  const long rc = (long)R * Cc;
+  const bool vec = (Cc & 3) == 0;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int bb = (int)(i / per_b);
+    const int rem = (int)(i - (long)bb * per_b);
+    const int r = rem / c4n, c = (rem - r * c4n) * 4;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const float *src = ws + (long)bb * splits * rc + (long)r * Cc + c;
+    for (int s = 0; s < splits; ++s, src += rc) {
+      if (vec) {
+        const float4 v = *reinterpret_cast<const float4 *>(src);
+        acc[0] += v.x; acc[1] += v.y; acc[2] += v.z; acc[3] += v.w;
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (c + q < Cc) acc[q] += src[q];
+      }
+    }
+    float *cb = C + (long)bb * strideC;
+    if (!trans) {
+      const long colbase = col_group > 0 ? (long)(c / col_group) * group_stride + c % col_group : c;
+      float *dst = cb + (long)r * ldc + colbase;
+      if (vec && (col_group == 0 || (col_group & 3) == 0) && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+        float4 o = make_float4(alpha * acc[0], alpha * acc[1], alpha * acc[2], alpha * acc[3]);
+        if (beta != 0.f) {
+          const float4 old = *reinterpret_cast<const float4 *>(dst);
+          o.x += beta * old.x; o.y += beta * old.y; o.z += beta * old.z; o.w += beta * old.w;
+        }
+        *reinterpret_cast<float4 *>(dst) = o;
+        continue;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (c + q >= Cc) break;
+      const int row = trans ? c + q : r, col = trans ? r : c + q;
+      float *dst = cb + (long)row * ldc +
+                   (col_group > 0 ? (long)(col / col_group) * group_stride + col % col_group : col);
+      *dst = beta != 0.f ? alpha * acc[q] + beta * *dst : alpha * acc[q];
+    }
+  }
 }
 
 }  // namespace
@@ -350,26 +529,29 @@ bool tc_gemm_supported(const GemmArgs &g) {
   return encode_fn() != nullptr;
 }
 
-namespace {
-// C[b] = alpha * sum_s ws[b][s] + beta * C[b], summed in split order (deterministic).
-__global__ void splitk_reduce_kernel(const float *__restrict__ ws, int splits, int batch, int M, int N,
-                                     float *C, long ldc, long strideC, float alpha, float beta) {
-  const size_t mn = (size_t)M * N, total = mn * batch;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const size_t bb = i / mn, r = i % mn;
-    float acc = 0.f;
-    for (int s = 0; s < splits; ++s) acc += ws[(bb * splits + s) * mn + r];
-    const size_t m = r / N, n = r % N;
-    float *c = C + bb * strideC + m * ldc + n;
-    *c = beta != 0.f ? alpha * acc + beta * *c : alpha * acc;
+cudaError_t tc_gemm(const GemmArgs &g0, cudaStream_t st, float *ws, size_t ws_floats) {
+  if (g0.M <= 0 || g0.N <= 0 || g0.batch <= 0) return cudaSuccess;
+  GemmArgs g = g0;
+  // A short output (M <= 64 rows, e.g. a 32-row head gradient) wastes most of
+  // the 128-row MMA: form C^T = opB^T opA^T instead and let the split-K
+  // reduction write it back transposed.
+  bool trans = false;
+  const size_t out_floats = (size_t)g0.batch * g0.M * g0.N;
+  if (g.M <= 64 && g.N >= 128 && ws && out_floats <= ws_floats) {
+    trans = true;
+    g.M = g0.N; g.N = g0.M;
+    g.A = g0.B; g.lda = g0.ldb; g.strideA = g0.strideB; g.transA = !g0.transB;
+    g.B = g0.A; g.ldb = g0.lda; g.strideB = g0.strideA; g.transB = !g0.transA;
   }
-}
-}  // namespace
-
-cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st, float *ws, size_t ws_floats) {
+  // the column-group and transposed outputs exist only in the split-K reduction
+  const bool need_ws = trans || g.col_group > 0;
+  if (need_ws && (!ws || out_floats > ws_floats)) return cudaErrorInvalidValue;
   // A: K-major when not transposed (row m contiguous along k).
   const bool a_k = !g.transA, b_k = g.transB;
+  const bool split3 = !g.tf32;
+  const TcTuning &t = tuning();
+  int BN = g.N <= 32 ? 32 : g.N <= 64 ? 64 : (split3 || g.N < 256) ? 128 : 256;
+  if (t.bn == 32 || t.bn == 64 || t.bn == 128 || (t.bn == 256 && !split3)) BN = t.bn;
   CUtensorMap ma, mb;
   const bool a_batched = g.strideA != 0 && g.batch > 1;
   bool ok;
@@ -378,7 +560,6 @@ cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st, float *ws, size_t ws_flo
   else      // dims: m (contiguous), k, batch
     ok = make_map(&ma, g.A, g.M, g.K, a_batched ? g.batch : 1, g.lda, g.strideA, 32, BK, false);
   if (!ok) return cudaErrorInvalidValue;
-  const int BN = g.N >= 128 ? 128 : 32;
   const bool b_batched = g.strideB != 0 && g.batch > 1;
   if (b_k)  // B stored [n][k]
     ok = make_map(&mb, g.B, g.K, g.N, b_batched ? g.batch : 1, g.ldb, g.strideB, BK, BN, true);
@@ -386,20 +567,30 @@ cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st, float *ws, size_t ws_flo
     ok = make_map(&mb, g.B, g.N, g.K, b_batched ? g.batch : 1, g.ldb, g.strideB, 32, BK, false);
   if (!ok) return cudaErrorInvalidValue;
   TcParams p{g.M, g.N, g.K, a_k, b_k, g.C, g.ldc, g.strideC, g.alpha, g.beta, a_batched ? 1 : 0,
-             b_batched ? 1 : 0, 1, 0, 0, g.tf32 ? 1 : 0};
+             b_batched ? 1 : 0, 1, 0, 0, 0};
   const int tiles_n = (g.N + BN - 1) / BN, tiles_m = (g.M + BM - 1) / BM;
   const int tiles = tiles_n * tiles_m * g.batch;
   const int kblocks = (g.K + BK - 1) / BK;
   int zdim = g.batch;
   // Split K when the output (all batches) has too few tiles to fill the GPU
   // and K is long enough; the partial sums go to the workspace.
+  int splits = 1, chunk = kblocks;
   if (ws && tiles < 148 && kblocks >= 64) {
-    int splits = (2 * 148 + tiles - 1) / tiles;
+    splits = (2 * 148 + tiles - 1) / tiles;
     if (splits > 16) splits = 16;
     if (splits > kblocks / 4) splits = kblocks / 4;
-    const int chunk = (kblocks + splits - 1) / splits;
+    chunk = (kblocks + splits - 1) / splits;
     splits = (kblocks + chunk - 1) / chunk;
-    if ((size_t)splits * g.batch * g.M * g.N <= ws_floats && splits > 1) {
+  }
+  if (ws && splits > 1 && (size_t)splits * out_floats > ws_floats) {  // as many splits as the workspace holds
+    splits = (int)(ws_floats / out_floats);
+    if (splits < 1) splits = 1;
+    chunk = (kblocks + splits - 1) / splits;
+    splits = (kblocks + chunk - 1) / chunk;
+  }
+  const bool use_ws = need_ws || splits > 1;
+  if (use_ws) {
+    {
       p.ksplit = splits;
       p.kchunk = chunk;
       p.C = ws;
@@ -410,6 +601,7 @@ cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st, float *ws, size_t ws_flo
       zdim = splits * g.batch;
     }
   }
+  const bool to_ws = p.C == ws && ws != nullptr && use_ws;
   // Coalesced epilogue through bulk tensor stores when C allows a tensor map
   // (16-byte aligned rows) and beta is 0 or 1 (reduce-add in L2).
   CUtensorMap mc;
@@ -419,20 +611,28 @@ cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t st, float *ws, size_t ws_flo
       make_map_sw(&mc, p.C, g.N, g.M, zdim, p.ldc, p.strideC, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B))
     p.tma_epi = 1;
   dim3 grid(tiles_n, tiles_m, zdim);
-  if (BN == 128) {
-    const size_t smem = tc_smem<128>();
-    cudaFuncSetAttribute(tcgemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    tcgemm_kernel<128><<<grid, TC_THREADS, smem, st>>>(ma, mb, mc, p);
+  // two CTAs per SM whenever the grid covers the GPU more than once: one
+  // CTA's prologue, first-load latency and epilogue then overlap the other's
+  // main loop, which pays more than a deeper ring (measured: 3xTF32 at
+  // 16384 x 512 x 512 x 8, 557 -> 480 us with a 1-stage ring per CTA)
+  int cps = (long)tiles_n * tiles_m * zdim > 148 ? 2 : 1;
+  if (t.cps == 1 || t.cps == 2) cps = t.cps;
+  cudaError_t e;
+  if (split3) {
+    e = BN == 32 ? launch_tc<32, true>(grid, ma, mb, mc, p, cps, st)
+        : BN == 64 ? launch_tc<64, true>(grid, ma, mb, mc, p, cps, st)
+                   : launch_tc<128, true>(grid, ma, mb, mc, p, cps, st);
   } else {
-    const size_t smem = tc_smem<32>();
-    cudaFuncSetAttribute(tcgemm_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    tcgemm_kernel<32><<<grid, TC_THREADS, smem, st>>>(ma, mb, mc, p);
+    e = BN == 32 ? launch_tc<32, false>(grid, ma, mb, mc, p, cps, st)
+        : BN == 64 ? launch_tc<64, false>(grid, ma, mb, mc, p, cps, st)
+        : BN == 128 ? launch_tc<128, false>(grid, ma, mb, mc, p, cps, st)
+                    : launch_tc<256, false>(grid, ma, mb, mc, p, cps, st);
   }
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess || p.ksplit <= 1) return e;
+  if (e != cudaSuccess || !to_ws) return e;
   tc_extra_launches++;
-  splitk_reduce_kernel<<<148 * 4, 256, 0, st>>>(ws, p.ksplit, g.batch, g.M, g.N, g.C, g.ldc,
-                                                g.batch > 1 ? g.strideC : 0, g.alpha, g.beta);
+  splitk_reduce_kernel<<<148 * 4, 256, 0, st>>>(ws, p.ksplit, g.batch, g.M, g.N, g0.C, g0.ldc,
+                                                g.batch > 1 ? g0.strideC : 0, g0.alpha, g0.beta, trans ? 1 : 0,
+                                                g0.col_group, g0.group_stride);
   return cudaGetLastError();
 }
 
@@ -455,3 +655,14 @@ unsigned int tc_gemm_error(bool reset) {
 }
 
 }  // namespace aideen
+
+#ifdef AIDEEN_TC_PROF
+extern "C" int aideen_debug_tc_prof(unsigned long long *out, int n, int reset) {
+  if (out && cudaMemcpyFromSymbol(out, aideen::g_tc_prof, n * sizeof(unsigned long long)) != cudaSuccess) return 2;
+  if (reset) {
+    static unsigned long long zeros[4096 * 8];
+    cudaMemcpyToSymbol(aideen::g_tc_prof, zeros, sizeof(zeros));
+  }
+  return 0;
+}
+#endif

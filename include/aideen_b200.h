@@ -314,10 +314,13 @@ int aideen_adjoint_noalloc(const float *hstar, const float *branch, const float 
 /* ---- diagnostics (no counterpart in the reference) --------------------------
  * Runs a tcgen05 3xTF32 GEMM and the CUDA-core fp32 GEMM on the same seeded
  * device operands (C = op(A) op(B), row-major, `batch` independent problems)
- * and reports the relative L2 difference and both kernel times.  flags bit 0
+ * and reports the relative L2 difference and both kernel times (the tensor-core
+ * time averaged over 10 back-to-back calls).  flags bit 0
  * selects the persistent kernel on pre-split (hi/lo) operands instead of the
  * in-kernel-split one.  Allocates its own temporaries. */
 #define AIDEEN_SELFTEST_PRESPLIT 1
+/* flags bit 1: single TF32 products (operands rounded to tf32) instead of 3xTF32 */
+#define AIDEEN_SELFTEST_TF32 2
 int aideen_gemm_selftest(aideen_ctx *ctx, int M, int N, int K, int batch, int trans_a, int trans_b,
                          int flags, float *rel_err, float *ms_tc, float *ms_simt);
 
