@@ -44,8 +44,10 @@ __global__ void fpm_c_kernel(const float4 *__restrict__ hs, const float4 *__rest
     c[i] = 0.5f * (hs[i] + sig[i]);
 }
 
-// Coefficients of one (token, slot) row, computed by one warp; lane owns the
-// float4 columns lane + 32*i.  Every gradient term of the reference's token
+// Coefficients of one (token, slot) row, computed by WPR warps; row thread
+// rl = 32 * (warp % WPR) + lane owns the float4 columns rl + 32 * WPR * i, and
+// the row's four sums are combined in `red` ([WPR][4], in warp order) behind
+// the pair's named barrier `bar` (WPR > 1).  Every gradient term of the reference's token
 // step is linear in g = dL/dM[t]:
 //   alpha: g[t-1] = alpha * g + 0.5 v[t]      cpre:  g_pre (b_retain, W_retain_*)
 //   cbd:   b_delta term                       calog: a_log term
@@ -56,17 +58,23 @@ __global__ void fpm_c_kernel(const float4 *__restrict__ hs, const float4 *__rest
 // prm: the slot's parameters staged in shared memory,
 //   [0,d) b_retain  [d,2d) b_delta  [2d,3d) W_write_gate  [3d,4d) a = sigmoid(-a_log)
 //   [4d,5d) 0.5 tanh(diag W_x)
-template <int NV, bool FULL>
+__device__ __forceinline__ void pair_sync(int bar, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory");
+}
+
+template <int NV, int WPR, bool FULL>
 __device__ __forceinline__ void row_coefs(const FpmBwdArgs &a, const float *prm, int n, int s, int t,
-                                          float *sm_row, size_t plane, float *rz_out) {
+                                          float *sm_row, size_t plane, float *rz_out, float *red, int bar) {
   const int lane = threadIdx.x & 31;
+  const int wp = (threadIdx.x >> 5) % WPR;
+  const int rl = 32 * wp + lane;
   const int d = a.d, h = a.h;
   const size_t row = ((size_t)n * h + s) * d;
   float4 hv[NV], mp[NV], pr[NV], rt[NV];
   float hsq = 0.f, gdot = 0.f, psq = 0.f, dsq = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
-    const int k = 4 * (lane + 32 * i);
+    const int k = 4 * (rl + 32 * WPR * i);
     hv[i] = ld4(a.hstar + row + k);
     mp[i] = t > 0 ? ld4(a.hist + row - (size_t)a.B * h * d + k) : f4(0.f);  // token t-1, token-major rows
     const float4 dl = ld4(a.dpre + row + k) + ld4(prm + d + k);
@@ -83,6 +91,23 @@ __device__ __forceinline__ void row_coefs(const FpmBwdArgs &a, const float *prm,
   gdot = warp_sum(gdot);
   psq = warp_sum(psq);
   dsq = warp_sum(dsq);
+  if (WPR > 1) {
+    if (lane == 0) {
+      red[4 * wp + 0] = hsq;
+      red[4 * wp + 1] = gdot;
+      red[4 * wp + 2] = psq;
+      red[4 * wp + 3] = dsq;
+    }
+    pair_sync(bar, 32 * WPR);
+    hsq = gdot = psq = dsq = 0.f;
+#pragma unroll
+    for (int q = 0; q < WPR; ++q) {
+      hsq += red[4 * q + 0];
+      gdot += red[4 * q + 1];
+      psq += red[4 * q + 2];
+      dsq += red[4 * q + 3];
+    }
+  }
   const float raw_z = sigm(gdot * rsqrtf((float)d) + a.W[a.off_bwrite + s] + kGateBias);
   const float z = fminf(fmaxf(raw_z, 0.f), 1.f);
   const float prev_norm = sqrtf(fmaxf(psq, 1e-6f));
@@ -95,10 +120,10 @@ __device__ __forceinline__ void row_coefs(const FpmBwdArgs &a, const float *prm,
   const float inv_dn = 1.f / fmaxf(diff_norm, 1e-6f);
   const float inv_pn = 1.f / fmaxf(prev_norm, 1e-6f);
   const float zs = 0.5f / sqrtf(fmaxf(z, 1e-6f));
-  if (FULL && lane == 0) *rz_out = raw_z * (1.f - raw_z);
+  if (FULL && rl == 0) *rz_out = raw_z * (1.f - raw_z);
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
-    const int k = 4 * (lane + 32 * i);
+    const int k = 4 * (rl + 32 * WPR * i);
     const float4 am4 = ld4(prm + 3 * d + k), wx4 = ld4(prm + 4 * d + k);
     float o_alpha[4], o_pre[4], o_bd[4], o_alog[4], o_gz[4], o_wx[4], o_min[4];
     const float hvv[4] = {hv[i].x, hv[i].y, hv[i].z, hv[i].w};
@@ -141,16 +166,16 @@ __device__ __forceinline__ void row_coefs(const FpmBwdArgs &a, const float *prm,
   }
 }
 
-// One CTA per (chunk of CH tokens, slot, sequence); warp w computes token w's
-// coefficients into shared memory, then one thread per dimension walks the
-// chunk backwards.
+// One CTA per (chunk of CH tokens, slot, sequence); warps WPR*w .. WPR*w+WPR-1
+// compute token w's coefficients into shared memory, then one thread per
+// dimension walks the chunk backwards.
 //   FULL = false: chunk composite  g_in -> A * g_in + U  (alpha products and
 //                 the accumulated read seeds), written to a.cA / a.cU.
 //   FULL = true:  from the chunk's entry value a.gin, emit dm and g_pre, the
 //                 per-chunk sums of every elementwise gradient term, and the
 //                 write-gate terms (W_write_gate, b_write_mem).
-template <int NV, int CH, bool FULL>
-__global__ void __launch_bounds__(32 * CH) fpm_chunk_kernel(FpmBwdArgs a) {
+template <int NV, int CH, int WPR, bool FULL>
+__global__ void __launch_bounds__(32 * CH * WPR) fpm_chunk_kernel(FpmBwdArgs a) {
   extern __shared__ __align__(16) float sm[];
   const int ch = (FULL ? 0 : a.ch0) + blockIdx.x, s = blockIdx.y, b = blockIdx.z;
   const int d = a.d, h = a.h, T = a.T, nch = a.nch;
@@ -159,29 +184,31 @@ __global__ void __launch_bounds__(32 * CH) fpm_chunk_kernel(FpmBwdArgs a) {
   float *rz = vs + plane;
   float *graw = rz + CH;
   float *prm = graw + CH;   // 5 * d staged slot parameters (CH is even)
+  float *red = prm + 5 * d;  // [CH][WPR][4] row sums
   {
     const float4 *src = reinterpret_cast<const float4 *>(a.slot_prm + (size_t)s * 5 * d);
     for (int k = threadIdx.x; k < 5 * d / 4; k += blockDim.x) reinterpret_cast<float4 *>(prm)[k] = src[k];
   }
   __syncthreads();
-  const int w = threadIdx.x >> 5;
+  const int w = (threadIdx.x >> 5) / WPR;  // token of the chunk this warp works on
+  const int rl = threadIdx.x % (32 * WPR);
   const int t0 = ch * CH;
   const int nt = min(CH, T - t0);
   const size_t N = (size_t)a.B * T;
   if (w < nt) {
-    const int lane = threadIdx.x & 31;
     const size_t n = (size_t)(t0 + w) * a.B + b;
     const float *vrow = a.v + ((size_t)s * N + n) * d;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const int k = 4 * (lane + 32 * i);
+      const int k = 4 * (rl + 32 * WPR * i);
       const float4 x = ld4(vrow + k);
       st4(vs + (size_t)w * d + k, make_float4(isfinite(x.x) ? kReadGradScale * x.x : 0.f,
                                               isfinite(x.y) ? kReadGradScale * x.y : 0.f,
                                               isfinite(x.z) ? kReadGradScale * x.z : 0.f,
                                               isfinite(x.w) ? kReadGradScale * x.w : 0.f));
     }
-    row_coefs<NV, FULL>(a, prm, (int)n, s, t0 + w, sm + (size_t)w * d, plane, rz + w);
+    row_coefs<NV, WPR, FULL>(a, prm, (int)n, s, t0 + w, sm + (size_t)w * d, plane, rz + w, red + 4 * WPR * w,
+                             1 + w);
   }
   __syncthreads();
   const size_t bc = ((size_t)b * nch + ch) * h + s;   // (sequence, chunk, slot) row of the partials
@@ -230,11 +257,19 @@ __global__ void __launch_bounds__(32 * CH) fpm_chunk_kernel(FpmBwdArgs a) {
     float acc = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const int k = 4 * (lane + 32 * i);
+      const int k = 4 * (rl + 32 * WPR * i);
       acc += dot4(ld4(cg + k), ld4(dm + k));
     }
     acc = warp_sum(acc);
-    if (lane == 0) graw[w] = acc * rz[w];
+    if (WPR > 1) {
+      float *r2 = red + 4 * WPR * w;  // free again: the row sums were consumed before the scan
+      if (lane == 0) r2[rl >> 5] = acc;
+      pair_sync(1 + w, 32 * WPR);
+      acc = 0.f;
+#pragma unroll
+      for (int q = 0; q < WPR; ++q) acc += r2[q];
+    }
+    if (rl == 0) graw[w] = acc * rz[w];
   }
   __syncthreads();
   for (int k = threadIdx.x; k < d; k += blockDim.x) {
@@ -348,20 +383,21 @@ int fpm_chunk_len(int d) { return d > 512 ? 2 : 4; }
 
 size_t fpm_chunk_smem(int d, bool full) {
   const int CH = fpm_chunk_len(d);
-  return ((full ? 7 : 2) * (size_t)CH * d + 2 * CH + 5 * (size_t)d) * sizeof(float);
+  return ((full ? 7 : 2) * (size_t)CH * d + 2 * CH + 5 * (size_t)d + 8 * (size_t)CH) * sizeof(float);
 }
 
-template <int NV, int CH, bool FULL>
+template <int NV, int CH, int WPR, bool FULL>
 static cudaError_t chunk_launch(const FpmBwdArgs &a, cudaStream_t st) {
+  static_assert(CH <= 15, "one named barrier per token row");
   const size_t smem = fpm_chunk_smem(a.d, FULL);
-  auto k = fpm_chunk_kernel<NV, CH, FULL>;
+  auto k = fpm_chunk_kernel<NV, CH, WPR, FULL>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int nx = (!FULL && a.ch1 > 0) ? a.ch1 - a.ch0 : a.nch;
   if (nx <= 0) return cudaSuccess;
   FpmBwdArgs b = a;
   if (FULL || a.ch1 <= 0) b.ch0 = 0;
-  k<<<dim3(nx, a.h, a.B), 32 * CH, smem, st>>>(b);
+  k<<<dim3(nx, a.h, a.B), 32 * CH * WPR, smem, st>>>(b);
   return cudaGetLastError();
 }
 
@@ -369,10 +405,10 @@ template <bool FULL>
 static cudaError_t chunk_dispatch(const FpmBwdArgs &a, cudaStream_t st) {
   if (a.nch != (a.T + fpm_chunk_len(a.d) - 1) / fpm_chunk_len(a.d)) return cudaErrorInvalidValue;
   switch (a.d / 128) {
-    case 1: return chunk_launch<1, 4, FULL>(a, st);
-    case 2: return chunk_launch<2, 4, FULL>(a, st);
-    case 4: return chunk_launch<4, 4, FULL>(a, st);
-    case 8: return chunk_launch<8, 2, FULL>(a, st);
+    case 1: return chunk_launch<1, 4, 1, FULL>(a, st);
+    case 2: return chunk_launch<1, 4, 2, FULL>(a, st);
+    case 4: return chunk_launch<2, 4, 2, FULL>(a, st);
+    case 8: return chunk_launch<4, 2, 2, FULL>(a, st);
     default: return cudaErrorInvalidValue;
   }
 }
