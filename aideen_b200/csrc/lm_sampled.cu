@@ -322,8 +322,18 @@ __global__ void emb_adam_kernel(float *__restrict__ emb, float *__restrict__ M1,
   const int t = uniq[u], o0 = off[u], o1 = off[u + 1];
   const float ic = 1.f / (float)(o1 - o0 > 0 ? o1 - o0 : 1);
   for (int j = threadIdx.x * 4; j < d; j += blockDim.x * 4) {
-    float4 g = f4(0.f);
-    for (int q = o0; q < o1; ++q) g = g + ld4(grad + (size_t)pos[q] * d + j);
+    // eight independent partial sums (positions q = o0 + 8i + r), combined in
+    // a fixed order: a frequent token's rows stream with 8 loads in flight
+    float4 gp[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) gp[r] = f4(0.f);
+    int q = o0;
+    for (; q + 8 <= o1; q += 8) {
+#pragma unroll
+      for (int r = 0; r < 8; ++r) gp[r] = gp[r] + ld4(grad + (size_t)pos[q + r] * d + j);
+    }
+    for (int r = 0; q < o1; ++q, ++r) gp[r] = gp[r] + ld4(grad + (size_t)pos[q] * d + j);
+    float4 g = ((gp[0] + gp[1]) + (gp[2] + gp[3])) + ((gp[4] + gp[5]) + (gp[6] + gp[7]));
     g = ic * g;
     const size_t idx = (size_t)t * d + j;
     float4 m = ld4(M1 + idx), s = ld4(M2 + idx), w = ld4(emb + idx);

@@ -5,7 +5,7 @@
 //               (aideen-training-lab/src/optimizer.rs:105-183)
 //   clipped_sgd w <- w*(1 - lr*wd [main weights]) - clamp(lr*g*scale, +-0.5)
 //               (fused_deq_update.wgsl:402-410, 809-823)
-//   spectral    power iteration + rescale, one CTA per matrix
+//   spectral    power iteration + rescale, a cluster of 8 CTAs per matrix
 //               (aideen-block/src/shaders/spectral_renorm.wgsl:83-196)
 //   softmax_ce / rmsnorm_bwd: dense LM-head loss and dL/dH_pooled
 //               (lm_train.wgsl:79-130, 327-395)
@@ -16,23 +16,45 @@ namespace cg = cooperative_groups;
 
 namespace aideen {
 
+// Two float4 groups per thread and iteration (8 independent 16-byte loads in
+// flight); the gradient and moments stream through with evict-first hints,
+// the weights (read again by the next forward) with default caching.
+__device__ __forceinline__ void adam4(float *__restrict__ w, const float *__restrict__ g, float *__restrict__ m1,
+                                      float *__restrict__ m2, size_t i, float4 gg, float4 m, float4 v, float4 ww,
+                                      float lr, float b1, float b2, float eps, float bc1, float bc2) {
+  m = b1 * m + (1.f - b1) * gg;
+  v = b2 * v + (1.f - b2) * (gg * gg);
+  __stcs(reinterpret_cast<float4 *>(m1) + i, m);
+  __stcs(reinterpret_cast<float4 *>(m2) + i, v);
+  ww.x -= lr * (m.x / bc1) / (sqrtf(v.x / bc2) + eps);
+  ww.y -= lr * (m.y / bc1) / (sqrtf(v.y / bc2) + eps);
+  ww.z -= lr * (m.z / bc1) / (sqrtf(v.z / bc2) + eps);
+  ww.w -= lr * (m.w / bc1) / (sqrtf(v.w / bc2) + eps);
+  reinterpret_cast<float4 *>(w)[i] = ww;
+}
+
 __global__ void adam_kernel(float *__restrict__ w, const float *__restrict__ g, float *__restrict__ m1,
                             float *__restrict__ m2, size_t n, float lr, float b1, float b2,
                             float eps, float bc1, float bc2, float gs) {
   const size_t n4 = n / 4;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
-    const float4 gg = gs * ld4(g + 4 * i);
-    const float4 m = b1 * ld4(m1 + 4 * i) + (1.f - b1) * gg;
-    const float4 v = b2 * ld4(m2 + 4 * i) + (1.f - b2) * (gg * gg);
-    st4(m1 + 4 * i, m);
-    st4(m2 + 4 * i, v);
-    float4 ww = ld4(w + 4 * i);
-    ww.x -= lr * (m.x / bc1) / (sqrtf(v.x / bc2) + eps);
-    ww.y -= lr * (m.y / bc1) / (sqrtf(v.y / bc2) + eps);
-    ww.z -= lr * (m.z / bc1) / (sqrtf(v.z / bc2) + eps);
-    ww.w -= lr * (m.w / bc1) / (sqrtf(v.w / bc2) + eps);
-    st4(w + 4 * i, ww);
+  const float4 *g4 = reinterpret_cast<const float4 *>(g);
+  const float4 *a4 = reinterpret_cast<const float4 *>(m1);
+  const float4 *b4 = reinterpret_cast<const float4 *>(m2);
+  const float4 *w4 = reinterpret_cast<const float4 *>(w);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += 2 * stride) {
+    const size_t j = i + stride;
+    const bool two = j < n4;
+    const float4 ga = __ldcs(g4 + i), ma = __ldcs(a4 + i), va = __ldcs(b4 + i), wa = w4[i];
+    float4 gb = f4(0.f), mb = f4(0.f), vb = f4(0.f), wb = f4(0.f);
+    if (two) {
+      gb = __ldcs(g4 + j);
+      mb = __ldcs(a4 + j);
+      vb = __ldcs(b4 + j);
+      wb = w4[j];
+    }
+    adam4(w, g, m1, m2, i, gs * ga, ma, va, wa, lr, b1, b2, eps, bc1, bc2);
+    if (two) adam4(w, g, m1, m2, j, gs * gb, mb, vb, wb, lr, b1, b2, eps, bc1, bc2);
   }
   if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {  // tail
     const size_t i = n4 * 4 + threadIdx.x;
@@ -75,8 +97,6 @@ cudaError_t launch_clipped_sgd(float *w, const float *g, size_t n, size_t main_l
   return cudaGetLastError();
 }
 
-// One CTA (1024 threads) per matrix.  Row-major view A[r][c] = M[r*d + c]:
-// v = A^T u / |A^T u|, u = A v, sigma = |u|, u /= sigma; rescale if sigma > thr.
 struct SpecArgs {
   float *W;
   int d, h, n_iters;
@@ -85,84 +105,32 @@ struct SpecArgs {
   float *sigmas;
 };
 
-__global__ void __launch_bounds__(1024) spectral_kernel(SpecArgs a) {
-  extern __shared__ float sm[];
-  float *u = sm, *v = sm + a.d, *red = sm + 2 * a.d;  // red: 64
-  const int mi = blockIdx.x, h = a.h, d = a.d;
-  size_t off;
-  float thr;
-  if (mi < h) { off = a.wq + (size_t)mi * d * d; thr = a.attn; }
-  else if (mi < 2 * h) { off = a.wk + (size_t)(mi - h) * d * d; thr = a.attn; }
-  else if (mi < 3 * h) { off = a.wv + (size_t)(mi - 2 * h) * d * d; thr = a.wvth; }
-  else if (mi < 4 * h) { off = a.wo + (size_t)(mi - 3 * h) * d * d; thr = a.woth; }
-  else if (mi < 5 * h) { off = a.win + (size_t)(mi - 4 * h) * d * d; thr = a.winth; }
-  else if (mi == 5 * h) { off = a.wx; thr = a.fpm; }
-  else { off = a.wout; thr = a.fpm; }
-  float *M = a.W + off;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-  const float u0 = 1.f / sqrtf((float)d);
-  for (int i = tid; i < d; i += blockDim.x) u[i] = u0;
-  __syncthreads();
-  float sigma = 1.f;
-  for (int it = 0; it < a.n_iters; ++it) {
-    float part = 0.f;
-    for (int c = tid; c < d; c += blockDim.x) {  // v[c] = sum_r A[r][c] u[r]
-      float acc = 0.f;
-      for (int r = 0; r < d; ++r) acc += M[(size_t)r * d + c] * u[r];
-      v[c] = acc;
-      part += acc * acc;
-    }
-    part = warp_sum(part);
-    if (lane == 0) red[warp] = part;
-    __syncthreads();
-    float vn = 0.f;
-    for (int w = 0; w < nw; ++w) vn += red[w];
-    vn = sqrtf(vn + 1e-12f);
-    for (int c = tid; c < d; c += blockDim.x) v[c] /= vn;
-    __syncthreads();
-    float upart = 0.f;
-    for (int r = warp; r < d; r += nw) {  // u[r] = sum_c A[r][c] v[c], warp per row
-      float acc = 0.f;
-      for (int c = lane; c < d; c += 32) acc += M[(size_t)r * d + c] * v[c];
-      acc = warp_sum(acc);
-      if (lane == 0) { u[r] = acc; upart += acc * acc; }
-    }
-    if (lane == 0) red[32 + warp] = upart;
-    __syncthreads();
-    float un = 0.f;
-    for (int w = 0; w < nw; ++w) un += red[32 + w];
-    sigma = sqrtf(un + 1e-12f);
-    for (int r = tid; r < d; r += blockDim.x) u[r] /= sigma;
-    __syncthreads();
-  }
-  if (tid == 0 && a.sigmas) a.sigmas[mi] = sigma;
-  if (sigma > thr) {
-    const float sc = thr / sigma;
-    for (size_t i = tid; i < (size_t)d * d; i += blockDim.x) M[i] *= sc;
-  }
-}
-
-// Cluster variant for d <= 512: a cluster of 8 CTAs per matrix, CTA q of the
-// cluster keeping rows [q*R, (q+1)*R) (R = d/8) in shared memory for all the
-// power iterations.  Per iteration: v = A^T u from per-CTA partials summed
-// through distributed shared memory (each CTA owns a column slice), then
-// u = A v on the local rows; the norms are summed across the cluster.  The
-// arithmetic is the single-CTA kernel's (same sums, same normalisations).
+// Power iteration (d a multiple of 128, d <= 1024): a cluster of 8 CTAs per
+// matrix, CTA q owning rows [q*R, (q+1)*R), R = d/8, streamed from L2 on every
+// sweep (all 5h+2 matrices stay L2-resident and every CTA of the launch is
+// resident at once).  One sweep over the local rows forms both u_r = A_r . v
+// (a warp per row) and this CTA's share of A^T u, kept per lane (lane owns
+// the float4 columns lane + 32 i); the shares are summed over warps and then
+// over the cluster in rank order.  Sweep 0 uses the reference's start vector
+// u = 1/sqrt(d); sweep k >= 1 gives sigma_k = |A v_k| and v_{k+1} = A^T u_k /
+// |A^T u_k|, the same vectors as the reference's v = A^T u / |A^T u|,
+// u = A v, sigma = |u|, u /= sigma (the scale of u cancels in the next
+// normalisation).
 constexpr int kSpecCluster = 8;
 
-__global__ void __launch_bounds__(256) spectral_cluster_kernel(SpecArgs a) {
+template <int NV>
+__global__ void __launch_bounds__(256, NV <= 4 ? 3 : 1) spectral_sweep_kernel(SpecArgs a) {
   extern __shared__ __align__(16) float smc[];
   cg::cluster_group cl = cg::this_cluster();
   const int d = a.d, h = a.h, R = d / kSpecCluster;
   const int q = (int)cl.block_rank();
   const int mi = blockIdx.x / kSpecCluster;
-  float *Ms = smc;                 // R x d
-  float *vpart = Ms + (size_t)R * d;  // d   partial A^T u over local rows
-  float *vslice = vpart + d;       // R   reduced column slice [q*R, (q+1)*R)
-  float *vfull = vslice + R;       // d
-  float *uloc = vfull + d;         // R
-  float *nrm = uloc + R;           // [0] slice |v|^2, [1] local |u|^2
-  float *red = nrm + 4;            // 32
+  float *vfull = smc;                 // d   normalised v
+  float *vpart = vfull + d;           // d   this CTA's share of A^T u
+  float *wpart = vpart + d;           // 8 x d per-warp shares
+  float *vslice = wpart + 8 * d;      // R   cluster sum of the column slice [q*R, (q+1)*R)
+  float *nrm = vslice + R;            // [0] slice |v|^2, [1] local |u|^2 (published between the syncs)
+  float *red = nrm + 4;               // 8 per-warp |u|^2
   size_t off;
   float thr;
   if (mi < h) { off = a.wq + (size_t)mi * d * d; thr = a.attn; }
@@ -173,70 +141,85 @@ __global__ void __launch_bounds__(256) spectral_cluster_kernel(SpecArgs a) {
   else if (mi == 5 * h) { off = a.wx; thr = a.fpm; }
   else { off = a.wout; thr = a.fpm; }
   float *M = a.W + off + (size_t)q * R * d;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-  for (int i = tid * 4; i < R * d; i += blockDim.x * 4) st4(Ms + i, ld4(M + i));
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float u0 = 1.f / sqrtf((float)d);
-  for (int i = tid; i < R; i += blockDim.x) uloc[i] = u0;
-  __syncthreads();
   float sigma = 1.f;
-  for (int it = 0; it < a.n_iters; ++it) {
-    // partial v over the local rows
-    for (int c = tid; c < d; c += blockDim.x) {
-      float acc = 0.f;
-      for (int r = 0; r < R; ++r) acc += Ms[(size_t)r * d + c] * uloc[r];
-      vpart[c] = acc;
+  for (int it = 0; it <= a.n_iters; ++it) {
+    float4 vr[NV], acc[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      vr[i] = it > 0 ? ld4(vfull + 4 * (lane + 32 * i)) : f4(0.f);
+      acc[i] = f4(0.f);
     }
+    float uu = 0.f;
+#pragma unroll 1
+    for (int r = warp; r < R; r += 8) {
+      float4 av[NV];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) av[i] = ld4(M + (size_t)r * d + 4 * (lane + 32 * i));
+      float ur = u0;
+      if (it > 0) {
+        float p = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) p += dot4(av[i], vr[i]);
+        ur = warp_sum(p);
+        uu += ur * ur;
+      }
+#pragma unroll
+      for (int i = 0; i < NV; ++i) acc[i] = fma4(av[i], f4(ur), acc[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) st4(wpart + (size_t)warp * d + 4 * (lane + 32 * i), acc[i]);
+    if (lane == 0) red[warp] = uu;
+    __syncthreads();
+    for (int c = tid; c < d; c += blockDim.x) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) t += wpart[(size_t)w * d + c];
+      vpart[c] = t;
+    }
+    float uu_cta = 0.f;
+    if (tid == 0)
+      for (int w = 0; w < 8; ++w) uu_cta += red[w];
     cl.sync();
-    // this CTA's column slice, summed over the cluster in rank order
+    if (tid == 0) nrm[1] = uu_cta;
+    // this CTA's column slice of A^T u, summed over the cluster in rank order
     float part = 0.f;
     for (int i = tid; i < R; i += blockDim.x) {
-      float acc = 0.f;
-      for (int p = 0; p < kSpecCluster; ++p) acc += cl.map_shared_rank(vpart, p)[q * R + i];
-      vslice[i] = acc;
-      part += acc * acc;
+      float t = 0.f;
+#pragma unroll
+      for (int p = 0; p < kSpecCluster; ++p) t += cl.map_shared_rank(vpart, p)[q * R + i];
+      vslice[i] = t;
+      part += t * t;
     }
     part = warp_sum(part);
+    __syncthreads();  // red[] reads above are done
     if (lane == 0) red[warp] = part;
     __syncthreads();
     if (tid == 0) {
       float t = 0.f;
-      for (int w = 0; w < nw; ++w) t += red[w];
+      for (int w = 0; w < 8; ++w) t += red[w];
       nrm[0] = t;
     }
     cl.sync();
-    float vn2 = 0.f;
-    for (int p = 0; p < kSpecCluster; ++p) vn2 += cl.map_shared_rank(nrm, p)[0];
+    float vn2 = 0.f, un2 = 0.f;
+#pragma unroll
+    for (int p = 0; p < kSpecCluster; ++p) {
+      const float *pn = cl.map_shared_rank(nrm, p);
+      vn2 += pn[0];
+      un2 += pn[1];
+    }
+    if (it > 0) sigma = sqrtf(un2 + 1e-12f);
     const float vn = sqrtf(vn2 + 1e-12f);
     for (int c = tid; c < d; c += blockDim.x) vfull[c] = cl.map_shared_rank(vslice, c / R)[c % R] / vn;
-    __syncthreads();
-    // u = A v on the local rows, warp per row
-    float upart = 0.f;
-    for (int r = warp; r < R; r += nw) {
-      float acc = 0.f;
-      for (int c = lane; c < d; c += 32) acc += Ms[(size_t)r * d + c] * vfull[c];
-      acc = warp_sum(acc);
-      if (lane == 0) { uloc[r] = acc; upart += acc * acc; }
-    }
-    if (lane == 0) red[warp] = upart;
-    __syncthreads();
-    if (tid == 0) {
-      float t = 0.f;
-      for (int w = 0; w < nw; ++w) t += red[w];
-      nrm[1] = t;
-    }
-    cl.sync();
-    float un2 = 0.f;
-    for (int p = 0; p < kSpecCluster; ++p) un2 += cl.map_shared_rank(nrm, p)[1];
-    sigma = sqrtf(un2 + 1e-12f);
-    for (int r = tid; r < R; r += blockDim.x) uloc[r] /= sigma;
     __syncthreads();
   }
   if (tid == 0 && q == 0 && a.sigmas) a.sigmas[mi] = sigma;
   if (sigma > thr) {
     const float sc = thr / sigma;
-    for (int i = tid * 4; i < R * d; i += blockDim.x * 4) st4(M + i, sc * ld4(Ms + i));
+    for (int i = tid * 4; i < R * d; i += blockDim.x * 4) st4(M + i, sc * ld4(M + i));
   }
-  cl.sync();  // peers' last remote reads of this CTA's norms are done
+  cl.sync();  // peers' last remote reads of this CTA's vectors and norms are done
 }
 
 cudaError_t launch_spectral(float *W, int d, int h, const Layout &L, int n_iters, float attn,
@@ -244,11 +227,12 @@ cudaError_t launch_spectral(float *W, int d, int h, const Layout &L, int n_iters
                             cudaStream_t st) {
   SpecArgs a{W, d, h, n_iters, L.wq, L.wk, L.wv, L.wo, L.win, L.wx, L.wout,
              attn, win, fpm, wv, wo, sigmas};
-  if (d % kSpecCluster == 0 && d <= 512) {
+  if (d % 128 == 0 && d <= 1024) {
     const int R = d / kSpecCluster;
-    const size_t smem = ((size_t)R * d + 2 * (size_t)d + 2 * (size_t)R + 4 + 32) * sizeof(float);
-    cudaError_t e = cudaFuncSetAttribute(spectral_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+    const size_t smem = (10 * (size_t)d + (size_t)R + 12) * sizeof(float);
+    auto kern = d == 128 ? spectral_sweep_kernel<1> : d == 256 ? spectral_sweep_kernel<2>
+              : d == 512 ? spectral_sweep_kernel<4> : spectral_sweep_kernel<8>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((5 * h + 2) * kSpecCluster);
@@ -262,13 +246,11 @@ cudaError_t launch_spectral(float *W, int d, int h, const Layout &L, int n_iters
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, spectral_cluster_kernel, a);
+    e = cudaLaunchKernelEx(&cfg, kern, a);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
   }
-  const size_t smem = (2 * (size_t)d + 64) * sizeof(float);
-  spectral_kernel<<<5 * h + 2, 1024, smem, st>>>(a);
-  return cudaGetLastError();
+  return cudaErrorInvalidValue;  // the library's d (128, 256, 512, 1024) always takes the cluster kernel
 }
 
 // ---------------------------------------------------------------- LM head

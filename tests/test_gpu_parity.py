@@ -202,8 +202,8 @@ def test_clipped_sgd_update():
     be.close()
 
 
-def test_spectral_renorm_parity():
-    d, h = 256, 2
+@pytest.mark.parametrize("d,h", [(128, 4), (256, 2), (512, 8), (1024, 16)])
+def test_spectral_renorm_parity(d, h):
     W = init_all_weights(d, h, seed=9, attn_sigma=0.9, win_sigma=0.9)
     be = GpuDeqBackend(d, h, max_batch=1, max_seq_len=1)
     be.upload_weights(W)
