@@ -112,6 +112,7 @@ struct aideen_ctx {
   cudaStream_t est = nullptr;
   cudaEvent_t ev_e0 = nullptr, ev_emb = nullptr;
   bool emb_pending = false, emb_csr_ready = false;
+  bool emb_done = false;  // this step's embedding update is already queued
   bool lm_reduced = false;  // this step's LM-head gradients were already summed over ranks
   // data-parallel train step with Adam: the core gradients are reduce-scattered
   // in two buckets (the attention-branch block as soon as its chain ends,
@@ -862,6 +863,7 @@ int pipeline_chunks(aideen_ctx *ctx, const aideen_run *r) {
 int lm_sampled_prepare(aideen_ctx *ctx, int N, const aideen_step_args *a);
 int lm_sampled_rows(aideen_ctx *ctx, long r0, int R, bool first);
 int lm_sampled_finish(aideen_ctx *ctx, int N, const aideen_step_args *a);
+int run_emb_update(aideen_ctx *ctx, int N, const aideen_step_args *a);
 
 int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aideen_stats *stats) {
   const aideen_run *r = &a->run;
@@ -1039,6 +1041,14 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   if (sampled) {
     CHK(lm_sampled_finish(ctx, N, a));
     tl_mark(ctx, "lm_fin", st);
+    // dL/dpooled is final here and nothing later in the step reads the
+    // embedding: on one GPU its row update runs on the embedding stream beside
+    // the adjoint and the gradient chains (the same result as running it last;
+    // with a communicator its gradient all-gather stays at the step's end)
+    if (a->emb_update == 1 && ctx->emb_csr_ready && !(ctx->comm && ctx->nranks > 1)) {
+      CHK(run_emb_update(ctx, N, a));
+      ctx->emb_done = true;
+    }
     AdjointArgs aa{};
     aa.N = N; aa.h = h; aa.d = d; aa.iters = a->adj_iters; aa.anderson_m = a->anderson_m;
     aa.beta = r->damping;
@@ -1847,6 +1857,7 @@ int aideen_forward_tokens(aideen_ctx *ctx, const aideen_run *run, const int32_t 
   const int N = run->batch * run->seq_len;
   CHK(copy_in_rows(ctx, ctx->b.tokens, tokens, run->batch, run->seq_len, 1, 1, where));
   CU(join_emb(ctx));
+  ctx->emb_done = false;
   KL(launch_embed(ctx->b.tokens, ctx->b.emb, ctx->b.S_in, N, ctx->cfg.d_model, ctx->cfg.vocab, ctx->stream));
   return run_forward(ctx, run, stats);
 }
@@ -1989,6 +2000,7 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
   CHK(copy_in_rows(ctx, ctx->b.targets, targets, a->run.batch, a->run.seq_len, 1, 1, where));
   if (a->emb_update > 2) return set_err(ctx, AIDEEN_E_INVALID, "emb_update must be 0, 1 or 2");
   CU(join_emb(ctx));
+  ctx->emb_done = false;
   KL(launch_embed(ctx->b.tokens, ctx->b.emb, ctx->b.S_in, N, ctx->cfg.d_model, ctx->cfg.vocab, ctx->stream));
   if (a->emb_update) CHK(emb_csr_early(ctx, N));
   const bool sampled = a->lm_samples > 0;
@@ -2025,7 +2037,8 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
     KL(launch_spectral(ctx->b.W, ctx->cfg.d_model, ctx->cfg.h_slots, ctx->P, 12, 0.10f, 0.30f, 0.70f,
                        0.50f, 0.50f, ctx->b.sigmas, ctx->stream));
   // the reference updates the embedding rows last (trainer.rs:3282-3300)
-  if (a->emb_update) CHK(run_emb_update(ctx, N, a));
+  if (a->emb_update && !ctx->emb_done) CHK(run_emb_update(ctx, N, a));
+  ctx->emb_done = false;
   if (loss_out) {
     CU(cudaMemcpyAsync(loss_out, ctx->b.scal + 1, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
     CHK(sync_and_check(ctx));
