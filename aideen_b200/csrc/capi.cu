@@ -675,9 +675,11 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   size_t boff[2], blen[2];
   grad_buckets(ctx, boff, blen);
   if (ctx->shard_step) CHK(reduce_scatter_bucket(ctx, boff[0], blen[0]));  // beside the FPM backward
+  if (ctx->shard_step) tl_mark(ctx, "rs0", st);
   if (fork_fpm) CU(cudaStreamWaitEvent(st, ctx->ev_fdone, 0));
   else if (ctx->last_run.fpm) CHK(run_fpm_backward(ctx));
   if (ctx->shard_step) CHK(reduce_scatter_bucket(ctx, boff[1], blen[1]));
+  if (ctx->shard_step) tl_mark(ctx, "rs1", st);
   return AIDEEN_OK;
 }
 
@@ -1042,10 +1044,11 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
     CHK(lm_sampled_finish(ctx, N, a));
     tl_mark(ctx, "lm_fin", st);
     // dL/dpooled is final here and nothing later in the step reads the
-    // embedding: on one GPU its row update runs on the embedding stream beside
-    // the adjoint and the gradient chains (the same result as running it last;
-    // with a communicator its gradient all-gather stays at the step's end)
-    if (a->emb_update == 1 && ctx->emb_csr_ready && !(ctx->comm && ctx->nranks > 1)) {
+    // embedding: its row update runs on the embedding stream beside the
+    // adjoint and the gradient chains (the same result as running it last).
+    // With a communicator the gradient rows' all-gather is issued here on the
+    // context stream, in the same place of every rank's collective sequence.
+    if (a->emb_update == 1 && ctx->emb_csr_ready) {
       CHK(run_emb_update(ctx, N, a));
       ctx->emb_done = true;
     }
@@ -1288,6 +1291,7 @@ int run_emb_update(aideen_ctx *ctx, int N, const aideen_step_args *a) {
                                              ncclGetErrorString(nr != ncclSuccess ? nr : n2));
     tok = b.tok_all;
     grad = b.grad_all;
+    tl_mark(ctx, "emb_ag", st);
   }
   const aideen_update *u = &a->update;
   const double t = u->step < 1 ? 1.0 : (double)u->step;
@@ -1412,6 +1416,7 @@ int run_update_sharded(aideen_ctx *ctx, const aideen_update *u, float bc1, float
     if (rem) KL(launch_adam(b.W + orr, b.G + orr, b.M1 + orr, b.M2 + orr, rem, u->lr, u->beta1, u->beta2, u->eps,
                             bc1, bc2, u->grad_scale, st));
   }
+  tl_mark(ctx, "adam_sh", st);
   ncclResult_t r = ncclGroupStart();
   for (int k = 0; k < 2 && r == ncclSuccess; ++k) {
     const size_t cnt = blen[k] / n;
@@ -2032,13 +2037,14 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
   if (sampled) up.update_lm_head = 0;  // its rows were updated inside the LM stage
   CHK(run_update(ctx, &up));
   tl_mark(ctx, "update", ctx->stream);
-  tl_flush(ctx);
   if (a->renorm)
     KL(launch_spectral(ctx->b.W, ctx->cfg.d_model, ctx->cfg.h_slots, ctx->P, 12, 0.10f, 0.30f, 0.70f,
                        0.50f, 0.50f, ctx->b.sigmas, ctx->stream));
   // the reference updates the embedding rows last (trainer.rs:3282-3300)
   if (a->emb_update && !ctx->emb_done) CHK(run_emb_update(ctx, N, a));
   ctx->emb_done = false;
+  tl_mark(ctx, "end", ctx->stream);
+  tl_flush(ctx);
   if (loss_out) {
     CU(cudaMemcpyAsync(loss_out, ctx->b.scal + 1, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
     CHK(sync_and_check(ctx));
