@@ -209,6 +209,7 @@ int prof_class(const char *expr, int phase) {
   if (phase >= 0) return phase;
   if (strstr(expr, "launch_picard")) return AIDEEN_PROF_PICARD;
   if (strstr(expr, "launch_adjoint")) return AIDEEN_PROF_ADJOINT;
+  if (strstr(expr, "source_grad")) return AIDEEN_PROF_OTHER;
   if (strstr(expr, "gemm_any") || strstr(expr, "gemm_split")) return AIDEEN_PROF_GEMM;
   if (strstr(expr, "launch_softmax_ce")) return AIDEEN_PROF_LM_SOFTMAX;
   if (strstr(expr, "launch_adam") || strstr(expr, "launch_clipped_sgd")) return AIDEEN_PROF_OPTIMIZER;
@@ -662,10 +663,13 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
                                (long)d * d, ctx->signal_scale))));
     tl_mark(ctx, "wg_in", st);
     if (want_ds) {
-      for (int s = 0; s < h; ++s)
-        KL(gemm_any(ctx, gemm(N, d, d, 1, b.dsig + (size_t)s * d, (long)h * d, 0, false,
-                         W + L.win + (size_t)s * d * d, d, 0, true, b.dS, d, 0, ctx->signal_scale,
-                         s == 0 ? 0.f : 1.f)));
+      // the source gradient (not a weight gradient: profiled with "other")
+      auto source_grad_gemm = [&](int s) {
+        return gemm_any(ctx, gemm(N, d, d, 1, b.dsig + (size_t)s * d, (long)h * d, 0, false,
+                                  W + L.win + (size_t)s * d * d, d, 0, true, b.dS, d, 0, ctx->signal_scale,
+                                  s == 0 ? 0.f : 1.f));
+      };
+      for (int s = 0; s < h; ++s) KL(source_grad_gemm(s));
     }
   } else if (want_ds) {
     CU(cudaMemsetAsync(b.dS, 0, (size_t)N * d * sizeof(float), st));
@@ -2186,7 +2190,7 @@ int aideen_gemm_selftest(aideen_ctx *ctx, int M, int N, int K, int batch, int tr
     cudaEvent_t e0, e1, e2;
     cudaEventCreate(&e0); cudaEventCreate(&e1); cudaEventCreate(&e2);
     float *wsp = nullptr;
-    const size_t wsn = 16 * (size_t)M * N;
+    const size_t wsn = 16 * (size_t)M * N * batch;  // up to 16 split-K partials of every output
     cudaMalloc(&wsp, wsn * 4);
     run_tc(wsp, wsn);  // warm-up
     const int reps = 10;

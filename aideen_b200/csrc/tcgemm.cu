@@ -426,6 +426,7 @@ int env_int(const char *name) {
 }
 struct TcTuning {
   int bn = env_int("AIDEEN_TC_BN"), stages = env_int("AIDEEN_TC_STAGES"), cps = env_int("AIDEEN_TC_CPS");
+  int slots = env_int("AIDEEN_TC_SLOTS");
 };
 const TcTuning &tuning() {
   static TcTuning t;
@@ -580,10 +581,15 @@ cudaError_t tc_gemm(const GemmArgs &g0, cudaStream_t st, float *ws, size_t ws_fl
   const int kblocks = (g.K + BK - 1) / BK;
   int zdim = g.batch;
   // Split K when the output (all batches) has too few tiles to fill the GPU
-  // and K is long enough; the partial sums go to the workspace.
+  // and K is long enough: as many splits as fit whole in one wave of the
+  // resident CTA slots (two per SM when half the shared memory still holds a
+  // 2-stage ring, else one); a second, partial wave would run alone.
+  const int sb = split3 ? 2 * (BM + BN) * BK * 4 : (BM + BN) * BK * 4;
   int splits = 1, chunk = kblocks;
   if (ws && tiles < 148 && kblocks >= 64) {
-    splits = (2 * 148 + tiles - 1) / tiles;
+    const int slots = t.slots > 0 ? t.slots : 148 * (ring_stages(sb, 2, MAX_STAGES, BN) >= 2 ? 2 : 1);
+    splits = slots / tiles;
+    if (splits < 1) splits = 1;
     if (splits > 16) splits = 16;
     if (splits > kblocks / 4) splits = kblocks / 4;
     chunk = (kblocks + splits - 1) / splits;

@@ -131,7 +131,8 @@ uint64_t aideen_launch_count(const aideen_ctx *ctx);
  * context's stream; aideen_profile_read synchronises and returns cumulative
  * milliseconds and launch counts per class. */
 /* Classes: Picard solve; adjoint; GEMMs of the slot projections and weight
- * gradients; every kernel of the LM head (its GEMMs, softmax, reductions, and
+ * gradients (the per-slot source-gradient GEMMs of aideen_weight_grads count
+ * as "everything else"); every kernel of the LM head (its GEMMs, softmax, reductions, and
  * the sampled head's Adam step); the optimizer sweeps; the FPM backward (its
  * GEMMs included); everything else. */
 enum { AIDEEN_PROF_PICARD = 0, AIDEEN_PROF_ADJOINT = 1, AIDEEN_PROF_GEMM = 2,
