@@ -795,13 +795,16 @@ void tl_mark(aideen_ctx *ctx, const char *name, cudaStream_t s) {
 void tl_flush(aideen_ctx *ctx) {
   if (ctx->tl.empty()) return;
   cudaDeviceSynchronize();
-  fprintf(stderr, "[timeline]");
+  std::string line = "[timeline r" + std::to_string(ctx->rank) + "]";
   for (auto &m : ctx->tl) {
     float ms = 0.f;
     cudaEventElapsedTime(&ms, ctx->tl.front().second, m.second);
-    fprintf(stderr, " %s=%.3f", m.first.c_str(), ms);
+    char buf[96];
+    snprintf(buf, sizeof(buf), " %s=%.3f", m.first.c_str(), ms);
+    line += buf;
   }
-  fprintf(stderr, "\n");
+  line += "\n";
+  fputs(line.c_str(), stderr);  // one write per step, whole lines from every rank
   for (auto &m : ctx->tl) cudaEventDestroy(m.second);
   ctx->tl.clear();
 }
