@@ -130,10 +130,23 @@ def cpu_baseline(n_seq: int = B_PER_GPU):
     t0 = time.perf_counter()
     O.train_step(emb[tok], tg, W, lm, cfg, lm_samples=LM_SAMPLES, tokens=tok, emb=emb)
     dt = time.perf_counter() - t0
-    return {"value": n_seq * T / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{n_seq} sequence(s) x {T} tokens of the d512/h8/vocab50257 reference step "
-                      f"(sampled LM head, embedding update; numpy float64 oracle, BLAS threads = host "
-                      f"cores), {dt:.1f} s"}
+    out = {"value": n_seq * T / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+           "sample": f"{n_seq} sequence(s) x {T} tokens of the d512/h8/vocab50257 reference step "
+                     f"(sampled LM head, embedding update; numpy float64 oracle, BLAS threads = host "
+                     f"cores), {dt:.1f} s"}
+    # the same restatement on one host thread (BLAS limited to 1), 2 sequences
+    try:
+        from threadpoolctl import threadpool_limits
+        n1 = min(2, n_seq)
+        with threadpool_limits(limits=1):
+            t0 = time.perf_counter()
+            O.train_step(emb[tok[:n1]], tg[:n1], W, lm, cfg, lm_samples=LM_SAMPLES, tokens=tok[:n1], emb=emb)
+            d1 = time.perf_counter() - t0
+        out["single_thread"] = {"value": n1 * T / d1, "unit": "tokens/s", "cores": 1,
+                                "sample": f"{n1} sequence(s) x {T} tokens, {d1:.1f} s"}
+    except ImportError:
+        pass
+    return out
 
 
 def adjoint_micro(torch, hbm, src, device):
