@@ -124,6 +124,7 @@ struct aideen_ctx {
   int sm_budget = 0;      // SMs the GEMM / softmax / adjoint launches may use (0: all)
   // optional stage timeline of the pipelined step (AIDEEN_PIPE_TIMELINE=1, stderr)
   std::vector<std::pair<std::string, cudaEvent_t>> tl;
+  std::vector<double> tl_host;  // host microseconds at each mark
   ncclComm_t comm = nullptr;
   int nranks = 1, rank = 0;
   std::string err;
@@ -790,20 +791,30 @@ void tl_mark(aideen_ctx *ctx, const char *name, cudaStream_t s) {
   cudaEventCreate(&e);
   cudaEventRecord(e, s);
   ctx->tl.push_back({name, e});
+  ctx->tl_host.push_back(
+      std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now().time_since_epoch()).count());
 }
 
 void tl_flush(aideen_ctx *ctx) {
   if (ctx->tl.empty()) return;
   cudaDeviceSynchronize();
   std::string line = "[timeline r" + std::to_string(ctx->rank) + "]";
-  for (auto &m : ctx->tl) {
+  for (size_t i = 0; i < ctx->tl.size(); ++i) {
     float ms = 0.f;
-    cudaEventElapsedTime(&ms, ctx->tl.front().second, m.second);
+    cudaEventElapsedTime(&ms, ctx->tl.front().second, ctx->tl[i].second);
     char buf[96];
-    snprintf(buf, sizeof(buf), " %s=%.3f", m.first.c_str(), ms);
+    snprintf(buf, sizeof(buf), " %s=%.3f", ctx->tl[i].first.c_str(), ms);
+    line += buf;
+  }
+  // the host clock at each mark (ms after the first): when the host enqueued it
+  line += " | host:";
+  for (size_t i = 0; i < ctx->tl_host.size(); ++i) {
+    char buf[96];
+    snprintf(buf, sizeof(buf), " %s=%.3f", ctx->tl[i].first.c_str(), (ctx->tl_host[i] - ctx->tl_host[0]) / 1e3);
     line += buf;
   }
   line += "\n";
+  ctx->tl_host.clear();
   fputs(line.c_str(), stderr);  // one write per step, whole lines from every rank
   for (auto &m : ctx->tl) cudaEventDestroy(m.second);
   ctx->tl.clear();
@@ -873,6 +884,7 @@ int lm_sampled_prepare(aideen_ctx *ctx, int N, const aideen_step_args *a);
 int lm_sampled_rows(aideen_ctx *ctx, long r0, int R, bool first);
 int lm_sampled_finish(aideen_ctx *ctx, int N, const aideen_step_args *a);
 int run_emb_update(aideen_ctx *ctx, int N, const aideen_step_args *a);
+int emb_csr_early(aideen_ctx *ctx, int N);
 
 int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aideen_stats *stats) {
   const aideen_run *r = &a->run;
@@ -897,17 +909,14 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   CU(cudaEventRecord(ctx->ev_prep, st));
   ctx->last_run = *r;
   ctx->N = N;
-  if (sampled) CHK(lm_sampled_prepare(ctx, N, a));
-  else KL(launch_count_active(b.targets, N, b.scal, st));
   int nsm = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   const int budget = nsm - B * h;
-  CU(cudaMemsetAsync(b.colpart, 0, (size_t)nsm * Vp * sizeof(float), st));
-  // the last chunk's consumers run after the solve has finished: all SMs
-  const bool cap_last = getenv("AIDEEN_PIPELINE_CAP_LAST") != nullptr;
   // Picard chunks on the high-priority stream: chunk 0 after its rows' prep,
-  // the others after the remaining rows' prep
+  // the others after the remaining rows' prep.  Chunk 0 is enqueued before
+  // the host spends time on anything the solve does not wait for (when the
+  // host has just synchronised, the GPU otherwise idles meanwhile).
   CU(cudaStreamWaitEvent(ctx->pic, ctx->ev_prep, 0));
   PicardArgs p = picard_args(ctx, r);
   p.t0 = 0;
@@ -916,6 +925,12 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   CU(launch_picard(p, r->fpm != 0, ctx->pic));
   CU(cudaEventRecord(ctx->ev_pic[0], ctx->pic));
   tl_mark(ctx, "pic0", ctx->pic);
+  if (a->emb_update) CHK(emb_csr_early(ctx, N));
+  if (sampled) CHK(lm_sampled_prepare(ctx, N, a));
+  else KL(launch_count_active(b.targets, N, b.scal, st));
+  CU(cudaMemsetAsync(b.colpart, 0, (size_t)nsm * Vp * sizeof(float), st));
+  // the last chunk's consumers run after the solve has finished: all SMs
+  const bool cap_last = getenv("AIDEEN_PIPELINE_CAP_LAST") != nullptr;
   CHK(run_forward_prep_rows(ctx, r, R0, N - R0));
   tl_mark(ctx, "prep", st);
   CU(cudaEventRecord(ctx->ev_prep, st));
@@ -1869,6 +1884,7 @@ int aideen_forward_tokens(aideen_ctx *ctx, const aideen_run *run, const int32_t 
   const int N = run->batch * run->seq_len;
   CHK(copy_in_rows(ctx, ctx->b.tokens, tokens, run->batch, run->seq_len, 1, 1, where));
   CU(join_emb(ctx));
+  tl_mark(ctx, "entry", ctx->stream);
   ctx->emb_done = false;
   KL(launch_embed(ctx->b.tokens, ctx->b.emb, ctx->b.S_in, N, ctx->cfg.d_model, ctx->cfg.vocab, ctx->stream));
   return run_forward(ctx, run, stats);
@@ -2012,11 +2028,13 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
   CHK(copy_in_rows(ctx, ctx->b.targets, targets, a->run.batch, a->run.seq_len, 1, 1, where));
   if (a->emb_update > 2) return set_err(ctx, AIDEEN_E_INVALID, "emb_update must be 0, 1 or 2");
   CU(join_emb(ctx));
+  tl_mark(ctx, "entry", ctx->stream);
   ctx->emb_done = false;
   KL(launch_embed(ctx->b.tokens, ctx->b.emb, ctx->b.S_in, N, ctx->cfg.d_model, ctx->cfg.vocab, ctx->stream));
-  if (a->emb_update) CHK(emb_csr_early(ctx, N));
   const bool sampled = a->lm_samples > 0;
   const int nch = pipeline_chunks(ctx, &a->run);
+  // (the pipelined step builds the embedding CSR after its first solve launch)
+  if (a->emb_update && nch <= 1) CHK(emb_csr_early(ctx, N));
   if (nch > 1) {
     CHK(run_step_pipelined(ctx, a, nch, stats));
   } else {
