@@ -113,6 +113,11 @@ struct aideen_ctx {
   cudaEvent_t ev_e0 = nullptr, ev_emb = nullptr;
   bool emb_pending = false, emb_csr_ready = false;
   bool emb_done = false;  // this step's embedding update is already queued
+  // The Adam moments are zero wherever the gradient always is (the columns
+  // 32..d-1 of W_q/W_k/W_v and the rows 32..d-1 of W_o, which the 32-wide
+  // heads never read): the update may skip those entries (Adam leaves an
+  // entry with zero gradient and zero moments exactly unchanged).
+  bool adam_dead_zero = true;
   bool lm_reduced = false;  // this step's LM-head gradients were already summed over ranks
   // data-parallel train step with Adam: the core gradients are reduce-scattered
   // in two buckets (the attention-branch block as soon as its chain ends,
@@ -1478,8 +1483,36 @@ int run_update(aideen_ctx *ctx, const aideen_update *u) {
     const double t = u->step < 1 ? 1.0 : (double)u->step;
     const float bc1 = (float)(1.0 - std::pow((double)u->beta1, t));
     const float bc2 = (float)(1.0 - std::pow((double)u->beta2, t));
-    KL(launch_adam(b.W, b.G, b.M1, b.M2, ctx->W_len, u->lr, u->beta1, u->beta2, u->eps, bc1, bc2,
-                   u->grad_scale, st));
+    if (ctx->adam_dead_zero && !getenv("AIDEEN_ADAM_FULL")) {
+      // only the entries a gradient can reach: ~1/2.7 of the parameters
+      const Layout &L = ctx->P;
+      const size_t d = ctx->cfg.d_model, h = ctx->cfg.h_slots;
+      AdamSegs sg{};
+      auto add = [&](size_t off, size_t rows, size_t row_len, size_t stride) {
+        sg.off[sg.n] = off;
+        sg.rows[sg.n] = (int)rows;
+        sg.row4[sg.n] = (int)(row_len / 4);
+        sg.stride[sg.n] = (long)stride;
+        sg.start4[sg.n + 1] = sg.start4[sg.n] + rows * (row_len / 4);
+        ++sg.n;
+      };
+      const size_t tail = ctx->W_len - L.win, tail4 = tail / 4 * 4;
+      add(L.wq, h * d, kHeadDim, d);                  // W_q: columns 0..31 of every row
+      add(L.q_bias, 1, L.wk - L.q_bias, 0);           // q bias (and alignment padding)
+      add(L.wk, h * d, kHeadDim, d);
+      add(L.k_bias, 1, L.wv - L.k_bias, 0);
+      add(L.wv, h * d, kHeadDim, d);
+      add(L.wo, h, (size_t)kHeadDim * d, d * d);      // W_o: rows 0..31 of every slot
+      add(L.win, 1, tail4, 0);                        // W_in and every later tensor
+      KL(launch_adam_segs(b.W, b.G, b.M1, b.M2, sg, u->lr, u->beta1, u->beta2, u->eps, bc1, bc2, u->grad_scale,
+                          st));
+      if (tail4 < tail)
+        KL(launch_adam(b.W + L.win + tail4, b.G + L.win + tail4, b.M1 + L.win + tail4, b.M2 + L.win + tail4,
+                       tail - tail4, u->lr, u->beta1, u->beta2, u->eps, bc1, bc2, u->grad_scale, st));
+    } else {
+      KL(launch_adam(b.W, b.G, b.M1, b.M2, ctx->W_len, u->lr, u->beta1, u->beta2, u->eps, bc1, bc2,
+                     u->grad_scale, st));
+    }
     if (u->update_lm_head && ctx->lm_ready) CHK(run_lm_update(ctx, u, bc1, bc2));
   } else if (u->rule == AIDEEN_RULE_CLIPPED_SGD) {
     KL(launch_clipped_sgd(b.W, b.G, ctx->W_len, ctx->P.hist, u->lr, u->weight_decay, u->grad_scale, st));
@@ -1787,6 +1820,24 @@ int aideen_upload_adam(aideen_ctx *ctx, const float *m_core, const float *v_core
   if (!ctx) return AIDEEN_E_INVALID;
   if ((m_core || v_core) && n_core != ctx->Lx.total) return set_err(ctx, AIDEEN_E_INVALID, "bad moment length");
   CU(join_side(ctx));
+  {
+    // moments that are non-zero where no gradient reaches keep the full Adam sweep
+    const Layout &L = ctx->Lx;
+    const size_t d = ctx->cfg.d_model, h = ctx->cfg.h_slots;
+    auto dead_zero = [&](const float *m) {
+      if (!m) return true;
+      for (size_t blk : {L.wq, L.wk, L.wv})
+        for (size_t r = 0; r < h * d; ++r)
+          for (size_t c = kHeadDim; c < d; ++c)
+            if (m[blk + r * d + c] != 0.f) return false;
+      for (size_t s = 0; s < h; ++s)
+        for (size_t i = (size_t)kHeadDim * d; i < d * d; ++i)
+          if (m[L.wo + s * d * d + i] != 0.f) return false;
+      return true;
+    };
+    const bool ok = dead_zero(m_core) && dead_zero(v_core);
+    ctx->adam_dead_zero = (m_core && v_core) ? ok : (ctx->adam_dead_zero && ok);
+  }
   for (int i = 0; i < 2; ++i) {
     const float *src = i ? v_core : m_core;
     if (!src) continue;
@@ -1857,6 +1908,7 @@ int aideen_reset_state(aideen_ctx *ctx) {
 int aideen_reset_optimizer(aideen_ctx *ctx) {
   if (!ctx) return AIDEEN_E_INVALID;
   CU(join_side(ctx));
+  ctx->adam_dead_zero = true;
   CU(cudaMemsetAsync(ctx->b.M1, 0, ctx->W_len * 4, ctx->stream));
   CU(cudaMemsetAsync(ctx->b.M2, 0, ctx->W_len * 4, ctx->stream));
   if (ctx->lm_len) {

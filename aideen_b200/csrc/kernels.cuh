@@ -150,6 +150,16 @@ cudaError_t launch_add_rowbias(float *dst, const float *x, const float *bias, si
                                cudaStream_t st);
 
 // optimizer / renorm
+// Strided segments of a parameter vector (float offsets, rows of row4
+// float4s, `stride` floats apart; start4 = prefix sums of rows * row4).
+struct AdamSegs {
+  unsigned long long off[8], start4[9];
+  long stride[8];
+  int rows[8], row4[8];
+  int n;
+};
+cudaError_t launch_adam_segs(float *w, const float *g, float *m1, float *m2, const AdamSegs &sg, float lr,
+                             float b1, float b2, float eps, float bc1, float bc2, float gs, cudaStream_t st);
 cudaError_t launch_adam(float *w, const float *g, float *m1, float *m2, size_t n, float lr,
                         float b1, float b2, float eps, float bc1, float bc2, float gs,
                         cudaStream_t st);

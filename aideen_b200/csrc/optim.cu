@@ -67,6 +67,41 @@ __global__ void adam_kernel(float *__restrict__ w, const float *__restrict__ g, 
   }
 }
 
+static int sweep_blocks(size_t n4) {
+  size_t b = (n4 + 255) / 256;
+  if (b > 148 * 8) b = 148 * 8;
+  return b < 1 ? 1 : (int)b;
+}
+
+// Adam over a list of strided segments (rows of row4 float4s, `stride` floats
+// apart): the same arithmetic as adam_kernel on exactly the listed entries.
+__global__ void adam_segs_kernel(float *__restrict__ w, const float *__restrict__ g, float *__restrict__ m1,
+                                 float *__restrict__ m2, AdamSegs sg, float lr, float b1, float b2, float eps,
+                                 float bc1, float bc2, float gs) {
+  const unsigned long long total = sg.start4[sg.n];
+  const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
+  const float4 *g4 = reinterpret_cast<const float4 *>(g);
+  const float4 *a4 = reinterpret_cast<const float4 *>(m1);
+  const float4 *b4 = reinterpret_cast<const float4 *>(m2);
+  const float4 *w4 = reinterpret_cast<const float4 *>(w);
+  for (unsigned long long i = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x; i < total; i += stride) {
+    int k = 0;
+    while (k + 1 < sg.n && i >= sg.start4[k + 1]) ++k;
+    const unsigned long long li = i - sg.start4[k];
+    const unsigned long long r = li / (unsigned)sg.row4[k], c = li - r * (unsigned)sg.row4[k];
+    const size_t q = (sg.off[k] + r * (unsigned long long)sg.stride[k]) / 4 + c;  // float4 index
+    adam4(w, g, m1, m2, q, gs * __ldcs(g4 + q), __ldcs(a4 + q), __ldcs(b4 + q), w4[q], lr, b1, b2, eps, bc1, bc2);
+  }
+}
+
+cudaError_t launch_adam_segs(float *w, const float *g, float *m1, float *m2, const AdamSegs &sg, float lr,
+                             float b1, float b2, float eps, float bc1, float bc2, float gs, cudaStream_t st) {
+  if (sg.n <= 0 || sg.start4[sg.n] == 0) return cudaSuccess;
+  adam_segs_kernel<<<sweep_blocks(sg.start4[sg.n]), 256, 0, st>>>(w, g, m1, m2, sg, lr, b1, b2, eps, bc1, bc2,
+                                                                   gs);
+  return cudaGetLastError();
+}
+
 __global__ void clipped_sgd_kernel(float *__restrict__ w, const float *__restrict__ g, size_t n,
                                    size_t main_len, float lr, float wd, float gs) {
   const size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -77,11 +112,6 @@ __global__ void clipped_sgd_kernel(float *__restrict__ w, const float *__restric
   }
 }
 
-static int sweep_blocks(size_t n4) {
-  size_t b = (n4 + 255) / 256;
-  if (b > 148 * 8) b = 148 * 8;
-  return b < 1 ? 1 : (int)b;
-}
 
 cudaError_t launch_adam(float *w, const float *g, float *m1, float *m2, size_t n, float lr, float b1,
                         float b2, float eps, float bc1, float bc2, float gs, cudaStream_t st) {

@@ -231,6 +231,46 @@ def test_train_step_api_matches_oracle():
     be.close()
 
 
+def test_adam_skips_only_entries_no_gradient_reaches(monkeypatch):
+    """The update that sweeps only the entries a gradient can reach (W_q/W_k/W_v
+    columns 0..31, W_o rows 0..31, everything else whole) leaves weights and
+    moments bitwise equal to the full sweep, over three steps; moments uploaded
+    with non-zero entries there switch it back to the full sweep."""
+    d, h, B, T, V = 128, 4, 2, 8, 50
+    rng = np.random.default_rng(3)
+    tok = rng.integers(0, V, (B, T)).astype(np.int32)
+    tg = rng.integers(0, V, (B, T)).astype(np.int32)
+    out = []
+    for full in (False, True):
+        if full:
+            monkeypatch.setenv("AIDEEN_ADAM_FULL", "1")
+        else:
+            monkeypatch.delenv("AIDEEN_ADAM_FULL", raising=False)
+        W, be, S, rc, cfg = _setup(dict(d=d, h=h, B=B, T=T, fpm=True), vocab=V)
+        be.upload_lm_head(*init_lm_head(d, V))
+        be.upload_embedding(init_embedding(d, V))
+        for k in range(3):
+            be.train_step(tok, tg, B, T, rc, adj_iters=12, lr=1e-3, step=k + 1)
+        mc, vc, _, _ = be.read_adam()
+        out.append((be.read_weights(), mc, vc))
+        be.close()
+    for a, b in zip(out[0], out[1]):
+        assert np.array_equal(a, b)
+    # non-zero moments where no gradient reaches: the full sweep again
+    monkeypatch.delenv("AIDEEN_ADAM_FULL", raising=False)
+    W, be, S, rc, cfg = _setup(dict(d=d, h=h, B=B, T=T, fpm=True), vocab=V)
+    be.upload_lm_head(*init_lm_head(d, V))
+    be.upload_embedding(init_embedding(d, V))
+    L = be.layout
+    m = np.zeros(L.total, np.float32)
+    m[L.wq + d - 1] = 1e-3                        # row 0, column d-1 of slot 0's W_q
+    be.upload_adam(m, np.full(L.total, 1e-6, np.float32))
+    w0 = be.read_weights()
+    be.train_step(tok, tg, B, T, rc, adj_iters=12, lr=1e-3, step=2)
+    assert be.read_weights()[L.wq + d - 1] != w0[L.wq + d - 1]
+    be.close()
+
+
 def test_rejects_sizes_beyond_caps():
     be = GpuDeqBackend(128, 2, max_batch=1, max_seq_len=4)
     be.upload_weights(init_all_weights(128, 2))
