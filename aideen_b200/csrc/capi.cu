@@ -111,6 +111,8 @@ struct aideen_ctx {
   // start, the row Adam once dL/dpooled exists; the next gather joins it
   cudaStream_t est = nullptr;
   cudaEvent_t ev_e0 = nullptr, ev_emb = nullptr;
+  cudaEvent_t ev_gz0 = nullptr, ev_gz = nullptr;  // gradient buffer zeroed on the embedding stream
+  bool g_zeroed = false;                           // ... for this step's weight gradients
   bool emb_pending = false, emb_csr_ready = false;
   bool emb_done = false;  // this step's embedding update is already queued
   // The Adam moments are zero wherever the gradient always is (the columns
@@ -575,7 +577,12 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   float *G = b.G;
   const bool sc = ctx->last_run.slot_coord != 0;
   const int H32 = h * kHeadDim;
-  CU(cudaMemsetAsync(G, 0, ctx->W_len * sizeof(float), st));
+  if (ctx->g_zeroed) {
+    CU(cudaStreamWaitEvent(st, ctx->ev_gz, 0));
+    ctx->g_zeroed = false;
+  } else {
+    CU(cudaMemsetAsync(G, 0, ctx->W_len * sizeof(float), st));
+  }
   // The FPM backward writes only its own gradient segments: without
   // profiling it runs on its own stream (and split-K workspace) beside the
   // attention-branch gradients below.
@@ -931,6 +938,15 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   CU(cudaEventRecord(ctx->ev_pic[0], ctx->pic));
   tl_mark(ctx, "pic0", ctx->pic);
   if (a->emb_update) CHK(emb_csr_early(ctx, N));
+  // the gradient buffer is zeroed beside the solve instead of at the start of
+  // the weight gradients (stream order: after the previous step's update)
+  if (ctx->est && !ctx->prof) {
+    CU(cudaEventRecord(ctx->ev_gz0, st));
+    CU(cudaStreamWaitEvent(ctx->est, ctx->ev_gz0, 0));
+    CU(cudaMemsetAsync(b.G, 0, ctx->W_len * sizeof(float), ctx->est));
+    CU(cudaEventRecord(ctx->ev_gz, ctx->est));
+    ctx->g_zeroed = true;
+  }
   if (sampled) CHK(lm_sampled_prepare(ctx, N, a));
   else KL(launch_count_active(b.targets, N, b.scal, st));
   CU(cudaMemsetAsync(b.colpart, 0, (size_t)nsm * Vp * sizeof(float), st));
@@ -1616,6 +1632,8 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_emb, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_da, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_dqkv, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_gz0, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_gz, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_adone, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_adj, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_lmg, cudaEventDisableTiming);
@@ -1678,6 +1696,8 @@ void aideen_destroy(aideen_ctx *ctx) {
   if (ctx->hK) cudaFreeHost(ctx->hK);
   if (ctx->ev_K) cudaEventDestroy(ctx->ev_K);
   if (ctx->ev_e0) cudaEventDestroy(ctx->ev_e0);
+  if (ctx->ev_gz0) cudaEventDestroy(ctx->ev_gz0);
+  if (ctx->ev_gz) cudaEventDestroy(ctx->ev_gz);
   if (ctx->ev_emb) cudaEventDestroy(ctx->ev_emb);
   if (ctx->ev_da) cudaEventDestroy(ctx->ev_da);
   if (ctx->ev_dqkv) cudaEventDestroy(ctx->ev_dqkv);
@@ -2069,6 +2089,11 @@ int aideen_renormalize_spectral(aideen_ctx *ctx, uint32_t n_iters, float attn, f
 int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t *tokens,
                       const int32_t *targets, int where, float *loss_out, aideen_stats *stats) {
   if (!ctx || !a) return AIDEEN_E_INVALID;
+  // the early-zeroed gradient buffer belongs to this call only (also when it fails)
+  struct GzGuard {
+    aideen_ctx *c;
+    ~GzGuard() { c->g_zeroed = false; }
+  } gz_guard{ctx};
   CHK(check_run(ctx, &a->run));
   if (!ctx->emb_ready || !ctx->lm_ready)
     return set_err(ctx, AIDEEN_E_INVALID, "train step needs the embedding and the LM head");
