@@ -407,6 +407,11 @@ cudaError_t launch_adjoint(const AdjointArgs &a0, cudaStream_t st, int *g) {
   }
 }
 
+unsigned int *adjoint_error_dev() {
+  void *p = nullptr;
+  return cudaGetSymbolAddress(&p, g_adjoint_error) == cudaSuccess ? static_cast<unsigned int *>(p) : nullptr;
+}
+
 cudaError_t adjoint_error_async(unsigned int *host_flag, cudaStream_t st) {
   cudaError_t e = cudaMemcpyFromSymbolAsync(host_flag, g_adjoint_error, sizeof(unsigned int), 0,
                                             cudaMemcpyDeviceToHost, st);

@@ -120,6 +120,10 @@ struct aideen_ctx {
   // heads never read): the update may skip those entries (Adam leaves an
   // entry with zero gradient and zero moments exactly unchanged).
   bool adam_dead_zero = true;
+  // pinned mailbox of the synchronising reads: [0] adjoint error word,
+  // [1] Picard error word, [2] loss; device addresses of the two words
+  uint32_t *hbox = nullptr;
+  unsigned int *d_adj_err = nullptr, *d_pic_err = nullptr;
   bool lm_reduced = false;  // this step's LM-head gradients were already summed over ranks
   // data-parallel train step with Adam: the core gradients are reduce-scattered
   // in two buckets (the attention-branch block as soon as its chain ends,
@@ -184,9 +188,22 @@ int set_err(aideen_ctx *c, int code, const std::string &msg) {
 // on the same device.
 int sync_and_check(aideen_ctx *ctx) {
   unsigned int adj = 0, pic = 0;
-  cudaError_t e = adjoint_error_async(&adj, ctx->stream);
-  if (e == cudaSuccess) e = picard_error_async(&pic, ctx->stream);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  cudaError_t e = cudaSuccess;
+  if (ctx->hbox && ctx->d_adj_err && ctx->d_pic_err) {
+    // both words into pinned memory and cleared on the stream, one wait
+    cudaStream_t st = ctx->stream;
+    e = cudaMemcpyAsync(&ctx->hbox[0], ctx->d_adj_err, 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&ctx->hbox[1], ctx->d_pic_err, 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ctx->d_adj_err, 0, 4, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ctx->d_pic_err, 0, 4, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    adj = ctx->hbox[0];
+    pic = ctx->hbox[1];
+  } else {
+    e = adjoint_error_async(&adj, ctx->stream);
+    if (e == cudaSuccess) e = picard_error_async(&pic, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  }
   if (e != cudaSuccess) return set_err(ctx, AIDEEN_E_CUDA, std::string("sync: ") + cudaGetErrorString(e));
   if (adj) return set_err(ctx, AIDEEN_E_TIMEOUT, "adjoint: a bounded stage wait ran out (its outputs are invalid)");
   if (pic) return set_err(ctx, AIDEEN_E_TIMEOUT, "Picard memory-row exchange: a bounded wait ran out");
@@ -512,8 +529,14 @@ int run_lm_head(aideen_ctx *ctx, int N, float *loss_out) {
   KL(launch_rmsnorm_bwd(b.dy, b.pooled, b.lrms, glm, b.dl_dh, b.ggp, N, d, st));
   KL(launch_colsum(b.ggp, N, d, d, b.Glm + ctx->lm_g, d, 0, false, st));
   if (loss_out) {
-    CU(cudaMemcpyAsync(loss_out, b.scal + 1, sizeof(float), cudaMemcpyDeviceToHost, st));
-    CU(cudaStreamSynchronize(st));
+    if (ctx->hbox) {
+      CU(cudaMemcpyAsync(&ctx->hbox[2], b.scal + 1, sizeof(float), cudaMemcpyDeviceToHost, st));
+      CU(cudaStreamSynchronize(st));
+      memcpy(loss_out, &ctx->hbox[2], sizeof(float));
+    } else {
+      CU(cudaMemcpyAsync(loss_out, b.scal + 1, sizeof(float), cudaMemcpyDeviceToHost, st));
+      CU(cudaStreamSynchronize(st));
+    }
   }
   return AIDEEN_OK;
 }
@@ -1632,6 +1655,9 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_emb, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_da, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_dqkv, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaMallocHost((void **)&ctx->hbox, 4 * sizeof(uint32_t));
+  ctx->d_adj_err = adjoint_error_dev();
+  ctx->d_pic_err = picard_error_dev();
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_gz0, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_gz, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_adone, cudaEventDisableTiming);
@@ -1694,6 +1720,7 @@ void aideen_destroy(aideen_ctx *ctx) {
   if (ctx->ast) { cudaStreamSynchronize(ctx->ast); cudaStreamDestroy(ctx->ast); }
   if (ctx->est) cudaStreamDestroy(ctx->est);
   if (ctx->hK) cudaFreeHost(ctx->hK);
+  if (ctx->hbox) cudaFreeHost(ctx->hbox);
   if (ctx->ev_K) cudaEventDestroy(ctx->ev_K);
   if (ctx->ev_e0) cudaEventDestroy(ctx->ev_e0);
   if (ctx->ev_gz0) cudaEventDestroy(ctx->ev_gz0);
@@ -2148,8 +2175,12 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
   tl_mark(ctx, "end", ctx->stream);
   tl_flush(ctx);
   if (loss_out) {
-    CU(cudaMemcpyAsync(loss_out, ctx->b.scal + 1, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+    // through the pinned mailbox: one asynchronous copy, one wait (in
+    // sync_and_check) instead of a blocking pageable copy
+    float *dst = ctx->hbox ? reinterpret_cast<float *>(&ctx->hbox[2]) : loss_out;
+    CU(cudaMemcpyAsync(dst, ctx->b.scal + 1, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
     CHK(sync_and_check(ctx));
+    if (ctx->hbox) memcpy(loss_out, dst, sizeof(float));
   }
   return AIDEEN_OK;
 }

@@ -1054,6 +1054,11 @@ cudaError_t launch_attn_scale(const AttnArgs &a, int rows, cudaStream_t st) {
 
 // Reads (and clears) the flag a Picard launch sets when a bounded inbox wait
 // gave up; ordered on `st` after the solve.
+unsigned int *picard_error_dev() {
+  void *p = nullptr;
+  return cudaGetSymbolAddress(&p, g_picard_error) == cudaSuccess ? static_cast<unsigned int *>(p) : nullptr;
+}
+
 cudaError_t picard_error_async(unsigned int *host_flag, cudaStream_t st) {
   static const unsigned int zero = 0;
   cudaError_t e = cudaMemcpyFromSymbolAsync(host_flag, g_picard_error, sizeof(unsigned int), 0,

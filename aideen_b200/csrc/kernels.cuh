@@ -49,6 +49,7 @@ cudaError_t tc_gemm_split(const GemmArgs &g, const float *A_lo, const float *B_l
                           const float *row_bias = nullptr, float2 *row_stats = nullptr);
 unsigned int tc_split_error(bool reset);
 cudaError_t picard_error_async(unsigned int *host_flag, cudaStream_t st);
+unsigned int *picard_error_dev();   // device address of the Picard error word
 // x -> (hi, lo) with hi exact in tf32 and lo = x - hi (n % 4 == 0).
 cudaError_t launch_split_hilo(const float *x, float *hi, float *lo, size_t n, cudaStream_t st);
 // out[c][r] = split(x[r][c]): transposed hi / lo copies (row stride ldt).
@@ -99,6 +100,7 @@ struct AdjointArgs {
 };
 // Reads and clears the adjoint's timeout flag (stream-ordered copy into host_flag).
 cudaError_t adjoint_error_async(unsigned int *host_flag, cudaStream_t st);
+unsigned int *adjoint_error_dev();  // device address of the adjoint error word
 // Dynamic shared memory of one adjoint CTA for these inputs (h*d floats per
 // staged tensor, double-buffered; plus the Anderson ring where it is used).
 size_t adjoint_smem_bytes(int h, int d, bool has_b, bool has_rs, bool has_tok, int anderson_m);
