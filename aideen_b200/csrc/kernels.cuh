@@ -29,7 +29,8 @@ struct GemmArgs {
   int col_group; long group_stride;
 };
 cudaError_t gemm_f32(const GemmArgs &g, cudaStream_t s);
-// Same contract on tcgen05 tensor cores (3xTF32, fp32-accurate); no abias.
+// Same contract on tcgen05 tensor cores (3xTF32, fp32-accurate, or single TF32
+// with g.tf32); no abias; g.col_group needs the split-K workspace.
 bool tc_gemm_supported(const GemmArgs &g);
 // ws: optional workspace for split-K partial sums (ws_floats capacity).
 cudaError_t tc_gemm(const GemmArgs &g, cudaStream_t s, float *ws = nullptr, size_t ws_floats = 0);
