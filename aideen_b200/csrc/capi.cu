@@ -60,6 +60,7 @@ struct DevBufs {
   float *ws = nullptr;     // split-K partial sums of the tensor-core GEMM
   float *ws2 = nullptr;    // the same for GEMMs on the FPM-backward stream
   float *ws3 = nullptr;    // and for the attention-gradient side stream
+  float *ws4 = nullptr;    // and for the FPM backward's second stream
   // FPM backward (allocated on first use): [N][h][d] unless noted
   float *fc = nullptr, *frp = nullptr, *fdl = nullptr, *fminner = nullptr, *fdm = nullptr,
         *fgpre = nullptr;
@@ -98,6 +99,8 @@ struct aideen_ctx {
   cudaEvent_t ev_prep = nullptr, ev_pic[kMaxChunks] = {};
   // FPM backward stream: runs beside the attention-branch weight gradients
   cudaStream_t fst = nullptr;
+  cudaStream_t fst2 = nullptr;  // the FPM backward's W_out gradient beside its other GEMMs
+  cudaEvent_t ev_f0 = nullptr, ev_f2 = nullptr;
   cudaEvent_t ev_g0 = nullptr, ev_fdone = nullptr;
   // last pipeline chunk: dW_lm and the LM-head bias / gain sums on their own
   // stream beside the weight gradients; joined before the gradients are used
@@ -802,6 +805,27 @@ int run_fpm_backward(aideen_ctx *ctx, bool prepare_only) {
   KL(launch_fpm_carry(a, st));
   KL(launch_fpm_chunks(a, st));
   tl_mark(ctx, "f_chunks", st);
+  // W_out[r][c] = sum_{n,s} dm[n][s][r] m_inner[n][s][c]: needs only the
+  // replay's outputs, so it runs on a second stream (own split-K workspace)
+  // beside the finalize and the rank-32 gradient GEMMs below
+  const bool wout_side = ctx->fst2 && st == ctx->fst && !ctx->prof;
+  auto wout_gemm = [&] {
+    return gemm_any(ctx, tf32(gemm(d, d, N * h, 1, b.fdm, d, 0, true, b.fminner, d, 0, false, G + L.wout, d, 0)));
+  };
+  if (wout_side) {
+    CU(cudaEventRecord(ctx->ev_f0, st));
+    CU(cudaStreamWaitEvent(ctx->fst2, ctx->ev_f0, 0));
+    float *keep_ws = b.ws;
+    ctx->stream = ctx->fst2;
+    b.ws = b.ws4;
+    const cudaError_t we = wout_gemm();
+    ctx->stream = st;
+    b.ws = keep_ws;
+    ctx->launches++;
+    ctx->launches += tc_take_extra_launches();
+    CU(we);
+    CU(cudaEventRecord(ctx->ev_f2, ctx->fst2));
+  }
   KL(launch_fpm_finalize(a, G, st));
   tl_mark(ctx, "f_fin", st);
   // W_retain_down[s][r][k] = sum_n up[n][s][r] g_pre[n][s][k]
@@ -814,8 +838,8 @@ int run_fpm_backward(aideen_ctx *ctx, bool prepare_only) {
   // W_retain_up[s][j][r] = sum_n c[n][s][j] dup[n][s][r]
   KL(gemm_any(ctx, tf32(gemm(d, R, N, h, b.fc, hd, d, true, b.fdup, HR, R, false, G + L.w_retain_up, R,
                              (long)d * R))));
-  // W_out[r][c] = sum_{n,s} dm[n][s][r] m_inner[n][s][c]
-  KL(gemm_any(ctx, tf32(gemm(d, d, N * h, 1, b.fdm, d, 0, true, b.fminner, d, 0, false, G + L.wout, d, 0))));
+  if (wout_side) CU(cudaStreamWaitEvent(st, ctx->ev_f2, 0));
+  else KL(wout_gemm());
   return AIDEEN_OK;
 }
 
@@ -1618,7 +1642,7 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   A(&b.yThi, d * ((N + 3) / 4 * 4)); A(&b.yTlo, d * ((N + 3) / 4 * 4)); A(&b.ggp, N * d); A(&b.lrms, N); A(&b.loss_rows, N);
   A(&b.scal, 4); A(&b.stage, ctx->Lx.total);
   ctx->ws_floats = 16 * N * d;  // up to 16 splits of an [N][d] output
-  A(&b.ws, ctx->ws_floats); A(&b.ws2, ctx->ws_floats); A(&b.ws3, ctx->ws_floats); A(&b.stats, 4); A(&b.sigmas, 5 * h + 2);
+  A(&b.ws, ctx->ws_floats); A(&b.ws2, ctx->ws_floats); A(&b.ws3, ctx->ws_floats); A(&b.ws4, ctx->ws_floats); A(&b.stats, 4); A(&b.sigmas, 5 * h + 2);
   if (V) {
     A(&b.lmp, ctx->lm_len); A(&b.Glm, ctx->lm_len); A(&b.Mlm1, ctx->lm_len); A(&b.Mlm2, ctx->lm_len);
     A(&b.logits, N * (size_t)ctx->Vp); A(&b.emb, V * d);
@@ -1645,7 +1669,10 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
     int lo = 0, hi = 0;
     cudaDeviceGetStreamPriorityRange(&lo, &hi);
     e = cudaStreamCreateWithPriority(&ctx->fst, cudaStreamNonBlocking, hi);
+    if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&ctx->fst2, cudaStreamNonBlocking, hi);
   }
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_f0, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_f2, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_g0, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_fdone, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->lmst, cudaStreamNonBlocking);
@@ -1703,7 +1730,7 @@ void aideen_destroy(aideen_ctx *ctx) {
                   b.Mlm2, b.y, b.lrms, b.logits, b.dy, b.ggp, b.loss_rows, b.scal, b.emb, b.stats,
                   b.sigmas, b.stage, b.ws, b.fc, b.frp, b.fdl, b.fminner, b.fdm, b.fgpre, b.fup,
                   b.fkw, b.fdup, b.fA, b.fU, b.fgin, b.fcarry, b.fpart, b.fpart_bw, b.fprm, b.src,
-                  b.dlog_lo, b.yhi, b.ylo, b.yThi, b.yTlo, b.whi, b.wlo, b.colpart, b.perm, b.ws2, b.ws3, b.rowstats,
+                  b.dlog_lo, b.yhi, b.ylo, b.yThi, b.yTlo, b.whi, b.wlo, b.colpart, b.perm, b.ws2, b.ws3, b.ws4, b.rowstats,
                   b.lS, b.lWS, b.ints, b.lerr, b.tg_all, b.tok_all, b.grad_all, b.cuniq, b.coff, b.cpos,
                   b.Me1, b.Me2};
   for (void *p : ptrs)
@@ -1714,6 +1741,9 @@ void aideen_destroy(aideen_ctx *ctx) {
   if (ctx->pic) { cudaStreamSynchronize(ctx->pic); cudaStreamDestroy(ctx->pic); }
   if (ctx->ev_prep) cudaEventDestroy(ctx->ev_prep);
   if (ctx->fst) { cudaStreamSynchronize(ctx->fst); cudaStreamDestroy(ctx->fst); }
+  if (ctx->fst2) { cudaStreamSynchronize(ctx->fst2); cudaStreamDestroy(ctx->fst2); }
+  if (ctx->ev_f0) cudaEventDestroy(ctx->ev_f0);
+  if (ctx->ev_f2) cudaEventDestroy(ctx->ev_f2);
   if (ctx->ev_g0) cudaEventDestroy(ctx->ev_g0);
   if (ctx->ev_fdone) cudaEventDestroy(ctx->ev_fdone);
   if (ctx->lmst) { cudaStreamSynchronize(ctx->lmst); cudaStreamDestroy(ctx->lmst); }
