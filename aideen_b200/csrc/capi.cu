@@ -109,6 +109,7 @@ struct aideen_ctx {
   // attention-branch weight gradients: the GEMMs off the dsig chain run on ast
   cudaStream_t ast = nullptr;
   cudaEvent_t ev_da = nullptr, ev_dqkv = nullptr, ev_adone = nullptr;
+  cudaEvent_t ev_dsig = nullptr;
   bool lmg_pending = false;
   // embedding update on its own stream (one GPU): the token CSR from the step's
   // start, the row Adam once dL/dpooled exists; the next gather joins it
@@ -659,6 +660,10 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
     if (fork_attn) {
       CU(cudaEventRecord(ctx->ev_da, st));
       CU(cudaStreamWaitEvent(ctx->ast, ctx->ev_da, 0));
+      // dsig's initial value needs only g_pre and attn_bwd_scale's dRc: on
+      // the side stream beside dn and the softmax backward
+      KL(launch_dsig_init(a, b.dsig, N * h, 1, sst));
+      CU(cudaEventRecord(ctx->ev_dsig, sst));
     }
     // gW_o[s][c][o] = sum_n n[n][s][c] da[n][s][o]
     KL(on_side([&] {
@@ -685,13 +690,14 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
     }));
     KL(launch_colsum(b.dQ, N, H32, H96, G + L.q_bias, kHeadDim, d, false, sst, 96));
     KL(launch_colsum(b.dK, N, H32, H96, G + L.k_bias, kHeadDim, d, false, sst, 96));
-    if (fork_attn) CU(cudaEventRecord(ctx->ev_adone, ctx->ast));
     tl_mark(ctx, "wg_qkv", st);
-    KL(launch_dsig_init(a, b.dsig, N * h, 1, st));
+    if (fork_attn) CU(cudaStreamWaitEvent(st, ctx->ev_dsig, 0));
+    else KL(launch_dsig_init(a, b.dsig, N * h, 1, st));
     // dsrc[n][s][j] += sum_c d{Q|K|V}[n][s][c] Wcat[s][j][c], one GEMM of depth 96
     KL(gemm_any(ctx, gemm(N, d, 96, h, b.dqkv, H96, 96, false, b.Wcat, 96, (long)d * 96, true, b.dsig,
                           (long)h * d, d, 1.f, 1.f)));
     tl_mark(ctx, "dsrc", st);
+    if (fork_attn) CU(cudaEventRecord(ctx->ev_adone, ctx->ast));
     KL(launch_colsum(b.dsig, N, h * d, (long)h * d, G + L.slot_anchor, h * d, 0, false, st));
   } else {
     KL(launch_dsig_init(a, b.dsig, N * h, 0, st));
@@ -1682,6 +1688,7 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_emb, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_da, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_dqkv, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_dsig, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaMallocHost((void **)&ctx->hbox, 4 * sizeof(uint32_t));
   ctx->d_adj_err = adjoint_error_dev();
   ctx->d_pic_err = picard_error_dev();
@@ -1758,6 +1765,7 @@ void aideen_destroy(aideen_ctx *ctx) {
   if (ctx->ev_emb) cudaEventDestroy(ctx->ev_emb);
   if (ctx->ev_da) cudaEventDestroy(ctx->ev_da);
   if (ctx->ev_dqkv) cudaEventDestroy(ctx->ev_dqkv);
+  if (ctx->ev_dsig) cudaEventDestroy(ctx->ev_dsig);
   if (ctx->ev_adone) cudaEventDestroy(ctx->ev_adone);
   if (ctx->ev_adj) cudaEventDestroy(ctx->ev_adj);
   if (ctx->ev_lmg) cudaEventDestroy(ctx->ev_lmg);
