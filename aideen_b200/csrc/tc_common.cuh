@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <unordered_map>
+
 namespace aideen {
 namespace {
 
@@ -133,18 +135,50 @@ inline EncodeFn encode_fn() {
 
 
 // 3-D fp32 tensor map: dim0 contiguous (extent e0), dim1 stride s1 elements,
-// dim2 stride s2 elements (0: packed after dim1).
+// dim2 stride s2 elements (0: packed after dim1).  Encoded maps are kept per
+// host thread, keyed by every argument: a training step encodes the same ~80
+// maps every time, and a map depends only on the address and the shape.
+struct MapKey {
+  const void *base;
+  uint64_t e0, e1, e2, s1, s2;
+  uint32_t box0, box1, sw;
+  bool operator==(const MapKey &o) const {
+    return base == o.base && e0 == o.e0 && e1 == o.e1 && e2 == o.e2 && s1 == o.s1 && s2 == o.s2 &&
+           box0 == o.box0 && box1 == o.box1 && sw == o.sw;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey &k) const {
+    uint64_t h = reinterpret_cast<uint64_t>(k.base);
+    for (uint64_t v : {k.e0, k.e1, k.e2, k.s1, k.s2, (uint64_t)k.box0 << 32 | k.box1, (uint64_t)k.sw})
+      h = (h ^ v) * 0x100000001B3ull;
+    return (size_t)h;
+  }
+};
+
 inline bool make_map_sw(CUtensorMap *m, const float *base, uint64_t e0, uint64_t e1, uint64_t e2,
                         uint64_t s1, uint64_t s2, uint32_t box0, uint32_t box1, CUtensorMapSwizzle sw) {
+  static thread_local std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  const MapKey key{base, e0, e1, e2, s1, s2, box0, box1, (uint32_t)sw};
+  const auto it = cache.find(key);
+  if (it != cache.end()) {
+    *m = it->second;
+    return true;
+  }
   EncodeFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[3] = {e0, e1, e2 ? e2 : 1};
   const cuuint64_t strides[2] = {s1 * 4, (s2 ? s2 : s1 * e1) * 4};
   const cuuint32_t box[3] = {box0, box1, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  const bool ok = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  if (ok) {
+    if (cache.size() > 4096) cache.clear();
+    cache.emplace(key, *m);
+  }
+  return ok;
 }
 
 }  // namespace aideen

@@ -405,16 +405,8 @@ __global__ void __launch_bounds__(TC_THREADS) tcgemm_kernel(const __grid_constan
 // 3-D fp32 map: dim0 contiguous (extent e0), dim1 stride s1 elements, dim2 stride s2.
 bool make_map(CUtensorMap *m, const float *base, uint64_t e0, uint64_t e1, uint64_t e2, uint64_t s1,
               uint64_t s2, uint32_t box0, uint32_t box1, bool kmajor) {
-  EncodeFn fn = encode_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[3] = {e0, e1, e2 ? e2 : 1};
-  const cuuint64_t strides[2] = {s1 * 4, (s2 ? s2 : s1 * e1) * 4};
-  const cuuint32_t box[3] = {box0, box1, 1};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE,
-            kmajor ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return make_map_sw(m, base, e0, e1, e2, s1, s2, box0, box1,
+                     kmajor ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
 }
 
 // Tuning knobs read once from the environment (0 = the built-in choice):
