@@ -116,24 +116,27 @@ def make_tokens(rank: int, B: int):
     return np.ascontiguousarray(ids[:, :-1]), np.ascontiguousarray(ids[:, 1:])
 
 
-def cpu_baseline(n_seq: int = B_PER_GPU):
-    """Oracle (CPU restatement of the reference math) on `n_seq` sequences of the
-    bench workload at the full model size (n_seq = B_PER_GPU: one GPU's whole step)."""
+def cpu_baseline(n_seq: int = B_PER_GPU, t_len: int = T, single_thread: bool = True):
+    """Oracle (CPU restatement of the reference math) on `n_seq` sequences of
+    `t_len` tokens of the bench workload at the full model size (n_seq =
+    B_PER_GPU, t_len = T: one GPU's whole step)."""
     from oracle import deq_oracle as O
     from aideen_b200.weights import init_all_weights, init_embedding, init_lm_head
     W = init_all_weights(D, H, seed=0)
     lm = init_lm_head(D, VOCAB)
     emb = init_embedding(D, VOCAB)
     tok, tg = make_tokens(0, B_PER_GPU)
-    tok, tg = tok[:n_seq], tg[:n_seq]
+    tok, tg = np.ascontiguousarray(tok[:n_seq, :t_len]), np.ascontiguousarray(tg[:n_seq, :t_len])
     cfg = O.Cfg(d=D, h=H, fpm=True, max_iters=MAX_ITERS, adj_iters=ADJ_ITERS, anderson_m=ANDERSON_M)
     t0 = time.perf_counter()
     O.train_step(emb[tok], tg, W, lm, cfg, lm_samples=LM_SAMPLES, tokens=tok, emb=emb)
     dt = time.perf_counter() - t0
-    out = {"value": n_seq * T / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-           "sample": f"{n_seq} sequence(s) x {T} tokens of the d512/h8/vocab50257 reference step "
+    out = {"value": n_seq * t_len / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+           "sample": f"{n_seq} sequence(s) x {t_len} tokens of the d512/h8/vocab50257 reference step "
                      f"(sampled LM head, embedding update; numpy float64 oracle, BLAS threads = host "
                      f"cores), {dt:.1f} s"}
+    if not single_thread:
+        return out
     # the same restatement on one host thread (BLAS limited to 1), 2 sequences
     try:
         from threadpoolctl import threadpool_limits
@@ -308,21 +311,46 @@ def configs4_step(device, steps=2, warmup=1):
             "tokens_per_s": B * Tl / (ms / 1e3), "ms_per_step": ms, "steps": steps}
 
 
+def arm_config(world, dense_lm=False):
+    """The workload both arms report (the reference arm times a bounded sample
+    of it, described in its cpu_baseline.sample)."""
+    return {"workload": "DEQ+FPM train step (BASELINE configs[2] per-GPU shard), the reference's "
+                        + ("dense-CE variant" if dense_lm else
+                           "full step: sampled-softmax LM head (num_samples 512) with its Adam "
+                           "step, embedding-row Adam update"),
+            "d_r": D, "h_slots": H, "ctx": T, "batch_per_gpu": B_PER_GPU,
+            "global_batch": B_PER_GPU * world, "vocab": VOCAB, "lm_samples": 0 if dense_lm else LM_SAMPLES,
+            "max_iters": MAX_ITERS, "adj_iters": ADJ_ITERS, "anderson_m": ANDERSON_M,
+            "parallelism": f"dp{world}", "l2": "256 MB buffer written before every step, inside the timed region"}
+
+
 def run_reference(args, rank, world):
+    """The reference arm: the CPU restatement on the host cores, each step the
+    same bounded sample of the workload (2 of the 8 sequences, full length:
+    shorter samples would be dominated by the step's fixed costs, the sampled
+    vocabulary and the embedding update).  As many of the requested steps are
+    timed as fit in about 150 s (at least one), so the run stays short for any
+    --steps; the line says how many were timed."""
     if rank != 0:
         return
+    n_seq = 2
+    t0 = time.perf_counter()
+    for _ in range(min(args.warmup, 1)):
+        cpu_baseline(n_seq, T, single_thread=False)
+    t_step = (time.perf_counter() - t0) if args.warmup > 0 else 0.0
+    n_timed = args.steps if t_step <= 0 else max(1, min(args.steps, int(150.0 / t_step)))
     times = []
-    for i in range(args.warmup + args.steps):
-        cb = cpu_baseline(2)
-        if i >= args.warmup:
-            times.append(cb["value"])
+    for _ in range(n_timed):
+        cb = cpu_baseline(n_seq, T, single_thread=False)
+        times.append(cb["value"])
     v = float(np.mean(times))
     cb["value"] = v
+    cb["sample"] += (f"; {n_timed} of the {args.steps} requested steps timed (mean), the rest skipped "
+                     f"to keep the run near 150 s")
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "dtype": "f64", "data": "synthetic (Zipf(1.1) ids, seeded)",
-            "config": {"workload": "DEQ+FPM train step, CPU restatement, bounded sample",
-                       "d_r": D, "h_slots": H, "ctx": T, "vocab": VOCAB},
+            "config": arm_config(world),
             "cpu_baseline": cb,
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -530,14 +558,7 @@ def main():
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (Zipf(1.1) token ids, seeded; random-init weights)",
-                "config": {"workload": "DEQ+FPM train step (BASELINE configs[2] per-GPU shard), the reference's "
-                                       + ("dense-CE variant" if args.dense_lm else
-                                          "full step: sampled-softmax LM head (num_samples 512) with its Adam "
-                                          "step, embedding-row Adam update"),
-                           "d_r": D, "h_slots": H, "ctx": T, "batch_per_gpu": B_PER_GPU,
-                           "global_batch": B_PER_GPU * world, "vocab": VOCAB, "lm_samples": lm_samples,
-                           "max_iters": MAX_ITERS, "adj_iters": ADJ_ITERS, "anderson_m": ANDERSON_M,
-                           "parallelism": f"dp{world}", "l2": "256 MB buffer written before every step, inside the timed region"},
+                "config": arm_config(world, args.dense_lm),
                 "e2e": {"value": e2e, "unit": "tokens/s",
                         "h2d_bytes_per_step": int(tok.nbytes + tg.nbytes), "d2h_bytes_per_step": 4},
                 "gpu_launches": int(launches),
