@@ -26,6 +26,13 @@ constexpr uint32_t kSpinLimit = 1u << 26;
 
 // Set when a bounded wait of the adjoint ran out (the rows of that CTA's
 // remaining tokens were not written); read and cleared by adjoint_error_async.
+// Anderson iterates in registers instead of the shared-memory ring (a tuning
+// switch read once per process).
+static bool adj_reg_hist() {
+  static const bool on = getenv("AIDEEN_ADJ_REG_HIST") != nullptr;
+  return on;
+}
+
 __device__ unsigned int g_adjoint_error;
 
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
@@ -383,7 +390,7 @@ static cudaError_t adjoint_dispatch_m(const AdjointArgs &a, cudaStream_t st, int
     case 4:
       // iterates in shared memory (two tokens per SM) while two CTAs' rings and
       // stages fit: 4 x h x d floats of ring per CTA
-      if (small && 4 * (size_t)a.h * a.d <= 16384 && !getenv("AIDEEN_ADJ_REG_HIST"))
+      if (small && 4 * (size_t)a.h * a.d <= 16384 && !adj_reg_hist())
         return adjoint_launch<F, 4, 256, 2, true>(a, st, g);
       return small ? adjoint_launch<F, 4, 256, 1>(a, st, g) : adjoint_launch<F, 4, 512, 1>(a, st, g);
     default: return cudaErrorInvalidValue;
@@ -423,7 +430,7 @@ cudaError_t adjoint_error_async(unsigned int *host_flag, cudaStream_t st) {
 size_t adjoint_smem_bytes(int h, int d, bool has_b, bool has_rs, bool has_tok, int anderson_m) {
   const size_t hd = (size_t)h * d;
   const size_t stage_f = hd * (1 + has_b + has_rs) + (has_tok ? (size_t)d : 0);
-  const bool hs = anderson_m == 4 && h <= 8 && 4 * hd <= 16384 && !getenv("AIDEEN_ADJ_REG_HIST");
+  const bool hs = anderson_m == 4 && h <= 8 && 4 * hd <= 16384 && !adj_reg_hist();
   return 128 + 192 * 4 + 2 * stage_f * 4 + (hs ? 4 * hd * 4 : 0);
 }
 

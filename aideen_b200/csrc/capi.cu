@@ -307,6 +307,8 @@ int copy_in_rows(aideen_ctx *ctx, void *dst, const void *src, int B, int T, int 
   return AIDEEN_OK;
 }
 
+bool no_sharded_update() { return getenv("AIDEEN_NO_SHARDED_UPDATE") != nullptr; }  // per step (tests toggle it)
+
 bool tf32_grads_enabled() {
   static const bool on = getenv("AIDEEN_GRAD_3XTF32") == nullptr;
   return on;
@@ -892,7 +894,8 @@ void tl_flush(aideen_ctx *ctx) {
 int chunk_bound(int j, int nch, int T) {
   int w[aideen_ctx::kMaxChunks] = {0};
   int tot = 0;
-  const char *e = getenv("AIDEEN_PIPELINE_WEIGHTS");
+  static const char *const weights = getenv("AIDEEN_PIPELINE_WEIGHTS");
+  const char *e = weights;
   for (int i = 0; i < nch; ++i) {
     int wi = i + 1;
     if (e && *e) {
@@ -921,7 +924,7 @@ int chunk_bound_aligned(int j, int nch, int T, int B) {
 // Token chunks of the training step for the pipelined schedule (0: run the
 // step sequentially).  Pipelining pays when the Picard solve leaves SMs idle.
 int pipeline_chunks(aideen_ctx *ctx, const aideen_run *r) {
-  if (ctx->prof || getenv("AIDEEN_NO_PIPELINE")) return 0;
+  if (ctx->prof || getenv("AIDEEN_NO_PIPELINE")) return 0;  // read per step (tests toggle it)
   int nsm = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
@@ -929,7 +932,8 @@ int pipeline_chunks(aideen_ctx *ctx, const aideen_run *r) {
   if (nsm - picard_ctas < 32) return 0;
   if (r->batch % 4 != 0) return 0;  // chunk row offsets must keep 16-byte alignment of y^T columns
   int nch = 3;
-  if (const char *e = getenv("AIDEEN_PIPELINE_CHUNKS")) nch = atoi(e);
+  static const char *const chunks = getenv("AIDEEN_PIPELINE_CHUNKS");
+  if (chunks) nch = atoi(chunks);
   if (nch > aideen_ctx::kMaxChunks) nch = aideen_ctx::kMaxChunks;
   if (nch < 2) return 0;
   for (int j = 0; j < nch; ++j)  // every chunk holds at least one token
@@ -1004,7 +1008,7 @@ int run_step_pipelined(aideen_ctx *ctx, const aideen_step_args *a, int nch, aide
   else KL(launch_count_active(b.targets, N, b.scal, st));
   CU(cudaMemsetAsync(b.colpart, 0, (size_t)nsm * Vp * sizeof(float), st));
   // the last chunk's consumers run after the solve has finished: all SMs
-  const bool cap_last = getenv("AIDEEN_PIPELINE_CAP_LAST") != nullptr;
+  static const bool cap_last = getenv("AIDEEN_PIPELINE_CAP_LAST") != nullptr;
   CHK(run_forward_prep_rows(ctx, r, R0, N - R0));
   tl_mark(ctx, "prep", st);
   CU(cudaEventRecord(ctx->ev_prep, st));
@@ -2189,7 +2193,7 @@ int aideen_train_step(aideen_ctx *ctx, const aideen_step_args *a, const int32_t 
   // data parallel with Adam: sharded update (no profiling: its per-class
   // timing assumes one stream)
   ctx->shard_step = a->update.allreduce && ctx->comm && ctx->nranks > 1 && a->update.rule == AIDEEN_RULE_ADAM &&
-                    !ctx->prof && !getenv("AIDEEN_NO_SHARDED_UPDATE");
+                    !ctx->prof && !no_sharded_update();
   const int wg = run_weight_grads(ctx, a->emb_update == 2);
   if (wg != AIDEEN_OK) {
     ctx->shard_step = false;

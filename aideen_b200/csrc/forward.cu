@@ -1099,8 +1099,10 @@ static cudaError_t picard_launch(const PicardArgs &a, cudaStream_t st) {
   // memory (one 256-thread block per SM owns all 512 columns); with h <= 8 a
   // fourth one moves there too, and the freed shared memory holds the inbox of
   // the pushed memory rows / read keys
-  p.use_tmem = (a.d == 512 && p.n_resident == 3 && !getenv("AIDEEN_PICARD_NO_TMEM")) ? 1 : 0;
-  p.push = (p.use_tmem && a.h <= 8 && !getenv("AIDEEN_PICARD_NO_PUSH")) ? 1 : 0;
+  static const bool no_tmem = getenv("AIDEEN_PICARD_NO_TMEM") != nullptr;
+  static const bool no_push = getenv("AIDEEN_PICARD_NO_PUSH") != nullptr;
+  p.use_tmem = (a.d == 512 && p.n_resident == 3 && !no_tmem) ? 1 : 0;
+  p.push = (p.use_tmem && a.h <= 8 && !no_push) ? 1 : 0;
   if (p.push) {
     p.n_resident = 2;
     smem -= mat_bytes;
