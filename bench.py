@@ -152,6 +152,70 @@ def cpu_baseline(n_seq: int = B_PER_GPU, t_len: int = T, single_thread: bool = T
     return out
 
 
+def _guarded(fn):
+    """A host-side baseline that fails is recorded in the line, not fatal."""
+    try:
+        return fn()
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+
+
+def cpu_adjoint_baseline(n_tok_all: int = 16384, n_tok_one: int = 2048, iters: int = 20):
+    """configs[3]'s adjoint on the host: the C restatement (oracle/adjoint_c.c,
+    float32, gcc -O3 with AVX-512 / AVX2 clones, pthreads over (token, slot)
+    entries) on the whole workload (16384 tokens x 8 slots x 512, h*, branch and
+    per-slot RHS ~ N(0,1), 20 iterations, v and g_pre written) at every host
+    core, and on a 2048-token sample on one thread; GB/s by the same 16*E*d
+    accounting as the GPU entry."""
+    import ctypes as C
+    from oracle.build_c import load
+    lib = load()
+    rng = np.random.default_rng(0)
+    out = {}
+    for key, n_tok, threads in (("all_cores", n_tok_all, 0), ("single_thread", n_tok_one, 1)):
+        hs, br, rs = (rng.standard_normal((n_tok, H, D), dtype=np.float32) for _ in range(3))
+        ns = np.ones(D, np.float32)
+        v, g = np.empty_like(hs), np.empty_like(hs)
+        ptr = lambda a: a.ctypes.data_as(C.c_void_p)
+        v.fill(0.0)
+        g.fill(0.0)
+        args = (ptr(hs), ptr(br), ptr(rs), None, ptr(ns), n_tok, H, D, iters, C.c_float(0.85), ptr(v), ptr(g),
+                threads)
+        assert lib.oracle_adjoint_c(*args) == 0   # warm-up (thread start-up, caches)
+        t0 = time.perf_counter()
+        rc = lib.oracle_adjoint_c(ptr(hs), ptr(br), ptr(rs), None, ptr(ns), n_tok, H, D, iters, C.c_float(0.85),
+                                  ptr(v), ptr(g), threads)
+        dt = time.perf_counter() - t0
+        assert rc == 0
+        out[key] = {"value": 16 * n_tok * H * D / dt / 1e9, "unit": "GB/s",
+                    "cores": os.cpu_count() if threads == 0 else 1,
+                    "sample": f"{n_tok} tokens x {H} slots x {D}, {iters} iterations, {dt * 1e3:.1f} ms"}
+    r = dict(out["all_cores"])
+    r.update(kind="port", single_thread=out["single_thread"],
+             note="C restatement of the clean adjoint (oracle/adjoint_c.c), float32")
+    return r
+
+
+def cpu_weight_grad_baseline(n_tok: int = 2048):
+    """configs[3]'s weight-gradient GEMMs on the host: numpy float32 matmul (the
+    interpreter's BLAS, every host core) on n_tok tokens of the same shapes: per
+    slot the W_in gradient (d x N by N x d) and the four 32-wide head gradients
+    (d x N by N x 32).  TFLOP/s by the same algorithmic count."""
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal((H, D, n_tok), dtype=np.float32)   # per-slot operand, transposed
+    b = rng.standard_normal((H, n_tok, D), dtype=np.float32)
+    c = rng.standard_normal((H, n_tok, 4 * 32), dtype=np.float32)
+    np.matmul(a[:1], b[:1])  # BLAS start-up outside the timing
+    t0 = time.perf_counter()
+    np.matmul(a, b)
+    np.matmul(a, c)
+    dt = time.perf_counter() - t0
+    flops = H * (2 * n_tok * D * D + 4 * 2 * n_tok * D * 32)
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n_tok} tokens x {H} slots x {D} (1/{16384 // n_tok} of the workload), {dt * 1e3:.1f} ms",
+            "note": "numpy float32 matmul (BLAS) on the same GEMM shapes"}
+
+
 def adjoint_micro(torch, hbm, src, device):
     """isolated clean adjoint on a given fixed point, B*T = 16384
     tokens x 8 slots x d 512, h* and branch ~ N(0,1), per-slot RHS ~ N(0,1), exactly 20
@@ -199,7 +263,8 @@ def adjoint_micro(torch, hbm, src, device):
             # under ncu (805.3 MB read, 498.8 MB written)
             "traffic": 805.3e6 + 498.8e6,
             "note": "algorithmic bytes per the 16*E*d definition; the kernel also writes g_pre (E*d) and "
-                    "per-CTA NormScale partials, which the weight gradients read"}
+                    "per-CTA NormScale partials, which the weight gradients read",
+            "cpu_baseline": _guarded(cpu_adjoint_baseline)}
 
 
 def weight_grad_micro(torch, device):
@@ -239,7 +304,8 @@ def weight_grad_micro(torch, device):
             "algorithmic_flops": flops, "ms": ms, "achieved_tflops": ach, "tf32_peak": tf32,
             "peak_source": "half of " + tsrc, "tensor_util_of_tf32": ach / tf32,
             "note": "the weight-gradient GEMMs issue one tf32 MMA per product (TF32 rate is their "
-                    "ceiling); dn and dsrc, also in this class, issue three (3xTF32)"}
+                    "ceiling); dn and dsrc, also in this class, issue three (3xTF32)",
+            "cpu_baseline": _guarded(cpu_weight_grad_baseline)}
 
 
 def configs1_step(device, steps=20, warmup=3):

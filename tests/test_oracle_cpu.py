@@ -155,6 +155,33 @@ def test_cross_entropy_identity():
 
 
 # ---------------------------------------------------------------- adjoint
+@pytest.mark.parametrize("N,h,d,iters,tok,slot", [(5, 4, 128, 12, True, True), (3, 8, 512, 20, False, True),
+                                                   (2, 16, 1024, 7, True, False), (0, 8, 512, 4, True, True)])
+def test_c_adjoint_matches_numpy_oracle(N, h, d, iters, tok, slot):
+    """The compiled C restatement timed as the CPU baseline (oracle/adjoint_c.c,
+    float32) against the float64 numpy oracle, on several thread counts (the
+    entries split into contiguous ranges must not change a result)."""
+    import ctypes as C
+    from oracle.build_c import load
+    lib = load()
+    rng = np.random.default_rng(N * 131 + d)
+    hs, br, rs = (rng.standard_normal((N, h, d)).astype(np.float32) for _ in range(3))
+    rt = rng.standard_normal((N, d)).astype(np.float32) if tok else None
+    ns = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    ptr = lambda a: None if a is None else a.ctypes.data_as(C.c_void_p)
+    vr, gr, _, _ = O.adjoint(hs, br, rt, ns, O.Cfg(d=d, h=h, adj_iters=iters, damping=0.85),
+                             rhs_slot=rs if slot else None)
+    for threads in (1, 3, 0):
+        v, g = np.full_like(hs, np.nan), np.full_like(hs, np.nan)
+        assert lib.oracle_adjoint_c(ptr(hs), ptr(br), ptr(rs) if slot else None, ptr(rt), ptr(ns), N, h, d, iters,
+                                    C.c_float(0.85), ptr(v), ptr(g), threads) == 0
+        if N:
+            assert np.linalg.norm(v - vr) / np.linalg.norm(vr) < 1e-5
+            assert np.linalg.norm(g - gr) / np.linalg.norm(gr) < 1e-5
+    assert lib.oracle_adjoint_c(ptr(hs), ptr(br), None, None, ptr(ns), N, 0, d, iters, C.c_float(0.85),
+                                ptr(v), None, 1) == -1   # h = 0 refused
+
+
 def test_adjoint_converges_to_linear_solve():
     rng = np.random.default_rng(2)
     N, h, d = 3, 2, 16
