@@ -24,6 +24,8 @@ It restates, in float64 numpy, the reference's live GPU semantics:
 * temporal carrier (simple)  `aideen-backbone/src/fixed_point_memory_reasoning.rs:1455-1486`
 * sampled-softmax LM head    `aideen-backbone/src/shaders/lm_train.wgsl:79-395`, `gpu_lm_head.rs:213-281`
 * embedding-row Adam         `aideen-backbone/src/shaders/embedding_train.wgsl:100-147`
+* associative branch (upper h/2 slots, default flags; Cfg.assoc)
+                             `deq_slot_attn_unified_clean.wgsl:554-556, 1216-1563, 1970-1971, 2293-2948`
 
 Weight gradients are derived analytically (implicit-function theorem through
 the map the clean adjoint linearises); the reference's own stage-4 shaders
@@ -51,6 +53,12 @@ HOMEO_PLATEAU_TOL = 0.10      # FPM_HOMEO_PLATEAU_TOL
 FPM_ALPHA_H = 0.2
 FPM_GATE_BIAS = -1.5
 FPM_RESIDUAL_SCALE = 0.1
+# associative branch, default flags (deq_slot_attn_unified_clean.wgsl:79-96, deq_bridge.rs:176-350)
+ASSOC_WRITE_CAP = 0.95
+ASSOC_OCCUPIED_THRESHOLD = 1e-4
+ASSOC_USAGE_DECAY = 0.999
+ASSOC_TO_FPM_SCALE = 0.02
+ASSOC_SUPPRESS_COS = 0.85        # ENABLE_ASSOC_SUPPRESS_VALUE_SOURCE threshold (`:2755`)
 
 
 def es(spec, *ops):
@@ -98,7 +106,12 @@ class Offsets:
         self.w_q_mem = o; o += h * d * r
         self.w_k_mem = o; o += h * d * r
         self.b_read_mem = o; o += h
-        o += 3 * h * d * r + h + h * d + h   # associative block (kept off)
+        self.w_k_assoc = o; o += h * d * r    # associative block (`:232-237`)
+        self.w_v_assoc = o; o += h * d * r
+        self.w_q_assoc = o; o += h * d * r
+        self.alpha_assoc = o; o += h
+        self.w_event_assoc = o; o += h * d
+        self.b_event_assoc = o; o += h
         self.total = o
 
 
@@ -138,6 +151,7 @@ class View:
         self.Wqm = w[L.w_q_mem:L.w_q_mem + h * d * r].reshape(h, d, r)
         self.Wkm = w[L.w_k_mem:L.w_k_mem + h * d * r].reshape(h, d, r)
         self.bread = w[L.b_read_mem:L.b_read_mem + h]
+        self.alpha_assoc = w[L.alpha_assoc:L.alpha_assoc + h]
 
 
 @dataclass
@@ -155,6 +169,7 @@ class Cfg:
     adj_iters: int = 12
     anderson_m: int = 0            # adjoint Anderson depth (0 = off)
     fwd_anderson_m: int = 0        # forward Anderson depth (0 = plain Picard)
+    assoc: bool = False            # associative branch of the upper h/2 slots (needs fpm)
 
 
 def rms(x, axis=-1, eps=1e-6):
@@ -271,6 +286,67 @@ def fpm_write(h_star, sig_t, m_prev, V: View, Wx_diag):
     return retain * m_prev + (1.0 - retain) * base
 
 
+def _rms_floor(x):
+    """sqrt(mean(x^2) + 1e-6) floored at 1e-6 (the shader's max(rms, 1e-6))."""
+    return np.maximum(np.sqrt((x * x).mean(-1) + 1e-6), 1e-6)
+
+
+def assoc_read(bank_v, sig_t, V: View, cfg: Cfg):
+    """Associative read of one token, default flags (`deq_slot_attn_unified_clean.wgsl:1216-1563`):
+    one bank and a hard read, so the bank is selected whatever its address score, and the
+    read returns its value.  Injected into the memory context:
+    sigmoid(alpha_assoc[s]) * bank_v * |signal| * alpha_m / max(|bank_v|, 1e-3).
+    bank_v, sig_t: [B,h,d]; returns [B,h,d] for every slot (the caller keeps the upper half)."""
+    sig_norm = np.sqrt(np.maximum((sig_t * sig_t).sum(-1), 1e-6))
+    v_norm = np.sqrt(np.maximum((bank_v * bank_v).sum(-1), 1e-6))
+    alpha = 1.0 / (1.0 + np.exp(-V.alpha_assoc))[None, :]
+    scale = sig_norm * max(cfg.fpm_alpha_m, 0.001) / np.maximum(v_norm, 1e-6)
+    return (alpha * scale)[..., None] * bank_v
+
+
+def assoc_write(x_t, state, m, h_star, t):
+    """Associative write of one token, default flags (`:2293-2948`): returns the
+    memory after the consolidation, the unnormalised payload the stored signal is
+    replaced with, and updates `state` (bank value V, usage u, previous source P;
+    each [B,h,...]) in place.
+
+    value   = x / rms(x), renormalised by its own rms   (x = this token's S_in row)
+    payload = value + P / rms(P), then / rms(payload)    (ASSOC_REL_VALUE_MIX = 1)
+    mass    = [t > 0] * [bank empty: usage < 1e-4] * [cos(V, P / rms(P)) <= 0.85]
+    V <- (1 - mass) V + mass payload;  usage <- clamp(max(0.999 usage, mass), 0, 1)
+    m <- (1 - c) m + c h*/rms(h*),  c = 0.02 * min(1, 0.95) * mass  (no FPM write on
+         these slots, so the write-gate factor keeps its initial 1.0, `:1970`)
+    P <- value.
+    x_t: [B,d]; m, h_star: [B,h,d]."""
+    Vb, u, P = state["V"], state["u"], state["P"]
+    x = np.broadcast_to(np.asarray(x_t, np.float64)[:, None, :], P.shape)
+    val0 = x / _rms_floor(x)[..., None]
+    val = val0 / _rms_floor(val0)[..., None]
+    Pn = P / _rms_floor(P)[..., None]
+    pay_raw = val + Pn
+    pay = pay_raw / _rms_floor(pay_raw)[..., None]
+    u_c = np.clip(np.where(np.isfinite(u), u, 0.0), 0.0, 1.0)
+    empty = u_c < ASSOC_OCCUPIED_THRESHOLD
+    vv = (Vb * Vb).sum(-1)
+    pp = (Pn * Pn).sum(-1)
+    cos = (Vb * Pn).sum(-1) / np.sqrt(np.maximum(vv * pp, 1e-12))
+    cos = np.where(np.isfinite(cos), cos, -1.0)
+    allow = empty & ~(cos > ASSOC_SUPPRESS_COS)
+    mass = (1.0 if t > 0 else 0.0) * allow.astype(np.float64)
+    state["V"] = (1.0 - mass)[..., None] * Vb + mass[..., None] * pay
+    c = ASSOC_TO_FPM_SCALE * min(1.0, ASSOC_WRITE_CAP) * mass
+    hu = h_star / _rms_floor(h_star)[..., None]
+    m_new = (1.0 - c)[..., None] * m + c[..., None] * hu
+    state["u"] = np.clip(np.maximum(ASSOC_USAGE_DECAY * u_c, mass), 0.0, 1.0)
+    state["P"] = val
+    return m_new, pay_raw
+
+
+def assoc_state_zeros(B, h, d):
+    """The reset state (reset_state, gpu_deq.rs:3141-3160: AssocBuf and PrevHStarBuf zeroed)."""
+    return dict(V=np.zeros((B, h, d)), u=np.zeros((B, h)), P=np.zeros((B, h, d)))
+
+
 def temporal_step(m_prev, h_star, V: View):
     """The simple temporal carrier `temporal_step` (fixed_point_memory_reasoning.rs:1455-1486;
     GPU form hist_v2_temporal.wgsl:60-108): per slot,
@@ -310,10 +386,19 @@ class ForwardOut:
     mstate: np.ndarray        # [B,h,d]
     fpm_ctx: np.ndarray       # [B,T,h,d]
     attn_cache: dict = field(default_factory=dict)   # flattened [B*T, ...]
+    # the signal the adjoint's branch is built from: the projection, except on the
+    # associative slots, where the write replaced it with the payload (`:2497`)
+    branch_signal: np.ndarray = None
+    assoc_state: dict = None  # bank value V, usage u, previous source P after the chunk
 
 
-def forward(S_in, W, cfg: Cfg, mstate=None) -> ForwardOut:
-    """Forward DEQ solve over a [B,T,d] chunk (token carry on, `:900`)."""
+def forward(S_in, W, cfg: Cfg, mstate=None, assoc_state=None) -> ForwardOut:
+    """Forward DEQ solve over a [B,T,d] chunk (token carry on, `:900`).
+
+    With cfg.fpm and cfg.assoc the upper h/2 slots run the reference's default
+    associative branch instead of the FPM write (`:554-556, 1971`): `assoc_read`
+    at the memory read, `assoc_write` after the solve; `assoc_state` carries its
+    state across chunks (zeros: the reset state)."""
     d, h = cfg.d, cfg.h
     V = View(W, d, h)
     S = np.asarray(S_in, np.float64)
@@ -335,6 +420,13 @@ def forward(S_in, W, cfg: Cfg, mstate=None) -> ForwardOut:
     ctx_all = np.zeros((B, T, h, d))
     hcur = None
     am = cfg.fwd_anderson_m
+    assoc = cfg.fpm and cfg.assoc
+    upper = (np.arange(h) >= h // 2)[None, :, None]
+    ast = None
+    if assoc:
+        ast = assoc_state_zeros(B, h, d) if assoc_state is None else {
+            k: np.asarray(x, np.float64).copy() for k, x in assoc_state.items()}
+    branch_sig = signal.copy()
     for t in range(T):
         sig = signal[:, t]
         if t == 0:
@@ -351,6 +443,8 @@ def forward(S_in, W, cfg: Cfg, mstate=None) -> ForwardOut:
                 break
             if cfg.fpm and it == 1:
                 ctx_new = fpm_read(hcur, sig, keys, m, V, cfg)
+                if assoc:
+                    ctx_new = ctx_new + np.where(upper, assoc_read(ast["V"], sig, V, cfg), 0.0)
                 ctx = np.where(active[..., None], ctx_new, ctx)
             dep = sig + hcur + anchor + (A[:, t] if it == 0 else 0.0)
             pre = dep + (ctx if (cfg.fpm and it >= 1) else 0.0)
@@ -388,11 +482,21 @@ def forward(S_in, W, cfg: Cfg, mstate=None) -> ForwardOut:
         iters[:, t] = it_count
         ctx_all[:, t] = ctx
         if cfg.fpm:
-            m = fpm_write(hcur, sig, m, V, Wx_diag)
+            m_w = fpm_write(hcur, sig, m, V, Wx_diag)
+            if assoc:
+                old = {k: x.copy() for k, x in ast.items()}
+                m_a, pay_raw = assoc_write(S[:, t], ast, m, hcur, t)
+                for k in ast:  # the lower slots hold no associative state
+                    msk = upper if ast[k].ndim == 3 else upper[..., 0]
+                    ast[k] = np.where(msk, ast[k], old[k])
+                m_w = np.where(upper, m_a, m_w)
+                branch_sig[:, t] = np.where(upper, pay_raw, sig)
+            m = m_w
             hist[:, t] = m
     pooled = hstar.mean(axis=2)
     return ForwardOut(signal=signal, A=A, hstar=hstar, iters=iters, pooled=pooled,
-                      hist_ctx=hist, mstate=m, fpm_ctx=ctx_all, attn_cache=cache)
+                      hist_ctx=hist, mstate=m, fpm_ctx=ctx_all, attn_cache=cache,
+                      branch_signal=branch_sig, assoc_state=ast)
 
 
 # ---------------------------------------------------------------------------
@@ -738,6 +842,10 @@ def weight_grads(S_flat, signal, A, cache, v, g_pre, pre, r_pre, W, cfg: Cfg):
         G[L.k_bias:L.k_bias + h * d].reshape(h, d)[:, :hd] = dK.sum(0)
         dsig += dsrc
         G[L.slot_anchor:L.slot_anchor + h * d] = dsig.sum(0).ravel()
+    if cfg.fpm and cfg.assoc:
+        # the associative slots' branch holds the payload, not their signal
+        # (`:2497`), so the direct term reaches W_in and S_in from the lower slots only
+        dsig = dsig - np.where((np.arange(h) >= h // 2)[None, :, None], g_pre, 0.0)
     if not V.signal_zero:
         G[L.win:L.win + h * d * d] = (es('nj,nso->sjo', S_flat, dsig) * V.sig_scale).ravel()
         dS = es('sjo,nso->nj', V.Win, dsig) * V.sig_scale
@@ -768,9 +876,12 @@ def fpm_backward(hstar, signal, hist, v, W, d, h, carry=None):
     h_unit + wx*h_unit + write (no sqrt(z) factor) for m_inner and the a_log term,
     the novelty gradient is applied per dimension, W_x's carrier gradient omits
     the (1 - retain) factor, the read path contributes 0.5 * v[t] to dL/dM[t-1],
-    and m_prev is zero at t = 0 of the chunk.  The associative branch (off) and
-    the W_k_write / W_v_write updates (compiled out: ENABLE_FPM_WRITE_BWD = false,
-    FPM_DIRECT_WRITE_SCALE = 0) contribute nothing.
+    and m_prev is zero at t = 0 of the chunk.  The W_k_write / W_v_write updates
+    (compiled out: ENABLE_FPM_WRITE_BWD = false, FPM_DIRECT_WRITE_SCALE = 0)
+    contribute nothing.  With the associative branch on, `signal` is the stored
+    signal the reference reads here (`:399`), the payload on the associative
+    slots; the branch's own parameter gradients (alpha_assoc, the address and
+    event weights, the bank state, `:475-1290`) are not restated.
 
     Gradients are returned as raw sums over all sequences and tokens, in the
     AllWeights layout; the reference's per-family divisors (B*T for the slot
@@ -921,14 +1032,15 @@ def spectral_renorm(W, d, h, n_iters=12, attn=0.10, win=0.30, fpm=0.70, wv=0.50,
 
 def branch_of(fwd: ForwardOut, W, cfg: Cfg):
     V = View(W, cfg.d, cfg.h)
+    sig = fwd.signal if fwd.branch_signal is None else fwd.branch_signal
     if cfg.slot_coord:
-        return fwd.signal + fwd.A + V.anchor[None, None]
-    return fwd.signal.copy()
+        return sig + fwd.A + V.anchor[None, None]
+    return sig.copy()
 
 
 def train_step(S_in, targets, W, lm, cfg: Cfg, adam_state=None, step=1, lr=1e-3,
                mstate=None, fpm_carry=None, lm_samples=0, sample_seed=LM_SAMPLE_SEED,
-               lm_state=None, tokens=None, emb=None, emb_state=None, emb_grad="dl_dh"):
+               lm_state=None, tokens=None, emb=None, emb_state=None, emb_grad="dl_dh", assoc_state=None):
     """Forward -> LM head -> adjoint -> weight grads -> Adam (DEQ core and LM head).
 
     lm_samples = 0: dense full-vocabulary CE; the LM-head gradients join the
@@ -944,7 +1056,7 @@ def train_step(S_in, targets, W, lm, cfg: Cfg, adam_state=None, step=1, lr=1e-3,
     B, T, d = S_in.shape
     h = cfg.h
     N = B * T
-    fwd = forward(S_in, W, cfg, mstate)
+    fwd = forward(S_in, W, cfg, mstate, assoc_state)
     w_lm, b_lm, g_lm = lm
     tg = np.asarray(targets).reshape(N)
     sampled = None
@@ -967,7 +1079,9 @@ def train_step(S_in, targets, W, lm, cfg: Cfg, adam_state=None, step=1, lr=1e-3,
                          v, g_pre, pre, r_pre, W, cfg)
     fpm_out = None
     if cfg.fpm:
-        fpm_out = fpm_backward(fwd.hstar, fwd.signal, fwd.hist_ctx, v, W, d, h, carry=fpm_carry)
+        # the reference's FPM backward reads the stored signal (fused_fpm_retain_bwd.wgsl:399),
+        # the payload on associative slots
+        fpm_out = fpm_backward(fwd.hstar, fwd.branch_signal, fwd.hist_ctx, v, W, d, h, carry=fpm_carry)
         G = G + fpm_out["G"]
     if adam_state is None:
         adam_state = (np.zeros_like(G), np.zeros_like(G))

@@ -587,3 +587,110 @@ def test_adjoint_matches_numeric_picard_on_the_live_map_tightly():
             jt.ravel()[idx] = ((live_map(hp.reshape(h, d)) - live_map(hm.reshape(h, d))) * v_ref).sum() / 2e-5
         v_ref = b_rep + jt
     assert np.linalg.norm(v[0] - v_ref) / np.linalg.norm(v_ref) < 1e-6
+
+
+# ---------------------------------------------------------------- associative branch
+def _val(x):
+    """x / rms(x), renormalised by its own rms (the write's value)."""
+    r = lambda y: np.maximum(np.sqrt((y * y).mean(-1) + 1e-6), 1e-6)[..., None]
+    v0 = x / r(x)
+    return v0 / r(v0)
+
+
+def test_assoc_read_injects_the_bank_value_at_the_memory_read_scale():
+    """With one bank and a hard read the bank is read whatever its score
+    (deq_slot_attn_unified_clean.wgsl:1376-1385): the injection is the bank value
+    scaled to sigmoid(alpha_assoc) * |signal| * alpha_m, and zero for an empty bank."""
+    d, h = 64, 4
+    W = init_all_weights(d, h, seed=3)
+    V = O.View(W, d, h)
+    cfg = O.Cfg(d=d, h=h, fpm=True, assoc=True)
+    rng = np.random.default_rng(0)
+    bank = rng.standard_normal((2, h, d))
+    sig = rng.standard_normal((2, h, d))
+    inj = O.assoc_read(bank, sig, V, cfg)
+    alpha = 1.0 / (1.0 + np.exp(-V.alpha_assoc))
+    want = alpha[None] * np.linalg.norm(sig, axis=-1) * cfg.fpm_alpha_m
+    assert np.allclose(np.linalg.norm(inj, axis=-1), want, rtol=1e-12)
+    assert np.allclose(np.abs((inj * bank).sum(-1)), np.linalg.norm(inj, axis=-1) * np.linalg.norm(bank, axis=-1))
+    assert not O.assoc_read(np.zeros((2, h, d)), sig, V, cfg).any()
+
+
+def test_assoc_branch_forward_default_flags():
+    """The upper h/2 slots under the reference's default flags: no FPM write, one bank
+    write at t = 1 (the bank is then occupied), the 0.019 consolidation of h* into the
+    memory on that token only, the previous source carried as the normalised S_in row,
+    and the stored signal replaced by the unnormalised payload."""
+    d, h, B, T = 64, 4, 2, 6
+    W = init_all_weights(d, h, seed=3)
+    rng = np.random.default_rng(1)
+    S = rng.standard_normal((B, T, d)) * 0.5
+    cfg = O.Cfg(d=d, h=h, fpm=True, assoc=True, max_iters=12)
+    f = O.forward(S, W, cfg)
+    up, lo = slice(h // 2, h), slice(0, h // 2)
+    hs = f.hstar
+    rms = lambda y: np.maximum(np.sqrt((y * y).mean(-1) + 1e-6), 1e-6)[..., None]
+    # memory of the upper slots: 0 at t = 0, the consolidation at t = 1, then unchanged
+    assert not f.hist_ctx[:, 0, up].any()
+    c = 0.02 * 0.95
+    assert np.allclose(f.hist_ctx[:, 1, up], c * hs[:, 1, up] / rms(hs[:, 1, up]), atol=1e-14)
+    for t in range(2, T):
+        assert np.array_equal(f.hist_ctx[:, t, up], f.hist_ctx[:, 1, up])
+    # the lower slots kept the FPM write: their memory moves every token
+    assert all(np.abs(f.hist_ctx[:, t, lo] - f.hist_ctx[:, t - 1, lo]).max() > 0 for t in range(1, T))
+    # bank state after the chunk
+    val = _val(S)                                    # [B,T,d]
+    pay1 = val[:, 1] + val[:, 0] / rms(val[:, 0])
+    st = f.assoc_state
+    assert np.allclose(st["V"][:, up], (pay1 / rms(pay1))[:, None], atol=1e-13)
+    assert np.allclose(st["u"][:, up], 0.999 ** (T - 2))
+    assert np.allclose(st["P"][:, up], val[:, T - 1][:, None], atol=1e-13)
+    assert not st["V"][:, lo].any() and not st["u"][:, lo].any() and not st["P"][:, lo].any()
+    # the adjoint's branch: the payload on the upper slots, the signal below
+    for t in range(T):
+        prev = val[:, t - 1] / rms(val[:, t - 1]) if t else 0.0
+        assert np.allclose(f.branch_signal[:, t, up], (val[:, t] + prev)[:, None], atol=1e-12)
+    assert np.array_equal(f.branch_signal[:, :, lo], f.signal[:, :, lo])
+    # a second chunk continues from the carried state: the bank stays occupied (no write)
+    f2 = O.forward(S, W, cfg, mstate=f.mstate, assoc_state=f.assoc_state)
+    assert np.allclose(f2.assoc_state["V"][:, up], st["V"][:, up])
+    assert np.allclose(f2.assoc_state["u"][:, up], st["u"][:, up] * 0.999 ** T)
+    for t in range(T):
+        assert np.array_equal(f2.hist_ctx[:, t, up], f.mstate[:, up])
+    # without the FPM memory the branch is inert
+    g = O.forward(S, W, O.Cfg(d=d, h=h, fpm=False, assoc=True))
+    g0 = O.forward(S, W, O.Cfg(d=d, h=h, fpm=False))
+    assert np.array_equal(g.hstar, g0.hstar) and np.array_equal(g.branch_signal, g0.signal)
+
+
+def test_assoc_write_suppressed_when_the_bank_already_holds_the_previous_source():
+    """ENABLE_ASSOC_SUPPRESS_VALUE_SOURCE (`:2755`): an empty-usage bank whose value
+    already points along the previous source (cosine > 0.85) is not written."""
+    d, h, B = 32, 2, 1
+    st = O.assoc_state_zeros(B, h, d)
+    rng = np.random.default_rng(2)
+    P = rng.standard_normal((B, h, d))
+    st["P"] = P.copy()
+    st["V"] = P + 0.01 * rng.standard_normal((B, h, d))   # usage 0: empty, but cos ~ 1
+    m = rng.standard_normal((B, h, d))
+    m2, _ = O.assoc_write(rng.standard_normal((B, d)), st, m, rng.standard_normal((B, h, d)), t=3)
+    assert np.array_equal(m2, m) and not st["u"].any()
+
+
+def test_assoc_signal_gradient_reaches_win_only_from_the_lower_slots():
+    """With the payload as the associative slots' branch, their adjoint reaches
+    W_in (and S_in) only through attention; without attention not at all."""
+    d, h, B, T, Vv = 32, 4, 1, 5, 17
+    W = init_all_weights(d, h, seed=4)
+    lm = init_lm_head(d, Vv)
+    rng = np.random.default_rng(3)
+    S = rng.standard_normal((B, T, d)) * 0.5
+    tg = rng.integers(0, Vv, (B, T))
+    cfg = O.Cfg(d=d, h=h, fpm=True, assoc=True, slot_coord=False, max_iters=8, adj_iters=8)
+    r = O.train_step(S, tg, W, lm, cfg)
+    L = O.Offsets(d, h)
+    gwin = r["grads"][L.win:L.win + h * d * d].reshape(h, d, d)
+    assert not gwin[h // 2:].any() and np.abs(gwin[:h // 2]).max() > 0
+    r0 = O.train_step(S, tg, W, lm, O.Cfg(d=d, h=h, fpm=True, slot_coord=False, max_iters=8, adj_iters=8))
+    gwin0 = r0["grads"][L.win:L.win + h * d * d].reshape(h, d, d)
+    assert np.abs(gwin0[h // 2:]).max() > 0
