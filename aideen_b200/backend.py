@@ -167,17 +167,22 @@ class RunConfig:
                    int(self.fpm), self.fpm_alpha_m, self.fpm_tau, self.fpm_read_gate_min, self.anderson_m)
 
 
+CFG_ASSOC = 1  # aideen_cfg.flags bit: associative branch on the upper slots
+
+
 class GpuDeqBackend:
     """One context = one GPU, one CUDA stream, all device buffers."""
 
     def __init__(self, d_model: int, h_slots: int, max_batch: int, max_seq_len: int,
-                 vocab: int = 0, device: int = 0):
+                 vocab: int = 0, device: int = 0, assoc: bool = False):
+        """assoc: the reference's default associative branch on the upper h/2
+        slots whenever the FPM memory is on (AIDEEN_CFG_ASSOC)."""
         self.lib = load_library()
         self.d, self.h, self.vocab = d_model, h_slots, vocab
         self.max_batch, self.max_seq_len = max_batch, max_seq_len
         self.layout = Layout(d_model, h_slots)
         st = C.c_int(0)
-        cfg = _Cfg(d_model, h_slots, max_batch, max_seq_len, vocab, 0)
+        cfg = _Cfg(d_model, h_slots, max_batch, max_seq_len, vocab, CFG_ASSOC if assoc else 0)
         self.ctx = self.lib.aideen_create(C.byref(cfg), device, C.byref(st))
         if not self.ctx:
             raise AideenError(f"aideen_create failed with status {st.value}")

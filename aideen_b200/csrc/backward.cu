@@ -562,6 +562,26 @@ cudaError_t launch_dsig_init(const AttnBwdArgs &a, float *dsig, int rows, int sl
   return cudaGetLastError();
 }
 
+__global__ void sub_upper_slots_kernel(float *__restrict__ dsig, const float *__restrict__ gpre, int N, int h,
+                                       int d) {
+  const int hu = h - h / 2;             // upper slots h/2 .. h-1
+  const size_t row4 = (size_t)hu * d / 4;  // float4 per token over the upper slots
+  const size_t total4 = (size_t)N * row4;
+  const size_t off = (size_t)(h / 2) * d;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total4;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t n = i / row4, k = (i % row4) * 4;
+    const size_t idx = n * (size_t)h * d + off + k;
+    st4(dsig + idx, ld4(dsig + idx) - ld4(gpre + idx));
+  }
+}
+
+cudaError_t launch_sub_upper_slots(float *dsig, const float *gpre, int N, int h, int d, cudaStream_t st) {
+  if (N <= 0 || h < 2) return cudaSuccess;
+  sub_upper_slots_kernel<<<grid_for((size_t)N * (h - h / 2) * d / 4), 256, 0, st>>>(dsig, gpre, N, h, d);
+  return cudaGetLastError();
+}
+
 __global__ void add_kernel(float *__restrict__ dst, const float *__restrict__ x,
                            const float *__restrict__ y, size_t n4) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;

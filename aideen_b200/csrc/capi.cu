@@ -31,6 +31,10 @@ struct DevBufs {
   int32_t *tokens = nullptr, *targets = nullptr;
   float *signal = nullptr, *A = nullptr, *amat = nullptr;
   float *src = nullptr;  // [N][h][d] signal + slot anchor (attention source rows)
+  // associative branch (AIDEEN_CFG_ASSOC): per (sequence, upper slot) bank value,
+  // previous source [B][h][d] and usage [B][h], carried like MState; the stored
+  // signal [N][h][d] (the payload on the upper slots) the FPM backward reads
+  float *assoc_v = nullptr, *assoc_p = nullptr, *assoc_u = nullptr, *sig_store = nullptr;
   float *perm = nullptr;  // row-permutation scratch, max_tokens * h * d floats (on first use)
   float *Qh = nullptr, *Kh = nullptr, *Vh = nullptr, *alpha = nullptr, *nmix = nullptr,
         *rmix = nullptr, *scale = nullptr, *rho = nullptr, *Rsrc = nullptr;
@@ -135,6 +139,7 @@ struct aideen_ctx {
   // and the weights are all-gathered
   bool shard_step = false;
   bool fpm_prepared = false;  // the FPM backward's forward-only stage already ran this step
+  bool assoc = false;         // AIDEEN_CFG_ASSOC: associative branch on the upper slots with FPM
   int fpm_comp_done = 0;  // FPM chunk composites [0, this) already formed this step
   int sm_budget = 0;      // SMs the GEMM / softmax / adjoint launches may use (0: all)
   // optional stage timeline of the pipelined step (AIDEEN_PIPE_TIMELINE=1, stderr)
@@ -446,6 +451,10 @@ PicardArgs picard_args(aideen_ctx *ctx, const aideen_run *r) {
   p.iters = b.iters;
   p.t0 = 0;
   p.t1 = r->seq_len;
+  p.assoc = ctx->assoc && r->fpm ? 1 : 0;
+  p.off_alpha_assoc = L.alpha_assoc;
+  p.s_in = b.S_in;
+  p.assoc_v = b.assoc_v; p.assoc_p = b.assoc_p; p.assoc_u = b.assoc_u; p.sig_store = b.sig_store;
   p.anderson_m = r->anderson_m >= 2 ? (int)r->anderson_m : 0;  // depth 1 never mixes
   return p;
 }
@@ -704,6 +713,10 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   } else {
     KL(launch_dsig_init(a, b.dsig, N * h, 0, st));
   }
+  // associative slots: their branch holds the payload, not their signal, so the
+  // direct term g_pre reaches W_in and S_in from the lower slots only (the
+  // anchor above keeps it)
+  if (ctx->assoc && ctx->last_run.fpm) KL(launch_sub_upper_slots(b.dsig, b.gpre, N, h, d, st));
   if (!ctx->signal_zero) {
     // gW_in[s][j][o] = sigma * sum_n S_in[n][j] dsig[n][s][o]
     KL(gemm_any(ctx, tf32(gemm(d, d, N, h, b.S_in, d, 0, true, b.dsig, (long)h * d, d, false, G + L.win, d,
@@ -784,7 +797,8 @@ int run_fpm_backward(aideen_ctx *ctx, bool prepare_only) {
   struct PhaseReset { aideen_ctx *c; ~PhaseReset() { c->prof_phase = -1; } } phase_reset{ctx};
   if (!ctx->fpm_prepared || prepare_only) {
   // forward-only stage: c and the rank-32 projections (needs h*, not v)
-  KL(launch_fpm_c(b.hstar, b.signal, b.fc, (size_t)N * h * d, st));
+  // c = (h* + stored signal) / 2: the payload on the associative slots
+  KL(launch_fpm_c(b.hstar, ctx->assoc ? b.sig_store : b.signal, b.fc, (size_t)N * h * d, st));
   // up[n][s][r] = sum_j c W_retain_up[s][j][r];  kw = same with W_k_write
   KL(gemm_any(ctx, gemm(N, R, d, h, b.fc, hd, d, false, W + L.w_retain_up, R, (long)d * R, false,
                    b.fup, HR, R)));
@@ -1614,7 +1628,8 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   if (!cfg) return fail(AIDEEN_E_INVALID);
   const uint32_t d = cfg->d_model, h = cfg->h_slots;
   if (!(d == 128 || d == 256 || d == 512 || d == 1024) || h < 1 || h > 16 || cfg->max_batch == 0 ||
-      cfg->max_seq_len == 0)
+      cfg->max_seq_len == 0 || (cfg->flags & ~(uint32_t)AIDEEN_CFG_ASSOC) != 0 ||
+      ((cfg->flags & AIDEEN_CFG_ASSOC) && h < 2))
     return fail(AIDEEN_E_INVALID);
   if (cudaSetDevice(device) != cudaSuccess) return fail(AIDEEN_E_CUDA);
   aideen_ctx *ctx = new aideen_ctx();
@@ -1647,6 +1662,14 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   A(&b.hstar, Nhd); A(&b.pre, Nhd); A(&b.hist, Nhd); A(&b.fpmctx, Nhd);
   A(&b.v, Nhd); A(&b.gpre, Nhd); A(&b.dsig, Nhd); A(&b.da, Nhd);
   A(&b.mstate, (size_t)cfg->max_batch * h * d); A(&b.fcarry, (size_t)cfg->max_batch * h * d);
+  ctx->assoc = (cfg->flags & AIDEEN_CFG_ASSOC) != 0;
+  if (ctx->assoc) {
+    A(&b.assoc_v, (size_t)cfg->max_batch * h * d); A(&b.assoc_p, (size_t)cfg->max_batch * h * d);
+    A(&b.assoc_u, (size_t)cfg->max_batch * h); A(&b.sig_store, Nhd);
+    if (e == cudaSuccess) e = cudaMemset(b.assoc_v, 0, (size_t)cfg->max_batch * h * d * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemset(b.assoc_p, 0, (size_t)cfg->max_batch * h * d * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemset(b.assoc_u, 0, (size_t)cfg->max_batch * h * sizeof(float));
+  }
   A(&b.pooled, N * d); A(&b.dl_dh, N * d); A(&b.nsg, N * d); A(&b.dS, N * d);
   A(&b.y, N * d); A(&b.dy, N * d); A(&b.yhi, N * d); A(&b.ylo, N * d);
   A(&b.yThi, d * ((N + 3) / 4 * 4)); A(&b.yTlo, d * ((N + 3) / 4 * 4)); A(&b.ggp, N * d); A(&b.lrms, N); A(&b.loss_rows, N);
@@ -1735,6 +1758,7 @@ void aideen_destroy(aideen_ctx *ctx) {
   if (ctx->comm) ncclCommDestroy(ctx->comm);
   DevBufs &b = ctx->b;
   void *ptrs[] = {b.W, b.G, b.M1, b.M2, b.S_in, b.tokens, b.targets, b.signal, b.A, b.amat, b.qkv,
+                  b.assoc_v, b.assoc_p, b.assoc_u, b.sig_store,
                   b.dqkv, b.Wcat, b.alpha, b.nmix, b.rmix, b.scale, b.rho, b.Rsrc, b.hstar, b.pre,
                   b.pooled, b.hist, b.fpmctx, b.mstate, b.iters, b.v, b.gpre, b.dl_dh, b.rhs_slot,
                   b.nsg, b.da, b.dn, b.dsig, b.dRc, b.dS, b.lmp, b.Glm, b.Mlm1,
@@ -1991,6 +2015,12 @@ int aideen_reset_state(aideen_ctx *ctx) {
   // the TBPTT carry of the FPM backward is cleared with the memory (gpu_deq.rs:3147)
   CU(cudaMemsetAsync(ctx->b.fcarry, 0,
                      (size_t)ctx->cfg.max_batch * ctx->cfg.h_slots * ctx->cfg.d_model * 4, ctx->stream));
+  if (ctx->assoc) {  // the banks and the previous source (gpu_deq.rs:3141-3160)
+    const size_t bh = (size_t)ctx->cfg.max_batch * ctx->cfg.h_slots;
+    CU(cudaMemsetAsync(ctx->b.assoc_v, 0, bh * ctx->cfg.d_model * 4, ctx->stream));
+    CU(cudaMemsetAsync(ctx->b.assoc_p, 0, bh * ctx->cfg.d_model * 4, ctx->stream));
+    CU(cudaMemsetAsync(ctx->b.assoc_u, 0, bh * 4, ctx->stream));
+  }
   return AIDEEN_OK;
 }
 

@@ -492,7 +492,22 @@ __device__ __forceinline__ void bsum(BlockReducer &R, float (&v)[K]) {
 }
 
 // NW > 0: blockDim = 32 * NW fixed at compile time (static block reductions).
-template <bool FPM, int MAXT, int NW>
+// ASSOC (with FPM): the upper h/2 slots run the reference's default associative
+// branch (deq_slot_attn_unified_clean.wgsl:554-556) in place of the FPM write:
+//   read   the one bank's value V, hard-read whatever its address score
+//          (:1376-1385), added to the memory context scaled to
+//          sigmoid(alpha_assoc) * |signal| * alpha_m / max(|V|, 1e-3) (:1505-1563);
+//   write  (:2293-2948) value = x / rms(x) renormalised (x: the token's S_in row),
+//          payload = value + P / rms(P) (P: the previous token's value), written
+//          into V when the bank is empty (usage < 1e-4), t > 0 and
+//          cos(V, P / rms(P)) <= 0.85; usage <- max(0.999 usage, mass); the
+//          memory takes in 0.019 * mass of h* / rms(h*) (the FPM write is skipped
+//          on these slots, :1971, so its gate factor stays 1.0 capped at 0.95);
+//          the stored signal, which the adjoint's branch and the FPM backward
+//          read, becomes the unnormalised payload (:2497).
+// V and P live in this CTA's shared memory (each thread its own two elements),
+// the usage in a register; all three are loaded and stored per launch.
+template <bool FPM, int MAXT, int NW, bool ASSOC = false>
 __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
   extern __shared__ float4 sm4[];
   float *sm = reinterpret_cast<float *>(sm4);
@@ -508,6 +523,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
   const int b = blockIdx.x / h, s = blockIdx.x % h;
   const int j0 = picard_j0();
   const int warp = threadIdx.x >> 5;
+  const bool upper = ASSOC && s >= h / 2;  // an associative slot
   const float inv_d = 1.f / (float)d;
   const float *W = a.W;
   const float2 NS = ld2(W + a.off_ns + j0);
@@ -592,7 +608,10 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
   }
   // push mode inbox: [2][h][d] memory rows and [2][h][32] read keys of every
   // slot, double-buffered by token parity, one mbarrier per buffer
-  float *inbox_m = wprm + 3 * d;
+  // ASSOC: bank value V and previous source P of this CTA's slot
+  float *asv = wprm + 3 * d;
+  float *asp = asv + d;
+  float *inbox_m = wprm + 3 * d + (ASSOC ? 2 * d : 0);
   float *inbox_k = inbox_m + 2 * (size_t)h * d;
   uint64_t *inbar = reinterpret_cast<uint64_t *>(inbox_k + 2 * (size_t)h * kRank);
   const uint32_t inbox_bytes = (uint32_t)h * (uint32_t)(d + kRank) * 4u;
@@ -625,12 +644,26 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
   long long _pt = clock64();
   long long _pacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #endif
+  // ASSOC: the carried bank state of this slot (V and P into this thread's own
+  // shared-memory slots, so no barrier orders them), sigmoid(alpha_assoc[s])
+  float au = 0.f, aalpha = 0.f;
+  const size_t aso = ((size_t)b * h + s) * d + j0;
+  if constexpr (ASSOC) {
+    if (upper) {
+      st2(asv + j0, ld2(a.assoc_v + aso));
+      st2(asp + j0, ld2(a.assoc_p + aso));
+      au = a.assoc_u[b * h + s];
+      aalpha = 1.f / (1.f + expf(-W[a.off_alpha_assoc + s]));
+    }
+  }
   // rows of the next token, loaded one token ahead
   // rows are token-major: row (t, b) = t * B + b
   const size_t e0 = (((size_t)a.t0 * a.B + b) * h + s) * d + j0;
   const size_t tstride = (size_t)a.B * h * d;  // one token step in a row-major [N][h][d] buffer
   float2 sig_nx = ld2(a.signal + e0);
   float2 Av_nx = a.slot_coord ? ld2(a.A + e0) : f2(0.f);
+  // ASSOC: the next token's S_in row ([N][d], token-major)
+  float2 x_nx = upper ? ld2(a.s_in + ((size_t)a.t0 * a.B + b) * d + j0) : f2(0.f);
   // sum of squares of the next token's iteration-0 `dep` and `signal`,
   // reduced together with the previous token's last block reduction
   float dep0_sq = 0.f, sig_sq = 0.f;
@@ -639,10 +672,14 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
     const size_t e = (n * h + s) * d + j0;
     const float2 sig = sig_nx;
     const float2 Av = Av_nx;
+    const float2 xin = x_nx;
     if (t + 1 < a.t1) {
       sig_nx = ld2(a.signal + e + tstride);
       if (a.slot_coord) Av_nx = ld2(a.A + e + tstride);
+      if (upper) x_nx = ld2(a.s_in + ((size_t)(t + 1) * a.B + b) * d + j0);
     }
+    // ASSOC sums of this token (iteration 0's reduction): |x|^2, |P|^2, x.P, V.P, |V|^2
+    float a_xx = 0.f, a_pp = 0.f, a_xp = 0.f, a_vp = 0.f, a_vv = 0.f;
     if (t == 0) {
       float v[1] = {dot2(sig, sig)};
       bsum<NW>(R, v);
@@ -776,6 +813,10 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
           // |mu| >= 1e-3 (the 1e-6 floor on |mu|^2), so 1 / max(|mu|, 1e-6) = rsqrt(|mu|^2)
           const float coef = sig_norm * fmaxf(a.alpha_m, 0.001f) * rsqrtf(fmaxf(v1[0], 1e-6f)) * wsm[16];
           ctx = coef * mu;
+          if (upper) {  // the bank's value, hard-read (:1505-1563)
+            const float sc = aalpha * sig_norm * fmaxf(a.alpha_m, 0.001f) / fmaxf(sqrtf(fmaxf(a_vv, 1e-6f)), 1e-6f);
+            ctx = ctx + sc * ld2(asv + j0);
+          }
           PT(2);
         }
       }
@@ -809,7 +850,22 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
 #pragma unroll
         for (int q = 0; q < 5; ++q) q5[q] = v7[2 + q];
       } else if (FPM && it == 0) {
-        bsum<NW>(R, v2);
+        if (upper) {
+          const float2 Vv = ld2(asv + j0), Pv = ld2(asp + j0);
+          float v8[8] = {v2[0], v2[1], v2[2], dot2(xin, xin), dot2(Pv, Pv), dot2(xin, Pv), dot2(Vv, Pv),
+                         dot2(Vv, Vv)};
+          bsum<NW>(R, v8);
+          v2[0] = v8[0];
+          v2[1] = v8[1];
+          v2[2] = v8[2];
+          a_xx = v8[3];
+          a_pp = v8[4];
+          a_xp = v8[5];
+          a_vp = v8[6];
+          a_vv = v8[7];
+        } else {
+          bsum<NW>(R, v2);
+        }
       } else {
         float v2b[2] = {v2[0], v2[1]};
         bsum<NW>(R, v2b);
@@ -867,47 +923,85 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
         }
         PT(0);
       }
-      // post-solve memory write (:1965-2140)
-      const float2 c = 0.5f * (hcur + sig);
-      PT(4);
-      float2 pv, dv;
-      if (a.use_tmem && a.push) {
-        mv2_d_to_32_tmem(tmem + 0, tmem + 128, c, vec, part);   // bottleneck | retain-up
-        PT(5);
-        mv2_32_to_d_tmem(tmem + 256, vec, tmem + 384, vec + 32, pv, dv);
-      } else if (a.use_tmem) {
-        mv_d_to_32_smem_tmem(mat[2], tmem + 0, c, j0, xs, vec, part);   // bottleneck | retain-up
-        PT(5);
-        mv2_32_to_d_tmem(tmem + 128, vec, tmem + 256, vec + 32, pv, dv);
+      float2 mn;
+      if (upper) {
+        // associative write in place of the FPM write (:2293-2948); one
+        // reduction: |h*|^2 and the next token's |dep0|^2, |signal|^2
+        const float2 dep0n = sig_nx + hcur + anc + Av_nx;
+        float v3[3] = {dot2(hcur, hcur), dot2(dep0n, dep0n), dot2(sig_nx, sig_nx)};
+        bsum<NW>(R, v3);
+        dep0_sq = v3[1];
+        sig_sq = v3[2];
+        const float irc = 1.f / fmaxf(sqrtf(a_xx * inv_d + 1e-6f), 1e-6f);
+        const float irv = 1.f / fmaxf(sqrtf(a_xx * irc * irc * inv_d + 1e-6f), 1e-6f);
+        const float kv = irc * irv;  // value = kv * x
+        const float irp = 1.f / fmaxf(sqrtf(a_pp * inv_d + 1e-6f), 1e-6f);
+        const float2 Pv = ld2(asp + j0), Vv = ld2(asv + j0);
+        const float2 val = kv * xin;
+        const float2 pay_raw = val + irp * Pv;
+        const float qq = a_xx * kv * kv + 2.f * a_xp * kv * irp + a_pp * irp * irp;  // |payload|^2
+        const float irq = 1.f / fmaxf(sqrtf(qq * inv_d + 1e-6f), 1e-6f);
+        const float uc = fminf(fmaxf(isfinite(au) ? au : 0.f, 0.f), 1.f);
+        float cosv = a_vp * irp / sqrtf(fmaxf(a_vv * a_pp * irp * irp, 1e-12f));
+        if (!isfinite(cosv)) cosv = -1.f;
+        const float mass = (t > 0 && uc < 1e-4f && !(cosv > 0.85f)) ? 1.f : 0.f;
+        st2(asv + j0, (1.f - mass) * Vv + (mass * irq) * pay_raw);
+        st2(asp + j0, val);
+        au = fminf(fmaxf(fmaxf(0.999f * uc, mass), 0.f), 1.f);
+        const float cc = 0.02f * 0.95f * mass;
+        const float irh = 1.f / fmaxf(sqrtf(v3[0] * inv_d + 1e-6f), 1e-6f);
+        mn = (1.f - cc) * m + (cc * irh) * hcur;
+        // the stored signal is the payload from here on: the adjoint's branch and
+        // the FPM backward read it
+        pre_adj = pay_raw + hcur;
+        if (a.slot_coord) pre_adj = pre_adj + Av + anc;
+        st2(a.sig_store + e, pay_raw);
       } else {
-        mv_d_to_32<2>(mat[2], mat[3], c, j0, xs, vec, part);   // bottleneck | retain-up
-        PT(5);
-        mv2_32_to_d(mat[4], vec, mat[5], vec + 32, d, j0, pv, dv);
+        // post-solve memory write (:1965-2140)
+        const float2 c = 0.5f * (hcur + sig);
+        PT(4);
+        float2 pv, dv;
+        if (a.use_tmem && a.push) {
+          mv2_d_to_32_tmem(tmem + 0, tmem + 128, c, vec, part);   // bottleneck | retain-up
+          PT(5);
+          mv2_32_to_d_tmem(tmem + 256, vec, tmem + 384, vec + 32, pv, dv);
+        } else if (a.use_tmem) {
+          mv_d_to_32_smem_tmem(mat[2], tmem + 0, c, j0, xs, vec, part);   // bottleneck | retain-up
+          PT(5);
+          mv2_32_to_d_tmem(tmem + 128, vec, tmem + 256, vec + 32, pv, dv);
+        } else {
+          mv_d_to_32<2>(mat[2], mat[3], c, j0, xs, vec, part);   // bottleneck | retain-up
+          PT(5);
+          mv2_32_to_d(mat[4], vec, mat[5], vec + 32, d, j0, pv, dv);
+        }
+        PT(6);
+        const float2 prop = tanh2(ld2(wprm + j0) + pv);
+        const float2 df = prop - m;
+        // the next token's iteration-0 |dep|^2 and |signal|^2 ride along
+        const float2 dep0n = sig_nx + hcur + anc + Av_nx;
+        float v3[6] = {dot2(m, m), dot2(df, df), dot2(hcur, hcur), dot2(ld2(wprm + d + j0), c), dot2(dep0n, dep0n),
+                       dot2(sig_nx, sig_nx)};
+        bsum<NW>(R, v3);
+        dep0_sq = v3[4];
+        sig_sq = v3[5];
+        const float2 hu = rsqrtf(fmaxf(v3[2] * inv_d, 1e-6f)) * hcur;
+        const float raw_z = __fdividef(1.f, 1.f + __expf(-(v3[3] * rsqrtf((float)d) + wsm[40] - 1.5f)));
+        const float z = fminf(fmaxf(raw_z, 0.f), 1.f);
+        const float pq = fmaxf(v3[0], 1e-6f), dq = fmaxf(v3[1], 1e-6f);
+        const float prev_norm = pq * rsqrtf(pq);
+        const float diff_norm = dq * rsqrtf(dq);
+        const float novelty = __fdividef(diff_norm, diff_norm + prev_norm + 1e-6f);
+        const float2 rrv = sigmoid2(ld2(wprm + 2 * d + j0) + dv);
+        const float2 retain = f2(1.f) - novelty * (f2(1.f) - rrv);
+        const float2 write = (z * 0.1f) * prop;
+        const float zq = fmaxf(z, 1e-6f);
+        const float2 x = (zq * rsqrtf(zq)) * hu + wxv * hu + write;
+        const float2 base = adv * m + (f2(1.f) - adv) * x;
+        mn = retain * m + (f2(1.f) - retain) * base;
       }
-      PT(6);
-      const float2 prop = tanh2(ld2(wprm + j0) + pv);
-      const float2 df = prop - m;
-      // the next token's iteration-0 |dep|^2 and |signal|^2 ride along
-      const float2 dep0n = sig_nx + hcur + anc + Av_nx;
-      float v3[6] = {dot2(m, m), dot2(df, df), dot2(hcur, hcur), dot2(ld2(wprm + d + j0), c), dot2(dep0n, dep0n),
-                     dot2(sig_nx, sig_nx)};
-      bsum<NW>(R, v3);
-      dep0_sq = v3[4];
-      sig_sq = v3[5];
-      const float2 hu = rsqrtf(fmaxf(v3[2] * inv_d, 1e-6f)) * hcur;
-      const float raw_z = __fdividef(1.f, 1.f + __expf(-(v3[3] * rsqrtf((float)d) + wsm[40] - 1.5f)));
-      const float z = fminf(fmaxf(raw_z, 0.f), 1.f);
-      const float pq = fmaxf(v3[0], 1e-6f), dq = fmaxf(v3[1], 1e-6f);
-      const float prev_norm = pq * rsqrtf(pq);
-      const float diff_norm = dq * rsqrtf(dq);
-      const float novelty = __fdividef(diff_norm, diff_norm + prev_norm + 1e-6f);
-      const float2 rrv = sigmoid2(ld2(wprm + 2 * d + j0) + dv);
-      const float2 retain = f2(1.f) - novelty * (f2(1.f) - rrv);
-      const float2 write = (z * 0.1f) * prop;
-      const float zq = fmaxf(z, 1e-6f);
-      const float2 x = (zq * rsqrtf(zq)) * hu + wxv * hu + write;
-      const float2 base = adv * m + (f2(1.f) - adv) * x;
-      const float2 mn = retain * m + (f2(1.f) - retain) * base;
+      if constexpr (ASSOC) {
+        if (!upper) st2(a.sig_store + e, sig);
+      }
       st2(mbuf + (cur ^ 1) * d + j0, mn);
       m = mn;
       PT(4);
@@ -959,6 +1053,13 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
   if (threadIdx.x == 0)
     for (int i = 0; i < 8; ++i) g_picard_prof[blockIdx.x * 8 + i] += _pacc[i];
 #endif
+  if constexpr (ASSOC) {
+    if (upper) {
+      st2(a.assoc_v + aso, ld2(asv + j0));
+      st2(a.assoc_p + aso, ld2(asp + j0));
+      if (threadIdx.x == 0) a.assoc_u[b * h + s] = au;
+    }
+  }
   if constexpr (FPM) {
     st2(a.mstate + ((size_t)b * h + s) * d + j0, m);
     if (a.push) {  // no CTA leaves while a peer may still push into it
@@ -1072,10 +1173,11 @@ static size_t picard_smem_base(int d) {
   return (size_t)(512 + 64 + 1024 + 64 + 64 + 6 * d) * sizeof(float);
 }
 
-template <bool FPM, int MAXT, int NW = 0>
+template <bool FPM, int MAXT, int NW = 0, bool ASSOC = false>
 static cudaError_t picard_launch(const PicardArgs &a, cudaStream_t st) {
   const int threads = a.d / 2;
-  size_t smem = picard_smem_base(a.d);
+  // ASSOC: the bank value and previous source of the CTA's slot (2 d floats)
+  size_t smem = picard_smem_base(a.d) + (ASSOC ? 2 * (size_t)a.d * sizeof(float) : 0);
   if (!FPM) {
     cudaError_t e = cudaFuncSetAttribute(picard_kernel<false, MAXT, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
@@ -1083,7 +1185,7 @@ static cudaError_t picard_launch(const PicardArgs &a, cudaStream_t st) {
     picard_kernel<false, MAXT, NW><<<a.B * a.h, threads, smem, st>>>(a);
     return cudaGetLastError();
   }
-  cudaError_t e = cudaFuncSetAttribute(picard_kernel<true, MAXT, NW>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaError_t e = cudaFuncSetAttribute(picard_kernel<true, MAXT, NW, ASSOC>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e != cudaSuccess) return e;
   int dev = 0, optin = 0;
   cudaGetDevice(&dev);
@@ -1108,7 +1210,7 @@ static cudaError_t picard_launch(const PicardArgs &a, cudaStream_t st) {
     smem -= mat_bytes;
     smem += (2 * (size_t)a.h * (a.d + kRank) + 4) * sizeof(float);
   }
-  e = cudaFuncSetAttribute(picard_kernel<true, MAXT, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  e = cudaFuncSetAttribute(picard_kernel<true, MAXT, NW, ASSOC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.B * a.h);
@@ -1122,13 +1224,18 @@ static cudaError_t picard_launch(const PicardArgs &a, cudaStream_t st) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, picard_kernel<true, MAXT, NW>, p);
+  e = cudaLaunchKernelEx(&cfg, picard_kernel<true, MAXT, NW, ASSOC>, p);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
 cudaError_t launch_picard(const PicardArgs &a, bool fpm, cudaStream_t st) {
   if (a.B <= 0 || a.T <= 0 || a.t1 <= a.t0) return cudaSuccess;
+  if (fpm && a.assoc) {  // the associative branch on the upper slots
+    if (a.d > 512) return picard_launch<true, 512, 0, true>(a, st);
+    if (a.d == 512) return picard_launch<true, 256, 8, true>(a, st);
+    return picard_launch<true, 256, 0, true>(a, st);
+  }
   if (a.d > 512) return fpm ? picard_launch<true, 512>(a, st) : picard_launch<false, 512>(a, st);
   if (a.d == 512)  // 256 threads: eight warps, static reductions
     return fpm ? picard_launch<true, 256, 8>(a, st) : picard_launch<false, 256, 8>(a, st);

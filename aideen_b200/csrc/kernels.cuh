@@ -82,6 +82,13 @@ struct PicardArgs {
   const float *signal, *A;
   float *hstar, *pre, *hist, *fpmctx, *mstate;
   int32_t *iters;
+  // associative branch of the upper h/2 slots (with FPM; see picard_kernel)
+  int assoc;
+  size_t off_alpha_assoc;
+  const float *s_in;               // [N][d] token-major S_in rows
+  float *assoc_v, *assoc_p;        // [B][h][d] bank value, previous source (carried)
+  float *assoc_u;                  // [B][h] bank usage (carried)
+  float *sig_store;                // [N][h][d] stored signal: the payload on the upper slots
 };
 
 struct AdjointArgs {
@@ -132,6 +139,9 @@ cudaError_t launch_adjoint(const AdjointArgs &a, cudaStream_t st, int *grid_out 
 cudaError_t launch_source_grad(const float *gpre, float *out, int N, int h, int d, cudaStream_t st);
 cudaError_t launch_attn_bwd_scale(const AttnBwdArgs &a, int rows, cudaStream_t st);
 cudaError_t launch_attn_bwd_softmax(const AttnBwdArgs &a, int N, cudaStream_t st);
+// dsig[n][s][:] -= g_pre[n][s][:] for the upper h/2 slots (the associative
+// slots, whose branch does not hold their signal).
+cudaError_t launch_sub_upper_slots(float *dsig, const float *gpre, int N, int h, int d, cudaStream_t st);
 cudaError_t launch_dsig_init(const AttnBwdArgs &a, float *dsig, int rows, int slot_coord,
                              cudaStream_t st);
 // out[map(c)] (+)= sum_r X[r*ld + c], c < ncols; map(c) = (c/seg)*ostride + c%seg.

@@ -54,8 +54,18 @@ typedef struct aideen_cfg {
   uint32_t max_batch;    /* forward_batch_cap */
   uint32_t max_seq_len;  /* forward_seq_cap */
   uint32_t vocab;        /* LM head / embedding rows; 0 = no LM head */
-  uint32_t flags;        /* reserved, 0 */
+  uint32_t flags;        /* AIDEEN_CFG_* bits; 0 = none */
 } aideen_cfg;
+/* flags bit 0: with the FPM memory on, the upper h/2 slots run the reference's
+ * default associative branch (deq_slot_attn_unified_clean.wgsl:554-556, on at
+ * FPM stage 4) in place of the FPM write: a one-bank hard read added to the
+ * memory context, a single bank write per empty bank, a 0.019 consolidation of
+ * h* into the slot's memory, and the payload as the slot's stored signal (the
+ * adjoint's branch and the FPM backward read it).  Its own parameter gradients
+ * (alpha_assoc, address and event weights, fused_fpm_retain_bwd.wgsl:475-1290)
+ * are not computed.  The bank state is carried across calls and cleared by
+ * aideen_reset_state.  Needs h_slots >= 2. */
+#define AIDEEN_CFG_ASSOC 1u
 
 /* One forward dispatch (RunUniforms, deq_slot_attn_unified_clean.wgsl:1-21;
  * DeqComputeShape, deq_bridge.rs:4-25). */
