@@ -645,15 +645,18 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
   long long _pacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #endif
   // ASSOC: the carried bank state of this slot (V and P into this thread's own
-  // shared-memory slots, so no barrier orders them), sigmoid(alpha_assoc[s])
-  float au = 0.f, aalpha = 0.f;
+  // shared-memory slots, so no barrier orders them); the usage in a register
+  // (every thread updates it identically); sigmoid(alpha_assoc[s]) in wsm[54]
+  // and the token's five sums in wsm[48..52], so nothing else of the branch
+  // stays live in registers across the Picard iterations
+  float au = 0.f;
   const size_t aso = ((size_t)b * h + s) * d + j0;
   if constexpr (ASSOC) {
     if (upper) {
       st2(asv + j0, ld2(a.assoc_v + aso));
       st2(asp + j0, ld2(a.assoc_p + aso));
       au = a.assoc_u[b * h + s];
-      aalpha = 1.f / (1.f + expf(-W[a.off_alpha_assoc + s]));
+      if (threadIdx.x == 0) wsm[54] = 1.f / (1.f + expf(-W[a.off_alpha_assoc + s]));
     }
   }
   // rows of the next token, loaded one token ahead
@@ -662,8 +665,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
   const size_t tstride = (size_t)a.B * h * d;  // one token step in a row-major [N][h][d] buffer
   float2 sig_nx = ld2(a.signal + e0);
   float2 Av_nx = a.slot_coord ? ld2(a.A + e0) : f2(0.f);
-  // ASSOC: the next token's S_in row ([N][d], token-major)
-  float2 x_nx = upper ? ld2(a.s_in + ((size_t)a.t0 * a.B + b) * d + j0) : f2(0.f);
+
   // sum of squares of the next token's iteration-0 `dep` and `signal`,
   // reduced together with the previous token's last block reduction
   float dep0_sq = 0.f, sig_sq = 0.f;
@@ -672,14 +674,12 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
     const size_t e = (n * h + s) * d + j0;
     const float2 sig = sig_nx;
     const float2 Av = Av_nx;
-    const float2 xin = x_nx;
     if (t + 1 < a.t1) {
       sig_nx = ld2(a.signal + e + tstride);
       if (a.slot_coord) Av_nx = ld2(a.A + e + tstride);
-      if (upper) x_nx = ld2(a.s_in + ((size_t)(t + 1) * a.B + b) * d + j0);
     }
-    // ASSOC sums of this token (iteration 0's reduction): |x|^2, |P|^2, x.P, V.P, |V|^2
-    float a_xx = 0.f, a_pp = 0.f, a_xp = 0.f, a_vp = 0.f, a_vv = 0.f;
+    // ASSOC: this token's S_in row ([N][d], token-major)
+    const float *xrow = a.s_in + ((size_t)t * a.B + b) * d + j0;
     if (t == 0) {
       float v[1] = {dot2(sig, sig)};
       bsum<NW>(R, v);
@@ -814,7 +814,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
           const float coef = sig_norm * fmaxf(a.alpha_m, 0.001f) * rsqrtf(fmaxf(v1[0], 1e-6f)) * wsm[16];
           ctx = coef * mu;
           if (upper) {  // the bank's value, hard-read (:1505-1563)
-            const float sc = aalpha * sig_norm * fmaxf(a.alpha_m, 0.001f) / fmaxf(sqrtf(fmaxf(a_vv, 1e-6f)), 1e-6f);
+            const float sc = wsm[54] * sig_norm * fmaxf(a.alpha_m, 0.001f) / fmaxf(sqrtf(fmaxf(wsm[52], 1e-6f)), 1e-6f);
             ctx = ctx + sc * ld2(asv + j0);
           }
           PT(2);
@@ -851,18 +851,19 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
         for (int q = 0; q < 5; ++q) q5[q] = v7[2 + q];
       } else if (FPM && it == 0) {
         if (upper) {
-          const float2 Vv = ld2(asv + j0), Pv = ld2(asp + j0);
+          // this token's sums |x|^2, |P|^2, x.P, V.P, |V|^2 ride along, parked
+          // in wsm[48..52] (read after later barriers)
+          const float2 Vv = ld2(asv + j0), Pv = ld2(asp + j0), xin = ld2(xrow);
           float v8[8] = {v2[0], v2[1], v2[2], dot2(xin, xin), dot2(Pv, Pv), dot2(xin, Pv), dot2(Vv, Pv),
                          dot2(Vv, Vv)};
           bsum<NW>(R, v8);
           v2[0] = v8[0];
           v2[1] = v8[1];
           v2[2] = v8[2];
-          a_xx = v8[3];
-          a_pp = v8[4];
-          a_xp = v8[5];
-          a_vp = v8[6];
-          a_vv = v8[7];
+          if (threadIdx.x == 0) {
+#pragma unroll
+            for (int q = 0; q < 5; ++q) wsm[48 + q] = v8[3 + q];
+          }
         } else {
           bsum<NW>(R, v2);
         }
@@ -932,6 +933,8 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
         bsum<NW>(R, v3);
         dep0_sq = v3[1];
         sig_sq = v3[2];
+        const float a_xx = wsm[48], a_pp = wsm[49], a_xp = wsm[50], a_vp = wsm[51], a_vv = wsm[52];
+        const float2 xin = ld2(xrow);
         const float irc = 1.f / fmaxf(sqrtf(a_xx * inv_d + 1e-6f), 1e-6f);
         const float irv = 1.f / fmaxf(sqrtf(a_xx * irc * irc * inv_d + 1e-6f), 1e-6f);
         const float kv = irc * irv;  // value = kv * x

@@ -34,6 +34,9 @@ sys.path.insert(0, ROOT)
 D, H, T, B_PER_GPU, VOCAB = 512, 8, 256, 8, 50257
 MAX_ITERS, ADJ_ITERS, ANDERSON_M = 20, 12, 4
 LM_SAMPLES = 512          # the reference's ArchitectureConfig num_samples default (state.rs:54)
+# the associative branch of the upper slots: on in the reference's default runtime
+# at d_r = 512 (FPM stage 4, deq_slot_attn_unified_clean.wgsl:554-556)
+ASSOC = True
 METRIC = "train tokens/s @d_r=512,h_slots=8,ctx=256"
 
 
@@ -127,7 +130,7 @@ def cpu_baseline(n_seq: int = B_PER_GPU, t_len: int = T, single_thread: bool = T
     emb = init_embedding(D, VOCAB)
     tok, tg = make_tokens(0, B_PER_GPU)
     tok, tg = np.ascontiguousarray(tok[:n_seq, :t_len]), np.ascontiguousarray(tg[:n_seq, :t_len])
-    cfg = O.Cfg(d=D, h=H, fpm=True, max_iters=MAX_ITERS, adj_iters=ADJ_ITERS, anderson_m=ANDERSON_M)
+    cfg = O.Cfg(d=D, h=H, fpm=True, max_iters=MAX_ITERS, adj_iters=ADJ_ITERS, anderson_m=ANDERSON_M, assoc=ASSOC)
     t0 = time.perf_counter()
     O.train_step(emb[tok], tg, W, lm, cfg, lm_samples=LM_SAMPLES, tokens=tok, emb=emb)
     dt = time.perf_counter() - t0
@@ -315,7 +318,7 @@ def configs1_step(device, steps=20, warmup=3):
     import torch
     from aideen_b200.backend import GpuDeqBackend, RunConfig, HOST
     from aideen_b200.weights import init_all_weights, init_embedding, init_lm_head
-    be = GpuDeqBackend(D, H, max_batch=1, max_seq_len=T, vocab=VOCAB, device=device)
+    be = GpuDeqBackend(D, H, max_batch=1, max_seq_len=T, vocab=VOCAB, device=device, assoc=ASSOC)
     be.upload_weights(init_all_weights(D, H, seed=0))
     be.upload_lm_head(*init_lm_head(D, VOCAB))
     be.upload_embedding(init_embedding(D, VOCAB))
@@ -387,6 +390,7 @@ def arm_config(world, dense_lm=False):
             "d_r": D, "h_slots": H, "ctx": T, "batch_per_gpu": B_PER_GPU,
             "global_batch": B_PER_GPU * world, "vocab": VOCAB, "lm_samples": 0 if dense_lm else LM_SAMPLES,
             "max_iters": MAX_ITERS, "adj_iters": ADJ_ITERS, "anderson_m": ANDERSON_M,
+            "assoc": "associative branch on the upper 4 slots (reference default)" if ASSOC else "off",
             "parallelism": f"dp{world}", "l2": "256 MB buffer written before every step, inside the timed region"}
 
 
@@ -457,7 +461,7 @@ def main():
         return
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    be = GpuDeqBackend(D, H, max_batch=B_PER_GPU, max_seq_len=T, vocab=VOCAB, device=local)
+    be = GpuDeqBackend(D, H, max_batch=B_PER_GPU, max_seq_len=T, vocab=VOCAB, device=local, assoc=ASSOC)
     stream = torch.cuda.Stream()
     be.set_stream(stream.cuda_stream)
     W = init_all_weights(D, H, seed=0)

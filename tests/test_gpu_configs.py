@@ -80,23 +80,25 @@ def test_d1024_h16_step():
     assert_step(e, loss, r)
 
 
-def _reference_step(d, h, B, T, V, ns, fwd_m=0, max_iters=20, adj=12, am=4, emb_src=1, step=1):
+def _reference_step(d, h, B, T, V, ns, fwd_m=0, max_iters=20, adj=12, am=4, emb_src=1, step=1, assoc=False):
     """The reference's full step: sampled-softmax LM head with its own Adam step,
     DEQ core Adam, embedding rows updated from dL/dpooled (emb_src 1) or the
-    exact dL/dS_in (emb_src 2)."""
+    exact dL/dS_in (emb_src 2); assoc: the associative branch on the upper slots
+    (the reference's default runtime, as bench.py runs it)."""
     ids = zipf_tokens(B * (T + 1), V, seed=11).reshape(B, T + 1)
     tok, tg = ids[:, :-1].copy(), ids[:, 1:].copy()
     tg[0, 1] = -1                                    # an ignored target
     W = init_all_weights(d, h, seed=0)
     lm, emb = init_lm_head(d, V), init_embedding(d, V)
-    be = GpuDeqBackend(d, h, max_batch=B, max_seq_len=T, vocab=V)
+    be = GpuDeqBackend(d, h, max_batch=B, max_seq_len=T, vocab=V, assoc=assoc)
     be.upload_weights(W)
     be.upload_lm_head(*lm)
     be.upload_embedding(emb)
     rc = RunConfig(max_iters=max_iters, fpm=True, anderson_m=fwd_m)
     loss = be.train_step(tok, tg, B, T, rc, adj_iters=adj, anderson_m=am, lr=1e-3, step=step,
                          lm_samples=ns, emb_update=emb_src)
-    cfg = O.Cfg(d=d, h=h, fpm=True, max_iters=max_iters, adj_iters=adj, anderson_m=am, fwd_anderson_m=fwd_m)
+    cfg = O.Cfg(d=d, h=h, fpm=True, max_iters=max_iters, adj_iters=adj, anderson_m=am, fwd_anderson_m=fwd_m,
+                assoc=assoc)
     r = O.train_step(emb[tok], tg, W, lm, cfg, step=step, lm_samples=ns, tokens=tok, emb=emb,
                      emb_grad="dl_dh" if emb_src == 1 else "ds_in")
     N = B * T
@@ -135,10 +137,11 @@ def _reference_step(d, h, B, T, V, ns, fwd_m=0, max_iters=20, adj=12, am=4, emb_
     return e
 
 
-@pytest.mark.parametrize("shape", [(128, 4, 2, 16, 97, 32), (512, 8, 8, 256, 50257, 512)],
-                         ids=["small", "bench_shard"])
-def test_reference_full_step_sampled_lm_and_embedding(shape):
-    e = _reference_step(*shape)
+@pytest.mark.parametrize("shape,assoc", [((128, 4, 2, 16, 97, 32), False), ((512, 8, 8, 256, 50257, 512), False),
+                                         ((512, 8, 8, 256, 50257, 512), True)],
+                         ids=["small", "bench_shard", "bench_shard_assoc"])
+def test_reference_full_step_sampled_lm_and_embedding(shape, assoc):
+    e = _reference_step(*shape, assoc=assoc)
     assert e["S_equal"] == 1.0 and e["iters_mismatch"] == 0.0 and e["lm_untouched"] == 0.0
     for k in ("loss", "hstar", "dl_dh", "v", "core_grads", "dW_sampled", "db_sampled"):
         assert e[k] < 1e-3, (k, e)
