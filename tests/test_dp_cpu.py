@@ -40,11 +40,11 @@ def _case():
     return W, lm, emb, tok, tg
 
 
-def _rank(rank, world, port, out):
+def _rank(rank, world, port, out, assoc=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     W, lm, emb, tok, tg = _case()
-    cfg = O.Cfg(d=D, h=H, max_iters=12, adj_iters=30, fpm=True)
+    cfg = O.Cfg(d=D, h=H, max_iters=12, adj_iters=30, fpm=True, assoc=assoc)
     r = O.train_step(emb[tok[rank:rank + 1]], tg[rank:rank + 1], W, lm, cfg)
     g = torch.from_numpy(np.concatenate([r["grads"], r["lm_grads"]]))
     dist.all_reduce(g)
@@ -55,11 +55,14 @@ def _rank(rank, world, port, out):
     dist.destroy_process_group()
 
 
-def test_allreduced_shard_gradients_equal_full_batch_gradient():
+@pytest.mark.parametrize("assoc", [False, True], ids=["fpm", "fpm_assoc"])
+def test_allreduced_shard_gradients_equal_full_batch_gradient(assoc):
+    """assoc: the associative branch of the upper slots keeps per-sequence state
+    only (banks, previous source), so it shards like the FPM memory."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_rank, args=(r, 2, port, q, assoc)) for r in range(2)]
     for p in ps:
         p.start()
     g_dp = q.get(timeout=240)
@@ -69,7 +72,7 @@ def test_allreduced_shard_gradients_equal_full_batch_gradient():
     W, lm, emb, tok, tg = _case()
     # full batch: mean over both sequences' tokens.  With per-sequence FPM memory
     # and equal shard sizes, the mean of the shard means is the global mean.
-    cfg = O.Cfg(d=D, h=H, max_iters=12, adj_iters=30, fpm=True)
+    cfg = O.Cfg(d=D, h=H, max_iters=12, adj_iters=30, fpm=True, assoc=assoc)
     r = O.train_step(emb[tok], tg, W, lm, cfg)
     g_full = np.concatenate([r["grads"], r["lm_grads"]])
     err = np.linalg.norm(g_dp - g_full) / np.linalg.norm(g_full)
