@@ -31,3 +31,12 @@ def test_all_weights_len_host_function():
     lib = backend.load_library()
     for d, h in [(128, 4), (512, 8), (1024, 16)]:
         assert lib.aideen_all_weights_len(d, h) == all_weights_len(d, h)
+
+
+def test_header_constants_match_the_python_mirror():
+    """The aideen_cfg flag bit and the constants the Python mirror passes through
+    the C ABI are the header's."""
+    src = open(os.path.join(ROOT, "include", "aideen_b200.h")).read()
+    defs = dict(re.findall(r"#define\s+(AIDEEN_\w+)\s+(\d+)u?", src))
+    assert int(defs["AIDEEN_CFG_ASSOC"]) == backend.CFG_ASSOC
+    assert int(defs["AIDEEN_UNIQUE_ID_BYTES"]) == 128
