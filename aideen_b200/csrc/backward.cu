@@ -582,6 +582,49 @@ cudaError_t launch_sub_upper_slots(float *dsig, const float *gpre, int N, int h,
   return cudaGetLastError();
 }
 
+// One CTA per upper slot; a warp per token row, fixed striding and a fixed
+// block reduction order (deterministic).
+__global__ void __launch_bounds__(256) assoc_alpha_grad_kernel(const float *__restrict__ v,
+                                                               const float *__restrict__ vread,
+                                                               const float *__restrict__ alpha_raw, int N, int h,
+                                                               int d, float *__restrict__ g_alpha) {
+  __shared__ float red[8];
+  const int s = h / 2 + blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float acc = 0.f;
+  for (int n = warp; n < N; n += 8) {
+    const float *vr = v + ((size_t)s * N + n) * d;
+    const float *br = vread + ((size_t)n * h + s) * d;
+    float dot = 0.f, vv = 0.f;
+    for (int j = lane * 4; j < d; j += 128) {
+      float4 g = ld4(vr + j);
+      const float4 q = ld4(br + j);
+      if (!finite4(g)) g = make_float4(isfinite(g.x) ? g.x : 0.f, isfinite(g.y) ? g.y : 0.f,
+                                       isfinite(g.z) ? g.z : 0.f, isfinite(g.w) ? g.w : 0.f);
+      dot += dot4(g, q);
+      vv += dot4(q, q);
+    }
+    dot = warp_sum(dot);
+    vv = warp_sum(vv);
+    acc += dot / fmaxf(sqrtf(vv / (float)d), 0.1f);
+  }
+  if (lane == 0) red[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < 8; ++w) t += red[w];
+    const float a = 1.f / (1.f + expf(-alpha_raw[s]));
+    g_alpha[s] = a * (1.f - a) * t;
+  }
+}
+
+cudaError_t launch_assoc_alpha_grad(const float *v, const float *vread, const float *alpha_raw, int N, int h, int d,
+                                    float *g_alpha, cudaStream_t st) {
+  if (N <= 0 || h < 2) return cudaSuccess;
+  assoc_alpha_grad_kernel<<<h - h / 2, 256, 0, st>>>(v, vread, alpha_raw, N, h, d, g_alpha);
+  return cudaGetLastError();
+}
+
 __global__ void add_kernel(float *__restrict__ dst, const float *__restrict__ x,
                            const float *__restrict__ y, size_t n4) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;

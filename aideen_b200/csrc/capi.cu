@@ -35,6 +35,7 @@ struct DevBufs {
   // previous source [B][h][d] and usage [B][h], carried like MState; the stored
   // signal [N][h][d] (the payload on the upper slots) the FPM backward reads
   float *assoc_v = nullptr, *assoc_p = nullptr, *assoc_u = nullptr, *sig_store = nullptr;
+  float *assoc_read = nullptr;  // [N][h][d] bank value each token read (upper slots)
   float *perm = nullptr;  // row-permutation scratch, max_tokens * h * d floats (on first use)
   float *Qh = nullptr, *Kh = nullptr, *Vh = nullptr, *alpha = nullptr, *nmix = nullptr,
         *rmix = nullptr, *scale = nullptr, *rho = nullptr, *Rsrc = nullptr;
@@ -455,6 +456,7 @@ PicardArgs picard_args(aideen_ctx *ctx, const aideen_run *r) {
   p.off_alpha_assoc = L.alpha_assoc;
   p.s_in = b.S_in;
   p.assoc_v = b.assoc_v; p.assoc_p = b.assoc_p; p.assoc_u = b.assoc_u; p.sig_store = b.sig_store;
+  p.assoc_read = b.assoc_read;
   p.anderson_m = r->anderson_m >= 2 ? (int)r->anderson_m : 0;  // depth 1 never mixes
   return p;
 }
@@ -716,7 +718,11 @@ int run_weight_grads(aideen_ctx *ctx, bool want_ds) {
   // associative slots: their branch holds the payload, not their signal, so the
   // direct term g_pre reaches W_in and S_in from the lower slots only (the
   // anchor above keeps it)
-  if (ctx->assoc && ctx->last_run.fpm) KL(launch_sub_upper_slots(b.dsig, b.gpre, N, h, d, st));
+  if (ctx->assoc && ctx->last_run.fpm) {
+    KL(launch_sub_upper_slots(b.dsig, b.gpre, N, h, d, st));
+    // the reference's alpha_assoc gradient from the adjoint and the values read
+    KL(launch_assoc_alpha_grad(b.v, b.assoc_read, W + L.alpha_assoc, N, h, d, G + L.alpha_assoc, st));
+  }
   if (!ctx->signal_zero) {
     // gW_in[s][j][o] = sigma * sum_n S_in[n][j] dsig[n][s][o]
     KL(gemm_any(ctx, tf32(gemm(d, d, N, h, b.S_in, d, 0, true, b.dsig, (long)h * d, d, false, G + L.win, d,
@@ -1665,7 +1671,7 @@ aideen_ctx *aideen_create(const aideen_cfg *cfg, int device, int *status) {
   ctx->assoc = (cfg->flags & AIDEEN_CFG_ASSOC) != 0;
   if (ctx->assoc) {
     A(&b.assoc_v, (size_t)cfg->max_batch * h * d); A(&b.assoc_p, (size_t)cfg->max_batch * h * d);
-    A(&b.assoc_u, (size_t)cfg->max_batch * h); A(&b.sig_store, Nhd);
+    A(&b.assoc_u, (size_t)cfg->max_batch * h); A(&b.sig_store, Nhd); A(&b.assoc_read, Nhd);
     if (e == cudaSuccess) e = cudaMemset(b.assoc_v, 0, (size_t)cfg->max_batch * h * d * sizeof(float));
     if (e == cudaSuccess) e = cudaMemset(b.assoc_p, 0, (size_t)cfg->max_batch * h * d * sizeof(float));
     if (e == cudaSuccess) e = cudaMemset(b.assoc_u, 0, (size_t)cfg->max_batch * h * sizeof(float));
@@ -1758,7 +1764,7 @@ void aideen_destroy(aideen_ctx *ctx) {
   if (ctx->comm) ncclCommDestroy(ctx->comm);
   DevBufs &b = ctx->b;
   void *ptrs[] = {b.W, b.G, b.M1, b.M2, b.S_in, b.tokens, b.targets, b.signal, b.A, b.amat, b.qkv,
-                  b.assoc_v, b.assoc_p, b.assoc_u, b.sig_store,
+                  b.assoc_v, b.assoc_p, b.assoc_u, b.sig_store, b.assoc_read,
                   b.dqkv, b.Wcat, b.alpha, b.nmix, b.rmix, b.scale, b.rho, b.Rsrc, b.hstar, b.pre,
                   b.pooled, b.hist, b.fpmctx, b.mstate, b.iters, b.v, b.gpre, b.dl_dh, b.rhs_slot,
                   b.nsg, b.da, b.dn, b.dsig, b.dRc, b.dS, b.lmp, b.Glm, b.Mlm1,

@@ -940,6 +940,7 @@ __global__ void __launch_bounds__(MAXT) picard_kernel(PicardArgs a) {
         const float kv = irc * irv;  // value = kv * x
         const float irp = 1.f / fmaxf(sqrtf(a_pp * inv_d + 1e-6f), 1e-6f);
         const float2 Pv = ld2(asp + j0), Vv = ld2(asv + j0);
+        st2(a.assoc_read + e, Vv);  // the value this token read (the alpha_assoc gradient's input)
         const float2 val = kv * xin;
         const float2 pay_raw = val + irp * Pv;
         const float qq = a_xx * kv * kv + 2.f * a_xp * kv * irp + a_pp * irp * irp;  // |payload|^2

@@ -89,6 +89,7 @@ struct PicardArgs {
   float *assoc_v, *assoc_p;        // [B][h][d] bank value, previous source (carried)
   float *assoc_u;                  // [B][h] bank usage (carried)
   float *sig_store;                // [N][h][d] stored signal: the payload on the upper slots
+  float *assoc_read;               // [N][h][d] bank value each token read (upper slots' rows)
 };
 
 struct AdjointArgs {
@@ -142,6 +143,12 @@ cudaError_t launch_attn_bwd_softmax(const AttnBwdArgs &a, int N, cudaStream_t st
 // dsig[n][s][:] -= g_pre[n][s][:] for the upper h/2 slots (the associative
 // slots, whose branch does not hold their signal).
 cudaError_t launch_sub_upper_slots(float *dsig, const float *gpre, int N, int h, int d, cudaStream_t st);
+// The reference's alpha_assoc gradient (fused_fpm_retain_bwd.wgsl:1129-1160,
+// 1281-1284), default flags: for every upper slot s,
+//   G[s] = sigmoid'(alpha_s) * sum_n (v[s][n] . V[n][s]) / max(rms(V[n][s]), 0.1)
+// with V the bank value token n read and v the adjoint ([h][N][d]); written, not added.
+cudaError_t launch_assoc_alpha_grad(const float *v, const float *vread, const float *alpha_raw, int N, int h, int d,
+                                    float *g_alpha, cudaStream_t st);
 cudaError_t launch_dsig_init(const AttnBwdArgs &a, float *dsig, int rows, int slot_coord,
                              cudaStream_t st);
 // out[map(c)] (+)= sum_r X[r*ld + c], c < ncols; map(c) = (c/seg)*ostride + c%seg.

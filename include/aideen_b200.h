@@ -61,9 +61,10 @@ typedef struct aideen_cfg {
  * FPM stage 4) in place of the FPM write: a one-bank hard read added to the
  * memory context, a single bank write per empty bank, a 0.019 consolidation of
  * h* into the slot's memory, and the payload as the slot's stored signal (the
- * adjoint's branch and the FPM backward read it).  Its own parameter gradients
- * (alpha_assoc, address and event weights, fused_fpm_retain_bwd.wgsl:475-1290)
- * are not computed.  The bank state is carried across calls and cleared by
+ * adjoint's branch and the FPM backward read it).  Of its own parameters,
+ * alpha_assoc gets the reference's gradient (fused_fpm_retain_bwd.wgsl:1129-1160,
+ * 1281-1284); the address and event weights, which change no output under the
+ * default flags (one bank, hard read, event gate off), get none.  The bank state is carried across calls and cleared by
  * aideen_reset_state.  Needs h_slots >= 2. */
 #define AIDEEN_CFG_ASSOC 1u
 

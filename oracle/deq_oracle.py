@@ -342,6 +342,27 @@ def assoc_write(x_t, state, m, h_star, t):
     return m_new, pay_raw
 
 
+def assoc_alpha_grad(assoc_read, v, W, d, h):
+    """The reference's alpha_assoc gradient, default flags (`fused_fpm_retain_bwd.wgsl:
+    1129-1160, 1281-1284`): one bank, read confidence and slot prior 1, so per
+    upper slot s
+        G[s] = sigmoid'(alpha_s) * sum_{b,t} (v[b,t,s] . V[b,t,s]) / max(rms(V[b,t,s]), 0.1)
+    with V the bank value token t read and v the clean adjoint (non-finite entries
+    as 0).  Like the rest of that backward it is the reference's formula, not the
+    exact derivative of the forward's injection (which scales V to
+    sigmoid(alpha) |signal| alpha_m / |V|).  assoc_read [B,T,h,d]; v [B*T,h,d]."""
+    V = View(W, d, h)
+    vr = np.asarray(assoc_read, np.float64).reshape(-1, h, d)
+    vv = np.asarray(v, np.float64)
+    vv = np.where(np.isfinite(vv), vv, 0.0)
+    rms_v = np.sqrt((vr * vr).sum(-1) / d)
+    tot = ((vv * vr).sum(-1) / np.maximum(rms_v, 0.1)).sum(0)        # [h]
+    a = 1.0 / (1.0 + np.exp(-V.alpha_assoc))
+    g = a * (1.0 - a) * tot
+    g[: h // 2] = 0.0
+    return g
+
+
 def assoc_state_zeros(B, h, d):
     """The reset state (reset_state, gpu_deq.rs:3141-3160: AssocBuf and PrevHStarBuf zeroed)."""
     return dict(V=np.zeros((B, h, d)), u=np.zeros((B, h)), P=np.zeros((B, h, d)))
@@ -390,6 +411,7 @@ class ForwardOut:
     # associative slots, where the write replaced it with the payload (`:2497`)
     branch_signal: np.ndarray = None
     assoc_state: dict = None  # bank value V, usage u, previous source P after the chunk
+    assoc_read: np.ndarray = None  # [B,T,h,d] bank value each token read (before its write)
 
 
 def forward(S_in, W, cfg: Cfg, mstate=None, assoc_state=None) -> ForwardOut:
@@ -427,6 +449,7 @@ def forward(S_in, W, cfg: Cfg, mstate=None, assoc_state=None) -> ForwardOut:
         ast = assoc_state_zeros(B, h, d) if assoc_state is None else {
             k: np.asarray(x, np.float64).copy() for k, x in assoc_state.items()}
     branch_sig = signal.copy()
+    vread = np.zeros((B, T, h, d)) if assoc else None
     for t in range(T):
         sig = signal[:, t]
         if t == 0:
@@ -484,6 +507,7 @@ def forward(S_in, W, cfg: Cfg, mstate=None, assoc_state=None) -> ForwardOut:
         if cfg.fpm:
             m_w = fpm_write(hcur, sig, m, V, Wx_diag)
             if assoc:
+                vread[:, t] = np.where(upper, ast["V"], 0.0)
                 old = {k: x.copy() for k, x in ast.items()}
                 m_a, pay_raw = assoc_write(S[:, t], ast, m, hcur, t)
                 for k in ast:  # the lower slots hold no associative state
@@ -496,7 +520,7 @@ def forward(S_in, W, cfg: Cfg, mstate=None, assoc_state=None) -> ForwardOut:
     pooled = hstar.mean(axis=2)
     return ForwardOut(signal=signal, A=A, hstar=hstar, iters=iters, pooled=pooled,
                       hist_ctx=hist, mstate=m, fpm_ctx=ctx_all, attn_cache=cache,
-                      branch_signal=branch_sig, assoc_state=ast)
+                      branch_signal=branch_sig, assoc_state=ast, assoc_read=vread)
 
 
 # ---------------------------------------------------------------------------
@@ -880,8 +904,9 @@ def fpm_backward(hstar, signal, hist, v, W, d, h, carry=None):
     (compiled out: ENABLE_FPM_WRITE_BWD = false, FPM_DIRECT_WRITE_SCALE = 0)
     contribute nothing.  With the associative branch on, `signal` is the stored
     signal the reference reads here (`:399`), the payload on the associative
-    slots; the branch's own parameter gradients (alpha_assoc, the address and
-    event weights, the bank state, `:475-1290`) are not restated.
+    slots; of the branch's own parameter gradients (`:475-1290`) alpha_assoc is
+    restated (`assoc_alpha_grad`, added by `train_step`), the address and event
+    weights' and the bank state's are not.
 
     Gradients are returned as raw sums over all sequences and tokens, in the
     AllWeights layout; the reference's per-family divisors (B*T for the slot
@@ -1083,6 +1108,9 @@ def train_step(S_in, targets, W, lm, cfg: Cfg, adam_state=None, step=1, lr=1e-3,
         # the payload on associative slots
         fpm_out = fpm_backward(fwd.hstar, fwd.branch_signal, fwd.hist_ctx, v, W, d, h, carry=fpm_carry)
         G = G + fpm_out["G"]
+        if cfg.assoc:
+            L_ = Offsets(d, h)
+            G[L_.alpha_assoc:L_.alpha_assoc + h] += assoc_alpha_grad(fwd.assoc_read, v, W, d, h)
     if adam_state is None:
         adam_state = (np.zeros_like(G), np.zeros_like(G))
     Wn, m1, m2 = adam(W, G, adam_state[0], adam_state[1], step, lr=lr)

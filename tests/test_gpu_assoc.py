@@ -59,7 +59,8 @@ def test_assoc_forward_parity_over_two_calls(c):
 def test_assoc_train_step_parity(c):
     """A whole step with the dense LM head: the adjoint linearises the payload
     branch of the upper slots, W_in and S_in receive their direct term from the
-    lower slots only, the FPM backward reads the stored signal."""
+    lower slots only, the FPM backward reads the stored signal, and alpha_assoc
+    gets the reference's gradient."""
     d, h, B, T, V = c["d"], c["h"], c["B"], c["T"], 61
     W = init_all_weights(d, h, seed=6)
     lm, emb = init_lm_head(d, V), init_embedding(d, V)
@@ -75,6 +76,10 @@ def test_assoc_train_step_parity(c):
     cfg = O.Cfg(d=d, h=h, max_iters=12, fpm=True, assoc=True, adj_iters=12)
     r = O.train_step(emb[tok], tg, W, lm, cfg)
     assert_step(step_errors(be, r, W, lm, B, T), loss, r)
+    # the reference's alpha_assoc gradient (upper slots; zero below)
+    L = O.Offsets(d, h)
+    ga = be.read_grads()[L.alpha_assoc:L.alpha_assoc + h]
+    assert rel(ga, r["grads"][L.alpha_assoc:L.alpha_assoc + h]) < TOL and not ga[: h // 2].any()
     be.close()
 
 

@@ -694,3 +694,36 @@ def test_assoc_signal_gradient_reaches_win_only_from_the_lower_slots():
     r0 = O.train_step(S, tg, W, lm, O.Cfg(d=d, h=h, fpm=True, slot_coord=False, max_iters=8, adj_iters=8))
     gwin0 = r0["grads"][L.win:L.win + h * d * d].reshape(h, d, d)
     assert np.abs(gwin0[h // 2:]).max() > 0
+
+
+def test_assoc_alpha_gradient_formula():
+    """alpha_assoc gets sigmoid'(alpha) * sum (v . V) / max(rms(V), 0.1) over the
+    tokens that read a written bank, on the upper slots only; none without the branch."""
+    d, h, B, T, Vv = 32, 4, 2, 5, 17
+    W = init_all_weights(d, h, seed=4)
+    lm = init_lm_head(d, Vv)
+    rng = np.random.default_rng(5)
+    S = rng.standard_normal((B, T, d)) * 0.5
+    tg = rng.integers(0, Vv, (B, T))
+    cfg = O.Cfg(d=d, h=h, fpm=True, assoc=True, max_iters=8, adj_iters=8)
+    r = O.train_step(S, tg, W, lm, cfg)
+    L = O.Offsets(d, h)
+    g = r["grads"][L.alpha_assoc:L.alpha_assoc + h]
+    f = r["fwd"]
+    V = O.View(W, d, h)
+    v = r["v"].reshape(B, T, h, d)
+    want = np.zeros(h)
+    for s in range(h // 2, h):
+        a = 1 / (1 + np.exp(-V.alpha_assoc[s]))
+        tot = 0.0
+        for b in range(B):
+            for t in range(T):
+                x = f.assoc_read[b, t, s]
+                tot += (v[b, t, s] * x).sum() / max(np.sqrt((x * x).mean()), 0.1)
+        want[s] = a * (1 - a) * tot
+    assert np.allclose(g, want, rtol=1e-12, atol=0)
+    assert not g[: h // 2].any() and np.abs(g[h // 2:]).min() > 0
+    # the bank is empty at t = 0 and 1 (written at t = 1, read from t = 2 on)
+    assert not f.assoc_read[:, :2].any() and f.assoc_read[:, 2:, h // 2:].any()
+    r0 = O.train_step(S, tg, W, lm, O.Cfg(d=d, h=h, fpm=True, max_iters=8, adj_iters=8))
+    assert not r0["grads"][L.alpha_assoc:L.alpha_assoc + h].any()
