@@ -63,8 +63,9 @@ typedef struct aideen_cfg {
  * h* into the slot's memory, and the payload as the slot's stored signal (the
  * adjoint's branch and the FPM backward read it).  Of its own parameters,
  * alpha_assoc gets the reference's gradient (fused_fpm_retain_bwd.wgsl:1129-1160,
- * 1281-1284); the address and event weights, which change no output under the
- * default flags (one bank, hard read, event gate off), get none.  The bank state is carried across calls and cleared by
+ * 1281-1284); under these default flags the reference's terms for the address,
+ * value and event weights are exactly zero (one bank, event gate off), and so
+ * are they here.  The bank state is carried across calls and cleared by
  * aideen_reset_state.  Needs h_slots >= 2. */
 #define AIDEEN_CFG_ASSOC 1u
 

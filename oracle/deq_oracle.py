@@ -904,9 +904,12 @@ def fpm_backward(hstar, signal, hist, v, W, d, h, carry=None):
     (compiled out: ENABLE_FPM_WRITE_BWD = false, FPM_DIRECT_WRITE_SCALE = 0)
     contribute nothing.  With the associative branch on, `signal` is the stored
     signal the reference reads here (`:399`), the payload on the associative
-    slots; of the branch's own parameter gradients (`:475-1290`) alpha_assoc is
-    restated (`assoc_alpha_grad`, added by `train_step`), the address and event
-    weights' and the bank state's are not.
+    slots.  Of the branch's own parameter gradients (`:475-1290`) only alpha_assoc
+    is nonzero under the default flags (`assoc_alpha_grad`, added by
+    `train_step`): with one bank the read's score gradient p * (g - p g) is 0,
+    so the address weights get nothing (`:976, 1266`), the event-gate factor
+    gate * (1 - gate) is 0 with the gate off (`:964`), and the value gradient
+    reaches no parameter.
 
     Gradients are returned as raw sums over all sequences and tokens, in the
     AllWeights layout; the reference's per-family divisors (B*T for the slot
