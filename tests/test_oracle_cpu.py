@@ -727,3 +727,31 @@ def test_assoc_alpha_gradient_formula():
     assert not f.assoc_read[:, :2].any() and f.assoc_read[:, 2:, h // 2:].any()
     r0 = O.train_step(S, tg, W, lm, O.Cfg(d=d, h=h, fpm=True, max_iters=8, adj_iters=8))
     assert not r0["grads"][L.alpha_assoc:L.alpha_assoc + h].any()
+
+
+def test_assoc_read_differentiates_previous_context_like_the_reference_probe():
+    """The reference's probe `test_assoc_read_differentiates_previous_context_probe`
+    (aideen-backbone/tests/picard_pipeline_test.rs:1745-1800, with
+    `run_four_token_sequence_with_assoc_enabled` :684-800): one-hot S_in rows
+    (key, mid, key, final), d 512, h 8, 4 Picard iterations, FPM stage 4 with one
+    bank, the FPM and associative matrices zero (alpha_assoc 0).  The value
+    read at token 3 must differ (L2 > 1e-4) between two sequences whose key
+    token differs; the restatement's bank, written at token 1 from the key's
+    normalised source, does."""
+    d, h, T = 512, 8, 4
+    W = init_all_weights(d, h, seed=42).astype(np.float64)
+    L = O.Offsets(d, h)
+    for a, b in [(L.w_retain_up, L.b_retain + h * d), (L.w_q_mem, L.b_read_mem + h),
+                 (L.w_k_assoc, L.total)]:
+        W[a:b] = 0.0
+    cfg = O.Cfg(d=d, h=h, fpm=True, assoc=True, max_iters=4)
+
+    def read3(key):
+        S = np.zeros((1, T, d))
+        S[0, 0, key] = S[0, 2, key] = 1.0
+        S[0, 1, 2] = S[0, 3, 3] = 1.0
+        return O.forward(S, W, cfg).assoc_read[0, 3, h // 2:]
+
+    ra, rb = read3(0), read3(1)
+    assert np.all(np.isfinite(ra)) and np.all(np.isfinite(rb))
+    assert np.linalg.norm(ra - rb) > 1e-4
